@@ -1,0 +1,102 @@
+/*
+ * nnc_cuda.h — control surface of the B200 operator library (libnnc_cuda.so).
+ *
+ * The reference operator library (nnc-py runtime/x86/ops.c) is synchronous,
+ * host-memory and stateless; its runtime header (runtime/include/
+ * nnc_runtime.h:22-42) declares allocation/scheduler hooks that nothing
+ * defines. On a GPU the operators need a device, a stream, a precision mode
+ * for the tensor-core contractions, scratch memory and an error channel;
+ * this header provides them. Everything here is extern "C" with plain
+ * pointers and integers.
+ *
+ * State model:
+ *   - device, stream, precision and the sticky error status are per host
+ *     thread (a thread that never calls the setters uses device 0, the
+ *     legacy default stream, TF32 precision);
+ *   - scratch ("workspace") memory is per (thread, device): either supplied by
+ *     the caller (nnc_cuda_set_workspace) or grown on demand with stream-ordered
+ *     allocation on the current stream.
+ */
+#ifndef NNC_CUDA_H
+#define NNC_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include "nnc_types.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ---------------------------------------------------------- */
+#define NNC_CUDA_OK 0
+#define NNC_CUDA_ERR_INVALID 1      /* NULL tensor/data/shape, shape mismatch */
+#define NNC_CUDA_ERR_UNSUPPORTED 2  /* valid for the reference, not supported here */
+#define NNC_CUDA_ERR_LAUNCH 3       /* CUDA runtime / launch error */
+#define NNC_CUDA_ERR_NOMEM 4        /* workspace or slab allocation failed */
+#define NNC_CUDA_ERR_DEVICE_TIMEOUT 5 /* a bounded in-kernel wait expired */
+
+/* ---- storage tags carried in Tensor::dtype above the element type -------- */
+#define NNC_CUDA_DTYPE_MASK 0xff
+/* 4-D activation stored channels-last ([N][H][W][C]) while Tensor::shape
+ * keeps the logical NCHW extents. Only the conv/pool entry points and the
+ * element-wise ops accept it. */
+#define NNC_CUDA_TAG_NHWC 0x100
+/* Conv weight re-laid out by nnc_cuda_prepack_conv_weight. */
+#define NNC_CUDA_TAG_PACKED_CONV 0x200
+
+/* ---- precision of tcgen05 contractions (conv, gemm, matmul) -------------- */
+#define NNC_CUDA_PRECISION_TF32 0   /* one TF32 MMA per k-step */
+#define NNC_CUDA_PRECISION_3XTF32 1 /* hi*hi + hi*lo + lo*hi split: ~fp32 accuracy */
+
+/* ---- device / stream / status ------------------------------------------- */
+int nnc_cuda_init(int device);           /* set device + create its state */
+int nnc_cuda_set_device(int device);
+int nnc_cuda_get_device(void);
+void nnc_cuda_set_stream(void* stream);  /* cudaStream_t; NULL = legacy default */
+void* nnc_cuda_get_stream(void);
+int nnc_cuda_sync(void);                 /* synchronise the current stream */
+int nnc_cuda_get_last_error(void);       /* sticky per-thread status */
+const char* nnc_cuda_get_last_error_string(void);
+void nnc_cuda_clear_error(void);
+/* Reads (and clears) the device-side error word that kernels set when a
+ * bounded wait expires; synchronises the current stream first. Returns
+ * NNC_CUDA_OK or NNC_CUDA_ERR_DEVICE_TIMEOUT (also recorded as sticky). */
+int nnc_cuda_check_device_status(void);
+
+void nnc_cuda_set_precision(int mode);
+int nnc_cuda_get_precision(void);
+
+/* ---- scratch memory ----------------------------------------------------------
+ * Caller-owned workspace used by ops that need scratch (layout conversion for
+ * NCHW conv calls, operand transposes, 3xTF32 operand splits). Passing NULL/0
+ * returns to on-demand growth. */
+int nnc_cuda_set_workspace(void* device_ptr, size_t bytes);
+size_t nnc_cuda_get_workspace_capacity(void);
+
+/* ---- prepacking of constant conv weights ------------------------------------
+ * Re-lays a constant OIHW conv weight into the tensor-core layout (O, KH, KW,
+ * I padded, TF32 hi/lo planes) at dst (device, bytes from
+ * nnc_cuda_prepacked_conv_weight_bytes), then points w->data at dst and tags
+ * w->dtype with NNC_CUDA_TAG_PACKED_CONV. Enqueued on the current stream. */
+size_t nnc_cuda_prepacked_conv_weight_bytes(const Tensor* w);
+int nnc_cuda_prepack_conv_weight(Tensor* w, void* dst, size_t dst_bytes);
+
+/* ---- layout conversion at model boundaries (logical shapes are NCHW) ---- */
+void nnc_cuda_nchw_to_nhwc(Tensor* input, Tensor* output);
+void nnc_cuda_nhwc_to_nchw(Tensor* input, Tensor* output);
+
+/* ---- observability ------------------------------------------------------------
+ * When enabled (or NNC_CUDA_TRACE=1 in the environment), every operator call
+ * records CUDA events around its launches; nnc_cuda_trace_dump prints one line
+ * per call (name, stream-ordered start/end in microseconds) to stderr and
+ * clears the log. Synchronises the current stream. */
+void nnc_cuda_trace_enable(int on);
+int nnc_cuda_trace_dump(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NNC_CUDA_H */

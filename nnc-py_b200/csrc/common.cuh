@@ -1,0 +1,88 @@
+// Shared host/device helpers of libnnc_cuda.so: tensor metadata, status
+// reporting, the per-thread execution context and launch checking.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stdio.h>
+
+#include "nnc_cuda.h"
+#include "nnc_ops.h"
+
+namespace nnc {
+
+// ---------------------------------------------------------------------------
+// Per-thread execution context (device, stream, precision, sticky status).
+// ---------------------------------------------------------------------------
+struct ThreadCtx {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  int precision = NNC_CUDA_PRECISION_TF32;
+  int status = NNC_CUDA_OK;
+  char message[512] = {0};
+};
+ThreadCtx& ctx();
+
+// Records a failure: sets the sticky status, keeps the first message and
+// prints one line to stderr (the reference prints and returns on invalid
+// tensors, ops.c:728-744).
+void fail(int code, const char* op, const char* fmt, ...)
+    __attribute__((format(printf, 3, 4)));
+
+// Checks the result of a launch / runtime call; false (and status set) on error.
+bool check_cuda(cudaError_t err, const char* op, const char* what);
+inline bool check_launch(const char* op) {
+  return check_cuda(cudaGetLastError(), op, "kernel launch");
+}
+
+// Device-side error word of the current device (bounded waits that expire
+// set it to NNC_CUDA_ERR_DEVICE_TIMEOUT; the host reads it on demand).
+int* device_error_word();
+int sm_count();
+
+// Scratch memory on the current device for the current stream.
+void* workspace(size_t bytes, const char* op);
+
+// Opened at the top of every entry point: refreshes the thread's device from
+// the CUDA runtime (so callers that switch devices with cudaSetDevice or
+// torch.cuda.set_device are followed) and, when tracing is enabled
+// (nnc_cuda_trace_enable / NNC_CUDA_TRACE=1), brackets the call's launches
+// with CUDA events on the current stream.
+struct OpScope {
+  explicit OpScope(const char* name);
+  ~OpScope();
+  const char* name_;
+  int slot_;
+};
+
+// ---------------------------------------------------------------------------
+// Tensor metadata helpers (host).
+// ---------------------------------------------------------------------------
+inline int elem_type(const Tensor* t) { return (int)t->dtype & NNC_CUDA_DTYPE_MASK; }
+inline int tag_of(const Tensor* t) { return (int)t->dtype & ~NNC_CUDA_DTYPE_MASK; }
+inline bool is_nhwc(const Tensor* t) { return (tag_of(t) & NNC_CUDA_TAG_NHWC) != 0; }
+inline size_t elem_size(int dtype) {
+  switch (dtype) {
+    case NNC_DTYPE_FLOAT16: return 2;
+    case NNC_DTYPE_INT8:
+    case NNC_DTYPE_UINT8:
+    case NNC_DTYPE_BOOL: return 1;
+    case NNC_DTYPE_INT64: return 8;
+    default: return 4;
+  }
+}
+// Product of the extents (the reference's tensor_numel, ops.c:22-28).
+inline int64_t numel(const Tensor* t) {
+  int64_t n = 1;
+  for (int i = 0; i < t->ndim; ++i) n *= t->shape[i];
+  return n;
+}
+// NULL checks shared by every entry point.
+bool valid_tensor(const Tensor* t, const char* op, const char* name);
+inline bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
+
+// Ceil-div and grid sizing in multiples of the SM count.
+__host__ __device__ inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
+int grid_for(int64_t work_items, int threads, int max_ctas_per_sm = 8);
+
+}  // namespace nnc

@@ -1,0 +1,712 @@
+// Dense contractions: nnc_gemm / nnc_gemm_nt / nnc_matmul (+ relu variants)
+// on the sm_100a tensor cores (tcgen05.mma kind::tf32, accumulators in TMEM,
+// operands staged by TMA).
+//
+// Kernel shape (persistent, one CTA per SM, 192 threads):
+//   warp 0      TMA producer: streams 128 x 32 A tiles and BN x 32 B tiles
+//               (both K-major, 128-byte swizzle) into a STAGES-deep ring;
+//   warp 1      allocates TMEM and issues the MMAs (one thread), 4 k-steps of
+//               K = 8 per 32-wide stage; commits free the ring slots;
+//   warps 2..5  epilogue: tcgen05.ld of the 128 x BN fp32 accumulator,
+//               alpha / beta*C / relu, stores to global.
+// Two TMEM accumulators (2 x BN columns) let tile i's epilogue overlap tile
+// i+1's main loop.
+//
+// Precision: TF32 mode issues one MMA per k-step. 3xTF32 mode splits A and B
+// into hi = tf32(x) and lo = x - hi planes and issues lo*hi + hi*lo + hi*hi,
+// which recovers ~fp32 accuracy (the reference accumulates in fp64,
+// ops.c:1800-1840). Shapes the TMA path cannot take (K % 4 != 0, unaligned
+// bases, very small M or N) go to a SIMT kernel with fp64 accumulation.
+#include <math.h>
+
+#include "common.cuh"
+#include "movement.cuh"
+#include "tc.cuh"
+
+namespace nnc {
+namespace {
+
+constexpr int BM = 128;
+constexpr int BK = 32;  // fp32 elements per 128-byte swizzle row
+constexpr int kTCThreads = 192;
+
+struct GemmArgs {
+  int M, N, K;
+  int m_tiles, n_tiles;
+  int64_t tiles;
+  int a_batched, b_batched;
+  float alpha, beta;
+  const float* C;
+  int c_mode;  // 0: none, 1: C[n] (1-D), 2: C[m * ldc + n]
+  int64_t ldc, c_batch_stride;
+  float* D;
+  int64_t ldd, d_batch_stride;
+  int relu;
+  int* err;
+};
+
+__device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
+  return (uint8_t*)(((uintptr_t)p + 1023) & ~(uintptr_t)1023);
+}
+
+template <int BN, int SPLIT, int STAGES>
+struct GemmCfg {
+  static constexpr uint32_t A_BYTES = BM * BK * 4;
+  static constexpr uint32_t B_BYTES = BN * BK * 4;
+  static constexpr uint32_t STAGE_BYTES = SPLIT * (A_BYTES + B_BYTES);
+  static constexpr uint32_t TMEM_COLS = 2 * BN;  // power of two for BN in {64,128,256}
+  static constexpr size_t SMEM = (size_t)STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*bars*/;
+};
+
+template <int BN, int SPLIT, int STAGES>
+__global__ void __launch_bounds__(kTCThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmA1,
+                   const __grid_constant__ CUtensorMap tmB0, const __grid_constant__ CUtensorMap tmB1,
+                   const GemmArgs g) {
+  using Cfg = GemmCfg<BN, SPLIT, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* done = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kblocks = (g.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      tc::mbar_init(&full[s], 1);
+      tc::mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      tc::mbar_init(&tfull[a], 1);
+      tc::mbar_init(&tempty[a], 4);
+    }
+    tc::mbar_init(done, 1);
+    tc::fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tc::prefetch_tmap(&tmA0);
+    tc::prefetch_tmap(&tmB0);
+    if (SPLIT == 2) {
+      tc::prefetch_tmap(&tmA1);
+      tc::prefetch_tmap(&tmB1);
+    }
+  }
+  if (warp == 1) {
+    tc::tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+    tc::tmem_relinquish();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer ----------------
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int64_t t = blockIdx.x; t < g.tiles && ok; t += gridDim.x) {
+        const int per_b = g.m_tiles * g.n_tiles;
+        const int b = (int)(t / per_b);
+        const int mt = (int)((t % per_b) / g.n_tiles), nt = (int)((t % per_b) % g.n_tiles);
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!tc::mbar_wait(&empty[stage], phase ^ 1, g.err)) {
+            ok = false;
+            break;
+          }
+          uint8_t* s = smem + stage * Cfg::STAGE_BYTES;
+          tc::mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
+          const int kx = kb * BK;
+          tc::tma_load_3d(s, &tmA0, &full[stage], kx, mt * BM, b * g.a_batched);
+          if (SPLIT == 2)
+            tc::tma_load_3d(s + Cfg::A_BYTES, &tmA1, &full[stage], kx, mt * BM, b * g.a_batched);
+          uint8_t* sb = s + SPLIT * Cfg::A_BYTES;
+          tc::tma_load_3d(sb, &tmB0, &full[stage], kx, nt * BN, b * g.b_batched);
+          if (SPLIT == 2)
+            tc::tma_load_3d(sb + Cfg::B_BYTES, &tmB1, &full[stage], kx, nt * BN, b * g.b_batched);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer ----------------
+      constexpr uint32_t idesc = tc::idesc_tf32(BM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int64_t t = blockIdx.x; t < g.tiles && ok; t += gridDim.x, ++local) {
+        const int acc = local & 1;
+        const uint32_t aphase = (local >> 1) & 1;
+        if (!tc::mbar_wait(&tempty[acc], aphase ^ 1, g.err)) break;
+        tc::tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!tc::mbar_wait(&full[stage], phase, g.err)) {
+            ok = false;
+            break;
+          }
+          tc::tc_fence_after();
+          const uint32_t sa = tc::smem_u32(smem + stage * Cfg::STAGE_BYTES);
+          const uint32_t sb = sa + SPLIT * Cfg::A_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / 8; ++k) {
+            const uint64_t a0 = tc::desc_kmajor_sw128(sa + k * 32);
+            const uint64_t b0 = tc::desc_kmajor_sw128(sb + k * 32);
+            const uint32_t first = (kb | k) != 0;
+            if (SPLIT == 1) {
+              tc::mma_tf32(d_tmem, a0, b0, idesc, first);
+            } else {
+              const uint64_t a1 = tc::desc_kmajor_sw128(sa + Cfg::A_BYTES + k * 32);
+              const uint64_t b1 = tc::desc_kmajor_sw128(sb + Cfg::B_BYTES + k * 32);
+              tc::mma_tf32(d_tmem, a1, b0, idesc, first);  // lo * hi
+              tc::mma_tf32(d_tmem, a0, b1, idesc, 1);      // hi * lo
+              tc::mma_tf32(d_tmem, a0, b0, idesc, 1);      // hi * hi
+            }
+          }
+          tc::mma_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        tc::mma_commit(&tfull[acc]);
+      }
+      // Drain: every MMA issued above has completed once `done` fires.
+      tc::mma_commit(done);
+      tc::mbar_wait(done, 0, g.err);
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5) ----------------
+    const int quad = warp & 3;  // TMEM lanes [32*quad, 32*quad + 32)
+    int local = 0;
+    const bool vec_ok = ((g.ldd & 3) == 0) && ((((uintptr_t)g.D) & 15) == 0);
+    for (int64_t t = blockIdx.x; t < g.tiles; t += gridDim.x, ++local) {
+      const int per_b = g.m_tiles * g.n_tiles;
+      const int b = (int)(t / per_b);
+      const int mt = (int)((t % per_b) / g.n_tiles), nt = (int)((t % per_b) % g.n_tiles);
+      const int acc = local & 1;
+      const uint32_t aphase = (local >> 1) & 1;
+      if (!tc::mbar_wait(&tfull[acc], aphase, g.err)) break;
+      tc::tc_fence_after();
+      const int row = mt * BM + quad * 32 + lane;
+      float* drow = g.D + (int64_t)b * g.d_batch_stride + (int64_t)row * g.ldd;
+      const float* crow = nullptr;
+      if (g.c_mode == 2) crow = g.C + (int64_t)b * g.c_batch_stride + (int64_t)row * g.ldc;
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 16) {
+        uint32_t r[16];
+        __syncwarp();  // tcgen05.ld is .sync.aligned: the warp must be converged
+        tc::tmem_ld16(tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN + c0, r);
+        tc::tmem_ld_wait();
+        const int n0 = nt * BN + c0;
+        if (row < g.M && n0 < g.N) {
+          float v[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            float x = g.alpha * __uint_as_float(r[j]);
+            const int n = n0 + j;
+            if (g.c_mode == 1 && n < g.N) x = fmaf(g.beta, g.C[n], x);
+            if (g.c_mode == 2 && n < g.N) x = fmaf(g.beta, crow[n], x);
+            if (g.relu) x = x > 0.0f ? x : 0.0f;
+            v[j] = x;
+          }
+          if (vec_ok && n0 + 16 <= g.N) {
+            float4* d4 = reinterpret_cast<float4*>(drow + n0);
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              d4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              if (n0 + j < g.N) drow[n0 + j] = v[j];
+          }
+        }
+      }
+      tc::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&tempty[acc]);
+    }
+  }
+
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+// hi = tf32(x), lo = x - hi (exact in fp32), for matrices of `mat` elements
+// read at x + b * in_bs and written densely.
+__global__ void __launch_bounds__(256) split_tf32_kernel(const float* __restrict__ x,
+                                                         int64_t in_bs, float* __restrict__ hi,
+                                                         float* __restrict__ lo, int64_t mat,
+                                                         int64_t n) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const float v = x[(i / mat) * in_bs + i % mat];
+    const float h = tc::to_tf32(v);
+    hi[i] = h;
+    lo[i] = v - h;
+  }
+}
+
+// SIMT fallback: one output per thread, fp64 accumulation over K with
+// generic strides (covers every transpose mode, vectors, odd K).
+struct SimtArgs {
+  int M, N, K, batches;
+  const float* A;
+  int64_t sam, sak, a_bs;
+  const float* B;
+  int64_t sbk, sbn, b_bs;
+  float alpha, beta;
+  const float* C;
+  int c_mode;
+  int64_t ldc, c_bs;
+  float* D;
+  int64_t ldd, d_bs;
+  int relu;
+};
+
+__global__ void __launch_bounds__(256) gemm_simt_kernel(const SimtArgs a) {
+  constexpr int T = 16;
+  __shared__ float As[T][T + 1];
+  __shared__ float Bs[T][T + 1];
+  const int tx = threadIdx.x % T, ty = threadIdx.x / T;
+  const int64_t tiles_m = cdiv(a.M, T), tiles_n = cdiv(a.N, T);
+  for (int64_t t = blockIdx.x; t < (int64_t)a.batches * tiles_m * tiles_n; t += gridDim.x) {
+    const int64_t b = t / (tiles_m * tiles_n);
+    const int64_t rem = t % (tiles_m * tiles_n);
+    const int m = (int)(rem / tiles_n) * T + ty, n = (int)(rem % tiles_n) * T + tx;
+    const float* A = a.A + b * a.a_bs;
+    const float* B = a.B + b * a.b_bs;
+    double acc = 0.0;
+    for (int k0 = 0; k0 < a.K; k0 += T) {
+      const int am = (int)(rem / tiles_n) * T + ty, ak = k0 + tx;
+      As[ty][tx] = (am < a.M && ak < a.K) ? A[am * a.sam + ak * a.sak] : 0.0f;
+      const int bk = k0 + ty, bn = (int)(rem % tiles_n) * T + tx;
+      Bs[ty][tx] = (bk < a.K && bn < a.N) ? B[bk * a.sbk + bn * a.sbn] : 0.0f;
+      __syncthreads();
+#pragma unroll
+      for (int k = 0; k < T; ++k) acc += (double)As[ty][k] * (double)Bs[k][tx];
+      __syncthreads();
+    }
+    if (m < a.M && n < a.N) {
+      acc *= (double)a.alpha;
+      if (a.c_mode == 1) acc += (double)a.beta * (double)a.C[n];
+      if (a.c_mode == 2) acc += (double)a.beta * (double)a.C[b * a.c_bs + (int64_t)m * a.ldc + n];
+      float o = (float)acc;
+      if (a.relu) o = o > 0.0f ? o : 0.0f;
+      a.D[b * a.d_bs + (int64_t)m * a.ldd + n] = o;
+    }
+  }
+}
+
+// ------------------------------------------------------------------ host --
+
+// A contraction after shape analysis: D[b] = alpha * op(A[b]) op(B[b]) + beta * C.
+struct Problem {
+  int M, N, K, batches;
+  const float* A;
+  bool a_trans;  // A stored [K, M] instead of [M, K]
+  int64_t a_bs;  // batch stride in elements (0 = broadcast)
+  const float* B;
+  bool b_kmajor;  // B stored [N, K] (K-major) instead of [K, N]
+  int64_t b_bs;
+  float alpha, beta;
+  const float* C;
+  int c_mode;
+  int64_t ldc, c_bs;
+  float* D;
+  int64_t d_bs;
+  int relu;
+};
+
+template <int BN, int SPLIT, int STAGES>
+bool launch_tc(const Problem& p, const float* A0, const float* A1, const float* B0,
+               const float* B1, const char* op) {
+  using Cfg = GemmCfg<BN, SPLIT, STAGES>;
+  CUtensorMap ta0, ta1, tb0, tb1;
+  const uint64_t a_dims[3] = {(uint64_t)p.K, (uint64_t)p.M, (uint64_t)(p.a_bs ? p.batches : 1)};
+  const uint64_t a_str[2] = {(uint64_t)p.K * 4, (uint64_t)(p.a_bs ? p.a_bs : (int64_t)p.M * p.K) * 4};
+  const uint64_t b_dims[3] = {(uint64_t)p.K, (uint64_t)p.N, (uint64_t)(p.b_bs ? p.batches : 1)};
+  const uint64_t b_str[2] = {(uint64_t)p.K * 4, (uint64_t)(p.b_bs ? p.b_bs : (int64_t)p.N * p.K) * 4};
+  const uint32_t a_box[3] = {BK, BM, 1}, b_box[3] = {BK, BN, 1};
+  if (!encode_tmap_f32(&ta0, A0, 3, a_dims, a_str, a_box, nullptr, op)) return false;
+  if (!encode_tmap_f32(&tb0, B0, 3, b_dims, b_str, b_box, nullptr, op)) return false;
+  ta1 = ta0;
+  tb1 = tb0;
+  if (SPLIT == 2) {
+    if (!encode_tmap_f32(&ta1, A1, 3, a_dims, a_str, a_box, nullptr, op)) return false;
+    if (!encode_tmap_f32(&tb1, B1, 3, b_dims, b_str, b_box, nullptr, op)) return false;
+  }
+  GemmArgs g;
+  g.M = p.M;
+  g.N = p.N;
+  g.K = p.K;
+  g.m_tiles = (int)cdiv(p.M, BM);
+  g.n_tiles = (int)cdiv(p.N, BN);
+  g.tiles = (int64_t)p.batches * g.m_tiles * g.n_tiles;
+  g.a_batched = p.a_bs ? 1 : 0;
+  g.b_batched = p.b_bs ? 1 : 0;
+  g.alpha = p.alpha;
+  g.beta = p.beta;
+  g.C = p.C;
+  g.c_mode = p.c_mode;
+  g.ldc = p.ldc;
+  g.c_batch_stride = p.c_bs;
+  g.D = p.D;
+  g.ldd = p.N;
+  g.d_batch_stride = p.d_bs;
+  g.relu = p.relu;
+  g.err = device_error_word();
+  auto kern = gemm_tc_kernel<BN, SPLIT, STAGES>;
+  static bool attr_set = false;  // per instantiation
+  if (!attr_set) {
+    if (!check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)Cfg::SMEM),
+                    op, "cudaFuncSetAttribute"))
+      return false;
+    attr_set = true;
+  }
+  const int grid = (int)(g.tiles < sm_count() ? g.tiles : sm_count());
+  kern<<<grid, kTCThreads, Cfg::SMEM, ctx().stream>>>(ta0, ta1, tb0, tb1, g);
+  return check_launch(op);
+}
+
+void launch_simt(const Problem& p, const char* op) {
+  SimtArgs a;
+  a.M = p.M;
+  a.N = p.N;
+  a.K = p.K;
+  a.batches = p.batches;
+  a.A = p.A;
+  a.sam = p.a_trans ? 1 : p.K;
+  a.sak = p.a_trans ? p.M : 1;
+  a.a_bs = p.a_bs;
+  a.B = p.B;
+  a.sbk = p.b_kmajor ? 1 : p.N;
+  a.sbn = p.b_kmajor ? p.K : 1;
+  a.b_bs = p.b_bs;
+  a.alpha = p.alpha;
+  a.beta = p.beta;
+  a.C = p.C;
+  a.c_mode = p.c_mode;
+  a.ldc = p.ldc;
+  a.c_bs = p.c_bs;
+  a.D = p.D;
+  a.ldd = p.N;
+  a.d_bs = p.d_bs;
+  a.relu = p.relu;
+  const int64_t tiles = (int64_t)p.batches * cdiv(p.M, 16) * cdiv(p.N, 16);
+  const int grid = (int)(tiles < (int64_t)sm_count() * 8 ? tiles : (int64_t)sm_count() * 8);
+  gemm_simt_kernel<<<grid, 256, 0, ctx().stream>>>(a);
+  check_launch(op);
+}
+
+// Splits `total / mat` matrices of `mat` elements, read at src + b * in_bs
+// (in_bs == 0: one matrix), into dense hi / lo planes.
+bool split_batches(const float* src, int64_t in_bs, float* hi, float* lo, int64_t mat,
+                   int64_t total, const char* op) {
+  split_tf32_kernel<<<grid_for(total, 256, 8), 256, 0, ctx().stream>>>(
+      src, in_bs ? in_bs : mat, hi, lo, mat, total);
+  return check_launch(op);
+}
+
+void run_problem(Problem p, const char* op) {
+  if ((int64_t)p.M * p.N * p.batches == 0) return;
+  const bool tiny = p.M < 64 || p.N < 16 || (int64_t)p.M * p.N * p.K < (1 << 18);
+  // TMA needs 16-byte aligned bases and row pitches; A batches must be dense
+  // (the reference's overlapping batch offsets, see matmul_impl, take the
+  // SIMT path).
+  const bool tma_ok = (p.K % 4 == 0) && aligned16(p.A) && aligned16(p.B) &&
+                      (p.a_bs == 0 || p.a_bs == (int64_t)p.M * p.K) && p.K > 0;
+  if (tiny || !tma_ok) {
+    launch_simt(p, op);
+    return;
+  }
+  const bool split = ctx().precision == NNC_CUDA_PRECISION_3XTF32;
+  // Scratch: K-major copies of transposed operands, then hi/lo planes.
+  const int64_t a_elems = (int64_t)(p.a_bs ? p.batches : 1) * p.M * p.K;
+  const int64_t b_elems = (int64_t)(p.b_bs ? p.batches : 1) * p.N * p.K;
+  size_t need = 0;
+  if (p.a_trans) need += a_elems * 4;
+  if (!p.b_kmajor) need += b_elems * 4;
+  if (split) need += 2 * (a_elems + b_elems) * 4;
+  float* ws = need ? (float*)workspace(need + 64, op) : nullptr;
+  if (need && !ws) return;
+  float* cur = ws;
+  const float* A = p.A;
+  const float* B = p.B;
+  if (p.a_trans) {  // [K, M] -> [M, K], batches made dense
+    if (!batched_transpose_f32(A, cur, p.a_bs ? p.batches : 1, p.K, p.M, op, p.a_bs)) return;
+    A = cur;
+    cur += a_elems;
+    if (p.a_bs) p.a_bs = (int64_t)p.M * p.K;
+  }
+  if (!p.b_kmajor) {  // [K, N] -> [N, K], batches made dense
+    if (!batched_transpose_f32(B, cur, p.b_bs ? p.batches : 1, p.K, p.N, op, p.b_bs)) return;
+    B = cur;
+    cur += b_elems;
+    if (p.b_bs) p.b_bs = (int64_t)p.N * p.K;
+  }
+  const int64_t a_in_bs = p.a_bs, b_in_bs = p.b_bs;
+  if (split) {  // the hi/lo planes are dense copies
+    if (p.a_bs) p.a_bs = (int64_t)p.M * p.K;
+    if (p.b_bs) p.b_bs = (int64_t)p.N * p.K;
+  }
+  if (!split) {
+    if (p.N > 128 && (int64_t)cdiv(p.M, BM) * cdiv(p.N, 256) * p.batches >= sm_count())
+      launch_tc<256, 1, 4>(p, A, nullptr, B, nullptr, op);
+    else if (p.N > 64)
+      launch_tc<128, 1, 6>(p, A, nullptr, B, nullptr, op);
+    else
+      launch_tc<64, 1, 8>(p, A, nullptr, B, nullptr, op);
+    return;
+  }
+  float* a_hi = cur;
+  float* a_lo = a_hi + a_elems;
+  float* b_hi = a_lo + a_elems;
+  float* b_lo = b_hi + b_elems;
+  if (!split_batches(A, a_in_bs, a_hi, a_lo, (int64_t)p.M * p.K, a_elems, op) ||
+      !split_batches(B, b_in_bs, b_hi, b_lo, (int64_t)p.N * p.K, b_elems, op))
+    return;
+  if (p.N > 64)
+    launch_tc<128, 2, 3>(p, a_hi, a_lo, b_hi, b_lo, op);
+  else
+    launch_tc<64, 2, 4>(p, a_hi, a_lo, b_hi, b_lo, op);
+}
+
+bool f32(const Tensor* t, const char* op, const char* name) {
+  if (!valid_tensor(t, op, name)) return false;
+  if (elem_type(t) != NNC_DTYPE_FLOAT32 || tag_of(t) != 0) {
+    fail(NNC_CUDA_ERR_UNSUPPORTED, op, "%s: needs an untagged float32 tensor", name);
+    return false;
+  }
+  return true;
+}
+
+bool set_c(Problem& p, Tensor* c, int M, int N, const char* op) {
+  p.C = nullptr;
+  p.c_mode = 0;
+  p.ldc = N;
+  p.c_bs = 0;
+  if (!c) return true;
+  if (!f32(c, op, "c")) return false;
+  p.C = (const float*)c->data;
+  if (c->ndim == 1) {
+    if (numel(c) < N) {
+      fail(NNC_CUDA_ERR_INVALID, op, "c has %lld elements, needs %d", (long long)numel(c), N);
+      return false;
+    }
+    p.c_mode = 1;
+  } else {
+    if (numel(c) < (int64_t)M * N) {
+      fail(NNC_CUDA_ERR_INVALID, op, "c has %lld elements, needs %lld", (long long)numel(c),
+           (long long)M * N);
+      return false;
+    }
+    p.c_mode = 2;
+  }
+  return true;
+}
+
+// nnc_gemm semantics (ops.c:1732-1841).
+void gemm_impl(Tensor* a, Tensor* b, Tensor* c, Tensor* out, float alpha, float beta,
+               int trans_a, int trans_b, int relu, const char* op) {
+  OpScope scope(op);
+  if (!f32(a, op, "a") || !f32(b, op, "b") || !f32(out, op, "output")) return;
+  int M, N, K;
+  if (a->ndim == 2 && b->ndim == 2) {
+    M = (int)(trans_a ? a->shape[1] : a->shape[0]);
+    K = (int)(trans_a ? a->shape[0] : a->shape[1]);
+    N = (int)(trans_b ? b->shape[0] : b->shape[1]);
+    const int kb = (int)(trans_b ? b->shape[1] : b->shape[0]);
+    if (kb != K) {
+      fail(NNC_CUDA_ERR_INVALID, op, "inner dimensions differ (%d vs %d)", K, kb);
+      return;
+    }
+  } else if (a->ndim == 1 && b->ndim == 2) {
+    M = 1;
+    K = (int)a->shape[0];
+    N = (int)b->shape[1];
+    trans_a = 0;  // N = b->shape[1] even when trans_b is set, as ops.c:1779-1784
+  } else if (a->ndim == 2 && b->ndim == 1) {
+    M = (int)a->shape[0];
+    K = (int)a->shape[1];
+    N = 1;
+    trans_b = 0;
+  } else {
+    M = 1;
+    K = (int)numel(a);
+    N = (int)numel(b);
+    trans_a = 0;
+    trans_b = 0;
+  }
+  if (numel(out) < (int64_t)M * N || numel(a) < (int64_t)M * K || numel(b) < (int64_t)K * N) {
+    fail(NNC_CUDA_ERR_INVALID, op, "operand sizes do not cover M=%d N=%d K=%d", M, N, K);
+    return;
+  }
+  Problem p{};
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.batches = 1;
+  p.A = (const float*)a->data;
+  p.a_trans = trans_a != 0;
+  p.B = (const float*)b->data;
+  p.b_kmajor = trans_b != 0;
+  p.alpha = alpha;
+  p.beta = beta;
+  p.D = (float*)out->data;
+  p.relu = relu;
+  if (!set_c(p, c, M, N, op)) return;
+  run_problem(p, op);
+}
+
+// nnc_gemm_nt semantics (ops.c:1843-1886): B stored [N, K].
+void gemm_nt_impl(Tensor* a, Tensor* b, Tensor* c, Tensor* out, float alpha, float beta, int relu,
+                  const char* op) {
+  OpScope scope(op);
+  if (!f32(a, op, "a") || !f32(b, op, "b") || !f32(out, op, "output")) return;
+  int M, N, K;
+  if (a->ndim == 2 && b->ndim == 2) {
+    M = (int)a->shape[0];
+    K = (int)a->shape[1];
+    N = (int)b->shape[0];
+  } else if (a->ndim == 1 && b->ndim == 2) {
+    M = 1;
+    K = (int)a->shape[0];
+    N = (int)b->shape[0];
+  } else {
+    M = 1;
+    K = (int)numel(a);
+    N = (b->ndim == 2) ? (int)b->shape[0] : (int)numel(b);
+  }
+  if (numel(out) < (int64_t)M * N) {
+    fail(NNC_CUDA_ERR_INVALID, op, "output too small");
+    return;
+  }
+  Problem p{};
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.batches = 1;
+  p.A = (const float*)a->data;
+  p.B = (const float*)b->data;
+  p.b_kmajor = true;
+  p.alpha = alpha;
+  p.beta = beta;
+  p.D = (float*)out->data;
+  p.relu = relu;
+  if (!set_c(p, c, M, N, op)) return;
+  run_problem(p, op);
+}
+
+// nnc_matmul semantics (ops.c:1607-1730), optional bias (row broadcast) + relu.
+void matmul_impl(Tensor* a, Tensor* b, Tensor* bias, Tensor* out, int relu, const char* op) {
+  OpScope scope(op);
+  if (!f32(a, op, "a") || !f32(b, op, "b") || !f32(out, op, "output")) return;
+  Problem p{};
+  p.alpha = 1.0f;
+  p.beta = 1.0f;
+  p.A = (const float*)a->data;
+  p.B = (const float*)b->data;
+  p.D = (float*)out->data;
+  p.relu = relu;
+  p.batches = 1;
+  if (a->ndim == 2 && b->ndim == 2) {
+    p.M = (int)a->shape[0];
+    p.K = (int)a->shape[1];
+    p.N = (int)b->shape[1];
+  } else if (a->ndim == 1 && b->ndim == 2) {
+    p.M = 1;
+    p.K = (int)a->shape[0];
+    p.N = (int)b->shape[1];
+  } else if (a->ndim == 2 && b->ndim == 1) {
+    p.M = (int)a->shape[0];
+    p.K = (int)a->shape[1];
+    p.N = 1;
+  } else if (a->ndim >= 2 && b->ndim >= 2) {
+    const int od = out->ndim;
+    int64_t batch = 1;
+    for (int i = 0; i < od - 2; ++i) batch *= out->shape[i];
+    p.M = (int)out->shape[od - 2];
+    p.N = (int)out->shape[od - 1];
+    p.K = (int)a->shape[a->ndim - 1];
+    // Batch offsets exactly as ops.c:1686-1708 computes them: the offset of
+    // batch i in `a` is i * (numel(a) / (M_a * K)) elements — the number of
+    // matrices in a, not their size — and likewise for b unless b has fewer
+    // dims than the output (then offset 0). Output batches are dense (M * N).
+    p.a_bs = numel(a) / (a->shape[a->ndim - 2] * a->shape[a->ndim - 1]);
+    p.b_bs = (b->ndim < od) ? 0 : numel(b) / (b->shape[b->ndim - 2] * b->shape[b->ndim - 1]);
+    if (batch == 1) {
+      p.a_bs = 0;
+      p.b_bs = 0;
+    }
+    p.batches = (int)batch;
+    p.d_bs = (int64_t)p.M * p.N;
+  } else {
+    fail(NNC_CUDA_ERR_UNSUPPORTED, op, "unsupported ranks (%d, %d)", a->ndim, b->ndim);
+    return;
+  }
+  if (numel(out) < (int64_t)p.M * p.N * p.batches) {
+    fail(NNC_CUDA_ERR_INVALID, op, "output too small");
+    return;
+  }
+  p.b_kmajor = false;
+  p.C = nullptr;
+  p.c_mode = 0;
+  p.ldc = p.N;
+  if (bias) {
+    if (!f32(bias, op, "bias")) return;
+    if (numel(bias) < p.N) {
+      fail(NNC_CUDA_ERR_INVALID, op, "bias shorter than N");
+      return;
+    }
+    p.C = (const float*)bias->data;
+    p.c_mode = 1;
+  }
+  run_problem(p, op);
+}
+
+}  // namespace
+}  // namespace nnc
+
+using namespace nnc;
+
+extern "C" {
+
+void nnc_gemm(Tensor* a, Tensor* b, Tensor* c, Tensor* output, float alpha, float beta,
+              int trans_a, int trans_b) {
+  gemm_impl(a, b, c, output, alpha, beta, trans_a, trans_b, 0, "nnc_gemm");
+}
+void nnc_gemm_relu(Tensor* a, Tensor* b, Tensor* c, Tensor* output, float alpha, float beta,
+                   int trans_a, int trans_b) {
+  gemm_impl(a, b, c, output, alpha, beta, trans_a, trans_b, 1, "nnc_gemm_relu");
+}
+void nnc_gemm_nt(Tensor* a, Tensor* b, Tensor* c, Tensor* output, float alpha, float beta) {
+  gemm_nt_impl(a, b, c, output, alpha, beta, 0, "nnc_gemm_nt");
+}
+void nnc_gemm_nt_relu(Tensor* a, Tensor* b, Tensor* c, Tensor* output, float alpha, float beta) {
+  gemm_nt_impl(a, b, c, output, alpha, beta, 1, "nnc_gemm_nt_relu");
+}
+void nnc_matmul(Tensor* a, Tensor* b, Tensor* output) {
+  matmul_impl(a, b, nullptr, output, 0, "nnc_matmul");
+}
+void nnc_matmul_relu(Tensor* a, Tensor* b, Tensor* bias, Tensor* output) {
+  matmul_impl(a, b, bias, output, 1, "nnc_matmul_relu");
+}
+
+}  // extern "C"

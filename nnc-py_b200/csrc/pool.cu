@@ -1,0 +1,189 @@
+// 2-D max / average pooling (reference ops.c:316-461).
+//
+// Window semantics are the reference's: the window [o*stride - pad,
+// o*stride - pad + k) is clamped to the input, so padding never contributes;
+// only the top/left pad is passed and the output extent comes from
+// output->shape. Max keeps the first in-window value and replaces it only by
+// a strictly greater one; an empty window yields -3.402823e38f. Average sums
+// in row-major window order in fp32 and divides by the in-bounds count
+// (0 for an empty window). Both are bit-identical to the reference.
+//
+// Layouts: NCHW (untagged tensors) — one thread per output element, writes
+// coalesced along W; NHWC (NNC_CUDA_TAG_NHWC) — one thread per output pixel
+// and 4-channel group, 128-bit loads/stores along C.
+#include "common.cuh"
+
+namespace nnc {
+namespace {
+
+constexpr float kEmptyMax = -3.402823e38f;
+
+struct PoolGeom {
+  int N, C, H, W, OH, OW, kh, kw, sh, sw, ph, pw;
+};
+
+__device__ __forceinline__ void window(const PoolGeom& g, int oh, int ow, int& h0, int& h1,
+                                       int& w0, int& w1) {
+  h0 = oh * g.sh - g.ph;
+  w0 = ow * g.sw - g.pw;
+  h1 = h0 + g.kh;
+  w1 = w0 + g.kw;
+  h0 = h0 < 0 ? 0 : h0;
+  w0 = w0 < 0 ? 0 : w0;
+  h1 = h1 > g.H ? g.H : h1;
+  w1 = w1 > g.W ? g.W : w1;
+}
+
+template <bool MAX>
+__global__ void __launch_bounds__(256) pool_nchw_kernel(const float* __restrict__ in,
+                                                        float* __restrict__ out, PoolGeom g) {
+  const int64_t total = (int64_t)g.N * g.C * g.OH * g.OW;
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int ow = (int)(idx % g.OW);
+    const int oh = (int)((idx / g.OW) % g.OH);
+    const int64_t nc = idx / ((int64_t)g.OW * g.OH);
+    int h0, h1, w0, w1;
+    window(g, oh, ow, h0, h1, w0, w1);
+    const float* plane = in + nc * g.H * g.W;
+    if (MAX) {
+      float m = kEmptyMax;
+      bool has = false;
+      for (int h = h0; h < h1; ++h)
+        for (int w = w0; w < w1; ++w) {
+          const float v = plane[h * g.W + w];
+          if (!has || v > m) {
+            m = v;
+            has = true;
+          }
+        }
+      out[idx] = m;
+    } else {
+      float s = 0.0f;
+      int cnt = 0;
+      for (int h = h0; h < h1; ++h)
+        for (int w = w0; w < w1; ++w) {
+          s = __fadd_rn(s, plane[h * g.W + w]);
+          ++cnt;
+        }
+      out[idx] = cnt > 0 ? __fdiv_rn(s, (float)cnt) : 0.0f;
+    }
+  }
+}
+
+template <bool MAX, int V>
+__global__ void __launch_bounds__(256) pool_nhwc_kernel(const float* __restrict__ in,
+                                                        float* __restrict__ out, PoolGeom g) {
+  // V channels per thread (4 with 16-byte alignment, else 1).
+  const int cg = g.C / V;
+  const int64_t total = (int64_t)g.N * g.OH * g.OW * cg;
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int c = (int)(idx % cg) * V;
+    int64_t p = idx / cg;
+    const int ow = (int)(p % g.OW);
+    const int oh = (int)((p / g.OW) % g.OH);
+    const int n = (int)(p / ((int64_t)g.OW * g.OH));
+    int h0, h1, w0, w1;
+    window(g, oh, ow, h0, h1, w0, w1);
+    const float* img = in + (int64_t)n * g.H * g.W * g.C + c;
+    float acc[V];
+    bool has = false;
+    int cnt = 0;
+#pragma unroll
+    for (int j = 0; j < V; ++j) acc[j] = MAX ? kEmptyMax : 0.0f;
+    for (int h = h0; h < h1; ++h)
+      for (int w = w0; w < w1; ++w) {
+        const float* src = img + ((int64_t)h * g.W + w) * g.C;
+        float v[V];
+        if constexpr (V == 4) {
+          const float4 t = *reinterpret_cast<const float4*>(src);
+          v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+        } else {
+          v[0] = src[0];
+        }
+#pragma unroll
+        for (int j = 0; j < V; ++j) {
+          if (MAX) {
+            if (!has || v[j] > acc[j]) acc[j] = v[j];
+          } else {
+            acc[j] = __fadd_rn(acc[j], v[j]);
+          }
+        }
+        has = true;
+        ++cnt;
+      }
+    float* dst = out + p * g.C + c;
+#pragma unroll
+    for (int j = 0; j < V; ++j) {
+      if (!MAX) acc[j] = cnt > 0 ? __fdiv_rn(acc[j], (float)cnt) : 0.0f;
+    }
+    if constexpr (V == 4) {
+      *reinterpret_cast<float4*>(dst) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    } else {
+      dst[0] = acc[0];
+    }
+  }
+}
+
+template <bool MAX>
+void pool_impl(Tensor* input, Tensor* output, int kh, int kw, int sh, int sw, int ph, int pw,
+               const char* op) {
+  OpScope scope(op);
+  if (!valid_tensor(input, op, "input") || !valid_tensor(output, op, "output")) return;
+  if (input->ndim != 4 || output->ndim != 4) {
+    // The reference returns silently for non-4-D tensors (ops.c:332-334).
+    fail(NNC_CUDA_ERR_INVALID, op, "expected 4-D tensors");
+    return;
+  }
+  if (elem_type(input) != NNC_DTYPE_FLOAT32 || elem_type(output) != NNC_DTYPE_FLOAT32) {
+    fail(NNC_CUDA_ERR_UNSUPPORTED, op, "only float32 is supported");
+    return;
+  }
+  if (is_nhwc(input) != is_nhwc(output)) {
+    fail(NNC_CUDA_ERR_UNSUPPORTED, op, "input and output layouts differ");
+    return;
+  }
+  if (kh <= 0 || kw <= 0 || sh <= 0 || sw <= 0) {
+    fail(NNC_CUDA_ERR_INVALID, op, "kernel and stride must be positive");
+    return;
+  }
+  PoolGeom g{(int)input->shape[0],  (int)input->shape[1],  (int)input->shape[2],
+             (int)input->shape[3],  (int)output->shape[2], (int)output->shape[3],
+             kh, kw, sh, sw, ph, pw};
+  if (output->shape[0] != g.N || output->shape[1] != g.C) {
+    fail(NNC_CUDA_ERR_INVALID, op, "output N/C differ from the input");
+    return;
+  }
+  const int64_t total = (int64_t)g.N * g.C * g.OH * g.OW;
+  if (total == 0) return;
+  const float* pi = (const float*)input->data;
+  float* po = (float*)output->data;
+  if (!is_nhwc(input)) {
+    pool_nchw_kernel<MAX><<<grid_for(total, 256, 8), 256, 0, ctx().stream>>>(pi, po, g);
+  } else if (g.C % 4 == 0 && aligned16(pi) && aligned16(po)) {
+    pool_nhwc_kernel<MAX, 4><<<grid_for(total / 4, 256, 8), 256, 0, ctx().stream>>>(pi, po, g);
+  } else {
+    pool_nhwc_kernel<MAX, 1><<<grid_for(total, 256, 8), 256, 0, ctx().stream>>>(pi, po, g);
+  }
+  check_launch(op);
+}
+
+}  // namespace
+}  // namespace nnc
+
+extern "C" {
+
+void nnc_maxpool2d(Tensor* input, Tensor* output, int kernel_h, int kernel_w, int stride_h,
+                   int stride_w, int pad_h, int pad_w) {
+  nnc::pool_impl<true>(input, output, kernel_h, kernel_w, stride_h, stride_w, pad_h, pad_w,
+                       "nnc_maxpool2d");
+}
+
+void nnc_avgpool2d(Tensor* input, Tensor* output, int kernel_h, int kernel_w, int stride_h,
+                   int stride_w, int pad_h, int pad_w) {
+  nnc::pool_impl<false>(input, output, kernel_h, kernel_w, stride_h, stride_w, pad_h, pad_w,
+                        "nnc_avgpool2d");
+}
+
+}  // extern "C"

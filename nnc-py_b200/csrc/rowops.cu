@@ -1,0 +1,360 @@
+// Row-wise operators: softmax, layernorm, reducemean / reducesum.
+//
+// All three decompose the tensor as [outer, dim, inner] around `axis` exactly
+// like the reference (ops.c:260-310, :2095-2171, :1892-1989).
+//   inner == 1 : one CTA per row; the row is read once into registers (up to
+//                kMaxVPT values per thread), reduced with warp shuffles, and
+//                written once — 8 bytes of HBM traffic per element.
+//   inner  > 1 : one thread per (outer, inner) column walking `dim` with
+//                stride `inner`; consecutive threads read consecutive
+//                addresses, so every pass is coalesced.
+// Reductions accumulate in fp64 (the reference uses Kahan-compensated fp32
+// for reduce, plain fp32 for softmax/layernorm); results agree to within a
+// few fp32 ulps and the final roundings/divisions are the reference's.
+#include <math.h>
+
+#include "common.cuh"
+
+namespace nnc {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kMaxVPT = 32;  // registers per thread for a cached row (8192 floats)
+
+__device__ __forceinline__ double warp_sum(double v) {
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Block-wide reductions for kThreads threads; `red` holds kThreads/32 slots.
+__device__ double block_sum(double v, double* red) {
+  v = warp_sum(v);
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  __syncthreads();
+  if (lane == 0) red[wid] = v;
+  __syncthreads();
+  double t = (threadIdx.x < kThreads / 32) ? red[threadIdx.x] : 0.0;
+  if (wid == 0) t = warp_sum(t);
+  if (threadIdx.x == 0) red[0] = t;
+  __syncthreads();
+  return red[0];
+}
+__device__ float block_max(float v, float* red) {
+  v = warp_max(v);
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  __syncthreads();
+  if (lane == 0) red[wid] = v;
+  __syncthreads();
+  float t = (threadIdx.x < kThreads / 32) ? red[threadIdx.x] : -INFINITY;
+  if (wid == 0) t = warp_max(t);
+  if (threadIdx.x == 0) red[0] = t;
+  __syncthreads();
+  return red[0];
+}
+
+// ---------------------------------------------------------------- softmax --
+// Row kernel: per row max, sum of expf(x - max), out = expf(x - max) / sum
+// (ops.c:283-307). Values cached in registers when dim <= kThreads*kMaxVPT.
+__global__ void __launch_bounds__(kThreads) softmax_row_kernel(const float* __restrict__ in,
+                                                               float* __restrict__ out,
+                                                               int64_t rows, int64_t dim) {
+  __shared__ double red_d[kThreads / 32];
+  __shared__ float red_f[kThreads / 32];
+  const bool cached = dim <= (int64_t)kThreads * kMaxVPT;
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+    const float* x = in + row * dim;
+    float* y = out + row * dim;
+    float v[kMaxVPT];
+    float m = -INFINITY;
+    if (cached) {
+#pragma unroll
+      for (int k = 0; k < kMaxVPT; ++k) {
+        const int64_t i = threadIdx.x + (int64_t)k * kThreads;
+        v[k] = (i < dim) ? x[i] : -INFINITY;
+        m = (v[k] > m) ? v[k] : m;
+      }
+    } else {
+      for (int64_t i = threadIdx.x; i < dim; i += kThreads) m = (x[i] > m) ? x[i] : m;
+    }
+    m = block_max(m, red_f);
+    double s = 0.0;
+    if (cached) {
+#pragma unroll
+      for (int k = 0; k < kMaxVPT; ++k) {
+        const int64_t i = threadIdx.x + (int64_t)k * kThreads;
+        if (i < dim) {
+          v[k] = expf(v[k] - m);
+          s += (double)v[k];
+        }
+      }
+    } else {
+      for (int64_t i = threadIdx.x; i < dim; i += kThreads) s += (double)expf(x[i] - m);
+    }
+    const float sum = (float)block_sum(s, red_d);
+    if (cached) {
+#pragma unroll
+      for (int k = 0; k < kMaxVPT; ++k) {
+        const int64_t i = threadIdx.x + (int64_t)k * kThreads;
+        if (i < dim) y[i] = __fdiv_rn(v[k], sum);
+      }
+    } else {
+      for (int64_t i = threadIdx.x; i < dim; i += kThreads) y[i] = __fdiv_rn(expf(x[i] - m), sum);
+    }
+  }
+}
+
+// Strided kernel (inner > 1): one thread per (outer, inner) column.
+__global__ void __launch_bounds__(kThreads) softmax_col_kernel(const float* __restrict__ in,
+                                                               float* __restrict__ out,
+                                                               int64_t outer, int64_t dim,
+                                                               int64_t inner) {
+  const int64_t cols = outer * inner;
+  for (int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; c < cols;
+       c += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t o = c / inner, j = c % inner;
+    const float* x = in + o * dim * inner + j;
+    float* y = out + o * dim * inner + j;
+    float m = -INFINITY;
+    for (int64_t s = 0; s < dim; ++s) m = (x[s * inner] > m) ? x[s * inner] : m;
+    double acc = 0.0;
+    for (int64_t s = 0; s < dim; ++s) acc += (double)expf(x[s * inner] - m);
+    const float sum = (float)acc;
+    for (int64_t s = 0; s < dim; ++s) y[s * inner] = __fdiv_rn(expf(x[s * inner] - m), sum);
+  }
+}
+
+// -------------------------------------------------------------- layernorm --
+// Normalises each [norm, inner] slab (ops.c:2130-2168): mean, variance of
+// (x - mean), std = sqrtf(var + eps), y = scale[i] * ((x - mean) / std) + bias[i]
+// with scale/bias indexed by the axis coordinate i.
+__global__ void __launch_bounds__(kThreads) layernorm_kernel(
+    const float* __restrict__ in, const float* __restrict__ scale, const float* __restrict__ bias,
+    float* __restrict__ out, int64_t rows, int64_t norm, int64_t inner, float eps) {
+  __shared__ double red_d[kThreads / 32];
+  const int64_t len = norm * inner;
+  const bool cached = len <= (int64_t)kThreads * kMaxVPT;
+  const float inv_n = (float)len;
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+    const float* x = in + row * len;
+    float* y = out + row * len;
+    float v[kMaxVPT];
+    double s = 0.0;
+    if (cached) {
+#pragma unroll
+      for (int k = 0; k < kMaxVPT; ++k) {
+        const int64_t i = threadIdx.x + (int64_t)k * kThreads;
+        v[k] = (i < len) ? x[i] : 0.0f;
+        s += (double)v[k];
+      }
+    } else {
+      for (int64_t i = threadIdx.x; i < len; i += kThreads) s += (double)x[i];
+    }
+    const float mean = __fdiv_rn((float)block_sum(s, red_d), inv_n);
+    double q = 0.0;
+    if (cached) {
+#pragma unroll
+      for (int k = 0; k < kMaxVPT; ++k) {
+        const int64_t i = threadIdx.x + (int64_t)k * kThreads;
+        if (i < len) {
+          const float d = __fsub_rn(v[k], mean);
+          q += (double)__fmul_rn(d, d);
+        }
+      }
+    } else {
+      for (int64_t i = threadIdx.x; i < len; i += kThreads) {
+        const float d = __fsub_rn(x[i], mean);
+        q += (double)__fmul_rn(d, d);
+      }
+    }
+    const float var = __fdiv_rn((float)block_sum(q, red_d), inv_n);
+    const float sd = __fsqrt_rn(__fadd_rn(var, eps));
+    if (cached) {
+#pragma unroll
+      for (int k = 0; k < kMaxVPT; ++k) {
+        const int64_t i = threadIdx.x + (int64_t)k * kThreads;
+        if (i < len) {
+          const int64_t a = i / inner;
+          const float g = scale ? scale[a] : 1.0f;
+          const float b = bias ? bias[a] : 0.0f;
+          y[i] = __fadd_rn(__fmul_rn(g, __fdiv_rn(__fsub_rn(v[k], mean), sd)), b);
+        }
+      }
+    } else {
+      for (int64_t i = threadIdx.x; i < len; i += kThreads) {
+        const int64_t a = i / inner;
+        const float g = scale ? scale[a] : 1.0f;
+        const float b = bias ? bias[a] : 0.0f;
+        y[i] = __fadd_rn(__fmul_rn(g, __fdiv_rn(__fsub_rn(x[i], mean), sd)), b);
+      }
+    }
+  }
+}
+
+// ----------------------------------------------------------------- reduce --
+// Row kernel (inner == 1): fp64 accumulation of the row, out = (float)sum
+// (or (float)sum / (float)dim for the mean, ops.c:1927).
+__global__ void __launch_bounds__(kThreads) reduce_row_kernel(const float* __restrict__ in,
+                                                              float* __restrict__ out,
+                                                              int64_t rows, int64_t dim,
+                                                              int mean) {
+  __shared__ double red_d[kThreads / 32];
+  const bool vec = ((dim & 3) == 0) && ((((uintptr_t)in) & 15) == 0);
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+    double s = 0.0;
+    if (vec) {
+      const float4* x4 = reinterpret_cast<const float4*>(in + row * dim);
+      for (int64_t i = threadIdx.x; i < (dim >> 2); i += kThreads) {
+        const float4 t = x4[i];
+        s += (double)t.x + (double)t.y + (double)t.z + (double)t.w;
+      }
+    } else {
+      const float* x = in + row * dim;
+      for (int64_t i = threadIdx.x; i < dim; i += kThreads) s += (double)x[i];
+    }
+    s = block_sum(s, red_d);
+    if (threadIdx.x == 0) {
+      const float f = (float)s;
+      out[row] = mean ? __fdiv_rn(f, (float)dim) : f;
+    }
+  }
+}
+
+// Column kernel (inner > 1): the reference's Kahan loop verbatim per column,
+// so results are bit-identical to ops.c:1914-1925.
+__global__ void __launch_bounds__(kThreads) reduce_col_kernel(const float* __restrict__ in,
+                                                              float* __restrict__ out,
+                                                              int64_t outer, int64_t dim,
+                                                              int64_t inner, int mean) {
+  const int64_t cols = outer * inner;
+  for (int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; c < cols;
+       c += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t o = c / inner, j = c % inner;
+    const float* x = in + o * dim * inner + j;
+    float sum = 0.0f, comp = 0.0f;
+    for (int64_t r = 0; r < dim; ++r) {
+      const float yv = __fsub_rn(x[r * inner], comp);
+      const float t = __fadd_rn(sum, yv);
+      comp = __fsub_rn(__fsub_rn(t, sum), yv);
+      sum = t;
+    }
+    out[o * inner + j] = mean ? __fdiv_rn(sum, (float)dim) : sum;
+  }
+}
+
+bool decompose(const Tensor* t, int axis, int64_t* outer, int64_t* dim, int64_t* inner,
+               const char* op) {
+  int ax = axis < 0 ? axis + t->ndim : axis;
+  if (ax < 0 || ax >= t->ndim) {
+    fail(NNC_CUDA_ERR_INVALID, op, "axis %d out of range for ndim %d", axis, t->ndim);
+    return false;
+  }
+  *outer = 1;
+  for (int i = 0; i < ax; ++i) *outer *= t->shape[i];
+  *dim = t->shape[ax];
+  *inner = 1;
+  for (int i = ax + 1; i < t->ndim; ++i) *inner *= t->shape[i];
+  return true;
+}
+
+bool f32_plain(const Tensor* t, const char* op, const char* name) {
+  if (!valid_tensor(t, op, name)) return false;
+  if (elem_type(t) != NNC_DTYPE_FLOAT32 || tag_of(t) != 0) {
+    fail(NNC_CUDA_ERR_UNSUPPORTED, op, "%s: needs an untagged float32 tensor", name);
+    return false;
+  }
+  return true;
+}
+
+void reduce_impl(Tensor* in, Tensor* out, int axis, int mean, const char* op) {
+  OpScope scope(op);
+  if (!f32_plain(in, op, "input") || !f32_plain(out, op, "output")) return;
+  int64_t outer, dim, inner;
+  if (!decompose(in, axis, &outer, &dim, &inner, op)) return;
+  if (numel(out) != outer * inner) {
+    fail(NNC_CUDA_ERR_INVALID, op, "output has %lld elements, expected %lld",
+         (long long)numel(out), (long long)(outer * inner));
+    return;
+  }
+  if (outer * inner == 0) return;
+  const float* pi = (const float*)in->data;
+  float* po = (float*)out->data;
+  if (inner == 1) {
+    const int grid = (int)(outer < (int64_t)sm_count() * 16 ? outer : (int64_t)sm_count() * 16);
+    reduce_row_kernel<<<grid, kThreads, 0, ctx().stream>>>(pi, po, outer, dim, mean);
+  } else {
+    reduce_col_kernel<<<grid_for(outer * inner, kThreads, 8), kThreads, 0, ctx().stream>>>(
+        pi, po, outer, dim, inner, mean);
+  }
+  check_launch(op);
+}
+
+}  // namespace
+}  // namespace nnc
+
+using namespace nnc;
+
+extern "C" {
+
+void nnc_softmax(Tensor* input, Tensor* output, int axis) {
+  const char* op = "nnc_softmax";
+  OpScope scope(op);
+  if (!f32_plain(input, op, "input") || !f32_plain(output, op, "output")) return;
+  int64_t outer, dim, inner;
+  if (!decompose(input, axis, &outer, &dim, &inner, op)) return;
+  if (numel(output) < outer * dim * inner) {
+    fail(NNC_CUDA_ERR_INVALID, op, "output smaller than input");
+    return;
+  }
+  if (outer * dim * inner == 0) return;
+  const float* pi = (const float*)input->data;
+  float* po = (float*)output->data;
+  if (inner == 1) {
+    const int grid = (int)(outer < (int64_t)sm_count() * 8 ? outer : (int64_t)sm_count() * 8);
+    softmax_row_kernel<<<grid, kThreads, 0, ctx().stream>>>(pi, po, outer, dim);
+  } else {
+    softmax_col_kernel<<<grid_for(outer * inner, kThreads, 8), kThreads, 0, ctx().stream>>>(
+        pi, po, outer, dim, inner);
+  }
+  check_launch(op);
+}
+
+void nnc_layernorm(Tensor* input, Tensor* scale, Tensor* bias, Tensor* output, int axis,
+                   float epsilon) {
+  const char* op = "nnc_layernorm";
+  OpScope scope(op);
+  if (!f32_plain(input, op, "input") || !f32_plain(output, op, "output")) return;
+  if ((scale && !f32_plain(scale, op, "scale")) || (bias && !f32_plain(bias, op, "bias"))) return;
+  int64_t outer, norm, inner;
+  if (!decompose(input, axis, &outer, &norm, &inner, op)) return;
+  if (numel(output) < outer * norm * inner) {
+    fail(NNC_CUDA_ERR_INVALID, op, "output smaller than input");
+    return;
+  }
+  if ((scale && numel(scale) < norm) || (bias && numel(bias) < norm)) {
+    fail(NNC_CUDA_ERR_INVALID, op, "scale/bias shorter than the normalised axis (%lld)",
+         (long long)norm);
+    return;
+  }
+  if (outer * norm * inner == 0) return;
+  const int grid = (int)(outer < (int64_t)sm_count() * 8 ? outer : (int64_t)sm_count() * 8);
+  layernorm_kernel<<<grid, kThreads, 0, ctx().stream>>>(
+      (const float*)input->data, scale ? (const float*)scale->data : nullptr,
+      bias ? (const float*)bias->data : nullptr, (float*)output->data, outer, norm, inner, epsilon);
+  check_launch(op);
+}
+
+void nnc_reducemean(Tensor* input, Tensor* output, int axis, int keepdims) {
+  (void)keepdims;  // the output layout is identical with or without the kept axis
+  reduce_impl(input, output, axis, 1, "nnc_reducemean");
+}
+
+void nnc_reducesum(Tensor* input, Tensor* output, int axis, int keepdims) {
+  (void)keepdims;
+  reduce_impl(input, output, axis, 0, "nnc_reducesum");
+}
+
+}  // extern "C"

@@ -1,0 +1,266 @@
+// Execution context of libnnc_cuda.so: per-thread device/stream/precision and
+// sticky status, per-device error word, scratch memory, per-op tracing.
+#include <stdarg.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <mutex>
+#include <vector>
+
+#include "common.cuh"
+
+namespace nnc {
+
+namespace {
+constexpr int kMaxDevices = 64;
+
+struct DeviceState {
+  bool ready = false;
+  int* error_word = nullptr;  // device int, 0 = ok
+  int sms = 148;
+};
+DeviceState g_dev[kMaxDevices];
+std::mutex g_dev_mu;
+
+struct Workspace {
+  void* ptr[kMaxDevices] = {};
+  size_t cap[kMaxDevices] = {};
+  void* user_ptr[kMaxDevices] = {};
+  size_t user_cap[kMaxDevices] = {};
+};
+thread_local Workspace t_ws;
+
+struct TraceRec {
+  const char* name;
+  cudaEvent_t start, stop;
+};
+thread_local std::vector<TraceRec> t_trace;
+int g_trace_on = -1;  // -1: read NNC_CUDA_TRACE on first use
+
+bool trace_on() {
+  if (g_trace_on < 0) {
+    const char* e = getenv("NNC_CUDA_TRACE");
+    g_trace_on = (e && e[0] == '1') ? 1 : 0;
+  }
+  return g_trace_on == 1;
+}
+
+DeviceState& dev_state(int dev) {
+  DeviceState& s = g_dev[dev];
+  if (!s.ready) {
+    std::lock_guard<std::mutex> lock(g_dev_mu);
+    if (!s.ready) {
+      int prev = 0;
+      cudaGetDevice(&prev);
+      cudaSetDevice(dev);
+      cudaDeviceGetAttribute(&s.sms, cudaDevAttrMultiProcessorCount, dev);
+      if (cudaMalloc(&s.error_word, sizeof(int)) == cudaSuccess) {
+        cudaMemset(s.error_word, 0, sizeof(int));
+      } else {
+        s.error_word = nullptr;
+      }
+      cudaSetDevice(prev);
+      s.ready = true;
+    }
+  }
+  return s;
+}
+}  // namespace
+
+ThreadCtx& ctx() {
+  thread_local ThreadCtx c;
+  return c;
+}
+
+void fail(int code, const char* op, const char* fmt, ...) {
+  ThreadCtx& c = ctx();
+  char buf[400];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  if (c.status == NNC_CUDA_OK) {
+    c.status = code;
+    snprintf(c.message, sizeof(c.message), "%s: %s", op, buf);
+  }
+  fprintf(stderr, "%s: %s\n", op, buf);
+  fflush(stderr);
+}
+
+bool check_cuda(cudaError_t err, const char* op, const char* what) {
+  if (err == cudaSuccess) return true;
+  fail(err == cudaErrorMemoryAllocation ? NNC_CUDA_ERR_NOMEM : NNC_CUDA_ERR_LAUNCH, op,
+       "%s failed: %s", what, cudaGetErrorString(err));
+  return false;
+}
+
+int* device_error_word() { return dev_state(ctx().device).error_word; }
+int sm_count() { return dev_state(ctx().device).sms; }
+
+int grid_for(int64_t work_items, int threads, int max_ctas_per_sm) {
+  int64_t want = cdiv(work_items, threads);
+  int64_t cap = (int64_t)sm_count() * max_ctas_per_sm;
+  if (want < 1) want = 1;
+  return (int)(want < cap ? want : cap);
+}
+
+bool valid_tensor(const Tensor* t, const char* op, const char* name) {
+  if (!t) {
+    fail(NNC_CUDA_ERR_INVALID, op, "NULL tensor pointer (%s)", name);
+    return false;
+  }
+  if (!t->shape && t->ndim > 0) {
+    fail(NNC_CUDA_ERR_INVALID, op, "NULL shape pointer (%s)", name);
+    return false;
+  }
+  if (t->ndim < 0 || t->ndim > 8) {
+    fail(NNC_CUDA_ERR_INVALID, op, "ndim %d out of range (%s)", t->ndim, name);
+    return false;
+  }
+  if (!t->data && numel(t) > 0) {
+    fail(NNC_CUDA_ERR_INVALID, op, "NULL data pointer (%s)", name);
+    return false;
+  }
+  return true;
+}
+
+void* workspace(size_t bytes, const char* op) {
+  ThreadCtx& c = ctx();
+  const int d = c.device;
+  if (bytes == 0) bytes = 256;
+  if (t_ws.user_ptr[d]) {
+    if (bytes <= t_ws.user_cap[d]) return t_ws.user_ptr[d];
+    fail(NNC_CUDA_ERR_NOMEM, op, "needs %zu bytes of workspace, caller supplied %zu", bytes,
+         t_ws.user_cap[d]);
+    return nullptr;
+  }
+  if (bytes <= t_ws.cap[d]) return t_ws.ptr[d];
+  // Grow stream-ordered: earlier work on this stream that still reads the
+  // old buffer completes before the free takes effect.
+  size_t want = bytes + bytes / 4;
+  want = (want + (2u << 20) - 1) & ~size_t((2u << 20) - 1);
+  if (t_ws.ptr[d]) {
+    cudaFreeAsync(t_ws.ptr[d], c.stream);
+    t_ws.ptr[d] = nullptr;
+    t_ws.cap[d] = 0;
+  }
+  void* p = nullptr;
+  if (!check_cuda(cudaMallocAsync(&p, want, c.stream), op, "workspace allocation")) return nullptr;
+  t_ws.ptr[d] = p;
+  t_ws.cap[d] = want;
+  return p;
+}
+
+OpScope::OpScope(const char* name) : name_(name), slot_(-1) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess && dev >= 0 && dev < kMaxDevices) ctx().device = dev;
+  if (!trace_on()) return;
+  TraceRec r{name, nullptr, nullptr};
+  cudaEventCreate(&r.start);
+  cudaEventCreate(&r.stop);
+  cudaEventRecord(r.start, ctx().stream);
+  t_trace.push_back(r);
+  slot_ = (int)t_trace.size() - 1;
+}
+
+OpScope::~OpScope() {
+  if (slot_ >= 0 && slot_ < (int)t_trace.size()) cudaEventRecord(t_trace[slot_].stop, ctx().stream);
+}
+
+}  // namespace nnc
+
+using namespace nnc;
+
+extern "C" {
+
+int nnc_cuda_init(int device) {
+  int count = 0;
+  if (!check_cuda(cudaGetDeviceCount(&count), "nnc_cuda_init", "cudaGetDeviceCount")) return ctx().status;
+  if (device < 0 || device >= count || device >= 64) {
+    fail(NNC_CUDA_ERR_INVALID, "nnc_cuda_init", "device %d out of range (%d devices)", device, count);
+    return NNC_CUDA_ERR_INVALID;
+  }
+  if (!check_cuda(cudaSetDevice(device), "nnc_cuda_init", "cudaSetDevice")) return ctx().status;
+  ctx().device = device;
+  DeviceState& s = dev_state(device);
+  if (!s.error_word) {
+    fail(NNC_CUDA_ERR_NOMEM, "nnc_cuda_init", "could not allocate the device error word");
+    return NNC_CUDA_ERR_NOMEM;
+  }
+  return NNC_CUDA_OK;
+}
+
+int nnc_cuda_set_device(int device) { return nnc_cuda_init(device); }
+int nnc_cuda_get_device(void) { return ctx().device; }
+void nnc_cuda_set_stream(void* stream) { ctx().stream = (cudaStream_t)stream; }
+void* nnc_cuda_get_stream(void) { return (void*)ctx().stream; }
+
+int nnc_cuda_sync(void) {
+  check_cuda(cudaStreamSynchronize(ctx().stream), "nnc_cuda_sync", "cudaStreamSynchronize");
+  return ctx().status;
+}
+
+int nnc_cuda_get_last_error(void) { return ctx().status; }
+const char* nnc_cuda_get_last_error_string(void) { return ctx().message; }
+void nnc_cuda_clear_error(void) {
+  ctx().status = NNC_CUDA_OK;
+  ctx().message[0] = 0;
+}
+
+int nnc_cuda_check_device_status(void) {
+  int* w = device_error_word();
+  if (!w) return ctx().status;
+  int h = 0;
+  if (!check_cuda(cudaStreamSynchronize(ctx().stream), "nnc_cuda_check_device_status", "sync"))
+    return ctx().status;
+  if (!check_cuda(cudaMemcpy(&h, w, sizeof(int), cudaMemcpyDeviceToHost),
+                  "nnc_cuda_check_device_status", "read error word"))
+    return ctx().status;
+  if (h != 0) {
+    cudaMemset(w, 0, sizeof(int));
+    fail(NNC_CUDA_ERR_DEVICE_TIMEOUT, "nnc_cuda_check_device_status",
+         "a kernel's bounded wait expired (code %d)", h);
+    return NNC_CUDA_ERR_DEVICE_TIMEOUT;
+  }
+  return NNC_CUDA_OK;
+}
+
+void nnc_cuda_set_precision(int mode) {
+  ctx().precision = (mode == NNC_CUDA_PRECISION_3XTF32) ? NNC_CUDA_PRECISION_3XTF32
+                                                         : NNC_CUDA_PRECISION_TF32;
+}
+int nnc_cuda_get_precision(void) { return ctx().precision; }
+
+int nnc_cuda_set_workspace(void* device_ptr, size_t bytes) {
+  const int d = ctx().device;
+  t_ws.user_ptr[d] = bytes ? device_ptr : nullptr;
+  t_ws.user_cap[d] = device_ptr ? bytes : 0;
+  return NNC_CUDA_OK;
+}
+
+size_t nnc_cuda_get_workspace_capacity(void) {
+  const int d = ctx().device;
+  return t_ws.user_ptr[d] ? t_ws.user_cap[d] : t_ws.cap[d];
+}
+
+void nnc_cuda_trace_enable(int on) { g_trace_on = on ? 1 : 0; }
+
+int nnc_cuda_trace_dump(void) {
+  cudaStreamSynchronize(ctx().stream);
+  if (t_trace.empty()) return 0;
+  const int n = (int)t_trace.size();
+  cudaEvent_t t0 = t_trace[0].start;
+  for (int i = 0; i < n; ++i) {
+    float s = 0.f, e = 0.f;
+    cudaEventElapsedTime(&s, t0, t_trace[i].start);
+    cudaEventElapsedTime(&e, t0, t_trace[i].stop);
+    fprintf(stderr, "[nnc_cuda_trace] #%d op=%s start_us=%.1f end_us=%.1f dur_us=%.1f\n", i,
+            t_trace[i].name, s * 1e3, e * 1e3, (e - s) * 1e3);
+    cudaEventDestroy(t_trace[i].start);
+    cudaEventDestroy(t_trace[i].stop);
+  }
+  t_trace.clear();
+  return n;
+}
+
+}  // extern "C"

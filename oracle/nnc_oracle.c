@@ -1,0 +1,521 @@
+/*
+ * nnc_oracle.c — CPU restatement of nnc-py's operator semantics.
+ *
+ * TEST INFRASTRUCTURE ONLY. This library is the checker for the CUDA
+ * operator library: only tests/, __graft_entry__.smoke() and bench.py's
+ * cpu_baseline leg may load it. Nothing in the product path (libnnc_cuda.so,
+ * the nnc_cuda package, generated model code) links or calls it.
+ *
+ * Each function restates the algorithm of the reference implementation
+ * (nnc-py runtime/x86/ops.c, cited per function): same accumulation types,
+ * same loop/summation order where it affects rounding, same broadcast and
+ * window rules, same quirks. It exports the reference's symbol names so the
+ * parity tests drive it exactly like the CUDA library. It is pinned against
+ * the reference itself (oracle/_ref/libref_ops.so built from the reference
+ * sources) and against golden vectors in tests/golden/.
+ *
+ * Build: make -C oracle   (gcc -O2 -ffp-contract=off, no FMA contraction).
+ */
+#include <math.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include "nnc_ops.h"
+
+static int64_t count_of(const Tensor* t) {
+    int64_t n = 1;
+    for (int d = 0; d < t->ndim; ++d) n *= t->shape[d];
+    return n;
+}
+
+/* Splits t around `axis` (negative counts from the end) into
+ * [outer, t->shape[axis], inner]. */
+static int around_axis(const Tensor* t, int axis, int64_t* outer, int64_t* mid, int64_t* inner) {
+    int a = axis < 0 ? axis + t->ndim : axis;
+    *outer = 1;
+    *inner = 1;
+    for (int d = 0; d < a; ++d) *outer *= t->shape[d];
+    for (int d = a + 1; d < t->ndim; ++d) *inner *= t->shape[d];
+    *mid = t->shape[a];
+    return a;
+}
+
+/* ---------------------------------------------------------------------------
+ * Binary element-wise with the reference's modular suffix broadcast
+ * (ops.c:82-224, :3233-3346). The first min(n, na, nb) outputs combine
+ * a[i] and b[i]; when exactly one operand has n elements the rest of the
+ * output indexes the other operand modulo its length.
+ * ------------------------------------------------------------------------- */
+typedef float (*binary_fn)(float, float);
+
+static float f_add(float x, float y) { return x + y; }
+static float f_sub(float x, float y) { return x - y; }
+static float f_mul(float x, float y) { return x * y; }
+static float f_div(float x, float y) { return x / y; }
+static float f_add_relu(float x, float y) {
+    float s = x + y;
+    return s > 0.0f ? s : 0.0f;
+}
+static float f_add_sigmoid(float x, float y) {
+    float s = x + y;
+    return 1.0f / (1.0f + expf(-s));
+}
+
+static void broadcast_apply(Tensor* a, Tensor* b, Tensor* out, binary_fn f) {
+    const int64_t n = count_of(out), na = count_of(a), nb = count_of(b);
+    const float* x = (const float*)a->data;
+    const float* y = (const float*)b->data;
+    float* z = (float*)out->data;
+    int64_t head = n;
+    if (na < head) head = na;
+    if (nb < head) head = nb;
+    for (int64_t i = 0; i < head; ++i) z[i] = f(x[i], y[i]);
+    if (nb == n && na < n) {
+        for (int64_t i = head; i < n; ++i) z[i] = f(x[i % na], y[i]);
+    } else if (na == n && nb < n) {
+        for (int64_t i = head; i < n; ++i) z[i] = f(x[i], y[i % nb]);
+    }
+}
+
+void nnc_add(Tensor* a, Tensor* b, Tensor* out) { broadcast_apply(a, b, out, f_add); }
+void nnc_sub(Tensor* a, Tensor* b, Tensor* out) { broadcast_apply(a, b, out, f_sub); }
+void nnc_mul(Tensor* a, Tensor* b, Tensor* out) { broadcast_apply(a, b, out, f_mul); }
+void nnc_div(Tensor* a, Tensor* b, Tensor* out) { broadcast_apply(a, b, out, f_div); }
+void nnc_add_relu(Tensor* a, Tensor* b, Tensor* out) { broadcast_apply(a, b, out, f_add_relu); }
+void nnc_add_sigmoid(Tensor* a, Tensor* b, Tensor* out) { broadcast_apply(a, b, out, f_add_sigmoid); }
+
+/* ---------------------------------------------------------------------------
+ * Unary element-wise over numel(output) (ops.c:230-258, :2253-2262,
+ * :2434-2515), with libm expf/tanhf/sqrtf/logf as in the reference.
+ * fmaxf/fminf are spelled out because their signed-zero result depends on
+ * argument order, which gcc may swap: the compiled reference returns the
+ * non-NaN operand for a NaN and the SECOND argument for equal operands, with
+ * relu's fmaxf(0.0f, x) emitted as a call on (x, 0) — so relu(-0) = +0.
+ * ------------------------------------------------------------------------- */
+static float max_second_on_tie(float x, float y) {
+    if (isnan(x)) return y;
+    if (isnan(y)) return x;
+    return x > y ? x : y;
+}
+static float min_second_on_tie(float x, float y) {
+    if (isnan(x)) return y;
+    if (isnan(y)) return x;
+    return x < y ? x : y;
+}
+
+typedef float (*unary_fn)(float, float, float);
+
+static float u_relu(float v, float lo, float hi) { (void)lo; (void)hi; return v > 0.0f ? v : 0.0f; }
+static float u_sigmoid(float v, float lo, float hi) { (void)lo; (void)hi; return 1.0f / (1.0f + expf(-v)); }
+static float u_tanh(float v, float lo, float hi) { (void)lo; (void)hi; return tanhf(v); }
+static float u_clip(float v, float lo, float hi) { return min_second_on_tie(max_second_on_tie(v, lo), hi); }
+static float u_sqrt(float v, float lo, float hi) { (void)lo; (void)hi; return v >= 0.0f ? sqrtf(v) : NAN; }
+static float u_pow2(float v, float lo, float hi) { (void)lo; (void)hi; return v * v; }
+static float u_exp(float v, float lo, float hi) { (void)lo; (void)hi; return expf(v); }
+static float u_log(float v, float lo, float hi) { (void)lo; (void)hi; return v > 0.0f ? logf(v) : NAN; }
+static float u_abs(float v, float lo, float hi) { (void)lo; (void)hi; return fabsf(v); }
+static float u_neg(float v, float lo, float hi) { (void)lo; (void)hi; return -v; }
+
+static void map_unary(Tensor* in, Tensor* out, unary_fn f, float lo, float hi) {
+    const int64_t n = count_of(out);
+    const float* x = (const float*)in->data;
+    float* z = (float*)out->data;
+    for (int64_t i = 0; i < n; ++i) z[i] = f(x[i], lo, hi);
+}
+
+void nnc_relu(Tensor* in, Tensor* out) { map_unary(in, out, u_relu, 0, 0); }
+void nnc_sigmoid(Tensor* in, Tensor* out) { map_unary(in, out, u_sigmoid, 0, 0); }
+void nnc_tanh(Tensor* in, Tensor* out) { map_unary(in, out, u_tanh, 0, 0); }
+void nnc_clip(Tensor* in, Tensor* out, float lo, float hi) { map_unary(in, out, u_clip, lo, hi); }
+void nnc_sqrt(Tensor* in, Tensor* out) { map_unary(in, out, u_sqrt, 0, 0); }
+void nnc_pow(Tensor* in, Tensor* out) { map_unary(in, out, u_pow2, 0, 0); }
+void nnc_exp(Tensor* in, Tensor* out) { map_unary(in, out, u_exp, 0, 0); }
+void nnc_log(Tensor* in, Tensor* out) { map_unary(in, out, u_log, 0, 0); }
+void nnc_abs(Tensor* in, Tensor* out) { map_unary(in, out, u_abs, 0, 0); }
+void nnc_neg(Tensor* in, Tensor* out) { map_unary(in, out, u_neg, 0, 0); }
+
+/* ---------------------------------------------------------------------------
+ * Softmax (ops.c:260-310): per [outer, :, inner] column — running max with
+ * '>', sequential fp32 sum of expf(x - max), then expf(x - max) / sum.
+ * ------------------------------------------------------------------------- */
+void nnc_softmax(Tensor* in, Tensor* out, int axis) {
+    int64_t outer, dim, inner;
+    around_axis(in, axis, &outer, &dim, &inner);
+    const float* x = (const float*)in->data;
+    float* z = (float*)out->data;
+    for (int64_t o = 0; o < outer; ++o) {
+        for (int64_t j = 0; j < inner; ++j) {
+            const int64_t base = o * dim * inner + j;
+            float m = -INFINITY;
+            for (int64_t s = 0; s < dim; ++s)
+                if (x[base + s * inner] > m) m = x[base + s * inner];
+            float total = 0.0f;
+            for (int64_t s = 0; s < dim; ++s) total += expf(x[base + s * inner] - m);
+            for (int64_t s = 0; s < dim; ++s) z[base + s * inner] = expf(x[base + s * inner] - m) / total;
+        }
+    }
+}
+
+/* ---------------------------------------------------------------------------
+ * LayerNorm (ops.c:2095-2171): each [norm, inner] slab — sequential fp32
+ * mean and variance, std = sqrtf(var + eps), y = g[i] * ((x - mean) / std)
+ * + b[i] with g/b indexed by the axis coordinate (NULL: 1 / 0).
+ * ------------------------------------------------------------------------- */
+void nnc_layernorm(Tensor* in, Tensor* scale, Tensor* bias, Tensor* out, int axis, float eps) {
+    int64_t outer, norm, inner;
+    around_axis(in, axis, &outer, &norm, &inner);
+    const float* x = (const float*)in->data;
+    const float* g = scale ? (const float*)scale->data : NULL;
+    const float* bb = bias ? (const float*)bias->data : NULL;
+    float* z = (float*)out->data;
+    const int64_t len = norm * inner;
+    for (int64_t o = 0; o < outer; ++o) {
+        const float* row = x + o * len;
+        float* dst = z + o * len;
+        float mean = 0.0f;
+        for (int64_t i = 0; i < len; ++i) mean += row[i];
+        mean /= (float)len;
+        float var = 0.0f;
+        for (int64_t i = 0; i < len; ++i) {
+            float d = row[i] - mean;
+            var += d * d;
+        }
+        var /= (float)len;
+        const float sd = sqrtf(var + eps);
+        for (int64_t i = 0; i < norm; ++i) {
+            const float gi = g ? g[i] : 1.0f;
+            const float bi = bb ? bb[i] : 0.0f;
+            for (int64_t j = 0; j < inner; ++j) {
+                float t = (row[i * inner + j] - mean) / sd;
+                dst[i * inner + j] = gi * t + bi;
+            }
+        }
+    }
+}
+
+/* ---------------------------------------------------------------------------
+ * ReduceSum / ReduceMean over one axis (ops.c:1892-1989): Kahan-compensated
+ * fp32 sum per output, mean = sum / (float)dim; keepdims does not change the
+ * output's linear layout.
+ * ------------------------------------------------------------------------- */
+static void reduce_axis(Tensor* in, Tensor* out, int axis, int mean) {
+    int64_t outer, dim, inner;
+    around_axis(in, axis, &outer, &dim, &inner);
+    const float* x = (const float*)in->data;
+    float* z = (float*)out->data;
+    for (int64_t o = 0; o < outer; ++o) {
+        for (int64_t j = 0; j < inner; ++j) {
+            float acc = 0.0f, lost = 0.0f;
+            for (int64_t r = 0; r < dim; ++r) {
+                float y = x[(o * dim + r) * inner + j] - lost;
+                float t = acc + y;
+                lost = (t - acc) - y;
+                acc = t;
+            }
+            z[o * inner + j] = mean ? acc / (float)dim : acc;
+        }
+    }
+}
+
+void nnc_reducemean(Tensor* in, Tensor* out, int axis, int keepdims) { (void)keepdims; reduce_axis(in, out, axis, 1); }
+void nnc_reducesum(Tensor* in, Tensor* out, int axis, int keepdims) { (void)keepdims; reduce_axis(in, out, axis, 0); }
+
+/* ---------------------------------------------------------------------------
+ * Pooling (ops.c:316-461): window start o*stride - pad, clamped to the input;
+ * output extent from output->shape. Max: first value, then strictly greater;
+ * empty window -3.402823e38f. Avg: sequential fp32 sum / in-bounds count.
+ * ------------------------------------------------------------------------- */
+static void pool2d(Tensor* in, Tensor* out, int kh, int kw, int sh, int sw, int ph, int pw, int is_max) {
+    if (!in || !out || !in->data || !out->data || in->ndim != 4 || out->ndim != 4) return;
+    const int N = (int)in->shape[0], C = (int)in->shape[1], H = (int)in->shape[2], W = (int)in->shape[3];
+    const int OH = (int)out->shape[2], OW = (int)out->shape[3];
+    const float* x = (const float*)in->data;
+    float* z = (float*)out->data;
+    for (int64_t nc = 0; nc < (int64_t)N * C; ++nc) {
+        const float* plane = x + nc * H * W;
+        for (int oh = 0; oh < OH; ++oh) {
+            for (int ow = 0; ow < OW; ++ow) {
+                int h0 = oh * sh - ph, w0 = ow * sw - pw;
+                int h1 = h0 + kh, w1 = w0 + kw;
+                if (h0 < 0) h0 = 0;
+                if (w0 < 0) w0 = 0;
+                if (h1 > H) h1 = H;
+                if (w1 > W) w1 = W;
+                float acc = is_max ? -3.402823e38f : 0.0f;
+                int seen = 0;
+                for (int h = h0; h < h1; ++h) {
+                    for (int w = w0; w < w1; ++w) {
+                        const float v = plane[h * W + w];
+                        if (is_max) {
+                            if (!seen || v > acc) acc = v;
+                        } else {
+                            acc += v;
+                        }
+                        ++seen;
+                    }
+                }
+                if (!is_max) acc = seen > 0 ? acc / seen : 0.0f;
+                z[(nc * OH + oh) * OW + ow] = acc;
+            }
+        }
+    }
+}
+
+void nnc_maxpool2d(Tensor* in, Tensor* out, int kh, int kw, int sh, int sw, int ph, int pw) { pool2d(in, out, kh, kw, sh, sw, ph, pw, 1); }
+void nnc_avgpool2d(Tensor* in, Tensor* out, int kh, int kw, int sh, int sw, int ph, int pw) { pool2d(in, out, kh, kw, sh, sw, ph, pw, 0); }
+
+/* ---------------------------------------------------------------------------
+ * Convolution (ops.c:720-1050 and its specialisations :1052-1447): for each
+ * output, fp64 sum starting at the bias, over (c_in, kh, kw) with
+ * out-of-range taps skipped, one rounding to fp32, then the activation.
+ * ------------------------------------------------------------------------- */
+enum { ACT_NONE = 0, ACT_RELU = 1, ACT_SIGMOID = 2 };
+
+static float activate(float v, int act) {
+    if (act == ACT_RELU) return v > 0.0f ? v : 0.0f;
+    if (act == ACT_SIGMOID) return 1.0f / (1.0f + expf(-v));
+    return v;
+}
+
+static void conv2d(Tensor* in, Tensor* wt, Tensor* bias, Tensor* out, int kh, int kw, int sh, int sw,
+                   int ph, int pw, int act) {
+    if (!in || !wt || !out || !in->data || !wt->data || !out->data) return;
+    const int N = (int)in->shape[0], C = (int)in->shape[1], H = (int)in->shape[2], W = (int)in->shape[3];
+    const int CO = (int)wt->shape[0], OH = (int)out->shape[2], OW = (int)out->shape[3];
+    const float* x = (const float*)in->data;
+    const float* w = (const float*)wt->data;
+    const float* b = bias ? (const float*)bias->data : NULL;
+    float* z = (float*)out->data;
+    for (int n = 0; n < N; ++n) {
+        for (int co = 0; co < CO; ++co) {
+            for (int oh = 0; oh < OH; ++oh) {
+                for (int ow = 0; ow < OW; ++ow) {
+                    double acc = b ? (double)b[co] : 0.0;
+                    for (int ci = 0; ci < C; ++ci) {
+                        const float* xp = x + ((int64_t)n * C + ci) * H * W;
+                        const float* wp = w + ((int64_t)co * C + ci) * kh * kw;
+                        for (int i = 0; i < kh; ++i) {
+                            const int h = oh * sh - ph + i;
+                            if (h < 0 || h >= H) continue;
+                            for (int j = 0; j < kw; ++j) {
+                                const int ww = ow * sw - pw + j;
+                                if (ww < 0 || ww >= W) continue;
+                                acc += (double)xp[h * W + ww] * (double)wp[i * kw + j];
+                            }
+                        }
+                    }
+                    z[(((int64_t)n * CO + co) * OH + oh) * OW + ow] = activate((float)acc, act);
+                }
+            }
+        }
+    }
+}
+
+void nnc_conv(Tensor* i, Tensor* w, Tensor* b, Tensor* o, int kh, int kw, int sh, int sw, int ph, int pw) { conv2d(i, w, b, o, kh, kw, sh, sw, ph, pw, ACT_NONE); }
+void nnc_conv_relu(Tensor* i, Tensor* w, Tensor* b, Tensor* o, int kh, int kw, int sh, int sw, int ph, int pw) { conv2d(i, w, b, o, kh, kw, sh, sw, ph, pw, ACT_RELU); }
+void nnc_conv_sigmoid(Tensor* i, Tensor* w, Tensor* b, Tensor* o, int kh, int kw, int sh, int sw, int ph, int pw) { conv2d(i, w, b, o, kh, kw, sh, sw, ph, pw, ACT_SIGMOID); }
+void nnc_conv1x1(Tensor* i, Tensor* w, Tensor* b, Tensor* o, int sh, int sw, int ph, int pw) { conv2d(i, w, b, o, 1, 1, sh, sw, ph, pw, ACT_NONE); }
+void nnc_conv_relu1x1(Tensor* i, Tensor* w, Tensor* b, Tensor* o, int sh, int sw, int ph, int pw) { conv2d(i, w, b, o, 1, 1, sh, sw, ph, pw, ACT_RELU); }
+void nnc_conv3x3_s1(Tensor* i, Tensor* w, Tensor* b, Tensor* o) { conv2d(i, w, b, o, 3, 3, 1, 1, 1, 1, ACT_NONE); }
+void nnc_conv_relu3x3_s1(Tensor* i, Tensor* w, Tensor* b, Tensor* o) { conv2d(i, w, b, o, 3, 3, 1, 1, 1, 1, ACT_RELU); }
+void nnc_conv7x7_s2(Tensor* i, Tensor* w, Tensor* b, Tensor* o) { conv2d(i, w, b, o, 7, 7, 2, 2, 3, 3, ACT_NONE); }
+void nnc_conv_relu7x7_s2(Tensor* i, Tensor* w, Tensor* b, Tensor* o) { conv2d(i, w, b, o, 7, 7, 2, 2, 3, 3, ACT_RELU); }
+
+/* The fused residual group is the reference composition nnc_conv followed
+ * by nnc_add_relu (ops.c:1449, :3233). */
+void nnc_conv_add_relu(Tensor* i, Tensor* w, Tensor* b, Tensor* r, Tensor* o, int kh, int kw, int sh,
+                       int sw, int ph, int pw) {
+    conv2d(i, w, b, o, kh, kw, sh, sw, ph, pw, ACT_NONE);
+    nnc_add_relu(o, r, o);
+}
+void nnc_conv_add_relu1x1(Tensor* i, Tensor* w, Tensor* b, Tensor* r, Tensor* o, int sh, int sw, int ph, int pw) {
+    nnc_conv_add_relu(i, w, b, r, o, 1, 1, sh, sw, ph, pw);
+}
+void nnc_conv_add_relu3x3_s1(Tensor* i, Tensor* w, Tensor* b, Tensor* r, Tensor* o) {
+    nnc_conv_add_relu(i, w, b, r, o, 3, 3, 1, 1, 1, 1);
+}
+
+/* ---------------------------------------------------------------------------
+ * Gemm (ops.c:1732-1841) and Gemm-NT (ops.c:1843-1886): fp64 dot product,
+ * times alpha, plus beta * c ([N] when 1-D, else [M, N]), one rounding.
+ * ------------------------------------------------------------------------- */
+static void gemm_core(const float* A, const float* B, const Tensor* c, float* D, int M, int N, int K,
+                      int ta, int tb, float alpha, float beta, int relu) {
+    const float* C = c ? (const float*)c->data : NULL;
+    for (int i = 0; i < M; ++i) {
+        for (int j = 0; j < N; ++j) {
+            double acc = 0.0;
+            for (int k = 0; k < K; ++k) {
+                const float av = ta ? A[(int64_t)k * M + i] : A[(int64_t)i * K + k];
+                const float bv = tb ? B[(int64_t)j * K + k] : B[(int64_t)k * N + j];
+                acc += (double)av * (double)bv;
+            }
+            acc *= (double)alpha;
+            if (C) acc += (double)beta * (double)(c->ndim == 1 ? C[j] : C[(int64_t)i * N + j]);
+            float v = (float)acc;
+            if (relu) v = v > 0.0f ? v : 0.0f;
+            D[(int64_t)i * N + j] = v;
+        }
+    }
+}
+
+static void gemm_dispatch(Tensor* a, Tensor* b, Tensor* c, Tensor* out, float alpha, float beta, int ta,
+                          int tb, int relu) {
+    int M, N, K;
+    if (a->ndim == 2 && b->ndim == 2) {
+        M = (int)(ta ? a->shape[1] : a->shape[0]);
+        K = (int)(ta ? a->shape[0] : a->shape[1]);
+        N = (int)(tb ? b->shape[0] : b->shape[1]);
+    } else if (a->ndim == 1 && b->ndim == 2) {
+        M = 1; K = (int)a->shape[0]; N = (int)b->shape[1]; ta = 0;
+    } else if (a->ndim == 2 && b->ndim == 1) {
+        M = (int)a->shape[0]; K = (int)a->shape[1]; N = 1; tb = 0;
+    } else {
+        /* The reference's flattened fallback leaves ta/tb as passed. */
+        M = 1; K = (int)count_of(a); N = (int)count_of(b);
+    }
+    gemm_core((const float*)a->data, (const float*)b->data, c, (float*)out->data, M, N, K, ta, tb, alpha, beta, relu);
+}
+
+void nnc_gemm(Tensor* a, Tensor* b, Tensor* c, Tensor* o, float alpha, float beta, int ta, int tb) { gemm_dispatch(a, b, c, o, alpha, beta, ta, tb, 0); }
+void nnc_gemm_relu(Tensor* a, Tensor* b, Tensor* c, Tensor* o, float alpha, float beta, int ta, int tb) { gemm_dispatch(a, b, c, o, alpha, beta, ta, tb, 1); }
+
+static void gemm_nt_dispatch(Tensor* a, Tensor* b, Tensor* c, Tensor* out, float alpha, float beta, int relu) {
+    int M, N, K;
+    if (a->ndim == 2 && b->ndim == 2) {
+        M = (int)a->shape[0]; K = (int)a->shape[1]; N = (int)b->shape[0];
+    } else if (a->ndim == 1 && b->ndim == 2) {
+        M = 1; K = (int)a->shape[0]; N = (int)b->shape[0];
+    } else {
+        M = 1; K = (int)count_of(a); N = b->ndim == 2 ? (int)b->shape[0] : (int)count_of(b);
+    }
+    gemm_core((const float*)a->data, (const float*)b->data, c, (float*)out->data, M, N, K, 0, 1, alpha, beta, relu);
+}
+
+void nnc_gemm_nt(Tensor* a, Tensor* b, Tensor* c, Tensor* o, float alpha, float beta) { gemm_nt_dispatch(a, b, c, o, alpha, beta, 0); }
+void nnc_gemm_nt_relu(Tensor* a, Tensor* b, Tensor* c, Tensor* o, float alpha, float beta) { gemm_nt_dispatch(a, b, c, o, alpha, beta, 1); }
+
+/* ---------------------------------------------------------------------------
+ * MatMul (ops.c:1607-1730): Kahan-compensated fp32 dot products. For the
+ * batched case the reference offsets batch i of `a` by i * (numel(a) /
+ * (rows * cols)) elements — the matrix count, not the matrix size — and the
+ * same for `b` unless b has fewer dims than the output (offset 0); output
+ * batches are dense. That rule is restated here unchanged.
+ * ------------------------------------------------------------------------- */
+static float kahan_dot(const float* a, int64_t sa, const float* b, int64_t sb, int K) {
+    float acc = 0.0f, lost = 0.0f;
+    for (int k = 0; k < K; ++k) {
+        float y = a[k * sa] * b[k * sb] - lost;
+        float t = acc + y;
+        lost = (t - acc) - y;
+        acc = t;
+    }
+    return acc;
+}
+
+static void matmul_any(Tensor* a, Tensor* b, const Tensor* bias, Tensor* out, int relu) {
+    const float* A = (const float*)a->data;
+    const float* B = (const float*)b->data;
+    const float* bs = bias ? (const float*)bias->data : NULL;
+    float* D = (float*)out->data;
+    int64_t batches = 1, a_off = 0, b_off = 0;
+    int M, N, K;
+    if (a->ndim == 2 && b->ndim == 2) {
+        M = (int)a->shape[0]; K = (int)a->shape[1]; N = (int)b->shape[1];
+    } else if (a->ndim == 1 && b->ndim == 2) {
+        M = 1; K = (int)a->shape[0]; N = (int)b->shape[1];
+    } else if (a->ndim == 2 && b->ndim == 1) {
+        M = (int)a->shape[0]; K = (int)a->shape[1]; N = 1;
+    } else if (a->ndim >= 2 && b->ndim >= 2) {
+        const int od = out->ndim;
+        for (int d = 0; d < od - 2; ++d) batches *= out->shape[d];
+        M = (int)out->shape[od - 2];
+        N = (int)out->shape[od - 1];
+        K = (int)a->shape[a->ndim - 1];
+        a_off = count_of(a) / (a->shape[a->ndim - 2] * a->shape[a->ndim - 1]);
+        b_off = b->ndim < od ? 0 : count_of(b) / (b->shape[b->ndim - 2] * b->shape[b->ndim - 1]);
+    } else {
+        return;
+    }
+    for (int64_t bi = 0; bi < batches; ++bi) {
+        const float* Ab = A + bi * a_off;
+        const float* Bb = B + bi * b_off;
+        float* Db = D + bi * (int64_t)M * N;
+        for (int i = 0; i < M; ++i) {
+            for (int j = 0; j < N; ++j) {
+                float v = kahan_dot(Ab + (int64_t)i * K, 1, Bb + j, N, K);
+                if (bs) v += bs[j];
+                if (relu) v = v > 0.0f ? v : 0.0f;
+                Db[(int64_t)i * N + j] = v;
+            }
+        }
+    }
+}
+
+void nnc_matmul(Tensor* a, Tensor* b, Tensor* out) { matmul_any(a, b, NULL, out, 0); }
+/* The symbol nnc-py's CEmitter emits for FUSED_MATMUL_RELU
+ * (codegen/c_emitter.py:1143-1171), absent from the reference's ops.c:
+ * restated as relu(matmul(a, b) + bias). */
+void nnc_matmul_relu(Tensor* a, Tensor* b, Tensor* bias, Tensor* out) { matmul_any(a, b, bias, out, 1); }
+
+/* ---------------------------------------------------------------------------
+ * Data movement (ops.c:1510-1601, :1995-2086, :2173-2251).
+ * ------------------------------------------------------------------------- */
+static void copy_prefix(Tensor* in, Tensor* out) {
+    const int64_t n = count_of(out);
+    memmove(out->data, in->data, (size_t)n * sizeof(float));
+}
+void nnc_reshape(Tensor* in, Tensor* out, int64_t* shape, int ndim) { (void)shape; (void)ndim; copy_prefix(in, out); }
+void nnc_flatten(Tensor* in, Tensor* out, int axis) { (void)axis; copy_prefix(in, out); }
+void nnc_squeeze(Tensor* in, Tensor* out, int axis) { (void)axis; copy_prefix(in, out); }
+void nnc_unsqueeze(Tensor* in, Tensor* out, int axis) { (void)axis; copy_prefix(in, out); }
+void nnc_identity(Tensor* in, Tensor* out) {
+    int64_t n = count_of(out), m = count_of(in);
+    memmove(out->data, in->data, (size_t)(n < m ? n : m) * sizeof(float));
+}
+
+void nnc_transpose(Tensor* in, Tensor* out, int64_t* perm, int ndim) {
+    int64_t p[8], in_stride[8], dims[8];
+    for (int d = 0; d < ndim; ++d) p[d] = perm ? perm[d] : ndim - 1 - d;
+    in_stride[ndim - 1] = 1;
+    for (int d = ndim - 2; d >= 0; --d) in_stride[d] = in_stride[d + 1] * in->shape[d + 1];
+    for (int d = 0; d < ndim; ++d) dims[d] = out->shape[d];
+    const float* x = (const float*)in->data;
+    float* z = (float*)out->data;
+    const int64_t n = count_of(out);
+    for (int64_t o = 0; o < n; ++o) {
+        int64_t rem = o, src = 0;
+        for (int d = ndim - 1; d >= 0; --d) {
+            src += (rem % dims[d]) * in_stride[p[d]];
+            rem /= dims[d];
+        }
+        z[o] = x[src];
+    }
+}
+
+void nnc_concat(Tensor** inputs, Tensor* out, int num, int axis) {
+    int64_t outer, odim, inner;
+    const int a = around_axis(out, axis, &outer, &odim, &inner);
+    const size_t es = out->dtype == NNC_DTYPE_INT64 ? 8 : 4;
+    int64_t offset = 0;
+    for (int k = 0; k < num; ++k) {
+        const int64_t d = inputs[k]->shape[a];
+        for (int64_t o = 0; o < outer; ++o)
+            memcpy((char*)out->data + (size_t)((o * odim + offset) * inner) * es,
+                   (const char*)inputs[k]->data + (size_t)(o * d * inner) * es, (size_t)(d * inner) * es);
+        offset += d;
+    }
+}
+
+void nnc_split(Tensor* in, Tensor** outputs, int num, int axis) {
+    int64_t outer, dim, inner;
+    around_axis(in, axis, &outer, &dim, &inner);
+    const int64_t part = dim / num; /* equal parts only */
+    const size_t es = in->dtype == NNC_DTYPE_INT64 ? 8 : 4;
+    for (int k = 0; k < num; ++k)
+        for (int64_t o = 0; o < outer; ++o)
+            memcpy((char*)outputs[k]->data + (size_t)(o * part * inner) * es,
+                   (const char*)in->data + (size_t)((o * dim + k * part) * inner) * es, (size_t)(part * inner) * es);
+}

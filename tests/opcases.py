@@ -1,0 +1,492 @@
+"""Operator cases shared by the oracle pin tests, the golden-fixture
+generator and the GPU parity tests.
+
+A case is a JSON-able dict::
+
+    {"name": ..., "op": "nnc_conv", "tol": "exact" | "tc" | <rtol float>,
+     "args": [arg, ...]}
+
+with arguments
+    {"k": "t", "n": <array name>}            input tensor
+    {"k": "o", "n": <name>, "shape": [...]}  output tensor (pre-filled 7.0)
+    {"k": "null"}                            NULL tensor
+    {"k": "i", "v": int} / {"k": "f", "v": float}
+    {"k": "perm", "v": [..] | None}          int64_t* (NULL when None)
+    {"k": "tl", "n": [names]}                Tensor** of inputs
+    {"k": "ol", "n": [names], "shape": [[..], ..]}  Tensor** of outputs
+
+and the input arrays in a dict {name: np.ndarray}. The same case runs on
+any library exporting the reference's nnc_* symbols over host memory
+(oracle, compiled reference) via :func:`run_host`, or on the CUDA library
+via :func:`run_cuda`.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import zlib
+
+import numpy as np
+
+from nnc_cuda import lib as L
+from nnc_cuda import tensor as T
+
+SENTINEL = 7.0
+
+
+# ----------------------------------------------------------------- running --
+def _outputs(case):
+    outs = []
+    for a in case["args"]:
+        if a["k"] == "o":
+            outs.append((a["n"], a["shape"], a.get("dtype", "float32")))
+        elif a["k"] == "ol":
+            for n, s in zip(a["n"], a["shape"]):
+                outs.append((n, s, a.get("dtype", "float32")))
+    return outs
+
+
+def _scalar(a):
+    if a["k"] == "i":
+        return ctypes.c_int(int(a["v"]))
+    if a["k"] == "f":
+        return ctypes.c_float(float(a["v"]))
+    raise KeyError(a["k"])
+
+
+def run_host(so, case, arrays):
+    """Runs `case` on a host-memory library; returns {output name: array}."""
+    keep = []
+    bufs = {n: np.ascontiguousarray(v).copy() for n, v in arrays.items()}
+    for n, s, dt in _outputs(case):
+        bufs[n] = np.full(s, SENTINEL, dtype=dt)
+    cargs = []
+    for a in case["args"]:
+        k = a["k"]
+        if k in ("t", "o"):
+            r = T.from_numpy(bufs[a["n"]])
+            keep.append(r)
+            cargs.append(r.ptr)
+        elif k == "null":
+            cargs.append(None)
+        elif k in ("i", "f"):
+            cargs.append(_scalar(a))
+        elif k == "perm":
+            if a["v"] is None:
+                cargs.append(None)
+            else:
+                arr = (ctypes.c_int64 * len(a["v"]))(*a["v"])
+                keep.append(arr)
+                cargs.append(ctypes.cast(arr, ctypes.POINTER(ctypes.c_int64)))
+        elif k in ("tl", "ol"):
+            refs = [T.from_numpy(bufs[n]) for n in a["n"]]
+            keep.extend(refs)
+            arr = T.tensor_array(refs)
+            keep.append(arr)
+            cargs.append(arr)
+        else:
+            raise KeyError(k)
+    getattr(so, case["op"])(*cargs)
+    return {n: bufs[n] for n, _, _ in _outputs(case)}
+
+
+def run_cuda(so, case, arrays, nhwc=()):
+    """Runs `case` on libnnc_cuda.so with device buffers.
+
+    Names in `nhwc` are 4-D tensors passed channels-last with the
+    NNC_CUDA_TAG_NHWC tag (logical NCHW shape kept); their results are
+    converted back to NCHW.
+    """
+    import torch
+
+    keep = []
+    dev = {}
+
+    def to_dev(name, a):
+        t = torch.from_numpy(np.ascontiguousarray(a)).cuda()
+        if name in nhwc:
+            t = t.permute(0, 2, 3, 1).contiguous()
+        return t
+
+    for n, v in arrays.items():
+        dev[n] = to_dev(n, v)
+    for n, s, dt in _outputs(case):
+        dev[n] = to_dev(n, np.full(s, SENTINEL, dtype=dt))
+
+    def ref(name):
+        t = dev[name]
+        if name in nhwc:
+            shape = (t.shape[0], t.shape[3], t.shape[1], t.shape[2])
+            return T.from_torch(t, tag=L.TAG_NHWC, shape=shape)
+        return T.from_torch(t)
+
+    cargs = []
+    for a in case["args"]:
+        k = a["k"]
+        if k in ("t", "o"):
+            r = ref(a["n"])
+            keep.append(r)
+            cargs.append(r.ptr)
+        elif k == "null":
+            cargs.append(None)
+        elif k in ("i", "f"):
+            cargs.append(_scalar(a))
+        elif k == "perm":
+            if a["v"] is None:
+                cargs.append(None)
+            else:
+                arr = (ctypes.c_int64 * len(a["v"]))(*a["v"])
+                keep.append(arr)
+                cargs.append(ctypes.cast(arr, ctypes.POINTER(ctypes.c_int64)))
+        elif k in ("tl", "ol"):
+            refs = [ref(n) for n in a["n"]]
+            keep.extend(refs)
+            arr = T.tensor_array(refs)
+            keep.append(arr)
+            cargs.append(arr)
+        else:
+            raise KeyError(k)
+    so.nnc_cuda_set_stream(ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    getattr(so, case["op"])(*cargs)
+    torch.cuda.synchronize()
+    status = so.nnc_cuda_get_last_error()
+    assert status == 0, so.nnc_cuda_get_last_error_string().decode()
+    out = {}
+    for n, _, _ in _outputs(case):
+        t = dev[n]
+        if n in nhwc:
+            t = t.permute(0, 3, 1, 2).contiguous()
+        out[n] = t.cpu().numpy()
+    return out
+
+
+# ------------------------------------------------------------- comparing --
+def assert_close(got, want, tol, what=""):
+    """tol: "exact" (bitwise, NaN payloads included) or a float rtol applied
+    normwise: |got - want| <= rtol * (|want| + max|want|), NaNs in the same
+    places."""
+    assert got.shape == want.shape, f"{what}: shape {got.shape} vs {want.shape}"
+    if tol == "exact":
+        g = got.view(np.uint32 if got.dtype == np.float32 else np.uint64)
+        w = want.view(np.uint32 if want.dtype == np.float32 else np.uint64)
+        bad = np.flatnonzero(g != w)
+        assert bad.size == 0, (
+            f"{what}: {bad.size} of {g.size} differ; first at {bad[0]}: "
+            f"got {got.flat[bad[0]]!r} want {want.flat[bad[0]]!r}"
+        )
+        return
+    gn, wn = np.isnan(got), np.isnan(want)
+    assert np.array_equal(gn, wn), f"{what}: NaN positions differ"
+    g = np.where(gn, 0, got).astype(np.float64)
+    w = np.where(wn, 0, want).astype(np.float64)
+    scale = float(np.max(np.abs(w))) if w.size else 0.0
+    err = np.abs(g - w)
+    lim = tol * (np.abs(w) + scale)
+    bad = np.flatnonzero(err > lim)
+    assert bad.size == 0, (
+        f"{what}: {bad.size} of {g.size} exceed rtol {tol} (normwise); worst rel "
+        f"{float(np.max(err) / max(scale, 1e-30)):.3g}; first at {bad[0]}: "
+        f"got {got.flat[bad[0]]!r} want {want.flat[bad[0]]!r}"
+    )
+
+
+# Tolerances of the tensor-core contractions (normwise rtol, see assert_close).
+TC_RTOL = {0: 2e-3, 1: 1e-5}  # NNC_CUDA_PRECISION_TF32, _3XTF32
+
+
+# --------------------------------------------------------- seeded cases --
+def rng_for(name: str) -> np.random.Generator:
+    return np.random.default_rng(zlib.crc32(name.encode()))
+
+
+def _t(n):
+    return {"k": "t", "n": n}
+
+
+def _o(n, shape, dtype="float32"):
+    return {"k": "o", "n": n, "shape": list(shape), "dtype": dtype}
+
+
+NULL = {"k": "null"}
+
+
+def _i(v):
+    return {"k": "i", "v": int(v)}
+
+
+def _f(v):
+    return {"k": "f", "v": float(v)}
+
+
+EDGE = np.array(
+    [0.0, -0.0, 1.0, -1.0, np.nan, -np.nan, np.inf, -np.inf, 3.4e38, -3.4e38, 1e-40, -1e-40,
+     0.5, -2.5, 88.7, -88.7, 1e-8, 7.0, -7.0, 20.0],
+    dtype=np.float32,
+)
+
+
+def conv_out(h, k, s, p):
+    return (h + 2 * p - k) // s + 1
+
+
+def seeded_cases():
+    """(case, arrays) pairs: small seeded cases per hot-path op."""
+    out = []
+
+    def add(case, arrays):
+        out.append((case, {k: np.asarray(v, dtype=v.dtype) for k, v in arrays.items()}))
+
+    # --- binary element-wise, incl. every broadcast branch of ops.c:82-118
+    for op in ("nnc_add", "nnc_sub", "nnc_mul", "nnc_div", "nnc_add_relu", "nnc_add_sigmoid"):
+        tol = 2e-6 if op == "nnc_add_sigmoid" else "exact"
+        for tag, sa, sb, so in (
+            ("same", (3, 5, 7), (3, 5, 7), (3, 5, 7)),
+            ("bscalar", (4, 33), (1,), (4, 33)),
+            ("ascalar", (1,), (4, 33), (4, 33)),
+            ("bsuffix", (6, 8, 12), (12,), (6, 8, 12)),
+            ("asuffix", (10,), (7, 10), (7, 10)),
+            ("bodd", (5, 7), (7,), (5, 7)),
+            ("partial", (6,), (4,), (10,)),
+        ):
+            name = f"{op}_{tag}"
+            r = rng_for(name)
+            a = r.standard_normal(sa).astype(np.float32)
+            b = r.standard_normal(sb).astype(np.float32)
+            if op == "nnc_div":
+                b = np.where(np.abs(b) < 0.05, 0.5, b).astype(np.float32)
+            add({"name": name, "op": op, "tol": tol, "args": [_t("a"), _t("b"), _o("out", so)]},
+                {"a": a, "b": b})
+        name = f"{op}_edge"
+        a = np.tile(EDGE, 4)
+        b = np.repeat(EDGE, 4)
+        add({"name": name, "op": op, "tol": "exact" if tol == "exact" else tol,
+             "args": [_t("a"), _t("b"), _o("out", a.shape)]}, {"a": a, "b": b})
+
+    # --- unary
+    for op, tol in (("nnc_relu", "exact"), ("nnc_sigmoid", 2e-6), ("nnc_tanh", 2e-6),
+                    ("nnc_sqrt", "exact"), ("nnc_pow", "exact"), ("nnc_exp", 2e-6),
+                    ("nnc_log", 2e-6), ("nnc_abs", "exact"), ("nnc_neg", "exact")):
+        for tag, shape in (("vec", (1027,)), ("mat", (17, 19))):
+            name = f"{op}_{tag}"
+            r = rng_for(name)
+            x = (r.standard_normal(shape) * 3).astype(np.float32)
+            add({"name": name, "op": op, "tol": tol, "args": [_t("x"), _o("out", shape)]}, {"x": x})
+        add({"name": f"{op}_edge", "op": op, "tol": tol, "args": [_t("x"), _o("out", EDGE.shape)]},
+            {"x": EDGE.copy()})
+    for lo, hi in ((-1.0, 1.0), (0.0, 6.0), (-3.402823e38, 3.402823e38)):
+        name = f"nnc_clip_{lo:g}_{hi:g}"
+        r = rng_for(name)
+        x = np.concatenate([r.standard_normal(500).astype(np.float32) * 4, EDGE])
+        add({"name": name, "op": "nnc_clip", "tol": "exact",
+             "args": [_t("x"), _o("out", x.shape), _f(lo), _f(hi)]}, {"x": x})
+
+    # --- softmax / layernorm / reduce
+    for tag, shape, axis in (("last", (37, 129), -1), ("axis0", (5, 6, 7), 0),
+                             ("mid", (4, 9, 6), 1), ("wide", (3, 9000), 1), ("ten", (2, 10), 1)):
+        name = f"nnc_softmax_{tag}"
+        r = rng_for(name)
+        x = (r.standard_normal(shape) * 2).astype(np.float32)
+        add({"name": name, "op": "nnc_softmax", "tol": 2e-6,
+             "args": [_t("x"), _o("out", shape), _i(axis)]}, {"x": x})
+    for tag, shape, axis, with_params in (("last", (33, 300), -1, True), ("slab", (4, 6, 5), 1, True),
+                                          ("noparams", (8, 64), -1, False), ("wide", (3, 10000), -1, True)):
+        name = f"nnc_layernorm_{tag}"
+        r = rng_for(name)
+        x = r.standard_normal(shape).astype(np.float32)
+        norm = shape[axis]
+        arrays = {"x": x}
+        args = [_t("x")]
+        if with_params:
+            arrays["g"] = r.uniform(0.5, 1.5, norm).astype(np.float32)
+            arrays["b"] = r.uniform(-0.1, 0.1, norm).astype(np.float32)
+            args += [_t("g"), _t("b")]
+        else:
+            args += [NULL, NULL]
+        args += [_o("out", shape), _i(axis), _f(1e-5)]
+        add({"name": name, "op": "nnc_layernorm", "tol": 1e-5, "args": args}, arrays)
+    for op in ("nnc_reducesum", "nnc_reducemean"):
+        for tag, shape, axis, keep, tol in (("last", (17, 301), -1, 1, 1e-6), ("lastnk", (9, 64), 1, 0, 1e-6),
+                                            ("axis0", (9, 8, 7), 0, 1, "exact"), ("mid", (3, 50, 4), 1, 0, "exact")):
+            name = f"{op}_{tag}"
+            r = rng_for(name)
+            x = r.standard_normal(shape).astype(np.float32)
+            oshape = list(shape)
+            if keep:
+                oshape[axis] = 1
+            else:
+                oshape.pop(axis)
+            add({"name": name, "op": op, "tol": tol,
+                 "args": [_t("x"), _o("out", oshape), _i(axis), _i(keep)]}, {"x": x})
+
+    # --- pooling
+    for op in ("nnc_maxpool2d", "nnc_avgpool2d"):
+        for tag, shape, k, s, p in (("k3s2p1", (2, 3, 11, 13), 3, 2, 1), ("k2s2", (2, 6, 28, 28), 2, 2, 0),
+                                    ("global7", (2, 8, 7, 7), 7, 7, 0), ("empty", (1, 1, 2, 2), 1, 1, 4),
+                                    ("k3s1p1", (1, 4, 6, 5), 3, 1, 1)):
+            name = f"{op}_{tag}"
+            r = rng_for(name)
+            x = r.standard_normal(shape).astype(np.float32)
+            if tag == "k3s2p1":
+                x.flat[::17] = np.nan
+            oh, ow = conv_out(shape[2], k, s, p), conv_out(shape[3], k, s, p)
+            add({"name": name, "op": op, "tol": "exact",
+                 "args": [_t("x"), _o("out", (shape[0], shape[1], oh, ow)), _i(k), _i(k), _i(s), _i(s), _i(p), _i(p)]},
+                {"x": x})
+
+    # --- convolution (tensor-core tolerance)
+    for tag, n, c, h, w, co, k, s, p, bias in (
+        ("k3s1p1", 2, 5, 9, 11, 7, 3, 1, 1, True),
+        ("k3s2p1", 2, 8, 12, 10, 16, 3, 2, 1, True),
+        ("k1s2", 2, 32, 8, 8, 40, 1, 2, 0, True),
+        ("k5p0", 3, 1, 32, 32, 6, 5, 1, 0, True),
+        ("k7s2p3", 1, 3, 23, 23, 8, 7, 2, 3, True),
+        ("c64", 2, 64, 8, 8, 64, 3, 1, 1, False),
+        ("c130", 1, 32, 6, 6, 130, 3, 1, 1, True),
+    ):
+        for op in ("nnc_conv", "nnc_conv_relu"):
+            name = f"{op}_{tag}"
+            r = rng_for(name)
+            x = r.standard_normal((n, c, h, w)).astype(np.float32)
+            wt = (r.standard_normal((co, c, k, k)) / np.sqrt(c * k * k)).astype(np.float32)
+            arrays = {"x": x, "w": wt}
+            if bias:
+                arrays["b"] = r.uniform(-0.1, 0.1, co).astype(np.float32)
+            oh, ow = conv_out(h, k, s, p), conv_out(w, k, s, p)
+            add({"name": name, "op": op, "tol": "tc",
+                 "args": [_t("x"), _t("w"), _t("b") if bias else NULL, _o("out", (n, co, oh, ow)),
+                          _i(k), _i(k), _i(s), _i(s), _i(p), _i(p)]}, arrays)
+    for op, k, s, p, extra in (("nnc_conv3x3_s1", 3, 1, 1, []), ("nnc_conv_relu3x3_s1", 3, 1, 1, []),
+                               ("nnc_conv7x7_s2", 7, 2, 3, []), ("nnc_conv_relu7x7_s2", 7, 2, 3, []),
+                               ("nnc_conv1x1", 1, 2, 0, [2, 2, 0, 0]), ("nnc_conv_relu1x1", 1, 1, 0, [1, 1, 0, 0])):
+        name = f"{op}_seeded"
+        r = rng_for(name)
+        c, h, co = (3, 30, 16) if k == 7 else (24, 10, 20)
+        x = r.standard_normal((2, c, h, h)).astype(np.float32)
+        wt = (r.standard_normal((co, c, k, k)) / np.sqrt(c * k * k)).astype(np.float32)
+        b = r.uniform(-0.1, 0.1, co).astype(np.float32)
+        oh = conv_out(h, k, s, p)
+        add({"name": name, "op": op, "tol": "tc",
+             "args": [_t("x"), _t("w"), _t("b"), _o("out", (2, co, oh, oh))] + [_i(v) for v in extra]},
+            {"x": x, "w": wt, "b": b})
+    name = "nnc_conv_sigmoid_seeded"
+    r = rng_for(name)
+    x = r.standard_normal((2, 6, 9, 9)).astype(np.float32)
+    wt = (r.standard_normal((10, 6, 3, 3)) / 7).astype(np.float32)
+    add({"name": name, "op": "nnc_conv_sigmoid", "tol": "tc",
+         "args": [_t("x"), _t("w"), NULL, _o("out", (2, 10, 9, 9)), _i(3), _i(3), _i(1), _i(1), _i(1), _i(1)]},
+        {"x": x, "w": wt})
+
+    # --- gemm / gemm_nt / matmul
+    for ta in (0, 1):
+        for tb in (0, 1):
+            for cmode in ("none", "row", "full"):
+                name = f"nnc_gemm_t{ta}{tb}_{cmode}"
+                r = rng_for(name)
+                M, N, K = 70, 50, 36
+                a = r.standard_normal((K, M) if ta else (M, K)).astype(np.float32)
+                b = r.standard_normal((N, K) if tb else (K, N)).astype(np.float32)
+                arrays = {"a": a, "b": b}
+                cargs = NULL
+                if cmode != "none":
+                    arrays["c"] = r.standard_normal((N,) if cmode == "row" else (M, N)).astype(np.float32)
+                    cargs = _t("c")
+                add({"name": name, "op": "nnc_gemm", "tol": "tc",
+                     "args": [_t("a"), _t("b"), cargs, _o("out", (M, N)), _f(0.75), _f(-1.25), _i(ta), _i(tb)]},
+                    arrays)
+    for tag, M, N, K in (("tc", 200, 160, 96), ("oddk", 130, 70, 57), ("small", 5, 3, 4)):
+        name = f"nnc_gemm_nt_{tag}"
+        r = rng_for(name)
+        a = r.standard_normal((M, K)).astype(np.float32)
+        b = r.standard_normal((N, K)).astype(np.float32)
+        c = r.standard_normal((N,)).astype(np.float32)
+        add({"name": name, "op": "nnc_gemm_nt", "tol": "tc",
+             "args": [_t("a"), _t("b"), _t("c"), _o("out", (M, N)), _f(1.0), _f(1.0)]}, {"a": a, "b": b, "c": c})
+    for tag, sa, sb, so in (("2d", (96, 64), (64, 80), (96, 80)), ("vecmat", (40,), (40, 24), (24,)),
+                            ("matvec", (24, 40), (40,), (24,)), ("batched", (2, 3, 4, 5), (2, 3, 5, 6), (2, 3, 4, 6)),
+                            ("bcast", (3, 64, 32), (32, 48), (3, 64, 48)), ("b1", (1, 128, 64), (64, 72), (1, 128, 72))):
+        name = f"nnc_matmul_{tag}"
+        r = rng_for(name)
+        a = r.standard_normal(sa).astype(np.float32)
+        b = r.standard_normal(sb).astype(np.float32)
+        add({"name": name, "op": "nnc_matmul", "tol": "tc", "args": [_t("a"), _t("b"), _o("out", so)]},
+            {"a": a, "b": b})
+
+    # --- data movement
+    for tag, shape, perm in (("2d", (5, 7), (1, 0)), ("3d", (2, 3, 4), (1, 0, 2)), ("3dlast", (4, 5, 6), (0, 2, 1)),
+                             ("null", (3, 4, 5), None), ("heads", (2, 8, 4, 16), (0, 2, 1, 3)),
+                             ("4dgen", (2, 3, 5, 7), (3, 1, 0, 2))):
+        name = f"nnc_transpose_{tag}"
+        r = rng_for(name)
+        x = r.standard_normal(shape).astype(np.float32)
+        p = perm if perm is not None else tuple(reversed(range(len(shape))))
+        oshape = tuple(shape[i] for i in p)
+        add({"name": name, "op": "nnc_transpose", "tol": "exact",
+             "args": [_t("x"), _o("out", oshape), {"k": "perm", "v": list(perm) if perm else None}, _i(len(shape))]},
+            {"x": x})
+    for op in ("nnc_reshape", "nnc_flatten", "nnc_squeeze", "nnc_unsqueeze", "nnc_identity"):
+        name = f"{op}_seeded"
+        r = rng_for(name)
+        x = r.standard_normal((4, 6, 5)).astype(np.float32)
+        extra = {"nnc_reshape": [{"k": "perm", "v": [24, 5]}, _i(2)], "nnc_identity": []}.get(op, [_i(1)])
+        add({"name": name, "op": op, "tol": "exact", "args": [_t("x"), _o("out", (24, 5))] + extra}, {"x": x})
+    for tag, shapes, axis, dt in (("axis0", [(2, 3), (4, 3)], 0, np.float32), ("axis1", [(2, 3, 4), (2, 5, 4), (2, 1, 4)], 1, np.float32),
+                                  ("last", [(3, 2), (3, 7)], -1, np.float32), ("i64", [(2, 3), (2, 2)], 1, np.int64)):
+        name = f"nnc_concat_{tag}"
+        r = rng_for(name)
+        arrays = {}
+        for j, s in enumerate(shapes):
+            arrays[f"x{j}"] = (r.standard_normal(s) * 100).astype(dt)
+        ax = axis % len(shapes[0])
+        oshape = list(shapes[0])
+        oshape[ax] = sum(s[ax] for s in shapes)
+        dts = "int64" if dt == np.int64 else "float32"
+        add({"name": name, "op": "nnc_concat", "tol": "exact",
+             "args": [{"k": "tl", "n": list(arrays)}, _o("out", oshape, dts), _i(len(shapes)), _i(axis)]}, arrays)
+    for tag, shape, parts, axis in (("axis1", (2, 6, 3), 3, 1), ("axis0", (4, 5), 2, 0), ("last", (3, 8), 4, -1)):
+        name = f"nnc_split_{tag}"
+        r = rng_for(name)
+        x = r.standard_normal(shape).astype(np.float32)
+        ax = axis % len(shape)
+        os_ = list(shape)
+        os_[ax] //= parts
+        names = [f"out{j}" for j in range(parts)]
+        add({"name": name, "op": "nnc_split", "tol": "exact",
+             "args": [_t("x"), {"k": "ol", "n": names, "shape": [os_] * parts}, _i(parts), _i(axis)]}, {"x": x})
+    return out
+
+
+def fused_cases():
+    """Cases for the entry points without a reference counterpart; their
+    expected values come from the oracle's restatement of the reference
+    composition."""
+    out = []
+    for op, k, s, p, extra in (("nnc_conv_add_relu", 3, 2, 1, [3, 3, 2, 2, 1, 1]),
+                               ("nnc_conv_add_relu1x1", 1, 2, 0, [2, 2, 0, 0]),
+                               ("nnc_conv_add_relu3x3_s1", 3, 1, 1, [])):
+        name = f"{op}_seeded"
+        r = rng_for(name)
+        x = r.standard_normal((2, 16, 10, 10)).astype(np.float32)
+        wt = (r.standard_normal((24, 16, k, k)) / np.sqrt(16 * k * k)).astype(np.float32)
+        b = r.uniform(-0.1, 0.1, 24).astype(np.float32)
+        oh = conv_out(10, k, s, p)
+        res = r.standard_normal((2, 24, oh, oh)).astype(np.float32)
+        out.append(({"name": name, "op": op, "tol": "tc",
+                     "args": [_t("x"), _t("w"), _t("b"), _t("res"), _o("out", (2, 24, oh, oh))] + [_i(v) for v in extra]},
+                    {"x": x, "w": wt, "b": b, "res": res}))
+    for op in ("nnc_gemm_relu", "nnc_gemm_nt_relu"):
+        name = f"{op}_seeded"
+        r = rng_for(name)
+        a = r.standard_normal((150, 64)).astype(np.float32)
+        b = r.standard_normal((90, 64)).astype(np.float32)
+        c = r.standard_normal((90,)).astype(np.float32)
+        tail = [_f(1.0), _f(1.0)] + ([_i(0), _i(1)] if op == "nnc_gemm_relu" else [])
+        out.append(({"name": name, "op": op, "tol": "tc",
+                     "args": [_t("a"), _t("b"), _t("c"), _o("out", (150, 90))] + tail}, {"a": a, "b": b, "c": c}))
+    name = "nnc_matmul_relu_seeded"
+    r = rng_for(name)
+    a = r.standard_normal((128, 48)).astype(np.float32)
+    b = r.standard_normal((48, 40)).astype(np.float32)
+    bias = r.standard_normal((40,)).astype(np.float32)
+    out.append(({"name": name, "op": "nnc_matmul_relu", "tol": "tc",
+                 "args": [_t("a"), _t("b"), _t("bias"), _o("out", (128, 40))]}, {"a": a, "b": b, "bias": bias}))
+    return out

@@ -1,0 +1,180 @@
+"""GPU parity: every golden case through libnnc_cuda.so (device buffers,
+C-ABI), against the committed fixtures; tensor-core cases in both precision
+modes; the NHWC-tagged and prepacked-weight paths; host-side validation."""
+
+import ctypes
+
+import numpy as np
+import pytest
+
+import golden_cases as G
+import opcases as C
+from nnc_cuda import lib as L
+
+pytestmark = pytest.mark.gpu
+
+CONV_OPS = {"nnc_conv", "nnc_conv_relu", "nnc_conv_sigmoid", "nnc_conv1x1", "nnc_conv_relu1x1", "nnc_conv3x3_s1",
+            "nnc_conv_relu3x3_s1", "nnc_conv7x7_s2", "nnc_conv_relu7x7_s2", "nnc_conv_add_relu",
+            "nnc_conv_add_relu1x1", "nnc_conv_add_relu3x3_s1"}
+POOL_OPS = {"nnc_maxpool2d", "nnc_avgpool2d"}
+
+
+def _tol(case, precision):
+    return C.TC_RTOL[precision] if case["tol"] == "tc" else case["tol"]
+
+
+def _check(case, got, precision, what=""):
+    want = G.outputs(case)
+    assert set(got) == set(want)
+    for k in want:
+        C.assert_close(got[k], want[k], _tol(case, precision), f"{case['name']}{what}:{k}")
+
+
+@pytest.mark.parametrize("name", G.names())
+def test_golden_case(cuda_lib, name):
+    case = G.by_name(name)
+    precisions = (0, 1) if case["tol"] == "tc" else (0,)
+    for p in precisions:
+        cuda_lib.nnc_cuda_set_precision(p)
+        got = C.run_cuda(cuda_lib, case, G.inputs(case))
+        _check(case, got, p, f"[prec{p}]")
+
+
+def _nhwc_names(case):
+    names = set()
+    for a in case["args"]:
+        if a["k"] in ("t", "o") and a["n"] in ("x", "out", "res", "input_data"):
+            names.add(a["n"])
+    return names
+
+
+@pytest.mark.parametrize("name", [c["name"] for c in G.cases() if c["op"] in CONV_OPS | POOL_OPS])
+def test_golden_case_nhwc_tagged(cuda_lib, name):
+    """Activations passed channels-last with NNC_CUDA_TAG_NHWC (the layout the
+    cuda codegen target keeps in its arena) give the same results."""
+    case = G.by_name(name)
+    ins = G.inputs(case)
+    nhwc = {n for n in _nhwc_names(case) if n == "out" or (n in ins and ins[n].ndim == 4)}
+    for p in ((0, 1) if case["tol"] == "tc" else (0,)):
+        cuda_lib.nnc_cuda_set_precision(p)
+        got = C.run_cuda(cuda_lib, case, ins, nhwc=nhwc)
+        _check(case, got, p, f"[nhwc,prec{p}]")
+
+
+@pytest.mark.parametrize("name", [c["name"] for c in G.cases() if c["op"] in CONV_OPS])
+def test_conv_prepacked_weight(cuda_lib, name):
+    """A weight re-laid out once by nnc_cuda_prepack_conv_weight (as the cuda
+    target's constant loader does) gives the same results as raw OIHW."""
+    import torch
+
+    from nnc_cuda import tensor as T
+
+    case = G.by_name(name)
+    ins = G.inputs(case)
+    wname = next(a["n"] for a in case["args"][1:2])
+    w = torch.from_numpy(ins[wname]).cuda()
+    wref = T.from_torch(w)
+    nbytes = cuda_lib.nnc_cuda_prepacked_conv_weight_bytes(wref.ptr)
+    packed = torch.empty(nbytes // 4, dtype=torch.float32, device="cuda")
+    assert cuda_lib.nnc_cuda_prepack_conv_weight(wref.ptr, ctypes.c_void_p(packed.data_ptr()), nbytes) == 0
+    assert wref.struct.dtype & L.TAG_PACKED_CONV
+    for p in (0, 1):
+        cuda_lib.nnc_cuda_set_precision(p)
+        got = _run_with_weight(cuda_lib, case, ins, wname, wref)
+        _check(case, got, p, f"[packed,prec{p}]")
+
+
+def _run_with_weight(so, case, ins, wname, wref):
+    """run_cuda with the weight argument replaced by a prepared descriptor."""
+    import torch
+
+    from nnc_cuda import tensor as T
+
+    keep, cargs, outs = [], [], {}
+    for a in case["args"]:
+        if a["k"] == "t" and a["n"] == wname:
+            cargs.append(wref.ptr)
+        elif a["k"] == "t":
+            t = torch.from_numpy(ins[a["n"]]).cuda()
+            r = T.from_torch(t)
+            keep.append(r)
+            cargs.append(r.ptr)
+        elif a["k"] == "o":
+            t = torch.full(a["shape"], C.SENTINEL, dtype=torch.float32, device="cuda")
+            outs[a["n"]] = t
+            r = T.from_torch(t)
+            keep.append(r)
+            cargs.append(r.ptr)
+        elif a["k"] == "null":
+            cargs.append(None)
+        elif a["k"] == "i":
+            cargs.append(ctypes.c_int(a["v"]))
+        elif a["k"] == "f":
+            cargs.append(ctypes.c_float(a["v"]))
+    so.nnc_cuda_set_stream(ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    getattr(so, case["op"])(*cargs)
+    torch.cuda.synchronize()
+    assert so.nnc_cuda_get_last_error() == 0, so.nnc_cuda_get_last_error_string()
+    return {k: v.cpu().numpy() for k, v in outs.items()}
+
+
+# ---------------------------------------------------------------- bigger --
+def _oracle():
+    from oracle import oracle as O
+
+    return O.load_oracle()
+
+
+@pytest.mark.parametrize("prec", [0, 1])
+@pytest.mark.parametrize("shape", [(512, 512, 512), (1000, 384, 256), (256, 1000, 512), (300, 700, 124)])
+def test_gemm_nt_sizes_vs_oracle(cuda_lib, prec, shape):
+    M, N, K = shape
+    r = np.random.default_rng(M * 7 + N)
+    arrays = {"a": r.standard_normal((M, K)).astype(np.float32), "b": r.standard_normal((N, K)).astype(np.float32),
+              "c": r.standard_normal((N,)).astype(np.float32)}
+    case = {"name": "g", "op": "nnc_gemm_nt", "args": [C._t("a"), C._t("b"), C._t("c"), C._o("out", (M, N)),
+                                                       C._f(1.0), C._f(1.0)]}
+    cuda_lib.nnc_cuda_set_precision(prec)
+    got = C.run_cuda(cuda_lib, case, arrays)["out"]
+    want = C.run_host(_oracle(), case, arrays)["out"]
+    C.assert_close(got, want, C.TC_RTOL[prec], f"gemm_nt{shape}")
+
+
+@pytest.mark.parametrize("prec", [0, 1])
+@pytest.mark.parametrize("cfg", [(4, 64, 28, 64, 3, 1, 1), (2, 128, 14, 256, 3, 2, 1), (2, 256, 7, 512, 3, 1, 1),
+                                 (2, 3, 56, 64, 7, 2, 3), (2, 64, 28, 128, 1, 2, 0)])
+def test_conv_resnet_layers_vs_oracle(cuda_lib, prec, cfg):
+    n, c, h, co, k, s, p = cfg
+    r = np.random.default_rng(sum(cfg))
+    oh = C.conv_out(h, k, s, p)
+    arrays = {"x": r.standard_normal((n, c, h, h)).astype(np.float32),
+              "w": (r.standard_normal((co, c, k, k)) * np.sqrt(2.0 / (c * k * k))).astype(np.float32),
+              "b": r.uniform(-0.01, 0.01, co).astype(np.float32),
+              "res": r.standard_normal((n, co, oh, oh)).astype(np.float32)}
+    case = {"name": "c", "op": "nnc_conv_add_relu", "args": [C._t("x"), C._t("w"), C._t("b"), C._t("res"),
+            C._o("out", (n, co, oh, oh)), C._i(k), C._i(k), C._i(s), C._i(s), C._i(p), C._i(p)]}
+    cuda_lib.nnc_cuda_set_precision(prec)
+    want = C.run_host(_oracle(), case, arrays)["out"]
+    got = C.run_cuda(cuda_lib, case, arrays)["out"]
+    C.assert_close(got, want, C.TC_RTOL[prec], f"conv{cfg}")
+    got_nhwc = C.run_cuda(cuda_lib, case, arrays, nhwc={"x", "res", "out"})["out"]
+    C.assert_close(got_nhwc, want, C.TC_RTOL[prec], f"conv{cfg}[nhwc]")
+
+
+# ------------------------------------------------------------ validation --
+def test_invalid_shapes_set_status_without_launch(cuda_lib):
+    import torch
+
+    from nnc_cuda import tensor as T
+
+    x = torch.zeros((1, 3, 8, 8), device="cuda")
+    w = torch.zeros((4, 5, 3, 3), device="cuda")  # C_in mismatch
+    o = torch.zeros((1, 4, 8, 8), device="cuda")
+    rx, rw, ro = T.from_torch(x), T.from_torch(w), T.from_torch(o)
+    cuda_lib.nnc_conv(rx.ptr, rw.ptr, None, ro.ptr, 3, 3, 1, 1, 1, 1)
+    assert cuda_lib.nnc_cuda_get_last_error() == L.ERR_INVALID
+    cuda_lib.nnc_cuda_clear_error()
+    cuda_lib.nnc_conv3x3_s1(rx.ptr, rw.ptr, None, T.from_torch(torch.zeros((1, 4, 7, 7), device="cuda")).ptr)
+    assert cuda_lib.nnc_cuda_get_last_error() == L.ERR_INVALID
+    cuda_lib.nnc_cuda_clear_error()
+    assert cuda_lib.nnc_cuda_check_device_status() == 0
