@@ -162,14 +162,20 @@ def run_cuda(so, case, arrays, nhwc=()):
 
 # ------------------------------------------------------------- comparing --
 def assert_close(got, want, tol, what=""):
-    """tol: "exact" (bitwise, NaN payloads included) or a float rtol applied
-    normwise: |got - want| <= rtol * (|want| + max|want|), NaNs in the same
-    places."""
+    """tol: "exact" — every non-NaN value bit-identical (signed zeros
+    included) and NaNs in the same places (NaN payload bits are not compared:
+    the GPU produces canonical NaNs where x86 propagates an operand's payload)
+    — or a float rtol applied normwise: |got - want| <= rtol * (|want| +
+    max|want|), NaNs in the same places."""
     assert got.shape == want.shape, f"{what}: shape {got.shape} vs {want.shape}"
     if tol == "exact":
         g = got.view(np.uint32 if got.dtype == np.float32 else np.uint64)
         w = want.view(np.uint32 if want.dtype == np.float32 else np.uint64)
-        bad = np.flatnonzero(g != w)
+        differ = g != w
+        if got.dtype.kind == "f":
+            gn, wn = np.isnan(got), np.isnan(want)
+            differ = np.where(gn & wn, False, differ)
+        bad = np.flatnonzero(differ)
         assert bad.size == 0, (
             f"{what}: {bad.size} of {g.size} differ; first at {bad[0]}: "
             f"got {got.flat[bad[0]]!r} want {want.flat[bad[0]]!r}"
