@@ -1,0 +1,359 @@
+"""ResNet-18 fp32 images/s on B200 (BASELINE.json metric; config 5: the
+-O3 cuda-target build, global batch 1024 split evenly over the GPUs).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--precision tf32|3xtf32]
+    torchrun --nproc-per-node N bench.py --gpus N ...      (one rank per GPU)
+    python bench.py --impl reference ...                   (the reference's CPU build)
+
+Our arm: every rank loads nnc-py_b200/models_gen/resnet18_o3_b<1024/N>
+(libmodel.so over libnnc_cuda.so), uploads the seeded weights, and runs
+its shard of the seeded input. A step = one forward of the whole global
+batch; ranks add an NCCL gather of the logits to rank 0 when N > 1 (the
+config's output gather). Timing: W untimed warm-up steps, then K steps
+bracketed by barrier + synchronize, CUDA events on the launching stream,
+max over ranks. Inputs (616 MB) exceed the 126 MB L2, so no flush is
+needed. `e2e` repeats the measurement through the model's host-buffer path:
+every step copies its input shard from pinned host memory and reads the
+logits back. `roofline` covers the dominant kernel (the tcgen05 implicit-GEMM
+conv): algorithmic conv FLOPs per step / conv device time, both measured
+live in the timed region with per-call CUDA events.
+
+Reference arm: rank 0 runs the reference's own x86 build of the same graph
+(nnc-py X86Backend, legacy -O3 pass list, runtime/x86/ops.c, gcc -O3; see
+oracle/ref_models.py) on all host cores, one process per core, each running
+batch-1 forwards (nnc-py's benchmark definition of workload batch).
+"""
+
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import pathlib
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = pathlib.Path(__file__).resolve().parent
+sys.path[:0] = [str(ROOT), str(ROOT / "nnc-py_b200")]
+
+METRIC = "ResNet-18 fp32 images/s at 1/8 B200; conv/GEMM tensor-pipe %; eltwise HBM %"
+GLOBAL_BATCH = 1024
+IMG_BYTES = 3 * 224 * 224 * 4
+LOGIT_BYTES = 1000 * 4
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpus: list[int]):
+        self.gpus = gpus
+        self.proc = None
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", ",".join(str(g) for g in self.gpus)], stdout=self.file, stderr=subprocess.DEVNULL)
+        except FileNotFoundError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        self.proc.wait(timeout=10)
+        self.file.flush()
+        rows = [r.split(",") for r in pathlib.Path(self.file.name).read_text().splitlines() if r.count(",") >= 8]
+        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
+        reasons = set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for r in rows:
+            for n, v in zip(names, r[5:9]):
+                if v.strip().lower() == "active":
+                    reasons.add(n)
+        busy = [s for s in sm if s > 500] or sm
+        return {"sm_mhz": statistics.median(busy) if busy else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(rows)}
+
+
+def conv_flops(model) -> float:
+    total = 0.0
+    for n in model.nodes:
+        if n.op != "Conv":
+            continue
+        x, w = n.inputs[0], n.inputs[1]
+        out = model.shapes[n.outputs[0]]
+        cout, cin, kh, kw = model.shapes[w]
+        total += 2.0 * out[0] * cout * out[2] * out[3] * cin * kh * kw
+    return total
+
+
+def cpu_reference(tag: str, procs: int, per_proc: int, workdir: pathlib.Path, first: int = 0):
+    """Runs the reference's x86 build on `procs` processes x `per_proc`
+    images; returns (images/s, wall seconds)."""
+    from oracle import refmodel as R  # test/baseline infrastructure only
+
+    from nnc_cuda import workloads as W
+
+    meta = R.info(tag)
+    consts = workdir / f"{tag}_constants.bin"
+    if not consts.exists():
+        R.write_constants(tag, consts)
+    inp = workdir / "ref_input.bin"
+    if not inp.exists():
+        inp.write_bytes(W.resnet18(1).input_array(per_proc, offset=first).tobytes())
+    exe = ROOT / "oracle" / "_ref" / tag / "model_x86"
+    t0 = time.perf_counter()
+    ps = [subprocess.Popen([str(exe), str(consts), str(inp), str(workdir / f"out{i}.bin"), "1", "0", str(per_proc)],
+                           stdout=subprocess.DEVNULL) for i in range(procs)]
+    rcs = [p.wait() for p in ps]
+    wall = time.perf_counter() - t0
+    if any(rcs):
+        raise RuntimeError(f"reference build failed: {rcs}")
+    assert meta["batch"] == 1
+    return procs * per_proc / wall, wall
+
+
+def reference_arm(opt):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    tag = "resnet18_o3_b1"
+    cores = len(os.sched_getaffinity(0))
+    work = pathlib.Path(tempfile.mkdtemp(prefix="nnc_refarm_"))
+    per_proc = 1
+    for _ in range(opt.warmup):
+        cpu_reference(tag, cores, per_proc, work)
+    rates, walls = [], []
+    for _ in range(opt.steps):
+        r, w = cpu_reference(tag, cores, per_proc, work)
+        rates.append(r)
+        walls.append(w)
+    total_imgs = cores * per_proc * opt.steps
+    value = total_imgs / sum(walls)
+    line = {"impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "images/s",
+            "n_gpus": opt.gpus, "steps": opt.steps, "warmup": opt.warmup,
+            "ms_per_step": round(1e3 * sum(walls) / opt.steps, 3), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32 (fp64 conv/gemm accumulation)", "data": "synthetic",
+            "config": {"workload": "resnet18 fp32 224x224, reference x86 build (nnc-py X86Backend, legacy -O3 "
+                                   "passes, ops.c, gcc -O3 -std=c11), batch-1 model, one process per core",
+                       "global_batch": GLOBAL_BATCH, "step_sample": f"{cores} processes x {per_proc} image(s)"},
+            "cpu_baseline": {"value": round(value, 3), "unit": "images/s", "cores": cores, "kind": "reference",
+                             "sample": f"{cores} processes x {per_proc} image per step, {opt.steps} steps"},
+            "e2e": {"value": round(value, 3), "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def our_arm(opt):
+    import torch
+
+    from nnc_cuda import lib as L
+    from nnc_cuda import workloads as W
+    from nnc_cuda.model import CudaModel
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != opt.gpus:
+        raise SystemExit(f"--gpus {opt.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    B = GLOBAL_BATCH // world
+    tag = f"resnet18_o3_b{B}"
+    rt = L.load()
+    model = CudaModel(tag)
+    model.init(local)
+    wl = W.resnet18(B)
+    stream = torch.cuda.Stream()
+    model.set_stream(stream.cuda_stream)
+    model.load_constants(wl)
+    prec = L.PRECISION_3XTF32 if opt.precision == "3xtf32" else L.PRECISION_TF32
+    rt.nnc_cuda_set_precision(prec)
+
+    x_host = torch.from_numpy(wl.input_array(B, offset=rank * B)).pin_memory()
+    logits_host = torch.empty((B, 1000), dtype=torch.float32).pin_memory()
+    gathered = torch.empty((GLOBAL_BATCH, 1000), dtype=torch.float32, device="cuda") if world > 1 else None
+    mine = torch.empty((B, 1000), dtype=torch.float32, device="cuda") if world > 1 else None
+    in_bytes, out_bytes = B * IMG_BYTES, B * LOGIT_BYTES
+
+    def h2d():
+        rt.nnc_cuda_memcpy_async(ctypes.c_void_p(model.input_ptr()), ctypes.c_void_p(x_host.data_ptr()), in_bytes, 1)
+
+    def d2h():
+        rt.nnc_cuda_memcpy_async(ctypes.c_void_p(logits_host.data_ptr()), ctypes.c_void_p(model.output_ptr()),
+                                 out_bytes, 2)
+
+    def gather():
+        if world > 1:
+            rt.nnc_cuda_memcpy_async(ctypes.c_void_p(mine.data_ptr()), ctypes.c_void_p(model.output_ptr()), out_bytes, 3)
+            with torch.cuda.stream(stream):
+                dist.all_gather_into_tensor(gathered, mine)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    with torch.cuda.stream(stream):
+        h2d()
+        for _ in range(opt.warmup):
+            model.run()
+            gather()
+    barrier()
+    if rt.nnc_cuda_get_last_error() != 0:
+        raise RuntimeError(rt.nnc_cuda_get_last_error_string().decode())
+
+    # ---- device-resident timing (value) ----
+    sampler = ClockSampler([local]) if rank == 0 else None
+    if sampler:
+        sampler.start()
+    launches0 = rt.nnc_cuda_launch_count()
+    rt.nnc_cuda_trace_clear()
+    rt.nnc_cuda_trace_enable(1)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    ev0.record(stream)
+    with torch.cuda.stream(stream):
+        for _ in range(opt.steps):
+            model.run()
+            gather()
+    ev1.record(stream)
+    barrier()
+    ms = ev0.elapsed_time(ev1)
+    launches = rt.nnc_cuda_launch_count() - launches0
+    rt.nnc_cuda_trace_enable(0)
+    n = rt.nnc_cuda_trace_count()
+    conv_us = sum(rt.nnc_cuda_trace_us(i) for i in range(n) if rt.nnc_cuda_trace_name(i).startswith(b"nnc_conv"))
+    op_us = {}
+    for i in range(n):
+        nm = rt.nnc_cuda_trace_name(i).decode()
+        op_us[nm] = op_us.get(nm, 0.0) + rt.nnc_cuda_trace_us(i)
+    rt.nnc_cuda_trace_clear()
+    clocks = sampler.stop() if sampler else None
+    ms_max = max_over_ranks(ms)
+    conv_ms_step = max_over_ranks(conv_us / 1e3 / opt.steps)
+
+    # ---- end-to-end through host buffers (e2e) ----
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    with torch.cuda.stream(stream):
+        for _ in range(opt.steps):
+            h2d()
+            model.run()
+            d2h()
+            gather()
+    e1.record(stream)
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1))
+    if rt.nnc_cuda_get_last_error() != 0 or rt.nnc_cuda_check_device_status() != 0:
+        raise RuntimeError(rt.nnc_cuda_get_last_error_string().decode())
+
+    line = None
+    if rank == 0:
+        pk = peaks()
+        tf32_peak = pk["bf16_tflops"] / 2.0
+        peak = tf32_peak / (3.0 if prec == L.PRECISION_3XTF32 else 1.0)
+        cflops = conv_flops(wl)  # per rank per step
+        achieved = cflops / (conv_ms_step * 1e-3) / 1e12 if conv_ms_step > 0 else None
+        value = opt.steps * GLOBAL_BATCH / (ms_max * 1e-3)
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "images/s", "n_gpus": world, "steps": opt.steps,
+            "warmup": opt.warmup, "ms_per_step": round(ms_max / opt.steps, 4), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None,
+            "dtype": "tf32" if prec == L.PRECISION_TF32 else "f32 (3xtf32)",
+            "data": "synthetic",
+            "config": {"workload": "resnet18 fp32 224x224, nnc -O3 cuda target (conv+relu, conv+add+relu fused), "
+                                   f"global batch {GLOBAL_BATCH} split over {world} GPU(s)",
+                       "model": "resnet18", "global_batch": GLOBAL_BATCH, "per_gpu_batch": B, "seq_len": None,
+                       "parallelism": f"dp{world} (batch shards, logits gathered to rank 0)" if world > 1 else "single GPU",
+                       "precision": opt.precision, "l2": "inputs (616 MB/step) larger than L2; no flush"},
+            "roofline": {"bound": "tensor", "kernel": "conv_tc_kernel (tcgen05 implicit GEMM)",
+                         "achieved": round(achieved, 2) if achieved else None, "peak": round(peak, 1),
+                         "unit": "TFLOP/s", "frac": round(achieved / peak, 4) if achieved else None,
+                         "traffic": roofline_traffic(),
+                         "peak_note": f"dense TF32 = bf16/2 of {pk['source']} MEASURED_PEAKS.json"
+                                      + (", /3 for the 3 MMAs of 3xTF32" if prec == L.PRECISION_3XTF32 else ""),
+                         "conv_ms_per_step": round(conv_ms_step, 4),
+                         "conv_gflop_per_step_per_gpu": round(cflops / 1e9, 1)},
+            "e2e": {"value": round(opt.steps * GLOBAL_BATCH / (e2e_ms * 1e-3), 2), "unit": "images/s",
+                    "h2d_bytes_per_step": GLOBAL_BATCH * IMG_BYTES, "d2h_bytes_per_step": GLOBAL_BATCH * LOGIT_BYTES},
+            "gpu_launches": int(launches),
+            "clocks": clocks,
+            "op_ms_per_step": {k: round(v / 1e3 / opt.steps, 4) for k, v in sorted(op_us.items(), key=lambda kv: -kv[1])},
+        }
+    if world == 1 and rank == 0 and not opt.no_cpu_baseline:
+        work = pathlib.Path(tempfile.mkdtemp(prefix="nnc_cpu_"))
+        cores = len(os.sched_getaffinity(0))
+        per = 2
+        rate, wall = cpu_reference("resnet18_o3_b1", cores, per, work)
+        line["cpu_baseline"] = {"value": round(rate, 3), "unit": "images/s", "cores": cores, "kind": "reference",
+                                "sample": f"{cores} processes x {per} images (batch-1 x86 build, {wall:.1f} s wall)"}
+    if line:
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def roofline_traffic():
+    """DRAM bytes per conv launch from the committed ncu summary, if any."""
+    p = ROOT / "profiles" / "conv_tc_resnet18_traffic.txt"
+    if p.exists():
+        for line in p.read_text().splitlines():
+            if line.startswith("bytes_per_launch="):
+                return float(line.split("=")[1])
+    return None
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--precision", choices=["tf32", "3xtf32"], default="tf32")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    opt = ap.parse_args()
+    if opt.warmup < 3:
+        opt.warmup = 3
+    if opt.impl == "reference":
+        return reference_arm(opt)
+    return our_arm(opt)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

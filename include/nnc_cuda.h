@@ -87,6 +87,13 @@ int nnc_cuda_prepack_conv_weight(Tensor* w, void* dst, size_t dst_bytes);
 void nnc_cuda_nchw_to_nhwc(Tensor* input, Tensor* output);
 void nnc_cuda_nhwc_to_nchw(Tensor* input, Tensor* output);
 
+/* ---- plumbing for callers without their own CUDA runtime binding --------
+ * Stream-ordered copy on the current stream; kind: 1 host->device,
+ * 2 device->host, 3 device->device (cudaMemcpyKind values). */
+int nnc_cuda_memcpy_async(void* dst, const void* src, size_t bytes, int kind);
+/* Number of kernels this thread has launched through the library. */
+long long nnc_cuda_launch_count(void);
+
 /* ---- observability ------------------------------------------------------------
  * When enabled (or NNC_CUDA_TRACE=1 in the environment), every operator call
  * records CUDA events around its launches; nnc_cuda_trace_dump prints one line
@@ -94,6 +101,13 @@ void nnc_cuda_nhwc_to_nchw(Tensor* input, Tensor* output);
  * clears the log. Synchronises the current stream. */
 void nnc_cuda_trace_enable(int on);
 int nnc_cuda_trace_dump(void);
+/* Programmatic access to the same log: nnc_cuda_trace_count synchronises
+ * the current stream and returns the number of recorded calls; entry i has
+ * an operator name and a device duration in microseconds. */
+int nnc_cuda_trace_count(void);
+const char* nnc_cuda_trace_name(int i);
+float nnc_cuda_trace_us(int i);
+void nnc_cuda_trace_clear(void);
 
 #ifdef __cplusplus
 }

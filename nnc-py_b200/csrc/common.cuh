@@ -20,6 +20,7 @@ struct ThreadCtx {
   int precision = NNC_CUDA_PRECISION_TF32;
   int status = NNC_CUDA_OK;
   char message[512] = {0};
+  long long launches = 0;
 };
 ThreadCtx& ctx();
 
@@ -31,7 +32,9 @@ void fail(int code, const char* op, const char* fmt, ...)
 
 // Checks the result of a launch / runtime call; false (and status set) on error.
 bool check_cuda(cudaError_t err, const char* op, const char* what);
+// Call once right after every kernel launch: checks it and counts it.
 inline bool check_launch(const char* op) {
+  ++ctx().launches;
   return check_cuda(cudaGetLastError(), op, "kernel launch");
 }
 

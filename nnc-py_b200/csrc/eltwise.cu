@@ -215,12 +215,13 @@ void binary_dispatch(Tensor* a, Tensor* b, Tensor* out, const char* name) {
     else if (am == kModular && bm == kIdent) launch_vec<OP, kModular, kIdent>(pa, pb, po, n4, an, bn);
     else launch_vec<OP, kIdent, kModular>(pa, pb, po, n4, an, bn);
     done = n4 << 2;
+    if (!check_launch(name)) return;
   }
   if (done < count) {
     const int grid = grid_for(count - done, 256, 8);
     binary_scalar_kernel<OP><<<grid, 256, 0, ctx().stream>>>(pa, pb, po, done, count, a_mod, b_mod);
+    check_launch(name);
   }
-  check_launch(name);
 }
 
 template <int OP>

@@ -243,6 +243,43 @@ size_t nnc_cuda_get_workspace_capacity(void) {
   return t_ws.user_ptr[d] ? t_ws.user_cap[d] : t_ws.cap[d];
 }
 
+int nnc_cuda_memcpy_async(void* dst, const void* src, size_t bytes, int kind) {
+  if (kind < 1 || kind > 3) {
+    fail(NNC_CUDA_ERR_INVALID, "nnc_cuda_memcpy_async", "kind %d is not 1, 2 or 3", kind);
+    return NNC_CUDA_ERR_INVALID;
+  }
+  if (!check_cuda(cudaMemcpyAsync(dst, src, bytes, (cudaMemcpyKind)kind, ctx().stream),
+                  "nnc_cuda_memcpy_async", "cudaMemcpyAsync"))
+    return ctx().status;
+  return NNC_CUDA_OK;
+}
+
+long long nnc_cuda_launch_count(void) { return ctx().launches; }
+
+int nnc_cuda_trace_count(void) {
+  cudaStreamSynchronize(ctx().stream);
+  return (int)t_trace.size();
+}
+
+const char* nnc_cuda_trace_name(int i) {
+  return (i >= 0 && i < (int)t_trace.size()) ? t_trace[i].name : "";
+}
+
+float nnc_cuda_trace_us(int i) {
+  if (i < 0 || i >= (int)t_trace.size()) return -1.f;
+  float ms = 0.f;
+  if (cudaEventElapsedTime(&ms, t_trace[i].start, t_trace[i].stop) != cudaSuccess) return -1.f;
+  return ms * 1e3f;
+}
+
+void nnc_cuda_trace_clear(void) {
+  for (auto& r : t_trace) {
+    cudaEventDestroy(r.start);
+    cudaEventDestroy(r.stop);
+  }
+  t_trace.clear();
+}
+
 void nnc_cuda_trace_enable(int on) { g_trace_on = on ? 1 : 0; }
 
 int nnc_cuda_trace_dump(void) {

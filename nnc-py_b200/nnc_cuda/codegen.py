@@ -1,0 +1,776 @@
+"""The ``cuda`` target for nnc-py's compiler (needs nnc-py importable).
+
+Plugs in where nnc-py adds targets — ``Compiler._create_backend``
+(compiler.py:266-285) and the CLI's ``-t`` choice (cli.py:33-37) — and emits
+the same artifact set as the x86 backend (codegen/x86_backend.py:89-147):
+
+* ``model.c``    nnc-py's own CEmitter (codegen/c_emitter.py) with one
+                 addition: nodes fused by :class:`ConvAddReluFusionPass`
+                 call ``nnc_conv_add_relu*``; every other call line is the
+                 one the reference emits;
+* ``model.h``    entry points (nnc_run + device/arena/constant management);
+* ``tensors.c``  the Tensor globals; activations are bound at run time into
+                 ONE device arena sized by the cost_aware liveness plan
+                 (passes/memory_planning.py:72-111), constants into one slab;
+                 4-D activations that only meet conv / pool / element-wise
+                 ops carry NNC_CUDA_TAG_NHWC (channels-last);
+* ``constants_loader.c``  reads the NNCB v1 container
+                 (codegen/x86_emitters/constants_loader.py:40-144), uploads
+                 once per device and prepacks conv weights on the device;
+* ``model_runtime.c``     arena/slab allocation and per-device binding;
+* ``test_runner.c``       shards the batch over the GPUs of one node, gathers
+                 the outputs to GPU 0 over NVLink and writes them;
+* ``Makefile``   nvcc, -arch=sm_100a, links libnnc_cuda.so;
+* ``manifest.json``  shapes, constant order/symbols, arena size.
+"""
+
+from __future__ import annotations
+
+import json
+import pathlib
+import re
+import sys
+from typing import Any
+
+import numpy as np
+
+from .workloads import Model
+
+REFERENCE_SRC = pathlib.Path("/root/reference/src")
+
+
+def _import_nnc_py():
+    try:
+        import nnc_py  # noqa: F401
+    except ImportError:
+        if (REFERENCE_SRC / "nnc_py").exists():
+            sys.path.insert(0, str(REFERENCE_SRC))
+        import nnc_py  # noqa: F401
+
+
+_import_nnc_py()
+
+from nnc_py.codegen.base import BackendBase, CodeGenResult  # noqa: E402
+from nnc_py.codegen.c_emitter import CEmitter  # noqa: E402
+from nnc_py.ir.context import CompileContext  # noqa: E402
+from nnc_py.ir.graph import Graph  # noqa: E402
+from nnc_py.ir.node import Node, OpType  # noqa: E402
+from nnc_py.ir.tensor import TensorShape, TensorType  # noqa: E402
+from nnc_py.ir.types import DataType  # noqa: E402
+from nnc_py.passes.base import PassBase, PassManager  # noqa: E402
+from nnc_py.utils.name_manager import NameManager  # noqa: E402
+
+TAG_NHWC = 0x100
+ARENA_ALIGN = 256
+
+
+# --------------------------------------------------------------- graph ----
+def to_nnc_graph(model: Model) -> Graph:
+    """Builds nnc-py IR (ir/graph.py) from a workload Model."""
+    g = Graph(model.name)
+    for name, shape in model.shapes.items():
+        g.add_tensor(TensorType(DataType.FLOAT32, TensorShape(list(shape)), name))
+    for name, arr in model.constants.items():
+        g.constants[name] = arr
+    for n in model.nodes:
+        g.add_node(Node(OpType(n.op), n.name, list(n.inputs), list(n.outputs), dict(n.attrs)))
+    g.inputs = list(model.inputs)
+    g.outputs = list(model.outputs)
+    return g
+
+
+# -------------------------------------------------------------- passes ----
+class ConvAddReluFusionPass(PassBase):
+    """Collapses Conv -> Add(+ReLU) into one conv whose epilogue adds the
+    residual and applies ReLU (the Conv+Add+Relu group the cuda target adds
+    next to nnc-py's built-in patterns, pattern/fusion_patterns.py:104-152).
+
+    Runs after PatternFusion, so the Add+ReLU is already a FUSED_ADD_RELU
+    node. The conv must feed only that node. The fused node keeps op type
+    CONV2D (so liveness, memory planning and PrepackLowering treat it as a
+    conv, never in-place) with inputs [x, w, b, residual] and
+    metadata ``cuda_fused = "conv_add_relu"``.
+    """
+
+    @property
+    def name(self) -> str:
+        return "CudaConvAddReluFusion"
+
+    def _execute(self, ctx: CompileContext) -> None:
+        g = ctx.graph
+        for node in list(g.topological_sort()):
+            if node.op_type != OpType.FUSED_ADD_RELU or len(node.inputs) != 2:
+                continue
+            for pos in (0, 1):
+                src = node.inputs[pos]
+                prods = g.get_producers(src)
+                if len(prods) != 1:
+                    continue
+                conv = prods[0]
+                if conv.op_type != OpType.CONV2D or conv.metadata.get("cuda_fused"):
+                    continue
+                if len(g.get_consumers(src)) != 1 or src in g.outputs:
+                    continue
+                residual = node.inputs[1 - pos]
+                if list(g.tensors[residual].shape.dims) != list(g.tensors[node.outputs[0]].shape.dims):
+                    continue
+                inputs = list(conv.inputs)
+                if len(inputs) == 2:
+                    inputs.append("")  # no bias
+                fused = Node(OpType.CONV2D, f"{conv.name}_add_relu", inputs[:3] + [residual],
+                             list(node.outputs), dict(conv.attrs),
+                             metadata={"cuda_fused": "conv_add_relu", "fused_from": [conv.name, node.name]})
+                g.nodes.pop(conv.name)
+                g.nodes.pop(node.name)
+                g.tensors.pop(src, None)
+                g.add_node(fused)  # also drops nnc-py's cached dependency graph
+                break
+
+
+def cuda_passes(opt_level: int) -> list[PassBase]:
+    """Pass lists of the cuda target.
+
+    O0-O2: nnc-py's own lists (passes/base.py:88-106). O3: cleanup, nnc-py's
+    PatternFusion (conv_relu, add_relu, ...), the Conv+Add+Relu group,
+    PrepackLowering (entry-point selection, Gemm weight prepack), liveness
+    and the cost_aware arena plan. nnc-py's NPU tiling passes are not used:
+    the GPU kernels tile internally.
+    """
+    from nnc_py.passes.dead_code_elimination import DeadCodeEliminationPass
+    from nnc_py.passes.identity_elimination import IdentityEliminationPass
+    from nnc_py.passes.liveness import LivenessAnalysisPass
+    from nnc_py.passes.memory_planning import MemoryPlanningPassV2
+    from nnc_py.passes.pattern_fusion import PatternFusionPass
+    from nnc_py.passes.prepack_lowering import PrepackLoweringPass
+
+    if opt_level < 3:
+        return PassManager.get_default_passes(opt_level)
+    return [IdentityEliminationPass(), DeadCodeEliminationPass(), PatternFusionPass(), ConvAddReluFusionPass(),
+            PrepackLoweringPass(), LivenessAnalysisPass(), MemoryPlanningPassV2()]
+
+
+# -------------------------------------------------------------- layout ----
+_NHWC_OPS = {OpType.CONV2D, OpType.FUSED_CONV_RELU, OpType.FUSED_CONV_SIGMOID, OpType.FUSED_CONV_BIAS_RELU,
+             OpType.MAXPOOL, OpType.AVGPOOL, OpType.GLOBAL_AVGPOOL}
+_ELTWISE = {OpType.RELU, OpType.SIGMOID, OpType.TANH, OpType.CLIP, OpType.ADD, OpType.SUB, OpType.MUL,
+            OpType.DIV, OpType.FUSED_ADD_RELU, OpType.FUSED_ADD_SIGMOID}
+
+
+def channels_last_tensors(ctx: CompileContext) -> set[str]:
+    """4-D activations that can live channels-last: every producer/consumer
+    is a conv/pool (which take either layout) or an element-wise op whose 4-D
+    operands all share one layout. Graph inputs/outputs stay NCHW unless
+    their spatial extent is 1 x 1 (then both layouts have the same bytes)."""
+    g = ctx.graph
+    four_d = {n for n, t in g.tensors.items() if n not in g.constants and len(t.shape.dims) == 4}
+    parent = {n: n for n in four_d}
+
+    def find(a):
+        while parent[a] != a:
+            parent[a] = parent[parent[a]]
+            a = parent[a]
+        return a
+
+    bad = set()
+    for node in g.nodes.values():
+        acts = [t for t in list(node.inputs) + list(node.outputs) if t in four_d]
+        if node.op_type in _ELTWISE:
+            full = [t for t in acts if list(g.tensors[t].shape.dims) == list(g.tensors[node.outputs[0]].shape.dims)]
+            for t in full[1:]:
+                parent[find(t)] = find(full[0])
+            for t in acts:
+                if t not in full:
+                    bad.add(t)  # broadcast operand: keep logical order
+        elif node.op_type in _NHWC_OPS:
+            if node.op_type in (OpType.MAXPOOL, OpType.AVGPOOL, OpType.GLOBAL_AVGPOOL):
+                if node.inputs[0] in four_d and node.outputs[0] in four_d:
+                    parent[find(node.outputs[0])] = find(node.inputs[0])
+            if node.metadata.get("cuda_fused") == "conv_add_relu":
+                res, out = node.inputs[3], node.outputs[0]
+                if res in four_d and out in four_d:
+                    parent[find(res)] = find(out)
+        else:
+            for t in acts:
+                dims = g.tensors[t].shape.dims
+                if int(dims[2]) * int(dims[3]) != 1:
+                    bad.add(t)
+    for t in list(g.inputs) + list(g.outputs):
+        if t in four_d:
+            dims = g.tensors[t].shape.dims
+            if int(dims[2]) * int(dims[3]) != 1:
+                bad.add(t)
+    bad_roots = {find(t) for t in bad}
+    return {t for t in four_d if find(t) not in bad_roots}
+
+
+# ------------------------------------------------------------- emitter ----
+class CudaEmitter(CEmitter):
+    """nnc-py's CEmitter with the cuda target's fused conv+add+relu call."""
+
+    def _emit_includes(self, ctx: CompileContext) -> None:
+        super()._emit_includes(ctx)
+        self.write_line('#include "nnc_cuda.h"')
+        self.write_line()
+
+    def _emit_operator_call(self, ctx: CompileContext, node: Node) -> None:
+        if node.metadata.get("cuda_fused") == "conv_add_relu":
+            sym = ctx.tensor_symbols
+            x, w, b, r = node.inputs[:4]
+            out = node.outputs[0]
+            bias = f"&{sym[b]}" if b else "NULL"
+            args = [f"&{sym[x]}", f"&{sym[w]}", bias, f"&{sym[r]}", f"&{sym[out]}"]
+            kind = node.metadata.get("lowering", {}).get("kernel_kind")
+            ks = node.attrs.get("kernel_shape", [1, 1])
+            st = node.attrs.get("strides", [1, 1])
+            pd = node.attrs.get("pads", [0, 0, 0, 0])
+            if kind == "spatial_3x3":
+                self.write_line(f"nnc_conv_add_relu3x3_s1({', '.join(args)});")
+            elif kind == "pointwise_1x1":
+                self.write_line(f"nnc_conv_add_relu1x1({', '.join(args + [str(st[0]), str(st[1]), str(pd[0]), str(pd[1])])});")
+            else:
+                extra = [str(ks[0]), str(ks[1]), str(st[0]), str(st[1]), str(pd[0]), str(pd[1])]
+                self.write_line(f"nnc_conv_add_relu({', '.join(args + extra)});")
+            return
+        super()._emit_operator_call(ctx, node)
+
+
+# ------------------------------------------------------------- backend ----
+def _c_array(vals) -> str:
+    return "{" + ", ".join(str(int(v)) for v in vals) + "}"
+
+
+def _align(x: int, a: int = ARENA_ALIGN) -> int:
+    return (x + a - 1) // a * a
+
+
+def _packed_conv_bytes(shape) -> int:
+    cout, cin, kh, kw = (int(s) for s in shape)
+    c4 = (cin + 3) // 4 * 4
+    kpad = (kh * kw * c4 + 31) // 32 * 32
+    return 2 * cout * kpad * 4
+
+
+class CudaBackend(BackendBase):
+    """Backend for ``Compiler(target="cuda")`` (see module docstring)."""
+
+    def __init__(self, debug_mode: bool = False, channels_last: bool = True):
+        self.debug_mode = debug_mode
+        self.channels_last = channels_last
+
+    def generate(self, ctx: CompileContext) -> CodeGenResult:
+        self._assign_symbols(ctx)
+        res = CodeGenResult()
+        plan = ctx.metadata.get("memory_allocation_plan")
+        if plan is None:
+            raise ValueError("cuda target needs a memory plan (run liveness + memory planning)")
+        layout = channels_last_tensors(ctx) if self.channels_last else set()
+        arena, arena_bytes = self._arena_offsets(ctx, plan)
+        consts, const_bytes = self._const_layout(ctx)
+        entry = ctx.metadata.get("entry_point", "nnc_run")
+        res.add_file("model.c", CudaEmitter().emit(ctx), "source")
+        res.add_file("model.h", self._model_h(ctx, entry), "header")
+        res.add_file("tensors.c", self._tensors_c(ctx, arena, arena_bytes, consts, const_bytes, layout), "source")
+        res.add_file("constants_loader.c", _CONSTANTS_LOADER, "source")
+        res.add_file("model_runtime.c", _MODEL_RUNTIME, "source")
+        res.add_file("test_runner.c", self._runner_c(ctx), "source")
+        res.add_file("Makefile", _MAKEFILE, "build")
+        manifest = {
+            "graph": ctx.graph.name,
+            "inputs": [{"name": n, "symbol": ctx.tensor_symbols[n], "shape": list(map(int, ctx.graph.tensors[n].shape.dims))} for n in ctx.graph.inputs],
+            "outputs": [{"name": n, "symbol": ctx.tensor_symbols[n], "shape": list(map(int, ctx.graph.tensors[n].shape.dims))} for n in ctx.graph.outputs],
+            "constants": [{"name": c["name"], "symbol": c["symbol"], "shape": c["shape"]} for c in consts],
+            "arena_bytes": arena_bytes,
+            "const_bytes": const_bytes,
+            "channels_last": sorted(ctx.tensor_symbols[t] for t in layout),
+            "calls": re.findall(r"\b(nnc_[a-z0-9_]+)\(&", res.files[0].content),
+        }
+        res.add_file("manifest.json", json.dumps(manifest, indent=1) + "\n", "build")
+        res.metadata["manifest"] = manifest
+        return res
+
+    # symbols as nnc-py's x86 backend names them (x86_backend.py:3563-3576)
+    def _assign_symbols(self, ctx: CompileContext) -> None:
+        nm = NameManager()
+        for t in ctx.graph.tensors:
+            ctx.tensor_symbols[t] = nm.get_symbol(t, prefix="tensor_")
+        for n in ctx.graph.nodes:
+            ctx.node_symbols[n] = nm.get_symbol(n, prefix="node_")
+
+    def _arena_offsets(self, ctx, plan):
+        """Byte offsets of every activation in the single device arena: the
+        cost_aware plan's offsets as they are (aliases and reuse included;
+        the plan aligns to 16 bytes, which is what the kernels' vector and
+        TMA paths need). Tensors the plan leaves out are appended."""
+        offsets = {name: int(a.offset) for name, a in plan.tensor_allocations.items()}
+        end = max([int(plan.total_fast_memory)] +
+                  [int(a.offset) + int(a.size) for a in plan.tensor_allocations.values()])
+        for t in list(ctx.graph.inputs) + list(ctx.graph.outputs):
+            if t not in offsets:
+                offsets[t] = _align(end)
+                end = offsets[t] + _align(int(np.prod(ctx.graph.tensors[t].shape.dims)) * 4)
+        for t, tt in ctx.graph.tensors.items():
+            if t in ctx.graph.constants or t in offsets:
+                continue
+            used = any(t in n.inputs or t in n.outputs for n in ctx.graph.nodes.values())
+            if used:
+                offsets[t] = _align(end)
+                end = offsets[t] + _align(int(np.prod(tt.shape.dims)) * 4)
+        return offsets, _align(end)
+
+    def _const_layout(self, ctx):
+        conv_weights = set()
+        for n in ctx.graph.nodes.values():
+            if n.op_type in (OpType.CONV2D, OpType.FUSED_CONV_RELU, OpType.FUSED_CONV_SIGMOID,
+                             OpType.FUSED_CONV_BIAS_RELU) and len(n.inputs) > 1 and n.inputs[1] in ctx.graph.constants:
+                conv_weights.add(n.inputs[1])
+        consts, off = [], 0
+        for name, arr in ctx.graph.constants.items():
+            arr = np.asarray(arr)
+            entry = {"name": name, "symbol": ctx.tensor_symbols[name], "shape": [int(s) for s in arr.shape],
+                     "nbytes": int(arr.nbytes), "offset": off, "packed_offset": -1, "packed_bytes": 0}
+            off = _align(off + int(arr.nbytes))
+            consts.append(entry)
+        for e in consts:
+            if e["name"] in conv_weights and len(e["shape"]) == 4:
+                e["packed_offset"] = off
+                e["packed_bytes"] = _packed_conv_bytes(e["shape"])
+                off = _align(off + e["packed_bytes"])
+        return consts, _align(max(off, ARENA_ALIGN))
+
+    def _model_h(self, ctx, entry):
+        ins = ", ".join(ctx.tensor_symbols[n] for n in ctx.graph.inputs)
+        outs = ", ".join(ctx.tensor_symbols[n] for n in ctx.graph.outputs)
+        return f"""/* Auto-generated by nnc_cuda (cuda target) - DO NOT EDIT */
+#ifndef NNC_MODEL_H
+#define NNC_MODEL_H
+
+#include <stddef.h>
+#include "nnc_types.h"
+
+#ifdef __cplusplus
+extern "C" {{
+#endif
+
+/* Inputs: {ins}; outputs: {outs}. Tensor data are device pointers. */
+
+/* Enqueues the forward pass on the calling thread's current stream
+ * (nnc_cuda_set_stream); returns without synchronising. */
+void {entry}(void);
+
+/* Selects `device`, allocates its activation arena and constant slab
+ * (one cudaMalloc each) and binds the tensors to them. */
+int nnc_model_init(int device);
+/* Rebinds the tensors to an initialised device's arena / constants. */
+int nnc_model_select(int device);
+void nnc_model_free(int device);
+/* Reads an NNCB v1 constants file, uploads it to the selected device and
+ * prepacks the conv weights there. Call once per device. */
+int nnc_load_constants(const char* path);
+int nnc_load_constants_from_memory(const void* data, size_t size);
+size_t nnc_model_arena_bytes(void);
+size_t nnc_model_const_bytes(void);
+int nnc_model_num_inputs(void);
+int nnc_model_num_outputs(void);
+Tensor* nnc_model_input(int i);
+Tensor* nnc_model_output(int i);
+/* Synchronous host-buffer forward on the selected device: input host ->
+ * device, forward, output device -> host (pinned buffers recommended). */
+int nnc_model_run_host(const void* input, void* output);
+
+#ifdef __cplusplus
+}}
+#endif
+
+#endif
+"""
+
+    def _tensors_c(self, ctx, arena, arena_bytes, consts, const_bytes, layout):
+        g = ctx.graph
+        L = ["/* Auto-generated by nnc_cuda (cuda target) - DO NOT EDIT */",
+             "#include <stddef.h>", "#include <stdint.h>", '#include "nnc_types.h"', '#include "nnc_cuda.h"',
+             '#include "nnc_model_tables.h"', "",
+             f"const size_t nnc_arena_bytes = {arena_bytes}u;",
+             f"const size_t nnc_const_bytes = {const_bytes}u;", ""]
+        act_entries, const_entries = [], []
+        for name, tt in g.tensors.items():
+            sym = ctx.tensor_symbols[name]
+            dims = [int(d) for d in tt.shape.dims]
+            n = int(np.prod(dims)) if dims else 1
+            is_const = name in g.constants
+            if not is_const and name not in arena:
+                continue
+            tag = " | NNC_CUDA_TAG_NHWC" if name in layout else ""
+            L.append(f"static int64_t {sym}_dims[] = {_c_array(dims or [1])};")
+            L.append(f"Tensor {sym} = {{.data = NULL, .dtype = (nnc_dtype_t)(NNC_DTYPE_FLOAT32{tag}), "
+                     f".shape = {sym}_dims, .ndim = {len(dims)}, .nbytes = {n * 4}}};")
+            if not is_const:
+                act_entries.append(f"    {{&{sym}, {arena[name]}u}},")
+        L.append("")
+        for c in consts:
+            const_entries.append(f'    {{"{c["symbol"]}", &{c["symbol"]}, {c["offset"]}u, {c["packed_offset"]}, '
+                                 f'{c["packed_bytes"]}u, {c["nbytes"]}u}},')
+        L.append("const nnc_arena_entry nnc_arena_table[] = {")
+        L += act_entries or ["    {NULL, 0u},"]
+        L.append("};")
+        L.append(f"const int nnc_arena_count = {len(act_entries)};")
+        L.append("const nnc_const_entry nnc_const_table[] = {")
+        L += const_entries or ['    {"", NULL, 0u, -1, 0u, 0u},']
+        L.append("};")
+        L.append(f"const int nnc_const_count = {len(const_entries)};")
+        L.append("Tensor* const nnc_input_table[] = {" + ", ".join(f"&{ctx.tensor_symbols[n]}" for n in g.inputs) + "};")
+        L.append(f"const int nnc_input_count = {len(g.inputs)};")
+        L.append("Tensor* const nnc_output_table[] = {" + ", ".join(f"&{ctx.tensor_symbols[n]}" for n in g.outputs) + "};")
+        L.append(f"const int nnc_output_count = {len(g.outputs)};")
+        return "\n".join(L) + "\n"
+
+    def _runner_c(self, ctx):
+        return _TEST_RUNNER
+
+
+_TABLES_H = """/* Shared declarations of the generated tables (cuda target). */
+#ifndef NNC_MODEL_TABLES_H
+#define NNC_MODEL_TABLES_H
+#include <stddef.h>
+#include "nnc_types.h"
+typedef struct { Tensor* tensor; size_t offset; } nnc_arena_entry;
+typedef struct {
+    const char* symbol; Tensor* tensor; size_t offset; long long packed_offset;
+    size_t packed_bytes; size_t nbytes;
+} nnc_const_entry;
+extern const size_t nnc_arena_bytes, nnc_const_bytes;
+extern const nnc_arena_entry nnc_arena_table[];
+extern const int nnc_arena_count;
+extern const nnc_const_entry nnc_const_table[];
+extern const int nnc_const_count;
+extern Tensor* const nnc_input_table[];
+extern const int nnc_input_count;
+extern Tensor* const nnc_output_table[];
+extern const int nnc_output_count;
+#endif
+"""
+
+_MODEL_RUNTIME = r"""/* Auto-generated by nnc_cuda (cuda target) - DO NOT EDIT
+ * Device arena / constant slab management: one cudaMalloc each per device;
+ * the Tensor globals are rebound when another device is selected. */
+#include <cuda_runtime.h>
+#include <stdio.h>
+#include "model.h"
+#include "nnc_cuda.h"
+#include "nnc_model_tables.h"
+
+#define NNC_MAX_DEVICES 16
+typedef struct { char* arena; char* slab; int ready; int packed; } nnc_device_state;
+static nnc_device_state g_dev[NNC_MAX_DEVICES];
+static int g_cur = -1;
+
+static int report(cudaError_t e, const char* what) {
+    if (e == cudaSuccess) return 0;
+    fprintf(stderr, "nnc_model: %s: %s\n", what, cudaGetErrorString(e));
+    return 1;
+}
+
+size_t nnc_model_arena_bytes(void) { return nnc_arena_bytes; }
+size_t nnc_model_const_bytes(void) { return nnc_const_bytes; }
+int nnc_model_num_inputs(void) { return nnc_input_count; }
+int nnc_model_num_outputs(void) { return nnc_output_count; }
+Tensor* nnc_model_input(int i) { return (i >= 0 && i < nnc_input_count) ? nnc_input_table[i] : NULL; }
+Tensor* nnc_model_output(int i) { return (i >= 0 && i < nnc_output_count) ? nnc_output_table[i] : NULL; }
+
+int nnc_model_select(int device) {
+    if (device < 0 || device >= NNC_MAX_DEVICES || !g_dev[device].ready) return 1;
+    if (report(cudaSetDevice(device), "cudaSetDevice")) return 1;
+    nnc_cuda_init(device);
+    for (int i = 0; i < nnc_arena_count; ++i)
+        nnc_arena_table[i].tensor->data = g_dev[device].arena + nnc_arena_table[i].offset;
+    for (int i = 0; i < nnc_const_count; ++i) {
+        const nnc_const_entry* c = &nnc_const_table[i];
+        const int packed = g_dev[device].packed && c->packed_offset >= 0;
+        c->tensor->data = g_dev[device].slab + (packed ? (size_t)c->packed_offset : c->offset);
+    }
+    g_cur = device;
+    return 0;
+}
+
+int nnc_model_init(int device) {
+    if (device < 0 || device >= NNC_MAX_DEVICES) return 1;
+    if (g_dev[device].ready) return nnc_model_select(device);
+    if (report(cudaSetDevice(device), "cudaSetDevice")) return 1;
+    if (nnc_cuda_init(device) != 0) return 1;
+    if (report(cudaMalloc((void**)&g_dev[device].arena, nnc_arena_bytes), "arena cudaMalloc")) return 1;
+    if (report(cudaMalloc((void**)&g_dev[device].slab, nnc_const_bytes), "constant slab cudaMalloc")) return 1;
+    g_dev[device].ready = 1;
+    g_dev[device].packed = 0;
+    return nnc_model_select(device);
+}
+
+void nnc_model_free(int device) {
+    if (device < 0 || device >= NNC_MAX_DEVICES || !g_dev[device].ready) return;
+    cudaSetDevice(device);
+    cudaFree(g_dev[device].arena);
+    cudaFree(g_dev[device].slab);
+    g_dev[device].ready = 0;
+    if (g_cur == device) g_cur = -1;
+}
+
+/* Used by the constants loader. */
+char* nnc_model_slab(void) { return g_cur >= 0 ? g_dev[g_cur].slab : NULL; }
+void nnc_model_mark_packed(void) { if (g_cur >= 0) g_dev[g_cur].packed = 1; }
+int nnc_model_is_packed(void) { return g_cur >= 0 ? g_dev[g_cur].packed : 0; }
+
+int nnc_model_run_host(const void* input, void* output) {
+    if (g_cur < 0) return 1;
+    cudaStream_t s = (cudaStream_t)nnc_cuda_get_stream();
+    Tensor* in = nnc_input_table[0];
+    Tensor* out = nnc_output_table[0];
+    if (report(cudaMemcpyAsync(in->data, input, (size_t)in->nbytes, cudaMemcpyHostToDevice, s), "input copy")) return 1;
+    nnc_run();
+    if (report(cudaMemcpyAsync(output, out->data, (size_t)out->nbytes, cudaMemcpyDeviceToHost, s), "output copy")) return 1;
+    if (report(cudaStreamSynchronize(s), "sync")) return 1;
+    return nnc_cuda_get_last_error();
+}
+"""
+
+_CONSTANTS_LOADER = r"""/* Auto-generated by nnc_cuda (cuda target) - DO NOT EDIT
+ * Loads nnc-py's NNCB v1 constants container: 'NNCB', u32 version (1),
+ * u32 count, then per constant u32 name_len, name (NUL-terminated), u32
+ * dtype, u32 ndim, i64 shape[ndim], u64 nbytes, data. Entries must appear in
+ * the order and with the names/sizes of the generated table (as nnc-py's x86
+ * loader requires). Data go to the selected device's constant slab; conv
+ * weights are then prepacked on the device (nnc_cuda_prepack_conv_weight). */
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+#include "model.h"
+#include "nnc_cuda.h"
+#include "nnc_model_tables.h"
+
+char* nnc_model_slab(void);
+void nnc_model_mark_packed(void);
+int nnc_model_is_packed(void);
+
+static int rd(const unsigned char** p, const unsigned char* end, void* dst, size_t n) {
+    if ((size_t)(end - *p) < n) return 1;
+    memcpy(dst, *p, n);
+    *p += n;
+    return 0;
+}
+
+int nnc_load_constants_from_memory(const void* data, size_t size) {
+    const unsigned char* p = (const unsigned char*)data;
+    const unsigned char* end = p + size;
+    char* slab = nnc_model_slab();
+    uint32_t version = 0, count = 0;
+    if (!slab) { fprintf(stderr, "nnc_load_constants: no device selected\n"); return 1; }
+    if (size < 12 || memcmp(p, "NNCB", 4) != 0) { fprintf(stderr, "nnc_load_constants: bad magic\n"); return 1; }
+    p += 4;
+    if (rd(&p, end, &version, 4) || version != 1) { fprintf(stderr, "nnc_load_constants: unsupported version %u\n", version); return 1; }
+    if (rd(&p, end, &count, 4) || (int)count != nnc_const_count) {
+        fprintf(stderr, "nnc_load_constants: %u constants in file, model has %d\n", count, nnc_const_count);
+        return 1;
+    }
+    for (int i = 0; i < nnc_const_count; ++i) {
+        const nnc_const_entry* c = &nnc_const_table[i];
+        uint32_t name_len = 0, dtype = 0, ndim = 0;
+        uint64_t nbytes = 0;
+        if (rd(&p, end, &name_len, 4) || name_len == 0 || (size_t)(end - p) < name_len) return 1;
+        if (strncmp((const char*)p, c->symbol, name_len) != 0) {
+            fprintf(stderr, "nnc_load_constants: entry %d is '%.*s', expected '%s'\n", i, (int)name_len, (const char*)p, c->symbol);
+            return 1;
+        }
+        p += name_len;
+        if (rd(&p, end, &dtype, 4) || rd(&p, end, &ndim, 4) || ndim > 8) return 1;
+        if ((size_t)(end - p) < 8u * ndim) return 1;
+        p += 8u * ndim;
+        if (rd(&p, end, &nbytes, 8) || nbytes != c->nbytes || (uint64_t)(end - p) < nbytes) {
+            fprintf(stderr, "nnc_load_constants: '%s' has %llu bytes, expected %zu\n", c->symbol, (unsigned long long)nbytes, c->nbytes);
+            return 1;
+        }
+        if (cudaMemcpy(slab + c->offset, p, nbytes, cudaMemcpyHostToDevice) != cudaSuccess) return 1;
+        p += nbytes;
+    }
+    if (!nnc_model_is_packed()) {
+        for (int i = 0; i < nnc_const_count; ++i) {
+            const nnc_const_entry* c = &nnc_const_table[i];
+            if (c->packed_offset < 0) continue;
+            c->tensor->data = slab + c->offset;
+            c->tensor->dtype = (nnc_dtype_t)((int)c->tensor->dtype & NNC_CUDA_DTYPE_MASK);
+            if (nnc_cuda_prepack_conv_weight(c->tensor, slab + c->packed_offset, c->packed_bytes) != 0) return 1;
+        }
+        nnc_model_mark_packed();
+    } else {
+        /* Re-upload on an already packed device: repack from the fresh raw data. */
+        for (int i = 0; i < nnc_const_count; ++i) {
+            const nnc_const_entry* c = &nnc_const_table[i];
+            if (c->packed_offset < 0) continue;
+            int tagged = (int)c->tensor->dtype;
+            c->tensor->data = slab + c->offset;
+            c->tensor->dtype = (nnc_dtype_t)(tagged & NNC_CUDA_DTYPE_MASK);
+            if (nnc_cuda_prepack_conv_weight(c->tensor, slab + c->packed_offset, c->packed_bytes) != 0) return 1;
+        }
+    }
+    if (cudaStreamSynchronize((cudaStream_t)nnc_cuda_get_stream()) != cudaSuccess) return 1;
+    return nnc_cuda_get_last_error();
+}
+
+int nnc_load_constants(const char* path) {
+    FILE* f = fopen(path, "rb");
+    if (!f) { fprintf(stderr, "nnc_load_constants: cannot open %s\n", path); return 1; }
+    fseek(f, 0, SEEK_END);
+    long n = ftell(f);
+    fseek(f, 0, SEEK_SET);
+    void* buf = malloc((size_t)n);
+    int rc = (buf && fread(buf, 1, (size_t)n, f) == (size_t)n) ? nnc_load_constants_from_memory(buf, (size_t)n) : 1;
+    free(buf);
+    fclose(f);
+    return rc;
+}
+"""
+
+_TEST_RUNNER = r"""/* Auto-generated by nnc_cuda (cuda target) - DO NOT EDIT
+ * Usage: ./model constants.bin input.bin output.bin [num_gpus] [iters]
+ * input.bin holds num_gpus x (compiled batch) samples; GPU g runs samples
+ * [g*B, (g+1)*B) with its own arena and constants; the outputs are gathered
+ * to GPU 0 (peer copies over NVLink) and written to output.bin. With
+ * iters > 0 the forward is timed with CUDA events (max over GPUs). */
+#include <cuda_runtime.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include "model.h"
+#include "nnc_cuda.h"
+
+#define CHECK(x) do { cudaError_t e_ = (x); if (e_ != cudaSuccess) { fprintf(stderr, "%s: %s\n", #x, cudaGetErrorString(e_)); return 1; } } while (0)
+
+int main(int argc, char** argv) {
+    if (argc < 4) { fprintf(stderr, "usage: %s constants.bin input.bin output.bin [num_gpus] [iters]\n", argv[0]); return 2; }
+    int gpus = argc > 4 ? atoi(argv[4]) : 1;
+    int iters = argc > 5 ? atoi(argv[5]) : 0;
+    int avail = 0;
+    CHECK(cudaGetDeviceCount(&avail));
+    if (gpus < 1 || gpus > avail || gpus > 16) { fprintf(stderr, "need %d GPUs, have %d\n", gpus, avail); return 2; }
+    Tensor* in = nnc_model_input(0);
+    Tensor* out = nnc_model_output(0);
+    size_t in_b = (size_t)in->nbytes, out_b = (size_t)out->nbytes;
+    FILE* f = fopen(argv[2], "rb");
+    if (!f) { fprintf(stderr, "cannot open %s\n", argv[2]); return 1; }
+    char* host_in = NULL;
+    char* host_out = NULL;
+    CHECK(cudaMallocHost((void**)&host_in, in_b * gpus));
+    CHECK(cudaMallocHost((void**)&host_out, out_b * gpus));
+    if (fread(host_in, 1, in_b * gpus, f) != in_b * gpus) { fprintf(stderr, "input.bin must hold %zu bytes\n", in_b * gpus); return 1; }
+    fclose(f);
+    cudaStream_t streams[16];
+    cudaEvent_t t0[16], t1[16];
+    void* out_dev[16];
+    for (int g = 0; g < gpus; ++g) {
+        if (nnc_model_init(g) != 0) return 1;
+        CHECK(cudaStreamCreateWithFlags(&streams[g], cudaStreamNonBlocking));
+        nnc_cuda_set_stream(streams[g]);
+        if (nnc_load_constants(argv[1]) != 0) { fprintf(stderr, "constants failed on GPU %d\n", g); return 1; }
+        CHECK(cudaEventCreate(&t0[g]));
+        CHECK(cudaEventCreate(&t1[g]));
+        out_dev[g] = out->data;
+        if (g > 0) { int ok = 0; cudaDeviceCanAccessPeer(&ok, 0, g); if (ok) { cudaSetDevice(0); cudaDeviceEnablePeerAccess(g, 0); cudaSetDevice(g); } }
+    }
+    void* gather = NULL;
+    nnc_model_select(0);
+    CHECK(cudaMalloc(&gather, out_b * gpus));
+    int reps = iters > 0 ? iters : 1;
+    float worst = 0.f;
+    for (int it = 0; it < reps + (iters > 0 ? 1 : 0); ++it) {
+        for (int g = 0; g < gpus; ++g) {
+            nnc_model_select(g);
+            nnc_cuda_set_stream(streams[g]);
+            CHECK(cudaMemcpyAsync(in->data, host_in + (size_t)g * in_b, in_b, cudaMemcpyHostToDevice, streams[g]));
+            CHECK(cudaEventRecord(t0[g], streams[g]));
+            nnc_run();
+            CHECK(cudaEventRecord(t1[g], streams[g]));
+        }
+        for (int g = 0; g < gpus; ++g) {
+            CHECK(cudaSetDevice(g));
+            CHECK(cudaStreamSynchronize(streams[g]));
+            float ms = 0.f;
+            CHECK(cudaEventElapsedTime(&ms, t0[g], t1[g]));
+            if (it > 0 || iters == 0) worst = ms > worst ? ms : worst;
+        }
+    }
+    CHECK(cudaSetDevice(0));
+    for (int g = 0; g < gpus; ++g)
+        CHECK(cudaMemcpyPeerAsync((char*)gather + (size_t)g * out_b, 0, out_dev[g], g, out_b, streams[0]));
+    CHECK(cudaMemcpyAsync(host_out, gather, out_b * gpus, cudaMemcpyDeviceToHost, streams[0]));
+    CHECK(cudaStreamSynchronize(streams[0]));
+    if (nnc_cuda_get_last_error() != 0) { fprintf(stderr, "runtime error: %s\n", nnc_cuda_get_last_error_string()); return 1; }
+    f = fopen(argv[3], "wb");
+    if (!f || fwrite(host_out, 1, out_b * gpus, f) != out_b * gpus) return 1;
+    fclose(f);
+    printf("forward over %d GPU(s): %.3f ms (max over GPUs)\n", gpus, worst);
+    return 0;
+}
+"""
+
+_MAKEFILE = """# Auto-generated by nnc_cuda (cuda target) - DO NOT EDIT
+# NNC_CUDA_ROOT: repository root holding include/ and nnc-py_b200/nnc_cuda/libnnc_cuda.so
+NNC_CUDA_ROOT ?= ../../..
+NVCC ?= nvcc
+CFLAGS = -O2 -arch=sm_100a -Xcompiler -fPIC -I. -I$(NNC_CUDA_ROOT)/include
+LIBDIR = $(NNC_CUDA_ROOT)/nnc-py_b200/nnc_cuda
+LDFLAGS = -L$(LIBDIR) -lnnc_cuda -Xlinker -rpath,$(abspath $(LIBDIR))
+SRCS = model.c tensors.c constants_loader.c model_runtime.c
+
+all: libmodel.so model
+
+libmodel.so: $(SRCS) model.h nnc_model_tables.h
+\t$(NVCC) $(CFLAGS) -x cu -shared -o $@ $(SRCS) $(LDFLAGS)
+
+model: test_runner.c libmodel.so
+\t$(NVCC) $(CFLAGS) -x cu -o $@ test_runner.c -L. -lmodel -Xlinker -rpath,'$$ORIGIN' $(LDFLAGS)
+
+clean:
+\trm -f libmodel.so model
+
+.PHONY: all clean
+"""
+
+
+def compile_model(model: Model, out_dir: str | pathlib.Path, opt_level: int = 3,
+                  channels_last: bool = True) -> dict[str, Any]:
+    """Runs the cuda target on a workload Model and writes the artifacts."""
+    ctx = CompileContext(to_nnc_graph(model), "cuda", opt_level)
+    ctx.metadata["entry_point"] = "nnc_run"
+    pm = PassManager()
+    for p in cuda_passes(opt_level):
+        pm.register(p)
+    pm.run(ctx)
+    res = CudaBackend(channels_last=channels_last).generate(ctx)
+    out = pathlib.Path(out_dir)
+    out.mkdir(parents=True, exist_ok=True)
+    for a in res.files:
+        (out / a.filename).write_text(a.content) if isinstance(a.content, str) else (out / a.filename).write_bytes(a.content)
+    (out / "nnc_model_tables.h").write_text(_TABLES_H)
+    return res.metadata["manifest"]
+
+
+def install() -> None:
+    """Adds the ``cuda`` target to nnc-py's Compiler and CLI in-process."""
+    from nnc_py import cli as nnc_cli
+    from nnc_py import compiler as nnc_compiler
+
+    orig_create = nnc_compiler.Compiler._create_backend
+    orig_passes = nnc_compiler.Compiler._get_passes
+
+    def _create_backend(self, target):
+        if target == "cuda":
+            return CudaBackend(debug_mode=self.debug_mode)
+        return orig_create(self, target)
+
+    def _get_passes(self):
+        if self.target == "cuda":
+            return cuda_passes(self.opt_level)
+        return orig_passes(self)
+
+    nnc_compiler.Compiler._create_backend = _create_backend
+    nnc_compiler.Compiler._get_passes = _get_passes
+    for p in nnc_cli.compile.params:
+        if p.name == "target" and "cuda" not in p.type.choices:
+            p.type.choices = list(p.type.choices) + ["cuda"]

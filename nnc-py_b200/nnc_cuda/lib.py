@@ -61,13 +61,15 @@ _CTYPE_OF = {
     "float": ctypes.c_float,
     "int64_t*": ctypes.POINTER(ctypes.c_int64),
     "void*": ctypes.c_void_p,
+    "const void*": ctypes.c_void_p,
     "size_t": ctypes.c_size_t,
     "const char*": ctypes.c_char_p,
     "void": None,
+    "long long": ctypes.c_longlong,
 }
 
 _PROTO_RE = re.compile(
-    r"^\s*(void\*|void|int|size_t|const char\*)\s+(nnc_\w+)\s*\(([^)]*)\)\s*;", re.M | re.S
+    r"^\s*(void\*|void|int|size_t|const char\*|long long)\s+(nnc_\w+)\s*\(([^)]*)\)\s*;", re.M | re.S
 )
 
 

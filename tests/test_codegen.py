@@ -1,0 +1,113 @@
+"""The cuda codegen target (CPU-only; needs nnc-py importable, i.e. where the
+reference checkout exists — skipped elsewhere)."""
+
+import pathlib
+import re
+import sys
+
+import numpy as np
+import pytest
+
+ROOT = pathlib.Path(__file__).resolve().parent.parent
+REF_SRC = pathlib.Path("/root/reference/src")
+if REF_SRC.exists() and str(REF_SRC) not in sys.path:
+    sys.path.insert(0, str(REF_SRC))
+nnc_py = pytest.importorskip("nnc_py")
+
+from nnc_cuda import codegen as CG  # noqa: E402
+from nnc_cuda import workloads as W  # noqa: E402
+
+GEN = ROOT / "nnc-py_b200" / "models_gen"
+
+
+def test_committed_sources_are_up_to_date(tmp_path):
+    sys.path.insert(0, str(GEN))
+    import generate
+
+    for d, model, batch, opt in generate.CONFIGS:
+        out = tmp_path / d
+        CG.compile_model(W.BUILDERS[model](batch), out, opt_level=opt)
+        for f in sorted(p.name for p in out.iterdir()):
+            assert (GEN / d / f).read_text() == (out / f).read_text(), f"{d}/{f} is stale: rerun generate.py"
+
+
+def _x86_calls(model, opt):
+    from nnc_py.codegen.x86_backend import X86Backend
+    from nnc_py.ir.context import CompileContext
+    from nnc_py.passes.base import PassManager
+
+    ctx = CompileContext(CG.to_nnc_graph(model), "x86", opt)
+    ctx.metadata["entry_point"] = "nnc_run"
+    pm = PassManager()
+    for p in PassManager.get_default_passes(opt):
+        pm.register(p)
+    pm.run(ctx)
+    src = next(a.content for a in X86Backend().generate(ctx).files if a.filename == "model.c")
+    return re.findall(r"^\s*(nnc_\w+\(.*\));", src, re.M)
+
+
+@pytest.mark.parametrize("name,batch", [("resnet18", 2), ("lenet5", 4), ("transformer", 1)])
+def test_o1_call_lines_equal_the_x86_backend(tmp_path, name, batch):
+    """At O1 the cuda target emits exactly the operator calls nnc-py's x86
+    backend emits (the library is a drop-in for ops.c)."""
+    model = W.BUILDERS[name](batch)
+    CG.compile_model(model, tmp_path, opt_level=1)
+    ours = re.findall(r"^\s*(nnc_\w+\(.*\));", (tmp_path / "model.c").read_text(), re.M)
+    assert ours == _x86_calls(model, 1)
+
+
+def test_o3_fuses_every_residual_join(tmp_path):
+    man = CG.compile_model(W.resnet18(2), tmp_path, opt_level=3)
+    calls = man["calls"]
+    assert calls.count("nnc_conv_add_relu3x3_s1") == 8
+    assert "nnc_add" not in calls and "nnc_relu" not in calls and "nnc_add_relu" not in calls
+    assert calls.count("nnc_conv_relu3x3_s1") + calls.count("nnc_conv_relu") == 8
+    assert calls[0] == "nnc_conv_relu7x7_s2" and calls[-1] == "nnc_gemm_nt"
+
+
+def test_channels_last_assignment(tmp_path):
+    man = CG.compile_model(W.resnet18(2), tmp_path, opt_level=3)
+    cl = set(man["channels_last"])
+    assert "tensor_input" not in cl          # user-facing NCHW input
+    assert "tensor_pool1" in cl and "tensor_gap" in cl
+    assert "tensor_logits" not in cl and "tensor_flat" not in cl  # 2-D
+    man_t = CG.compile_model(W.transformer(1), tmp_path / "t", opt_level=1)
+    assert man_t["channels_last"] == []  # 4-D tensors meet transpose/softmax
+
+
+def test_arena_offsets_follow_the_cost_aware_plan(tmp_path):
+    man = CG.compile_model(W.resnet18(8), tmp_path, opt_level=3)
+    src = (tmp_path / "tensors.c").read_text()
+    offs = [int(v) for v in re.findall(r"\{&tensor_\w+, (\d+)u\}", src)]
+    assert offs and all(o % 16 == 0 for o in offs)
+    assert max(offs) < man["arena_bytes"]
+    # reuse: the arena is far smaller than all activations back to back
+    total = sum(int(np.prod(s)) * 4 for n, s in W.resnet18(8).shapes.items() if not n.endswith(("_w", "_b")))
+    assert man["arena_bytes"] < total / 3
+
+
+def test_compiler_and_cli_gain_the_cuda_target():
+    CG.install()
+    from nnc_py import cli as nnc_cli
+    from nnc_py.compiler import Compiler
+
+    c = Compiler(target="cuda", opt_level=3)
+    assert isinstance(c.backend, CG.CudaBackend)
+    names = [p.name for p in c._get_passes()]
+    assert "CudaConvAddReluFusion" in names
+    target = next(p for p in nnc_cli.compile.params if p.name == "target")
+    assert "cuda" in target.type.choices
+
+
+def test_constants_blob_matches_reference_container():
+    """The NNCB bytes the runtime uploads equal what nnc-py's x86 backend
+    writes for the same graph."""
+    from nnc_py.codegen.x86_emitters.constants_loader import generate_constants_binary
+    from nnc_py.ir.context import CompileContext
+
+    model = W.lenet5(1)
+    ctx = CompileContext(CG.to_nnc_graph(model), "x86", 1)
+    CG.CudaBackend()._assign_symbols(ctx)
+    ref_bytes, _ = generate_constants_binary(ctx)
+    ours = W.nncb_bytes([(ctx.tensor_symbols[n], a) for n, a in model.constants.items()])
+    assert ours == ref_bytes

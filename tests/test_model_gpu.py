@@ -1,0 +1,75 @@
+"""Model-level parity on the GPU: cuda-target builds of the BASELINE graphs
+(nnc-py_b200/models_gen) against the reference's own x86 build of the same
+graphs on the same seeded inputs (tests/golden/models.npz)."""
+
+import pathlib
+
+import numpy as np
+import pytest
+
+import opcases as C
+from nnc_cuda import lib as L
+from nnc_cuda import workloads as W
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = pathlib.Path(__file__).resolve().parent / "golden" / "models.npz"
+# End-to-end tolerances (normwise rtol, see opcases.assert_close): per-op
+# TF32 rounding compounds over ResNet-18's 20 convolutions.
+MODEL_RTOL = {L.PRECISION_TF32: 2e-2, L.PRECISION_3XTF32: 1e-4}
+
+
+@pytest.fixture(scope="module")
+def golden():
+    z = np.load(GOLDEN)
+    return {k: z[k] for k in z.files}
+
+
+def _model(tag):
+    from nnc_cuda.model import CudaModel
+
+    m = CudaModel(tag)
+    m.init(0)
+    return m
+
+
+@pytest.mark.parametrize("prec", [L.PRECISION_TF32, L.PRECISION_3XTF32])
+@pytest.mark.parametrize("tag", ["resnet18_o3_b2", "resnet18_o1_b2"])
+def test_resnet18_matches_reference_x86_build(cuda_lib, golden, tag, prec):
+    m = _model(tag)
+    m.load_constants(W.resnet18(2))
+    cuda_lib.nnc_cuda_set_precision(prec)
+    got = m.run_host(golden["resnet18_b2/input"])
+    want = golden["resnet18_b2/output"]
+    C.assert_close(got, want, MODEL_RTOL[prec], f"{tag} prec{prec}")
+    assert np.array_equal(got.argmax(1), want.argmax(1))
+
+
+@pytest.mark.parametrize("prec", [L.PRECISION_TF32, L.PRECISION_3XTF32])
+def test_resnet18_batch_shards_agree(cuda_lib, golden, prec):
+    """Sample independence (what batch sharding across GPUs relies on): the
+    first two images of a batch-128 forward equal the batch-2 reference."""
+    m = _model("resnet18_o3_b128")
+    model = W.resnet18(128)
+    m.load_constants(model)
+    cuda_lib.nnc_cuda_set_precision(prec)
+    got = m.run_host(model.input_array(128))
+    C.assert_close(got[:2], golden["resnet18_b2/output"], MODEL_RTOL[prec], f"b128[:2] prec{prec}")
+
+
+def test_lenet5_matches_reference_x86_build(cuda_lib, golden):
+    m = _model("lenet5_o1_b16")
+    m.load_constants(W.lenet5(16))
+    for prec in (L.PRECISION_TF32, L.PRECISION_3XTF32):
+        cuda_lib.nnc_cuda_set_precision(prec)
+        got = m.run_host(golden["lenet5_b16/input"])
+        C.assert_close(got, golden["lenet5_b16/output"], MODEL_RTOL[prec], f"lenet5 prec{prec}")
+
+
+def test_transformer_matches_reference_x86_build(cuda_lib, golden):
+    m = _model("transformer_o1_b1")
+    m.load_constants(W.transformer(1))
+    for prec in (L.PRECISION_TF32, L.PRECISION_3XTF32):
+        cuda_lib.nnc_cuda_set_precision(prec)
+        got = m.run_host(golden["transformer_b1/input"])
+        C.assert_close(got, golden["transformer_b1/output"], MODEL_RTOL[prec], f"transformer prec{prec}")
