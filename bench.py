@@ -340,6 +340,7 @@ def roofline_traffic():
 
 
 def main():
+    global GLOBAL_BATCH
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
@@ -347,9 +348,12 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--precision", choices=["tf32", "3xtf32"], default="tf32")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--global-batch", type=int, default=GLOBAL_BATCH,
+                    help="profiling only: a smaller global batch (the headline is 1024)")
     opt = ap.parse_args()
     if opt.warmup < 3:
         opt.warmup = 3
+    GLOBAL_BATCH = opt.global_batch
     if opt.impl == "reference":
         return reference_arm(opt)
     return our_arm(opt)

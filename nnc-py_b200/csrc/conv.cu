@@ -1,25 +1,34 @@
 // 2-D convolution as an implicit GEMM on the sm_100a tensor cores.
 //
-//   D[m, co] = sum_k A[m, k] * W[co, k]      m  = (n, oh, ow) output pixel
-//                                            k  = (kh, kw, ci) tap x channel
-// Activations are read channels-last (NHWC, channels padded to a multiple
-// of 4 = one 16-byte chunk), weights are packed [C_out][K_pad] with the same
-// k order (K_pad a multiple of 32). NCHW tensors at the API are converted to
-// NHWC in scratch memory; tensors tagged NNC_CUDA_TAG_NHWC are used in place.
+//   D[m, co] = sum_k A[m, k] * W[co, k]      m = (n, oh, ow) output pixel
+//                                            k = tap x input channel
+// Weights are packed [C_out][K_pad] (K_pad a multiple of 32) in one of two k
+// orders chosen from the weight shape (see weight_layout):
+//   chunk mode   k = (kh, kw, c) with channels padded to a multiple of 4, read
+//                NHWC: NNC_CUDA_TAG_NHWC inputs with C % 4 == 0 in place,
+//                others (NCHW drop-in calls, the RGB model input) converted
+//                in scratch memory first;
+//   element mode (reductions of at most 64, e.g. LeNet's 1x5x5 conv):
+//                k = (c, kh, kw), the OIHW order, read in place in either
+//                layout.
 //
 // Kernel (persistent, one CTA per SM, 288 threads):
-//   warps 0..3  producers: thread r gathers row r (one output pixel) of the
-//               128 x 32 A tile with 16-byte cp.async (zero-fill for taps
-//               that fall in the padding), written in the 128-byte swizzle
-//               layout; thread 0 also TMA-loads the BN x 32 weight tile.
-//               Arrival on the stage barrier is asynchronous
+//   warps 0..3  producers: gather the 128 x 32 A tile with cp.async (zero
+//               fill for taps in the padding) into the 128-byte swizzle
+//               layout — chunk mode: 16-byte copies, eight neighbouring
+//               threads per 128-byte row so each warp instruction reads four
+//               whole rows; element mode: 4-byte copies with per-k offsets
+//               from a shared-memory table. Thread 0 also TMA-loads the
+//               BN x 32 weight tile. Arrival is asynchronous
 //               (cp.async.mbarrier.arrive.noinc), so producers run ahead.
 //   warp 4      TMEM allocation + single-thread tcgen05.mma issue (kind::tf32,
 //               M = 128, N = BN, 4 k-steps per stage; 3 MMAs per k-step in
 //               3xTF32 mode), commits release ring slots and accumulators.
-//   warps 5..8  epilogue: tcgen05.ld, + bias, (+ residual), activation, store
-//               NHWC rows (16-byte vectors) or NCHW planes (coalesced across
-//               the warp's 32 consecutive pixels).
+//   warps 5..8  epilogue: tcgen05.ld of 32 columns at a time; NHWC outputs
+//               are staged through a 32 x 33 shared tile so bias, residual
+//               and stores run row-contiguously (eight lanes per 128-byte
+//               row); NCHW outputs store per channel plane, coalesced across
+//               the warp's 32 consecutive pixels.
 //
 // Reference semantics (ops.c:720-1050): window origin o*stride - pad with the
 // top/left pad only, out-of-range taps contribute zero, output extent from
@@ -40,17 +49,30 @@ constexpr int kConvThreads = 288;
 
 enum Act : int { kActNone = 0, kActRelu = 1, kActSigmoid = 2, kActAddRelu = 3 };
 
+// Gather modes for the A (activation) operand.
+//   kChunk:   NHWC input, C4 % 4 == 0; k = (kh, kw, c); each 16-byte chunk of
+//             a 128-byte stage row is four consecutive channels of one tap,
+//             copied by one thread; eight neighbouring threads fill a row, so
+//             a warp instruction covers four rows.
+//   kElement: any input layout (strides) and any channel count; k = (c, kh,
+//             kw), i.e. the OIHW weight order; 4-byte cp.async per element,
+//             per-k offsets from a table in shared memory.
+enum Mode : int { kChunk = 0, kElement = 1 };
+constexpr int kMaxElementK = 64;  // K_pad limit of the element mode (see weight_layout)
+
 struct ConvArgs {
+  int mode;
   // geometry
-  int N, H, W, C4;  // input (NHWC, C4 channels incl. padding)
+  int N, H, W, C4;  // input; C4 = channels as stored (kChunk: padded to 4)
   int OH, OW, Cout;
   int KH, KW, sh, sw, ph, pw;
-  int K;  // KH*KW*C4 (valid k), K_pad = kblocks*32
+  int K;  // valid k extent (kChunk: KH*KW*C4, kElement: C*KH*KW)
   int kblocks;
   int64_t M;  // N*OH*OW
   int m_tiles, n_tiles;
   int64_t tiles;
-  const float* x_hi;  // NHWC input (hi plane in 3xTF32 mode)
+  int64_t xs_n, xs_c, xs_h, xs_w;  // element-mode input strides (elements)
+  const float* x_hi;  // input (hi plane in 3xTF32 mode)
   const float* x_lo;  // lo plane (3xTF32) or nullptr
   const float* bias;
   const float* residual;  // same layout as the output
@@ -69,13 +91,19 @@ __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32
                "r"(src_bytes)
                : "memory");
 }
+__device__ __forceinline__ void cp_async4(uint32_t dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src),
+               "r"(src_bytes)
+               : "memory");
+}
 __device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
   asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(tc::smem_u32(bar))
                : "memory");
 }
-__device__ __forceinline__ void fence_proxy_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
+
+// Epilogue staging: one 32 x 33 fp32 tile per epilogue warp.
+constexpr int kStageCols = 32;
+constexpr uint32_t kEpiBytes = 4 * 32 * (kStageCols + 1) * 4;
 
 template <int BN, int SPLIT, int STAGES>
 struct ConvCfg {
@@ -83,8 +111,17 @@ struct ConvCfg {
   static constexpr uint32_t B_BYTES = BN * BK * 4;
   static constexpr uint32_t STAGE_BYTES = SPLIT * (A_BYTES + B_BYTES);
   static constexpr uint32_t TMEM_COLS = 2 * BN;
-  static constexpr size_t SMEM = (size_t)STAGES * STAGE_BYTES + 1024 + 256;
+  static constexpr uint32_t EPI_OFF = STAGES * STAGE_BYTES;
+  static constexpr uint32_t KTAB_OFF = EPI_OFF + kEpiBytes;
+  static constexpr uint32_t BAR_OFF = KTAB_OFF + 2 * kMaxElementK * 4;
+  static constexpr size_t SMEM = (size_t)BAR_OFF + 256 + 1024;
 };
+
+__device__ __forceinline__ float activate(float o, int act) {
+  if (act == kActRelu || act == kActAddRelu) return o > 0.0f ? o : 0.0f;
+  if (act == kActSigmoid) return 1.0f / (1.0f + expf(-o));
+  return o;
+}
 
 template <int BN, int SPLIT, int STAGES>
 __global__ void __launch_bounds__(kConvThreads, 1)
@@ -93,7 +130,10 @@ __global__ void __launch_bounds__(kConvThreads, 1)
   using Cfg = ConvCfg<BN, SPLIT, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES);
+  float* epi = reinterpret_cast<float*>(smem + Cfg::EPI_OFF);
+  int* ktab_off = reinterpret_cast<int*>(smem + Cfg::KTAB_OFF);
+  int* ktab_hw = ktab_off + kMaxElementK;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::BAR_OFF);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
@@ -116,6 +156,20 @@ __global__ void __launch_bounds__(kConvThreads, 1)
     tc::prefetch_tmap(&tmW0);
     if (SPLIT == 2) tc::prefetch_tmap(&tmW1);
   }
+  if (g.mode == kElement) {
+    // k -> (element offset from the window origin, kh << 16 | kw); -1 past K.
+    const int taps = g.KH * g.KW;
+    for (int k = threadIdx.x; k < g.kblocks * BK; k += blockDim.x) {
+      if (k < g.K) {
+        const int c = k / taps, t = k - c * taps, kh = t / g.KW, kw = t - kh * g.KW;
+        ktab_off[k] = (int)(c * g.xs_c + kh * g.xs_h + kw * g.xs_w);
+        ktab_hw[k] = (kh << 16) | kw;
+      } else {
+        ktab_off[k] = 0;
+        ktab_hw[k] = -1;
+      }
+    }
+  }
   if (warp == 4) {
     tc::tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
     tc::tmem_relinquish();
@@ -127,67 +181,112 @@ __global__ void __launch_bounds__(kConvThreads, 1)
 
   if (warp < 4) {
     // ---------------- producers: im2col gather of A, TMA of W ----------------
-    const int row = threadIdx.x;  // 0..127
+    const int t = threadIdx.x;  // 0..127
     const int64_t OHW = (int64_t)g.OH * g.OW;
     const int taps = g.KH * g.KW;
-    const bool chan32 = (g.C4 % 32) == 0;
     int stage = 0;
     uint32_t phase = 0;
     bool ok = true;
-    for (int64_t t = blockIdx.x; t < g.tiles && ok; t += gridDim.x) {
-      const int mt = (int)(t / g.n_tiles), nt = (int)(t % g.n_tiles);
-      const int64_t m = (int64_t)mt * BM + row;
-      const bool row_ok = m < g.M;
-      int n_img = 0, ih0 = 0, iw0 = 0;
-      if (row_ok) {
-        n_img = (int)(m / OHW);
-        const int rem = (int)(m % OHW);
-        ih0 = (rem / g.OW) * g.sh - g.ph;
-        iw0 = (rem % g.OW) * g.sw - g.pw;
-      }
-      const int64_t img_off = (int64_t)n_img * g.H * g.W * g.C4;
-      for (int kb = 0; kb < g.kblocks; ++kb) {
-        if (!tc::mbar_wait(&empty[stage], phase ^ 1, g.err)) {
-          ok = false;
-          break;
-        }
-        uint8_t* s = smem + stage * Cfg::STAGE_BYTES;
-        if (threadIdx.x == 0) {
-          tc::mbar_arrive_expect_tx(&full[stage], SPLIT * Cfg::B_BYTES);
-          uint8_t* sb = s + SPLIT * Cfg::A_BYTES;
-          tc::tma_load_2d(sb, &tmW0, &full[stage], kb * BK, nt * BN);
-          if (SPLIT == 2) tc::tma_load_2d(sb + Cfg::B_BYTES, &tmW1, &full[stage], kb * BK, nt * BN);
-        }
-        const uint32_t dst_row = tc::smem_u32(s) + row * 128;
-        const int k0 = kb * BK;
-        if (chan32) {
-          const int tap = k0 / g.C4, c0 = k0 - tap * g.C4;
-          const int ih = ih0 + tap / g.KW, iw = iw0 + tap % g.KW;
-          const bool v = row_ok && tap < taps && ih >= 0 && ih < g.H && iw >= 0 && iw < g.W;
-          const int64_t off = v ? img_off + ((int64_t)ih * g.W + iw) * g.C4 + c0 : 0;
+    for (int64_t tile = blockIdx.x; tile < g.tiles && ok; tile += gridDim.x) {
+      const int mt = (int)(tile / g.n_tiles), nt = (int)(tile % g.n_tiles);
+      if (g.mode == kChunk) {
+        // Thread t loads chunk j = t & 7 of rows r = (t >> 3) + 16 * i.
+        const int j = t & 7;
+        int ih0[8], iw0[8];
+        int64_t img[8];
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const uint32_t d = dst_row + ((j ^ (row & 7)) << 4);
-            cp_async16(d, g.x_hi + off + 4 * j, v ? 16u : 0u);
-            if (SPLIT == 2) cp_async16(d + Cfg::A_BYTES, g.x_lo + off + 4 * j, v ? 16u : 0u);
+        for (int i = 0; i < 8; ++i) {
+          const int64_t m = (int64_t)mt * BM + (t >> 3) + 16 * i;
+          if (m < g.M) {
+            const int64_t n_img = m / OHW;
+            const int rem = (int)(m - n_img * OHW);
+            ih0[i] = (rem / g.OW) * g.sh - g.ph;
+            iw0[i] = (rem % g.OW) * g.sw - g.pw;
+            img[i] = n_img * g.H * g.W * g.C4;
+          } else {
+            ih0[i] = -(1 << 28);  // never in range
+            iw0[i] = 0;
+            img[i] = 0;
           }
-        } else {
+        }
+        for (int kb = 0; kb < g.kblocks; ++kb) {
+          if (!tc::mbar_wait(&empty[stage], phase ^ 1, g.err)) {
+            ok = false;
+            break;
+          }
+          uint8_t* s = smem + stage * Cfg::STAGE_BYTES;
+          if (t == 0) {
+            tc::mbar_arrive_expect_tx(&full[stage], SPLIT * Cfg::B_BYTES);
+            uint8_t* sb = s + SPLIT * Cfg::A_BYTES;
+            tc::tma_load_2d(sb, &tmW0, &full[stage], kb * BK, nt * BN);
+            if (SPLIT == 2) tc::tma_load_2d(sb + Cfg::B_BYTES, &tmW1, &full[stage], kb * BK, nt * BN);
+          }
+          // This thread's 16-byte chunk covers k = kb*32 + 4j .. +3: one tap,
+          // four consecutive channels (C4 is a multiple of 4), the same for
+          // all eight of its rows.
+          const int k = kb * BK + 4 * j;
+          const int tap = k / g.C4, c0 = k - tap * g.C4;
+          const int kh = tap / g.KW, kw = tap - kh * g.KW;
+          const bool tap_ok = tap < taps;
+          const uint32_t sbase = tc::smem_u32(s);
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const int k = k0 + 4 * j;
-            const int tap = k / g.C4, c = k - tap * g.C4;
-            const int ih = ih0 + tap / g.KW, iw = iw0 + tap % g.KW;
-            const bool v = row_ok && tap < taps && ih >= 0 && ih < g.H && iw >= 0 && iw < g.W;
-            const int64_t off = v ? img_off + ((int64_t)ih * g.W + iw) * g.C4 + c : 0;
-            const uint32_t d = dst_row + ((j ^ (row & 7)) << 4);
+          for (int i = 0; i < 8; ++i) {
+            const int r = (t >> 3) + 16 * i;
+            const int ih = ih0[i] + kh, iw = iw0[i] + kw;
+            const bool v = tap_ok && (unsigned)ih < (unsigned)g.H && (unsigned)iw < (unsigned)g.W;
+            const int64_t off = v ? img[i] + ((int64_t)ih * g.W + iw) * g.C4 + c0 : 0;
+            const uint32_t d = sbase + r * 128 + ((j ^ (r & 7)) << 4);
             cp_async16(d, g.x_hi + off, v ? 16u : 0u);
             if (SPLIT == 2) cp_async16(d + Cfg::A_BYTES, g.x_lo + off, v ? 16u : 0u);
           }
+          cp_async_arrive_noinc(&full[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
         }
-        cp_async_arrive_noinc(&full[stage]);
-        if (++stage == STAGES) {
-          stage = 0;
-          phase ^= 1;
+      } else {
+        // Element mode: thread t owns row r = t and copies its 32 k values.
+        const int64_t m = (int64_t)mt * BM + t;
+        const bool row_ok = m < g.M;
+        int ih0 = -(1 << 28), iw0 = 0;
+        int64_t base = 0;
+        if (row_ok) {
+          const int64_t n_img = m / OHW;
+          const int rem = (int)(m - n_img * OHW);
+          ih0 = (rem / g.OW) * g.sh - g.ph;
+          iw0 = (rem % g.OW) * g.sw - g.pw;
+          base = n_img * g.xs_n + (int64_t)ih0 * g.xs_h + (int64_t)iw0 * g.xs_w;
+        }
+        for (int kb = 0; kb < g.kblocks; ++kb) {
+          if (!tc::mbar_wait(&empty[stage], phase ^ 1, g.err)) {
+            ok = false;
+            break;
+          }
+          uint8_t* s = smem + stage * Cfg::STAGE_BYTES;
+          if (t == 0) {
+            tc::mbar_arrive_expect_tx(&full[stage], SPLIT * Cfg::B_BYTES);
+            uint8_t* sb = s + SPLIT * Cfg::A_BYTES;
+            tc::tma_load_2d(sb, &tmW0, &full[stage], kb * BK, nt * BN);
+            if (SPLIT == 2) tc::tma_load_2d(sb + Cfg::B_BYTES, &tmW1, &full[stage], kb * BK, nt * BN);
+          }
+          const uint32_t drow = tc::smem_u32(s) + t * 128;
+#pragma unroll 8
+          for (int kk = 0; kk < BK; ++kk) {
+            const int k = kb * BK + kk;
+            const int hw = ktab_hw[k];
+            const int ih = ih0 + (hw >> 16), iw = iw0 + (hw & 0xffff);
+            const bool v = hw >= 0 && (unsigned)ih < (unsigned)g.H && (unsigned)iw < (unsigned)g.W;
+            const int64_t off = v ? base + ktab_off[k] : 0;
+            const uint32_t d = drow + (((kk >> 2) ^ (t & 7)) << 4) + ((kk & 3) << 2);
+            cp_async4(d, g.x_hi + off, v ? 4u : 0u);
+            if (SPLIT == 2) cp_async4(d + Cfg::A_BYTES, g.x_lo + off, v ? 4u : 0u);
+          }
+          cp_async_arrive_noinc(&full[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
         }
       }
     }
@@ -212,9 +311,11 @@ __global__ void __launch_bounds__(kConvThreads, 1)
             ok = false;
             break;
           }
-          // The A tile was written through the generic proxy (cp.async);
-          // make it visible to the tensor core's async-proxy reads.
-          fence_proxy_async_smem();
+          // The A tile's cp.async writes are complete once the stage barrier
+          // phase completes (cp.async.mbarrier.arrive tracks them); the
+          // tcgen05 fence orders the MMAs after that wait, as in CUTLASS's
+          // SM100 cp.async mainloop. A per-stage fence.proxy.async here would
+          // drain the producers' in-flight copies and serialise the ring.
           tc::tc_fence_after();
           const uint32_t sa = tc::smem_u32(smem + stage * Cfg::STAGE_BYTES);
           const uint32_t sb = sa + SPLIT * Cfg::A_BYTES;
@@ -247,9 +348,11 @@ __global__ void __launch_bounds__(kConvThreads, 1)
   } else {
     // ---------------- epilogue (warps 5..8) ----------------
     const int quad = warp & 3;
+    float* stage_tile = epi + quad * 32 * (kStageCols + 1);  // this warp's 32 x 33 tile
+    const bool vec_ok = (g.Cout % 4 == 0) && ((((uintptr_t)g.out) & 15) == 0) &&
+                        (!g.residual || ((((uintptr_t)g.residual) & 15) == 0));
+    const bool bias_vec = g.bias && ((((uintptr_t)g.bias) & 15) == 0);
     const int64_t OHW = (int64_t)g.OH * g.OW;
-    const bool vec = g.out_nhwc && (g.Cout % 4 == 0) && ((((uintptr_t)g.out) & 15) == 0) &&
-                     (!g.residual || ((((uintptr_t)g.residual) & 15) == 0));
     int local = 0;
     for (int64_t t = blockIdx.x; t < g.tiles; t += gridDim.x, ++local) {
       const int mt = (int)(t / g.n_tiles), nt = (int)(t % g.n_tiles);
@@ -257,80 +360,87 @@ __global__ void __launch_bounds__(kConvThreads, 1)
       const uint32_t aphase = (local >> 1) & 1;
       if (!tc::mbar_wait(&tfull[acc], aphase, g.err)) break;
       tc::tc_fence_after();
-      const int64_t m = (int64_t)mt * BM + quad * 32 + lane;
-      const bool row_ok = m < g.M;
-      int64_t n_img = 0, p = 0;
-      if (row_ok) {
-        n_img = m / OHW;
-        p = m % OHW;
-      }
+      const int64_t m_base = (int64_t)mt * BM + quad * 32;  // this warp's first row
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 16) {
-        uint32_t r[16];
+      for (int c0 = 0; c0 < BN; c0 += kStageCols) {
+        uint32_t r[2][16];
         __syncwarp();  // tcgen05.ld is .sync.aligned: the warp must be converged
-        tc::tmem_ld16(tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN + c0, r);
+        const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN + c0;
+        tc::tmem_ld16(taddr, r[0]);
+        tc::tmem_ld16(taddr + 16, r[1]);
         tc::tmem_ld_wait();
         const int co0 = nt * BN + c0;
-        if (!row_ok || co0 >= g.Cout) continue;
-        float v[16];
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int co = co0 + j;
-          float x = __uint_as_float(r[j]);
-          if (g.bias && co < g.Cout) x = __fadd_rn(x, g.bias[co]);
-          v[j] = x;
-        }
+        if (co0 >= g.Cout) continue;
         if (g.out_nhwc) {
-          float* dst = g.out + m * g.Cout + co0;
-          const float* res = g.residual ? g.residual + m * g.Cout + co0 : nullptr;
-          if (vec && co0 + 16 <= g.Cout) {
+          // Stage the 32 x 32 block, then write it row-contiguously: eight
+          // lanes cover one 128-byte row segment, a warp four rows.
 #pragma unroll
-            for (int j = 0; j < 16; j += 4) {
-              float4 o = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-              if (g.act == kActAddRelu) {
-                const float4 rr = *reinterpret_cast<const float4*>(res + j);
-                o.x = __fadd_rn(o.x, rr.x);
-                o.y = __fadd_rn(o.y, rr.y);
-                o.z = __fadd_rn(o.z, rr.z);
-                o.w = __fadd_rn(o.w, rr.w);
-              }
-              if (g.act == kActRelu || g.act == kActAddRelu) {
-                o.x = o.x > 0.0f ? o.x : 0.0f;
-                o.y = o.y > 0.0f ? o.y : 0.0f;
-                o.z = o.z > 0.0f ? o.z : 0.0f;
-                o.w = o.w > 0.0f ? o.w : 0.0f;
-              } else if (g.act == kActSigmoid) {
-                o.x = 1.0f / (1.0f + expf(-o.x));
-                o.y = 1.0f / (1.0f + expf(-o.y));
-                o.z = 1.0f / (1.0f + expf(-o.z));
-                o.w = 1.0f / (1.0f + expf(-o.w));
-              }
-              *reinterpret_cast<float4*>(dst + j) = o;
-            }
-          } else {
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              if (co0 + j >= g.Cout) break;
-              float o = v[j];
-              if (g.act == kActAddRelu) o = __fadd_rn(o, res[j]);
-              if (g.act == kActRelu || g.act == kActAddRelu) o = o > 0.0f ? o : 0.0f;
-              else if (g.act == kActSigmoid) o = 1.0f / (1.0f + expf(-o));
-              dst[j] = o;
+          for (int j = 0; j < 32; ++j) stage_tile[lane * (kStageCols + 1) + j] = __uint_as_float(r[j >> 4][j & 15]);
+          __syncwarp();
+          const int cl = (lane & 7) * 4;  // column within the block
+          const int co = co0 + cl;
+          float4 bv = make_float4(0.f, 0.f, 0.f, 0.f);
+          // 16-byte row accesses need C_out % 4 == 0 and aligned bases
+          // (vec_ok); otherwise the per-element path below is taken.
+          const bool col_ok = vec_ok && co + 3 < g.Cout;
+          if (g.bias) {
+            if (col_ok && bias_vec) {
+              bv = *reinterpret_cast<const float4*>(g.bias + co);
+            } else {
+              bv.x = co < g.Cout ? g.bias[co] : 0.f;
+              bv.y = co + 1 < g.Cout ? g.bias[co + 1] : 0.f;
+              bv.z = co + 2 < g.Cout ? g.bias[co + 2] : 0.f;
+              bv.w = co + 3 < g.Cout ? g.bias[co + 3] : 0.f;
             }
           }
+#pragma unroll 2
+          for (int it = 0; it < 8; ++it) {
+            const int rr = (lane >> 3) + 4 * it;
+            const int64_t m = m_base + rr;
+            if (m >= g.M) continue;
+            const float* srow = stage_tile + rr * (kStageCols + 1) + cl;
+            float4 o = make_float4(__fadd_rn(srow[0], bv.x), __fadd_rn(srow[1], bv.y),
+                                   __fadd_rn(srow[2], bv.z), __fadd_rn(srow[3], bv.w));
+            float* dst = g.out + m * g.Cout + co;
+            if (col_ok) {
+              if (g.act == kActAddRelu) {
+                const float4 rv = *reinterpret_cast<const float4*>(g.residual + m * g.Cout + co);
+                o.x = __fadd_rn(o.x, rv.x);
+                o.y = __fadd_rn(o.y, rv.y);
+                o.z = __fadd_rn(o.z, rv.z);
+                o.w = __fadd_rn(o.w, rv.w);
+              }
+              o.x = activate(o.x, g.act);
+              o.y = activate(o.y, g.act);
+              o.z = activate(o.z, g.act);
+              o.w = activate(o.w, g.act);
+              *reinterpret_cast<float4*>(dst) = o;
+            } else {
+              const float ov[4] = {o.x, o.y, o.z, o.w};
+              for (int q = 0; q < 4 && co + q < g.Cout; ++q) {
+                float v = ov[q];
+                if (g.act == kActAddRelu) v = __fadd_rn(v, g.residual[m * g.Cout + co + q]);
+                dst[q] = activate(v, g.act);
+              }
+            }
+          }
+          __syncwarp();
         } else {
           // NCHW: channel co of image n at plane offset p; lanes hold
           // consecutive pixels, so each store instruction is coalesced.
-          float* dst = g.out + (n_img * g.Cout + co0) * OHW + p;
-          const float* res = g.residual ? g.residual + (n_img * g.Cout + co0) * OHW + p : nullptr;
+          const int64_t m = m_base + lane;
+          if (m < g.M) {
+            const int64_t n_img = m / OHW, p = m - n_img * OHW;
+            float* dst = g.out + (n_img * g.Cout + co0) * OHW + p;
+            const float* res = g.residual ? g.residual + (n_img * g.Cout + co0) * OHW + p : nullptr;
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            if (co0 + j >= g.Cout) break;
-            float o = v[j];
-            if (g.act == kActAddRelu) o = __fadd_rn(o, res[(int64_t)j * OHW]);
-            if (g.act == kActRelu || g.act == kActAddRelu) o = o > 0.0f ? o : 0.0f;
-            else if (g.act == kActSigmoid) o = 1.0f / (1.0f + expf(-o));
-            dst[(int64_t)j * OHW] = o;
+            for (int j = 0; j < 32; ++j) {
+              if (co0 + j >= g.Cout) break;
+              float o = __uint_as_float(r[j >> 4][j & 15]);
+              if (g.bias) o = __fadd_rn(o, g.bias[co0 + j]);
+              if (g.act == kActAddRelu) o = __fadd_rn(o, res[(int64_t)j * OHW]);
+              dst[(int64_t)j * OHW] = activate(o, g.act);
+            }
           }
         }
       }
@@ -350,19 +460,26 @@ __global__ void __launch_bounds__(kConvThreads, 1)
 
 // ------------------------------------------------------ layout kernels ----
 
-// OIHW -> [plane][Cout][K_pad], k = (kh*KW + kw)*C4 + ci, zero padded.
-// split: plane 0 = tf32(w), plane 1 = w - tf32(w); else plane 0 = w.
+// OIHW -> [plane][Cout][K_pad], zero padded. Chunk mode: k = (kh*KW + kw)*C4
+// + ci (C4 = channels padded to 32); element mode: k = (ci*KH + kh)*KW + kw,
+// the OIHW order itself. split: plane 0 = tf32(w), plane 1 = w - tf32(w);
+// else plane 0 = w.
 __global__ void __launch_bounds__(256) pack_weight_kernel(const float* __restrict__ w,
                                                           float* __restrict__ out, int Cout,
                                                           int Cin, int KH, int KW, int C4,
-                                                          int Kpad, int split) {
+                                                          int Kpad, int split, int element) {
   const int64_t total = (int64_t)Cout * Kpad;
+  const int Kw = Cin * KH * KW;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
     const int co = (int)(i / Kpad), k = (int)(i % Kpad);
-    const int tap = k / C4, ci = k % C4;
     float v = 0.0f;
-    if (tap < KH * KW && ci < Cin) v = w[(((int64_t)co * Cin + ci) * KH + tap / KW) * KW + tap % KW];
+    if (element) {
+      if (k < Kw) v = w[(int64_t)co * Kw + k];
+    } else {
+      const int tap = k / C4, ci = k % C4;
+      if (tap < KH * KW && ci < Cin) v = w[(((int64_t)co * Cin + ci) * KH + tap / KW) * KW + tap % KW];
+    }
     if (split) {
       const float h = tc::to_tf32(v);
       out[i] = h;
@@ -408,6 +525,37 @@ __global__ void __launch_bounds__(256) nchw_to_nhwc_pad_kernel(const float* __re
   }
 }
 
+// NCHW [N][C][HW] -> NHWC [N][HW][C4] for C4 <= 16 (model inputs such as
+// RGB): one thread per pixel, reads coalesced along each channel plane,
+// writes C4 / 4 consecutive 16-byte vectors; optional hi/lo.
+__global__ void __launch_bounds__(256) nchw_to_nhwc_small_kernel(const float* __restrict__ x,
+                                                                 float* __restrict__ hi,
+                                                                 float* __restrict__ lo, int N,
+                                                                 int C, int64_t HW, int C4) {
+  const int64_t total = (int64_t)N * HW;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t n = i / HW, p = i - n * HW;
+    const float* src = x + n * C * HW + p;
+    for (int c0 = 0; c0 < C4; c0 += 4) {
+      float v[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) v[q] = (c0 + q < C) ? src[(int64_t)(c0 + q) * HW] : 0.0f;
+      float4* dh = reinterpret_cast<float4*>(hi + i * C4 + c0);
+      if (lo) {
+        float h[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) h[q] = tc::to_tf32(v[q]);
+        *dh = make_float4(h[0], h[1], h[2], h[3]);
+        *reinterpret_cast<float4*>(lo + i * C4 + c0) =
+            make_float4(v[0] - h[0], v[1] - h[1], v[2] - h[2], v[3] - h[3]);
+      } else {
+        *dh = make_float4(v[0], v[1], v[2], v[3]);
+      }
+    }
+  }
+}
+
 // NHWC (C channels) -> NHWC with C4 channels, optional hi/lo split.
 __global__ void __launch_bounds__(256) nhwc_repack_kernel(const float* __restrict__ x,
                                                           float* __restrict__ hi,
@@ -431,7 +579,33 @@ __global__ void __launch_bounds__(256) nhwc_repack_kernel(const float* __restric
 
 // ------------------------------------------------------------------ host --
 
-int kpad_of(int KH, int KW, int C4) { return (int)cdiv((int64_t)KH * KW * C4, BK) * BK; }
+// How a weight of shape [Cout, Cin, KH, KW] is packed, decided by the shape
+// alone (so a weight prepacked once matches every later call): chunk mode
+// with channels padded to a multiple of 4, or element mode for tiny K.
+struct WeightLayout {
+  int element;
+  int C4;    // chunk mode: channels per tap as stored (multiple of 4)
+  int K;     // valid k extent
+  int Kpad;  // multiple of 32
+};
+
+WeightLayout weight_layout(int Cin, int KH, int KW) {
+  WeightLayout L;
+  const int ke = (int)cdiv((int64_t)Cin * KH * KW, BK) * BK;
+  // Element order only for a single-k-block-or-two reduction (e.g. LeNet's
+  // 1x5x5 conv), where padding channels to 4 would multiply the K work.
+  L.element = ke <= 64;
+  if (L.element) {
+    L.C4 = Cin;
+    L.K = Cin * KH * KW;
+    L.Kpad = ke;
+  } else {
+    L.C4 = (Cin + 3) / 4 * 4;
+    L.K = KH * KW * L.C4;
+    L.Kpad = (int)cdiv(L.K, BK) * BK;
+  }
+  return L;
+}
 
 template <int BN, int SPLIT, int STAGES>
 bool launch_conv(ConvArgs g, const float* w0, const float* w1, const char* op) {
@@ -510,16 +684,21 @@ void conv_impl(Tensor* input, Tensor* weight, Tensor* bias, Tensor* residual, Te
   const int64_t M = (int64_t)N * OH * OW;
   if (M == 0 || Cout == 0) return;
   const bool split = ctx().precision == NNC_CUDA_PRECISION_3XTF32;
-  const int C4 = (C + 3) & ~3;
-  const int Kpad = kpad_of(KH, KW, C4);
+  const WeightLayout wl = weight_layout(C, KH, KW);
+  const int C4 = wl.C4;
+  const int Kpad = wl.Kpad;
   const bool packed = (tag_of(weight) & NNC_CUDA_TAG_PACKED_CONV) != 0;
 
-  // Scratch: NHWC input planes (unless usable in place) + packed weights.
-  const bool in_place = is_nhwc(input) && C4 == C && !split;
-  const int64_t x_elems = (int64_t)N * H * W * C4;
+  // Scratch: input planes when the input cannot be read in place (chunk
+  // mode needs NHWC with C a multiple of 32; 3xTF32 needs hi/lo planes), and
+  // packed weights unless prepacked.
+  // (Chunk mode issues 16-byte copies: the base must be 16-byte aligned.)
+  const bool in_place =
+      wl.element ? !split : (is_nhwc(input) && C4 == C && !split && aligned16(input->data));
+  const int64_t x_elems = wl.element ? numel(input) : (int64_t)N * H * W * C4;
   const int64_t w_elems = (int64_t)Cout * Kpad;
   size_t need = 0;
-  if (!in_place) need += (size_t)(split ? 2 : 1) * x_elems * 4;
+  if (!in_place) need += (size_t)(split ? 2 : 1) * ((x_elems + 63) / 64 * 64) * 4;
   if (!packed) need += (size_t)(split ? 2 : 1) * w_elems * 4;
   float* ws = need ? (float*)workspace(need + 256, op) : nullptr;
   if (need && !ws) return;
@@ -529,16 +708,25 @@ void conv_impl(Tensor* input, Tensor* weight, Tensor* bias, Tensor* residual, Te
   const float* x_lo = nullptr;
   if (!in_place) {
     float* hi = cur;
-    float* lo = split ? cur + x_elems : nullptr;
-    cur += (split ? 2 : 1) * x_elems;
-    if (is_nhwc(input)) {
+    const int64_t x_span = (x_elems + 63) / 64 * 64;  // keep every plane 256-byte aligned
+    float* lo = split ? cur + x_span : nullptr;
+    cur += (split ? 2 : 1) * x_span;
+    if (wl.element) {  // same layout, element-wise hi/lo split
+      nhwc_repack_kernel<<<grid_for(x_elems, 256, 8), 256, 0, ctx().stream>>>(
+          (const float*)input->data, hi, lo, x_elems, 1, 1);
+    } else if (is_nhwc(input)) {
       nhwc_repack_kernel<<<grid_for(x_elems, 256, 8), 256, 0, ctx().stream>>>(
           (const float*)input->data, hi, lo, (int64_t)N * H * W, C, C4);
     } else {
-      const int64_t tiles = (int64_t)N * cdiv((int64_t)H * W, 32) * cdiv(C4, 32);
-      const int grid = (int)(tiles < (int64_t)sm_count() * 16 ? tiles : (int64_t)sm_count() * 16);
-      nchw_to_nhwc_pad_kernel<<<grid, 256, 0, ctx().stream>>>((const float*)input->data, hi, lo, N,
-                                                              C, (int64_t)H * W, C4);
+      if (C4 <= 16) {
+        nchw_to_nhwc_small_kernel<<<grid_for((int64_t)N * H * W, 256, 8), 256, 0, ctx().stream>>>(
+            (const float*)input->data, hi, lo, N, C, (int64_t)H * W, C4);
+      } else {
+        const int64_t tiles = (int64_t)N * cdiv((int64_t)H * W, 32) * cdiv(C4, 32);
+        const int grid = (int)(tiles < (int64_t)sm_count() * 16 ? tiles : (int64_t)sm_count() * 16);
+        nchw_to_nhwc_pad_kernel<<<grid, 256, 0, ctx().stream>>>((const float*)input->data, hi, lo,
+                                                                N, C, (int64_t)H * W, C4);
+      }
     }
     if (!check_launch(op)) return;
     x_hi = hi;
@@ -549,13 +737,25 @@ void conv_impl(Tensor* input, Tensor* weight, Tensor* bias, Tensor* residual, Te
   if (!packed) {
     float* wp = cur;
     pack_weight_kernel<<<grid_for(w_elems, 256, 8), 256, 0, ctx().stream>>>(
-        (const float*)weight->data, wp, Cout, C, KH, KW, C4, Kpad, split ? 1 : 0);
+        (const float*)weight->data, wp, Cout, C, KH, KW, C4, Kpad, split ? 1 : 0, wl.element);
     if (!check_launch(op)) return;
     w0 = wp;
     w1 = wp + w_elems;
   }
 
   ConvArgs g{};
+  g.mode = wl.element ? kElement : kChunk;
+  if (is_nhwc(input)) {
+    g.xs_n = (int64_t)H * W * C;
+    g.xs_c = 1;
+    g.xs_h = (int64_t)W * C;
+    g.xs_w = C;
+  } else {
+    g.xs_n = (int64_t)C * H * W;
+    g.xs_c = (int64_t)H * W;
+    g.xs_h = W;
+    g.xs_w = 1;
+  }
   g.N = N;
   g.H = H;
   g.W = W;
@@ -569,7 +769,7 @@ void conv_impl(Tensor* input, Tensor* weight, Tensor* bias, Tensor* residual, Te
   g.sw = sw;
   g.ph = ph;
   g.pw = pw;
-  g.K = KH * KW * C4;
+  g.K = wl.K;
   g.kblocks = Kpad / BK;
   g.M = M;
   g.x_hi = x_hi;
@@ -710,8 +910,8 @@ void nnc_conv_add_relu3x3_s1(Tensor* input, Tensor* weight, Tensor* bias, Tensor
 
 size_t nnc_cuda_prepacked_conv_weight_bytes(const Tensor* w) {
   if (!w || !w->shape || w->ndim != 4) return 0;
-  const int C4 = ((int)w->shape[1] + 3) & ~3;
-  return (size_t)2 * w->shape[0] * kpad_of((int)w->shape[2], (int)w->shape[3], C4) * 4;
+  const WeightLayout wl = weight_layout((int)w->shape[1], (int)w->shape[2], (int)w->shape[3]);
+  return (size_t)2 * w->shape[0] * wl.Kpad * 4;
 }
 
 int nnc_cuda_prepack_conv_weight(Tensor* w, void* dst, size_t dst_bytes) {
@@ -729,11 +929,10 @@ int nnc_cuda_prepack_conv_weight(Tensor* w, void* dst, size_t dst_bytes) {
   }
   const int Cout = (int)w->shape[0], Cin = (int)w->shape[1], KH = (int)w->shape[2],
             KW = (int)w->shape[3];
-  const int C4 = (Cin + 3) & ~3;
-  const int Kpad = kpad_of(KH, KW, C4);
-  const int64_t total = (int64_t)Cout * Kpad;
+  const WeightLayout wl = weight_layout(Cin, KH, KW);
+  const int64_t total = (int64_t)Cout * wl.Kpad;
   pack_weight_kernel<<<grid_for(total, 256, 8), 256, 0, ctx().stream>>>(
-      (const float*)w->data, (float*)dst, Cout, Cin, KH, KW, C4, Kpad, 1);
+      (const float*)w->data, (float*)dst, Cout, Cin, KH, KW, wl.C4, wl.Kpad, 1, wl.element);
   if (!check_launch(op)) return ctx().status;
   w->data = dst;
   w->dtype = (nnc_dtype_t)((int)w->dtype | NNC_CUDA_TAG_PACKED_CONV);

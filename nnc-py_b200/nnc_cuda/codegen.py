@@ -244,9 +244,13 @@ def _align(x: int, a: int = ARENA_ALIGN) -> int:
 
 
 def _packed_conv_bytes(shape) -> int:
+    """Size of nnc_cuda_prepack_conv_weight's output (conv.cu weight_layout):
+    hi + lo planes of [C_out][K_pad]; K_pad = C_in*KH*KW rounded up to 32 when
+    that is <= 64 (element order), else KH*KW*C4 rounded up to 32 with C4 =
+    C_in rounded up to 4 (chunk order)."""
     cout, cin, kh, kw = (int(s) for s in shape)
-    c4 = (cin + 3) // 4 * 4
-    kpad = (kh * kw * c4 + 31) // 32 * 32
+    ke = (cin * kh * kw + 31) // 32 * 32
+    kpad = ke if ke <= 64 else (kh * kw * ((cin + 3) // 4 * 4) + 31) // 32 * 32
     return 2 * cout * kpad * 4
 
 

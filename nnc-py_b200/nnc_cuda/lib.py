@@ -69,7 +69,7 @@ _CTYPE_OF = {
 }
 
 _PROTO_RE = re.compile(
-    r"^\s*(void\*|void|int|size_t|const char\*|long long)\s+(nnc_\w+)\s*\(([^)]*)\)\s*;", re.M | re.S
+    r"^\s*((?:const\s+)?(?:long\s+long|\w+)\s*\**)\s*(nnc_\w+)\s*\(([^)]*)\)\s*;", re.M | re.S
 )
 
 
@@ -79,6 +79,9 @@ def header_prototypes(header: str) -> dict[str, tuple[str, list[str]]]:
     text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
     protos: dict[str, tuple[str, list[str]]] = {}
     for ret, name, args in _PROTO_RE.findall(text):
+        ret = " ".join(ret.replace("*", " *").split()).replace(" *", "*")
+        if ret not in _CTYPE_OF:
+            raise ValueError(f"unsupported return type {ret!r} of {name}")
         args = " ".join(args.split())
         types: list[str] = []
         if args and args != "void":

@@ -70,5 +70,16 @@ def test_prepacked_weight_size():
     so = L.load()
     shape = (ctypes.c_int64 * 4)(64, 3, 7, 7)
     t = L.Tensor(None, 0, ctypes.cast(shape, ctypes.POINTER(ctypes.c_int64)), 4, 0)
-    # C padded to 4, K = 7*7*4 = 196 -> 224; two planes of 64 x 224 fp32.
+    # C_in = 3 padded to 4 (chunk order): K = 7*7*4 = 196 -> 224; two planes of 64 x 224.
     assert so.nnc_cuda_prepacked_conv_weight_bytes(ctypes.byref(t)) == 2 * 64 * 224 * 4
+
+
+def test_parser_sees_every_declaration():
+    """Every nnc_* prototype in the headers is typed (a missed declaration
+    would leave ctypes guessing its return type)."""
+    import re
+
+    for h in ("nnc_ops.h", "nnc_cuda.h"):
+        text = re.sub(r"/\*.*?\*/", "", (L.INCLUDE_DIR / h).read_text(), flags=re.S)
+        decls = set(re.findall(r"\b(nnc_\w+)\s*\(", text))
+        assert decls == set(L.header_prototypes(h)), decls ^ set(L.header_prototypes(h))
