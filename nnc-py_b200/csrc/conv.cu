@@ -12,19 +12,22 @@
 //                k = (c, kh, kw), the OIHW order, read in place in either
 //                layout.
 //
-// Kernel (persistent, one CTA per SM, 288 threads):
-//   warps 0..3  producers: gather the 128 x 32 A tile with cp.async (zero
+// Kernel (persistent, one CTA per SM, 416 threads = 13 warps):
+//   warps 0..7  producers: gather the 128 x 32 A tile with cp.async (zero
 //               fill for taps in the padding) into the 128-byte swizzle
-//               layout — chunk mode: 16-byte copies, eight neighbouring
-//               threads per 128-byte row so each warp instruction reads four
-//               whole rows; element mode: 4-byte copies with per-k offsets
-//               from a shared-memory table. Thread 0 also TMA-loads the
-//               BN x 32 weight tile. Arrival is asynchronous
+//               layout. Chunk mode: 16-byte copies, eight neighbouring
+//               threads per 128-byte row (a warp instruction covers four
+//               rows); each thread owns four rows whose base offsets and
+//               tap-validity masks are computed once per tile, and advances
+//               its (tap, channel) position incrementally, so a copy costs a
+//               handful of instructions. Element mode: 4-byte copies with
+//               per-k offsets from a shared-memory table. Thread 0 also
+//               TMA-loads the BN x 32 weight tile. Arrival is asynchronous
 //               (cp.async.mbarrier.arrive.noinc), so producers run ahead.
-//   warp 4      TMEM allocation + single-thread tcgen05.mma issue (kind::tf32,
+//   warp 8      TMEM allocation + single-thread tcgen05.mma issue (kind::tf32,
 //               M = 128, N = BN, 4 k-steps per stage; 3 MMAs per k-step in
 //               3xTF32 mode), commits release ring slots and accumulators.
-//   warps 5..8  epilogue: tcgen05.ld of 32 columns at a time; NHWC outputs
+//   warps 9..12 epilogue: tcgen05.ld of 32 columns at a time; NHWC outputs
 //               are staged through a 32 x 33 shared tile so bias, residual
 //               and stores run row-contiguously (eight lanes per 128-byte
 //               row); NCHW outputs store per channel plane, coalesced across
@@ -44,20 +47,26 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BK = 32;
-constexpr int kProducerThreads = 128;
-constexpr int kConvThreads = 288;
+constexpr int kProducerWarps = 4;
+constexpr int kProducerThreads = 32 * kProducerWarps;
+constexpr int kMmaWarp = kProducerWarps;
+constexpr int kEpilogueWarps = 8;  // two per TMEM lane quadrant, splitting the columns
+constexpr int kConvThreads = 32 * (kProducerWarps + 1 + kEpilogueWarps);
+constexpr int kRowsPerThread = BM * 8 / kProducerThreads;  // chunk mode: 8
+constexpr int kRowStep = kProducerThreads / 8;              // chunk mode: rows per pass
+constexpr int kElemPerThread = BM * BK / kProducerThreads;  // element mode: 32
 
 enum Act : int { kActNone = 0, kActRelu = 1, kActSigmoid = 2, kActAddRelu = 3 };
 
-// Gather modes for the A (activation) operand.
-//   kChunk:   NHWC input, C4 % 4 == 0; k = (kh, kw, c); each 16-byte chunk of
-//             a 128-byte stage row is four consecutive channels of one tap,
-//             copied by one thread; eight neighbouring threads fill a row, so
-//             a warp instruction covers four rows.
-//   kElement: any input layout (strides) and any channel count; k = (c, kh,
-//             kw), i.e. the OIHW weight order; 4-byte cp.async per element,
-//             per-k offsets from a table in shared memory.
-enum Mode : int { kChunk = 0, kElement = 1 };
+// How the A (activation) operand reaches shared memory (see the file comment).
+//   kIm2col128: TMA im2col, C4 % 32 == 0: one load of 128 pixels x 32
+//               channels per stage into the 128-byte swizzle layout;
+//   kIm2col16:  TMA im2col, C4 % 4 == 0: eight loads of 128 pixels x 4
+//               channels per stage, each a 2 KB column of 8-row x 16-byte core
+//               matrices (K-major, no swizzle);
+//   kChunk / kElement: cp.async gathers by the producer warps (windows the
+//               im2col bounding box cannot describe, and tiny reductions).
+enum Mode : int { kChunk = 0, kElement = 1, kIm2col128 = 2, kIm2col16 = 3 };
 constexpr int kMaxElementK = 64;  // K_pad limit of the element mode (see weight_layout)
 
 struct ConvArgs {
@@ -103,7 +112,7 @@ __device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
 
 // Epilogue staging: one 32 x 33 fp32 tile per epilogue warp.
 constexpr int kStageCols = 32;
-constexpr uint32_t kEpiBytes = 4 * 32 * (kStageCols + 1) * 4;
+constexpr uint32_t kEpiBytes = kEpilogueWarps * 32 * (kStageCols + 1) * 4;
 
 template <int BN, int SPLIT, int STAGES>
 struct ConvCfg {
@@ -126,6 +135,7 @@ __device__ __forceinline__ float activate(float o, int act) {
 template <int BN, int SPLIT, int STAGES>
 __global__ void __launch_bounds__(kConvThreads, 1)
     conv_tc_kernel(const __grid_constant__ CUtensorMap tmW0, const __grid_constant__ CUtensorMap tmW1,
+                   const __grid_constant__ CUtensorMap tmX0, const __grid_constant__ CUtensorMap tmX1,
                    const ConvArgs g) {
   using Cfg = ConvCfg<BN, SPLIT, STAGES>;
   extern __shared__ uint8_t smem_raw[];
@@ -141,20 +151,27 @@ __global__ void __launch_bounds__(kConvThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const bool tma_a = g.mode == kIm2col128 || g.mode == kIm2col16;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      tc::mbar_init(&full[s], kProducerThreads + 1);
+      // TMA feeding: one expect_tx arrival; gathers: every producer thread
+      // arrives (cp.async.mbarrier.arrive.noinc) plus the weight TMA.
+      tc::mbar_init(&full[s], tma_a ? 1 : kProducerThreads + 1);
       tc::mbar_init(&empty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
       tc::mbar_init(&tfull[a], 1);
-      tc::mbar_init(&tempty[a], 4);
+      tc::mbar_init(&tempty[a], kEpilogueWarps);
     }
     tc::mbar_init(done, 1);
     tc::fence_barrier_init();
     tc::prefetch_tmap(&tmW0);
     if (SPLIT == 2) tc::prefetch_tmap(&tmW1);
+    if (tma_a) {
+      tc::prefetch_tmap(&tmX0);
+      if (SPLIT == 2) tc::prefetch_tmap(&tmX1);
+    }
   }
   if (g.mode == kElement) {
     // k -> (element offset from the window origin, kh << 16 | kw); -1 past K.
@@ -170,7 +187,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
       }
     }
   }
-  if (warp == 4) {
+  if (warp == kMmaWarp) {
     tc::tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
     tc::tmem_relinquish();
   }
@@ -179,36 +196,118 @@ __global__ void __launch_bounds__(kConvThreads, 1)
   tc::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  if (warp < 4) {
+  if (tma_a && warp < kProducerWarps) {
+    // ---------------- producer (one thread): TMA im2col of A, TMA of W ----------------
+    if (threadIdx.x == 0) {
+      const int64_t OHW = (int64_t)g.OH * g.OW;
+      const int taps = g.KH * g.KW;
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int64_t tile = blockIdx.x; tile < g.tiles && ok; tile += gridDim.x) {
+        const int mt = (int)(tile / g.n_tiles), nt = (int)(tile % g.n_tiles);
+        // Window origin of the tile's first output pixel: the im2col
+        // traversal continues from there in (n, oh, ow) order.
+        const int64_t m0 = (int64_t)mt * BM;
+        const int n0 = (int)(m0 / OHW);
+        const int rem = (int)(m0 - (int64_t)n0 * OHW);
+        const int w0 = (rem % g.OW) * g.sw - g.pw, h0 = (rem / g.OW) * g.sh - g.ph;
+        for (int kb = 0; kb < g.kblocks; ++kb) {
+          if (!tc::mbar_wait(&empty[stage], phase ^ 1, g.err)) {
+            ok = false;
+            break;
+          }
+          uint8_t* s = smem + stage * Cfg::STAGE_BYTES;
+          tc::mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
+          uint8_t* sb = s + SPLIT * Cfg::A_BYTES;
+          tc::tma_load_2d(sb, &tmW0, &full[stage], kb * BK, nt * BN);
+          if (SPLIT == 2) tc::tma_load_2d(sb + Cfg::B_BYTES, &tmW1, &full[stage], kb * BK, nt * BN);
+          if (g.mode == kIm2col128) {
+            const int k0 = kb * BK, tap = k0 / g.C4, c0 = k0 - tap * g.C4;
+            const uint16_t kh = (uint16_t)(tap / g.KW), kw = (uint16_t)(tap % g.KW);
+            tc::tma_load_im2col_4d(s, &tmX0, &full[stage], c0, w0, h0, n0, kw, kh);
+            if (SPLIT == 2)
+              tc::tma_load_im2col_4d(s + Cfg::A_BYTES, &tmX1, &full[stage], c0, w0, h0, n0, kw, kh);
+          } else {
+#pragma unroll 1
+            for (int j = 0; j < 8; ++j) {
+              // k = kb*32 + 4j -> (tap, channel group); past the last tap the
+              // channel coordinate C4 is out of range, so the column is zeros.
+              const int k = kb * BK + 4 * j;
+              int tap = k / g.C4, c0 = k - tap * g.C4;
+              if (tap >= taps) {
+                tap = 0;
+                c0 = g.C4;
+              }
+              const uint16_t kh = (uint16_t)(tap / g.KW), kw = (uint16_t)(tap % g.KW);
+              tc::tma_load_im2col_4d(s + j * 2048, &tmX0, &full[stage], c0, w0, h0, n0, kw, kh);
+              if (SPLIT == 2)
+                tc::tma_load_im2col_4d(s + Cfg::A_BYTES + j * 2048, &tmX1, &full[stage], c0, w0, h0,
+                                       n0, kw, kh);
+            }
+          }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      // Let the last issued loads land before the CTA can exit.
+      if (ok) {
+        for (int q = 0; q < STAGES; ++q) {
+          if (stage == 0) {
+            stage = STAGES;
+            phase ^= 1;
+          }
+          --stage;
+          tc::mbar_wait(&full[stage], phase, g.err);
+        }
+      }
+    }
+  } else if (warp < kProducerWarps) {
     // ---------------- producers: im2col gather of A, TMA of W ----------------
-    const int t = threadIdx.x;  // 0..127
+    const int t = threadIdx.x;  // 0..kProducerThreads-1
     const int64_t OHW = (int64_t)g.OH * g.OW;
     const int taps = g.KH * g.KW;
+    const bool use_mask = taps <= 64;
     int stage = 0;
     uint32_t phase = 0;
     bool ok = true;
     for (int64_t tile = blockIdx.x; tile < g.tiles && ok; tile += gridDim.x) {
       const int mt = (int)(tile / g.n_tiles), nt = (int)(tile % g.n_tiles);
       if (g.mode == kChunk) {
-        // Thread t loads chunk j = t & 7 of rows r = (t >> 3) + 16 * i.
+        // Thread t copies chunk j = t & 7 (channels 4j..4j+3 of the stage's
+        // 32) of rows r_i = (t >> 3) + kRowStep * i.
         const int j = t & 7;
-        int ih0[8], iw0[8];
-        int64_t img[8];
+        int ih0[kRowsPerThread], iw0[kRowsPerThread];
+        int64_t base[kRowsPerThread];
+        uint64_t mask[kRowsPerThread];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int64_t m = (int64_t)mt * BM + (t >> 3) + 16 * i;
+        for (int i = 0; i < kRowsPerThread; ++i) {
+          const int64_t m = (int64_t)mt * BM + (t >> 3) + kRowStep * i;
+          mask[i] = 0;
+          ih0[i] = -(1 << 28);
+          iw0[i] = 0;
+          base[i] = 0;
           if (m < g.M) {
             const int64_t n_img = m / OHW;
             const int rem = (int)(m - n_img * OHW);
             ih0[i] = (rem / g.OW) * g.sh - g.ph;
             iw0[i] = (rem % g.OW) * g.sw - g.pw;
-            img[i] = n_img * g.H * g.W * g.C4;
-          } else {
-            ih0[i] = -(1 << 28);  // never in range
-            iw0[i] = 0;
-            img[i] = 0;
+            base[i] = (n_img * g.H * g.W + (int64_t)ih0[i] * g.W + iw0[i]) * g.C4;
+            if (use_mask) {
+              for (int kh = 0; kh < g.KH; ++kh) {
+                if ((unsigned)(ih0[i] + kh) >= (unsigned)g.H) continue;
+                for (int kw = 0; kw < g.KW; ++kw)
+                  if ((unsigned)(iw0[i] + kw) < (unsigned)g.W) mask[i] |= 1ull << (kh * g.KW + kw);
+              }
+            }
           }
         }
+        // This thread's chunk position: k = kb * 32 + 4j -> (tap, channel).
+        int tap = (4 * j) / g.C4, c = 4 * j - tap * g.C4;
+        int kh = tap / g.KW, kw = tap - kh * g.KW;
+        int64_t toff = ((int64_t)kh * g.W + kw) * g.C4;
         for (int kb = 0; kb < g.kblocks; ++kb) {
           if (!tc::mbar_wait(&empty[stage], phase ^ 1, g.err)) {
             ok = false;
@@ -221,20 +320,19 @@ __global__ void __launch_bounds__(kConvThreads, 1)
             tc::tma_load_2d(sb, &tmW0, &full[stage], kb * BK, nt * BN);
             if (SPLIT == 2) tc::tma_load_2d(sb + Cfg::B_BYTES, &tmW1, &full[stage], kb * BK, nt * BN);
           }
-          // This thread's 16-byte chunk covers k = kb*32 + 4j .. +3: one tap,
-          // four consecutive channels (C4 is a multiple of 4), the same for
-          // all eight of its rows.
-          const int k = kb * BK + 4 * j;
-          const int tap = k / g.C4, c0 = k - tap * g.C4;
-          const int kh = tap / g.KW, kw = tap - kh * g.KW;
           const bool tap_ok = tap < taps;
           const uint32_t sbase = tc::smem_u32(s);
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const int r = (t >> 3) + 16 * i;
-            const int ih = ih0[i] + kh, iw = iw0[i] + kw;
-            const bool v = tap_ok && (unsigned)ih < (unsigned)g.H && (unsigned)iw < (unsigned)g.W;
-            const int64_t off = v ? img[i] + ((int64_t)ih * g.W + iw) * g.C4 + c0 : 0;
+          for (int i = 0; i < kRowsPerThread; ++i) {
+            const int r = (t >> 3) + kRowStep * i;
+            bool v;
+            if (use_mask) {
+              v = tap_ok && ((mask[i] >> tap) & 1ull);
+            } else {
+              v = tap_ok && (unsigned)(ih0[i] + kh) < (unsigned)g.H &&
+                  (unsigned)(iw0[i] + kw) < (unsigned)g.W;
+            }
+            const int64_t off = v ? base[i] + toff + c : 0;
             const uint32_t d = sbase + r * 128 + ((j ^ (r & 7)) << 4);
             cp_async16(d, g.x_hi + off, v ? 16u : 0u);
             if (SPLIT == 2) cp_async16(d + Cfg::A_BYTES, g.x_lo + off, v ? 16u : 0u);
@@ -244,19 +342,32 @@ __global__ void __launch_bounds__(kConvThreads, 1)
             stage = 0;
             phase ^= 1;
           }
+          // Advance by 32 channels (several taps when C4 < 32).
+          c += BK;
+          while (c >= g.C4 && tap < taps) {
+            c -= g.C4;
+            ++tap;
+            if (++kw == g.KW) {
+              kw = 0;
+              ++kh;
+            }
+            toff = ((int64_t)kh * g.W + kw) * g.C4;
+          }
         }
       } else {
-        // Element mode: thread t owns row r = t and copies its 32 k values.
-        const int64_t m = (int64_t)mt * BM + t;
-        const bool row_ok = m < g.M;
+        // Element mode: thread t copies k values [kElemPerThread * h,
+        // kElemPerThread * (h + 1)) of row r = t % BM of each 32-wide stage,
+        // h = t / BM.
+        const int r = t % BM, h = t / BM;
+        const int64_t m = (int64_t)mt * BM + r;
         int ih0 = -(1 << 28), iw0 = 0;
-        int64_t base = 0;
-        if (row_ok) {
+        int64_t rbase = 0;
+        if (m < g.M) {
           const int64_t n_img = m / OHW;
           const int rem = (int)(m - n_img * OHW);
           ih0 = (rem / g.OW) * g.sh - g.ph;
           iw0 = (rem % g.OW) * g.sw - g.pw;
-          base = n_img * g.xs_n + (int64_t)ih0 * g.xs_h + (int64_t)iw0 * g.xs_w;
+          rbase = n_img * g.xs_n + (int64_t)ih0 * g.xs_h + (int64_t)iw0 * g.xs_w;
         }
         for (int kb = 0; kb < g.kblocks; ++kb) {
           if (!tc::mbar_wait(&empty[stage], phase ^ 1, g.err)) {
@@ -270,15 +381,16 @@ __global__ void __launch_bounds__(kConvThreads, 1)
             tc::tma_load_2d(sb, &tmW0, &full[stage], kb * BK, nt * BN);
             if (SPLIT == 2) tc::tma_load_2d(sb + Cfg::B_BYTES, &tmW1, &full[stage], kb * BK, nt * BN);
           }
-          const uint32_t drow = tc::smem_u32(s) + t * 128;
-#pragma unroll 8
-          for (int kk = 0; kk < BK; ++kk) {
+          const uint32_t drow = tc::smem_u32(s) + r * 128;
+#pragma unroll 4
+          for (int q = 0; q < kElemPerThread; ++q) {
+            const int kk = kElemPerThread * h + q;
             const int k = kb * BK + kk;
             const int hw = ktab_hw[k];
             const int ih = ih0 + (hw >> 16), iw = iw0 + (hw & 0xffff);
             const bool v = hw >= 0 && (unsigned)ih < (unsigned)g.H && (unsigned)iw < (unsigned)g.W;
-            const int64_t off = v ? base + ktab_off[k] : 0;
-            const uint32_t d = drow + (((kk >> 2) ^ (t & 7)) << 4) + ((kk & 3) << 2);
+            const int64_t off = v ? rbase + ktab_off[k] : 0;
+            const uint32_t d = drow + (((kk >> 2) ^ (r & 7)) << 4) + ((kk & 3) << 2);
             cp_async4(d, g.x_hi + off, v ? 4u : 0u);
             if (SPLIT == 2) cp_async4(d + Cfg::A_BYTES, g.x_lo + off, v ? 4u : 0u);
           }
@@ -292,7 +404,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
     }
     // Let every cp.async of this thread land before the CTA can exit.
     asm volatile("cp.async.wait_all;" ::: "memory");
-  } else if (warp == 4) {
+  } else if (warp == kMmaWarp) {
     if (lane == 0) {
       // ---------------- MMA issuer ----------------
       constexpr uint32_t idesc = tc::idesc_tf32(BM, BN);
@@ -314,20 +426,25 @@ __global__ void __launch_bounds__(kConvThreads, 1)
           // The A tile's cp.async writes are complete once the stage barrier
           // phase completes (cp.async.mbarrier.arrive tracks them); the
           // tcgen05 fence orders the MMAs after that wait, as in CUTLASS's
-          // SM100 cp.async mainloop. A per-stage fence.proxy.async here would
-          // drain the producers' in-flight copies and serialise the ring.
+          // SM100 cp.async mainloop.
           tc::tc_fence_after();
           const uint32_t sa = tc::smem_u32(smem + stage * Cfg::STAGE_BYTES);
           const uint32_t sb = sa + SPLIT * Cfg::A_BYTES;
+          const bool a_cols = g.mode == kIm2col16;
 #pragma unroll
           for (int k = 0; k < BK / 8; ++k) {
-            const uint64_t a0 = tc::desc_kmajor_sw128(sa + k * 32);
+            // A: 128-byte swizzled rows (advance 32 bytes per k-step), or
+            // 2 KB core-matrix columns of 4 channels (two per k-step).
+            const uint64_t a0 = a_cols ? tc::desc_kmajor_noswizzle(sa + k * 4096, 2048, 128)
+                                       : tc::desc_kmajor_sw128(sa + k * 32);
             const uint64_t b0 = tc::desc_kmajor_sw128(sb + k * 32);
             const uint32_t accum = (kb | k) != 0;
             if (SPLIT == 1) {
               tc::mma_tf32(d_tmem, a0, b0, idesc, accum);
             } else {
-              const uint64_t a1 = tc::desc_kmajor_sw128(sa + Cfg::A_BYTES + k * 32);
+              const uint32_t sa1 = sa + Cfg::A_BYTES;
+              const uint64_t a1 = a_cols ? tc::desc_kmajor_noswizzle(sa1 + k * 4096, 2048, 128)
+                                         : tc::desc_kmajor_sw128(sa1 + k * 32);
               const uint64_t b1 = tc::desc_kmajor_sw128(sb + Cfg::B_BYTES + k * 32);
               tc::mma_tf32(d_tmem, a1, b0, idesc, accum);
               tc::mma_tf32(d_tmem, a0, b1, idesc, 1);
@@ -346,9 +463,12 @@ __global__ void __launch_bounds__(kConvThreads, 1)
       tc::mbar_wait(done, 0, g.err);
     }
   } else {
-    // ---------------- epilogue (warps 5..8) ----------------
-    const int quad = warp & 3;
-    float* stage_tile = epi + quad * 32 * (kStageCols + 1);  // this warp's 32 x 33 tile
+    // ---------------- epilogue (warps 9..16) ----------------
+    // Warp w reads TMEM lanes [32 (w % 4), +32) (the hardware's lane
+    // quadrant rule); the two warps of a quadrant take alternate 32-column
+    // chunks.
+    const int quad = warp & 3, half = (warp - kMmaWarp - 1) >> 2;
+    float* stage_tile = epi + (warp - kMmaWarp - 1) * 32 * (kStageCols + 1);  // this warp's 32 x 33 tile
     const bool vec_ok = (g.Cout % 4 == 0) && ((((uintptr_t)g.out) & 15) == 0) &&
                         (!g.residual || ((((uintptr_t)g.residual) & 15) == 0));
     const bool bias_vec = g.bias && ((((uintptr_t)g.bias) & 15) == 0);
@@ -362,27 +482,41 @@ __global__ void __launch_bounds__(kConvThreads, 1)
       tc::tc_fence_after();
       const int64_t m_base = (int64_t)mt * BM + quad * 32;  // this warp's first row
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += kStageCols) {
-        uint32_t r[2][16];
-        __syncwarp();  // tcgen05.ld is .sync.aligned: the warp must be converged
-        const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN + c0;
-        tc::tmem_ld16(taddr, r[0]);
-        tc::tmem_ld16(taddr + 16, r[1]);
-        tc::tmem_ld_wait();
+      for (int c0 = half * kStageCols; c0 < BN; c0 += 2 * kStageCols) {
         const int co0 = nt * BN + c0;
-        if (co0 >= g.Cout) continue;
+        if (co0 >= g.Cout) continue;  // warp-uniform: no TMEM load is skipped by part of a warp
+        const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN + c0;
         if (g.out_nhwc) {
           // Stage the 32 x 32 block, then write it row-contiguously: eight
           // lanes cover one 128-byte row segment, a warp four rows.
-#pragma unroll
-          for (int j = 0; j < 32; ++j) stage_tile[lane * (kStageCols + 1) + j] = __uint_as_float(r[j >> 4][j & 15]);
-          __syncwarp();
           const int cl = (lane & 7) * 4;  // column within the block
           const int co = co0 + cl;
-          float4 bv = make_float4(0.f, 0.f, 0.f, 0.f);
           // 16-byte row accesses need C_out % 4 == 0 and aligned bases
           // (vec_ok); otherwise the per-element path below is taken.
           const bool col_ok = vec_ok && co + 3 < g.Cout;
+          // Issue this chunk's residual loads first so their latency overlaps
+          // the staging below.
+          float4 rv[8];
+          if (g.act == kActAddRelu && col_ok) {
+#pragma unroll
+            for (int it = 0; it < 8; ++it) {
+              const int64_t m = m_base + (lane >> 3) + 4 * it;
+              rv[it] = m < g.M ? *reinterpret_cast<const float4*>(g.residual + m * g.Cout + co)
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+          }
+#pragma unroll
+          for (int h16 = 0; h16 < 2; ++h16) {
+            uint32_t r[16];
+            __syncwarp();  // tcgen05.ld is .sync.aligned: the warp must be converged
+            tc::tmem_ld16(taddr + 16 * h16, r);
+            tc::tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              stage_tile[lane * (kStageCols + 1) + 16 * h16 + j] = __uint_as_float(r[j]);
+          }
+          __syncwarp();
+          float4 bv = make_float4(0.f, 0.f, 0.f, 0.f);
           if (g.bias) {
             if (col_ok && bias_vec) {
               bv = *reinterpret_cast<const float4*>(g.bias + co);
@@ -393,7 +527,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
               bv.w = co + 3 < g.Cout ? g.bias[co + 3] : 0.f;
             }
           }
-#pragma unroll 2
+#pragma unroll
           for (int it = 0; it < 8; ++it) {
             const int rr = (lane >> 3) + 4 * it;
             const int64_t m = m_base + rr;
@@ -404,11 +538,10 @@ __global__ void __launch_bounds__(kConvThreads, 1)
             float* dst = g.out + m * g.Cout + co;
             if (col_ok) {
               if (g.act == kActAddRelu) {
-                const float4 rv = *reinterpret_cast<const float4*>(g.residual + m * g.Cout + co);
-                o.x = __fadd_rn(o.x, rv.x);
-                o.y = __fadd_rn(o.y, rv.y);
-                o.z = __fadd_rn(o.z, rv.z);
-                o.w = __fadd_rn(o.w, rv.w);
+                o.x = __fadd_rn(o.x, rv[it].x);
+                o.y = __fadd_rn(o.y, rv[it].y);
+                o.z = __fadd_rn(o.z, rv[it].z);
+                o.w = __fadd_rn(o.w, rv[it].w);
               }
               o.x = activate(o.x, g.act);
               o.y = activate(o.y, g.act);
@@ -429,17 +562,25 @@ __global__ void __launch_bounds__(kConvThreads, 1)
           // NCHW: channel co of image n at plane offset p; lanes hold
           // consecutive pixels, so each store instruction is coalesced.
           const int64_t m = m_base + lane;
-          if (m < g.M) {
-            const int64_t n_img = m / OHW, p = m - n_img * OHW;
-            float* dst = g.out + (n_img * g.Cout + co0) * OHW + p;
-            const float* res = g.residual ? g.residual + (n_img * g.Cout + co0) * OHW + p : nullptr;
+          const int64_t n_img = m / OHW, p = m - n_img * OHW;
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              if (co0 + j >= g.Cout) break;
-              float o = __uint_as_float(r[j >> 4][j & 15]);
-              if (g.bias) o = __fadd_rn(o, g.bias[co0 + j]);
-              if (g.act == kActAddRelu) o = __fadd_rn(o, res[(int64_t)j * OHW]);
-              dst[(int64_t)j * OHW] = activate(o, g.act);
+          for (int h16 = 0; h16 < 2; ++h16) {
+            uint32_t r[16];
+            __syncwarp();  // tcgen05.ld is .sync.aligned: the warp must be converged
+            tc::tmem_ld16(taddr + 16 * h16, r);
+            tc::tmem_ld_wait();
+            if (m < g.M) {
+              const int cb = co0 + 16 * h16;
+              float* dst = g.out + (n_img * g.Cout + cb) * OHW + p;
+              const float* res = g.residual ? g.residual + (n_img * g.Cout + cb) * OHW + p : nullptr;
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                if (cb + j >= g.Cout) break;
+                float o = __uint_as_float(r[j]);
+                if (g.bias) o = __fadd_rn(o, g.bias[cb + j]);
+                if (g.act == kActAddRelu) o = __fadd_rn(o, res[(int64_t)j * OHW]);
+                dst[(int64_t)j * OHW] = activate(o, g.act);
+              }
             }
           }
         }
@@ -452,7 +593,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
 
   tc::tc_fence_before();
   __syncthreads();
-  if (warp == 4) {
+  if (warp == kMmaWarp) {
     tc::tc_fence_after();
     tc::tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
   }
@@ -618,6 +759,23 @@ bool launch_conv(ConvArgs g, const float* w0, const float* w1, const char* op) {
   if (!encode_tmap_f32(&tw0, w0, 2, dims, strides, box, nullptr, op)) return false;
   tw1 = tw0;
   if (SPLIT == 2 && !encode_tmap_f32(&tw1, w1, 2, dims, strides, box, nullptr, op)) return false;
+  // Activation im2col maps over the NHWC input: bounding box = window
+  // origins of all output pixels, [-pad, (O-1)*stride - pad] per axis.
+  CUtensorMap tx0 = tw0, tx1 = tw0;
+  if (g.mode == kIm2col128 || g.mode == kIm2col16) {
+    const uint64_t xd[4] = {(uint64_t)g.C4, (uint64_t)g.W, (uint64_t)g.H, (uint64_t)g.N};
+    const uint64_t xs[3] = {(uint64_t)g.C4 * 4, (uint64_t)g.W * g.C4 * 4,
+                            (uint64_t)g.H * g.W * g.C4 * 4};
+    const int lower = -g.ph, upper = (g.OH - 1) * g.sh - g.ph - (g.H - 1);
+    const bool sw128 = g.mode == kIm2col128;
+    const uint32_t cpp = sw128 ? 32 : 4;
+    if (!encode_tmap_im2col_f32(&tx0, g.x_hi, xd, xs, lower, upper, cpp, BM, g.sh, sw128, op))
+      return false;
+    tx1 = tx0;
+    if (SPLIT == 2 &&
+        !encode_tmap_im2col_f32(&tx1, g.x_lo, xd, xs, lower, upper, cpp, BM, g.sh, sw128, op))
+      return false;
+  }
   g.n_tiles = (int)cdiv(g.Cout, BN);
   g.m_tiles = (int)cdiv(g.M, BM);
   g.tiles = (int64_t)g.m_tiles * g.n_tiles;
@@ -631,7 +789,7 @@ bool launch_conv(ConvArgs g, const float* w0, const float* w1, const char* op) {
     attr_set = true;
   }
   const int grid = (int)(g.tiles < sm_count() ? g.tiles : sm_count());
-  kern<<<grid, kConvThreads, Cfg::SMEM, ctx().stream>>>(tw0, tw1, g);
+  kern<<<grid, kConvThreads, Cfg::SMEM, ctx().stream>>>(tw0, tw1, tx0, tx1, g);
   return check_launch(op);
 }
 
@@ -745,6 +903,17 @@ void conv_impl(Tensor* input, Tensor* weight, Tensor* bias, Tensor* residual, Te
 
   ConvArgs g{};
   g.mode = wl.element ? kElement : kChunk;
+  if (!wl.element) {
+    // TMA im2col describes square windows with equal pads/strides on both
+    // axes (its bounding-box corners are shared here); the corners must lie
+    // in the map's signed range.
+    const int lower = -ph, upper_h = (OH - 1) * sh - ph - (H - 1),
+              upper_w = (OW - 1) * sw - pw - (W - 1);
+    const bool square = KH == KW && sh == sw && ph == pw && upper_h == upper_w;
+    if (square && lower >= -64 && upper_h >= -64 && upper_h <= 63 && sh <= 8 &&
+        OH > 0 && OW > 0 && aligned16(x_hi) && (!x_lo || aligned16(x_lo)))
+      g.mode = (C4 % 32 == 0) ? kIm2col128 : kIm2col16;
+  }
   if (is_nhwc(input)) {
     g.xs_n = (int64_t)H * W * C;
     g.xs_c = 1;

@@ -95,6 +95,20 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, u
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z), "r"(w)
       : "memory");
 }
+// im2col load over an NHWC tensor map: starts at pixel (w, h, n) of the map's
+// bounding box (which must be a real output pixel's window origin) and walks
+// pixelsPerColumn pixels along W, H, N; (ow, oh) is the filter-tap offset
+// added to every pixel; channels [c, c + channelsPerPixel).
+__device__ __forceinline__ void tma_load_im2col_4d(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                                   int c, int w, int h, int n, uint16_t ow,
+                                                   uint16_t oh) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.im2col.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2], {%7, %8};" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c), "r"(w), "r"(h), "r"(n),
+      "h"(ow), "h"(oh)
+      : "memory");
+}
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -170,6 +184,19 @@ __device__ __forceinline__ uint64_t desc_kmajor_sw128(uint32_t smem_addr) {
   return d;
 }
 
+// Shared-memory matrix descriptor: K-major operand without swizzling, made of
+// 8-row x 16-byte core matrices stored contiguously (128 bytes each): core
+// matrices adjacent along M are `sbo` bytes apart, along K `lbo` bytes apart.
+__device__ __forceinline__ uint64_t desc_kmajor_noswizzle(uint32_t smem_addr, uint32_t lbo,
+                                                          uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_addr & 0x3FFFFu) >> 4);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1u << 46;
+  return d;  // layout type 0 = SWIZZLE_NONE
+}
+
 // Instruction descriptor for kind::tf32 with fp32 accumulation, both operands
 // K-major: c_format F32 (1) at [4,6), a/b_format TF32 (2) at [7,10)/[10,13),
 // N >> 3 at [17,23), M >> 4 at [24,29).
@@ -194,5 +221,15 @@ __device__ __forceinline__ float to_tf32(float x) {
 bool encode_tmap_f32(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
                      const uint64_t* strides_bytes, const uint32_t* box,
                      const uint32_t* elem_strides, const char* op);
+
+// Host: encodes a 4-D im2col tensor map (fp32, zero OOB fill) over an NHWC
+// tensor: dims {C, W, H, N}, strides_bytes for W, H, N; bounding-box corners
+// {lower, upper} applied to both W and H (callers only use square windows);
+// elem_strides {1, stride, stride, 1}; swizzle128 selects SWIZZLE_128B (one
+// 128-byte row per pixel) or SWIZZLE_NONE.
+bool encode_tmap_im2col_f32(CUtensorMap* map, const void* base, const uint64_t* dims,
+                            const uint64_t* strides_bytes, int lower, int upper,
+                            uint32_t channels_per_pixel, uint32_t pixels_per_column,
+                            uint32_t stride, bool swizzle128, const char* op);
 
 }  // namespace nnc
