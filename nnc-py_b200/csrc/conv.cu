@@ -13,25 +13,31 @@
 //                layout.
 //
 // Kernel (persistent, one CTA per SM, 416 threads = 13 warps):
-//   warps 0..7  producers: gather the 128 x 32 A tile with cp.async (zero
-//               fill for taps in the padding) into the 128-byte swizzle
-//               layout. Chunk mode: 16-byte copies, eight neighbouring
-//               threads per 128-byte row (a warp instruction covers four
-//               rows); each thread owns four rows whose base offsets and
-//               tap-validity masks are computed once per tile, and advances
-//               its (tap, channel) position incrementally, so a copy costs a
-//               handful of instructions. Element mode: 4-byte copies with
-//               per-k offsets from a shared-memory table. Thread 0 also
-//               TMA-loads the BN x 32 weight tile. Arrival is asynchronous
+//   warps 0..3  producers. TMA modes (square windows, equal strides and pads;
+//               the common case): thread 0 alone issues per stage one TMA
+//               load of the BN x 32 weight tile and TMA im2col loads of the
+//               128 x 32 activation tile from the NHWC input (one load of 32
+//               channels into the 128-byte swizzle layout when C4 % 32 == 0,
+//               eight loads of 4-channel core-matrix columns otherwise).
+//               Gather modes (other windows, tiny reductions): all 128
+//               threads gather the A tile with cp.async (zero fill for taps
+//               in the padding). Chunk mode: 16-byte copies, eight
+//               neighbouring threads per 128-byte row; each thread owns eight
+//               rows whose base offsets and tap-validity masks are computed
+//               once per tile and advances its (tap, channel) position
+//               incrementally. Element mode: 4-byte copies with per-k offsets
+//               from a shared-memory table. Arrival is asynchronous
 //               (cp.async.mbarrier.arrive.noinc), so producers run ahead.
-//   warp 8      TMEM allocation + single-thread tcgen05.mma issue (kind::tf32,
+//   warp 4      TMEM allocation + single-thread tcgen05.mma issue (kind::tf32,
 //               M = 128, N = BN, 4 k-steps per stage; 3 MMAs per k-step in
 //               3xTF32 mode), commits release ring slots and accumulators.
-//   warps 9..12 epilogue: tcgen05.ld of 32 columns at a time; NHWC outputs
-//               are staged through a 32 x 33 shared tile so bias, residual
-//               and stores run row-contiguously (eight lanes per 128-byte
-//               row); NCHW outputs store per channel plane, coalesced across
-//               the warp's 32 consecutive pixels.
+//   warps 5..12 epilogue, two warps per TMEM lane quadrant, each taking
+//               alternate 32-column blocks (tcgen05.ld of 16 columns at a
+//               time); NHWC outputs are staged through a 32 x 33 shared tile
+//               so bias, residual (prefetched before staging) and stores run
+//               row-contiguously (eight lanes per 128-byte row); NCHW
+//               outputs store per channel plane, coalesced across the warp's
+//               32 consecutive pixels.
 //
 // Reference semantics (ops.c:720-1050): window origin o*stride - pad with the
 // top/left pad only, out-of-range taps contribute zero, output extent from
@@ -780,13 +786,15 @@ bool launch_conv(ConvArgs g, const float* w0, const float* w1, const char* op) {
   g.m_tiles = (int)cdiv(g.M, BM);
   g.tiles = (int64_t)g.m_tiles * g.n_tiles;
   auto kern = conv_tc_kernel<BN, SPLIT, STAGES>;
-  static bool attr_set = false;
-  if (!attr_set) {
+  // The dynamic shared-memory opt-in is a property of the function in each
+  // device's context: set it once per instantiation and device.
+  static bool attr_set[64] = {};
+  if (!attr_set[ctx().device]) {
     if (!check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)Cfg::SMEM),
                     op, "cudaFuncSetAttribute"))
       return false;
-    attr_set = true;
+    attr_set[ctx().device] = true;
   }
   const int grid = (int)(g.tiles < sm_count() ? g.tiles : sm_count());
   kern<<<grid, kConvThreads, Cfg::SMEM, ctx().stream>>>(tw0, tw1, tx0, tx1, g);

@@ -372,13 +372,15 @@ bool launch_tc(const Problem& p, const float* A0, const float* A1, const float* 
   g.relu = p.relu;
   g.err = device_error_word();
   auto kern = gemm_tc_kernel<BN, SPLIT, STAGES>;
-  static bool attr_set = false;  // per instantiation
-  if (!attr_set) {
+  // The dynamic shared-memory opt-in is a property of the function in each
+  // device's context: set it once per instantiation and device.
+  static bool attr_set[64] = {};
+  if (!attr_set[ctx().device]) {
     if (!check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)Cfg::SMEM),
                     op, "cudaFuncSetAttribute"))
       return false;
-    attr_set = true;
+    attr_set[ctx().device] = true;
   }
   const int grid = (int)(g.tiles < sm_count() ? g.tiles : sm_count());
   kern<<<grid, kTCThreads, Cfg::SMEM, ctx().stream>>>(ta0, ta1, tb0, tb1, g);
