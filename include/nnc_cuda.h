@@ -83,6 +83,30 @@ size_t nnc_cuda_get_workspace_capacity(void);
 size_t nnc_cuda_prepacked_conv_weight_bytes(const Tensor* w);
 int nnc_cuda_prepack_conv_weight(Tensor* w, void* dst, size_t dst_bytes);
 
+/* ---- convolution that allocates nothing ---------------------------------------
+ * No counterpart in the reference. nnc_conv (nnc_ops.h) with the same
+ * arguments and results, for callers that must not allocate device memory
+ * while they run. Its scratch (the NHWC copy of an NCHW input and the packed
+ * weights; each twice in 3xTF32 mode) lives in a file-scope 16 MiB device
+ * array, held by every GPU that loads the library until the process exits,
+ * instead of the workspace that the other entry points grow with
+ * cudaMallocAsync. It calls no cudaMalloc, cudaFree or other allocating
+ * routine; a call whose scratch would exceed 16 MiB is rejected with
+ * NNC_CUDA_ERR_INVALID before any work is queued.
+ *   - Call nnc_cuda_init() on the device first (it creates the device's error
+ *     word, which allocates); otherwise the call fails with
+ *     NNC_CUDA_ERR_INVALID.
+ *   - The first call on each device does the set-up: it resolves the array's
+ *     device address (cudaGetSymbolAddress) with that device current. Make
+ *     that first call before any stream capture.
+ *   - All calls on a device share the array, which keeps the previous call's
+ *     contents (nothing in it needs to start at zero: a call writes every
+ *     scratch byte it reads before reading it). Calls that overlap on the GPU
+ *     (other streams or threads on the same device) race on it. */
+void nnc_conv_static_scratch(Tensor* input, Tensor* weight, Tensor* bias, Tensor* output,
+                             int kernel_h, int kernel_w, int stride_h, int stride_w,
+                             int pad_h, int pad_w);
+
 /* ---- layout conversion at model boundaries (logical shapes are NCHW) ---- */
 void nnc_cuda_nchw_to_nhwc(Tensor* input, Tensor* output);
 void nnc_cuda_nhwc_to_nchw(Tensor* input, Tensor* output);

@@ -42,6 +42,10 @@ inline bool check_launch(const char* op) {
 // set it to NNC_CUDA_ERR_DEVICE_TIMEOUT; the host reads it on demand).
 int* device_error_word();
 int sm_count();
+// True once the current device's state (error word, SM count) exists, so
+// that device_error_word() and sm_count() allocate nothing; nnc_cuda_init
+// creates it. Never allocates.
+bool device_ready();
 
 // Scratch memory on the current device for the current stream.
 void* workspace(size_t bytes, const char* op);

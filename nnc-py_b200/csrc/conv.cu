@@ -45,6 +45,8 @@
 // (relu: v > 0 ? v : 0; sigmoid: 1 / (1 + expf(-v))).
 #include <math.h>
 
+#include <mutex>
+
 #include "common.cuh"
 #include "tc.cuh"
 
@@ -810,8 +812,45 @@ bool conv_f32(const Tensor* t, const char* op, const char* name) {
   return true;
 }
 
+// Fixed-size device scratch of nnc_conv_static_scratch: the converted input
+// planes and packed weights of one call live here instead of in the
+// runtime's growable workspace. File-scope, so every device that loads this
+// module holds kStaticScratchBytes until the process exits; all calls share
+// it, and it keeps the previous call's contents.
+constexpr size_t kStaticScratchBytes = size_t(16) << 20;  // 16 MiB
+static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
+
+struct StaticScratch {
+  float* ptr;
+  size_t bytes;
+};
+
+// Address of g_static_scratch on the current device, resolved once per device
+// (the first nnc_conv_static_scratch call on that device, with it current).
+// Returns false with the thread's status set when it cannot be resolved.
+bool static_scratch_on_device(StaticScratch* out, const char* op) {
+  static std::mutex mu;
+  static float* ptrs[64] = {};
+  const int dev = ctx().device;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!ptrs[dev]) {
+    float* ptr = nullptr;
+    if (!check_cuda(cudaGetSymbolAddress((void**)&ptr, g_static_scratch), op,
+                    "cudaGetSymbolAddress(g_static_scratch)"))
+      return false;
+    ptrs[dev] = ptr;
+  }
+  out->ptr = ptrs[dev];
+  out->bytes = kStaticScratchBytes;
+  return true;
+}
+
+// fixed == nullptr: scratch comes from the runtime workspace (which may grow
+// with cudaMallocAsync); otherwise from *fixed, and a call that needs more
+// than it holds is rejected before any work is queued.
 void conv_impl(Tensor* input, Tensor* weight, Tensor* bias, Tensor* residual, Tensor* output,
-               int KH, int KW, int sh, int sw, int ph, int pw, int act, const char* op) {
+               int KH, int KW, int sh, int sw, int ph, int pw, int act, const char* op,
+               const StaticScratch* fixed = nullptr) {
   if (!conv_f32(input, op, "input") || !conv_f32(weight, op, "weight") ||
       !conv_f32(output, op, "output"))
     return;
@@ -866,7 +905,19 @@ void conv_impl(Tensor* input, Tensor* weight, Tensor* bias, Tensor* residual, Te
   size_t need = 0;
   if (!in_place) need += (size_t)(split ? 2 : 1) * ((x_elems + 63) / 64 * 64) * 4;
   if (!packed) need += (size_t)(split ? 2 : 1) * w_elems * 4;
-  float* ws = need ? (float*)workspace(need + 256, op) : nullptr;
+  float* ws = nullptr;
+  if (need && fixed) {
+    if (need + 256 > fixed->bytes) {
+      fail(NNC_CUDA_ERR_INVALID, op,
+           "needs %zu bytes of scratch; the static scratch holds %zu (input %lldx%dx%dx%d, "
+           "weight %dx%dx%dx%d)",
+           need + 256, fixed->bytes, (long long)N, C, H, W, Cout, C, KH, KW);
+      return;
+    }
+    ws = fixed->ptr;
+  } else if (need) {
+    ws = (float*)workspace(need + 256, op);
+  }
   if (need && !ws) return;
   float* cur = ws;
 
@@ -987,6 +1038,27 @@ void nnc_conv(Tensor* input, Tensor* weight, Tensor* bias, Tensor* output, int k
   OpScope s("nnc_conv");
   conv_impl(input, weight, bias, nullptr, output, kernel_h, kernel_w, stride_h, stride_w, pad_h,
             pad_w, kActNone, "nnc_conv");
+}
+
+// nnc_conv with its scratch (converted input planes, packed weights) in the
+// file-scope 16 MiB g_static_scratch instead of the growable workspace:
+// allocates nothing. Every byte the kernel reads from the scratch is written
+// earlier in the same call, so nothing there needs clearing between calls.
+void nnc_conv_static_scratch(Tensor* input, Tensor* weight, Tensor* bias, Tensor* output,
+                             int kernel_h, int kernel_w, int stride_h, int stride_w, int pad_h,
+                             int pad_w) {
+  const char* op = "nnc_conv_static_scratch";
+  OpScope s(op);
+  // The device state (error word, SM count) must already exist: creating it
+  // allocates, which this entry point never does.
+  if (!device_ready()) {
+    fail(NNC_CUDA_ERR_INVALID, op, "call nnc_cuda_init(%d) on this device first", ctx().device);
+    return;
+  }
+  StaticScratch fixed;
+  if (!static_scratch_on_device(&fixed, op)) return;
+  conv_impl(input, weight, bias, nullptr, output, kernel_h, kernel_w, stride_h, stride_w, pad_h,
+            pad_w, kActNone, op, &fixed);
 }
 void nnc_conv_relu(Tensor* input, Tensor* weight, Tensor* bias, Tensor* output, int kernel_h,
                    int kernel_w, int stride_h, int stride_w, int pad_h, int pad_w) {

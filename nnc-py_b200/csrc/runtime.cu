@@ -95,6 +95,10 @@ bool check_cuda(cudaError_t err, const char* op, const char* what) {
 }
 
 int* device_error_word() { return dev_state(ctx().device).error_word; }
+bool device_ready() {
+  const DeviceState& s = g_dev[ctx().device];
+  return s.ready && s.error_word != nullptr;
+}
 int sm_count() { return dev_state(ctx().device).sms; }
 
 int grid_for(int64_t work_items, int threads, int max_ctas_per_sm) {
