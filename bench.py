@@ -303,7 +303,9 @@ def our_arm(opt):
             "roofline": {"bound": "tensor", "kernel": "conv_tc_kernel (tcgen05 implicit GEMM)",
                          "achieved": round(achieved, 2) if achieved else None, "peak": round(peak, 1),
                          "unit": "TFLOP/s", "frac": round(achieved / peak, 4) if achieved else None,
-                         "traffic": roofline_traffic(),
+                         "traffic": roofline_traffic(B),
+                         "traffic_scope": "DRAM bytes per step over all conv launches (ncu, scaled per image)",
+                         "algorithmic_bytes": round(conv_bytes(wl)),
                          "peak_note": f"dense TF32 = bf16/2 of {pk['source']} MEASURED_PEAKS.json"
                                       + (", /3 for the 3 MMAs of 3xTF32" if prec == L.PRECISION_3XTF32 else ""),
                          "conv_ms_per_step": round(conv_ms_step, 4),
@@ -329,13 +331,38 @@ def our_arm(opt):
     return 0
 
 
-def roofline_traffic():
-    """DRAM bytes per conv launch from the committed ncu summary, if any."""
+def conv_bytes(model) -> float:
+    """Algorithmic bytes of the conv entry points per step: each conv's input,
+    weight and output once, plus the residual read by a fused add."""
+    prod = {o: n for n in model.nodes for o in n.outputs}
+
+    def nbytes(t):
+        k = 4
+        for d in model.shapes[t]:
+            k *= d
+        return k
+
+    total = 0.0
+    for n in model.nodes:
+        if n.op == "Conv":
+            total += nbytes(n.inputs[0]) + nbytes(n.inputs[1]) + nbytes(n.outputs[0])
+        elif n.op == "Add":
+            a, b = n.inputs
+            if a in prod and prod[a].op == "Conv":
+                total += nbytes(b)
+            elif b in prod and prod[b].op == "Conv":
+                total += nbytes(a)
+    return total
+
+
+def roofline_traffic(images: int):
+    """DRAM bytes (read + write) of all conv launches of one step, from the
+    committed ncu summary's per-image figure, scaled to `images`."""
     p = ROOT / "profiles" / "conv_tc_resnet18_traffic.txt"
     if p.exists():
         for line in p.read_text().splitlines():
-            if line.startswith("bytes_per_launch="):
-                return float(line.split("=")[1])
+            if line.startswith("dram_bytes_per_image="):
+                return round(float(line.split("=")[1]) * images)
     return None
 
 
