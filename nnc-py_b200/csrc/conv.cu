@@ -44,6 +44,7 @@
 // output->shape, bias added before one rounding to fp32, then the activation
 // (relu: v > 0 ? v : 0; sigmoid: 1 / (1 + expf(-v))).
 #include <math.h>
+#include <stdlib.h>
 
 #include <mutex>
 
@@ -74,7 +75,10 @@ enum Act : int { kActNone = 0, kActRelu = 1, kActSigmoid = 2, kActAddRelu = 3 };
 //               matrices (K-major, no swizzle);
 //   kChunk / kElement: cp.async gathers by the producer warps (windows the
 //               im2col bounding box cannot describe, and tiny reductions).
-enum Mode : int { kChunk = 0, kElement = 1, kIm2col128 = 2, kIm2col16 = 3 };
+//   kHalo:      stride-1 windows, C4 % 32 == 0: one TMA load of an input
+//               window per 32-channel block, shared by every tap (see
+//               conv_halo_kernel).
+enum Mode : int { kChunk = 0, kElement = 1, kIm2col128 = 2, kIm2col16 = 3, kHalo = 4 };
 constexpr int kMaxElementK = 64;  // K_pad limit of the element mode (see weight_layout)
 
 struct ConvArgs {
@@ -88,6 +92,7 @@ struct ConvArgs {
   int64_t M;  // N*OH*OW
   int m_tiles, n_tiles;
   int64_t tiles;
+  int tiles_x, tiles_y;  // kHalo: 8 x 16 output blocks per image row / column
   int64_t xs_n, xs_c, xs_h, xs_w;  // element-mode input strides (elements)
   const float* x_hi;  // input (hi plane in 3xTF32 mode)
   const float* x_lo;  // lo plane (3xTF32) or nullptr
@@ -139,6 +144,138 @@ __device__ __forceinline__ float activate(float o, int act) {
   if (act == kActSigmoid) return 1.0f / (1.0f + expf(-o));
   return o;
 }
+
+// Epilogue of one accumulator tile for one warp: TMEM lanes [32 quad, +32)
+// (the hardware's lane-quadrant rule) of the BN-column accumulator at TMEM
+// column acc_col, 32-column chunks c0 = c_first, c_first + c_step, ... below
+// BN. rows(r) maps accumulator row r (0..127) to its output pixel
+// m = (n, oh, ow), or -1 when the row is padding.
+template <int BN, class RowMap>
+__device__ __forceinline__ void store_tile(const ConvArgs& g, uint32_t tmem_base, uint32_t acc_col,
+                                           int nt, int quad, int c_first, int c_step, int lane,
+                                           float* stage_tile, bool vec_ok, bool bias_vec,
+                                           const RowMap& rows) {
+  const int64_t OHW = (int64_t)g.OH * g.OW;
+#pragma unroll 1
+  for (int c0 = c_first; c0 < BN; c0 += c_step) {
+    const int co0 = nt * BN + c0;
+    if (co0 >= g.Cout) continue;  // warp-uniform: no TMEM load is skipped by part of a warp
+    const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + acc_col + c0;
+    if (g.out_nhwc) {
+      // Stage the 32 x 32 block, then write it row-contiguously: eight
+      // lanes cover one 128-byte row segment, a warp four rows.
+      const int cl = (lane & 7) * 4;  // column within the block
+      const int co = co0 + cl;
+      // 16-byte row accesses need C_out % 4 == 0 and aligned bases
+      // (vec_ok); otherwise the per-element path below is taken.
+      const bool col_ok = vec_ok && co + 3 < g.Cout;
+      // Issue this chunk's residual loads first so their latency overlaps
+      // the staging below.
+      float4 rv[8];
+      if (g.act == kActAddRelu && col_ok) {
+#pragma unroll
+        for (int it = 0; it < 8; ++it) {
+          const int64_t m = rows(quad * 32 + (lane >> 3) + 4 * it);
+          rv[it] = m >= 0 ? *reinterpret_cast<const float4*>(g.residual + m * g.Cout + co)
+                          : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      }
+#pragma unroll
+      for (int h16 = 0; h16 < 2; ++h16) {
+        uint32_t r[16];
+        __syncwarp();  // tcgen05.ld is .sync.aligned: the warp must be converged
+        tc::tmem_ld16(taddr + 16 * h16, r);
+        tc::tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          stage_tile[lane * (kStageCols + 1) + 16 * h16 + j] = __uint_as_float(r[j]);
+      }
+      __syncwarp();
+      float4 bv = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (g.bias) {
+        if (col_ok && bias_vec) {
+          bv = *reinterpret_cast<const float4*>(g.bias + co);
+        } else {
+          bv.x = co < g.Cout ? g.bias[co] : 0.f;
+          bv.y = co + 1 < g.Cout ? g.bias[co + 1] : 0.f;
+          bv.z = co + 2 < g.Cout ? g.bias[co + 2] : 0.f;
+          bv.w = co + 3 < g.Cout ? g.bias[co + 3] : 0.f;
+        }
+      }
+#pragma unroll
+      for (int it = 0; it < 8; ++it) {
+        const int rr = (lane >> 3) + 4 * it;
+        const int64_t m = rows(quad * 32 + rr);
+        if (m < 0) continue;
+        const float* srow = stage_tile + rr * (kStageCols + 1) + cl;
+        float4 o = make_float4(__fadd_rn(srow[0], bv.x), __fadd_rn(srow[1], bv.y),
+                               __fadd_rn(srow[2], bv.z), __fadd_rn(srow[3], bv.w));
+        float* dst = g.out + m * g.Cout + co;
+        if (col_ok) {
+          if (g.act == kActAddRelu) {
+            o.x = __fadd_rn(o.x, rv[it].x);
+            o.y = __fadd_rn(o.y, rv[it].y);
+            o.z = __fadd_rn(o.z, rv[it].z);
+            o.w = __fadd_rn(o.w, rv[it].w);
+          }
+          o.x = activate(o.x, g.act);
+          o.y = activate(o.y, g.act);
+          o.z = activate(o.z, g.act);
+          o.w = activate(o.w, g.act);
+          *reinterpret_cast<float4*>(dst) = o;
+        } else {
+          const float ov[4] = {o.x, o.y, o.z, o.w};
+          for (int q = 0; q < 4 && co + q < g.Cout; ++q) {
+            float v = ov[q];
+            if (g.act == kActAddRelu) v = __fadd_rn(v, g.residual[m * g.Cout + co + q]);
+            dst[q] = activate(v, g.act);
+          }
+        }
+      }
+      __syncwarp();
+    } else {
+      // NCHW: channel co of image n at plane offset p; lanes hold
+      // consecutive pixels, so each store instruction is coalesced.
+      const int64_t m = rows(quad * 32 + lane);
+      const int64_t n_img = m / OHW, p = m - n_img * OHW;
+#pragma unroll
+      for (int h16 = 0; h16 < 2; ++h16) {
+        uint32_t r[16];
+        __syncwarp();  // tcgen05.ld is .sync.aligned: the warp must be converged
+        tc::tmem_ld16(taddr + 16 * h16, r);
+        tc::tmem_ld_wait();
+        if (m >= 0) {
+          const int cb = co0 + 16 * h16;
+          float* dst = g.out + (n_img * g.Cout + cb) * OHW + p;
+          const float* res = g.residual ? g.residual + (n_img * g.Cout + cb) * OHW + p : nullptr;
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            if (cb + j >= g.Cout) break;
+            float o = __uint_as_float(r[j]);
+            if (g.bias) o = __fadd_rn(o, g.bias[cb + j]);
+            if (g.act == kActAddRelu) o = __fadd_rn(o, res[(int64_t)j * OHW]);
+            dst[(int64_t)j * OHW] = activate(o, g.act);
+          }
+        }
+      }
+    }
+  }
+}
+
+// Row maps of the two tile shapes: a run of 128 consecutive output pixels,
+// and an 8-wide x 16-tall block of one image (row r = 8 y + x).
+struct LinearRows {
+  int64_t m0, M;
+  __device__ __forceinline__ int64_t operator()(int r) const { return m0 + r < M ? m0 + r : -1; }
+};
+struct BlockRows {
+  int64_t img0;  // n * OH * OW
+  int y0, x0, OH, OW;
+  __device__ __forceinline__ int64_t operator()(int r) const {
+    const int y = y0 + (r >> 3), x = x0 + (r & 7);
+    return (y < OH && x < OW) ? img0 + (int64_t)y * OW + x : -1;
+  }
+};
 
 template <int BN, int SPLIT, int STAGES>
 __global__ void __launch_bounds__(kConvThreads, 1)
@@ -471,7 +608,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
       tc::mbar_wait(done, 0, g.err);
     }
   } else {
-    // ---------------- epilogue (warps 9..16) ----------------
+    // ---------------- epilogue (warps 5..12) ----------------
     // Warp w reads TMEM lanes [32 (w % 4), +32) (the hardware's lane
     // quadrant rule); the two warps of a quadrant take alternate 32-column
     // chunks.
@@ -480,7 +617,6 @@ __global__ void __launch_bounds__(kConvThreads, 1)
     const bool vec_ok = (g.Cout % 4 == 0) && ((((uintptr_t)g.out) & 15) == 0) &&
                         (!g.residual || ((((uintptr_t)g.residual) & 15) == 0));
     const bool bias_vec = g.bias && ((((uintptr_t)g.bias) & 15) == 0);
-    const int64_t OHW = (int64_t)g.OH * g.OW;
     int local = 0;
     for (int64_t t = blockIdx.x; t < g.tiles; t += gridDim.x, ++local) {
       const int mt = (int)(t / g.n_tiles), nt = (int)(t % g.n_tiles);
@@ -488,111 +624,8 @@ __global__ void __launch_bounds__(kConvThreads, 1)
       const uint32_t aphase = (local >> 1) & 1;
       if (!tc::mbar_wait(&tfull[acc], aphase, g.err)) break;
       tc::tc_fence_after();
-      const int64_t m_base = (int64_t)mt * BM + quad * 32;  // this warp's first row
-#pragma unroll 1
-      for (int c0 = half * kStageCols; c0 < BN; c0 += 2 * kStageCols) {
-        const int co0 = nt * BN + c0;
-        if (co0 >= g.Cout) continue;  // warp-uniform: no TMEM load is skipped by part of a warp
-        const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN + c0;
-        if (g.out_nhwc) {
-          // Stage the 32 x 32 block, then write it row-contiguously: eight
-          // lanes cover one 128-byte row segment, a warp four rows.
-          const int cl = (lane & 7) * 4;  // column within the block
-          const int co = co0 + cl;
-          // 16-byte row accesses need C_out % 4 == 0 and aligned bases
-          // (vec_ok); otherwise the per-element path below is taken.
-          const bool col_ok = vec_ok && co + 3 < g.Cout;
-          // Issue this chunk's residual loads first so their latency overlaps
-          // the staging below.
-          float4 rv[8];
-          if (g.act == kActAddRelu && col_ok) {
-#pragma unroll
-            for (int it = 0; it < 8; ++it) {
-              const int64_t m = m_base + (lane >> 3) + 4 * it;
-              rv[it] = m < g.M ? *reinterpret_cast<const float4*>(g.residual + m * g.Cout + co)
-                               : make_float4(0.f, 0.f, 0.f, 0.f);
-            }
-          }
-#pragma unroll
-          for (int h16 = 0; h16 < 2; ++h16) {
-            uint32_t r[16];
-            __syncwarp();  // tcgen05.ld is .sync.aligned: the warp must be converged
-            tc::tmem_ld16(taddr + 16 * h16, r);
-            tc::tmem_ld_wait();
-#pragma unroll
-            for (int j = 0; j < 16; ++j)
-              stage_tile[lane * (kStageCols + 1) + 16 * h16 + j] = __uint_as_float(r[j]);
-          }
-          __syncwarp();
-          float4 bv = make_float4(0.f, 0.f, 0.f, 0.f);
-          if (g.bias) {
-            if (col_ok && bias_vec) {
-              bv = *reinterpret_cast<const float4*>(g.bias + co);
-            } else {
-              bv.x = co < g.Cout ? g.bias[co] : 0.f;
-              bv.y = co + 1 < g.Cout ? g.bias[co + 1] : 0.f;
-              bv.z = co + 2 < g.Cout ? g.bias[co + 2] : 0.f;
-              bv.w = co + 3 < g.Cout ? g.bias[co + 3] : 0.f;
-            }
-          }
-#pragma unroll
-          for (int it = 0; it < 8; ++it) {
-            const int rr = (lane >> 3) + 4 * it;
-            const int64_t m = m_base + rr;
-            if (m >= g.M) continue;
-            const float* srow = stage_tile + rr * (kStageCols + 1) + cl;
-            float4 o = make_float4(__fadd_rn(srow[0], bv.x), __fadd_rn(srow[1], bv.y),
-                                   __fadd_rn(srow[2], bv.z), __fadd_rn(srow[3], bv.w));
-            float* dst = g.out + m * g.Cout + co;
-            if (col_ok) {
-              if (g.act == kActAddRelu) {
-                o.x = __fadd_rn(o.x, rv[it].x);
-                o.y = __fadd_rn(o.y, rv[it].y);
-                o.z = __fadd_rn(o.z, rv[it].z);
-                o.w = __fadd_rn(o.w, rv[it].w);
-              }
-              o.x = activate(o.x, g.act);
-              o.y = activate(o.y, g.act);
-              o.z = activate(o.z, g.act);
-              o.w = activate(o.w, g.act);
-              *reinterpret_cast<float4*>(dst) = o;
-            } else {
-              const float ov[4] = {o.x, o.y, o.z, o.w};
-              for (int q = 0; q < 4 && co + q < g.Cout; ++q) {
-                float v = ov[q];
-                if (g.act == kActAddRelu) v = __fadd_rn(v, g.residual[m * g.Cout + co + q]);
-                dst[q] = activate(v, g.act);
-              }
-            }
-          }
-          __syncwarp();
-        } else {
-          // NCHW: channel co of image n at plane offset p; lanes hold
-          // consecutive pixels, so each store instruction is coalesced.
-          const int64_t m = m_base + lane;
-          const int64_t n_img = m / OHW, p = m - n_img * OHW;
-#pragma unroll
-          for (int h16 = 0; h16 < 2; ++h16) {
-            uint32_t r[16];
-            __syncwarp();  // tcgen05.ld is .sync.aligned: the warp must be converged
-            tc::tmem_ld16(taddr + 16 * h16, r);
-            tc::tmem_ld_wait();
-            if (m < g.M) {
-              const int cb = co0 + 16 * h16;
-              float* dst = g.out + (n_img * g.Cout + cb) * OHW + p;
-              const float* res = g.residual ? g.residual + (n_img * g.Cout + cb) * OHW + p : nullptr;
-#pragma unroll
-              for (int j = 0; j < 16; ++j) {
-                if (cb + j >= g.Cout) break;
-                float o = __uint_as_float(r[j]);
-                if (g.bias) o = __fadd_rn(o, g.bias[cb + j]);
-                if (g.act == kActAddRelu) o = __fadd_rn(o, res[(int64_t)j * OHW]);
-                dst[(int64_t)j * OHW] = activate(o, g.act);
-              }
-            }
-          }
-        }
-      }
+      store_tile<BN>(g, tmem_base, acc * BN, nt, quad, half * kStageCols, 2 * kStageCols, lane,
+                     stage_tile, vec_ok, bias_vec, LinearRows{(int64_t)mt * BM, g.M});
       tc::tc_fence_before();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&tempty[acc]);
@@ -602,6 +635,283 @@ __global__ void __launch_bounds__(kConvThreads, 1)
   tc::tc_fence_before();
   __syncthreads();
   if (warp == kMmaWarp) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+// --------------------------------------------------------- halo kernel ----
+//
+// Stride-1 convolutions over an NHWC input whose stored channel count C4 is a
+// multiple of 32, C_out <= 128. A tile is an 8-wide x 32-tall block of one
+// image's output pixels, split into an upper and a lower 8 x 16 block (one
+// 128-row accumulator each, row r = 8 y + x), times BN output channels.
+//
+// Per 32-channel block one TMA load brings the tile's input window,
+// (32 + KH - 1) x (8 + KW - 1) pixels of 128 bytes in the 128-byte swizzle
+// layout, zero-filled outside the image (the padding). Every tap's A operand
+// is a descriptor into that window: tap (kh, kw) of the upper block starts at
+// window row kh (8 + KW - 1) + kw (the lower block 16 window rows further),
+// and its 8-row groups (one output row each) lie (8 + KW - 1) rows apart: the
+// swizzle follows absolute shared addresses, so any 128-byte row may start a
+// group. Only BN x 32 weight tiles stream per tap, G taps per ring stage, and
+// both blocks read the same stage.
+//
+// Issue rate: an mbarrier wait costs ~100 cycles even when the phase has
+// completed, and the tensor pipe runs only ~2 MMAs ahead of one issuing
+// thread, so a single issuer idles an N = 64 or 128 pipe at every wait. Two
+// MMA warps (one per block, separate accumulators) keep it busy: while one
+// waits the other issues, and measured together they reach the pipe's full
+// rate. Each loop runs on its whole warp with one elected lane issuing, and
+// descriptors advance by addition only.
+//
+// 352 threads: warp 0 lane 0 issues the TMA loads; warps 1 and 2 (upper,
+// lower block) issue the MMAs, warp 1 owning TMEM; warps 3..6 drain the upper
+// accumulators and warps 7..10 the lower ones (shared epilogue, store_tile).
+constexpr int kHaloTW = 8, kHaloTH = 16;    // one accumulator block
+constexpr int kHaloMaxK = 4;                 // largest KH and KW
+constexpr uint32_t kHaloSlotBytes = 50176;  // (32 + 3) x (8 + 3) rows x 128 B, 1 KB multiple
+constexpr int kHaloSlots = 2;
+constexpr int kHaloThreads = 32 * (3 + kEpilogueWarps);
+
+template <int BN, int G, int STAGES>
+struct HaloCfg {
+  static constexpr uint32_t B_BYTES = BN * BK * 4;      // one tap's weight tile
+  static constexpr uint32_t STAGE_BYTES = G * B_BYTES;  // G taps per ring stage
+  static constexpr uint32_t HALO_OFF = STAGES * STAGE_BYTES;
+  static constexpr uint32_t EPI_OFF = HALO_OFF + kHaloSlots * kHaloSlotBytes;
+  static constexpr uint32_t BAR_OFF = EPI_OFF + kEpiBytes;
+  static constexpr uint32_t TMEM_COLS = 4 * BN;  // {upper, lower} x double buffer
+  static constexpr size_t SMEM = (size_t)BAR_OFF + 256 + 1024;
+};
+
+template <int BN, int G, int STAGES>
+__global__ void __launch_bounds__(kHaloThreads, 1)
+    conv_halo_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
+                     const ConvArgs g) {
+  using Cfg = HaloCfg<BN, G, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint8_t* halo = smem + Cfg::HALO_OFF;
+  float* epi = reinterpret_cast<float*>(smem + Cfg::EPI_OFF);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::BAR_OFF);
+  uint64_t* empty = full + STAGES;
+  uint64_t* hfull = empty + STAGES;
+  uint64_t* hempty = hfull + kHaloSlots;
+  uint64_t* tfull = hempty + kHaloSlots;  // [acc][block]
+  uint64_t* tempty = tfull + 4;           // [acc][block]
+  uint64_t* done = tempty + 4;            // [block]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 2);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int hw = kHaloTW + g.KW - 1, hh = 2 * kHaloTH + g.KH - 1;  // window extent in pixels
+  const int taps = g.KH * g.KW, cblocks = g.C4 / BK;
+  const int per_img = g.tiles_x * g.tiles_y;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      tc::mbar_init(&full[s], 1);
+      tc::mbar_init(&empty[s], 2);  // both MMA warps release a stage
+    }
+    for (int h = 0; h < kHaloSlots; ++h) {
+      tc::mbar_init(&hfull[h], 1);
+      tc::mbar_init(&hempty[h], 2);
+    }
+    for (int a = 0; a < 4; ++a) {
+      tc::mbar_init(&tfull[a], 1);
+      tc::mbar_init(&tempty[a], kEpilogueWarps / 2);
+    }
+    tc::mbar_init(&done[0], 1);
+    tc::mbar_init(&done[1], 1);
+    tc::fence_barrier_init();
+    tc::prefetch_tmap(&tmW);
+    tc::prefetch_tmap(&tmX);
+  }
+  if (warp == 1) {
+    tc::tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+    tc::tmem_relinquish();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- producer: input windows and weight tiles ----------------
+      const uint32_t halo_bytes = (uint32_t)(hw * hh) * 128;
+      int stage = 0, hs = 0;
+      uint32_t phase = 0, hphase = 0;
+      bool ok = true;
+      for (int64_t tile = blockIdx.x; tile < g.tiles && ok; tile += gridDim.x) {
+        const int64_t mt = tile / g.n_tiles;
+        const int nt = (int)(tile % g.n_tiles);
+        const int n = (int)(mt / per_img), rem = (int)(mt % per_img);
+        const int y0 = (rem / g.tiles_x) * 2 * kHaloTH, x0 = (rem % g.tiles_x) * kHaloTW;
+        for (int cb = 0; cb < cblocks && ok; ++cb) {
+          if (!tc::mbar_wait(&hempty[hs], hphase ^ 1, g.err)) {
+            ok = false;
+            break;
+          }
+          tc::mbar_arrive_expect_tx(&hfull[hs], halo_bytes);
+          tc::tma_load_4d(halo + hs * kHaloSlotBytes, &tmX, &hfull[hs], cb * BK, x0 - g.pw,
+                          y0 - g.ph, n);
+          if (++hs == kHaloSlots) {
+            hs = 0;
+            hphase ^= 1;
+          }
+          for (int t0 = 0; t0 < taps; t0 += G) {
+            const int gt = taps - t0 < G ? taps - t0 : G;
+            if (!tc::mbar_wait(&empty[stage], phase ^ 1, g.err)) {
+              ok = false;
+              break;
+            }
+            tc::mbar_arrive_expect_tx(&full[stage], (uint32_t)gt * Cfg::B_BYTES);
+            for (int j = 0; j < gt; ++j)
+              tc::tma_load_2d(smem + stage * Cfg::STAGE_BYTES + j * Cfg::B_BYTES, &tmW, &full[stage],
+                              (t0 + j) * g.C4 + cb * BK, nt * BN);
+            if (++stage == STAGES) {
+              stage = 0;
+              phase ^= 1;
+            }
+          }
+        }
+      }
+      // Let the last issued loads land before the CTA can exit.
+      if (ok) {
+        for (int q = 0; q < STAGES; ++q) {
+          if (stage == 0) {
+            stage = STAGES;
+            phase ^= 1;
+          }
+          --stage;
+          tc::mbar_wait(&full[stage], phase, g.err);
+        }
+        for (int q = 0; q < kHaloSlots; ++q) {
+          if (hs == 0) {
+            hs = kHaloSlots;
+            hphase ^= 1;
+          }
+          --hs;
+          tc::mbar_wait(&hfull[hs], hphase, g.err);
+        }
+      }
+    }
+  } else if (warp <= 2) {
+    // ---------------- MMA issuers: warp 1 upper block, warp 2 lower block ----------------
+    const int blk = warp - 1;
+    constexpr uint32_t idesc = tc::idesc_tf32(BM, BN);
+    // Descriptor start addresses are in 16-byte units: adding (bytes >> 4)
+    // moves a descriptor (all shared addresses here are below 256 KB).
+    const uint64_t a_desc0 =
+        tc::desc_kmajor_sw128_sbo(tc::smem_u32(halo), (uint32_t)hw * 128) +
+        (uint32_t)(blk * kHaloTH * hw) * (128 >> 4);
+    const uint64_t b_desc0 = tc::desc_kmajor_sw128(tc::smem_u32(smem));
+    int stage = 0, hs = 0;
+    uint32_t phase = 0, hphase = 0;
+    int local = 0;
+    bool ok = true;
+    for (int64_t t = blockIdx.x; t < g.tiles && ok; t += gridDim.x, ++local) {
+      const int acc = local & 1;
+      const uint32_t aphase = (local >> 1) & 1;
+      if (!tc::mbar_wait_warp(&tempty[acc * 2 + blk], aphase ^ 1, g.err)) break;
+      tc::tc_fence_after();
+      const uint32_t d_tmem = tmem_base + (uint32_t)(acc * 2 + blk) * BN;
+      uint32_t accumulate = 0;  // the tile's first MMA overwrites the accumulator
+      for (int cb = 0; cb < cblocks && ok; ++cb) {
+        if (!tc::mbar_wait_warp(&hfull[hs], hphase, g.err)) {
+          ok = false;
+          break;
+        }
+        tc::tc_fence_after();
+        const uint64_t a_win = a_desc0 + (uint32_t)hs * (kHaloSlotBytes >> 4);
+        int kh = 0, kw = 0;
+        for (int t0 = 0; t0 < taps; t0 += G) {
+          const int gt = taps - t0 < G ? taps - t0 : G;
+          if (!tc::mbar_wait_warp(&full[stage], phase, g.err)) {
+            ok = false;
+            break;
+          }
+          tc::tc_fence_after();
+          const uint64_t b_stage = b_desc0 + (uint32_t)stage * (Cfg::STAGE_BYTES >> 4);
+          if (tc::elect_one()) {
+            int th = kh, tw = kw;
+            uint32_t accum = accumulate;
+#pragma unroll
+            for (int j = 0; j < G; ++j) {
+              if (j < gt) {
+                const uint64_t a = a_win + (uint32_t)(th * hw + tw) * (128 >> 4);
+                const uint64_t b = b_stage + (uint32_t)j * (Cfg::B_BYTES >> 4);
+#pragma unroll
+                for (int k = 0; k < BK / 8; ++k) {
+                  tc::mma_tf32(d_tmem, a + 2 * k, b + 2 * k, idesc, accum);
+                  accum = 1;
+                }
+                if (++tw == g.KW) {
+                  tw = 0;
+                  ++th;
+                }
+              }
+            }
+            tc::mma_commit(&empty[stage]);
+          }
+          __syncwarp();
+          accumulate = 1;
+          for (int j = 0; j < gt; ++j) {
+            if (++kw == g.KW) {
+              kw = 0;
+              ++kh;
+            }
+          }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        // The window is free once both blocks' taps that read it completed.
+        if (tc::elect_one()) tc::mma_commit(&hempty[hs]);
+        __syncwarp();
+        if (++hs == kHaloSlots) {
+          hs = 0;
+          hphase ^= 1;
+        }
+      }
+      if (tc::elect_one()) tc::mma_commit(&tfull[acc * 2 + blk]);
+      __syncwarp();
+    }
+    if (tc::elect_one()) tc::mma_commit(&done[blk]);
+    __syncwarp();
+    tc::mbar_wait_warp(&done[blk], 0, g.err);
+  } else {
+    // ---------------- epilogue: warps 3..6 upper, 7..10 lower block ----------------
+    const int e = warp - 3, blk = e >> 2, quad = warp & 3;
+    float* stage_tile = epi + e * 32 * (kStageCols + 1);
+    const bool vec_ok = (g.Cout % 4 == 0) && ((((uintptr_t)g.out) & 15) == 0) &&
+                        (!g.residual || ((((uintptr_t)g.residual) & 15) == 0));
+    const bool bias_vec = g.bias && ((((uintptr_t)g.bias) & 15) == 0);
+    const int64_t OHW = (int64_t)g.OH * g.OW;
+    int local = 0;
+    for (int64_t t = blockIdx.x; t < g.tiles; t += gridDim.x, ++local) {
+      const int64_t mt = t / g.n_tiles;
+      const int nt = (int)(t % g.n_tiles);
+      const int n = (int)(mt / per_img), rem = (int)(mt % per_img);
+      const int acc = local & 1;
+      const uint32_t aphase = (local >> 1) & 1;
+      if (!tc::mbar_wait(&tfull[acc * 2 + blk], aphase, g.err)) break;
+      tc::tc_fence_after();
+      store_tile<BN>(g, tmem_base, (uint32_t)(acc * 2 + blk) * BN, nt, quad, 0, kStageCols, lane,
+                     stage_tile, vec_ok, bias_vec,
+                     BlockRows{(int64_t)n * OHW, (rem / g.tiles_x) * 2 * kHaloTH + blk * kHaloTH,
+                               (rem % g.tiles_x) * kHaloTW, g.OH, g.OW});
+      tc::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&tempty[acc * 2 + blk]);
+    }
+  }
+
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
     tc::tc_fence_after();
     tc::tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
   }
@@ -803,6 +1113,59 @@ bool launch_conv(ConvArgs g, const float* w0, const float* w1, const char* op) {
   return check_launch(op);
 }
 
+template <int BN, int G, int STAGES>
+bool launch_halo(ConvArgs g, const float* w0, const char* op) {
+  using Cfg = HaloCfg<BN, G, STAGES>;
+  const int Kpad = g.kblocks * BK;
+  CUtensorMap tw, tx;
+  const uint64_t dims[2] = {(uint64_t)Kpad, (uint64_t)g.Cout};
+  const uint64_t strides[1] = {(uint64_t)Kpad * 4};
+  const uint32_t box[2] = {BK, BN};
+  if (!encode_tmap_f32(&tw, w0, 2, dims, strides, box, nullptr, op)) return false;
+  // Input windows: 32 channels x (8 + KW - 1) x (16 + KH - 1) pixels of one image.
+  const uint64_t xd[4] = {(uint64_t)g.C4, (uint64_t)g.W, (uint64_t)g.H, (uint64_t)g.N};
+  const uint64_t xs[3] = {(uint64_t)g.C4 * 4, (uint64_t)g.W * g.C4 * 4,
+                          (uint64_t)g.H * g.W * g.C4 * 4};
+  const uint32_t xbox[4] = {BK, (uint32_t)(kHaloTW + g.KW - 1), (uint32_t)(2 * kHaloTH + g.KH - 1),
+                            1};
+  if (!encode_tmap_f32(&tx, g.x_hi, 4, xd, xs, xbox, nullptr, op)) return false;
+  g.tiles_x = (int)cdiv(g.OW, kHaloTW);
+  g.tiles_y = (int)cdiv(g.OH, 2 * kHaloTH);
+  g.m_tiles = g.N * g.tiles_x * g.tiles_y;
+  g.n_tiles = (int)cdiv(g.Cout, BN);
+  g.tiles = (int64_t)g.m_tiles * g.n_tiles;
+  auto kern = conv_halo_kernel<BN, G, STAGES>;
+  static bool attr_set[64] = {};
+  if (!attr_set[ctx().device]) {
+    if (!check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)Cfg::SMEM),
+                    op, "cudaFuncSetAttribute"))
+      return false;
+    attr_set[ctx().device] = true;
+  }
+  const int grid = (int)(g.tiles < sm_count() ? g.tiles : sm_count());
+  kern<<<grid, kHaloThreads, Cfg::SMEM, ctx().stream>>>(tw, tx, g);
+  return check_launch(op);
+}
+
+// Whether the halo kernel serves a call: stride 1, windows of at most 4 x 4,
+// 32-channel blocks, C_out <= 128, TF32, and 8 x 32 output tiles that waste
+// at most ~35% of their rows on the image's ragged edge.
+// NNC_CUDA_CONV_HALO=0 in the environment turns the path off (the im2col
+// kernel then serves these calls).
+bool halo_eligible(int C4, int Cout, int KH, int KW, int sh, int sw, int ph, int pw, int OH, int OW,
+                   bool split) {
+  static const bool enabled = [] {
+    const char* e = getenv("NNC_CUDA_CONV_HALO");
+    return !(e && e[0] == '0');
+  }();
+  if (!enabled || split || sh != 1 || sw != 1 || C4 % BK != 0 || Cout > 128) return false;
+  if (KH > kHaloMaxK || KW > kHaloMaxK || ph < 0 || pw < 0 || ph >= KH || pw >= KW) return false;
+  const int64_t covered =
+      cdiv((int64_t)OW, kHaloTW) * kHaloTW * cdiv((int64_t)OH, 2 * kHaloTH) * 2 * kHaloTH;
+  return covered * 100 <= (int64_t)OH * OW * 135;
+}
+
 bool conv_f32(const Tensor* t, const char* op, const char* name) {
   if (!valid_tensor(t, op, name)) return false;
   if (elem_type(t) != NNC_DTYPE_FLOAT32) {
@@ -972,6 +1335,8 @@ void conv_impl(Tensor* input, Tensor* weight, Tensor* bias, Tensor* residual, Te
     if (square && lower >= -64 && upper_h >= -64 && upper_h <= 63 && sh <= 8 &&
         OH > 0 && OW > 0 && aligned16(x_hi) && (!x_lo || aligned16(x_lo)))
       g.mode = (C4 % 32 == 0) ? kIm2col128 : kIm2col16;
+    if (aligned16(x_hi) && halo_eligible(C4, Cout, KH, KW, sh, sw, ph, pw, OH, OW, split))
+      g.mode = kHalo;
   }
   if (is_nhwc(input)) {
     g.xs_n = (int64_t)H * W * C;
@@ -1009,7 +1374,12 @@ void conv_impl(Tensor* input, Tensor* weight, Tensor* bias, Tensor* residual, Te
   g.act = act;
   g.err = device_error_word();
 
-  if (!split) {
+  if (g.mode == kHalo) {
+    if (Cout > 64)
+      launch_halo<128, 1, 4>(g, w0, op);
+    else
+      launch_halo<64, 3, 3>(g, w0, op);
+  } else if (!split) {
     if (Cout > 128)
       launch_conv<256, 1, 4>(g, w0, nullptr, op);
     else if (Cout > 64)

@@ -153,6 +153,23 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
       : "memory");
 }
 
+// One lane of the (fully active) warp returns true: the MMA loops run on the
+// whole warp so their operands stay warp-uniform, and the elected lane issues.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b32 r;\n\t"
+      "elect.sync r|p, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
+}
+// mbar_wait by every lane of a warp; false on every lane if any lane timed out.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, int* err) {
+  const bool ok = mbar_wait(bar, parity, err);
+  return __all_sync(0xffffffffu, ok);
+}
+
 // 32 lanes x 32 bit, 16 consecutive columns: thread i of the warp receives
 // TMEM lane (addr.lane + i), columns [addr.col, addr.col + 16).
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
@@ -179,6 +196,20 @@ __device__ __forceinline__ uint64_t desc_kmajor_sw128(uint32_t smem_addr) {
   d |= (uint64_t)((smem_addr & 0x3FFFFu) >> 4);
   d |= (uint64_t)1u << 16;
   d |= (uint64_t)(1024u >> 4) << 32;
+  d |= (uint64_t)1u << 46;
+  d |= (uint64_t)2u << 61;
+  return d;
+}
+
+// The same layout with a caller-chosen distance between 8-row groups (a
+// multiple of 128 bytes): rows of a group are consecutive 128-byte rows, and
+// the swizzle phase follows the absolute address, so a group may start at any
+// 128-byte row (measured on sm_100a with the base-offset field left 0).
+__device__ __forceinline__ uint64_t desc_kmajor_sw128_sbo(uint32_t smem_addr, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_addr & 0x3FFFFu) >> 4);
+  d |= (uint64_t)1u << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
   d |= (uint64_t)1u << 46;
   d |= (uint64_t)2u << 61;
   return d;

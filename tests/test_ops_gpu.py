@@ -161,6 +161,46 @@ def test_conv_resnet_layers_vs_oracle(cuda_lib, prec, cfg):
     C.assert_close(got_nhwc, want, C.TC_RTOL[prec], f"conv{cfg}[nhwc]")
 
 
+# Stride-1 windows over 32-channel blocks take the halo-tile kernel in TF32
+# mode (and the im2col kernel in 3xTF32 mode): ragged 8 x 16 output blocks,
+# partial C_out tiles (48, 200), C_out not a multiple of 4 (scalar epilogue),
+# three channel blocks, a 4 x 4 window, a 1 x 1 window.
+HALO_CASES = [
+    # n, c, h, w, co, k, p, op
+    (2, 32, 30, 30, 48, 3, 1, "nnc_conv_add_relu"),
+    (1, 96, 24, 40, 64, 3, 1, "nnc_conv_add_relu"),
+    (2, 64, 32, 32, 200, 3, 1, "nnc_conv_add_relu"),
+    (1, 32, 30, 30, 64, 4, 2, "nnc_conv_add_relu"),
+    (2, 96, 28, 28, 128, 1, 0, "nnc_conv_relu"),
+    (2, 32, 30, 30, 30, 3, 1, "nnc_conv"),
+]
+
+
+@pytest.mark.parametrize("prec", [0, 1])
+@pytest.mark.parametrize("cfg", HALO_CASES, ids=lambda c: "x".join(str(v) for v in c[:7]))
+def test_conv_stride1_blocks_vs_oracle(cuda_lib, prec, cfg):
+    n, c, h, w, co, k, p, op = cfg
+    r = np.random.default_rng(7 + sum(cfg[:7]))
+    oh, ow = C.conv_out(h, k, 1, p), C.conv_out(w, k, 1, p)
+    arrays = {"x": r.standard_normal((n, c, h, w)).astype(np.float32),
+              "w": (r.standard_normal((co, c, k, k)) * np.sqrt(2.0 / (c * k * k))).astype(np.float32),
+              "b": r.uniform(-0.01, 0.01, co).astype(np.float32),
+              "res": r.standard_normal((n, co, oh, ow)).astype(np.float32)}
+    args = [C._t("x"), C._t("w"), C._t("b")]
+    nhwc = {"x", "out"}
+    if op == "nnc_conv_add_relu":
+        args.append(C._t("res"))
+        nhwc.add("res")
+    args += [C._o("out", (n, co, oh, ow)), C._i(k), C._i(k), C._i(1), C._i(1), C._i(p), C._i(p)]
+    case = {"name": "c", "op": op, "args": args}
+    cuda_lib.nnc_cuda_set_precision(prec)
+    want = C.run_host(_oracle(), case, arrays)["out"]
+    got = C.run_cuda(cuda_lib, case, arrays)["out"]
+    C.assert_close(got, want, C.TC_RTOL[prec], f"conv{cfg}")
+    got_nhwc = C.run_cuda(cuda_lib, case, arrays, nhwc=nhwc)["out"]
+    C.assert_close(got_nhwc, want, C.TC_RTOL[prec], f"conv{cfg}[nhwc]")
+
+
 # ------------------------------------------------------------ validation --
 def test_invalid_shapes_set_status_without_launch(cuda_lib):
     import torch
