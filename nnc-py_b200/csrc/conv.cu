@@ -1041,6 +1041,67 @@ __global__ void __launch_bounds__(256) nhwc_repack_kernel(const float* __restric
 // How a weight of shape [Cout, Cin, KH, KW] is packed, decided by the shape
 // alone (so a weight prepacked once matches every later call): chunk mode
 // with channels padded to a multiple of 4, or element mode for tiny K.
+// Space-to-depth input for stride-2 convolutions with few channels: output
+// pixel (i, j) of [N][ceil(H/2)][ceil(W/2)][32] holds, in channel
+// q C + c (q = 2 dy + dx), input channel c at (2i + dy, 2j + dx) (zero past
+// the image), and zeros in channels 4C..31. Input strides in elements
+// (NCHW or NHWC).
+__global__ void __launch_bounds__(256) s2d_input_kernel(const float* __restrict__ x,
+                                                        float* __restrict__ out, int N, int C, int H,
+                                                        int W, int H2, int W2, int64_t xs_n,
+                                                        int64_t xs_c, int64_t xs_h, int64_t xs_w) {
+  const int64_t total = (int64_t)N * H2 * W2;
+  for (int64_t p = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; p < total;
+       p += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t n = p / ((int64_t)H2 * W2);
+    const int rem = (int)(p - n * H2 * W2);
+    const int i = rem / W2, j = rem - (rem / W2) * W2;
+    float4* dst = reinterpret_cast<float4*>(out + p * BK);
+#pragma unroll
+    for (int k4 = 0; k4 < BK / 4; ++k4) {
+      float v[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int cc = 4 * k4 + e, q = cc / C, c = cc - q * C;
+        const int y = 2 * i + (q >> 1), xx = 2 * j + (q & 1);
+        v[e] = (q < 4 && y < H && xx < W) ? x[n * xs_n + c * xs_c + y * xs_h + xx * xs_w] : 0.0f;
+      }
+      dst[k4] = make_float4(v[0], v[1], v[2], v[3]);
+    }
+  }
+}
+
+// Space-to-depth weights: [C_out][KH2][KW2][32] in the halo kernel's k order,
+// W'[co, kh2, kw2, q C + c] = W[co, c, 2 (kh2 - pad_h) + dy + ph,
+// 2 (kw2 - pad_w) + dx + pw] inside the original window, else zero. The
+// source is the OIHW weight, or a prepacked one (chunk or element k order).
+__global__ void __launch_bounds__(256) s2d_weight_kernel(const float* __restrict__ w,
+                                                         float* __restrict__ out, int Cout, int C,
+                                                         int KH, int KW, int ph, int pw, int KH2,
+                                                         int KW2, int pad_h, int pad_w, int src_mode,
+                                                         int src_c4, int src_kpad) {
+  const int64_t total = (int64_t)Cout * KH2 * KW2 * BK;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int cc = (int)(i % BK);
+    const int64_t t = i / BK;
+    const int kw2 = (int)(t % KW2), kh2 = (int)((t / KW2) % KH2);
+    const int co = (int)(t / ((int64_t)KW2 * KH2));
+    const int q = cc / C, c = cc - q * C;
+    const int kh = 2 * (kh2 - pad_h) + (q >> 1) + ph, kw = 2 * (kw2 - pad_w) + (q & 1) + pw;
+    float v = 0.0f;
+    if (q < 4 && kh >= 0 && kh < KH && kw >= 0 && kw < KW) {
+      if (src_mode == 0)  // OIHW
+        v = w[(((int64_t)co * C + c) * KH + kh) * KW + kw];
+      else if (src_mode == 1)  // prepacked, chunk order k = (kh KW + kw) C4 + c
+        v = w[(int64_t)co * src_kpad + (kh * KW + kw) * src_c4 + c];
+      else  // prepacked, element order k = (c KH + kh) KW + kw
+        v = w[(int64_t)co * src_kpad + (c * KH + kh) * KW + kw];
+    }
+    out[i] = v;
+  }
+}
+
 struct WeightLayout {
   int element;
   int C4;    // chunk mode: channels per tap as stored (multiple of 4)
@@ -1208,6 +1269,26 @@ bool static_scratch_on_device(StaticScratch* out, const char* op) {
   return true;
 }
 
+// Stride-2 convolutions over at most 8 channels run as stride-1
+// convolutions over the space-to-depth input (4 C channels, padded to 32):
+// tap kh of the original window maps to s2d tap kh2 = (kh - ph - dy) / 2 +
+// pad_h for the pixel-row parity dy. Returns false when the s2d window would
+// exceed the halo kernel's 4 x 4.
+struct S2dPlan {
+  int KH2, KW2, pad_h, pad_w;
+};
+bool s2d_plan(int C, int KH, int KW, int sh, int sw, int ph, int pw, S2dPlan* p) {
+  if (sh != 2 || sw != 2 || C < 1 || 4 * C > BK || ph < 0 || pw < 0) return false;
+  auto floor_div2 = [](int a) { return a >= 0 ? a / 2 : -((-a + 1) / 2); };
+  const int a_min_h = -((ph + 1) / 2), a_max_h = floor_div2(KH - 1 - ph);
+  const int a_min_w = -((pw + 1) / 2), a_max_w = floor_div2(KW - 1 - pw);
+  p->KH2 = a_max_h - a_min_h + 1;
+  p->KW2 = a_max_w - a_min_w + 1;
+  p->pad_h = -a_min_h;
+  p->pad_w = -a_min_w;
+  return p->KH2 >= 1 && p->KW2 >= 1 && p->KH2 <= kHaloMaxK && p->KW2 <= kHaloMaxK;
+}
+
 // fixed == nullptr: scratch comes from the runtime workspace (which may grow
 // with cudaMallocAsync); otherwise from *fixed, and a call that needs more
 // than it holds is rejected before any work is queued.
@@ -1256,6 +1337,62 @@ void conv_impl(Tensor* input, Tensor* weight, Tensor* bias, Tensor* residual, Te
   const int C4 = wl.C4;
   const int Kpad = wl.Kpad;
   const bool packed = (tag_of(weight) & NNC_CUDA_TAG_PACKED_CONV) != 0;
+
+  // Stride-2 convolutions over few channels: space-to-depth, then the halo
+  // kernel (stride 1, 32 channels). Falls through to the general path when
+  // the rewritten call is not eligible or its scratch exceeds a fixed scratch.
+  S2dPlan s2d;
+  if (!split && s2d_plan(C, KH, KW, sh, sw, ph, pw, &s2d) &&
+      halo_eligible(BK, Cout, s2d.KH2, s2d.KW2, 1, 1, s2d.pad_h, s2d.pad_w, OH, OW, split)) {
+    const int H2 = (H + 1) / 2, W2 = (W + 1) / 2;
+    const int64_t x2 = (int64_t)N * H2 * W2 * BK, w2 = (int64_t)Cout * s2d.KH2 * s2d.KW2 * BK;
+    const size_t need2 = (size_t)((x2 + 63) / 64 * 64 + w2) * 4 + 256;
+    if (!fixed || need2 <= fixed->bytes) {
+      float* ws2 = fixed ? fixed->ptr : (float*)workspace(need2, op);
+      if (!ws2) return;
+      float* xs2 = ws2;
+      float* wts2 = ws2 + (x2 + 63) / 64 * 64;
+      const bool in_nhwc = is_nhwc(input);
+      s2d_input_kernel<<<grid_for(x2 / BK, 256, 8), 256, 0, ctx().stream>>>(
+          (const float*)input->data, xs2, N, C, H, W, H2, W2, (int64_t)H * W * C,
+          in_nhwc ? 1 : (int64_t)H * W, in_nhwc ? (int64_t)W * C : W, in_nhwc ? C : 1);
+      if (!check_launch(op)) return;
+      const int src_mode = packed ? (wl.element ? 2 : 1) : 0;
+      s2d_weight_kernel<<<grid_for(w2, 256, 8), 256, 0, ctx().stream>>>(
+          (const float*)weight->data, wts2, Cout, C, KH, KW, ph, pw, s2d.KH2, s2d.KW2, s2d.pad_h,
+          s2d.pad_w, src_mode, wl.C4, wl.Kpad);
+      if (!check_launch(op)) return;
+      ConvArgs g{};
+      g.mode = kHalo;
+      g.N = N;
+      g.H = H2;
+      g.W = W2;
+      g.C4 = BK;
+      g.OH = OH;
+      g.OW = OW;
+      g.Cout = Cout;
+      g.KH = s2d.KH2;
+      g.KW = s2d.KW2;
+      g.sh = g.sw = 1;
+      g.ph = s2d.pad_h;
+      g.pw = s2d.pad_w;
+      g.K = s2d.KH2 * s2d.KW2 * BK;
+      g.kblocks = g.K / BK;
+      g.M = M;
+      g.x_hi = xs2;
+      g.bias = bias ? (const float*)bias->data : nullptr;
+      g.residual = residual ? (const float*)residual->data : nullptr;
+      g.out = (float*)output->data;
+      g.out_nhwc = is_nhwc(output) ? 1 : 0;
+      g.act = act;
+      g.err = device_error_word();
+      if (Cout > 64)
+        launch_halo<128, 1, 4>(g, wts2, op);
+      else
+        launch_halo<64, 3, 3>(g, wts2, op);
+      return;
+    }
+  }
 
   // Scratch: input planes when the input cannot be read in place (chunk
   // mode needs NHWC with C a multiple of 32; 3xTF32 needs hi/lo planes), and

@@ -201,6 +201,59 @@ def test_conv_stride1_blocks_vs_oracle(cuda_lib, prec, cfg):
     C.assert_close(got_nhwc, want, C.TC_RTOL[prec], f"conv{cfg}[nhwc]")
 
 
+# Stride-2 windows over at most 8 channels run as stride-1 windows over a
+# space-to-depth copy of the input (TF32 mode): 7x7 p3 (the ResNet stem), odd
+# extents, one channel, a 3x3 window whose prepacked weight is in element
+# order, 8 channels, a 1x1 window; raw and prepacked weights, NCHW and NHWC.
+S2D_CASES = [
+    # n, c, h, w, co, k, p, op
+    (2, 3, 64, 64, 64, 7, 3, "nnc_conv_relu"),
+    (1, 3, 61, 63, 48, 7, 3, "nnc_conv_add_relu"),
+    (2, 1, 64, 64, 32, 5, 2, "nnc_conv"),
+    (2, 3, 64, 63, 64, 3, 1, "nnc_conv_add_relu"),
+    (1, 8, 64, 64, 96, 3, 1, "nnc_conv_relu"),
+    (2, 4, 64, 64, 64, 1, 0, "nnc_conv"),
+    (1, 3, 30, 30, 64, 7, 3, "nnc_conv_relu"),  # 15 x 15 output: the general path
+]
+
+
+@pytest.mark.parametrize("prec", [0, 1])
+@pytest.mark.parametrize("cfg", S2D_CASES, ids=lambda c: "x".join(str(v) for v in c[:7]))
+def test_conv_stride2_few_channels_vs_oracle(cuda_lib, prec, cfg):
+    import torch
+
+    from nnc_cuda import tensor as T
+
+    n, c, h, w, co, k, p, op = cfg
+    r = np.random.default_rng(11 + sum(cfg[:7]))
+    oh, ow = C.conv_out(h, k, 2, p), C.conv_out(w, k, 2, p)
+    arrays = {"x": r.standard_normal((n, c, h, w)).astype(np.float32),
+              "w": (r.standard_normal((co, c, k, k)) * np.sqrt(2.0 / (c * k * k))).astype(np.float32),
+              "b": r.uniform(-0.01, 0.01, co).astype(np.float32),
+              "res": r.standard_normal((n, co, oh, ow)).astype(np.float32)}
+    args = [C._t("x"), C._t("w"), C._t("b")]
+    nhwc = {"x", "out"}
+    if op == "nnc_conv_add_relu":
+        args.append(C._t("res"))
+        nhwc.add("res")
+    args += [C._o("out", (n, co, oh, ow)), C._i(k), C._i(k), C._i(2), C._i(2), C._i(p), C._i(p)]
+    case = {"name": "c", "op": op, "args": args}
+    cuda_lib.nnc_cuda_set_precision(prec)
+    want = C.run_host(_oracle(), case, arrays)["out"]
+    got = C.run_cuda(cuda_lib, case, arrays)["out"]
+    C.assert_close(got, want, C.TC_RTOL[prec], f"conv{cfg}")
+    got_nhwc = C.run_cuda(cuda_lib, case, arrays, nhwc=nhwc)["out"]
+    C.assert_close(got_nhwc, want, C.TC_RTOL[prec], f"conv{cfg}[nhwc]")
+    # Prepacked weight (the cuda target's constants), NCHW tensors.
+    wt = torch.from_numpy(arrays["w"]).cuda()
+    wref = T.from_torch(wt)
+    nbytes = cuda_lib.nnc_cuda_prepacked_conv_weight_bytes(wref.ptr)
+    packed = torch.empty(nbytes // 4, dtype=torch.float32, device="cuda")
+    assert cuda_lib.nnc_cuda_prepack_conv_weight(wref.ptr, ctypes.c_void_p(packed.data_ptr()), nbytes) == 0
+    got_p = _run_with_weight(cuda_lib, case, arrays, "w", wref)["out"]
+    C.assert_close(got_p, want, C.TC_RTOL[prec], f"conv{cfg}[prepacked]")
+
+
 # ------------------------------------------------------------ validation --
 def test_invalid_shapes_set_status_without_launch(cuda_lib):
     import torch
