@@ -202,33 +202,52 @@ __device__ __forceinline__ void store_tile(const ConvArgs& g, uint32_t tmem_base
           bv.w = co + 3 < g.Cout ? g.bias[co + 3] : 0.f;
         }
       }
+      if (col_ok) {
+        // Vector path, unrolled (rv stays in registers); the activation is
+        // decided once per chunk so the body stays short.
+        const bool add = g.act == kActAddRelu;
+        const bool relu = add || g.act == kActRelu;
+        const bool sig = g.act == kActSigmoid;
 #pragma unroll
-      for (int it = 0; it < 8; ++it) {
-        const int rr = (lane >> 3) + 4 * it;
-        const int64_t m = rows(quad * 32 + rr);
-        if (m < 0) continue;
-        const float* srow = stage_tile + rr * (kStageCols + 1) + cl;
-        float4 o = make_float4(__fadd_rn(srow[0], bv.x), __fadd_rn(srow[1], bv.y),
-                               __fadd_rn(srow[2], bv.z), __fadd_rn(srow[3], bv.w));
-        float* dst = g.out + m * g.Cout + co;
-        if (col_ok) {
-          if (g.act == kActAddRelu) {
+        for (int it = 0; it < 8; ++it) {
+          const int rr = (lane >> 3) + 4 * it;
+          const int64_t m = rows(quad * 32 + rr);
+          if (m < 0) continue;
+          const float* srow = stage_tile + rr * (kStageCols + 1) + cl;
+          float4 o = make_float4(__fadd_rn(srow[0], bv.x), __fadd_rn(srow[1], bv.y),
+                                 __fadd_rn(srow[2], bv.z), __fadd_rn(srow[3], bv.w));
+          if (add) {
             o.x = __fadd_rn(o.x, rv[it].x);
             o.y = __fadd_rn(o.y, rv[it].y);
             o.z = __fadd_rn(o.z, rv[it].z);
             o.w = __fadd_rn(o.w, rv[it].w);
           }
-          o.x = activate(o.x, g.act);
-          o.y = activate(o.y, g.act);
-          o.z = activate(o.z, g.act);
-          o.w = activate(o.w, g.act);
-          *reinterpret_cast<float4*>(dst) = o;
-        } else {
-          const float ov[4] = {o.x, o.y, o.z, o.w};
+          if (relu) {
+            o.x = o.x > 0.0f ? o.x : 0.0f;
+            o.y = o.y > 0.0f ? o.y : 0.0f;
+            o.z = o.z > 0.0f ? o.z : 0.0f;
+            o.w = o.w > 0.0f ? o.w : 0.0f;
+          } else if (sig) {
+            o.x = activate(o.x, kActSigmoid);
+            o.y = activate(o.y, kActSigmoid);
+            o.z = activate(o.z, kActSigmoid);
+            o.w = activate(o.w, kActSigmoid);
+          }
+          *reinterpret_cast<float4*>(g.out + m * g.Cout + co) = o;
+        }
+      } else {
+        // Per-element path: C_out % 4 != 0, unaligned bases, ragged last columns.
+#pragma unroll 1
+        for (int it = 0; it < 8; ++it) {
+          const int rr = (lane >> 3) + 4 * it;
+          const int64_t m = rows(quad * 32 + rr);
+          if (m < 0) continue;
+          const float* srow = stage_tile + rr * (kStageCols + 1) + cl;
+          const float bq[4] = {bv.x, bv.y, bv.z, bv.w};
           for (int q = 0; q < 4 && co + q < g.Cout; ++q) {
-            float v = ov[q];
+            float v = __fadd_rn(srow[q], bq[q]);
             if (g.act == kActAddRelu) v = __fadd_rn(v, g.residual[m * g.Cout + co + q]);
-            dst[q] = activate(v, g.act);
+            g.out[m * g.Cout + co + q] = activate(v, g.act);
           }
         }
       }
@@ -668,28 +687,32 @@ __global__ void __launch_bounds__(kConvThreads, 1)
 // 352 threads: warp 0 lane 0 issues the TMA loads; warps 1 and 2 (upper,
 // lower block) issue the MMAs, warp 1 owning TMEM; warps 3..6 drain the upper
 // accumulators and warps 7..10 the lower ones (shared epilogue, store_tile).
-constexpr int kHaloTW = 8, kHaloTH = 16;    // one accumulator block
-constexpr int kHaloMaxK = 4;                 // largest KH and KW
-constexpr uint32_t kHaloSlotBytes = 50176;  // (32 + 3) x (8 + 3) rows x 128 B, 1 KB multiple
+constexpr int kHaloTW = 8, kHaloTH = 16;  // one accumulator block
+constexpr int kHaloMaxK = 4;               // largest KH and KW
 constexpr int kHaloSlots = 2;
 constexpr int kHaloThreads = 32 * (3 + kEpilogueWarps);
 
-template <int BN, int G, int STAGES>
+// CB: channels per window row, 32 (128-byte rows, 128-byte swizzle) or 16
+// (64-byte rows, 64-byte swizzle: the space-to-depth stem's 12 channels).
+template <int BN, int G, int STAGES, int CB>
 struct HaloCfg {
-  static constexpr uint32_t B_BYTES = BN * BK * 4;      // one tap's weight tile
+  static constexpr int ROW = CB * 4;                    // bytes per window row
+  static constexpr uint32_t SLOT_BYTES = (2 * kHaloTH + kHaloMaxK - 1) *
+                                             (kHaloTW + kHaloMaxK - 1) * ROW / 1024 * 1024 + 1024;
+  static constexpr uint32_t B_BYTES = BN * CB * 4;      // one tap's weight tile
   static constexpr uint32_t STAGE_BYTES = G * B_BYTES;  // G taps per ring stage
   static constexpr uint32_t HALO_OFF = STAGES * STAGE_BYTES;
-  static constexpr uint32_t EPI_OFF = HALO_OFF + kHaloSlots * kHaloSlotBytes;
+  static constexpr uint32_t EPI_OFF = HALO_OFF + kHaloSlots * SLOT_BYTES;
   static constexpr uint32_t BAR_OFF = EPI_OFF + kEpiBytes;
   static constexpr uint32_t TMEM_COLS = 4 * BN;  // {upper, lower} x double buffer
   static constexpr size_t SMEM = (size_t)BAR_OFF + 256 + 1024;
 };
 
-template <int BN, int G, int STAGES>
+template <int BN, int G, int STAGES, int CB>
 __global__ void __launch_bounds__(kHaloThreads, 1)
     conv_halo_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
                      const ConvArgs g) {
-  using Cfg = HaloCfg<BN, G, STAGES>;
+  using Cfg = HaloCfg<BN, G, STAGES, CB>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   uint8_t* halo = smem + Cfg::HALO_OFF;
@@ -705,7 +728,7 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int hw = kHaloTW + g.KW - 1, hh = 2 * kHaloTH + g.KH - 1;  // window extent in pixels
-  const int taps = g.KH * g.KW, cblocks = g.C4 / BK;
+  const int taps = g.KH * g.KW, cblocks = g.C4 / CB;
   const int per_img = g.tiles_x * g.tiles_y;
 
   if (threadIdx.x == 0) {
@@ -739,7 +762,7 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
   if (warp == 0) {
     if (lane == 0) {
       // ---------------- producer: input windows and weight tiles ----------------
-      const uint32_t halo_bytes = (uint32_t)(hw * hh) * 128;
+      const uint32_t halo_bytes = (uint32_t)(hw * hh) * Cfg::ROW;
       int stage = 0, hs = 0;
       uint32_t phase = 0, hphase = 0;
       bool ok = true;
@@ -754,7 +777,7 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
             break;
           }
           tc::mbar_arrive_expect_tx(&hfull[hs], halo_bytes);
-          tc::tma_load_4d(halo + hs * kHaloSlotBytes, &tmX, &hfull[hs], cb * BK, x0 - g.pw,
+          tc::tma_load_4d(halo + hs * Cfg::SLOT_BYTES, &tmX, &hfull[hs], cb * CB, x0 - g.pw,
                           y0 - g.ph, n);
           if (++hs == kHaloSlots) {
             hs = 0;
@@ -769,7 +792,7 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
             tc::mbar_arrive_expect_tx(&full[stage], (uint32_t)gt * Cfg::B_BYTES);
             for (int j = 0; j < gt; ++j)
               tc::tma_load_2d(smem + stage * Cfg::STAGE_BYTES + j * Cfg::B_BYTES, &tmW, &full[stage],
-                              (t0 + j) * g.C4 + cb * BK, nt * BN);
+                              (t0 + j) * g.C4 + cb * CB, nt * BN);
             if (++stage == STAGES) {
               stage = 0;
               phase ^= 1;
@@ -804,9 +827,9 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
     // Descriptor start addresses are in 16-byte units: adding (bytes >> 4)
     // moves a descriptor (all shared addresses here are below 256 KB).
     const uint64_t a_desc0 =
-        tc::desc_kmajor_sw128_sbo(tc::smem_u32(halo), (uint32_t)hw * 128) +
-        (uint32_t)(blk * kHaloTH * hw) * (128 >> 4);
-    const uint64_t b_desc0 = tc::desc_kmajor_sw128(tc::smem_u32(smem));
+        tc::desc_kmajor_swz(tc::smem_u32(halo), (uint32_t)hw * Cfg::ROW, Cfg::ROW) +
+        (uint32_t)(blk * kHaloTH * hw) * (Cfg::ROW >> 4);
+    const uint64_t b_desc0 = tc::desc_kmajor_swz(tc::smem_u32(smem), 8 * Cfg::ROW, Cfg::ROW);
     int stage = 0, hs = 0;
     uint32_t phase = 0, hphase = 0;
     int local = 0;
@@ -824,7 +847,7 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
           break;
         }
         tc::tc_fence_after();
-        const uint64_t a_win = a_desc0 + (uint32_t)hs * (kHaloSlotBytes >> 4);
+        const uint64_t a_win = a_desc0 + (uint32_t)hs * (Cfg::SLOT_BYTES >> 4);
         int kh = 0, kw = 0;
         for (int t0 = 0; t0 < taps; t0 += G) {
           const int gt = taps - t0 < G ? taps - t0 : G;
@@ -840,10 +863,10 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
 #pragma unroll
             for (int j = 0; j < G; ++j) {
               if (j < gt) {
-                const uint64_t a = a_win + (uint32_t)(th * hw + tw) * (128 >> 4);
+                const uint64_t a = a_win + (uint32_t)(th * hw + tw) * (Cfg::ROW >> 4);
                 const uint64_t b = b_stage + (uint32_t)j * (Cfg::B_BYTES >> 4);
 #pragma unroll
-                for (int k = 0; k < BK / 8; ++k) {
+                for (int k = 0; k < CB / 8; ++k) {
                   tc::mma_tf32(d_tmem, a + 2 * k, b + 2 * k, idesc, accum);
                   accum = 1;
                 }
@@ -1042,10 +1065,11 @@ __global__ void __launch_bounds__(256) nhwc_repack_kernel(const float* __restric
 // alone (so a weight prepacked once matches every later call): chunk mode
 // with channels padded to a multiple of 4, or element mode for tiny K.
 // Space-to-depth input for stride-2 convolutions with few channels: output
-// pixel (i, j) of [N][ceil(H/2)][ceil(W/2)][32] holds, in channel
-// q C + c (q = 2 dy + dx), input channel c at (2i + dy, 2j + dx) (zero past
-// the image), and zeros in channels 4C..31. Input strides in elements
-// (NCHW or NHWC).
+// pixel (i, j) of [N][ceil(H/2)][ceil(W/2)][C2] (C2 = 16 or 32) holds, in
+// channel q C + c (q = 2 dy + dx), input channel c at (2i + dy, 2j + dx)
+// (zero past the image), and zeros in channels 4C..C2-1. Input strides in
+// elements (NCHW or NHWC).
+template <int C2>
 __global__ void __launch_bounds__(256) s2d_input_kernel(const float* __restrict__ x,
                                                         float* __restrict__ out, int N, int C, int H,
                                                         int W, int H2, int W2, int64_t xs_n,
@@ -1056,9 +1080,9 @@ __global__ void __launch_bounds__(256) s2d_input_kernel(const float* __restrict_
     const int64_t n = p / ((int64_t)H2 * W2);
     const int rem = (int)(p - n * H2 * W2);
     const int i = rem / W2, j = rem - (rem / W2) * W2;
-    float4* dst = reinterpret_cast<float4*>(out + p * BK);
+    float4* dst = reinterpret_cast<float4*>(out + p * C2);
 #pragma unroll
-    for (int k4 = 0; k4 < BK / 4; ++k4) {
+    for (int k4 = 0; k4 < C2 / 4; ++k4) {
       float v[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
@@ -1071,7 +1095,7 @@ __global__ void __launch_bounds__(256) s2d_input_kernel(const float* __restrict_
   }
 }
 
-// Space-to-depth weights: [C_out][KH2][KW2][32] in the halo kernel's k order,
+// Space-to-depth weights: [C_out][KH2][KW2][C2] in the halo kernel's k order,
 // W'[co, kh2, kw2, q C + c] = W[co, c, 2 (kh2 - pad_h) + dy + ph,
 // 2 (kw2 - pad_w) + dx + pw] inside the original window, else zero. The
 // source is the OIHW weight, or a prepacked one (chunk or element k order).
@@ -1079,12 +1103,12 @@ __global__ void __launch_bounds__(256) s2d_weight_kernel(const float* __restrict
                                                          float* __restrict__ out, int Cout, int C,
                                                          int KH, int KW, int ph, int pw, int KH2,
                                                          int KW2, int pad_h, int pad_w, int src_mode,
-                                                         int src_c4, int src_kpad) {
-  const int64_t total = (int64_t)Cout * KH2 * KW2 * BK;
+                                                         int src_c4, int src_kpad, int C2) {
+  const int64_t total = (int64_t)Cout * KH2 * KW2 * C2;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
-    const int cc = (int)(i % BK);
-    const int64_t t = i / BK;
+    const int cc = (int)(i % C2);
+    const int64_t t = i / C2;
     const int kw2 = (int)(t % KW2), kh2 = (int)((t / KW2) % KH2);
     const int co = (int)(t / ((int64_t)KW2 * KH2));
     const int q = cc / C, c = cc - q * C;
@@ -1174,28 +1198,28 @@ bool launch_conv(ConvArgs g, const float* w0, const float* w1, const char* op) {
   return check_launch(op);
 }
 
-template <int BN, int G, int STAGES>
+template <int BN, int G, int STAGES, int CB>
 bool launch_halo(ConvArgs g, const float* w0, const char* op) {
-  using Cfg = HaloCfg<BN, G, STAGES>;
-  const int Kpad = g.kblocks * BK;
+  using Cfg = HaloCfg<BN, G, STAGES, CB>;
+  const int Kpad = g.K;  // taps x C4, a multiple of CB
   CUtensorMap tw, tx;
   const uint64_t dims[2] = {(uint64_t)Kpad, (uint64_t)g.Cout};
   const uint64_t strides[1] = {(uint64_t)Kpad * 4};
-  const uint32_t box[2] = {BK, BN};
-  if (!encode_tmap_f32(&tw, w0, 2, dims, strides, box, nullptr, op)) return false;
-  // Input windows: 32 channels x (8 + KW - 1) x (16 + KH - 1) pixels of one image.
+  const uint32_t box[2] = {CB, BN};
+  if (!encode_tmap_f32(&tw, w0, 2, dims, strides, box, nullptr, op, Cfg::ROW)) return false;
+  // Input windows: CB channels x (8 + KW - 1) x (32 + KH - 1) pixels of one image.
   const uint64_t xd[4] = {(uint64_t)g.C4, (uint64_t)g.W, (uint64_t)g.H, (uint64_t)g.N};
   const uint64_t xs[3] = {(uint64_t)g.C4 * 4, (uint64_t)g.W * g.C4 * 4,
                           (uint64_t)g.H * g.W * g.C4 * 4};
-  const uint32_t xbox[4] = {BK, (uint32_t)(kHaloTW + g.KW - 1), (uint32_t)(2 * kHaloTH + g.KH - 1),
+  const uint32_t xbox[4] = {CB, (uint32_t)(kHaloTW + g.KW - 1), (uint32_t)(2 * kHaloTH + g.KH - 1),
                             1};
-  if (!encode_tmap_f32(&tx, g.x_hi, 4, xd, xs, xbox, nullptr, op)) return false;
+  if (!encode_tmap_f32(&tx, g.x_hi, 4, xd, xs, xbox, nullptr, op, Cfg::ROW)) return false;
   g.tiles_x = (int)cdiv(g.OW, kHaloTW);
   g.tiles_y = (int)cdiv(g.OH, 2 * kHaloTH);
   g.m_tiles = g.N * g.tiles_x * g.tiles_y;
   g.n_tiles = (int)cdiv(g.Cout, BN);
   g.tiles = (int64_t)g.m_tiles * g.n_tiles;
-  auto kern = conv_halo_kernel<BN, G, STAGES>;
+  auto kern = conv_halo_kernel<BN, G, STAGES, CB>;
   static bool attr_set[64] = {};
   if (!attr_set[ctx().device]) {
     if (!check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1215,12 +1239,12 @@ bool launch_halo(ConvArgs g, const float* w0, const char* op) {
 // NNC_CUDA_CONV_HALO=0 in the environment turns the path off (the im2col
 // kernel then serves these calls).
 bool halo_eligible(int C4, int Cout, int KH, int KW, int sh, int sw, int ph, int pw, int OH, int OW,
-                   bool split) {
+                   bool split, int cb = BK) {
   static const bool enabled = [] {
     const char* e = getenv("NNC_CUDA_CONV_HALO");
     return !(e && e[0] == '0');
   }();
-  if (!enabled || split || sh != 1 || sw != 1 || C4 % BK != 0 || Cout > 128) return false;
+  if (!enabled || split || sh != 1 || sw != 1 || C4 % cb != 0 || Cout > 128) return false;
   if (KH > kHaloMaxK || KW > kHaloMaxK || ph < 0 || pw < 0 || ph >= KH || pw >= KW) return false;
   const int64_t covered =
       cdiv((int64_t)OW, kHaloTW) * kHaloTW * cdiv((int64_t)OH, 2 * kHaloTH) * 2 * kHaloTH;
@@ -1342,10 +1366,11 @@ void conv_impl(Tensor* input, Tensor* weight, Tensor* bias, Tensor* residual, Te
   // kernel (stride 1, 32 channels). Falls through to the general path when
   // the rewritten call is not eligible or its scratch exceeds a fixed scratch.
   S2dPlan s2d;
+  const int C2 = 4 * C <= 16 ? 16 : BK;  // stored s2d channels: 64- or 128-byte pixel rows
   if (!split && s2d_plan(C, KH, KW, sh, sw, ph, pw, &s2d) &&
-      halo_eligible(BK, Cout, s2d.KH2, s2d.KW2, 1, 1, s2d.pad_h, s2d.pad_w, OH, OW, split)) {
+      halo_eligible(C2, Cout, s2d.KH2, s2d.KW2, 1, 1, s2d.pad_h, s2d.pad_w, OH, OW, split, C2)) {
     const int H2 = (H + 1) / 2, W2 = (W + 1) / 2;
-    const int64_t x2 = (int64_t)N * H2 * W2 * BK, w2 = (int64_t)Cout * s2d.KH2 * s2d.KW2 * BK;
+    const int64_t x2 = (int64_t)N * H2 * W2 * C2, w2 = (int64_t)Cout * s2d.KH2 * s2d.KW2 * C2;
     const size_t need2 = (size_t)((x2 + 63) / 64 * 64 + w2) * 4 + 256;
     if (!fixed || need2 <= fixed->bytes) {
       float* ws2 = fixed ? fixed->ptr : (float*)workspace(need2, op);
@@ -1353,21 +1378,28 @@ void conv_impl(Tensor* input, Tensor* weight, Tensor* bias, Tensor* residual, Te
       float* xs2 = ws2;
       float* wts2 = ws2 + (x2 + 63) / 64 * 64;
       const bool in_nhwc = is_nhwc(input);
-      s2d_input_kernel<<<grid_for(x2 / BK, 256, 8), 256, 0, ctx().stream>>>(
-          (const float*)input->data, xs2, N, C, H, W, H2, W2, (int64_t)H * W * C,
-          in_nhwc ? 1 : (int64_t)H * W, in_nhwc ? (int64_t)W * C : W, in_nhwc ? C : 1);
+      const int64_t sx_c = in_nhwc ? 1 : (int64_t)H * W, sx_h = in_nhwc ? (int64_t)W * C : W,
+                    sx_w = in_nhwc ? C : 1;
+      if (C2 == 16)
+        s2d_input_kernel<16><<<grid_for(x2 / C2, 256, 8), 256, 0, ctx().stream>>>(
+            (const float*)input->data, xs2, N, C, H, W, H2, W2, (int64_t)H * W * C, sx_c, sx_h,
+            sx_w);
+      else
+        s2d_input_kernel<BK><<<grid_for(x2 / C2, 256, 8), 256, 0, ctx().stream>>>(
+            (const float*)input->data, xs2, N, C, H, W, H2, W2, (int64_t)H * W * C, sx_c, sx_h,
+            sx_w);
       if (!check_launch(op)) return;
       const int src_mode = packed ? (wl.element ? 2 : 1) : 0;
       s2d_weight_kernel<<<grid_for(w2, 256, 8), 256, 0, ctx().stream>>>(
           (const float*)weight->data, wts2, Cout, C, KH, KW, ph, pw, s2d.KH2, s2d.KW2, s2d.pad_h,
-          s2d.pad_w, src_mode, wl.C4, wl.Kpad);
+          s2d.pad_w, src_mode, wl.C4, wl.Kpad, C2);
       if (!check_launch(op)) return;
       ConvArgs g{};
       g.mode = kHalo;
       g.N = N;
       g.H = H2;
       g.W = W2;
-      g.C4 = BK;
+      g.C4 = C2;
       g.OH = OH;
       g.OW = OW;
       g.Cout = Cout;
@@ -1376,8 +1408,8 @@ void conv_impl(Tensor* input, Tensor* weight, Tensor* bias, Tensor* residual, Te
       g.sh = g.sw = 1;
       g.ph = s2d.pad_h;
       g.pw = s2d.pad_w;
-      g.K = s2d.KH2 * s2d.KW2 * BK;
-      g.kblocks = g.K / BK;
+      g.K = s2d.KH2 * s2d.KW2 * C2;
+      g.kblocks = (int)cdiv(g.K, BK);
       g.M = M;
       g.x_hi = xs2;
       g.bias = bias ? (const float*)bias->data : nullptr;
@@ -1386,10 +1418,17 @@ void conv_impl(Tensor* input, Tensor* weight, Tensor* bias, Tensor* residual, Te
       g.out_nhwc = is_nhwc(output) ? 1 : 0;
       g.act = act;
       g.err = device_error_word();
-      if (Cout > 64)
-        launch_halo<128, 1, 4>(g, wts2, op);
-      else
-        launch_halo<64, 3, 3>(g, wts2, op);
+      if (C2 == 16) {
+        if (Cout > 64)
+          launch_halo<128, 2, 4, 16>(g, wts2, op);
+        else
+          launch_halo<64, 8, 3, 16>(g, wts2, op);
+      } else {
+        if (Cout > 64)
+          launch_halo<128, 1, 4, 32>(g, wts2, op);
+        else
+          launch_halo<64, 3, 3, 32>(g, wts2, op);
+      }
       return;
     }
   }
@@ -1513,9 +1552,9 @@ void conv_impl(Tensor* input, Tensor* weight, Tensor* bias, Tensor* residual, Te
 
   if (g.mode == kHalo) {
     if (Cout > 64)
-      launch_halo<128, 1, 4>(g, w0, op);
+      launch_halo<128, 1, 4, 32>(g, w0, op);
     else
-      launch_halo<64, 3, 3>(g, w0, op);
+      launch_halo<64, 3, 3, 32>(g, w0, op);
   } else if (!split) {
     if (Cout > 128)
       launch_conv<256, 1, 4>(g, w0, nullptr, op);

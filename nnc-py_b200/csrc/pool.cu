@@ -71,22 +71,26 @@ __global__ void __launch_bounds__(256) pool_nchw_kernel(const float* __restrict_
   }
 }
 
-template <bool MAX, int V>
+// Idx: the index type, int when every input and output element offset fits
+// (32-bit division and multiplication are several times cheaper than 64-bit,
+// and this loop is bound by its index arithmetic otherwise).
+template <bool MAX, int V, typename Idx>
 __global__ void __launch_bounds__(256) pool_nhwc_kernel(const float* __restrict__ in,
                                                         float* __restrict__ out, PoolGeom g) {
   // V channels per thread (4 with 16-byte alignment, else 1).
-  const int cg = g.C / V;
-  const int64_t total = (int64_t)g.N * g.OH * g.OW * cg;
-  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
-       idx += (int64_t)gridDim.x * blockDim.x) {
+  const Idx cg = g.C / V;
+  const Idx total = (Idx)g.N * g.OH * g.OW * cg;
+  for (Idx idx = blockIdx.x * (Idx)blockDim.x + threadIdx.x; idx < total;
+       idx += (Idx)gridDim.x * blockDim.x) {
     const int c = (int)(idx % cg) * V;
-    int64_t p = idx / cg;
+    const Idx p = idx / cg;
     const int ow = (int)(p % g.OW);
-    const int oh = (int)((p / g.OW) % g.OH);
-    const int n = (int)(p / ((int64_t)g.OW * g.OH));
+    const Idx q = p / g.OW;
+    const int oh = (int)(q % g.OH);
+    const int n = (int)(q / g.OH);
     int h0, h1, w0, w1;
     window(g, oh, ow, h0, h1, w0, w1);
-    const float* img = in + (int64_t)n * g.H * g.W * g.C + c;
+    const float* img = in + (Idx)n * g.H * g.W * g.C + c;
     float acc[V];
     bool has = false;
     int cnt = 0;
@@ -94,7 +98,7 @@ __global__ void __launch_bounds__(256) pool_nhwc_kernel(const float* __restrict_
     for (int j = 0; j < V; ++j) acc[j] = MAX ? kEmptyMax : 0.0f;
     for (int h = h0; h < h1; ++h)
       for (int w = w0; w < w1; ++w) {
-        const float* src = img + ((int64_t)h * g.W + w) * g.C;
+        const float* src = img + ((Idx)h * g.W + w) * g.C;
         float v[V];
         if constexpr (V == 4) {
           const float4 t = *reinterpret_cast<const float4*>(src);
@@ -161,10 +165,23 @@ void pool_impl(Tensor* input, Tensor* output, int kh, int kw, int sh, int sw, in
   float* po = (float*)output->data;
   if (!is_nhwc(input)) {
     pool_nchw_kernel<MAX><<<grid_for(total, 256, 8), 256, 0, ctx().stream>>>(pi, po, g);
-  } else if (g.C % 4 == 0 && aligned16(pi) && aligned16(po)) {
-    pool_nhwc_kernel<MAX, 4><<<grid_for(total / 4, 256, 8), 256, 0, ctx().stream>>>(pi, po, g);
   } else {
-    pool_nhwc_kernel<MAX, 1><<<grid_for(total, 256, 8), 256, 0, ctx().stream>>>(pi, po, g);
+    // 32-bit indexing when every offset (and the grid-stride overshoot) fits.
+    const int64_t in_elems = (int64_t)g.N * g.C * g.H * g.W;
+    const bool small = in_elems < (int64_t(1) << 30) && total < (int64_t(1) << 30);
+    if (g.C % 4 == 0 && aligned16(pi) && aligned16(po)) {
+      const int grid = grid_for(total / 4, 256, 8);
+      if (small)
+        pool_nhwc_kernel<MAX, 4, int><<<grid, 256, 0, ctx().stream>>>(pi, po, g);
+      else
+        pool_nhwc_kernel<MAX, 4, int64_t><<<grid, 256, 0, ctx().stream>>>(pi, po, g);
+    } else {
+      const int grid = grid_for(total, 256, 8);
+      if (small)
+        pool_nhwc_kernel<MAX, 1, int><<<grid, 256, 0, ctx().stream>>>(pi, po, g);
+      else
+        pool_nhwc_kernel<MAX, 1, int64_t><<<grid, 256, 0, ctx().stream>>>(pi, po, g);
+    }
   }
   check_launch(op);
 }

@@ -201,17 +201,20 @@ __device__ __forceinline__ uint64_t desc_kmajor_sw128(uint32_t smem_addr) {
   return d;
 }
 
-// The same layout with a caller-chosen distance between 8-row groups (a
-// multiple of 128 bytes): rows of a group are consecutive 128-byte rows, and
-// the swizzle phase follows the absolute address, so a group may start at any
-// 128-byte row (measured on sm_100a with the base-offset field left 0).
-__device__ __forceinline__ uint64_t desc_kmajor_sw128_sbo(uint32_t smem_addr, uint32_t sbo) {
+// K-major operand in the 128-byte (row_bytes 128, layout type 2) or 64-byte
+// (row_bytes 64, layout type 4) swizzle layout with a caller-chosen distance
+// between 8-row groups (a multiple of row_bytes): rows of a group are
+// consecutive rows, and the swizzle phase follows the absolute address, so a
+// group may start at any row (measured on sm_100a for both spans, with the
+// base-offset field left 0).
+__device__ __forceinline__ uint64_t desc_kmajor_swz(uint32_t smem_addr, uint32_t sbo,
+                                                    int row_bytes) {
   uint64_t d = 0;
   d |= (uint64_t)((smem_addr & 0x3FFFFu) >> 4);
   d |= (uint64_t)1u << 16;
   d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
   d |= (uint64_t)1u << 46;
-  d |= (uint64_t)2u << 61;
+  d |= (uint64_t)(row_bytes == 64 ? 4u : 2u) << 61;
   return d;
 }
 
@@ -246,12 +249,13 @@ __device__ __forceinline__ float to_tf32(float x) {
 
 }  // namespace tc
 
-// Host: encodes a tiled tensor map (fp32, SWIZZLE_128B, zero OOB fill) over
-// a row-major tensor with dims[0] innermost. Returns false (status set) on
-// failure. strides_bytes has rank-1 entries (dims 1..rank-1).
+// Host: encodes a tiled tensor map (fp32, zero OOB fill) over a row-major
+// tensor with dims[0] innermost, in the 128-byte (default) or 64-byte
+// swizzle layout (the box's inner extent must equal the span). Returns false
+// (status set) on failure. strides_bytes has rank-1 entries (dims 1..rank-1).
 bool encode_tmap_f32(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
                      const uint64_t* strides_bytes, const uint32_t* box,
-                     const uint32_t* elem_strides, const char* op);
+                     const uint32_t* elem_strides, const char* op, int swizzle_bytes = 128);
 
 // Host: encodes a 4-D im2col tensor map (fp32, zero OOB fill) over an NHWC
 // tensor: dims {C, W, H, N}, strides_bytes for W, H, N; bounding-box corners
