@@ -168,6 +168,7 @@ def our_arm(opt):
     import torch
 
     from nnc_cuda import lib as L
+    from nnc_cuda import shard as S
     from nnc_cuda import workloads as W
     from nnc_cuda.model import CudaModel
 
@@ -196,7 +197,9 @@ def our_arm(opt):
     prec = L.PRECISION_3XTF32 if opt.precision == "3xtf32" else L.PRECISION_TF32
     rt.nnc_cuda_set_precision(prec)
 
-    x_host = torch.from_numpy(wl.input_array(B, offset=rank * B)).pin_memory()
+    first, count = S.shard_range(GLOBAL_BATCH, world, rank)
+    assert count == B
+    x_host = torch.from_numpy(wl.input_array(B, offset=first)).pin_memory()
     logits_host = torch.empty((B, 1000), dtype=torch.float32).pin_memory()
     gathered = torch.empty((GLOBAL_BATCH, 1000), dtype=torch.float32, device="cuda") if world > 1 else None
     mine = torch.empty((B, 1000), dtype=torch.float32, device="cuda") if world > 1 else None
@@ -221,11 +224,7 @@ def our_arm(opt):
             dist.barrier()
 
     def max_over_ranks(v: float) -> float:
-        if world == 1:
-            return v
-        t = torch.tensor([v], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return S.max_over_ranks(v, world, dist, device="cuda")
 
     with torch.cuda.stream(stream):
         h2d()
