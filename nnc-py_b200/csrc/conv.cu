@@ -777,8 +777,8 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
             break;
           }
           tc::mbar_arrive_expect_tx(&hfull[hs], halo_bytes);
-          tc::tma_load_4d(halo + hs * Cfg::SLOT_BYTES, &tmX, &hfull[hs], cb * CB, x0 - g.pw,
-                          y0 - g.ph, n);
+          tc::tma_load_4d(halo + hs * Cfg::SLOT_BYTES, &tmX, &hfull[hs], cb * CB, x0 * g.sw - g.pw,
+                          y0 * g.sh - g.ph, n);
           if (++hs == kHaloSlots) {
             hs = 0;
             hphase ^= 1;
@@ -1137,8 +1137,10 @@ WeightLayout weight_layout(int Cin, int KH, int KW) {
   WeightLayout L;
   const int ke = (int)cdiv((int64_t)Cin * KH * KW, BK) * BK;
   // Element order only for a single-k-block-or-two reduction (e.g. LeNet's
-  // 1x5x5 conv), where padding channels to 4 would multiply the K work.
-  L.element = ke <= 64;
+  // 1x5x5 conv), where padding channels to 4 would multiply the K work. A
+  // 1 x 1 window over a multiple of 4 channels has the same k order and size
+  // in both layouts, so it takes the chunk order (and the TMA paths).
+  L.element = ke <= 64 && !(KH == 1 && KW == 1 && Cin % 4 == 0);
   if (L.element) {
     L.C4 = Cin;
     L.K = Cin * KH * KW;
@@ -1211,9 +1213,12 @@ bool launch_halo(ConvArgs g, const float* w0, const char* op) {
   const uint64_t xd[4] = {(uint64_t)g.C4, (uint64_t)g.W, (uint64_t)g.H, (uint64_t)g.N};
   const uint64_t xs[3] = {(uint64_t)g.C4 * 4, (uint64_t)g.W * g.C4 * 4,
                           (uint64_t)g.H * g.W * g.C4 * 4};
-  const uint32_t xbox[4] = {CB, (uint32_t)(kHaloTW + g.KW - 1), (uint32_t)(2 * kHaloTH + g.KH - 1),
-                            1};
-  if (!encode_tmap_f32(&tx, g.x_hi, 4, xd, xs, xbox, nullptr, op, Cfg::ROW)) return false;
+  // A strided (1 x 1, stride s) window reads every s-th pixel: the box spans
+  // s times the pixels it delivers (TMA element strides).
+  const uint32_t xbox[4] = {CB, (uint32_t)((kHaloTW + g.KW - 1) * g.sw),
+                            (uint32_t)((2 * kHaloTH + g.KH - 1) * g.sh), 1};
+  const uint32_t xes[4] = {1, (uint32_t)g.sw, (uint32_t)g.sh, 1};
+  if (!encode_tmap_f32(&tx, g.x_hi, 4, xd, xs, xbox, xes, op, Cfg::ROW)) return false;
   g.tiles_x = (int)cdiv(g.OW, kHaloTW);
   g.tiles_y = (int)cdiv(g.OH, 2 * kHaloTH);
   g.m_tiles = g.N * g.tiles_x * g.tiles_y;
@@ -1233,9 +1238,11 @@ bool launch_halo(ConvArgs g, const float* w0, const char* op) {
   return check_launch(op);
 }
 
-// Whether the halo kernel serves a call: stride 1, windows of at most 4 x 4,
-// 32-channel blocks, C_out <= 128, TF32, and 8 x 32 output tiles that waste
-// at most ~35% of their rows on the image's ragged edge.
+// Whether the halo kernel serves a call: stride 1 with windows of at most
+// 4 x 4, or a 1 x 1 window with stride 2 (a strided window load), 32-channel
+// blocks, TF32, and 8 x 32 output tiles that waste at most ~35% of their rows
+// on the image's ragged edge. C_out above 128 runs as several 128-channel
+// tiles.
 // NNC_CUDA_CONV_HALO=0 in the environment turns the path off (the im2col
 // kernel then serves these calls).
 bool halo_eligible(int C4, int Cout, int KH, int KW, int sh, int sw, int ph, int pw, int OH, int OW,
@@ -1244,7 +1251,9 @@ bool halo_eligible(int C4, int Cout, int KH, int KW, int sh, int sw, int ph, int
     const char* e = getenv("NNC_CUDA_CONV_HALO");
     return !(e && e[0] == '0');
   }();
-  if (!enabled || split || sh != 1 || sw != 1 || C4 % cb != 0 || Cout > 128) return false;
+  const bool strided_1x1 = KH == 1 && KW == 1 && sh == 2 && sw == 2;
+  if (!enabled || split || C4 % cb != 0) return false;
+  if (!(sh == 1 && sw == 1) && !strided_1x1) return false;
   if (KH > kHaloMaxK || KW > kHaloMaxK || ph < 0 || pw < 0 || ph >= KH || pw >= KW) return false;
   const int64_t covered =
       cdiv((int64_t)OW, kHaloTW) * kHaloTW * cdiv((int64_t)OH, 2 * kHaloTH) * 2 * kHaloTH;

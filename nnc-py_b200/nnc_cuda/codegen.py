@@ -246,8 +246,9 @@ def _align(x: int, a: int = ARENA_ALIGN) -> int:
 def _packed_conv_bytes(shape) -> int:
     """Size of nnc_cuda_prepack_conv_weight's output (conv.cu weight_layout):
     hi + lo planes of [C_out][K_pad]; K_pad = C_in*KH*KW rounded up to 32 when
-    that is <= 64 (element order), else KH*KW*C4 rounded up to 32 with C4 =
-    C_in rounded up to 4 (chunk order)."""
+    that is <= 64 (element order; a 1 x 1 window over a multiple of 4
+    channels takes the chunk order, which has the same K_pad), else
+    KH*KW*C4 rounded up to 32 with C4 = C_in rounded up to 4 (chunk order)."""
     cout, cin, kh, kw = (int(s) for s in shape)
     ke = (cin * kh * kw + 31) // 32 * 32
     kpad = ke if ke <= 64 else (kh * kw * ((cin + 3) // 4 * 4) + 31) // 32 * 32

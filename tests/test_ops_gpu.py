@@ -161,10 +161,10 @@ def test_conv_resnet_layers_vs_oracle(cuda_lib, prec, cfg):
     C.assert_close(got_nhwc, want, C.TC_RTOL[prec], f"conv{cfg}[nhwc]")
 
 
-# Stride-1 windows over 32-channel blocks take the halo-tile kernel in TF32
-# mode (and the im2col kernel in 3xTF32 mode): ragged 8 x 16 output blocks,
-# partial C_out tiles (48, 200), C_out not a multiple of 4 (scalar epilogue),
-# three channel blocks, a 4 x 4 window, a 1 x 1 window.
+# Stride-1 windows (and 1 x 1 windows with stride 2) over 32-channel blocks
+# take the halo-tile kernel in TF32 mode (the im2col kernel in 3xTF32 mode):
+# ragged output blocks, partial C_out tiles (48, 200), C_out not a multiple of
+# 4 (scalar epilogue), three channel blocks, a 4 x 4 window, 1 x 1 windows.
 HALO_CASES = [
     # n, c, h, w, co, k, p, op
     (2, 32, 30, 30, 48, 3, 1, "nnc_conv_add_relu"),
@@ -173,6 +173,9 @@ HALO_CASES = [
     (1, 32, 30, 30, 64, 4, 2, "nnc_conv_add_relu"),
     (2, 96, 28, 28, 128, 1, 0, "nnc_conv_relu"),
     (2, 32, 30, 30, 30, 3, 1, "nnc_conv"),
+    (2, 64, 56, 56, 128, 1, 0, "nnc_conv"),  # the ResNet stage-2 projection, stride 2
+    (1, 128, 56, 56, 256, 1, 0, "nnc_conv_add_relu"),  # stride 2, two 128-channel tiles
+    (2, 32, 20, 20, 64, 1, 0, "nnc_conv_relu"),  # 1 x 1 over 32 channels (chunk order)
 ]
 
 
@@ -180,8 +183,9 @@ HALO_CASES = [
 @pytest.mark.parametrize("cfg", HALO_CASES, ids=lambda c: "x".join(str(v) for v in c[:7]))
 def test_conv_stride1_blocks_vs_oracle(cuda_lib, prec, cfg):
     n, c, h, w, co, k, p, op = cfg
+    st = 2 if (k == 1 and h == 56) else 1
     r = np.random.default_rng(7 + sum(cfg[:7]))
-    oh, ow = C.conv_out(h, k, 1, p), C.conv_out(w, k, 1, p)
+    oh, ow = C.conv_out(h, k, st, p), C.conv_out(w, k, st, p)
     arrays = {"x": r.standard_normal((n, c, h, w)).astype(np.float32),
               "w": (r.standard_normal((co, c, k, k)) * np.sqrt(2.0 / (c * k * k))).astype(np.float32),
               "b": r.uniform(-0.01, 0.01, co).astype(np.float32),
@@ -191,7 +195,7 @@ def test_conv_stride1_blocks_vs_oracle(cuda_lib, prec, cfg):
     if op == "nnc_conv_add_relu":
         args.append(C._t("res"))
         nhwc.add("res")
-    args += [C._o("out", (n, co, oh, ow)), C._i(k), C._i(k), C._i(1), C._i(1), C._i(p), C._i(p)]
+    args += [C._o("out", (n, co, oh, ow)), C._i(k), C._i(k), C._i(st), C._i(st), C._i(p), C._i(p)]
     case = {"name": "c", "op": op, "args": args}
     cuda_lib.nnc_cuda_set_precision(prec)
     want = C.run_host(_oracle(), case, arrays)["out"]
