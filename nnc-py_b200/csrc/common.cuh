@@ -50,6 +50,10 @@ bool device_ready();
 // Scratch memory on the current device for the current stream.
 void* workspace(size_t bytes, const char* op);
 
+// Max pooling between two device buffers (pool.cu), nnc_maxpool2d semantics.
+bool launch_maxpool_f32(const float* in, float* out, int N, int C, int H, int W, int OH, int OW,
+                        int kh, int kw, int sh, int sw, int ph, int pw, bool nhwc, const char* op);
+
 // Opened at the top of every entry point: refreshes the thread's device from
 // the CUDA runtime (so callers that switch devices with cudaSetDevice or
 // torch.cuda.set_device are followed) and, when tracing is enabled

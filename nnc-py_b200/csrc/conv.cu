@@ -92,7 +92,10 @@ struct ConvArgs {
   int64_t M;  // N*OH*OW
   int m_tiles, n_tiles;
   int64_t tiles;
-  int tiles_x, tiles_y;  // kHalo: 8 x 16 output blocks per image row / column
+  int tiles_x, tiles_y;  // kHalo: 8 x 32 output tiles per image row / column
+  // Fused max pooling of the activated conv result (kHalo, one channel
+  // tile): pooled extent, window, stride, top/left pad.
+  int pool, PH, PW, pkh, pkw, psh, psw, pph, ppw;
   int64_t xs_n, xs_c, xs_h, xs_w;  // element-mode input strides (elements)
   const float* x_hi;  // input (hi plane in 3xTF32 mode)
   const float* x_lo;  // lo plane (3xTF32) or nullptr
@@ -661,10 +664,11 @@ __global__ void __launch_bounds__(kConvThreads, 1)
 
 // --------------------------------------------------------- halo kernel ----
 //
-// Stride-1 convolutions over an NHWC input whose stored channel count C4 is a
-// multiple of 32, C_out <= 128. A tile is an 8-wide x 32-tall block of one
-// image's output pixels, split into an upper and a lower 8 x 16 block (one
-// 128-row accumulator each, row r = 8 y + x), times BN output channels.
+// Stride-1 convolutions (and 1 x 1 windows with stride 2) over an NHWC input
+// whose stored channel count C4 is a multiple of the channel block. A tile is
+// an 8-wide x 32-tall block of one image's output pixels, split into an upper
+// and a lower 8 x 16 block (one 128-row accumulator each, row r = 8 y + x),
+// times BN <= 128 output channels.
 //
 // Per 32-channel block one TMA load brings the tile's input window,
 // (32 + KH - 1) x (8 + KW - 1) pixels of 128 bytes in the 128-byte swizzle
@@ -687,14 +691,28 @@ __global__ void __launch_bounds__(kConvThreads, 1)
 // 352 threads: warp 0 lane 0 issues the TMA loads; warps 1 and 2 (upper,
 // lower block) issue the MMAs, warp 1 owning TMEM; warps 3..6 drain the upper
 // accumulators and warps 7..10 the lower ones (shared epilogue, store_tile).
+//
+// POOL: the conv result (bias, ReLU) is max-pooled in the epilogue and only
+// the pooled tensor is written. A CTA then takes whole images and walks their
+// tiles in raster order, keeping in shared memory the previous tile's last
+// conv column and the previous tile row's last conv row, so every pooled
+// window (stride 2, at most one row/column before the tile) is complete in
+// exactly one tile: no atomics, no second pass.
 constexpr int kHaloTW = 8, kHaloTH = 16;  // one accumulator block
 constexpr int kHaloMaxK = 4;               // largest KH and KW
 constexpr int kHaloSlots = 2;
 constexpr int kHaloThreads = 32 * (3 + kEpilogueWarps);
+constexpr int kPoolMaxOW = 128;  // widest conv output the pooled epilogue carries a row of
+// POOL epilogue staging: the tile's conv result plus the row above it and the
+// column left of it, 33 rows x 9 columns of pixels (pixel (lr, lc) of the
+// tile, lr, lc >= -1, at row (lr + 1) 9 + lc + 1), 32 channels per pixel with
+// a 33-float stride.
+constexpr int kPoolExtW = kHaloTW + 1, kPoolExtH = 2 * kHaloTH + 1;
+constexpr uint32_t kPoolEpiBytes = (uint32_t)kPoolExtW * kPoolExtH * (kStageCols + 1) * 4;
 
 // CB: channels per window row, 32 (128-byte rows, 128-byte swizzle) or 16
 // (64-byte rows, 64-byte swizzle: the space-to-depth stem's 12 channels).
-template <int BN, int G, int STAGES, int CB>
+template <int BN, int G, int STAGES, int CB, bool POOL = false>
 struct HaloCfg {
   static constexpr int ROW = CB * 4;                    // bytes per window row
   static constexpr uint32_t SLOT_BYTES = (2 * kHaloTH + kHaloMaxK - 1) *
@@ -703,16 +721,133 @@ struct HaloCfg {
   static constexpr uint32_t STAGE_BYTES = G * B_BYTES;  // G taps per ring stage
   static constexpr uint32_t HALO_OFF = STAGES * STAGE_BYTES;
   static constexpr uint32_t EPI_OFF = HALO_OFF + kHaloSlots * SLOT_BYTES;
-  static constexpr uint32_t BAR_OFF = EPI_OFF + kEpiBytes;
+  // POOL carries: the previous tile row's last conv row (kPoolMaxOW pixels)
+  // and the previous tile's last conv column (33 rows), BN channels each.
+  static constexpr uint32_t EPI_BYTES = POOL ? (kPoolEpiBytes + 1023) / 1024 * 1024 : kEpiBytes;
+  static constexpr uint32_t CARRY_OFF = EPI_OFF + EPI_BYTES;
+  static constexpr uint32_t CARRY_BYTES = POOL ? (kPoolMaxOW + 33) * BN * 4 : 0;
+  static constexpr uint32_t BAR_OFF = CARRY_OFF + CARRY_BYTES;
   static constexpr uint32_t TMEM_COLS = 4 * BN;  // {upper, lower} x double buffer
   static constexpr size_t SMEM = (size_t)BAR_OFF + 256 + 1024;
 };
 
-template <int BN, int G, int STAGES, int CB>
+__device__ __forceinline__ void epi_bar_sync() {
+  asm volatile("bar.sync 1, 256;" ::: "memory");  // the 8 epilogue warps
+}
+
+// POOL epilogue of one tile, run by all 8 epilogue warps (e = 0..7; block
+// e >> 2, TMEM lane quadrant `quad`). Per 32-channel chunk: (1) each warp puts
+// its 32 accumulator rows, with bias and ReLU, into the staging tile, and the
+// row above / column left come in from the carries (zeros at the image's top
+// and left edges; positions past the conv result are staged as zeros); (2)
+// warp e computes pooled column e & 3 of pooled rows [8 (e >> 2), +8) of the
+// tile, one channel per lane, walking the window rows once and keeping each
+// row's maximum; (3) the carries take this tile's last column and last row.
+// ReLU results are >= 0 and never NaN, so the maximum is order-free and a
+// zero stands for window positions outside the conv result (a window always
+// holds its centre, so none is empty): the reference's first-then-strictly-
+// greater scan gives the same values. With the border in place every window
+// read is a fixed-offset shared load.
+template <int BN>
+__device__ __forceinline__ void pool_tile(const ConvArgs& g, uint32_t tmem_base, int acc, int e,
+                                          int quad, int lane, float* ext, float* row_carry,
+                                          float* col_carry, int n, int y0, int x0) {
+  constexpr int S = kStageCols + 1;  // floats per staged pixel
+  const int blk = e >> 2, tid = e * 32 + lane;
+  const int pc = e & 3, half = e >> 2;  // this warp's pooled column and row half
+  // This lane's accumulator row as a tile pixel.
+  const int ly = blk * kHaloTH + (quad * 32 + lane) / kHaloTW, lx = (quad * 32 + lane) % kHaloTW;
+  const bool in_img = y0 + ly < g.OH && x0 + lx < g.OW;
+  for (int c0 = 0; c0 < BN && c0 < g.Cout; c0 += kStageCols) {
+    const uint32_t taddr =
+        tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * 2 + blk) * BN + c0;
+    float* srow = ext + ((ly + 1) * kPoolExtW + lx + 1) * S;
+    // Lane j holds bias[c0 + j]; column j's bias is broadcast by shuffle.
+    // (With no bias, adding +0 changes no ReLU result.)
+    const float bias_l = (g.bias && c0 + lane < g.Cout) ? g.bias[c0 + lane] : 0.0f;
+    uint32_t r[32];
+    __syncwarp();  // tcgen05.ld is .sync.aligned: the warp must be converged
+    tc::tmem_ld16(taddr, *reinterpret_cast<uint32_t(*)[16]>(&r[0]));
+    tc::tmem_ld16(taddr + 16, *reinterpret_cast<uint32_t(*)[16]>(&r[16]));
+    tc::tmem_ld_wait();
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const float v = __fadd_rn(__uint_as_float(r[j]), __shfl_sync(0xffffffffu, bias_l, j));
+      srow[j] = (in_img && v > 0.0f) ? v : 0.0f;
+    }
+    // Border: ext row 0 = the row above (row_carry, zeros for the first tile
+    // row), ext column 0 = the column left (col_carry, zeros for x0 == 0).
+    for (int idx = tid; idx < (kPoolExtW - 1 + kPoolExtH) * kStageCols; idx += 256) {
+      const int p = idx / kStageCols, cc = idx % kStageCols;
+      if (p < kPoolExtW - 1) {  // ext (0, p + 1): row y0 - 1, column x0 + p
+        ext[(p + 1) * S + cc] = y0 > 0 ? row_carry[(x0 + p) * BN + c0 + cc] : 0.0f;
+      } else {  // ext (q, 0): column x0 - 1, row y0 - 1 + q
+        const int q = p - (kPoolExtW - 1);
+        ext[q * kPoolExtW * S + cc] = (x0 > 0 && (q > 0 || y0 > 0)) ? col_carry[q * BN + c0 + cc] : 0.0f;
+      }
+    }
+    epi_bar_sync();
+    // Pooled rows 8 half + k: window rows 2 (8 half + k) - pph + wy of the
+    // tile, i.e. ext rows 16 half - pph + 1 + 2 k + wy; columns 2 pc - ppw +
+    // wx, ext columns + 1.
+    const int co = c0 + lane;
+    const int px = (x0 >> 1) + pc;
+    const float* col0 = ext + ((16 * half - g.pph + 1) * kPoolExtW + 2 * pc - g.ppw + 1) * S + lane;
+    const int rows = 14 + g.pkh;
+    float h0 = 0.0f, h1 = 0.0f;  // maxima of the two previous window rows
+#pragma unroll
+    for (int i = 0; i < 17; ++i) {
+      if (i >= rows) break;
+      const float* p = col0 + i * (kPoolExtW * S);
+      float m = p[0];
+      if (g.pkw > 1) m = fmaxf(m, p[S]);
+      if (g.pkw > 2) m = fmaxf(m, p[2 * S]);
+      const int k2 = i - g.pkh + 1;  // pooled row k = k2 / 2 ends at window row i
+      if (k2 >= 0 && (k2 & 1) == 0) {
+        float o = m;
+        if (g.pkh > 1) o = fmaxf(o, h1);
+        if (g.pkh > 2) o = fmaxf(o, h0);
+        const int py = (y0 >> 1) + 8 * half + (k2 >> 1);
+        if (py < g.PH && px < g.PW && co < g.Cout)
+          g.out[(((int64_t)n * g.PH + py) * g.PW + px) * g.Cout + co] = o;
+      }
+      h0 = h1;
+      h1 = m;
+    }
+    epi_bar_sync();
+    // Carries: column x0 + 7 (ext column 8, rows -1 .. 31) and row y0 + 31
+    // (ext row 32, columns 0 .. 7).
+    for (int idx = tid; idx < (kPoolExtH + kPoolExtW - 1) * kStageCols; idx += 256) {
+      const int p = idx / kStageCols, cc = idx % kStageCols;
+      if (p < kPoolExtH)
+        col_carry[p * BN + c0 + cc] = ext[(p * kPoolExtW + kPoolExtW - 1) * S + cc];
+      else
+        row_carry[(x0 + p - kPoolExtH) * BN + c0 + cc] =
+            ext[((kPoolExtH - 1) * kPoolExtW + p - kPoolExtH + 1) * S + cc];
+    }
+    epi_bar_sync();
+  }
+}
+
+// The k-th tile a CTA processes, or -1 past its last: every gridDim-th tile,
+// or (POOL, one channel tile) every gridDim-th image with its tiles in
+// raster order.
+template <bool POOL>
+__device__ __forceinline__ int64_t halo_tile(const ConvArgs& g, int64_t k) {
+  if (!POOL) {
+    const int64_t t = blockIdx.x + k * gridDim.x;
+    return t < g.tiles ? t : -1;
+  }
+  const int64_t per = (int64_t)g.tiles_x * g.tiles_y;
+  const int64_t img = blockIdx.x + (k / per) * gridDim.x;
+  return img < g.N ? img * per + k % per : -1;
+}
+
+template <int BN, int G, int STAGES, int CB, bool POOL>
 __global__ void __launch_bounds__(kHaloThreads, 1)
     conv_halo_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
                      const ConvArgs g) {
-  using Cfg = HaloCfg<BN, G, STAGES, CB>;
+  using Cfg = HaloCfg<BN, G, STAGES, CB, POOL>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   uint8_t* halo = smem + Cfg::HALO_OFF;
@@ -746,6 +881,7 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
     }
     tc::mbar_init(&done[0], 1);
     tc::mbar_init(&done[1], 1);
+    tmem_slot[1] = 0;  // epilogue abort flag (POOL)
     tc::fence_barrier_init();
     tc::prefetch_tmap(&tmW);
     tc::prefetch_tmap(&tmX);
@@ -766,7 +902,9 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
       int stage = 0, hs = 0;
       uint32_t phase = 0, hphase = 0;
       bool ok = true;
-      for (int64_t tile = blockIdx.x; tile < g.tiles && ok; tile += gridDim.x) {
+      for (int64_t k = 0; ok; ++k) {
+        const int64_t tile = halo_tile<POOL>(g, k);
+        if (tile < 0) break;
         const int64_t mt = tile / g.n_tiles;
         const int nt = (int)(tile % g.n_tiles);
         const int n = (int)(mt / per_img), rem = (int)(mt % per_img);
@@ -832,9 +970,8 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
     const uint64_t b_desc0 = tc::desc_kmajor_swz(tc::smem_u32(smem), 8 * Cfg::ROW, Cfg::ROW);
     int stage = 0, hs = 0;
     uint32_t phase = 0, hphase = 0;
-    int local = 0;
     bool ok = true;
-    for (int64_t t = blockIdx.x; t < g.tiles && ok; t += gridDim.x, ++local) {
+    for (int64_t local = 0; ok && halo_tile<POOL>(g, local) >= 0; ++local) {
       const int acc = local & 1;
       const uint32_t aphase = (local >> 1) & 1;
       if (!tc::mbar_wait_warp(&tempty[acc * 2 + blk], aphase ^ 1, g.err)) break;
@@ -913,19 +1050,37 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
                         (!g.residual || ((((uintptr_t)g.residual) & 15) == 0));
     const bool bias_vec = g.bias && ((((uintptr_t)g.bias) & 15) == 0);
     const int64_t OHW = (int64_t)g.OH * g.OW;
-    int local = 0;
-    for (int64_t t = blockIdx.x; t < g.tiles; t += gridDim.x, ++local) {
+    float* row_carry = reinterpret_cast<float*>(smem + Cfg::CARRY_OFF);
+    float* col_carry = row_carry + kPoolMaxOW * BN;
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    for (int64_t local = 0;; ++local) {
+      const int64_t t = halo_tile<POOL>(g, local);
+      if (t < 0) break;
       const int64_t mt = t / g.n_tiles;
       const int nt = (int)(t % g.n_tiles);
       const int n = (int)(mt / per_img), rem = (int)(mt % per_img);
       const int acc = local & 1;
       const uint32_t aphase = (local >> 1) & 1;
-      if (!tc::mbar_wait(&tfull[acc * 2 + blk], aphase, g.err)) break;
+      const bool ready = tc::mbar_wait(&tfull[acc * 2 + blk], aphase, g.err);
+      if (POOL) {
+        // The pooled epilogue synchronises the 8 warps: agree on giving up
+        // (every wait above is bounded, so every warp gets here).
+        if (!ready) *abort_flag = 1;
+        epi_bar_sync();
+        if (*abort_flag) break;
+      } else if (!ready) {
+        break;
+      }
       tc::tc_fence_after();
-      store_tile<BN>(g, tmem_base, (uint32_t)(acc * 2 + blk) * BN, nt, quad, 0, kStageCols, lane,
-                     stage_tile, vec_ok, bias_vec,
-                     BlockRows{(int64_t)n * OHW, (rem / g.tiles_x) * 2 * kHaloTH + blk * kHaloTH,
-                               (rem % g.tiles_x) * kHaloTW, g.OH, g.OW});
+      if (POOL) {
+        pool_tile<BN>(g, tmem_base, acc, e, quad, lane, epi, row_carry, col_carry, n,
+                      (rem / g.tiles_x) * 2 * kHaloTH, (rem % g.tiles_x) * kHaloTW);
+      } else {
+        store_tile<BN>(g, tmem_base, (uint32_t)(acc * 2 + blk) * BN, nt, quad, 0, kStageCols, lane,
+                       stage_tile, vec_ok, bias_vec,
+                       BlockRows{(int64_t)n * OHW, (rem / g.tiles_x) * 2 * kHaloTH + blk * kHaloTH,
+                                 (rem % g.tiles_x) * kHaloTW, g.OH, g.OW});
+      }
       tc::tc_fence_before();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&tempty[acc * 2 + blk]);
@@ -1200,9 +1355,9 @@ bool launch_conv(ConvArgs g, const float* w0, const float* w1, const char* op) {
   return check_launch(op);
 }
 
-template <int BN, int G, int STAGES, int CB>
+template <int BN, int G, int STAGES, int CB, bool POOL = false>
 bool launch_halo(ConvArgs g, const float* w0, const char* op) {
-  using Cfg = HaloCfg<BN, G, STAGES, CB>;
+  using Cfg = HaloCfg<BN, G, STAGES, CB, POOL>;
   const int Kpad = g.K;  // taps x C4, a multiple of CB
   CUtensorMap tw, tx;
   const uint64_t dims[2] = {(uint64_t)Kpad, (uint64_t)g.Cout};
@@ -1224,7 +1379,7 @@ bool launch_halo(ConvArgs g, const float* w0, const char* op) {
   g.m_tiles = g.N * g.tiles_x * g.tiles_y;
   g.n_tiles = (int)cdiv(g.Cout, BN);
   g.tiles = (int64_t)g.m_tiles * g.n_tiles;
-  auto kern = conv_halo_kernel<BN, G, STAGES, CB>;
+  auto kern = conv_halo_kernel<BN, G, STAGES, CB, POOL>;
   static bool attr_set[64] = {};
   if (!attr_set[ctx().device]) {
     if (!check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1233,7 +1388,8 @@ bool launch_halo(ConvArgs g, const float* w0, const char* op) {
       return false;
     attr_set[ctx().device] = true;
   }
-  const int grid = (int)(g.tiles < sm_count() ? g.tiles : sm_count());
+  const int64_t units = POOL ? (int64_t)g.N : g.tiles;  // POOL: whole images per CTA
+  const int grid = (int)(units < sm_count() ? units : sm_count());
   kern<<<grid, kHaloThreads, Cfg::SMEM, ctx().stream>>>(tw, tx, g);
   return check_launch(op);
 }
@@ -1325,9 +1481,15 @@ bool s2d_plan(int C, int KH, int KW, int sh, int sw, int ph, int pw, S2dPlan* p)
 // fixed == nullptr: scratch comes from the runtime workspace (which may grow
 // with cudaMallocAsync); otherwise from *fixed, and a call that needs more
 // than it holds is rejected before any work is queued.
+// Max pooling applied to the conv result (nnc_conv_relu_maxpool): the conv's
+// own output extent and the pool window, stride and top/left pad.
+struct PoolSpec {
+  int conv_h, conv_w, kh, kw, sh, sw, ph, pw;
+};
+
 void conv_impl(Tensor* input, Tensor* weight, Tensor* bias, Tensor* residual, Tensor* output,
                int KH, int KW, int sh, int sw, int ph, int pw, int act, const char* op,
-               const StaticScratch* fixed = nullptr) {
+               const StaticScratch* fixed = nullptr, const PoolSpec* pool = nullptr) {
   if (!conv_f32(input, op, "input") || !conv_f32(weight, op, "weight") ||
       !conv_f32(output, op, "output"))
     return;
@@ -1340,7 +1502,10 @@ void conv_impl(Tensor* input, Tensor* weight, Tensor* bias, Tensor* residual, Te
   const int N = (int)input->shape[0], C = (int)input->shape[1], H = (int)input->shape[2],
             W = (int)input->shape[3];
   const int Cout = (int)weight->shape[0];
-  const int OH = (int)output->shape[2], OW = (int)output->shape[3];
+  // With a fused pool the output tensor is the pooled one; the conv extent
+  // comes with the pool spec.
+  const int OH = pool ? pool->conv_h : (int)output->shape[2];
+  const int OW = pool ? pool->conv_w : (int)output->shape[3];
   if (weight->shape[1] != C || weight->shape[2] != KH || weight->shape[3] != KW) {
     fail(NNC_CUDA_ERR_INVALID, op, "weight shape [%lld,%lld,%lld,%lld] does not match C=%d %dx%d",
          (long long)weight->shape[0], (long long)weight->shape[1], (long long)weight->shape[2],
@@ -1363,6 +1528,11 @@ void conv_impl(Tensor* input, Tensor* weight, Tensor* bias, Tensor* residual, Te
     fail(NNC_CUDA_ERR_INVALID, op, "residual must match the output's shape and layout");
     return;
   }
+  if (pool && (residual || pool->kh <= 0 || pool->kw <= 0 || pool->sh <= 0 || pool->sw <= 0 ||
+               OH <= 0 || OW <= 0)) {
+    fail(NNC_CUDA_ERR_INVALID, op, "invalid pooled conv geometry");
+    return;
+  }
   const int64_t M = (int64_t)N * OH * OW;
   if (M == 0 || Cout == 0) return;
   const bool split = ctx().precision == NNC_CUDA_PRECISION_3XTF32;
@@ -1376,7 +1546,14 @@ void conv_impl(Tensor* input, Tensor* weight, Tensor* bias, Tensor* residual, Te
   // the rewritten call is not eligible or its scratch exceeds a fixed scratch.
   S2dPlan s2d;
   const int C2 = 4 * C <= 16 ? 16 : BK;  // stored s2d channels: 64- or 128-byte pixel rows
-  if (!split && s2d_plan(C, KH, KW, sh, sw, ph, pw, &s2d) &&
+  // Fused pooling: one channel tile (C_out <= 64), a conv row that fits the
+  // row carry, a channels-last pooled output, and a stride-2 window reaching
+  // at most one row/column before its tile and none past it.
+  const bool pool_fused = pool && C2 == 16 && Cout <= 64 && OW <= kPoolMaxOW && is_nhwc(output) &&
+                          pool->sh == 2 && pool->sw == 2 && pool->ph >= 0 && pool->pw >= 0 &&
+                          pool->ph <= 1 && pool->pw <= 1 && pool->kh - pool->ph <= 2 &&
+                          pool->kw - pool->pw <= 2;
+  if (!split && (!pool || pool_fused) && s2d_plan(C, KH, KW, sh, sw, ph, pw, &s2d) &&
       halo_eligible(C2, Cout, s2d.KH2, s2d.KW2, 1, 1, s2d.pad_h, s2d.pad_w, OH, OW, split, C2)) {
     const int H2 = (H + 1) / 2, W2 = (W + 1) / 2;
     const int64_t x2 = (int64_t)N * H2 * W2 * C2, w2 = (int64_t)Cout * s2d.KH2 * s2d.KW2 * C2;
@@ -1427,7 +1604,19 @@ void conv_impl(Tensor* input, Tensor* weight, Tensor* bias, Tensor* residual, Te
       g.out_nhwc = is_nhwc(output) ? 1 : 0;
       g.act = act;
       g.err = device_error_word();
-      if (C2 == 16) {
+      if (pool_fused) {
+        g.pool = 1;
+        g.PH = (int)output->shape[2];
+        g.PW = (int)output->shape[3];
+        g.pkh = pool->kh;
+        g.pkw = pool->kw;
+        g.psh = pool->sh;
+        g.psw = pool->sw;
+        g.pph = pool->ph;
+        g.ppw = pool->pw;
+        launch_halo<64, 8, 2, 16, true>(g, wts2, op);
+        return;
+      } else if (C2 == 16) {
         if (Cout > 64)
           launch_halo<128, 2, 4, 16>(g, wts2, op);
         else
@@ -1440,6 +1629,27 @@ void conv_impl(Tensor* input, Tensor* weight, Tensor* bias, Tensor* residual, Te
       }
       return;
     }
+  }
+  if (pool) {
+    // Composition: the conv into a temporary tensor (the output's layout),
+    // then max pooling into the output.
+    const size_t tbytes = (size_t)N * Cout * OH * OW * 4;
+    void* tmp = nullptr;
+    if (!check_cuda(cudaMallocAsync(&tmp, tbytes, ctx().stream), op, "pooled conv temporary")) return;
+    int64_t tshape[4] = {N, Cout, OH, OW};
+    Tensor t{};
+    t.data = tmp;
+    t.dtype = output->dtype;
+    t.shape = tshape;
+    t.ndim = 4;
+    t.nbytes = (int64_t)tbytes;
+    conv_impl(input, weight, bias, nullptr, &t, KH, KW, sh, sw, ph, pw, act, op);
+    if (ctx().status == NNC_CUDA_OK)
+      launch_maxpool_f32((const float*)tmp, (float*)output->data, N, Cout, OH, OW,
+                         (int)output->shape[2], (int)output->shape[3], pool->kh, pool->kw, pool->sh,
+                         pool->sw, pool->ph, pool->pw, is_nhwc(output), op);
+    cudaFreeAsync(tmp, ctx().stream);
+    return;
   }
 
   // Scratch: input planes when the input cannot be read in place (chunk
@@ -1620,6 +1830,20 @@ void nnc_conv_relu(Tensor* input, Tensor* weight, Tensor* bias, Tensor* output, 
   OpScope s("nnc_conv_relu");
   conv_impl(input, weight, bias, nullptr, output, kernel_h, kernel_w, stride_h, stride_w, pad_h,
             pad_w, kActRelu, "nnc_conv_relu");
+}
+// relu(conv) followed by max pooling in one call (no reference counterpart:
+// the composition of nnc_conv_relu, ops.c:3122-3194, and nnc_maxpool2d,
+// ops.c:316-391). `output` is the pooled tensor; conv_h x conv_w is the conv
+// result's extent (the tensor the two reference calls would share).
+void nnc_conv_relu_maxpool(Tensor* input, Tensor* weight, Tensor* bias, Tensor* output,
+                           int kernel_h, int kernel_w, int stride_h, int stride_w, int pad_h,
+                           int pad_w, int conv_h, int conv_w, int pool_kh, int pool_kw,
+                           int pool_sh, int pool_sw, int pool_ph, int pool_pw) {
+  const char* op = "nnc_conv_relu_maxpool";
+  OpScope s(op);
+  const PoolSpec pool{conv_h, conv_w, pool_kh, pool_kw, pool_sh, pool_sw, pool_ph, pool_pw};
+  conv_impl(input, weight, bias, nullptr, output, kernel_h, kernel_w, stride_h, stride_w, pad_h,
+            pad_w, kActRelu, op, nullptr, &pool);
 }
 void nnc_conv_sigmoid(Tensor* input, Tensor* weight, Tensor* bias, Tensor* output, int kernel_h,
                       int kernel_w, int stride_h, int stride_w, int pad_h, int pad_w) {

@@ -187,6 +187,37 @@ void pool_impl(Tensor* input, Tensor* output, int kh, int kw, int sh, int sw, in
 }
 
 }  // namespace
+
+// Max pooling of a float32 tensor already on the device (for fused callers
+// whose pooled input is an intermediate): the same kernels and semantics as
+// nnc_maxpool2d. Returns false with the status set on a launch failure.
+bool launch_maxpool_f32(const float* in, float* out, int N, int C, int H, int W, int OH, int OW,
+                        int kh, int kw, int sh, int sw, int ph, int pw, bool nhwc, const char* op) {
+  PoolGeom g{N, C, H, W, OH, OW, kh, kw, sh, sw, ph, pw};
+  const int64_t total = (int64_t)N * C * OH * OW;
+  if (total == 0) return true;
+  if (!nhwc) {
+    pool_nchw_kernel<true><<<grid_for(total, 256, 8), 256, 0, ctx().stream>>>(in, out, g);
+  } else {
+    const int64_t in_elems = (int64_t)N * C * H * W;
+    const bool small = in_elems < (int64_t(1) << 30) && total < (int64_t(1) << 30);
+    if (C % 4 == 0 && aligned16(in) && aligned16(out)) {
+      const int grid = grid_for(total / 4, 256, 8);
+      if (small)
+        pool_nhwc_kernel<true, 4, int><<<grid, 256, 0, ctx().stream>>>(in, out, g);
+      else
+        pool_nhwc_kernel<true, 4, int64_t><<<grid, 256, 0, ctx().stream>>>(in, out, g);
+    } else {
+      const int grid = grid_for(total, 256, 8);
+      if (small)
+        pool_nhwc_kernel<true, 1, int><<<grid, 256, 0, ctx().stream>>>(in, out, g);
+      else
+        pool_nhwc_kernel<true, 1, int64_t><<<grid, 256, 0, ctx().stream>>>(in, out, g);
+    }
+  }
+  return check_launch(op);
+}
+
 }  // namespace nnc
 
 extern "C" {

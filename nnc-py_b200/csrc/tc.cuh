@@ -14,7 +14,7 @@
 namespace nnc {
 namespace tc {
 
-constexpr uint32_t kWaitLimit = 1u << 24;  // ~ seconds with the try_wait suspend hint
+constexpr uint32_t kWaitLimit = 1u << 24;  // tries; the 2 s time bound ends a wait first
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -35,14 +35,18 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                "r"(bytes)
                : "memory");
 }
+// One try with a suspend-time hint: a thread whose phase has not completed
+// sleeps in hardware until it does or kSuspendNs pass, instead of spinning
+// and taking issue slots from the warps that do the work.
+constexpr uint32_t kSuspendNs = 100000;  // 0.1 ms per try
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendNs)
       : "memory");
   return ok != 0;
 }
@@ -52,19 +56,16 @@ __device__ __forceinline__ uint64_t global_ns() {
   return t;
 }
 
-// Bounded wait for the phase with the given parity to complete: polls, backs
-// off with nanosleep after the first 4096 polls, and gives up after
-// kWaitNs nanoseconds (or kWaitLimit polls), recording the timeout.
+// Bounded wait for the phase with the given parity to complete: suspending
+// tries until it does, giving up after kWaitNs nanoseconds (or kWaitLimit
+// tries) and recording the timeout.
 constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_ns();
   for (uint32_t i = 0; i < kWaitLimit; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (i >= 4096) {
-      __nanosleep(128);
-      if ((i & 255) == 0 && global_ns() - t0 > kWaitNs) break;
-    }
+    if (global_ns() - t0 > kWaitNs) break;
   }
   if (err) atomicExch(err, 5 /* NNC_CUDA_ERR_DEVICE_TIMEOUT */);
   return false;

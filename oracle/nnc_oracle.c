@@ -330,6 +330,21 @@ void nnc_conv_add_relu(Tensor* i, Tensor* w, Tensor* b, Tensor* r, Tensor* o, in
     conv2d(i, w, b, o, kh, kw, sh, sw, ph, pw, ACT_NONE);
     nnc_add_relu(o, r, o);
 }
+/* The cuda target's fused Conv -> Relu -> MaxPool group: the reference
+ * composition nnc_conv_relu (ops.c:3122-3194) into an NCHW temporary of
+ * conv_h x conv_w, then nnc_maxpool2d (ops.c:316-391). */
+void nnc_conv_relu_maxpool(Tensor* i, Tensor* w, Tensor* b, Tensor* o, int kh, int kw, int sh, int sw,
+                           int ph, int pw, int conv_h, int conv_w, int pkh, int pkw, int psh, int psw,
+                           int pph, int ppw) {
+    int64_t shape[4] = {i->shape[0], w->shape[0], conv_h, conv_w};
+    const int64_t n = shape[0] * shape[1] * shape[2] * shape[3];
+    float* buf = (float*)malloc((size_t)(n > 0 ? n : 1) * sizeof(float));
+    if (!buf) return;
+    Tensor t = {buf, NNC_DTYPE_FLOAT32, shape, 4, n * (int64_t)sizeof(float)};
+    nnc_conv_relu(i, w, b, &t, kh, kw, sh, sw, ph, pw);
+    nnc_maxpool2d(&t, o, pkh, pkw, psh, psw, pph, ppw);
+    free(buf);
+}
 void nnc_conv_add_relu1x1(Tensor* i, Tensor* w, Tensor* b, Tensor* r, Tensor* o, int sh, int sw, int ph, int pw) {
     nnc_conv_add_relu(i, w, b, r, o, 1, 1, sh, sw, ph, pw);
 }

@@ -258,6 +258,40 @@ def test_conv_stride2_few_channels_vs_oracle(cuda_lib, prec, cfg):
     C.assert_close(got_p, want, C.TC_RTOL[prec], f"conv{cfg}[prepacked]")
 
 
+# relu(conv) then max pooling in one call: the fused space-to-depth halo
+# kernel with a pooled epilogue for stem-like shapes and a channels-last
+# output (ragged extents, a 2x2 pool, C_out 48), and the conv + pool
+# composition otherwise (NCHW output, 3xTF32, 8 input channels, stride 1).
+POOL_CASES = [
+    # n, c, h, w, co, k, s, p, (pool k, stride, pad)
+    (2, 3, 224, 224, 64, 7, 2, 3, (3, 2, 1)),
+    (1, 3, 62, 58, 64, 7, 2, 3, (3, 2, 1)),
+    (2, 3, 64, 64, 48, 7, 2, 3, (2, 2, 0)),
+    (2, 8, 40, 40, 64, 3, 2, 1, (3, 2, 1)),
+    (2, 16, 20, 20, 32, 3, 1, 1, (3, 2, 1)),
+]
+
+
+@pytest.mark.parametrize("prec", [0, 1])
+@pytest.mark.parametrize("cfg", POOL_CASES, ids=lambda c: "x".join(str(v) for v in c[:8]))
+def test_conv_relu_maxpool_vs_oracle(cuda_lib, prec, cfg):
+    n, c, h, w, co, k, st, p, (pk, ps, pp) = cfg
+    r = np.random.default_rng(5 + sum(cfg[:8]))
+    oh, ow = C.conv_out(h, k, st, p), C.conv_out(w, k, st, p)
+    ph, pw = C.conv_out(oh, pk, ps, pp), C.conv_out(ow, pk, ps, pp)
+    arrays = {"x": r.standard_normal((n, c, h, w)).astype(np.float32),
+              "w": (r.standard_normal((co, c, k, k)) * np.sqrt(2.0 / (c * k * k))).astype(np.float32),
+              "b": r.uniform(-0.01, 0.01, co).astype(np.float32)}
+    args = [C._t("x"), C._t("w"), C._t("b"), C._o("out", (n, co, ph, pw))] + [
+        C._i(v) for v in (k, k, st, st, p, p, oh, ow, pk, pk, ps, ps, pp, pp)]
+    case = {"name": "c", "op": "nnc_conv_relu_maxpool", "args": args}
+    cuda_lib.nnc_cuda_set_precision(prec)
+    want = C.run_host(_oracle(), case, arrays)["out"]
+    for layout in ((), ("out",), ("x", "out")):
+        got = C.run_cuda(cuda_lib, case, arrays, nhwc=set(layout))["out"]
+        C.assert_close(got, want, C.TC_RTOL[prec], f"conv_relu_maxpool{cfg}[{layout}]")
+
+
 # ------------------------------------------------------------ validation --
 def test_invalid_shapes_set_status_without_launch(cuda_lib):
     import torch
