@@ -56,43 +56,88 @@ def peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+    """SM clock, power and clock-event reasons of one GPU, sampled every 10 ms
+    by an NVML thread while the timed region runs (read-only NVML queries).
+    Falls back to `nvidia-smi -lms 200` when NVML cannot be loaded."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40),
+               ("sw_thermal_slowdown", 0x20), ("sw_power_cap", 0x4),
+               ("hw_power_brake_slowdown", 0x80))
+    SMI_FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+                  "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                  "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpus: list[int]):
-        self.gpus = gpus
+    def __init__(self, cuda_index: int):
+        self.cuda_index = cuda_index
+        self.samples: list[tuple[float, int, float]] = []
+        self.max_mhz = None
+        self.thread = None
         self.proc = None
-        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.source = None
+
+    def _nvml_loop(self, nvml, handle):
+        while not self._stop.is_set():
+            try:
+                sm = nvml.nvmlDeviceGetClockInfo(handle, nvml.NVML_CLOCK_SM)
+                why = nvml.nvmlDeviceGetCurrentClocksEventReasons(handle)
+                mw = nvml.nvmlDeviceGetPowerUsage(handle) / 1000.0
+                self.samples.append((float(sm), int(why), mw))
+            except Exception:  # a failed query leaves a gap, not an error
+                pass
+            self._stop.wait(0.01)
 
     def start(self):
+        import threading
+
+        import torch
+        try:
+            import pynvml as nvml
+            nvml.nvmlInit()
+            idx = torch.cuda._get_nvml_device_index(self.cuda_index)
+            handle = nvml.nvmlDeviceGetHandleByIndex(idx)
+            self.max_mhz = float(nvml.nvmlDeviceGetMaxClockInfo(handle, nvml.NVML_CLOCK_SM))
+            self._stop = threading.Event()
+            self.thread = threading.Thread(target=self._nvml_loop, args=(nvml, handle), daemon=True)
+            self.thread.start()
+            self.source = "nvml, 10 ms"
+            return
+        except Exception:
+            self.thread = None
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
-                 "-i", ",".join(str(g) for g in self.gpus)], stdout=self.file, stderr=subprocess.DEVNULL)
+                ["nvidia-smi", f"--query-gpu={self.SMI_FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.cuda_index)], stdout=self.file, stderr=subprocess.DEVNULL)
+            self.source = "nvidia-smi, 200 ms"
         except FileNotFoundError:
             self.proc = None
 
     def stop(self) -> dict:
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.terminate()
-        self.proc.wait(timeout=10)
-        self.file.flush()
-        rows = [r.split(",") for r in pathlib.Path(self.file.name).read_text().splitlines() if r.count(",") >= 8]
-        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
-        reasons = set()
-        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        for r in rows:
-            for n, v in zip(names, r[5:9]):
-                if v.strip().lower() == "active":
-                    reasons.add(n)
+        if self.thread is not None:
+            self._stop.set()
+            self.thread.join(timeout=5)
+            sm = [s for s, _, _ in self.samples]
+            reasons = sorted({n for _, why, _ in self.samples for n, bit in self.REASONS if why & bit})
+            power = [w for _, _, w in self.samples]
+        elif self.proc is not None:
+            self.proc.terminate()
+            self.proc.wait(timeout=10)
+            self.file.flush()
+            rows = [r.split(",") for r in pathlib.Path(self.file.name).read_text().splitlines()
+                    if r.count(",") >= 8]
+            sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
+            mx = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
+            self.max_mhz = max(mx) if mx else None
+            power = [float(r[3]) for r in rows if r[3].strip().replace(".", "").isdigit()]
+            names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+            reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.strip().lower() == "active"})
+        else:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no NVML and no nvidia-smi"], "samples": 0}
         busy = [s for s in sm if s > 500] or sm
-        return {"sm_mhz": statistics.median(busy) if busy else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": sorted(reasons), "samples": len(rows)}
+        return {"sm_mhz": statistics.median(busy) if busy else None, "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(sm),
+                "power_w_median": round(statistics.median(power), 1) if power else None,
+                "source": self.source}
 
 
 def conv_flops(model) -> float:
@@ -236,7 +281,7 @@ def our_arm(opt):
         raise RuntimeError(rt.nnc_cuda_get_last_error_string().decode())
 
     # ---- device-resident timing (value) ----
-    sampler = ClockSampler([local]) if rank == 0 else None
+    sampler = ClockSampler(local) if rank == 0 else None
     if sampler:
         sampler.start()
     launches0 = rt.nnc_cuda_launch_count()
@@ -389,7 +434,7 @@ def conv_bytes(model) -> float:
 def roofline_traffic(images: int):
     """DRAM bytes (read + write) of all conv launches of one step, from the
     committed ncu summary's per-image figure, scaled to `images`."""
-    p = ROOT / "profiles" / "conv_tc_resnet18_traffic.txt"
+    p = ROOT / "profiles" / "conv_kernels_resnet18_b256_traffic.txt"
     if p.exists():
         for line in p.read_text().splitlines():
             if line.startswith("dram_bytes_per_image="):

@@ -695,20 +695,21 @@ __global__ void __launch_bounds__(kConvThreads, 1)
 // POOL: the conv result (bias, ReLU) is max-pooled in the epilogue and only
 // the pooled tensor is written. A CTA then takes whole images and walks their
 // tiles in raster order, keeping in shared memory the previous tile's last
-// conv column and the previous tile row's last conv row, so every pooled
-// window (stride 2, at most one row/column before the tile) is complete in
-// exactly one tile: no atomics, no second pass.
+// column and the previous tile row's last conv row, so every pooled window
+// (stride 2, at most one row/column before its centre and one after) is
+// complete in the tile that holds its centre: no atomics, no second pass.
 constexpr int kHaloTW = 8, kHaloTH = 16;  // one accumulator block
 constexpr int kHaloMaxK = 4;               // largest KH and KW
 constexpr int kHaloSlots = 2;
 constexpr int kHaloThreads = 32 * (3 + kEpilogueWarps);
 constexpr int kPoolMaxOW = 128;  // widest conv output the pooled epilogue carries a row of
-// POOL epilogue staging: the tile's conv result plus the row above it and the
-// column left of it, 33 rows x 9 columns of pixels (pixel (lr, lc) of the
-// tile, lr, lc >= -1, at row (lr + 1) 9 + lc + 1), 32 channels per pixel with
-// a 33-float stride.
-constexpr int kPoolExtW = kHaloTW + 1, kPoolExtH = 2 * kHaloTH + 1;
-constexpr uint32_t kPoolEpiBytes = (uint32_t)kPoolExtW * kPoolExtH * (kStageCols + 1) * 4;
+// POOL shared buffers, in floats: the exchange of each warp's last conv row
+// with the warp below it ([chunk parity][8 row groups][8 columns], 32
+// channels at a 40-float stride), the row carry ([kPoolMaxOW columns], BN
+// channels at a BN + 8 stride) and the column carry ([8 row groups][2 centre
+// rows], BN channels).
+constexpr int kPoolXStride = 40;
+constexpr uint32_t kPoolXchgFloats = 2 * 8 * 8 * kPoolXStride;
 
 // CB: channels per window row, 32 (128-byte rows, 128-byte swizzle) or 16
 // (64-byte rows, 64-byte swizzle: the space-to-depth stem's 12 channels).
@@ -721,11 +722,11 @@ struct HaloCfg {
   static constexpr uint32_t STAGE_BYTES = G * B_BYTES;  // G taps per ring stage
   static constexpr uint32_t HALO_OFF = STAGES * STAGE_BYTES;
   static constexpr uint32_t EPI_OFF = HALO_OFF + kHaloSlots * SLOT_BYTES;
-  // POOL carries: the previous tile row's last conv row (kPoolMaxOW pixels)
-  // and the previous tile's last conv column (33 rows), BN channels each.
-  static constexpr uint32_t EPI_BYTES = POOL ? (kPoolEpiBytes + 1023) / 1024 * 1024 : kEpiBytes;
+  static constexpr uint32_t EPI_BYTES = POOL ? kPoolXchgFloats * 4 : kEpiBytes;
   static constexpr uint32_t CARRY_OFF = EPI_OFF + EPI_BYTES;
-  static constexpr uint32_t CARRY_BYTES = POOL ? (kPoolMaxOW + 33) * BN * 4 : 0;
+  static constexpr int ROW_CARRY_STRIDE = BN + 8;
+  static constexpr uint32_t CARRY_BYTES =
+      POOL ? (uint32_t)(kPoolMaxOW * ROW_CARRY_STRIDE + 16 * BN) * 4 : 0;
   static constexpr uint32_t BAR_OFF = CARRY_OFF + CARRY_BYTES;
   static constexpr uint32_t TMEM_COLS = 4 * BN;  // {upper, lower} x double buffer
   static constexpr size_t SMEM = (size_t)BAR_OFF + 256 + 1024;
@@ -735,97 +736,186 @@ __device__ __forceinline__ void epi_bar_sync() {
   asm volatile("bar.sync 1, 256;" ::: "memory");  // the 8 epilogue warps
 }
 
-// POOL epilogue of one tile, run by all 8 epilogue warps (e = 0..7; block
-// e >> 2, TMEM lane quadrant `quad`). Per 32-channel chunk: (1) each warp puts
-// its 32 accumulator rows, with bias and ReLU, into the staging tile, and the
-// row above / column left come in from the carries (zeros at the image's top
-// and left edges; positions past the conv result are staged as zeros); (2)
-// warp e computes pooled column e & 3 of pooled rows [8 (e >> 2), +8) of the
-// tile, one channel per lane, walking the window rows once and keeping each
-// row's maximum; (3) the carries take this tile's last column and last row.
-// ReLU results are >= 0 and never NaN, so the maximum is order-free and a
+// POOL epilogue of one tile, run by all 8 epilogue warps. Warp (blk, quad)
+// holds tile rows 4 G .. 4 G + 3, G = 4 blk + quad, as TMEM lanes 32 quad +
+// 8 yy + x. Per 32-channel chunk each warp reads its lanes with two 16x256b
+// loads, so thread t holds column x = t >> 2 of all four rows, channels
+// 8 q + 2 (t & 3) + {0, 1}, q = 0..3:
+//   vertical   centre rows yy = 0, 2 take rows yy - 1 .. yy + 1 from
+//              registers; row -1 is the last row of the warp above, passed
+//              through shared memory (the row carry for G = 0);
+//   horizontal centre columns x = 0, 2, 4, 6 take x +- 1 from threads t +- 4
+//              by shuffle; column -1 is the previous tile's column 7 (the
+//              column carry).
+// ReLU results are >= 0 and never NaN, so the maximum is order-free, and a
 // zero stands for window positions outside the conv result (a window always
 // holds its centre, so none is empty): the reference's first-then-strictly-
-// greater scan gives the same values. With the border in place every window
-// read is a fixed-offset shared load.
+// greater scan gives the same values. `parity` counts chunks (the exchange
+// buffer alternates).
 template <int BN>
-__device__ __forceinline__ void pool_tile(const ConvArgs& g, uint32_t tmem_base, int acc, int e,
-                                          int quad, int lane, float* ext, float* row_carry,
-                                          float* col_carry, int n, int y0, int x0) {
-  constexpr int S = kStageCols + 1;  // floats per staged pixel
-  const int blk = e >> 2, tid = e * 32 + lane;
-  const int pc = e & 3, half = e >> 2;  // this warp's pooled column and row half
-  // This lane's accumulator row as a tile pixel.
-  const int ly = blk * kHaloTH + (quad * 32 + lane) / kHaloTW, lx = (quad * 32 + lane) % kHaloTW;
-  const bool in_img = y0 + ly < g.OH && x0 + lx < g.OW;
-  for (int c0 = 0; c0 < BN && c0 < g.Cout; c0 += kStageCols) {
+__device__ __forceinline__ void pool_tile(const ConvArgs& g, uint32_t tmem_base, int acc, int blk,
+                                          int quad, int lane, float* xchg, float* row_carry,
+                                          float* col_carry, uint32_t& parity, int n, int y0,
+                                          int x0) {
+  constexpr int RS = BN + 8;  // row carry stride (floats per column)
+  const int G = 4 * blk + quad;
+  const int x = lane >> 2, cp = lane & 3;
+  const bool up = g.pph == 1, down = g.pkh - g.pph == 2;
+  const bool left = g.ppw == 1, right = g.pkw - g.ppw == 2;
+  const bool col_in = x0 + x < g.OW;
+  bool row_in[4];
+#pragma unroll
+  for (int yy = 0; yy < 4; ++yy) row_in[yy] = col_in && y0 + 4 * G + yy < g.OH;
+  const bool centre_x = (x & 1) == 0 && (x0 + x) / 2 < g.PW;
+  const int py0 = (y0 + 4 * G) / 2;  // pooled row of centre row yy = 0 (yy = 2: + 1)
+  const bool st0 = centre_x && py0 < g.PH, st2 = centre_x && py0 + 1 < g.PH;
+  float* const out0 = g.out + (((int64_t)n * g.PH + py0) * g.PW + (x0 + x) / 2) * g.Cout;
+  float* const out2 = out0 + (int64_t)g.PW * g.Cout;
+  const bool pair_ok = (g.Cout & 1) == 0 && ((((uintptr_t)g.out) & 7) == 0);
+  for (int c0 = 0; c0 < BN && c0 < g.Cout; c0 += 32) {
     const uint32_t taddr =
         tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * 2 + blk) * BN + c0;
-    float* srow = ext + ((ly + 1) * kPoolExtW + lx + 1) * S;
-    // Lane j holds bias[c0 + j]; column j's bias is broadcast by shuffle.
-    // (With no bias, adding +0 changes no ReLU result.)
-    const float bias_l = (g.bias && c0 + lane < g.Cout) ? g.bias[c0 + lane] : 0.0f;
-    uint32_t r[32];
+    uint32_t ra[16], rb[16];
     __syncwarp();  // tcgen05.ld is .sync.aligned: the warp must be converged
-    tc::tmem_ld16(taddr, *reinterpret_cast<uint32_t(*)[16]>(&r[0]));
-    tc::tmem_ld16(taddr + 16, *reinterpret_cast<uint32_t(*)[16]>(&r[16]));
+    tc::tmem_ld_16x256b_x4(taddr, ra);               // rows yy = 0, 1
+    tc::tmem_ld_16x256b_x4(taddr + (16u << 16), rb);  // rows yy = 2, 3
+    // Channel of value j = 2 q + h: c0 + 8 q + 2 cp + h.
+    float bj[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int ch = c0 + 8 * (j >> 1) + 2 * cp + (j & 1);
+      bj[j] = (g.bias && ch < g.Cout) ? __ldg(g.bias + ch) : 0.0f;
+    }
     tc::tmem_ld_wait();
+    float v[4][8];
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      const float v = __fadd_rn(__uint_as_float(r[j]), __shfl_sync(0xffffffffu, bias_l, j));
-      srow[j] = (in_img && v > 0.0f) ? v : 0.0f;
+    for (int j = 0; j < 8; ++j) {
+      const int q = j >> 1, h = j & 1;
+      const float a0 = __fadd_rn(__uint_as_float(ra[4 * q + h]), bj[j]);
+      const float a1 = __fadd_rn(__uint_as_float(ra[4 * q + 2 + h]), bj[j]);
+      const float a2 = __fadd_rn(__uint_as_float(rb[4 * q + h]), bj[j]);
+      const float a3 = __fadd_rn(__uint_as_float(rb[4 * q + 2 + h]), bj[j]);
+      v[0][j] = (row_in[0] && a0 > 0.0f) ? a0 : 0.0f;
+      v[1][j] = (row_in[1] && a1 > 0.0f) ? a1 : 0.0f;
+      v[2][j] = (row_in[2] && a2 > 0.0f) ? a2 : 0.0f;
+      v[3][j] = (row_in[3] && a3 > 0.0f) ? a3 : 0.0f;
     }
-    // Border: ext row 0 = the row above (row_carry, zeros for the first tile
-    // row), ext column 0 = the column left (col_carry, zeros for x0 == 0).
-    for (int idx = tid; idx < (kPoolExtW - 1 + kPoolExtH) * kStageCols; idx += 256) {
-      const int p = idx / kStageCols, cc = idx % kStageCols;
-      if (p < kPoolExtW - 1) {  // ext (0, p + 1): row y0 - 1, column x0 + p
-        ext[(p + 1) * S + cc] = y0 > 0 ? row_carry[(x0 + p) * BN + c0 + cc] : 0.0f;
-      } else {  // ext (q, 0): column x0 - 1, row y0 - 1 + q
-        const int q = p - (kPoolExtW - 1);
-        ext[q * kPoolExtW * S + cc] = (x0 > 0 && (q > 0 || y0 > 0)) ? col_carry[q * BN + c0 + cc] : 0.0f;
+    // Row -1 of group 0 is the row carry (zeros at the image's top edge);
+    // read before the barrier, after which group 7 overwrites it.
+    float above[8];
+    float* const xb = xchg + (parity & 1) * (8 * 8 * kPoolXStride);
+    float* const rc = row_carry + (x0 + x) * RS + c0 + 2 * cp;
+    if (G == 0) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 a = (up && y0 > 0 && col_in) ? *reinterpret_cast<const float2*>(rc + 8 * q)
+                                                  : make_float2(0.0f, 0.0f);
+        above[2 * q] = a.x;
+        above[2 * q + 1] = a.y;
       }
     }
-    epi_bar_sync();
-    // Pooled rows 8 half + k: window rows 2 (8 half + k) - pph + wy of the
-    // tile, i.e. ext rows 16 half - pph + 1 + 2 k + wy; columns 2 pc - ppw +
-    // wx, ext columns + 1.
-    const int co = c0 + lane;
-    const int px = (x0 >> 1) + pc;
-    const float* col0 = ext + ((16 * half - g.pph + 1) * kPoolExtW + 2 * pc - g.ppw + 1) * S + lane;
-    const int rows = 14 + g.pkh;
-    float h0 = 0.0f, h1 = 0.0f;  // maxima of the two previous window rows
+    if (G < 7) {
 #pragma unroll
-    for (int i = 0; i < 17; ++i) {
-      if (i >= rows) break;
-      const float* p = col0 + i * (kPoolExtW * S);
-      float m = p[0];
-      if (g.pkw > 1) m = fmaxf(m, p[S]);
-      if (g.pkw > 2) m = fmaxf(m, p[2 * S]);
-      const int k2 = i - g.pkh + 1;  // pooled row k = k2 / 2 ends at window row i
-      if (k2 >= 0 && (k2 & 1) == 0) {
-        float o = m;
-        if (g.pkh > 1) o = fmaxf(o, h1);
-        if (g.pkh > 2) o = fmaxf(o, h0);
-        const int py = (y0 >> 1) + 8 * half + (k2 >> 1);
-        if (py < g.PH && px < g.PW && co < g.Cout)
-          g.out[(((int64_t)n * g.PH + py) * g.PW + px) * g.Cout + co] = o;
+      for (int q = 0; q < 4; ++q)
+        *reinterpret_cast<float2*>(xb + ((G + 1) * 8 + x) * kPoolXStride + 8 * q + 2 * cp) =
+            make_float2(v[3][2 * q], v[3][2 * q + 1]);
+    }
+    epi_bar_sync();
+    if (G > 0) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 a =
+            *reinterpret_cast<const float2*>(xb + (G * 8 + x) * kPoolXStride + 8 * q + 2 * cp);
+        above[2 * q] = a.x;
+        above[2 * q + 1] = a.y;
       }
-      h0 = h1;
-      h1 = m;
     }
-    epi_bar_sync();
-    // Carries: column x0 + 7 (ext column 8, rows -1 .. 31) and row y0 + 31
-    // (ext row 32, columns 0 .. 7).
-    for (int idx = tid; idx < (kPoolExtH + kPoolExtW - 1) * kStageCols; idx += 256) {
-      const int p = idx / kStageCols, cc = idx % kStageCols;
-      if (p < kPoolExtH)
-        col_carry[p * BN + c0 + cc] = ext[(p * kPoolExtW + kPoolExtW - 1) * S + cc];
-      else
-        row_carry[(x0 + p - kPoolExtH) * BN + c0 + cc] =
-            ext[((kPoolExtH - 1) * kPoolExtW + p - kPoolExtH + 1) * S + cc];
+    // This tile's last row replaces the row carry for the tile row below
+    // (group 0 read the old one before the barrier).
+    if (G == 7 && col_in) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        *reinterpret_cast<float2*>(rc + 8 * q) = make_float2(v[3][2 * q], v[3][2 * q + 1]);
     }
-    epi_bar_sync();
+    // Vertical maxima of the two centre rows.
+    float m0[8], m2[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float a = v[0][j], b = v[2][j];
+      if (up) {
+        a = fmaxf(a, above[j]);
+        b = fmaxf(b, v[1][j]);
+      }
+      if (down) {
+        a = fmaxf(a, v[1][j]);
+        b = fmaxf(b, v[3][j]);
+      }
+      m0[j] = a;
+      m2[j] = b;
+    }
+    // Horizontal: columns x - 1 and x + 1 are threads t - 4 and t + 4;
+    // column -1 is the previous tile's column 7 (zeros at the left edge).
+    float* const cc = col_carry + (2 * G) * BN + c0 + 2 * cp;
+    float o0[8], o2[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float l0 = __shfl_up_sync(0xffffffffu, m0[j], 4);
+      const float l2 = __shfl_up_sync(0xffffffffu, m2[j], 4);
+      const float r0 = __shfl_down_sync(0xffffffffu, m0[j], 4);
+      const float r2 = __shfl_down_sync(0xffffffffu, m2[j], 4);
+      float a = m0[j], b = m2[j];
+      if (left && x > 0) {
+        a = fmaxf(a, l0);
+        b = fmaxf(b, l2);
+      }
+      if (right) {
+        a = fmaxf(a, r0);
+        b = fmaxf(b, r2);
+      }
+      o0[j] = a;
+      o2[j] = b;
+    }
+    if (left && x == 0 && x0 > 0) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int off = 8 * (j >> 1) + (j & 1);
+        o0[j] = fmaxf(o0[j], cc[off]);
+        o2[j] = fmaxf(o2[j], cc[BN + off]);
+      }
+    }
+    __syncwarp();  // column 0's carry reads precede column 7's writes
+    if (x == 7) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int off = 8 * (j >> 1) + (j & 1);
+        cc[off] = m0[j];
+        cc[BN + off] = m2[j];
+      }
+    }
+    // Pooled outputs: centre columns of centre rows, channel pairs.
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int ch = c0 + 8 * q + 2 * cp;
+      if (ch >= g.Cout) continue;
+      const bool pair = pair_ok && ch + 1 < g.Cout;
+      if (st0) {
+        if (pair) {
+          *reinterpret_cast<float2*>(out0 + ch) = make_float2(o0[2 * q], o0[2 * q + 1]);
+        } else {
+          out0[ch] = o0[2 * q];
+          if (ch + 1 < g.Cout) out0[ch + 1] = o0[2 * q + 1];
+        }
+      }
+      if (st2) {
+        if (pair) {
+          *reinterpret_cast<float2*>(out2 + ch) = make_float2(o2[2 * q], o2[2 * q + 1]);
+        } else {
+          out2[ch] = o2[2 * q];
+          if (ch + 1 < g.Cout) out2[ch + 1] = o2[2 * q + 1];
+        }
+      }
+    }
+    ++parity;
   }
 }
 
@@ -1051,7 +1141,8 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
     const bool bias_vec = g.bias && ((((uintptr_t)g.bias) & 15) == 0);
     const int64_t OHW = (int64_t)g.OH * g.OW;
     float* row_carry = reinterpret_cast<float*>(smem + Cfg::CARRY_OFF);
-    float* col_carry = row_carry + kPoolMaxOW * BN;
+    float* col_carry = row_carry + kPoolMaxOW * Cfg::ROW_CARRY_STRIDE;
+    uint32_t parity = 0;  // POOL: exchange-buffer alternation
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     for (int64_t local = 0;; ++local) {
       const int64_t t = halo_tile<POOL>(g, local);
@@ -1073,7 +1164,7 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
       }
       tc::tc_fence_after();
       if (POOL) {
-        pool_tile<BN>(g, tmem_base, acc, e, quad, lane, epi, row_carry, col_carry, n,
+        pool_tile<BN>(g, tmem_base, acc, blk, quad, lane, epi, row_carry, col_carry, parity, n,
                       (rem / g.tiles_x) * 2 * kHaloTH, (rem % g.tiles_x) * kHaloTW);
       } else {
         store_tile<BN>(g, tmem_base, (uint32_t)(acc * 2 + blk) * BN, nt, quad, 0, kStageCols, lane,
@@ -1247,6 +1338,60 @@ __global__ void __launch_bounds__(256) s2d_input_kernel(const float* __restrict_
       }
       dst[k4] = make_float4(v[0], v[1], v[2], v[3]);
     }
+  }
+}
+
+// The same rewrite for an NCHW input, one output row (n, i) per block: the
+// block stages input rows 2 i and 2 i + 1 of every channel in shared memory
+// with coalesced loads (16-byte ones when VEC: W and the strides a multiple of
+// 4 floats, an aligned base), then writes the row's W2 x C2 floats as
+// consecutive 16-byte stores. A thread's float4 index inside a pixel is fixed
+// (the block size is a multiple of C2 / 4), so its channel sources are too.
+template <int C2, bool VEC>
+__global__ void __launch_bounds__(128) s2d_rows_kernel(const float* __restrict__ x,
+                                                       float* __restrict__ out, int C, int H, int W,
+                                                       int H2, int W2, int64_t xs_n, int64_t xs_c,
+                                                       int64_t xs_h) {
+  extern __shared__ float rows[];  // [2 C][W]: row 2 c + dy = channel c, input row 2 i + dy
+  const int64_t row = blockIdx.x;  // n H2 + i
+  const int n = (int)(row / H2), i = (int)(row - (int64_t)n * H2);
+  const float* src = x + n * xs_n;
+  if (VEC) {
+    const int W4 = W >> 2;
+    for (int idx = threadIdx.x; idx < 2 * C * W4; idx += blockDim.x) {
+      const int rr = idx / W4, x4 = idx - rr * W4;
+      const int y = 2 * i + (rr & 1);
+      const float4 v = y < H ? __ldg(reinterpret_cast<const float4*>(src + (rr >> 1) * xs_c +
+                                                                       (int64_t)y * xs_h) + x4)
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
+      reinterpret_cast<float4*>(rows + rr * W)[x4] = v;
+    }
+  } else {
+    for (int idx = threadIdx.x; idx < 2 * C * W; idx += blockDim.x) {
+      const int rr = idx / W, xx = idx - rr * W;
+      const int y = 2 * i + (rr & 1);
+      rows[idx] = y < H ? __ldg(src + (rr >> 1) * xs_c + (int64_t)y * xs_h + xx) : 0.0f;
+    }
+  }
+  __syncthreads();
+  constexpr int P4 = C2 / 4;  // float4s per pixel
+  const int k4 = threadIdx.x % P4;
+  int off[4], dx[4];
+  bool used[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const int cc = 4 * k4 + e, q = cc / C, c = cc - q * C;
+    used[e] = q < 4;
+    dx[e] = q & 1;
+    off[e] = (2 * c + (q >> 1)) * W + dx[e];
+  }
+  float4* dst = reinterpret_cast<float4*>(out + row * W2 * C2);
+  for (int idx = threadIdx.x; idx < W2 * P4; idx += blockDim.x) {
+    const int j = idx / P4;
+    float v[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) v[e] = (used[e] && 2 * j + dx[e] < W) ? rows[off[e] + 2 * j] : 0.0f;
+    dst[idx] = make_float4(v[0], v[1], v[2], v[3]);
   }
 }
 
@@ -1547,12 +1692,15 @@ void conv_impl(Tensor* input, Tensor* weight, Tensor* bias, Tensor* residual, Te
   S2dPlan s2d;
   const int C2 = 4 * C <= 16 ? 16 : BK;  // stored s2d channels: 64- or 128-byte pixel rows
   // Fused pooling: one channel tile (C_out <= 64), a conv row that fits the
-  // row carry, a channels-last pooled output, and a stride-2 window reaching
-  // at most one row/column before its tile and none past it.
-  const bool pool_fused = pool && C2 == 16 && Cout <= 64 && OW <= kPoolMaxOW && is_nhwc(output) &&
-                          pool->sh == 2 && pool->sw == 2 && pool->ph >= 0 && pool->pw >= 0 &&
-                          pool->ph <= 1 && pool->pw <= 1 && pool->kh - pool->ph <= 2 &&
-                          pool->kw - pool->pw <= 2;
+  // row carry, a channels-last pooled output, and stride-2 windows that hold
+  // their centre (2 py, 2 px) inside the conv result and reach at most one
+  // row/column before and after it.
+  const bool pool_fused =
+      pool && C2 == 16 && Cout <= 64 && OW <= kPoolMaxOW && is_nhwc(output) && pool->sh == 2 &&
+      pool->sw == 2 && pool->ph >= 0 && pool->pw >= 0 && pool->ph <= 1 && pool->pw <= 1 &&
+      pool->kh > pool->ph && pool->kw > pool->pw && pool->kh - pool->ph <= 2 &&
+      pool->kw - pool->pw <= 2 && 2 * ((int)output->shape[2] - 1) < OH &&
+      2 * ((int)output->shape[3] - 1) < OW;
   if (!split && (!pool || pool_fused) && s2d_plan(C, KH, KW, sh, sw, ph, pw, &s2d) &&
       halo_eligible(C2, Cout, s2d.KH2, s2d.KW2, 1, 1, s2d.pad_h, s2d.pad_w, OH, OW, split, C2)) {
     const int H2 = (H + 1) / 2, W2 = (W + 1) / 2;
@@ -1566,14 +1714,33 @@ void conv_impl(Tensor* input, Tensor* weight, Tensor* bias, Tensor* residual, Te
       const bool in_nhwc = is_nhwc(input);
       const int64_t sx_c = in_nhwc ? 1 : (int64_t)H * W, sx_h = in_nhwc ? (int64_t)W * C : W,
                     sx_w = in_nhwc ? C : 1;
-      if (C2 == 16)
+      const size_t rows_smem = (size_t)2 * C * W * 4;
+      if (!in_nhwc && rows_smem <= 48 * 1024) {
+        const bool vec = W % 4 == 0 && (((uintptr_t)input->data) & 15) == 0;
+        const float* xin = (const float*)input->data;
+        const int64_t xs_n = (int64_t)H * W * C;
+        const unsigned blocks = (unsigned)((int64_t)N * H2);
+        if (C2 == 16 && vec)
+          s2d_rows_kernel<16, true><<<blocks, 128, rows_smem, ctx().stream>>>(
+              xin, xs2, C, H, W, H2, W2, xs_n, sx_c, sx_h);
+        else if (C2 == 16)
+          s2d_rows_kernel<16, false><<<blocks, 128, rows_smem, ctx().stream>>>(
+              xin, xs2, C, H, W, H2, W2, xs_n, sx_c, sx_h);
+        else if (vec)
+          s2d_rows_kernel<BK, true><<<blocks, 128, rows_smem, ctx().stream>>>(
+              xin, xs2, C, H, W, H2, W2, xs_n, sx_c, sx_h);
+        else
+          s2d_rows_kernel<BK, false><<<blocks, 128, rows_smem, ctx().stream>>>(
+              xin, xs2, C, H, W, H2, W2, xs_n, sx_c, sx_h);
+      } else if (C2 == 16) {
         s2d_input_kernel<16><<<grid_for(x2 / C2, 256, 8), 256, 0, ctx().stream>>>(
             (const float*)input->data, xs2, N, C, H, W, H2, W2, (int64_t)H * W * C, sx_c, sx_h,
             sx_w);
-      else
+      } else {
         s2d_input_kernel<BK><<<grid_for(x2 / C2, 256, 8), 256, 0, ctx().stream>>>(
             (const float*)input->data, xs2, N, C, H, W, H2, W2, (int64_t)H * W * C, sx_c, sx_h,
             sx_w);
+      }
       if (!check_launch(op)) return;
       const int src_mode = packed ? (wl.element ? 2 : 1) : 0;
       s2d_weight_kernel<<<grid_for(w2, 256, 8), 256, 0, ctx().stream>>>(
@@ -1614,7 +1781,7 @@ void conv_impl(Tensor* input, Tensor* weight, Tensor* bias, Tensor* residual, Te
         g.psw = pool->sw;
         g.pph = pool->ph;
         g.ppw = pool->pw;
-        launch_halo<64, 8, 2, 16, true>(g, wts2, op);
+        launch_halo<64, 8, 3, 16, true>(g, wts2, op);
         return;
       } else if (C2 == 16) {
         if (Cout > 64)

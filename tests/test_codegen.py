@@ -62,18 +62,20 @@ def test_o3_fuses_every_residual_join(tmp_path):
     assert calls.count("nnc_conv_add_relu3x3_s1") == 8
     assert "nnc_add" not in calls and "nnc_relu" not in calls and "nnc_add_relu" not in calls
     assert calls.count("nnc_conv_relu3x3_s1") + calls.count("nnc_conv_relu") == 8
-    assert calls[0] == "nnc_conv_relu7x7_s2" and calls[-1] == "nnc_gemm_nt"
+    assert calls[0] == "nnc_conv_relu_maxpool" and calls[-1] == "nnc_gemm_nt"
 
 
 def test_o3_conv_relu_maxpool_group(tmp_path):
-    """With the group enabled, the stem's Conv+ReLU -> MaxPool is one call
-    carrying the conv extent and the pool geometry; its conv result never
-    exists in the arena."""
-    man = CG.compile_model(W.resnet18(2), tmp_path, opt_level=3, fuse_conv_relu_maxpool=True)
+    """The stem's Conv+ReLU -> MaxPool is one call carrying the conv extent
+    and the pool geometry (its conv result never exists in the arena); with
+    the group disabled the two calls come back."""
+    man = CG.compile_model(W.resnet18(2), tmp_path, opt_level=3)
     calls = man["calls"]
     assert calls[0] == "nnc_conv_relu_maxpool" and "nnc_maxpool2d" not in calls
     line = next(l for l in (tmp_path / "model.c").read_text().splitlines() if "nnc_conv_relu_maxpool(" in l)
     assert line.strip().endswith("7, 7, 2, 2, 3, 3, 112, 112, 3, 3, 2, 2, 1, 1);")
+    off = CG.compile_model(W.resnet18(2), tmp_path / "off", opt_level=3, fuse_conv_relu_maxpool=False)
+    assert off["calls"][:2] == ["nnc_conv_relu7x7_s2", "nnc_maxpool2d"]
 
 
 def test_channels_last_assignment(tmp_path):

@@ -269,6 +269,12 @@ POOL_CASES = [
     (2, 3, 64, 64, 48, 7, 2, 3, (2, 2, 0)),
     (2, 8, 40, 40, 64, 3, 2, 1, (3, 2, 1)),
     (2, 16, 20, 20, 32, 3, 1, 1, (3, 2, 1)),
+    # 2x2 windows with a top/left pad: centres inside (fused), and a last
+    # centre past the conv result (the conv + pool composition).
+    (1, 3, 62, 62, 64, 7, 2, 3, (2, 2, 1)),
+    (1, 3, 64, 64, 64, 7, 2, 3, (2, 2, 1)),
+    # More images than SMs: CTAs walk several images (carries reset at each).
+    (150, 3, 56, 56, 64, 7, 2, 3, (3, 2, 1)),
 ]
 
 
