@@ -104,8 +104,23 @@ struct ConvArgs {
   float* out;
   int out_nhwc;
   int act;
+  int direct_epi;  // channels-last epilogues store from TMEM fragments (store_tile's `direct`)
   int* err;
 };
+
+// Output-channel order of packed conv weights. When C_out is a multiple of
+// 32, packed row 32 g + j holds channel 32 g + perm_col(j): the accumulator's
+// TMEM column j then holds that channel, and a 16x256b TMEM load (thread t:
+// columns 8 q + 2 (t & 3) + {0, 1}, q = 0..3) hands thread t channels
+// 4 (t & 3) + {0..3} and 16 + 4 (t & 3) + {0..3}: two 16-byte runs, so four
+// threads cover 64 contiguous bytes of a pixel and the epilogue's global
+// accesses are 16 bytes wide. Column j = 8 q + 2 c + h -> 16 (q >> 1) + 4 c +
+// 2 (q & 1) + h (a bijection of 0..31).
+__host__ __device__ __forceinline__ int perm_col(int j) {
+  const int q = j >> 3, c = (j >> 1) & 3, h = j & 1;
+  return 16 * (q >> 1) + 4 * c + 2 * (q & 1) + h;
+}
+__host__ __device__ __forceinline__ bool perm_rows(int cout) { return cout % 32 == 0; }
 
 __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
   return (uint8_t*)(((uintptr_t)p + 1023) & ~(uintptr_t)1023);
@@ -152,23 +167,124 @@ __device__ __forceinline__ float activate(float o, int act) {
 // (the hardware's lane-quadrant rule) of the BN-column accumulator at TMEM
 // column acc_col, 32-column chunks c0 = c_first, c_first + c_step, ... below
 // BN. rows(r) maps accumulator row r (0..127) to its output pixel
-// m = (n, oh, ow), or -1 when the row is padding.
-template <int BN, class RowMap>
+// m = (n, oh, ow), or -1 when the row is padding. Column j of a chunk holds
+// channel perm_col(j) when C_out is a multiple of 32 (the packed weights'
+// row order), else channel j.
+//
+// `direct` (channels-last, C_out a multiple of 32, 16-byte aligned output
+// and residual): a 16x256b TMEM load of 16 columns of one 16-lane half gives
+// thread t rows (t >> 2) + 16 hb + 8 k, k = 0, 1, at channels 16 u +
+// 4 (t & 3) + {0..3}; each run is stored (and its residual loaded) as one
+// 16-byte access, four threads covering 64 contiguous bytes of a pixel. This
+// path uses no shared memory and no shuffles, which the tensor pipe's operand
+// reads starve while the next tile's MMAs run (measured under N = 64 MMAs: an
+// 8 KB warp tile staged through shared memory takes ~12k cycles, stored from
+// the fragments 2-4k). Otherwise the chunk is staged through a 32 x 33 shared
+// tile and written row-contiguously (NHWC), or per channel plane (NCHW).
+// DIRECT_CODE compiles the direct path in (the halo kernel; the im2col
+// kernel's 13 warps leave it 128 registers per thread, too few for it).
+template <int BN, bool DIRECT_CODE, class RowMap>
 __device__ __forceinline__ void store_tile(const ConvArgs& g, uint32_t tmem_base, uint32_t acc_col,
                                            int nt, int quad, int c_first, int c_step, int lane,
                                            float* stage_tile, bool vec_ok, bool bias_vec,
-                                           const RowMap& rows) {
+                                           const RowMap& rows, bool direct) {
   const int64_t OHW = (int64_t)g.OH * g.OW;
+  const bool perm = perm_rows(g.Cout);
+  if (DIRECT_CODE && g.out_nhwc && direct) {
+    const bool add = g.act == kActAddRelu;
+    const bool relu = add || g.act == kActRelu;
+#pragma unroll 1
+    for (int c0 = c_first; c0 < BN; c0 += c_step) {
+      const int co0 = nt * BN + c0;
+      if (co0 >= g.Cout) continue;  // warp-uniform; C_out % 32 == 0: whole chunks
+      const int cb = co0 + 4 * (lane & 3);  // channels cb + 16 u + {0..3}, u = 0, 1
+      int64_t m[4];  // rows (t >> 2) + 8 k
+#pragma unroll
+      for (int k = 0; k < 4; ++k) m[k] = rows(quad * 32 + (lane >> 2) + 8 * k);
+      // The chunk's residual runs and its four TMEM loads are all in flight
+      // before the one wait: one memory round trip per chunk.
+      float4 rv[4][2];
+      if (add) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+#pragma unroll
+          for (int u = 0; u < 2; ++u)
+            rv[k][u] = m[k] >= 0
+                           ? __ldg(reinterpret_cast<const float4*>(g.residual + m[k] * g.Cout + cb + 16 * u))
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+      uint32_t r[4][8];  // [2 hb + u]: 16 columns c0 + 16 u of lanes + 16 hb
+      __syncwarp();      // tcgen05.ld is .sync.aligned: the warp must be converged
+#pragma unroll
+      for (int hb = 0; hb < 2; ++hb)
+#pragma unroll
+        for (int u = 0; u < 2; ++u)
+          tc::tmem_ld_16x256b_x2(
+              tmem_base + ((uint32_t)(quad * 32 + 16 * hb) << 16) + acc_col + c0 + 16 * u,
+              r[2 * hb + u]);
+      float4 bv[2];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        bv[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (g.bias) {
+          const float* bp = g.bias + cb + 16 * u;
+          bv[u] = bias_vec ? __ldg(reinterpret_cast<const float4*>(bp))
+                           : make_float4(__ldg(bp), __ldg(bp + 1), __ldg(bp + 2), __ldg(bp + 3));
+        }
+      }
+      tc::tmem_ld_wait();
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        if (m[k] < 0) continue;
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          // Row k is lane (t >> 2) + 8 (k & 1) of half k >> 1: registers
+          // 2 (k & 1) + {0, 1} (columns 2 c + {0, 1}) and 4 + 2 (k & 1) + {0, 1}
+          // (columns 8 + 2 c + {0, 1}) of load 2 (k >> 1) + u.
+          const uint32_t* q = r[2 * (k >> 1) + u];
+          const int i = 2 * (k & 1);
+          float4 o = make_float4(__fadd_rn(__uint_as_float(q[i]), bv[u].x),
+                                 __fadd_rn(__uint_as_float(q[i + 1]), bv[u].y),
+                                 __fadd_rn(__uint_as_float(q[4 + i]), bv[u].z),
+                                 __fadd_rn(__uint_as_float(q[4 + i + 1]), bv[u].w));
+          if (add) {
+            o.x = __fadd_rn(o.x, rv[k][u].x);
+            o.y = __fadd_rn(o.y, rv[k][u].y);
+            o.z = __fadd_rn(o.z, rv[k][u].z);
+            o.w = __fadd_rn(o.w, rv[k][u].w);
+          }
+          if (relu) {
+            o.x = o.x > 0.0f ? o.x : 0.0f;
+            o.y = o.y > 0.0f ? o.y : 0.0f;
+            o.z = o.z > 0.0f ? o.z : 0.0f;
+            o.w = o.w > 0.0f ? o.w : 0.0f;
+          } else {
+            o.x = activate(o.x, g.act);
+            o.y = activate(o.y, g.act);
+            o.z = activate(o.z, g.act);
+            o.w = activate(o.w, g.act);
+          }
+          *reinterpret_cast<float4*>(g.out + m[k] * g.Cout + cb + 16 * u) = o;
+        }
+      }
+    }
+    return;
+  }
 #pragma unroll 1
   for (int c0 = c_first; c0 < BN; c0 += c_step) {
     const int co0 = nt * BN + c0;
     if (co0 >= g.Cout) continue;  // warp-uniform: no TMEM load is skipped by part of a warp
     const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + acc_col + c0;
     if (g.out_nhwc) {
-      // Stage the 32 x 32 block, then write it row-contiguously: eight
-      // lanes cover one 128-byte row segment, a warp four rows.
-      const int cl = (lane & 7) * 4;  // column within the block
+      // Stage the 32 x 32 block, then write it row-contiguously: eight lanes
+      // cover one 128-byte row segment (channels co .. co + 3), a warp four
+      // rows. Channels cl + {0, 1} and cl + {2, 3} sit at staged columns
+      // sa + {0, 1} and sb + {0, 1} (perm_col inverted: 16 u + 2 c and + 8,
+      // cl = 16 u + 4 c).
+      const int cl = (lane & 7) * 4;  // channel offset within the block
       const int co = co0 + cl;
+      const int sa = perm ? 16 * ((lane & 7) >> 2) + 2 * (lane & 3) : cl;
+      const int sb = perm ? sa + 8 : cl + 2;
       // 16-byte row accesses need C_out % 4 == 0 and aligned bases
       // (vec_ok); otherwise the per-element path below is taken.
       const bool col_ok = vec_ok && co + 3 < g.Cout;
@@ -216,9 +332,9 @@ __device__ __forceinline__ void store_tile(const ConvArgs& g, uint32_t tmem_base
           const int rr = (lane >> 3) + 4 * it;
           const int64_t m = rows(quad * 32 + rr);
           if (m < 0) continue;
-          const float* srow = stage_tile + rr * (kStageCols + 1) + cl;
-          float4 o = make_float4(__fadd_rn(srow[0], bv.x), __fadd_rn(srow[1], bv.y),
-                                 __fadd_rn(srow[2], bv.z), __fadd_rn(srow[3], bv.w));
+          const float* srow = stage_tile + rr * (kStageCols + 1);
+          float4 o = make_float4(__fadd_rn(srow[sa], bv.x), __fadd_rn(srow[sa + 1], bv.y),
+                                 __fadd_rn(srow[sb], bv.z), __fadd_rn(srow[sb + 1], bv.w));
           if (add) {
             o.x = __fadd_rn(o.x, rv[it].x);
             o.y = __fadd_rn(o.y, rv[it].y);
@@ -245,10 +361,10 @@ __device__ __forceinline__ void store_tile(const ConvArgs& g, uint32_t tmem_base
           const int rr = (lane >> 3) + 4 * it;
           const int64_t m = rows(quad * 32 + rr);
           if (m < 0) continue;
-          const float* srow = stage_tile + rr * (kStageCols + 1) + cl;
+          const float* srow = stage_tile + rr * (kStageCols + 1);
           const float bq[4] = {bv.x, bv.y, bv.z, bv.w};
           for (int q = 0; q < 4 && co + q < g.Cout; ++q) {
-            float v = __fadd_rn(srow[q], bq[q]);
+            float v = __fadd_rn(srow[q < 2 ? sa + q : sb + q - 2], bq[q]);
             if (g.act == kActAddRelu) v = __fadd_rn(v, g.residual[m * g.Cout + co + q]);
             g.out[m * g.Cout + co + q] = activate(v, g.act);
           }
@@ -256,7 +372,7 @@ __device__ __forceinline__ void store_tile(const ConvArgs& g, uint32_t tmem_base
       }
       __syncwarp();
     } else {
-      // NCHW: channel co of image n at plane offset p; lanes hold
+      // NCHW: channel c of image n at plane offset p; lanes hold
       // consecutive pixels, so each store instruction is coalesced.
       const int64_t m = rows(quad * 32 + lane);
       const int64_t n_img = m / OHW, p = m - n_img * OHW;
@@ -267,16 +383,15 @@ __device__ __forceinline__ void store_tile(const ConvArgs& g, uint32_t tmem_base
         tc::tmem_ld16(taddr + 16 * h16, r);
         tc::tmem_ld_wait();
         if (m >= 0) {
-          const int cb = co0 + 16 * h16;
-          float* dst = g.out + (n_img * g.Cout + cb) * OHW + p;
-          const float* res = g.residual ? g.residual + (n_img * g.Cout + cb) * OHW + p : nullptr;
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
-            if (cb + j >= g.Cout) break;
+            const int c = co0 + (perm ? perm_col(16 * h16 + j) : 16 * h16 + j);
+            if (c >= g.Cout) break;  // (unpermuted chunks end at the last channel)
             float o = __uint_as_float(r[j]);
-            if (g.bias) o = __fadd_rn(o, g.bias[cb + j]);
-            if (g.act == kActAddRelu) o = __fadd_rn(o, res[(int64_t)j * OHW]);
-            dst[(int64_t)j * OHW] = activate(o, g.act);
+            if (g.bias) o = __fadd_rn(o, g.bias[c]);
+            const int64_t off = (n_img * g.Cout + c) * OHW + p;
+            if (g.act == kActAddRelu) o = __fadd_rn(o, g.residual[off]);
+            g.out[off] = activate(o, g.act);
           }
         }
       }
@@ -639,6 +754,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
     const bool vec_ok = (g.Cout % 4 == 0) && ((((uintptr_t)g.out) & 15) == 0) &&
                         (!g.residual || ((((uintptr_t)g.residual) & 15) == 0));
     const bool bias_vec = g.bias && ((((uintptr_t)g.bias) & 15) == 0);
+    const bool direct = vec_ok && perm_rows(g.Cout) && g.direct_epi;
     int local = 0;
     for (int64_t t = blockIdx.x; t < g.tiles; t += gridDim.x, ++local) {
       const int mt = (int)(t / g.n_tiles), nt = (int)(t % g.n_tiles);
@@ -646,8 +762,9 @@ __global__ void __launch_bounds__(kConvThreads, 1)
       const uint32_t aphase = (local >> 1) & 1;
       if (!tc::mbar_wait(&tfull[acc], aphase, g.err)) break;
       tc::tc_fence_after();
-      store_tile<BN>(g, tmem_base, acc * BN, nt, quad, half * kStageCols, 2 * kStageCols, lane,
-                     stage_tile, vec_ok, bias_vec, LinearRows{(int64_t)mt * BM, g.M});
+      store_tile<BN, false>(g, tmem_base, acc * BN, nt, quad, half * kStageCols, 2 * kStageCols,
+                            lane,
+                     stage_tile, vec_ok, bias_vec, LinearRows{(int64_t)mt * BM, g.M}, direct);
       tc::tc_fence_before();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&tempty[acc]);
@@ -771,7 +888,9 @@ __device__ __forceinline__ void pool_tile(const ConvArgs& g, uint32_t tmem_base,
   const bool st0 = centre_x && py0 < g.PH, st2 = centre_x && py0 + 1 < g.PH;
   float* const out0 = g.out + (((int64_t)n * g.PH + py0) * g.PW + (x0 + x) / 2) * g.Cout;
   float* const out2 = out0 + (int64_t)g.PW * g.Cout;
+  const bool perm = perm_rows(g.Cout);
   const bool pair_ok = (g.Cout & 1) == 0 && ((((uintptr_t)g.out) & 7) == 0);
+  const bool quad_ok = perm && ((((uintptr_t)g.out) & 15) == 0);
   for (int c0 = 0; c0 < BN && c0 < g.Cout; c0 += 32) {
     const uint32_t taddr =
         tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * 2 + blk) * BN + c0;
@@ -779,11 +898,12 @@ __device__ __forceinline__ void pool_tile(const ConvArgs& g, uint32_t tmem_base,
     __syncwarp();  // tcgen05.ld is .sync.aligned: the warp must be converged
     tc::tmem_ld_16x256b_x4(taddr, ra);               // rows yy = 0, 1
     tc::tmem_ld_16x256b_x4(taddr + (16u << 16), rb);  // rows yy = 2, 3
-    // Channel of value j = 2 q + h: c0 + 8 q + 2 cp + h.
+    // Value j = 2 q + h is TMEM column 8 q + 2 cp + h of the chunk.
     float bj[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      const int ch = c0 + 8 * (j >> 1) + 2 * cp + (j & 1);
+      const int col = 8 * (j >> 1) + 2 * cp + (j & 1);
+      const int ch = c0 + (perm ? perm_col(col) : col);
       bj[j] = (g.bias && ch < g.Cout) ? __ldg(g.bias + ch) : 0.0f;
     }
     tc::tmem_ld_wait();
@@ -892,10 +1012,26 @@ __device__ __forceinline__ void pool_tile(const ConvArgs& g, uint32_t tmem_base,
         cc[BN + off] = m2[j];
       }
     }
-    // Pooled outputs: centre columns of centre rows, channel pairs.
+    // Pooled outputs: centre columns of centre rows. Permuted channels give
+    // this thread c0 + 16 u + 4 cp + {0..3} (values 4 u .. 4 u + 3): 16-byte
+    // stores; otherwise channel pairs c0 + 8 q + 2 cp + {0, 1}.
+    if (quad_ok) {
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int ch = c0 + 16 * u + 4 * cp;
+        if (st0)
+          *reinterpret_cast<float4*>(out0 + ch) =
+              make_float4(o0[4 * u], o0[4 * u + 1], o0[4 * u + 2], o0[4 * u + 3]);
+        if (st2)
+          *reinterpret_cast<float4*>(out2 + ch) =
+              make_float4(o2[4 * u], o2[4 * u + 1], o2[4 * u + 2], o2[4 * u + 3]);
+      }
+      ++parity;
+      continue;
+    }
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
-      const int ch = c0 + 8 * q + 2 * cp;
+      const int ch = c0 + (perm ? perm_col(8 * q + 2 * cp) : 8 * q + 2 * cp);
       if (ch >= g.Cout) continue;
       const bool pair = pair_ok && ch + 1 < g.Cout;
       if (st0) {
@@ -1139,6 +1275,7 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
     const bool vec_ok = (g.Cout % 4 == 0) && ((((uintptr_t)g.out) & 15) == 0) &&
                         (!g.residual || ((((uintptr_t)g.residual) & 15) == 0));
     const bool bias_vec = g.bias && ((((uintptr_t)g.bias) & 15) == 0);
+    const bool direct = vec_ok && perm_rows(g.Cout) && g.direct_epi;
     const int64_t OHW = (int64_t)g.OH * g.OW;
     float* row_carry = reinterpret_cast<float*>(smem + Cfg::CARRY_OFF);
     float* col_carry = row_carry + kPoolMaxOW * Cfg::ROW_CARRY_STRIDE;
@@ -1167,10 +1304,11 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
         pool_tile<BN>(g, tmem_base, acc, blk, quad, lane, epi, row_carry, col_carry, parity, n,
                       (rem / g.tiles_x) * 2 * kHaloTH, (rem % g.tiles_x) * kHaloTW);
       } else {
-        store_tile<BN>(g, tmem_base, (uint32_t)(acc * 2 + blk) * BN, nt, quad, 0, kStageCols, lane,
+        store_tile<BN, true>(g, tmem_base, (uint32_t)(acc * 2 + blk) * BN, nt, quad, 0, kStageCols, lane,
                        stage_tile, vec_ok, bias_vec,
                        BlockRows{(int64_t)n * OHW, (rem / g.tiles_x) * 2 * kHaloTH + blk * kHaloTH,
-                                 (rem % g.tiles_x) * kHaloTW, g.OH, g.OW});
+                                 (rem % g.tiles_x) * kHaloTW, g.OH, g.OW},
+                       direct);
       }
       tc::tc_fence_before();
       __syncwarp();
@@ -1188,10 +1326,11 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
 
 // ------------------------------------------------------ layout kernels ----
 
-// OIHW -> [plane][Cout][K_pad], zero padded. Chunk mode: k = (kh*KW + kw)*C4
-// + ci (C4 = channels padded to 32); element mode: k = (ci*KH + kh)*KW + kw,
-// the OIHW order itself. split: plane 0 = tf32(w), plane 1 = w - tf32(w);
-// else plane 0 = w.
+// OIHW -> [plane][Cout][K_pad], zero padded, rows in perm_col order when
+// C_out is a multiple of 32. Chunk mode: k = (kh*KW + kw)*C4 + ci (C4 =
+// channels padded to 32); element mode: k = (ci*KH + kh)*KW + kw, the OIHW
+// order itself. split: plane 0 = tf32(w), plane 1 = w - tf32(w); else plane
+// 0 = w.
 __global__ void __launch_bounds__(256) pack_weight_kernel(const float* __restrict__ w,
                                                           float* __restrict__ out, int Cout,
                                                           int Cin, int KH, int KW, int C4,
@@ -1200,7 +1339,8 @@ __global__ void __launch_bounds__(256) pack_weight_kernel(const float* __restric
   const int Kw = Cin * KH * KW;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
-    const int co = (int)(i / Kpad), k = (int)(i % Kpad);
+    const int r = (int)(i / Kpad), k = (int)(i % Kpad);
+    const int co = perm_rows(Cout) ? (r & ~31) + perm_col(r & 31) : r;
     float v = 0.0f;
     if (element) {
       if (k < Kw) v = w[(int64_t)co * Kw + k];
@@ -1397,8 +1537,9 @@ __global__ void __launch_bounds__(128) s2d_rows_kernel(const float* __restrict__
 
 // Space-to-depth weights: [C_out][KH2][KW2][C2] in the halo kernel's k order,
 // W'[co, kh2, kw2, q C + c] = W[co, c, 2 (kh2 - pad_h) + dy + ph,
-// 2 (kw2 - pad_w) + dx + pw] inside the original window, else zero. The
-// source is the OIHW weight, or a prepacked one (chunk or element k order).
+// 2 (kw2 - pad_w) + dx + pw] inside the original window, else zero; rows in
+// perm_col order like every packed weight. The source is the OIHW weight, or
+// a prepacked one (chunk or element k order).
 __global__ void __launch_bounds__(256) s2d_weight_kernel(const float* __restrict__ w,
                                                          float* __restrict__ out, int Cout, int C,
                                                          int KH, int KW, int ph, int pw, int KH2,
@@ -1415,8 +1556,10 @@ __global__ void __launch_bounds__(256) s2d_weight_kernel(const float* __restrict
     const int kh = 2 * (kh2 - pad_h) + (q >> 1) + ph, kw = 2 * (kw2 - pad_w) + (q & 1) + pw;
     float v = 0.0f;
     if (q < 4 && kh >= 0 && kh < KH && kw >= 0 && kw < KW) {
+      // Row co holds channel perm_col order (a prepacked source row already does).
+      const int ch = perm_rows(Cout) ? (co & ~31) + perm_col(co & 31) : co;
       if (src_mode == 0)  // OIHW
-        v = w[(((int64_t)co * C + c) * KH + kh) * KW + kw];
+        v = w[(((int64_t)ch * C + c) * KH + kh) * KW + kw];
       else if (src_mode == 1)  // prepacked, chunk order k = (kh KW + kw) C4 + c
         v = w[(int64_t)co * src_kpad + (kh * KW + kw) * src_c4 + c];
       else  // prepacked, element order k = (c KH + kh) KW + kw
@@ -1451,6 +1594,17 @@ WeightLayout weight_layout(int Cin, int KH, int KW) {
     L.Kpad = (int)cdiv(L.K, BK) * BK;
   }
   return L;
+}
+
+// Whether channels-last epilogues store straight from TMEM fragments (the
+// default); NNC_CUDA_CONV_DIRECT_EPI=0 selects the shared-memory staged
+// stores (for comparison).
+static bool direct_epilogue() {
+  static const bool on = [] {
+    const char* e = getenv("NNC_CUDA_CONV_DIRECT_EPI");
+    return !(e && e[0] == '0');
+  }();
+  return on;
 }
 
 template <int BN, int SPLIT, int STAGES>
@@ -1496,6 +1650,7 @@ bool launch_conv(ConvArgs g, const float* w0, const float* w1, const char* op) {
     attr_set[ctx().device] = true;
   }
   const int grid = (int)(g.tiles < sm_count() ? g.tiles : sm_count());
+  g.direct_epi = direct_epilogue() ? 1 : 0;
   kern<<<grid, kConvThreads, Cfg::SMEM, ctx().stream>>>(tw0, tw1, tx0, tx1, g);
   return check_launch(op);
 }
@@ -1535,6 +1690,10 @@ bool launch_halo(ConvArgs g, const float* w0, const char* op) {
   }
   const int64_t units = POOL ? (int64_t)g.N : g.tiles;  // POOL: whole images per CTA
   const int grid = (int)(units < sm_count() ? units : sm_count());
+  // The direct epilogue pays off while the MMAs hold the shared-memory port
+  // (windows of several taps); a 1 x 1 window's short MMAs leave the port to
+  // the staged path, whose full-line stores measured faster there.
+  g.direct_epi = direct_epilogue() && g.KH * g.KW > 1 ? 1 : 0;
   kern<<<grid, kHaloThreads, Cfg::SMEM, ctx().stream>>>(tw, tx, g);
   return check_launch(op);
 }
