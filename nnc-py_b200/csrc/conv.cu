@@ -820,13 +820,15 @@ constexpr int kHaloMaxK = 4;               // largest KH and KW
 constexpr int kHaloSlots = 2;
 constexpr int kHaloThreads = 32 * (3 + kEpilogueWarps);
 constexpr int kPoolMaxOW = 128;  // widest conv output the pooled epilogue carries a row of
-// POOL shared buffers, in floats: the exchange of each warp's last conv row
-// with the warp below it ([chunk parity][8 row groups][8 columns], 32
-// channels at a 40-float stride), the row carry ([kPoolMaxOW columns], BN
-// channels at a BN + 8 stride) and the column carry ([8 row groups][2 centre
-// rows], BN channels).
-constexpr int kPoolXStride = 40;
-constexpr uint32_t kPoolXchgFloats = 2 * 8 * 8 * kPoolXStride;
+// POOL shared buffers. A thread's 8 values of a 32-channel chunk travel as
+// two float4 runs u = 0, 1 (values 4 u .. 4 u + 3), every run at a
+// 16-byte slot so each warp access is one conflict-free 128-byte wavefront
+// per 8 threads: the exchange of each warp's last conv row with the warp
+// below it ([chunk parity][u][8 row groups][32 threads] float4), the row
+// carry ([kPoolMaxOW columns] x BN values at a BN + 16 stride, value order
+// [chunk][u][thread & 3][4]) and the column carry ([8 row groups][2 centre
+// rows][chunk][u][thread & 3] float4).
+constexpr uint32_t kPoolXchgFloats = 2 * 2 * 8 * 32 * 4;
 
 // CB: channels per window row, 32 (128-byte rows, 128-byte swizzle) or 16
 // (64-byte rows, 64-byte swizzle: the space-to-depth stem's 12 channels).
@@ -841,7 +843,7 @@ struct HaloCfg {
   static constexpr uint32_t EPI_OFF = HALO_OFF + kHaloSlots * SLOT_BYTES;
   static constexpr uint32_t EPI_BYTES = POOL ? kPoolXchgFloats * 4 : kEpiBytes;
   static constexpr uint32_t CARRY_OFF = EPI_OFF + EPI_BYTES;
-  static constexpr int ROW_CARRY_STRIDE = BN + 8;
+  static constexpr int ROW_CARRY_STRIDE = BN + 16;
   static constexpr uint32_t CARRY_BYTES =
       POOL ? (uint32_t)(kPoolMaxOW * ROW_CARRY_STRIDE + 16 * BN) * 4 : 0;
   static constexpr uint32_t BAR_OFF = CARRY_OFF + CARRY_BYTES;
@@ -856,25 +858,34 @@ __device__ __forceinline__ void epi_bar_sync() {
 // POOL epilogue of one tile, run by all 8 epilogue warps. Warp (blk, quad)
 // holds tile rows 4 G .. 4 G + 3, G = 4 blk + quad, as TMEM lanes 32 quad +
 // 8 yy + x. Per 32-channel chunk each warp reads its lanes with two 16x256b
-// loads, so thread t holds column x = t >> 2 of all four rows, channels
-// 8 q + 2 (t & 3) + {0, 1}, q = 0..3:
+// loads, so thread t holds column x = t >> 2 of all four rows at TMEM columns
+// 8 q + 2 (t & 3) + {0, 1}, q = 0..3 (value j = 2 q + h; channel perm_col of
+// the column when C_out is a multiple of 32, which makes values 4 u .. 4 u + 3
+// channels 16 u + 4 (t & 3) + {0..3}):
 //   vertical   centre rows yy = 0, 2 take rows yy - 1 .. yy + 1 from
 //              registers; row -1 is the last row of the warp above, passed
 //              through shared memory (the row carry for G = 0);
 //   horizontal centre columns x = 0, 2, 4, 6 take x +- 1 from threads t +- 4
 //              by shuffle; column -1 is the previous tile's column 7 (the
 //              column carry).
+// Shared memory and shuffles are the scarce resource here (the MMAs of the
+// next tile hold the shared-memory port), so every shared access moves a
+// float4 and the buffers are laid out conflict-free.
 // ReLU results are >= 0 and never NaN, so the maximum is order-free, and a
 // zero stands for window positions outside the conv result (a window always
 // holds its centre, so none is empty): the reference's first-then-strictly-
 // greater scan gives the same values. `parity` counts chunks (the exchange
 // buffer alternates).
+__device__ __forceinline__ float4 ld4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+__device__ __forceinline__ void st4(float* p, const float* v) {
+  *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+}
 template <int BN>
 __device__ __forceinline__ void pool_tile(const ConvArgs& g, uint32_t tmem_base, int acc, int blk,
                                           int quad, int lane, float* xchg, float* row_carry,
                                           float* col_carry, uint32_t& parity, int n, int y0,
                                           int x0) {
-  constexpr int RS = BN + 8;  // row carry stride (floats per column)
+  constexpr int RS = BN + 16;  // row carry stride (floats per column)
   const int G = 4 * blk + quad;
   const int x = lane >> 2, cp = lane & 3;
   const bool up = g.pph == 1, down = g.pkh - g.pph == 2;
@@ -891,7 +902,8 @@ __device__ __forceinline__ void pool_tile(const ConvArgs& g, uint32_t tmem_base,
   const bool perm = perm_rows(g.Cout);
   const bool pair_ok = (g.Cout & 1) == 0 && ((((uintptr_t)g.out) & 7) == 0);
   const bool quad_ok = perm && ((((uintptr_t)g.out) & 15) == 0);
-  for (int c0 = 0; c0 < BN && c0 < g.Cout; c0 += 32) {
+  int chunk = 0;
+  for (int c0 = 0; c0 < BN && c0 < g.Cout; c0 += 32, ++chunk) {
     const uint32_t taddr =
         tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * 2 + blk) * BN + c0;
     uint32_t ra[16], rb[16];
@@ -900,11 +912,29 @@ __device__ __forceinline__ void pool_tile(const ConvArgs& g, uint32_t tmem_base,
     tc::tmem_ld_16x256b_x4(taddr + (16u << 16), rb);  // rows yy = 2, 3
     // Value j = 2 q + h is TMEM column 8 q + 2 cp + h of the chunk.
     float bj[8];
+    if (perm && g.bias && ((((uintptr_t)g.bias) & 15) == 0)) {
+      const float4 b0 = __ldg(reinterpret_cast<const float4*>(g.bias + c0 + 4 * cp));
+      const float4 b1 = __ldg(reinterpret_cast<const float4*>(g.bias + c0 + 16 + 4 * cp));
+      bj[0] = b0.x; bj[1] = b0.y; bj[2] = b0.z; bj[3] = b0.w;
+      bj[4] = b1.x; bj[5] = b1.y; bj[6] = b1.z; bj[7] = b1.w;
+    } else {
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int col = 8 * (j >> 1) + 2 * cp + (j & 1);
-      const int ch = c0 + (perm ? perm_col(col) : col);
-      bj[j] = (g.bias && ch < g.Cout) ? __ldg(g.bias + ch) : 0.0f;
+      for (int j = 0; j < 8; ++j) {
+        const int col = 8 * (j >> 1) + 2 * cp + (j & 1);
+        const int ch = c0 + (perm ? perm_col(col) : col);
+        bj[j] = (g.bias && ch < g.Cout) ? __ldg(g.bias + ch) : 0.0f;
+      }
+    }
+    // Row -1 of group 0 is the row carry (zeros at the image's top edge);
+    // read before the barrier, after which group 7 overwrites it.
+    float above[8];
+    float* const rc = row_carry + (x0 + x) * RS + chunk * 32 + 4 * cp;  // + 16 u
+    if (G == 0) {
+      const bool live = up && y0 > 0 && col_in;
+      const float4 a0 = live ? ld4(rc) : make_float4(0.f, 0.f, 0.f, 0.f);
+      const float4 a1 = live ? ld4(rc + 16) : make_float4(0.f, 0.f, 0.f, 0.f);
+      above[0] = a0.x; above[1] = a0.y; above[2] = a0.z; above[3] = a0.w;
+      above[4] = a1.x; above[5] = a1.y; above[6] = a1.z; above[7] = a1.w;
     }
     tc::tmem_ld_wait();
     float v[4][8];
@@ -920,42 +950,24 @@ __device__ __forceinline__ void pool_tile(const ConvArgs& g, uint32_t tmem_base,
       v[2][j] = (row_in[2] && a2 > 0.0f) ? a2 : 0.0f;
       v[3][j] = (row_in[3] && a3 > 0.0f) ? a3 : 0.0f;
     }
-    // Row -1 of group 0 is the row carry (zeros at the image's top edge);
-    // read before the barrier, after which group 7 overwrites it.
-    float above[8];
-    float* const xb = xchg + (parity & 1) * (8 * 8 * kPoolXStride);
-    float* const rc = row_carry + (x0 + x) * RS + c0 + 2 * cp;
-    if (G == 0) {
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const float2 a = (up && y0 > 0 && col_in) ? *reinterpret_cast<const float2*>(rc + 8 * q)
-                                                  : make_float2(0.0f, 0.0f);
-        above[2 * q] = a.x;
-        above[2 * q + 1] = a.y;
-      }
-    }
+    // Exchange slot of group G's last row: [parity][u][G + 1][lane] float4.
+    float* const xb = xchg + (parity & 1) * (2 * 8 * 32 * 4);
     if (G < 7) {
-#pragma unroll
-      for (int q = 0; q < 4; ++q)
-        *reinterpret_cast<float2*>(xb + ((G + 1) * 8 + x) * kPoolXStride + 8 * q + 2 * cp) =
-            make_float2(v[3][2 * q], v[3][2 * q + 1]);
+      st4(xb + ((0 * 8 + G + 1) * 32 + lane) * 4, &v[3][0]);
+      st4(xb + ((1 * 8 + G + 1) * 32 + lane) * 4, &v[3][4]);
     }
     epi_bar_sync();
     if (G > 0) {
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const float2 a =
-            *reinterpret_cast<const float2*>(xb + (G * 8 + x) * kPoolXStride + 8 * q + 2 * cp);
-        above[2 * q] = a.x;
-        above[2 * q + 1] = a.y;
-      }
+      const float4 a0 = ld4(xb + ((0 * 8 + G) * 32 + lane) * 4);
+      const float4 a1 = ld4(xb + ((1 * 8 + G) * 32 + lane) * 4);
+      above[0] = a0.x; above[1] = a0.y; above[2] = a0.z; above[3] = a0.w;
+      above[4] = a1.x; above[5] = a1.y; above[6] = a1.z; above[7] = a1.w;
     }
     // This tile's last row replaces the row carry for the tile row below
     // (group 0 read the old one before the barrier).
     if (G == 7 && col_in) {
-#pragma unroll
-      for (int q = 0; q < 4; ++q)
-        *reinterpret_cast<float2*>(rc + 8 * q) = make_float2(v[3][2 * q], v[3][2 * q + 1]);
+      st4(rc, &v[3][0]);
+      st4(rc + 16, &v[3][4]);
     }
     // Vertical maxima of the two centre rows.
     float m0[8], m2[8];
@@ -975,7 +987,6 @@ __device__ __forceinline__ void pool_tile(const ConvArgs& g, uint32_t tmem_base,
     }
     // Horizontal: columns x - 1 and x + 1 are threads t - 4 and t + 4;
     // column -1 is the previous tile's column 7 (zeros at the left edge).
-    float* const cc = col_carry + (2 * G) * BN + c0 + 2 * cp;
     float o0[8], o2[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
@@ -995,36 +1006,37 @@ __device__ __forceinline__ void pool_tile(const ConvArgs& g, uint32_t tmem_base,
       o0[j] = a;
       o2[j] = b;
     }
+    // Column carry slot of (G, centre row, chunk, u, cp): one float4.
+    float* const cc = col_carry + (((G * 2) * (BN / 32) + chunk) * 2 * 4 + cp) * 4;
+    constexpr int kRowStep = (BN / 32) * 2 * 4 * 4;  // centre row yy = 2
     if (left && x == 0 && x0 > 0) {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int off = 8 * (j >> 1) + (j & 1);
-        o0[j] = fmaxf(o0[j], cc[off]);
-        o2[j] = fmaxf(o2[j], cc[BN + off]);
-      }
+      const float4 p0 = ld4(cc), p1 = ld4(cc + 16);
+      const float4 q0 = ld4(cc + kRowStep), q1 = ld4(cc + kRowStep + 16);
+      o0[0] = fmaxf(o0[0], p0.x); o0[1] = fmaxf(o0[1], p0.y);
+      o0[2] = fmaxf(o0[2], p0.z); o0[3] = fmaxf(o0[3], p0.w);
+      o0[4] = fmaxf(o0[4], p1.x); o0[5] = fmaxf(o0[5], p1.y);
+      o0[6] = fmaxf(o0[6], p1.z); o0[7] = fmaxf(o0[7], p1.w);
+      o2[0] = fmaxf(o2[0], q0.x); o2[1] = fmaxf(o2[1], q0.y);
+      o2[2] = fmaxf(o2[2], q0.z); o2[3] = fmaxf(o2[3], q0.w);
+      o2[4] = fmaxf(o2[4], q1.x); o2[5] = fmaxf(o2[5], q1.y);
+      o2[6] = fmaxf(o2[6], q1.z); o2[7] = fmaxf(o2[7], q1.w);
     }
     __syncwarp();  // column 0's carry reads precede column 7's writes
     if (x == 7) {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int off = 8 * (j >> 1) + (j & 1);
-        cc[off] = m0[j];
-        cc[BN + off] = m2[j];
-      }
+      st4(cc, &m0[0]);
+      st4(cc + 16, &m0[4]);
+      st4(cc + kRowStep, &m2[0]);
+      st4(cc + kRowStep + 16, &m2[4]);
     }
     // Pooled outputs: centre columns of centre rows. Permuted channels give
     // this thread c0 + 16 u + 4 cp + {0..3} (values 4 u .. 4 u + 3): 16-byte
-    // stores; otherwise channel pairs c0 + 8 q + 2 cp + {0, 1}.
+    // stores; otherwise channel pairs.
     if (quad_ok) {
 #pragma unroll
       for (int u = 0; u < 2; ++u) {
         const int ch = c0 + 16 * u + 4 * cp;
-        if (st0)
-          *reinterpret_cast<float4*>(out0 + ch) =
-              make_float4(o0[4 * u], o0[4 * u + 1], o0[4 * u + 2], o0[4 * u + 3]);
-        if (st2)
-          *reinterpret_cast<float4*>(out2 + ch) =
-              make_float4(o2[4 * u], o2[4 * u + 1], o2[4 * u + 2], o2[4 * u + 3]);
+        if (st0) st4(out0 + ch, &o0[4 * u]);
+        if (st2) st4(out2 + ch, &o2[4 * u]);
       }
       ++parity;
       continue;
