@@ -183,13 +183,21 @@ __device__ __forceinline__ float activate(float o, int act) {
 // tile and written row-contiguously (NHWC), or per channel plane (NCHW).
 // DIRECT_CODE compiles the direct path in (the halo kernel; the im2col
 // kernel's 13 warps leave it 128 registers per thread, too few for it).
-template <int BN, bool DIRECT_CODE, class RowMap>
+// STAGED_CODE = false (an instance without a staging tile) compiles the
+// staged and NCHW paths out; a call that would need them records
+// NNC_CUDA_ERR_INVALID in the device error word and writes nothing (the host
+// never routes one there).
+template <int BN, bool DIRECT_CODE, class RowMap, bool STAGED_CODE = true>
 __device__ __forceinline__ void store_tile(const ConvArgs& g, uint32_t tmem_base, uint32_t acc_col,
                                            int nt, int quad, int c_first, int c_step, int lane,
                                            float* stage_tile, bool vec_ok, bool bias_vec,
                                            const RowMap& rows, bool direct) {
   const int64_t OHW = (int64_t)g.OH * g.OW;
   const bool perm = perm_rows(g.Cout);
+  if (!STAGED_CODE && !(DIRECT_CODE && g.out_nhwc && direct)) {
+    if (lane == 0 && g.err) atomicExch(g.err, 1 /* NNC_CUDA_ERR_INVALID */);
+    return;
+  }
   if (DIRECT_CODE && g.out_nhwc && direct) {
     const bool add = g.act == kActAddRelu;
     const bool relu = add || g.act == kActRelu;
@@ -270,6 +278,7 @@ __device__ __forceinline__ void store_tile(const ConvArgs& g, uint32_t tmem_base
     }
     return;
   }
+  if constexpr (STAGED_CODE) {
 #pragma unroll 1
   for (int c0 = c_first; c0 < BN; c0 += c_step) {
     const int co0 = nt * BN + c0;
@@ -397,6 +406,7 @@ __device__ __forceinline__ void store_tile(const ConvArgs& g, uint32_t tmem_base
       }
     }
   }
+  }  // STAGED_CODE
 }
 
 // Row maps of the two tile shapes: a run of 128 consecutive output pixels,
@@ -779,6 +789,204 @@ __global__ void __launch_bounds__(kConvThreads, 1)
   }
 }
 
+// ----------------------------------------------- paired im2col kernel ----
+//
+// The im2col route for C_out > 128 (ResNet stages 3-4) on CTA pairs
+// (tcgen05 cta_group::2): a cluster of two CTAs computes one tile of 256
+// output pixels x 256 channels. CTA r loads the im2col A tile of pixels
+// [m0 + 128 r, +128) and rows [n0 + 128 r, +128) of the weight tile; the even
+// CTA issues M = 256 MMAs that read both CTAs' operands at the same shared
+// offsets and accumulate into both CTAs' TMEM (CTA r's 128 lanes hold its
+// pixels x all 256 channels). Per k-block each SM receives 16 KB of A and
+// 16 KB of B instead of 16 + 32 KB, which is what bounds the single-CTA
+// kernel's N = 256 MMAs (TMA delivers ~52 B/clk of im2col rows and ~80 of
+// tiled rows per SM; the MMAs consume a k-block in 512 cycles).
+//
+// Barriers: the stage barriers full[s] of the even CTA count both CTAs' TMA
+// bytes (the loads name it through .cta_group::2); the even CTA's commits
+// arrive on empty[s], tfull[a] and done in both CTAs; every epilogue warp of
+// both CTAs arrives on the even CTA's tempty[a] (16 arrivals). Cluster
+// barriers after set-up and before the pair's TMEM is freed; the odd CTA
+// waits for the final commit before it leaves. No TMA load uses cluster
+// multicast.
+template <int STAGES>
+struct ConvPairCfg {
+  static constexpr int BN = 256;        // MMA N; each CTA holds BN / 2 weight rows
+  static constexpr uint32_t A_BYTES = BM * BK * 4;             // 16 KB
+  static constexpr uint32_t B_BYTES = (BN / 2) * BK * 4;       // 16 KB
+  static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr uint32_t TMEM_COLS = 2 * BN;                // double-buffered accumulator
+  static constexpr uint32_t EPI_OFF = STAGES * STAGE_BYTES;
+  static constexpr uint32_t BAR_OFF = EPI_OFF + kEpiBytes;
+  static constexpr size_t SMEM = (size_t)BAR_OFF + 256 + 1024;
+};
+
+template <int STAGES>
+__global__ void __launch_bounds__(kConvThreads, 1)
+    conv_tc2_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
+                    const ConvArgs g) {
+  using Cfg = ConvPairCfg<STAGES>;
+  constexpr int BN = Cfg::BN;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  float* epi = reinterpret_cast<float*>(smem + Cfg::EPI_OFF);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::BAR_OFF);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* done = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = tc::cluster_ctarank();  // 0: issues the MMAs
+  const int64_t cluster = blockIdx.x >> 1, clusters = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      tc::mbar_init(&full[s], 1);   // even CTA: its expect_tx arrival (+ both CTAs' bytes)
+      tc::mbar_init(&empty[s], 1);  // one pair commit
+    }
+    for (int a = 0; a < 2; ++a) {
+      tc::mbar_init(&tfull[a], 1);
+      tc::mbar_init(&tempty[a], 2 * kEpilogueWarps);  // even CTA: both CTAs' epilogue warps
+    }
+    tc::mbar_init(done, 1);
+    tc::fence_barrier_init();
+    tc::prefetch_tmap(&tmW);
+    tc::prefetch_tmap(&tmX);
+  }
+  if (warp == kMmaWarp) {
+    tc::tmem_alloc_pair(tmem_slot, Cfg::TMEM_COLS);
+    tc::tmem_relinquish_pair();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::cluster_sync();  // both CTAs' barriers initialised, TMEM allocated
+  tc::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp < kProducerWarps) {
+    // ---------------- producer (one thread per CTA): A half, B half ----------------
+    if (threadIdx.x == 0) {
+      const int64_t OHW = (int64_t)g.OH * g.OW;
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int64_t tile = cluster; tile < g.tiles && ok; tile += clusters) {
+        const int64_t mt = tile / g.n_tiles;
+        const int nt = (int)(tile % g.n_tiles);
+        // This CTA's first pixel; a half past the last pixel loads the
+        // pair's first half again (valid coordinates; its rows are masked).
+        int64_t m0 = mt * (2 * BM) + (int64_t)rank * BM;
+        if (m0 >= g.M) m0 = mt * (2 * BM);
+        const int n0 = (int)(m0 / OHW);
+        const int rem = (int)(m0 - (int64_t)n0 * OHW);
+        const int w0 = (rem % g.OW) * g.sw - g.pw, h0 = (rem / g.OW) * g.sh - g.ph;
+        for (int kb = 0; kb < g.kblocks; ++kb) {
+          if (!tc::mbar_wait(&empty[stage], phase ^ 1, g.err)) {
+            ok = false;
+            break;
+          }
+          uint8_t* s = smem + stage * Cfg::STAGE_BYTES;
+          if (rank == 0) tc::mbar_arrive_expect_tx(&full[stage], 2 * Cfg::STAGE_BYTES);
+          const uint32_t bar = tc::mapa(tc::smem_u32(&full[stage]), 0);
+          tc::tma_load_2d_pair(s + Cfg::A_BYTES, &tmW, bar, kb * BK, nt * BN + (int)rank * (BN / 2));
+          const int k0 = kb * BK, tap = k0 / g.C4, c0 = k0 - tap * g.C4;
+          const uint16_t kh = (uint16_t)(tap / g.KW), kw = (uint16_t)(tap % g.KW);
+          tc::tma_load_im2col_4d_pair(s, &tmX, bar, c0, w0, h0, n0, kw, kh);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      // The even CTA lets the last issued loads of both CTAs land before it
+      // can leave (the odd CTA's loads count on these barriers too).
+      if (ok && rank == 0) {
+        for (int q = 0; q < STAGES; ++q) {
+          if (stage == 0) {
+            stage = STAGES;
+            phase ^= 1;
+          }
+          --stage;
+          tc::mbar_wait(&full[stage], phase, g.err);
+        }
+      }
+    }
+  } else if (warp == kMmaWarp) {
+    if (rank == 0 && lane == 0) {
+      // ---------------- MMA issuer (even CTA) ----------------
+      constexpr uint32_t idesc = tc::idesc_tf32(2 * BM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int64_t t = cluster; t < g.tiles && ok; t += clusters, ++local) {
+        const int acc = local & 1;
+        const uint32_t aphase = (local >> 1) & 1;
+        if (!tc::mbar_wait(&tempty[acc], aphase ^ 1, g.err)) break;
+        tc::tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < g.kblocks; ++kb) {
+          if (!tc::mbar_wait(&full[stage], phase, g.err)) {
+            ok = false;
+            break;
+          }
+          tc::tc_fence_after();
+          const uint32_t sa = tc::smem_u32(smem + stage * Cfg::STAGE_BYTES);
+          const uint32_t sb = sa + Cfg::A_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / 8; ++k)
+            tc::mma_tf32_pair(d_tmem, tc::desc_kmajor_sw128(sa + k * 32),
+                              tc::desc_kmajor_sw128(sb + k * 32), idesc, (kb | k) != 0);
+          tc::mma_commit_pair_both(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        tc::mma_commit_pair_both(&tfull[acc]);
+      }
+      tc::mma_commit_pair_both(done);
+      tc::mbar_wait(done, 0, g.err);
+    }
+  } else {
+    // ---------------- epilogue (warps 5..12 of both CTAs) ----------------
+    const int quad = warp & 3, half = (warp - kMmaWarp - 1) >> 2;
+    float* stage_tile = epi + (warp - kMmaWarp - 1) * 32 * (kStageCols + 1);
+    const bool vec_ok = (g.Cout % 4 == 0) && ((((uintptr_t)g.out) & 15) == 0) &&
+                        (!g.residual || ((((uintptr_t)g.residual) & 15) == 0));
+    const bool bias_vec = g.bias && ((((uintptr_t)g.bias) & 15) == 0);
+    const uint32_t tempty0 = tc::mapa(tc::smem_u32(&tempty[0]), 0);
+    int local = 0;
+    for (int64_t t = cluster; t < g.tiles; t += clusters, ++local) {
+      const int64_t mt = t / g.n_tiles;
+      const int nt = (int)(t % g.n_tiles);
+      const int acc = local & 1;
+      const uint32_t aphase = (local >> 1) & 1;
+      if (!tc::mbar_wait(&tfull[acc], aphase, g.err)) break;
+      tc::tc_fence_after();
+      store_tile<BN, false>(g, tmem_base, acc * BN, nt, quad, half * kStageCols, 2 * kStageCols,
+                            lane, stage_tile, vec_ok, bias_vec,
+                            LinearRows{mt * (2 * BM) + (int64_t)rank * BM, g.M}, false);
+      tc::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive_cluster(tempty0 + acc * (uint32_t)sizeof(uint64_t));
+    }
+    // The odd CTA leaves only after the even CTA's last commit has arrived
+    // here (its barriers receive the pair's commits).
+    if (rank == 1 && warp == kMmaWarp + 1) tc::mbar_wait_warp(done, 0, g.err);
+  }
+
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::cluster_sync();  // no CTA frees the pair's TMEM or leaves while the other works
+  if (warp == kMmaWarp) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc_pair(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
 // --------------------------------------------------------- halo kernel ----
 //
 // Stride-1 convolutions (and 1 x 1 windows with stride 2) over an NHWC input
@@ -832,7 +1040,9 @@ constexpr uint32_t kPoolXchgFloats = 2 * 2 * 8 * 32 * 4;
 
 // CB: channels per window row, 32 (128-byte rows, 128-byte swizzle) or 16
 // (64-byte rows, 64-byte swizzle: the space-to-depth stem's 12 channels).
-template <int BN, int G, int STAGES, int CB, bool POOL = false>
+// STAGED = false: the instance serves only calls whose epilogue takes the
+// direct path (no shared staging tile; the space goes to the weight ring).
+template <int BN, int G, int STAGES, int CB, bool POOL = false, bool STAGED = true>
 struct HaloCfg {
   static constexpr int ROW = CB * 4;                    // bytes per window row
   static constexpr uint32_t SLOT_BYTES = (2 * kHaloTH + kHaloMaxK - 1) *
@@ -841,7 +1051,7 @@ struct HaloCfg {
   static constexpr uint32_t STAGE_BYTES = G * B_BYTES;  // G taps per ring stage
   static constexpr uint32_t HALO_OFF = STAGES * STAGE_BYTES;
   static constexpr uint32_t EPI_OFF = HALO_OFF + kHaloSlots * SLOT_BYTES;
-  static constexpr uint32_t EPI_BYTES = POOL ? kPoolXchgFloats * 4 : kEpiBytes;
+  static constexpr uint32_t EPI_BYTES = POOL ? kPoolXchgFloats * 4 : (STAGED ? kEpiBytes : 0);
   static constexpr uint32_t CARRY_OFF = EPI_OFF + EPI_BYTES;
   static constexpr int ROW_CARRY_STRIDE = BN + 16;
   static constexpr uint32_t CARRY_BYTES =
@@ -1081,11 +1291,11 @@ __device__ __forceinline__ int64_t halo_tile(const ConvArgs& g, int64_t k) {
   return img < g.N ? img * per + k % per : -1;
 }
 
-template <int BN, int G, int STAGES, int CB, bool POOL>
+template <int BN, int G, int STAGES, int CB, bool POOL, bool STAGED>
 __global__ void __launch_bounds__(kHaloThreads, 1)
     conv_halo_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
                      const ConvArgs g) {
-  using Cfg = HaloCfg<BN, G, STAGES, CB, POOL>;
+  using Cfg = HaloCfg<BN, G, STAGES, CB, POOL, STAGED>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   uint8_t* halo = smem + Cfg::HALO_OFF;
@@ -1316,7 +1526,8 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
         pool_tile<BN>(g, tmem_base, acc, blk, quad, lane, epi, row_carry, col_carry, parity, n,
                       (rem / g.tiles_x) * 2 * kHaloTH, (rem % g.tiles_x) * kHaloTW);
       } else {
-        store_tile<BN, true>(g, tmem_base, (uint32_t)(acc * 2 + blk) * BN, nt, quad, 0, kStageCols, lane,
+        store_tile<BN, true, BlockRows, STAGED>(g, tmem_base, (uint32_t)(acc * 2 + blk) * BN, nt, quad, 0,
+                                                kStageCols, lane,
                        stage_tile, vec_ok, bias_vec,
                        BlockRows{(int64_t)n * OHW, (rem / g.tiles_x) * 2 * kHaloTH + blk * kHaloTH,
                                  (rem % g.tiles_x) * kHaloTW, g.OH, g.OW},
@@ -1608,16 +1819,18 @@ WeightLayout weight_layout(int Cin, int KH, int KW) {
   return L;
 }
 
-// Whether channels-last epilogues store straight from TMEM fragments (the
-// default); NNC_CUDA_CONV_DIRECT_EPI=0 selects the shared-memory staged
-// stores (for comparison).
-static bool direct_epilogue() {
-  static const bool on = [] {
+// Which channels-last epilogues store straight from TMEM fragments:
+// NNC_CUDA_CONV_DIRECT_EPI unset or 1 = the default policy (halo_direct),
+// 0 = none (shared-memory staged stores, for comparison), 2 = every eligible
+// call including 1 x 1 windows (for comparison).
+static int direct_epilogue_mode() {
+  static const int mode = [] {
     const char* e = getenv("NNC_CUDA_CONV_DIRECT_EPI");
-    return !(e && e[0] == '0');
+    return e && e[0] == '0' ? 0 : (e && e[0] == '2' ? 2 : 1);
   }();
-  return on;
+  return mode;
 }
+static bool direct_epilogue() { return direct_epilogue_mode() != 0; }
 
 template <int BN, int SPLIT, int STAGES>
 bool launch_conv(ConvArgs g, const float* w0, const float* w1, const char* op) {
@@ -1667,9 +1880,86 @@ bool launch_conv(ConvArgs g, const float* w0, const float* w1, const char* op) {
   return check_launch(op);
 }
 
-template <int BN, int G, int STAGES, int CB, bool POOL = false>
+// Whether the im2col route runs C_out > 128 on CTA pairs (the default);
+// NNC_CUDA_CONV_PAIR=0 selects the single-CTA kernel (for comparison).
+static bool conv_pair_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("NNC_CUDA_CONV_PAIR");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
+template <int STAGES>
+bool launch_conv_pair(ConvArgs g, const float* w0, const char* op) {
+  using Cfg = ConvPairCfg<STAGES>;
+  constexpr int BN = Cfg::BN;
+  const int Kpad = g.kblocks * BK;
+  CUtensorMap tw, tx;
+  // Weights: each CTA loads BN / 2 rows of the pair's BN-row tile.
+  const uint64_t dims[2] = {(uint64_t)Kpad, (uint64_t)g.Cout};
+  const uint64_t strides[1] = {(uint64_t)Kpad * 4};
+  const uint32_t box[2] = {BK, BN / 2};
+  if (!encode_tmap_f32(&tw, w0, 2, dims, strides, box, nullptr, op)) return false;
+  const uint64_t xd[4] = {(uint64_t)g.C4, (uint64_t)g.W, (uint64_t)g.H, (uint64_t)g.N};
+  const uint64_t xs[3] = {(uint64_t)g.C4 * 4, (uint64_t)g.W * g.C4 * 4,
+                          (uint64_t)g.H * g.W * g.C4 * 4};
+  const int lower = -g.ph, upper = (g.OH - 1) * g.sh - g.ph - (g.H - 1);
+  if (!encode_tmap_im2col_f32(&tx, g.x_hi, xd, xs, lower, upper, 32, BM, g.sh, true, op))
+    return false;
+  g.n_tiles = (int)cdiv(g.Cout, BN);
+  g.m_tiles = (int)cdiv(g.M, 2 * BM);
+  g.tiles = (int64_t)g.m_tiles * g.n_tiles;
+  g.direct_epi = 0;
+  auto kern = conv_tc2_kernel<STAGES>;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(kConvThreads, 1, 1);
+  cfg.dynamicSmemBytes = Cfg::SMEM;
+  cfg.stream = ctx().stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  // Per device: the shared-memory opt-in, then how many pairs fit at once.
+  static bool attr_set[64] = {};
+  static int max_pairs[64] = {};
+  if (!attr_set[ctx().device]) {
+    if (!check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)Cfg::SMEM),
+                    op, "cudaFuncSetAttribute"))
+      return false;
+    int n = 0;
+    cfg.gridDim = dim3(2 * (sm_count() / 2), 1, 1);
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = sm_count() / 2;
+    }
+    max_pairs[ctx().device] = n;
+    attr_set[ctx().device] = true;
+  }
+  const int64_t pairs = g.tiles < max_pairs[ctx().device] ? g.tiles : max_pairs[ctx().device];
+  cfg.gridDim = dim3((unsigned)(2 * pairs), 1, 1);
+  if (!check_cuda(cudaLaunchKernelEx(&cfg, kern, tw, tx, g), op, "cudaLaunchKernelEx")) return false;
+  return check_launch(op);
+}
+
+// Whether a halo call's epilogue takes the direct path (store_tile's
+// `direct`, decided the same way in the kernel): channels-last output, C_out
+// a multiple of 32, 16-byte aligned output and residual, and a window of
+// several taps (a 1 x 1 window's short MMAs leave the shared-memory port to
+// the staged path, whose full-line stores measured faster there).
+static bool halo_direct(const ConvArgs& g) {
+  return direct_epilogue() && g.out_nhwc && perm_rows(g.Cout) &&
+         (g.KH * g.KW > 1 || direct_epilogue_mode() == 2) &&
+         (((uintptr_t)g.out) & 15) == 0 && (!g.residual || (((uintptr_t)g.residual) & 15) == 0);
+}
+
+template <int BN, int G, int STAGES, int CB, bool POOL = false, bool STAGED = true>
 bool launch_halo(ConvArgs g, const float* w0, const char* op) {
-  using Cfg = HaloCfg<BN, G, STAGES, CB, POOL>;
+  using Cfg = HaloCfg<BN, G, STAGES, CB, POOL, STAGED>;
   const int Kpad = g.K;  // taps x C4, a multiple of CB
   CUtensorMap tw, tx;
   const uint64_t dims[2] = {(uint64_t)Kpad, (uint64_t)g.Cout};
@@ -1691,7 +1981,7 @@ bool launch_halo(ConvArgs g, const float* w0, const char* op) {
   g.m_tiles = g.N * g.tiles_x * g.tiles_y;
   g.n_tiles = (int)cdiv(g.Cout, BN);
   g.tiles = (int64_t)g.m_tiles * g.n_tiles;
-  auto kern = conv_halo_kernel<BN, G, STAGES, CB, POOL>;
+  auto kern = conv_halo_kernel<BN, G, STAGES, CB, POOL, STAGED>;
   static bool attr_set[64] = {};
   if (!attr_set[ctx().device]) {
     if (!check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1702,10 +1992,11 @@ bool launch_halo(ConvArgs g, const float* w0, const char* op) {
   }
   const int64_t units = POOL ? (int64_t)g.N : g.tiles;  // POOL: whole images per CTA
   const int grid = (int)(units < sm_count() ? units : sm_count());
-  // The direct epilogue pays off while the MMAs hold the shared-memory port
-  // (windows of several taps); a 1 x 1 window's short MMAs leave the port to
-  // the staged path, whose full-line stores measured faster there.
-  g.direct_epi = direct_epilogue() && g.KH * g.KW > 1 ? 1 : 0;
+  g.direct_epi = halo_direct(g) ? 1 : 0;
+  if (!STAGED && !POOL && !g.direct_epi) {
+    fail(NNC_CUDA_ERR_INVALID, op, "internal: unstaged halo instance for a staged epilogue");
+    return false;
+  }
   kern<<<grid, kHaloThreads, Cfg::SMEM, ctx().stream>>>(tw, tx, g);
   return check_launch(op);
 }
@@ -2108,12 +2399,24 @@ void conv_impl(Tensor* input, Tensor* weight, Tensor* bias, Tensor* residual, Te
   g.err = device_error_word();
 
   if (g.mode == kHalo) {
-    if (Cout > 64)
-      launch_halo<128, 1, 4, 32>(g, w0, op);
-    else
-      launch_halo<64, 3, 3, 32>(g, w0, op);
+    // Direct-epilogue calls take the unstaged instances, whose deeper weight
+    // rings cover the weight stream's L2 latency.
+    const bool direct = halo_direct(g);
+    if (Cout > 64) {
+      if (direct)
+        launch_halo<128, 1, 7, 32, false, false>(g, w0, op);
+      else
+        launch_halo<128, 1, 4, 32>(g, w0, op);
+    } else {
+      if (direct)
+        launch_halo<64, 3, 5, 32, false, false>(g, w0, op);
+      else
+        launch_halo<64, 3, 3, 32>(g, w0, op);
+    }
   } else if (!split) {
-    if (Cout > 128)
+    if (Cout > 128 && g.mode == kIm2col128 && conv_pair_enabled())
+      launch_conv_pair<6>(g, w0, op);
+    else if (Cout > 128)
       launch_conv<256, 1, 4>(g, w0, nullptr, op);
     else if (Cout > 64)
       launch_conv<128, 1, 6>(g, w0, nullptr, op);

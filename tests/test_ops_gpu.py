@@ -205,6 +205,49 @@ def test_conv_stride1_blocks_vs_oracle(cuda_lib, prec, cfg):
     C.assert_close(got_nhwc, want, C.TC_RTOL[prec], f"conv{cfg}[nhwc]")
 
 
+# C_out above 128 over 32-channel NHWC inputs runs on CTA pairs in TF32 mode
+# (one 256-pixel x 256-channel tile per pair, the odd CTA holding the upper
+# 128 pixels and weight rows): tiles whose upper half is partly or wholly past
+# the last pixel (196, 49 and 784 pixels), partial channel tiles (384, 200 —
+# the latter not a multiple of 32), stride 2, and 98 tiles for fewer pairs,
+# so pairs run several tiles through both accumulators.
+PAIR_CASES = [
+    # n, c, h, w, co, k, s, p, op
+    (4, 256, 14, 14, 256, 3, 1, 1, "nnc_conv_add_relu"),
+    (1, 128, 14, 14, 256, 3, 1, 1, "nnc_conv_relu"),
+    (1, 256, 7, 7, 512, 3, 1, 1, "nnc_conv"),
+    (3, 128, 28, 28, 256, 3, 2, 1, "nnc_conv_relu"),
+    (2, 64, 16, 16, 384, 3, 1, 1, "nnc_conv_add_relu"),
+    (2, 160, 10, 12, 200, 3, 1, 1, "nnc_conv"),
+    (64, 32, 14, 14, 512, 3, 1, 1, "nnc_conv_add_relu"),
+]
+
+
+@pytest.mark.parametrize("prec", [0, 1])
+@pytest.mark.parametrize("cfg", PAIR_CASES, ids=lambda c: "x".join(str(v) for v in c[:8]))
+def test_conv_cta_pairs_vs_oracle(cuda_lib, prec, cfg):
+    n, c, h, w, co, k, st, p, op = cfg
+    r = np.random.default_rng(13 + sum(cfg[:8]))
+    oh, ow = C.conv_out(h, k, st, p), C.conv_out(w, k, st, p)
+    arrays = {"x": r.standard_normal((n, c, h, w)).astype(np.float32),
+              "w": (r.standard_normal((co, c, k, k)) * np.sqrt(2.0 / (c * k * k))).astype(np.float32),
+              "b": r.uniform(-0.01, 0.01, co).astype(np.float32),
+              "res": r.standard_normal((n, co, oh, ow)).astype(np.float32)}
+    args = [C._t("x"), C._t("w"), C._t("b")]
+    nhwc = {"x", "out"}
+    if op == "nnc_conv_add_relu":
+        args.append(C._t("res"))
+        nhwc.add("res")
+    args += [C._o("out", (n, co, oh, ow)), C._i(k), C._i(k), C._i(st), C._i(st), C._i(p), C._i(p)]
+    case = {"name": "c", "op": op, "args": args}
+    cuda_lib.nnc_cuda_set_precision(prec)
+    want = C.run_host(_oracle(), case, arrays)["out"]
+    got_nhwc = C.run_cuda(cuda_lib, case, arrays, nhwc=nhwc)["out"]
+    C.assert_close(got_nhwc, want, C.TC_RTOL[prec], f"conv{cfg}[nhwc]")
+    got = C.run_cuda(cuda_lib, case, arrays)["out"]
+    C.assert_close(got, want, C.TC_RTOL[prec], f"conv{cfg}")
+
+
 # Stride-2 windows over at most 8 channels run as stride-1 windows over a
 # space-to-depth copy of the input (TF32 mode): 7x7 p3 (the ResNet stem), odd
 # extents, one channel, a 3x3 window whose prepacked weight is in element
