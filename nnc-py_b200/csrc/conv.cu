@@ -791,9 +791,9 @@ __global__ void __launch_bounds__(kConvThreads, 1)
 
 // ----------------------------------------------- paired im2col kernel ----
 //
-// The im2col route for C_out > 128 (ResNet stages 3-4) on CTA pairs
+// The im2col route for C_out > 64 (ResNet stages 2-4) on CTA pairs
 // (tcgen05 cta_group::2): a cluster of two CTAs computes one tile of 256
-// output pixels x 256 channels. CTA r loads the im2col A tile of pixels
+// output pixels x BN (128 or 256) channels. CTA r loads the im2col A tile of pixels
 // [m0 + 128 r, +128) and rows [n0 + 128 r, +128) of the weight tile; the even
 // CTA issues M = 256 MMAs that read both CTAs' operands at the same shared
 // offsets and accumulate into both CTAs' TMEM (CTA r's 128 lanes hold its
@@ -809,11 +809,11 @@ __global__ void __launch_bounds__(kConvThreads, 1)
 // barriers after set-up and before the pair's TMEM is freed; the odd CTA
 // waits for the final commit before it leaves. No TMA load uses cluster
 // multicast.
-template <int STAGES>
+template <int BN_, int STAGES>
 struct ConvPairCfg {
-  static constexpr int BN = 256;        // MMA N; each CTA holds BN / 2 weight rows
+  static constexpr int BN = BN_;        // MMA N (128 or 256); each CTA holds BN / 2 weight rows
   static constexpr uint32_t A_BYTES = BM * BK * 4;             // 16 KB
-  static constexpr uint32_t B_BYTES = (BN / 2) * BK * 4;       // 16 KB
+  static constexpr uint32_t B_BYTES = (BN / 2) * BK * 4;       // 8 or 16 KB
   static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr uint32_t TMEM_COLS = 2 * BN;                // double-buffered accumulator
   static constexpr uint32_t EPI_OFF = STAGES * STAGE_BYTES;
@@ -821,11 +821,15 @@ struct ConvPairCfg {
   static constexpr size_t SMEM = (size_t)BAR_OFF + 256 + 1024;
 };
 
-template <int STAGES>
-__global__ void __launch_bounds__(kConvThreads, 1)
+// 10 warps: warp 0 produces (one thread), warp 1 issues (even CTA), warps
+// 2..9 drain TMEM; 3 warps per SM sub-partition at most leave 168 registers
+// per thread, room for the direct epilogue.
+constexpr int kPairMmaWarp = 1, kPairThreads = 32 * (2 + kEpilogueWarps);
+template <int BN_, int STAGES>
+__global__ void __launch_bounds__(kPairThreads, 1)
     conv_tc2_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
                     const ConvArgs g) {
-  using Cfg = ConvPairCfg<STAGES>;
+  using Cfg = ConvPairCfg<BN_, STAGES>;
   constexpr int BN = Cfg::BN;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
@@ -855,7 +859,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
     tc::prefetch_tmap(&tmW);
     tc::prefetch_tmap(&tmX);
   }
-  if (warp == kMmaWarp) {
+  if (warp == kPairMmaWarp) {
     tc::tmem_alloc_pair(tmem_slot, Cfg::TMEM_COLS);
     tc::tmem_relinquish_pair();
   }
@@ -865,7 +869,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
   tc::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  if (warp < kProducerWarps) {
+  if (warp < kPairMmaWarp) {
     // ---------------- producer (one thread per CTA): A half, B half ----------------
     if (threadIdx.x == 0) {
       const int64_t OHW = (int64_t)g.OH * g.OW;
@@ -913,7 +917,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
         }
       }
     }
-  } else if (warp == kMmaWarp) {
+  } else if (warp == kPairMmaWarp) {
     if (rank == 0 && lane == 0) {
       // ---------------- MMA issuer (even CTA) ----------------
       constexpr uint32_t idesc = tc::idesc_tf32(2 * BM, BN);
@@ -951,12 +955,13 @@ __global__ void __launch_bounds__(kConvThreads, 1)
       tc::mbar_wait(done, 0, g.err);
     }
   } else {
-    // ---------------- epilogue (warps 5..12 of both CTAs) ----------------
-    const int quad = warp & 3, half = (warp - kMmaWarp - 1) >> 2;
-    float* stage_tile = epi + (warp - kMmaWarp - 1) * 32 * (kStageCols + 1);
+    // ---------------- epilogue (warps 2..9 of both CTAs) ----------------
+    const int quad = warp & 3, half = (warp - kPairMmaWarp - 1) >> 2;
+    float* stage_tile = epi + (warp - kPairMmaWarp - 1) * 32 * (kStageCols + 1);
     const bool vec_ok = (g.Cout % 4 == 0) && ((((uintptr_t)g.out) & 15) == 0) &&
                         (!g.residual || ((((uintptr_t)g.residual) & 15) == 0));
     const bool bias_vec = g.bias && ((((uintptr_t)g.bias) & 15) == 0);
+    const bool direct = vec_ok && perm_rows(g.Cout) && g.direct_epi;
     const uint32_t tempty0 = tc::mapa(tc::smem_u32(&tempty[0]), 0);
     int local = 0;
     for (int64_t t = cluster; t < g.tiles; t += clusters, ++local) {
@@ -966,22 +971,22 @@ __global__ void __launch_bounds__(kConvThreads, 1)
       const uint32_t aphase = (local >> 1) & 1;
       if (!tc::mbar_wait(&tfull[acc], aphase, g.err)) break;
       tc::tc_fence_after();
-      store_tile<BN, false>(g, tmem_base, acc * BN, nt, quad, half * kStageCols, 2 * kStageCols,
-                            lane, stage_tile, vec_ok, bias_vec,
-                            LinearRows{mt * (2 * BM) + (int64_t)rank * BM, g.M}, false);
+      store_tile<BN, true>(g, tmem_base, acc * BN, nt, quad, half * kStageCols, 2 * kStageCols,
+                           lane, stage_tile, vec_ok, bias_vec,
+                           LinearRows{mt * (2 * BM) + (int64_t)rank * BM, g.M}, direct);
       tc::tc_fence_before();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive_cluster(tempty0 + acc * (uint32_t)sizeof(uint64_t));
     }
     // The odd CTA leaves only after the even CTA's last commit has arrived
     // here (its barriers receive the pair's commits).
-    if (rank == 1 && warp == kMmaWarp + 1) tc::mbar_wait_warp(done, 0, g.err);
+    if (rank == 1 && warp == kPairMmaWarp + 1) tc::mbar_wait_warp(done, 0, g.err);
   }
 
   tc::tc_fence_before();
   __syncthreads();
   tc::cluster_sync();  // no CTA frees the pair's TMEM or leaves while the other works
-  if (warp == kMmaWarp) {
+  if (warp == kPairMmaWarp) {
     tc::tc_fence_after();
     tc::tmem_dealloc_pair(tmem_base, Cfg::TMEM_COLS);
   }
@@ -1880,7 +1885,7 @@ bool launch_conv(ConvArgs g, const float* w0, const float* w1, const char* op) {
   return check_launch(op);
 }
 
-// Whether the im2col route runs C_out > 128 on CTA pairs (the default);
+// Whether the im2col route runs C_out > 64 on CTA pairs (the default);
 // NNC_CUDA_CONV_PAIR=0 selects the single-CTA kernel (for comparison).
 static bool conv_pair_enabled() {
   static const bool on = [] {
@@ -1890,9 +1895,9 @@ static bool conv_pair_enabled() {
   return on;
 }
 
-template <int STAGES>
+template <int BN_, int STAGES>
 bool launch_conv_pair(ConvArgs g, const float* w0, const char* op) {
-  using Cfg = ConvPairCfg<STAGES>;
+  using Cfg = ConvPairCfg<BN_, STAGES>;
   constexpr int BN = Cfg::BN;
   const int Kpad = g.kblocks * BK;
   CUtensorMap tw, tx;
@@ -1910,15 +1915,15 @@ bool launch_conv_pair(ConvArgs g, const float* w0, const char* op) {
   g.n_tiles = (int)cdiv(g.Cout, BN);
   g.m_tiles = (int)cdiv(g.M, 2 * BM);
   g.tiles = (int64_t)g.m_tiles * g.n_tiles;
-  g.direct_epi = 0;
-  auto kern = conv_tc2_kernel<STAGES>;
+  g.direct_epi = direct_epilogue() ? 1 : 0;
+  auto kern = conv_tc2_kernel<BN_, STAGES>;
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
-  cfg.blockDim = dim3(kConvThreads, 1, 1);
+  cfg.blockDim = dim3(kPairThreads, 1, 1);
   cfg.dynamicSmemBytes = Cfg::SMEM;
   cfg.stream = ctx().stream;
   cfg.attrs = attr;
@@ -2414,10 +2419,13 @@ void conv_impl(Tensor* input, Tensor* weight, Tensor* bias, Tensor* residual, Te
         launch_halo<64, 3, 3, 32>(g, w0, op);
     }
   } else if (!split) {
-    if (Cout > 128 && g.mode == kIm2col128 && conv_pair_enabled())
-      launch_conv_pair<6>(g, w0, op);
+    const bool pair = g.mode == kIm2col128 && conv_pair_enabled();
+    if (Cout > 128 && pair)
+      launch_conv_pair<256, 6>(g, w0, op);
     else if (Cout > 128)
       launch_conv<256, 1, 4>(g, w0, nullptr, op);
+    else if (Cout > 64 && pair)
+      launch_conv_pair<128, 8>(g, w0, op);
     else if (Cout > 64)
       launch_conv<128, 1, 6>(g, w0, nullptr, op);
     else

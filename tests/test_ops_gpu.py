@@ -205,9 +205,9 @@ def test_conv_stride1_blocks_vs_oracle(cuda_lib, prec, cfg):
     C.assert_close(got_nhwc, want, C.TC_RTOL[prec], f"conv{cfg}[nhwc]")
 
 
-# C_out above 128 over 32-channel NHWC inputs runs on CTA pairs in TF32 mode
-# (one 256-pixel x 256-channel tile per pair, the odd CTA holding the upper
-# 128 pixels and weight rows): tiles whose upper half is partly or wholly past
+# C_out above 64 over 32-channel NHWC inputs runs on CTA pairs in TF32 mode
+# (one 256-pixel x 256- or 128-channel tile per pair, the odd CTA holding the
+# upper 128 pixels and half of the weight rows): tiles whose upper half is partly or wholly past
 # the last pixel (196, 49 and 784 pixels), partial channel tiles (384, 200 —
 # the latter not a multiple of 32), stride 2, and 98 tiles for fewer pairs,
 # so pairs run several tiles through both accumulators.
@@ -220,6 +220,10 @@ PAIR_CASES = [
     (2, 64, 16, 16, 384, 3, 1, 1, "nnc_conv_add_relu"),
     (2, 160, 10, 12, 200, 3, 1, 1, "nnc_conv"),
     (64, 32, 14, 14, 512, 3, 1, 1, "nnc_conv_add_relu"),
+    # C_out in (64, 128]: 128-channel pair tiles (the ResNet stage-2
+    # stride-2 conv; a 100-channel tile past a 20-row image's halo limit).
+    (2, 64, 56, 56, 128, 3, 2, 1, "nnc_conv_relu"),
+    (1, 96, 20, 20, 100, 3, 1, 1, "nnc_conv_add_relu"),
 ]
 
 
