@@ -118,6 +118,22 @@ int nnc_cuda_memcpy_async(void* dst, const void* src, size_t bytes, int kind);
 /* Number of kernels this thread has launched through the library. */
 long long nnc_cuda_launch_count(void);
 
+/* ---- CUDA graphs (no reference counterpart: the x86 runtime has no launch
+ * cost to hide) ----------------------------------------------------------------
+ * nnc_cuda_graph_begin starts capturing this thread's current stream (a
+ * stream set with nnc_cuda_set_stream); the library calls that follow are
+ * recorded, not run, until nnc_cuda_graph_end, which returns a replayable
+ * graph (NULL on failure: a call inside the capture failed, or the capture
+ * was invalidated). Run the same calls once uncaptured first: the workspace
+ * cannot grow during a capture. nnc_cuda_graph_launch replays the graph on
+ * the current stream (its tensors' addresses are fixed at capture) and adds
+ * its kernels to nnc_cuda_launch_count. */
+int nnc_cuda_graph_begin(void);
+void* nnc_cuda_graph_end(void);
+int nnc_cuda_graph_launch(void* graph);
+long long nnc_cuda_graph_kernels(const void* graph);
+void nnc_cuda_graph_destroy(void* graph);
+
 /* ---- observability ------------------------------------------------------------
  * When enabled (or NNC_CUDA_TRACE=1 in the environment), every operator call
  * records CUDA events around its launches; nnc_cuda_trace_dump prints one line

@@ -36,6 +36,10 @@ struct TraceRec {
 };
 thread_local std::vector<TraceRec> t_trace;
 int g_trace_on = -1;  // -1: read NNC_CUDA_TRACE on first use
+// Between nnc_cuda_graph_begin and nnc_cuda_graph_end: the calls of this
+// thread are being captured (no tracing, no workspace growth).
+thread_local bool t_capturing = false;
+thread_local long long t_capture_launches0 = 0;
 
 bool trace_on() {
   if (g_trace_on < 0) {
@@ -139,6 +143,15 @@ void* workspace(size_t bytes, const char* op) {
     return nullptr;
   }
   if (bytes <= t_ws.cap[d]) return t_ws.ptr[d];
+  if (t_capturing) {
+    // Memory allocated inside a graph lives only while the graph runs; the
+    // workspace must already be large enough.
+    fail(NNC_CUDA_ERR_INVALID, op,
+         "needs %zu bytes of workspace while a graph is being captured (it holds %zu): run the "
+         "same calls once before capturing them",
+         bytes, t_ws.cap[d]);
+    return nullptr;
+  }
   // Grow stream-ordered: earlier work on this stream that still reads the
   // old buffer completes before the free takes effect.
   size_t want = bytes + bytes / 4;
@@ -158,7 +171,7 @@ void* workspace(size_t bytes, const char* op) {
 OpScope::OpScope(const char* name) : name_(name), slot_(-1) {
   int dev = 0;
   if (cudaGetDevice(&dev) == cudaSuccess && dev >= 0 && dev < kMaxDevices) ctx().device = dev;
-  if (!trace_on()) return;
+  if (!trace_on() || t_capturing) return;
   TraceRec r{name, nullptr, nullptr};
   cudaEventCreate(&r.start);
   cudaEventCreate(&r.stop);
@@ -259,6 +272,77 @@ int nnc_cuda_memcpy_async(void* dst, const void* src, size_t bytes, int kind) {
 }
 
 long long nnc_cuda_launch_count(void) { return ctx().launches; }
+
+// ---- CUDA graphs ---------------------------------------------------------
+struct NncGraph {
+  cudaGraphExec_t exec;
+  long long kernels;  // library kernels in one replay
+};
+
+int nnc_cuda_graph_begin(void) {
+  const char* op = "nnc_cuda_graph_begin";
+  if (t_capturing) {
+    fail(NNC_CUDA_ERR_INVALID, op, "a capture is already open on this thread");
+    return NNC_CUDA_ERR_INVALID;
+  }
+  if (ctx().stream == nullptr) {
+    fail(NNC_CUDA_ERR_INVALID, op, "capture needs a created stream (nnc_cuda_set_stream), not the "
+                                   "legacy default stream");
+    return NNC_CUDA_ERR_INVALID;
+  }
+  if (!check_cuda(cudaStreamBeginCapture(ctx().stream, cudaStreamCaptureModeThreadLocal), op,
+                  "cudaStreamBeginCapture"))
+    return ctx().status;
+  t_capturing = true;
+  t_capture_launches0 = ctx().launches;
+  return NNC_CUDA_OK;
+}
+
+void* nnc_cuda_graph_end(void) {
+  const char* op = "nnc_cuda_graph_end";
+  if (!t_capturing) {
+    fail(NNC_CUDA_ERR_INVALID, op, "no capture is open on this thread");
+    return nullptr;
+  }
+  t_capturing = false;
+  cudaGraph_t graph = nullptr;
+  if (!check_cuda(cudaStreamEndCapture(ctx().stream, &graph), op, "cudaStreamEndCapture"))
+    return nullptr;
+  const long long kernels = ctx().launches - t_capture_launches0;
+  ctx().launches = t_capture_launches0;  // captured, not launched
+  if (ctx().status != NNC_CUDA_OK) {  // a call inside the capture failed
+    cudaGraphDestroy(graph);
+    return nullptr;
+  }
+  cudaGraphExec_t exec = nullptr;
+  const bool ok = check_cuda(cudaGraphInstantiate(&exec, graph, 0), op, "cudaGraphInstantiate");
+  cudaGraphDestroy(graph);
+  if (!ok) return nullptr;
+  return new NncGraph{exec, kernels};
+}
+
+int nnc_cuda_graph_launch(void* graph) {
+  const char* op = "nnc_cuda_graph_launch";
+  if (!graph) {
+    fail(NNC_CUDA_ERR_INVALID, op, "NULL graph");
+    return NNC_CUDA_ERR_INVALID;
+  }
+  NncGraph* g = static_cast<NncGraph*>(graph);
+  if (!check_cuda(cudaGraphLaunch(g->exec, ctx().stream), op, "cudaGraphLaunch")) return ctx().status;
+  ctx().launches += g->kernels;
+  return NNC_CUDA_OK;
+}
+
+long long nnc_cuda_graph_kernels(const void* graph) {
+  return graph ? static_cast<const NncGraph*>(graph)->kernels : 0;
+}
+
+void nnc_cuda_graph_destroy(void* graph) {
+  if (!graph) return;
+  NncGraph* g = static_cast<NncGraph*>(graph);
+  cudaGraphExecDestroy(g->exec);
+  delete g;
+}
 
 int nnc_cuda_trace_count(void) {
   cudaStreamSynchronize(ctx().stream);

@@ -93,6 +93,30 @@ class CudaModel:
         """Enqueues one forward pass on the current stream (no sync)."""
         self.lib.nnc_run()
 
+    def capture(self) -> None:
+        """Records one forward pass on the library's current stream (set with
+        set_stream) into a CUDA graph; replay() then enqueues it in one
+        launch. Run the model once uncaptured first (workspace sizing)."""
+        self.release_graph()
+        if self.rt.nnc_cuda_graph_begin() != 0:
+            raise RuntimeError(f"capture failed: {self.rt.nnc_cuda_get_last_error_string()}")
+        self.lib.nnc_run()
+        g = self.rt.nnc_cuda_graph_end()
+        if not g:
+            raise RuntimeError(f"capture failed: {self.rt.nnc_cuda_get_last_error_string()}")
+        self.graph = g
+
+    def replay(self) -> None:
+        """Enqueues the captured forward pass on the current stream (no sync)."""
+        if self.rt.nnc_cuda_graph_launch(self.graph) != 0:
+            raise RuntimeError(f"graph launch failed: {self.rt.nnc_cuda_get_last_error_string()}")
+
+    def release_graph(self) -> None:
+        g = getattr(self, "graph", None)
+        if g:
+            self.rt.nnc_cuda_graph_destroy(g)
+        self.graph = None
+
     def run_host(self, x: np.ndarray) -> np.ndarray:
         """Host-buffer forward (H2D, forward, D2H; synchronous)."""
         x = np.ascontiguousarray(x, dtype=np.float32)

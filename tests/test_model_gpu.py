@@ -73,3 +73,52 @@ def test_transformer_matches_reference_x86_build(cuda_lib, golden):
         cuda_lib.nnc_cuda_set_precision(prec)
         got = m.run_host(golden["transformer_b1/input"])
         C.assert_close(got, golden["transformer_b1/output"], MODEL_RTOL[prec], f"transformer prec{prec}")
+
+
+def test_graph_replay_matches_direct_run(cuda_lib, golden):
+    """A forward pass captured into a CUDA graph (nnc_cuda_graph_*) and
+    replayed gives bit-identical logits to direct runs on new inputs written
+    into the same input tensor, and counts its kernels per replay."""
+    import ctypes
+
+    import torch
+
+    m = _model("resnet18_o3_b2")
+    m.load_constants(W.resnet18(2))
+    cuda_lib.nnc_cuda_set_precision(L.PRECISION_TF32)
+    stream = torch.cuda.Stream()
+    m.set_stream(stream.cuda_stream)
+    n_in = int(np.prod(m.in_shape))
+    inp = torch.empty(n_in, dtype=torch.float32, device="cuda")
+    out = torch.empty(int(np.prod(m.out_shape)), dtype=torch.float32, device="cuda")
+    r = np.random.default_rng(3)
+    xs = [golden["resnet18_b2/input"].ravel()] + [r.standard_normal(n_in).astype(np.float32) for _ in range(2)]
+
+    def run(x, graph):
+        inp.copy_(torch.from_numpy(x))
+        torch.cuda.synchronize()
+        cuda_lib.nnc_cuda_memcpy_async(ctypes.c_void_p(m.input_ptr()), ctypes.c_void_p(inp.data_ptr()), n_in * 4, 3)
+        m.replay() if graph else m.run()
+        cuda_lib.nnc_cuda_memcpy_async(ctypes.c_void_p(out.data_ptr()), ctypes.c_void_p(m.output_ptr()),
+                                       out.numel() * 4, 3)
+        stream.synchronize()
+        assert cuda_lib.nnc_cuda_get_last_error() == 0, cuda_lib.nnc_cuda_get_last_error_string()
+        return out.cpu().numpy().copy()
+
+    direct = [run(x, False) for x in xs]
+    before = cuda_lib.nnc_cuda_launch_count()
+    m.capture()
+    assert cuda_lib.nnc_cuda_launch_count() == before  # captured, not launched
+    kernels = cuda_lib.nnc_cuda_graph_kernels(m.graph)
+    assert kernels > 10
+    try:
+        for x, want in zip(xs, direct):
+            c0 = cuda_lib.nnc_cuda_launch_count()
+            got = run(x, True)
+            assert cuda_lib.nnc_cuda_launch_count() - c0 == kernels
+            assert np.array_equal(got, want)
+    finally:
+        m.release_graph()
+        cuda_lib.nnc_cuda_set_stream(None)
+    C.assert_close(direct[0].reshape(m.out_shape), golden["resnet18_b2/output"], MODEL_RTOL[L.PRECISION_TF32],
+                   "direct run")
