@@ -429,11 +429,12 @@ bool split_batches(const float* src, int64_t in_bs, float* hi, float* lo, int64_
 void run_problem(Problem p, const char* op) {
   if ((int64_t)p.M * p.N * p.batches == 0) return;
   const bool tiny = p.M < 64 || p.N < 16 || (int64_t)p.M * p.N * p.K < (1 << 18);
-  // TMA needs 16-byte aligned bases and row pitches; A batches must be dense
-  // (the reference's overlapping batch offsets, see matmul_impl, take the
-  // SIMT path).
-  const bool tma_ok = (p.K % 4 == 0) && aligned16(p.A) && aligned16(p.B) &&
-                      (p.a_bs == 0 || p.a_bs == (int64_t)p.M * p.K) && p.K > 0;
+  // TMA needs 16-byte aligned bases, row pitches and batch strides. The
+  // reference's batch offsets (see matmul_impl) may overlap; the A tensor map
+  // takes the batch stride as given (overlapping reads are fine), and B's
+  // transpose reads it (batches come out dense).
+  const bool tma_ok = (p.K % 4 == 0) && aligned16(p.A) && aligned16(p.B) && (p.a_bs % 4 == 0) &&
+                      p.K > 0;
   if (tiny || !tma_ok) {
     launch_simt(p, op);
     return;

@@ -2,8 +2,11 @@
 //
 // All three decompose the tensor as [outer, dim, inner] around `axis` exactly
 // like the reference (ops.c:260-310, :2095-2171, :1892-1989).
-//   inner == 1 : one CTA per row; the row is read once into registers (up to
-//                kMaxVPT values per thread), reduced with warp shuffles, and
+//   inner == 1 : rows of at most 1024 elements take one warp per row (the
+//                row in registers, shuffle reductions only); longer rows one
+//                128-thread block per row with the row cached in shared
+//                memory (up to 32768 elements; beyond that, one 256-thread
+//                block per row re-reading it). Every element is read once and
 //                written once — 8 bytes of HBM traffic per element.
 //   inner  > 1 : one thread per (outer, inner) column walking `dim` with
 //                stride `inner`; consecutive threads read consecutive
@@ -107,6 +110,115 @@ __global__ void __launch_bounds__(kThreads) softmax_row_kernel(const float* __re
   }
 }
 
+// Short rows (dim <= 32 VPT): one warp per row, VPT values per lane in
+// registers, shuffle reductions only; 8 rows per 256-thread block.
+template <int VPT>
+__global__ void __launch_bounds__(kThreads) softmax_warp_kernel(const float* __restrict__ in,
+                                                                float* __restrict__ out,
+                                                                int64_t rows, int dim) {
+  const int lane = threadIdx.x & 31;
+  const int64_t step = (int64_t)gridDim.x * (kThreads / 32);
+  for (int64_t row = (int64_t)blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5); row < rows;
+       row += step) {
+    const float* x = in + row * dim;
+    float* y = out + row * dim;
+    float v[VPT];
+    float m = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      const int i = lane + 32 * k;
+      v[k] = i < dim ? x[i] : -INFINITY;
+      m = (v[k] > m) ? v[k] : m;
+    }
+    m = warp_max(m);
+    double sacc = 0.0;
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      if (lane + 32 * k < dim) {
+        v[k] = expf(v[k] - m);
+        sacc += (double)v[k];
+      }
+    }
+    const float sum = (float)warp_sum(sacc);
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      const int i = lane + 32 * k;
+      if (i < dim) y[i] = __fdiv_rn(v[k], sum);
+    }
+  }
+}
+
+// Long rows (dim <= kSmemRowMax): one 128-thread block per row with the row
+// cached in shared memory (dynamic, dim floats), so many rows are in flight
+// per SM; 16-byte accesses when dim % 4 == 0 and the bases are aligned.
+constexpr int kRowThreads = 128;
+constexpr int kSmemRowMax = 32768;  // 128 KB of shared memory
+__device__ double block_sum128(double v, double* red) {
+  v = warp_sum(v);
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  __syncthreads();
+  if (lane == 0) red[wid] = v;
+  __syncthreads();
+  return red[0] + red[1] + red[2] + red[3];
+}
+__device__ float block_max128(float v, float* red) {
+  v = warp_max(v);
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  __syncthreads();
+  if (lane == 0) red[wid] = v;
+  __syncthreads();
+  const float a = red[0] > red[1] ? red[0] : red[1];
+  const float b = red[2] > red[3] ? red[2] : red[3];
+  return a > b ? a : b;
+}
+__global__ void __launch_bounds__(kRowThreads) softmax_smem_kernel(const float* __restrict__ in,
+                                                                   float* __restrict__ out,
+                                                                   int64_t rows, int dim) {
+  extern __shared__ __align__(16) float rowbuf[];
+  __shared__ double red_d[4];
+  __shared__ float red_f[4];
+  const bool vec = (dim & 3) == 0 && ((((uintptr_t)in) | ((uintptr_t)out)) & 15) == 0;
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+    const float* x = in + row * dim;
+    float* y = out + row * dim;
+    float m = -INFINITY;
+    if (vec) {
+      for (int i = threadIdx.x; i < dim / 4; i += kRowThreads) {
+        const float4 t = reinterpret_cast<const float4*>(x)[i];
+        reinterpret_cast<float4*>(rowbuf)[i] = t;
+        m = (t.x > m) ? t.x : m;
+        m = (t.y > m) ? t.y : m;
+        m = (t.z > m) ? t.z : m;
+        m = (t.w > m) ? t.w : m;
+      }
+    } else {
+      for (int i = threadIdx.x; i < dim; i += kRowThreads) {
+        const float t = x[i];
+        rowbuf[i] = t;
+        m = (t > m) ? t : m;
+      }
+    }
+    m = block_max128(m, red_f);
+    double sacc = 0.0;
+    for (int i = threadIdx.x; i < dim; i += kRowThreads) {
+      const float e = expf(rowbuf[i] - m);
+      rowbuf[i] = e;
+      sacc += (double)e;
+    }
+    const float sum = (float)block_sum128(sacc, red_d);
+    if (vec) {
+      for (int i = threadIdx.x; i < dim / 4; i += kRowThreads) {
+        const float4 e = reinterpret_cast<const float4*>(rowbuf)[i];
+        reinterpret_cast<float4*>(y)[i] =
+            make_float4(__fdiv_rn(e.x, sum), __fdiv_rn(e.y, sum), __fdiv_rn(e.z, sum), __fdiv_rn(e.w, sum));
+      }
+    } else {
+      for (int i = threadIdx.x; i < dim; i += kRowThreads) y[i] = __fdiv_rn(rowbuf[i], sum);
+    }
+    __syncthreads();  // rowbuf is reused by the next row
+  }
+}
+
 // Strided kernel (inner > 1): one thread per (outer, inner) column.
 __global__ void __launch_bounds__(kThreads) softmax_col_kernel(const float* __restrict__ in,
                                                                float* __restrict__ out,
@@ -191,6 +303,87 @@ __global__ void __launch_bounds__(kThreads) layernorm_kernel(
         y[i] = __fadd_rn(__fmul_rn(g, __fdiv_rn(__fsub_rn(x[i], mean), sd)), b);
       }
     }
+  }
+}
+
+// Short slabs (len <= 32 VPT): one warp per slab; `inner` == 1 indexes
+// scale/bias by the element, else by i / inner (32-bit: len fits).
+template <int VPT>
+__global__ void __launch_bounds__(kThreads) layernorm_warp_kernel(
+    const float* __restrict__ in, const float* __restrict__ scale, const float* __restrict__ bias,
+    float* __restrict__ out, int64_t rows, int len, int inner, float eps) {
+  const int lane = threadIdx.x & 31;
+  const int64_t step = (int64_t)gridDim.x * (kThreads / 32);
+  const float inv_n = (float)len;
+  for (int64_t row = (int64_t)blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5); row < rows;
+       row += step) {
+    const float* x = in + row * len;
+    float* y = out + row * len;
+    float v[VPT];
+    double sacc = 0.0;
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      const int i = lane + 32 * k;
+      v[k] = i < len ? x[i] : 0.0f;
+      sacc += (double)v[k];
+    }
+    const float mean = __fdiv_rn((float)warp_sum(sacc), inv_n);
+    double q = 0.0;
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      if (lane + 32 * k < len) {
+        const float d = __fsub_rn(v[k], mean);
+        q += (double)__fmul_rn(d, d);
+      }
+    }
+    const float var = __fdiv_rn((float)warp_sum(q), inv_n);
+    const float sd = __fsqrt_rn(__fadd_rn(var, eps));
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      const int i = lane + 32 * k;
+      if (i < len) {
+        const int a = inner == 1 ? i : i / inner;
+        const float gm = scale ? __ldg(scale + a) : 1.0f;
+        const float bt = bias ? __ldg(bias + a) : 0.0f;
+        y[i] = __fadd_rn(__fmul_rn(gm, __fdiv_rn(__fsub_rn(v[k], mean), sd)), bt);
+      }
+    }
+  }
+}
+
+// Long slabs (len <= kSmemRowMax): one 128-thread block per slab, the slab
+// cached in shared memory.
+__global__ void __launch_bounds__(kRowThreads) layernorm_smem_kernel(
+    const float* __restrict__ in, const float* __restrict__ scale, const float* __restrict__ bias,
+    float* __restrict__ out, int64_t rows, int len, int inner, float eps) {
+  extern __shared__ __align__(16) float rowbuf[];
+  __shared__ double red_d[4];
+  const float inv_n = (float)len;
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+    const float* x = in + row * len;
+    float* y = out + row * len;
+    double sacc = 0.0;
+    for (int i = threadIdx.x; i < len; i += kRowThreads) {
+      const float t = x[i];
+      rowbuf[i] = t;
+      sacc += (double)t;
+    }
+    const float mean = __fdiv_rn((float)block_sum128(sacc, red_d), inv_n);
+    double q = 0.0;
+    for (int i = threadIdx.x; i < len; i += kRowThreads) {
+      const float d = __fsub_rn(rowbuf[i], mean);
+      q += (double)__fmul_rn(d, d);
+    }
+    __syncthreads();  // red_d is reused
+    const float var = __fdiv_rn((float)block_sum128(q, red_d), inv_n);
+    const float sd = __fsqrt_rn(__fadd_rn(var, eps));
+    for (int i = threadIdx.x; i < len; i += kRowThreads) {
+      const int a = inner == 1 ? i : i / inner;
+      const float gm = scale ? __ldg(scale + a) : 1.0f;
+      const float bt = bias ? __ldg(bias + a) : 0.0f;
+      y[i] = __fadd_rn(__fmul_rn(gm, __fdiv_rn(__fsub_rn(rowbuf[i], mean), sd)), bt);
+    }
+    __syncthreads();  // rowbuf and red_d are reused by the next slab
   }
 }
 
@@ -312,7 +505,32 @@ void nnc_softmax(Tensor* input, Tensor* output, int axis) {
   if (outer * dim * inner == 0) return;
   const float* pi = (const float*)input->data;
   float* po = (float*)output->data;
-  if (inner == 1) {
+  if (inner == 1 && dim <= 1024) {
+    const int64_t blocks = cdiv(outer, (int64_t)(kThreads / 32));
+    const int grid = (int)(blocks < (int64_t)sm_count() * 16 ? blocks : (int64_t)sm_count() * 16);
+    const int d = (int)dim;
+    if (dim <= 32)
+      softmax_warp_kernel<1><<<grid, kThreads, 0, ctx().stream>>>(pi, po, outer, d);
+    else if (dim <= 64)
+      softmax_warp_kernel<2><<<grid, kThreads, 0, ctx().stream>>>(pi, po, outer, d);
+    else if (dim <= 128)
+      softmax_warp_kernel<4><<<grid, kThreads, 0, ctx().stream>>>(pi, po, outer, d);
+    else if (dim <= 256)
+      softmax_warp_kernel<8><<<grid, kThreads, 0, ctx().stream>>>(pi, po, outer, d);
+    else if (dim <= 512)
+      softmax_warp_kernel<16><<<grid, kThreads, 0, ctx().stream>>>(pi, po, outer, d);
+    else
+      softmax_warp_kernel<32><<<grid, kThreads, 0, ctx().stream>>>(pi, po, outer, d);
+  } else if (inner == 1 && dim <= kSmemRowMax) {
+    const size_t smem = (size_t)dim * 4;
+    if (smem > 48 * 1024 &&
+        !check_cuda(cudaFuncSetAttribute(softmax_smem_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)(kSmemRowMax * 4)),
+                    op, "cudaFuncSetAttribute"))
+      return;
+    const int grid = (int)(outer < (int64_t)sm_count() * 16 ? outer : (int64_t)sm_count() * 16);
+    softmax_smem_kernel<<<grid, kRowThreads, smem, ctx().stream>>>(pi, po, outer, (int)dim);
+  } else if (inner == 1) {
     const int grid = (int)(outer < (int64_t)sm_count() * 8 ? outer : (int64_t)sm_count() * 8);
     softmax_row_kernel<<<grid, kThreads, 0, ctx().stream>>>(pi, po, outer, dim);
   } else {
@@ -340,10 +558,39 @@ void nnc_layernorm(Tensor* input, Tensor* scale, Tensor* bias, Tensor* output, i
     return;
   }
   if (outer * norm * inner == 0) return;
-  const int grid = (int)(outer < (int64_t)sm_count() * 8 ? outer : (int64_t)sm_count() * 8);
-  layernorm_kernel<<<grid, kThreads, 0, ctx().stream>>>(
-      (const float*)input->data, scale ? (const float*)scale->data : nullptr,
-      bias ? (const float*)bias->data : nullptr, (float*)output->data, outer, norm, inner, epsilon);
+  const float* pi = (const float*)input->data;
+  const float* ps = scale ? (const float*)scale->data : nullptr;
+  const float* pb = bias ? (const float*)bias->data : nullptr;
+  float* po = (float*)output->data;
+  const int64_t len = norm * inner;
+  if (len <= 1024) {
+    const int64_t blocks = cdiv(outer, (int64_t)(kThreads / 32));
+    const int grid = (int)(blocks < (int64_t)sm_count() * 16 ? blocks : (int64_t)sm_count() * 16);
+    const int l = (int)len, in1 = (int)inner;
+    if (len <= 64)
+      layernorm_warp_kernel<2><<<grid, kThreads, 0, ctx().stream>>>(pi, ps, pb, po, outer, l, in1, epsilon);
+    else if (len <= 128)
+      layernorm_warp_kernel<4><<<grid, kThreads, 0, ctx().stream>>>(pi, ps, pb, po, outer, l, in1, epsilon);
+    else if (len <= 256)
+      layernorm_warp_kernel<8><<<grid, kThreads, 0, ctx().stream>>>(pi, ps, pb, po, outer, l, in1, epsilon);
+    else if (len <= 512)
+      layernorm_warp_kernel<16><<<grid, kThreads, 0, ctx().stream>>>(pi, ps, pb, po, outer, l, in1, epsilon);
+    else
+      layernorm_warp_kernel<32><<<grid, kThreads, 0, ctx().stream>>>(pi, ps, pb, po, outer, l, in1, epsilon);
+  } else if (len <= kSmemRowMax) {
+    const size_t smem = (size_t)len * 4;
+    if (smem > 48 * 1024 &&
+        !check_cuda(cudaFuncSetAttribute(layernorm_smem_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)(kSmemRowMax * 4)),
+                    op, "cudaFuncSetAttribute"))
+      return;
+    const int grid = (int)(outer < (int64_t)sm_count() * 16 ? outer : (int64_t)sm_count() * 16);
+    layernorm_smem_kernel<<<grid, kRowThreads, smem, ctx().stream>>>(pi, ps, pb, po, outer, (int)len,
+                                                                       (int)inner, epsilon);
+  } else {
+    const int grid = (int)(outer < (int64_t)sm_count() * 8 ? outer : (int64_t)sm_count() * 8);
+    layernorm_kernel<<<grid, kThreads, 0, ctx().stream>>>(pi, ps, pb, po, outer, norm, inner, epsilon);
+  }
   check_launch(op);
 }
 

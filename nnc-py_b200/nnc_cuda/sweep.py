@@ -1,0 +1,233 @@
+"""Measures the BASELINE configurations that bench.py does not, on one GPU:
+the single-op sweep against the measured peaks (tensor pipe for conv/GEMM,
+HBM for every other op) and the model throughput of LeNet-5 (N = 8192),
+ResNet-18 -O1 (N = 64, 256) and the small transformer (B = 256).
+
+    python -m nnc_cuda.sweep [--reps 10] [--json sweep.json] [--only ops|models]
+
+Every number is a median over `reps` calls timed with CUDA events on the
+launching stream. Before each timed op call the runner reads a 512 MB buffer
+(larger than the 126 MB L2), so inputs come from HBM; a model step replays one
+captured CUDA graph. Denominators: MEASURED_PEAKS.json at the repository root
+(HBM copy GB/s; dense TF32 = bf16 burst / 2, each op being timed alone), else
+the pool's fallback figures (6650 GB/s, 1590 TFLOP/s bf16). Inputs are seeded
+N(0, 1), the shapes are BASELINE.json's.
+"""
+
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import pathlib
+import statistics
+
+import numpy as np
+
+from . import lib as L
+from . import tensor as T
+
+ROOT = pathlib.Path(__file__).resolve().parents[2]
+
+
+def peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "tf32_tflops": d["bf16_tflops"] / 2.0, "source": "measured"}
+    return {"hbm_gbs": 6650.0, "tf32_tflops": 1590.0 / 2.0, "source": "fallback"}
+
+
+class Timer:
+    def __init__(self, so, torch, stream, reps: int):
+        self.so, self.torch, self.stream, self.reps = so, torch, stream, reps
+        self.flush_buf = torch.empty(512 << 18, dtype=torch.float32, device="cuda")  # 512 MB
+
+    def time_op(self, fn, warmup: int = 2) -> float:
+        """Median device time in ms of fn() (library calls on the stream)."""
+        torch = self.torch
+        with torch.cuda.stream(self.stream):
+            for _ in range(warmup):
+                fn()
+        self.stream.synchronize()
+        times = []
+        for _ in range(self.reps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with torch.cuda.stream(self.stream):
+                # Read (not write) the buffer: L2 then holds clean lines, so
+                # the timed call pays no write-back of the flush.
+                self.flush_sink = self.flush_buf.sum()
+                e0.record(self.stream)
+                fn()
+                e1.record(self.stream)
+            e1.synchronize()
+            times.append(e0.elapsed_time(e1))
+        if self.so.nnc_cuda_get_last_error() != 0:
+            raise RuntimeError(self.so.nnc_cuda_get_last_error_string().decode())
+        return statistics.median(times)
+
+
+def op_sweep(so, torch, timer: Timer, pk: dict) -> list[dict]:
+    g = torch.Generator(device="cuda").manual_seed(1)
+    rows = []
+
+    def rnd(*shape):
+        return torch.randn(*shape, generator=g, device="cuda")
+
+    def hbm(name, shape, fn, nbytes):
+        ms = timer.time_op(fn)
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        rows.append({"op": name, "shape": list(shape), "ms": round(ms, 4), "bound": "hbm",
+                     "algorithmic_bytes": int(nbytes), "achieved": round(gbs, 1), "unit": "GB/s",
+                     "frac": round(gbs / pk["hbm_gbs"], 3)})
+
+    def tensor(name, shape, fn, flops, note=""):
+        ms = timer.time_op(fn)
+        tfs = flops / (ms * 1e-3) / 1e12
+        row = {"op": name, "shape": list(shape), "ms": round(ms, 4), "bound": "tensor",
+               "flops": int(flops), "achieved": round(tfs, 1), "unit": "TFLOP/s",
+               "frac": round(tfs / pk["tf32_tflops"], 3)}
+        if note:
+            row["note"] = note
+        rows.append(row)
+
+    # GEMM M = N = K (NN and NT).
+    for n in (512, 2048, 8192):
+        a, b, o = rnd(n, n), rnd(n, n), torch.empty(n, n, device="cuda")
+        ra, rb, ro = T.from_torch(a), T.from_torch(b), T.from_torch(o)
+        tensor("nnc_gemm", (n, n, n), lambda: so.nnc_gemm(ra.ptr, rb.ptr, None, ro.ptr, 1.0, 0.0, 0, 0), 2.0 * n ** 3)
+        tensor("nnc_gemm_nt", (n, n, n), lambda: so.nnc_gemm_nt(ra.ptr, rb.ptr, None, ro.ptr, 1.0, 0.0), 2.0 * n ** 3)
+        del a, b, o
+    # Conv 3x3 p1 s1 at batch 64: the reference API (NCHW tensors, converted
+    # inside the call) and channels-last tensors (what generated models pass).
+    for c, h in ((64, 56), (128, 28), (256, 14), (512, 7)):
+        n = 64
+        x, w, bias = rnd(n, c, h, h), rnd(c, c, 3, 3) * 0.05, rnd(c) * 0.01
+        o = torch.empty(n, c, h, h, device="cuda")
+        rx, rw, rbias, ro = T.from_torch(x), T.from_torch(w), T.from_torch(bias), T.from_torch(o)
+        fl = 2.0 * n * c * c * h * h * 9
+        tensor("nnc_conv 3x3 (NCHW)", (n, c, h, h),
+               lambda: so.nnc_conv(rx.ptr, rw.ptr, rbias.ptr, ro.ptr, 3, 3, 1, 1, 1, 1), fl,
+               "includes the NCHW -> channels-last copy of the input")
+        xl = x.permute(0, 2, 3, 1).contiguous()
+        ol = torch.empty(n, h, h, c, device="cuda")
+        wp = torch.empty(so.nnc_cuda_prepacked_conv_weight_bytes(rw.ptr) // 4, device="cuda")
+        rwp = T.from_torch(w.clone())
+        assert so.nnc_cuda_prepack_conv_weight(rwp.ptr, ctypes.c_void_p(wp.data_ptr()), wp.numel() * 4) == 0
+        rxl = T.from_torch(xl, tag=L.TAG_NHWC, shape=(n, c, h, h))
+        rol = T.from_torch(ol, tag=L.TAG_NHWC, shape=(n, c, h, h))
+        tensor("nnc_conv 3x3 (channels-last, prepacked)", (n, c, h, h),
+               lambda: so.nnc_conv(rxl.ptr, rwp.ptr, rbias.ptr, rol.ptr, 3, 3, 1, 1, 1, 1), fl)
+        del x, w, o, xl, ol, wp
+    # Element-wise on 2^28 elements.
+    n = 1 << 28
+    a, b, o = rnd(n), rnd(n), torch.empty(n, device="cuda")
+    ra, rb, ro = T.from_torch(a), T.from_torch(b), T.from_torch(o)
+    hbm("nnc_add", (n,), lambda: so.nnc_add(ra.ptr, rb.ptr, ro.ptr), 12 * n)
+    hbm("nnc_mul", (n,), lambda: so.nnc_mul(ra.ptr, rb.ptr, ro.ptr), 12 * n)
+    hbm("nnc_relu", (n,), lambda: so.nnc_relu(ra.ptr, ro.ptr), 8 * n)
+    hbm("nnc_sigmoid", (n,), lambda: so.nnc_sigmoid(ra.ptr, ro.ptr), 8 * n)
+    hbm("nnc_tanh", (n,), lambda: so.nnc_tanh(ra.ptr, ro.ptr), 8 * n)
+    hbm("nnc_clip [-1, 1]", (n,), lambda: so.nnc_clip(ra.ptr, ro.ptr, -1.0, 1.0), 8 * n)
+    del a, b, o
+    # Row ops.
+    x, o = rnd(4096, 4096), torch.empty(4096, 4096, device="cuda")
+    rx, ro = T.from_torch(x), T.from_torch(o)
+    hbm("nnc_softmax", (4096, 4096), lambda: so.nnc_softmax(rx.ptr, ro.ptr, 1), 8 * 4096 * 4096)
+    del x, o
+    x, o = rnd(32768, 1024), torch.empty(32768, 1024, device="cuda")
+    gam = torch.rand(1024, generator=g, device="cuda") + 0.5
+    bet = (torch.rand(1024, generator=g, device="cuda") - 0.5) * 0.2
+    rx, ro, rg, rbt = T.from_torch(x), T.from_torch(o), T.from_torch(gam), T.from_torch(bet)
+    hbm("nnc_layernorm", (32768, 1024), lambda: so.nnc_layernorm(rx.ptr, rg.ptr, rbt.ptr, ro.ptr, -1, 1e-5),
+        8 * 32768 * 1024 + 8 * 1024)
+    del x, o
+    x, o = rnd(16384, 4096), torch.empty(16384, 1, device="cuda")
+    rx, ro = T.from_torch(x), T.from_torch(o)
+    hbm("nnc_reducemean", (16384, 4096), lambda: so.nnc_reducemean(rx.ptr, ro.ptr, 1, 1), 4 * 16384 * 4096 + 4 * 16384)
+    hbm("nnc_reducesum", (16384, 4096), lambda: so.nnc_reducesum(rx.ptr, ro.ptr, 1, 1), 4 * 16384 * 4096 + 4 * 16384)
+    return rows
+
+
+# Algorithmic FLOPs per sample of the BASELINE models (conv + GEMM/matmul).
+MODEL_FLOPS = {"lenet5": 0.833e6, "resnet18": 3.628e9, "transformer": 0.872e9}
+
+
+def model_runs(so, torch, pk: dict, reps: int) -> list[dict]:
+    from .model import CudaModel
+    from .workloads import BUILDERS
+
+    rows = []
+    for tag, name, batch in (("lenet5_o1_b8192", "lenet5", 8192), ("resnet18_o1_b64", "resnet18", 64),
+                             ("resnet18_o1_b256", "resnet18", 256), ("transformer_o1_b256", "transformer", 256)):
+        m = CudaModel(tag)
+        m.init(0)
+        wl = BUILDERS[name](batch)
+        m.load_constants(wl)
+        stream = torch.cuda.Stream()
+        m.set_stream(stream.cuda_stream)
+        x = torch.from_numpy(wl.input_array(batch)).cuda()
+        so.nnc_cuda_memcpy_async(ctypes.c_void_p(m.input_ptr()), ctypes.c_void_p(x.data_ptr()),
+                                 x.numel() * 4, 3)
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                m.run()
+        stream.synchronize()
+        m.capture()
+        with torch.cuda.stream(stream):
+            m.replay()
+        stream.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for _ in range(reps):
+                m.replay()
+            e1.record(stream)
+        e1.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        m.release_graph()
+        so.nnc_cuda_set_stream(None)
+        if so.nnc_cuda_get_last_error() != 0:
+            raise RuntimeError(so.nnc_cuda_get_last_error_string().decode())
+        tf = MODEL_FLOPS[name] * batch / (ms * 1e-3) / 1e12
+        rows.append({"model": tag, "batch": batch, "ms_per_forward": round(ms, 4),
+                     "samples_per_s": round(batch / (ms * 1e-3), 1), "tflops": round(tf, 1),
+                     "frac_tf32": round(tf / pk["tf32_tflops"], 3)})
+    return rows
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reps", type=int, default=10)
+    ap.add_argument("--json", type=str, default=None)
+    ap.add_argument("--only", choices=["ops", "models"], default=None)
+    opt = ap.parse_args()
+    import torch
+
+    so = L.load()
+    torch.cuda.set_device(0)
+    if so.nnc_cuda_init(0) != 0:
+        raise RuntimeError("nnc_cuda_init failed")
+    so.nnc_cuda_set_precision(L.PRECISION_TF32)
+    pk = peaks()
+    stream = torch.cuda.Stream()
+    so.nnc_cuda_set_stream(ctypes.c_void_p(stream.cuda_stream))
+    out = {"peaks": pk, "precision": "tf32"}
+    if opt.only in (None, "ops"):
+        out["ops"] = op_sweep(so, torch, Timer(so, torch, stream, opt.reps), pk)
+        for r in out["ops"]:
+            print(f"{r['op']:42s} {str(r['shape']):22s} {r['ms']:9.4f} ms {r['achieved']:9.1f} {r['unit']:8s} "
+                  f"{r['frac']:.3f}", flush=True)
+    if opt.only in (None, "models"):
+        so.nnc_cuda_set_stream(None)
+        out["models"] = model_runs(so, torch, pk, max(opt.reps, 20))
+        for r in out["models"]:
+            print(f"{r['model']:22s} {r['ms_per_forward']:9.4f} ms {r['samples_per_s']:12.1f} /s "
+                  f"{r['tflops']:7.1f} TF/s {r['frac_tf32']:.3f}", flush=True)
+    if opt.json:
+        pathlib.Path(opt.json).write_text(json.dumps(out, indent=1))
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

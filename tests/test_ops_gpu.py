@@ -345,6 +345,36 @@ def test_conv_relu_maxpool_vs_oracle(cuda_lib, prec, cfg):
         C.assert_close(got, want, C.TC_RTOL[prec], f"conv_relu_maxpool{cfg}[{layout}]")
 
 
+# Row-op dispatch: one warp per row up to 1024 elements, a block per row with
+# the row in shared memory up to 32768, a block re-reading the row beyond;
+# LayerNorm slabs over several axes (scale/bias indexed by i / inner) on the
+# warp and shared-memory paths. Tolerances as in the seeded cases.
+ROW_CASES = [
+    ("nnc_softmax", (300, 10), 1), ("nnc_softmax", (64, 1024), 1), ("nnc_softmax", (4, 4096), 1),
+    ("nnc_softmax", (2, 40000), 1), ("nnc_layernorm", (8, 1024), -1), ("nnc_layernorm", (5, 2000), -1),
+    ("nnc_layernorm", (2, 40000), -1), ("nnc_layernorm", (3, 4, 200), 1), ("nnc_layernorm", (2, 40, 50), 1),
+]
+
+
+@pytest.mark.parametrize("case", ROW_CASES, ids=lambda c: f"{c[0]}_{'x'.join(map(str, c[1]))}")
+def test_row_ops_dispatch_vs_oracle(cuda_lib, case):
+    op, shape, axis = case
+    r = np.random.default_rng(sum(shape) + len(op))
+    x = (r.standard_normal(shape) * 2).astype(np.float32)
+    arrays = {"x": x}
+    if op == "nnc_softmax":
+        args, tol = [C._t("x"), C._o("out", shape), C._i(axis)], 2e-6
+    else:
+        norm = int(np.prod(shape[axis:])) // int(np.prod(shape[axis + 1:])) if axis >= 0 else shape[-1]
+        arrays["g"] = r.uniform(0.5, 1.5, norm).astype(np.float32)
+        arrays["b"] = r.uniform(-0.1, 0.1, norm).astype(np.float32)
+        args, tol = [C._t("x"), C._t("g"), C._t("b"), C._o("out", shape), C._i(axis), C._f(1e-5)], 1e-5
+    c = {"name": "row", "op": op, "args": args}
+    want = C.run_host(_oracle(), c, arrays)["out"]
+    got = C.run_cuda(cuda_lib, c, arrays)["out"]
+    C.assert_close(got, want, tol, f"{op}{shape}")
+
+
 # ------------------------------------------------------------ validation --
 def test_invalid_shapes_set_status_without_launch(cuda_lib):
     import torch
