@@ -1797,6 +1797,86 @@ __global__ void __launch_bounds__(256) s2d_weight_kernel(const float* __restrict
   }
 }
 
+// ---------------------------------------------------- direct small conv ----
+// Convolutions with few output channels and a short reduction (C_out <= 16,
+// C KH KW <= 256: LeNet's 1 -> 6 and 6 -> 16 5x5 layers) on the CUDA cores:
+// a tensor-core tile would be mostly padding (N >= 64 of 16 channels, K
+// padded to 32), and the work is an HBM-bound stencil. One thread per output
+// pixel holds all C_out accumulators; each block stages the weights once in
+// shared memory as [c][kh][kw][co] (CO floats per tap, read by every thread
+// at the same address: a broadcast) in full fp32 (hi + lo planes of a
+// prepacked weight). Accumulation is fp32 FMA over k = (c, kh, kw), the
+// reference's order; bias, residual and activation as in store_tile.
+constexpr int kDirectMaxK = 256;
+template <int CO>
+__global__ void __launch_bounds__(128) conv_direct_kernel(ConvArgs g, const float* __restrict__ w,
+                                                          int src_mode, int src_c4, int src_kpad) {
+  __shared__ __align__(16) float ws[kDirectMaxK * CO];
+  const int K = g.K;  // C KH KW
+  const int C = K / (g.KH * g.KW);
+  for (int idx = threadIdx.x; idx < K * CO; idx += blockDim.x) {
+    const int k = idx / CO, co = idx - k * CO;
+    float v = 0.0f;
+    if (co < g.Cout) {
+      const int c = k / (g.KH * g.KW), t = k - c * (g.KH * g.KW);
+      if (src_mode == 0) {  // OIHW
+        v = w[(int64_t)co * K + k];
+      } else {
+        // Prepacked: [hi, lo][C_out][K_pad], chunk (tap, c) or element order.
+        const int64_t off = (int64_t)co * src_kpad + (src_mode == 1 ? t * src_c4 + c : k);
+        v = __fadd_rn(w[off], w[(int64_t)g.Cout * src_kpad + off]);
+      }
+    }
+    ws[k * CO + co] = v;
+  }
+  __syncthreads();
+  const int64_t OHW = (int64_t)g.OH * g.OW;
+  const bool add = g.act == kActAddRelu;
+  for (int64_t m = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; m < g.M;
+       m += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t n = m / OHW;
+    const int p = (int)(m - n * OHW);
+    const int oh = p / g.OW, ow = p - oh * g.OW;
+    const int ih0 = oh * g.sh - g.ph, iw0 = ow * g.sw - g.pw;
+    float acc[CO];
+#pragma unroll
+    for (int co = 0; co < CO; ++co) acc[co] = 0.0f;
+    // Element offsets stay 32-bit inside one image (host-checked).
+    const float* xn = g.x_hi + n * g.xs_n;
+    const int sc = (int)g.xs_c, shh = (int)g.xs_h, sww = (int)g.xs_w;
+    const float4* wk = reinterpret_cast<const float4*>(ws);
+    for (int c = 0; c < C; ++c) {
+      const float* xc = xn + c * sc;
+      for (int kh = 0; kh < g.KH; ++kh) {
+        const int ih = ih0 + kh;
+        const bool row_ok = (unsigned)ih < (unsigned)g.H;
+        const float* xr = xc + ih * shh;
+        for (int kw = 0; kw < g.KW; ++kw, wk += CO / 4) {
+          const int iw = iw0 + kw;
+          const float xv = (row_ok && (unsigned)iw < (unsigned)g.W) ? __ldg(xr + iw * sww) : 0.0f;
+#pragma unroll
+          for (int q = 0; q < CO / 4; ++q) {
+            const float4 wv = wk[q];
+            acc[4 * q] = fmaf(xv, wv.x, acc[4 * q]);
+            acc[4 * q + 1] = fmaf(xv, wv.y, acc[4 * q + 1]);
+            acc[4 * q + 2] = fmaf(xv, wv.z, acc[4 * q + 2]);
+            acc[4 * q + 3] = fmaf(xv, wv.w, acc[4 * q + 3]);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int co = 0; co < CO; ++co) {
+      if (co >= g.Cout) break;
+      const int64_t off = g.out_nhwc ? m * g.Cout + co : (n * g.Cout + co) * OHW + p;
+      float o = acc[co];
+      if (g.bias) o = __fadd_rn(o, __ldg(g.bias + co));
+      if (add) o = __fadd_rn(o, __ldg(g.residual + off));
+      g.out[off] = activate(o, g.act);
+    }
+  }
+}
+
 struct WeightLayout {
   int element;
   int C4;    // chunk mode: channels per tap as stored (multiple of 4)
@@ -2148,6 +2228,48 @@ void conv_impl(Tensor* input, Tensor* weight, Tensor* bias, Tensor* residual, Te
   const int64_t M = (int64_t)N * OH * OW;
   if (M == 0 || Cout == 0) return;
   const bool split = ctx().precision == NNC_CUDA_PRECISION_3XTF32;
+  // Few output channels and a short reduction: the direct CUDA-core kernel
+  // (full fp32, so either precision mode).
+  if (!pool && Cout <= 16 && (int64_t)C * KH * KW <= kDirectMaxK && (int64_t)C * H * W < (1ll << 31)) {
+    const bool packed_w = (tag_of(weight) & NNC_CUDA_TAG_PACKED_CONV) != 0;
+    const WeightLayout wl0 = weight_layout(C, KH, KW);
+    ConvArgs g{};
+    g.N = N;
+    g.H = H;
+    g.W = W;
+    g.OH = OH;
+    g.OW = OW;
+    g.Cout = Cout;
+    g.KH = KH;
+    g.KW = KW;
+    g.sh = sh;
+    g.sw = sw;
+    g.ph = ph;
+    g.pw = pw;
+    g.K = C * KH * KW;
+    g.M = M;
+    g.x_hi = (const float*)input->data;
+    const bool in_nhwc = is_nhwc(input);
+    g.xs_n = (int64_t)C * H * W;
+    g.xs_c = in_nhwc ? 1 : (int64_t)H * W;
+    g.xs_h = in_nhwc ? (int64_t)W * C : W;
+    g.xs_w = in_nhwc ? C : 1;
+    g.bias = bias ? (const float*)bias->data : nullptr;
+    g.residual = residual ? (const float*)residual->data : nullptr;
+    g.out = (float*)output->data;
+    g.out_nhwc = is_nhwc(output) ? 1 : 0;
+    g.act = act;
+    const int src_mode = packed_w ? (wl0.element ? 2 : 1) : 0;
+    const int grid = (int)(cdiv(M, 128) < (int64_t)sm_count() * 8 ? cdiv(M, 128) : (int64_t)sm_count() * 8);
+    if (Cout <= 8)
+      conv_direct_kernel<8><<<grid, 128, 0, ctx().stream>>>(g, (const float*)weight->data, src_mode,
+                                                            wl0.C4, wl0.Kpad);
+    else
+      conv_direct_kernel<16><<<grid, 128, 0, ctx().stream>>>(g, (const float*)weight->data, src_mode,
+                                                             wl0.C4, wl0.Kpad);
+    check_launch(op);
+    return;
+  }
   const WeightLayout wl = weight_layout(C, KH, KW);
   const int C4 = wl.C4;
   const int Kpad = wl.Kpad;

@@ -42,6 +42,8 @@ struct GemmArgs {
   float* D;
   int64_t ldd, d_batch_stride;
   int relu;
+  int tma_store;  // 1: D written by TMA stores through tmD (dense, 16-byte rows)
+  int b_mn;       // 1: B tiles are MN-major ({32 n, 32 k} boxes of a [K, N] matrix)
   int* err;
 };
 
@@ -55,18 +57,23 @@ struct GemmCfg {
   static constexpr uint32_t B_BYTES = BN * BK * 4;
   static constexpr uint32_t STAGE_BYTES = SPLIT * (A_BYTES + B_BYTES);
   static constexpr uint32_t TMEM_COLS = 2 * BN;  // power of two for BN in {64,128,256}
-  static constexpr size_t SMEM = (size_t)STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*bars*/;
+  // Epilogue staging: per epilogue warp two 32 x 32 fp32 boxes (4 KB each).
+  static constexpr uint32_t STAGING_BYTES = 4 * 2 * 4096;
+  static constexpr size_t SMEM =
+      (size_t)STAGES * STAGE_BYTES + STAGING_BYTES + 1024 /*align*/ + 256 /*bars*/;
 };
 
 template <int BN, int SPLIT, int STAGES>
 __global__ void __launch_bounds__(kTCThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmA1,
                    const __grid_constant__ CUtensorMap tmB0, const __grid_constant__ CUtensorMap tmB1,
-                   const GemmArgs g) {
+                   const __grid_constant__ CUtensorMap tmD, const GemmArgs g) {
   using Cfg = GemmCfg<BN, SPLIT, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES);
+  float* staging = reinterpret_cast<float*>(smem + STAGES * Cfg::STAGE_BYTES);
+  uint64_t* full =
+      reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES + Cfg::STAGING_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
@@ -127,9 +134,21 @@ __global__ void __launch_bounds__(kTCThreads, 1)
           if (SPLIT == 2)
             tc::tma_load_3d(s + Cfg::A_BYTES, &tmA1, &full[stage], kx, mt * BM, b * g.a_batched);
           uint8_t* sb = s + SPLIT * Cfg::A_BYTES;
-          tc::tma_load_3d(sb, &tmB0, &full[stage], kx, nt * BN, b * g.b_batched);
-          if (SPLIT == 2)
-            tc::tma_load_3d(sb + Cfg::B_BYTES, &tmB1, &full[stage], kx, nt * BN, b * g.b_batched);
+          if (g.b_mn) {
+#pragma unroll
+            for (int c = 0; c < BN / 32; ++c) {
+              tc::tma_load_3d(sb + c * 4096, &tmB0, &full[stage], nt * BN + 32 * c, kx,
+                              b * g.b_batched);
+              if (SPLIT == 2)
+                tc::tma_load_3d(sb + Cfg::B_BYTES + c * 4096, &tmB1, &full[stage],
+                                nt * BN + 32 * c, kx, b * g.b_batched);
+            }
+          } else {
+            tc::tma_load_3d(sb, &tmB0, &full[stage], kx, nt * BN, b * g.b_batched);
+            if (SPLIT == 2)
+              tc::tma_load_3d(sb + Cfg::B_BYTES, &tmB1, &full[stage], kx, nt * BN,
+                              b * g.b_batched);
+          }
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
@@ -140,7 +159,7 @@ __global__ void __launch_bounds__(kTCThreads, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------- MMA issuer ----------------
-      constexpr uint32_t idesc = tc::idesc_tf32(BM, BN);
+      const uint32_t idesc = tc::idesc_tf32(BM, BN) | (g.b_mn ? tc::kIdescBMajorMN : 0u);
       int stage = 0;
       uint32_t phase = 0;
       int local = 0;
@@ -162,13 +181,15 @@ __global__ void __launch_bounds__(kTCThreads, 1)
 #pragma unroll
           for (int k = 0; k < BK / 8; ++k) {
             const uint64_t a0 = tc::desc_kmajor_sw128(sa + k * 32);
-            const uint64_t b0 = tc::desc_kmajor_sw128(sb + k * 32);
+            const uint64_t b0 = g.b_mn ? tc::desc_mn_sw128_atom32(sb + k * 1024, 4096)
+                                       : tc::desc_kmajor_sw128(sb + k * 32);
             const uint32_t first = (kb | k) != 0;
             if (SPLIT == 1) {
               tc::mma_tf32(d_tmem, a0, b0, idesc, first);
             } else {
               const uint64_t a1 = tc::desc_kmajor_sw128(sa + Cfg::A_BYTES + k * 32);
-              const uint64_t b1 = tc::desc_kmajor_sw128(sb + Cfg::B_BYTES + k * 32);
+              const uint64_t b1 = g.b_mn ? tc::desc_mn_sw128_atom32(sb + Cfg::B_BYTES + k * 1024, 4096)
+                                         : tc::desc_kmajor_sw128(sb + Cfg::B_BYTES + k * 32);
               tc::mma_tf32(d_tmem, a1, b0, idesc, first);  // lo * hi
               tc::mma_tf32(d_tmem, a0, b1, idesc, 1);      // hi * lo
               tc::mma_tf32(d_tmem, a0, b0, idesc, 1);      // hi * hi
@@ -188,9 +209,16 @@ __global__ void __launch_bounds__(kTCThreads, 1)
     }
   } else {
     // ---------------- epilogue (warps 2..5) ----------------
+    // Each warp owns TMEM lanes (rows) [32*quad, 32*quad + 32). With tma_store
+    // it writes 32-column slices of its rows into a 128-byte-swizzled 32 x 32
+    // shared box (conflict-free: lane r puts 16-byte chunk j at j ^ (r & 7))
+    // and one lane stores the box with TMA, double-buffered; otherwise each
+    // thread stores its own row.
     const int quad = warp & 3;  // TMEM lanes [32*quad, 32*quad + 32)
     int local = 0;
     const bool vec_ok = ((g.ldd & 3) == 0) && ((((uintptr_t)g.D) & 15) == 0);
+    float* box0 = staging + quad * 2 * 1024;
+    int bsel = 0;
     for (int64_t t = blockIdx.x; t < g.tiles; t += gridDim.x, ++local) {
       const int per_b = g.m_tiles * g.n_tiles;
       const int b = (int)(t / per_b);
@@ -199,37 +227,62 @@ __global__ void __launch_bounds__(kTCThreads, 1)
       const uint32_t aphase = (local >> 1) & 1;
       if (!tc::mbar_wait(&tfull[acc], aphase, g.err)) break;
       tc::tc_fence_after();
-      const int row = mt * BM + quad * 32 + lane;
+      const int row0 = mt * BM + quad * 32;
+      const int row = row0 + lane;
       float* drow = g.D + (int64_t)b * g.d_batch_stride + (int64_t)row * g.ldd;
       const float* crow = nullptr;
       if (g.c_mode == 2) crow = g.C + (int64_t)b * g.c_batch_stride + (int64_t)row * g.ldc;
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 16) {
-        uint32_t r[16];
-        __syncwarp();  // tcgen05.ld is .sync.aligned: the warp must be converged
-        tc::tmem_ld16(tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN + c0, r);
-        tc::tmem_ld_wait();
+      for (int c0 = 0; c0 < BN; c0 += 32) {
         const int n0 = nt * BN + c0;
-        if (row < g.M && n0 < g.N) {
-          float v[16];
+        if (n0 >= g.N) break;  // warp-uniform
+        uint32_t r[32];
+        __syncwarp();  // tcgen05.ld is .sync.aligned: the warp must be converged
+        const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN + c0;
+        tc::tmem_ld16(taddr, *reinterpret_cast<uint32_t(*)[16]>(&r[0]));
+        tc::tmem_ld16(taddr + 16, *reinterpret_cast<uint32_t(*)[16]>(&r[16]));
+        tc::tmem_ld_wait();
+        float v[32];
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            float x = g.alpha * __uint_as_float(r[j]);
-            const int n = n0 + j;
-            if (g.c_mode == 1 && n < g.N) x = fmaf(g.beta, g.C[n], x);
-            if (g.c_mode == 2 && n < g.N) x = fmaf(g.beta, crow[n], x);
-            if (g.relu) x = x > 0.0f ? x : 0.0f;
-            v[j] = x;
+        for (int j = 0; j < 32; ++j) {
+          float x = g.alpha * __uint_as_float(r[j]);
+          const int n = n0 + j;
+          if (g.c_mode == 1 && n < g.N) x = fmaf(g.beta, __ldg(g.C + n), x);
+          if (g.c_mode == 2 && n < g.N && row < g.M) x = fmaf(g.beta, crow[n], x);
+          if (g.relu) x = x > 0.0f ? x : 0.0f;
+          v[j] = x;
+        }
+        if (g.tma_store) {
+          if (row0 >= g.M) continue;  // warp-uniform: the whole box lies below M
+          float* box = box0 + bsel * 1024;
+          if (lane == 0) tc::bulk_wait_group_read<1>();  // the store 2 slices ago read `box`
+          __syncwarp();
+          float4* brow = reinterpret_cast<float4*>(box + lane * 32);
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            brow[j ^ (lane & 7)] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+          tc::fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tc::tma_store_3d(&tmD, box, n0, row0, b);
+            tc::bulk_commit_group();
           }
-          if (vec_ok && n0 + 16 <= g.N) {
-            float4* d4 = reinterpret_cast<float4*>(drow + n0);
+          bsel ^= 1;
+        } else if (row < g.M) {
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
-              d4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-          } else {
+          for (int h = 0; h < 2; ++h) {
+            const int nh = n0 + 16 * h;
+            if (vec_ok && nh + 16 <= g.N) {
+              float4* d4 = reinterpret_cast<float4*>(drow + nh);
 #pragma unroll
-            for (int j = 0; j < 16; ++j)
-              if (n0 + j < g.N) drow[n0 + j] = v[j];
+              for (int j = 0; j < 4; ++j)
+                d4[j] = make_float4(v[16 * h + 4 * j], v[16 * h + 4 * j + 1],
+                                    v[16 * h + 4 * j + 2], v[16 * h + 4 * j + 3]);
+            } else {
+#pragma unroll
+              for (int j = 0; j < 16; ++j)
+                if (nh + j < g.N) drow[nh + j] = v[16 * h + j];
+            }
           }
         }
       }
@@ -237,6 +290,7 @@ __global__ void __launch_bounds__(kTCThreads, 1)
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&tempty[acc]);
     }
+    if (g.tma_store && lane == 0) tc::bulk_wait_group<0>();
   }
 
   tc::tc_fence_before();
@@ -340,16 +394,33 @@ bool launch_tc(const Problem& p, const float* A0, const float* A1, const float* 
   CUtensorMap ta0, ta1, tb0, tb1;
   const uint64_t a_dims[3] = {(uint64_t)p.K, (uint64_t)p.M, (uint64_t)(p.a_bs ? p.batches : 1)};
   const uint64_t a_str[2] = {(uint64_t)p.K * 4, (uint64_t)(p.a_bs ? p.a_bs : (int64_t)p.M * p.K) * 4};
-  const uint64_t b_dims[3] = {(uint64_t)p.K, (uint64_t)p.N, (uint64_t)(p.b_bs ? p.batches : 1)};
-  const uint64_t b_str[2] = {(uint64_t)p.K * 4, (uint64_t)(p.b_bs ? p.b_bs : (int64_t)p.N * p.K) * 4};
-  const uint32_t a_box[3] = {BK, BM, 1}, b_box[3] = {BK, BN, 1};
+  // B: K-major [N, K] rows, or MN-major [K, N] rows read as {32 n, BK k} boxes.
+  const bool mn = !p.b_kmajor;
+  const uint64_t b_dims[3] = {(uint64_t)(mn ? p.N : p.K), (uint64_t)(mn ? p.K : p.N),
+                              (uint64_t)(p.b_bs ? p.batches : 1)};
+  const uint64_t b_str[2] = {(uint64_t)(mn ? p.N : p.K) * 4,
+                             (uint64_t)(p.b_bs ? p.b_bs : (int64_t)p.N * p.K) * 4};
+  const uint32_t a_box[3] = {BK, BM, 1};
+  const uint32_t b_box[3] = {mn ? 32u : (uint32_t)BK, mn ? (uint32_t)BK : (uint32_t)BN, 1};
   if (!encode_tmap_f32(&ta0, A0, 3, a_dims, a_str, a_box, nullptr, op)) return false;
-  if (!encode_tmap_f32(&tb0, B0, 3, b_dims, b_str, b_box, nullptr, op)) return false;
+  const int b_swz = mn ? kSwizzle128Atom32 : 128;
+  if (!encode_tmap_f32(&tb0, B0, 3, b_dims, b_str, b_box, nullptr, op, b_swz)) return false;
   ta1 = ta0;
   tb1 = tb0;
   if (SPLIT == 2) {
     if (!encode_tmap_f32(&ta1, A1, 3, a_dims, a_str, a_box, nullptr, op)) return false;
-    if (!encode_tmap_f32(&tb1, B1, 3, b_dims, b_str, b_box, nullptr, op)) return false;
+    if (!encode_tmap_f32(&tb1, B1, 3, b_dims, b_str, b_box, nullptr, op, b_swz)) return false;
+  }
+  // D through TMA stores when its rows and batches start on 16-byte
+  // boundaries (N % 4 == 0, aligned base); 32 x 32 boxes, 128-byte swizzle.
+  CUtensorMap td = ta0;
+  const bool tma_store = (p.N % 4 == 0) && (p.d_bs % 4 == 0) && aligned16(p.D);
+  if (tma_store) {
+    const uint64_t d_dims[3] = {(uint64_t)p.N, (uint64_t)p.M, (uint64_t)p.batches};
+    const uint64_t d_str[2] = {(uint64_t)p.N * 4,
+                               (uint64_t)(p.batches > 1 ? p.d_bs : (int64_t)p.M * p.N) * 4};
+    const uint32_t d_box[3] = {32, 32, 1};
+    if (!encode_tmap_f32(&td, p.D, 3, d_dims, d_str, d_box, nullptr, op)) return false;
   }
   GemmArgs g;
   g.M = p.M;
@@ -370,6 +441,8 @@ bool launch_tc(const Problem& p, const float* A0, const float* A1, const float* 
   g.ldd = p.N;
   g.d_batch_stride = p.d_bs;
   g.relu = p.relu;
+  g.tma_store = tma_store ? 1 : 0;
+  g.b_mn = mn ? 1 : 0;
   g.err = device_error_word();
   auto kern = gemm_tc_kernel<BN, SPLIT, STAGES>;
   // The dynamic shared-memory opt-in is a property of the function in each
@@ -383,7 +456,7 @@ bool launch_tc(const Problem& p, const float* A0, const float* A1, const float* 
     attr_set[ctx().device] = true;
   }
   const int grid = (int)(g.tiles < sm_count() ? g.tiles : sm_count());
-  kern<<<grid, kTCThreads, Cfg::SMEM, ctx().stream>>>(ta0, ta1, tb0, tb1, g);
+  kern<<<grid, kTCThreads, Cfg::SMEM, ctx().stream>>>(ta0, ta1, tb0, tb1, td, g);
   return check_launch(op);
 }
 
@@ -430,9 +503,8 @@ void run_problem(Problem p, const char* op) {
   if ((int64_t)p.M * p.N * p.batches == 0) return;
   const bool tiny = p.M < 64 || p.N < 16 || (int64_t)p.M * p.N * p.K < (1 << 18);
   // TMA needs 16-byte aligned bases, row pitches and batch strides. The
-  // reference's batch offsets (see matmul_impl) may overlap; the A tensor map
-  // takes the batch stride as given (overlapping reads are fine), and B's
-  // transpose reads it (batches come out dense).
+  // reference's batch offsets (see matmul_impl) may overlap; the tensor maps
+  // take the batch strides as given (overlapping reads are fine).
   const bool tma_ok = (p.K % 4 == 0) && aligned16(p.A) && aligned16(p.B) && (p.a_bs % 4 == 0) &&
                       p.K > 0;
   if (tiny || !tma_ok) {
@@ -440,12 +512,13 @@ void run_problem(Problem p, const char* op) {
     return;
   }
   const bool split = ctx().precision == NNC_CUDA_PRECISION_3XTF32;
-  // Scratch: K-major copies of transposed operands, then hi/lo planes.
+  // Scratch: a K-major copy of a transposed A (and of a [K, N] B that cannot
+  // be read MN-major), then hi/lo planes.
   const int64_t a_elems = (int64_t)(p.a_bs ? p.batches : 1) * p.M * p.K;
   const int64_t b_elems = (int64_t)(p.b_bs ? p.batches : 1) * p.N * p.K;
   size_t need = 0;
   if (p.a_trans) need += a_elems * 4;
-  if (!p.b_kmajor) need += b_elems * 4;
+  if (!p.b_kmajor && !(p.N % 4 == 0 && p.b_bs % 4 == 0)) need += b_elems * 4;
   if (split) need += 2 * (a_elems + b_elems) * 4;
   float* ws = need ? (float*)workspace(need + 64, op) : nullptr;
   if (need && !ws) return;
@@ -458,11 +531,15 @@ void run_problem(Problem p, const char* op) {
     cur += a_elems;
     if (p.a_bs) p.a_bs = (int64_t)p.M * p.K;
   }
-  if (!p.b_kmajor) {  // [K, N] -> [N, K], batches made dense
+  // B stored [K, N] is read MN-major straight from its rows when they and its
+  // batches start on 16-byte boundaries; otherwise it is transposed first.
+  const bool b_mn = !p.b_kmajor && p.N % 4 == 0 && p.b_bs % 4 == 0;
+  if (!p.b_kmajor && !b_mn) {  // [K, N] -> [N, K], batches made dense
     if (!batched_transpose_f32(B, cur, p.b_bs ? p.batches : 1, p.K, p.N, op, p.b_bs)) return;
     B = cur;
     cur += b_elems;
     if (p.b_bs) p.b_bs = (int64_t)p.N * p.K;
+    p.b_kmajor = true;
   }
   const int64_t a_in_bs = p.a_bs, b_in_bs = p.b_bs;
   if (split) {  // the hi/lo planes are dense copies

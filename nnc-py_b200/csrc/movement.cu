@@ -4,6 +4,8 @@
 // :1995-2086, :2173-2251).
 #include <string.h>
 
+#include <type_traits>
+
 #include "common.cuh"
 #include "movement.cuh"
 
@@ -49,44 +51,70 @@ struct Perm {
 };
 
 // Generic N-D permutation: one thread per output element (coalesced writes).
-template <typename T>
+// Idx: unsigned when every offset fits 32 bits (32-bit division is several
+// times cheaper than 64-bit, and this loop is bound by its index arithmetic).
+template <typename T, typename Idx>
 __global__ void __launch_bounds__(256) permute_kernel(const T* __restrict__ in,
-                                                      T* __restrict__ out, int64_t total,
-                                                      Perm p) {
-  for (int64_t o = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; o < total;
-       o += (int64_t)gridDim.x * blockDim.x) {
-    int64_t rem = o, src = 0;
+                                                      T* __restrict__ out, Idx total, Perm p) {
+  for (Idx o = blockIdx.x * (Idx)blockDim.x + threadIdx.x; o < total;
+       o += (Idx)gridDim.x * blockDim.x) {
+    Idx rem = o, src = 0;
     for (int i = p.ndim - 1; i >= 0; --i) {
-      const int64_t idx = rem % p.out_dims[i];
-      rem /= p.out_dims[i];
-      src += idx * p.in_strides_by_out[i];
+      const Idx d = (Idx)p.out_dims[i];
+      const Idx q = rem / d;
+      src += (rem - q * d) * (Idx)p.in_strides_by_out[i];
+      rem = q;
     }
     out[o] = in[src];
   }
 }
 
 // Permutation that keeps the innermost dimension: moves rows of `inner`
-// contiguous elements (float4 vectors when inner % 4 == 0).
-__global__ void __launch_bounds__(256) permute_rows_vec4_kernel(const float4* __restrict__ in,
-                                                                float4* __restrict__ out,
-                                                                int64_t rows, int64_t inner4,
-                                                                Perm p) {
-  const int64_t total = rows * inner4;
-  for (int64_t o = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; o < total;
-       o += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t v = o % inner4;
-    int64_t rem = o / inner4, src = 0;
+// contiguous elements as V-float vectors (V = 4 or 2 by alignment).
+template <int V, typename Idx>
+__global__ void __launch_bounds__(256) permute_rows_kernel(const float* __restrict__ in,
+                                                           float* __restrict__ out, Idx rows,
+                                                           Idx inner_v, Perm p) {
+  using Vec = typename std::conditional<V == 4, float4, float2>::type;
+  const Idx total = rows * inner_v;
+  for (Idx o = blockIdx.x * (Idx)blockDim.x + threadIdx.x; o < total;
+       o += (Idx)gridDim.x * blockDim.x) {
+    Idx rem = o / inner_v;
+    const Idx v = o - rem * inner_v;
+    Idx src = 0;
     for (int i = p.ndim - 2; i >= 0; --i) {
-      const int64_t idx = rem % p.out_dims[i];
-      rem /= p.out_dims[i];
-      src += idx * p.in_strides_by_out[i];
+      const Idx d = (Idx)p.out_dims[i];
+      const Idx q = rem / d;
+      src += (rem - q * d) * (Idx)p.in_strides_by_out[i];
+      rem = q;
     }
-    out[o] = in[src / 4 + v];
+    reinterpret_cast<Vec*>(out)[o] = __ldg(reinterpret_cast<const Vec*>(in + src) + v);
   }
+}
+
+// Device-to-device copy of n 16-byte vectors, four in flight per thread.
+__global__ void __launch_bounds__(256) copy_vec4_kernel(const float4* __restrict__ in,
+                                                        float4* __restrict__ out, int64_t n) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  for (; i + 3 * stride < n; i += 4 * stride) {
+    float4 v[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) v[j] = __ldg(in + i + j * stride);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) out[i + j * stride] = v[j];
+  }
+  for (; i < n; i += stride) out[i] = __ldg(in + i);
 }
 
 bool copy_bytes(void* dst, const void* src, size_t bytes, const char* op) {
   if (bytes == 0 || dst == src) return true;
+  if ((((uintptr_t)dst | (uintptr_t)src | bytes) & 15) == 0) {
+    const int64_t n = (int64_t)(bytes / 16);
+    copy_vec4_kernel<<<grid_for(n, 256, 8), 256, 0, ctx().stream>>>((const float4*)src,
+                                                                    (float4*)dst, n);
+    return check_launch(op);
+  }
   return check_cuda(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, ctx().stream), op,
                     "cudaMemcpyAsync");
 }
@@ -161,19 +189,11 @@ void nnc_transpose(Tensor* input, Tensor* output, int64_t* perm, int ndim) {
   }
   int64_t pm[8];
   for (int i = 0; i < ndim; ++i) pm[i] = perm ? perm[i] : (ndim - 1 - i);  // NULL = reverse
-  int64_t in_strides[8];
-  in_strides[ndim - 1] = 1;
-  for (int i = ndim - 2; i >= 0; --i) in_strides[i] = in_strides[i + 1] * input->shape[i + 1];
-  Perm p;
-  p.ndim = ndim;
-  for (int i = 0; i < ndim; ++i) {
+  for (int i = 0; i < ndim; ++i)
     if (pm[i] < 0 || pm[i] >= ndim) {
       fail(NNC_CUDA_ERR_INVALID, op, "perm[%d] = %lld out of range", i, (long long)pm[i]);
       return;
     }
-    p.out_dims[i] = output->shape[i];
-    p.in_strides_by_out[i] = in_strides[pm[i]];
-  }
   const int64_t total = numel(output);
   if (total == 0) return;
   const size_t es = elem_size(elem_type(output));
@@ -181,27 +201,136 @@ void nnc_transpose(Tensor* input, Tensor* output, int64_t* perm, int ndim) {
     fail(NNC_CUDA_ERR_UNSUPPORTED, op, "element size %zu not supported", es);
     return;
   }
-  // Batched 2-D transpose of the last two dims (leading dims in order).
+  cudaStream_t st = ctx().stream;
+  // The reference walks the output shape with the input's strides and checks
+  // neither that perm is a permutation nor that the output is the permuted
+  // input; such calls take the literal element-wise path.
+  bool canonical = true;
+  {
+    bool seen[8] = {};
+    for (int i = 0; i < ndim; ++i) {
+      canonical &= !seen[pm[i]] && output->shape[i] == input->shape[pm[i]];
+      seen[pm[i]] = true;
+    }
+  }
+  if (!canonical) {
+    int64_t in_strides[8];
+    in_strides[ndim - 1] = 1;
+    for (int i = ndim - 2; i >= 0; --i) in_strides[i] = in_strides[i + 1] * input->shape[i + 1];
+    Perm p;
+    p.ndim = ndim;
+    for (int i = 0; i < ndim; ++i) {
+      p.out_dims[i] = output->shape[i];
+      p.in_strides_by_out[i] = in_strides[pm[i]];
+    }
+    const int grid = grid_for(total, 256, 8);
+    if (es == 4)
+      permute_kernel<float, int64_t><<<grid, 256, 0, st>>>((const float*)input->data,
+                                                          (float*)output->data, total, p);
+    else
+      permute_kernel<int64_t, int64_t><<<grid, 256, 0, st>>>(
+          (const int64_t*)input->data, (int64_t*)output->data, total, p);
+    check_launch(op);
+    return;
+  }
+  // Canonical form: drop unit dims, then merge input dims that stay adjacent
+  // and in order in the output. [N,S,h,d] -> [N,h,d,S] becomes the batched
+  // 2-D transpose [N][S][h*d] -> [N][h*d][S].
+  int keep[8], nk = 0;  // output positions of non-unit dims
+  for (int i = 0; i < ndim; ++i)
+    if (output->shape[i] != 1) keep[nk++] = i;
+  int64_t grp_first[8], grp_last[8];  // input dim range of each output group
+  int ng = 0;
+  for (int j = 0; j < nk; ++j) {
+    const int64_t d = pm[keep[j]];
+    // The next kept input dim after grp_last (skipping unit dims) must be d.
+    bool merge = false;
+    if (ng > 0) {
+      int64_t nxt = grp_last[ng - 1] + 1;
+      while (nxt < ndim && input->shape[nxt] == 1) ++nxt;
+      merge = nxt == d;
+    }
+    if (merge) {
+      grp_last[ng - 1] = d;
+    } else {
+      grp_first[ng] = d;
+      grp_last[ng] = d;
+      ++ng;
+    }
+  }
+  // Groups in input order give the merged input shape; gperm maps output
+  // group -> merged input dim.
+  int order[8];
+  for (int g = 0; g < ng; ++g) order[g] = g;
+  for (int a = 1; a < ng; ++a)
+    for (int b2 = a; b2 > 0 && grp_first[order[b2]] < grp_first[order[b2 - 1]]; --b2) {
+      const int t = order[b2];
+      order[b2] = order[b2 - 1];
+      order[b2 - 1] = t;
+    }
+  int64_t mshape[8], mstride[8];
+  int gperm[8];
+  for (int k = 0; k < ng; ++k) {
+    const int g = order[k];
+    gperm[g] = k;
+    mshape[k] = 1;
+    for (int64_t d = grp_first[g]; d <= grp_last[g]; ++d) mshape[k] *= input->shape[d];
+  }
+  if (ng > 0) mstride[ng - 1] = 1;
+  for (int k = ng - 2; k >= 0; --k) mstride[k] = mstride[k + 1] * mshape[k + 1];
+  bool ident = true;
+  for (int g = 0; g < ng; ++g) ident &= gperm[g] == g;
+  if (ident) {  // a pure reshape: one copy
+    copy_bytes(output->data, input->data, (size_t)total * es, op);
+    return;
+  }
   bool lead_identity = true;
-  for (int i = 0; i < ndim - 2; ++i) lead_identity &= (pm[i] == i);
-  if (es == 4 && ndim >= 2 && lead_identity && pm[ndim - 2] == ndim - 1 &&
-      pm[ndim - 1] == ndim - 2) {
-    const int64_t R = input->shape[ndim - 2], C = input->shape[ndim - 1];
+  for (int g = 0; g < ng - 2; ++g) lead_identity &= (gperm[g] == g);
+  if (es == 4 && ng >= 2 && lead_identity && gperm[ng - 2] == ng - 1 && gperm[ng - 1] == ng - 2) {
+    const int64_t R = mshape[ng - 2], C = mshape[ng - 1];
     batched_transpose_f32((const float*)input->data, (float*)output->data, total / (R * C), R, C,
                           op);
     return;
   }
-  const int64_t inner = output->shape[ndim - 1];
-  if (es == 4 && pm[ndim - 1] == ndim - 1 && inner % 4 == 0 && aligned16(input->data) &&
-      aligned16(output->data)) {
-    permute_rows_vec4_kernel<<<grid_for(total / 4, 256, 8), 256, 0, ctx().stream>>>(
-        (const float4*)input->data, (float4*)output->data, total / inner, inner / 4, p);
+  Perm p;
+  p.ndim = ng;
+  for (int g = 0; g < ng; ++g) {
+    p.out_dims[g] = mshape[gperm[g]];
+    p.in_strides_by_out[g] = mstride[gperm[g]];
+  }
+  const bool small = total < (int64_t(1) << 31);
+  const int64_t inner = p.out_dims[ng - 1];
+  const uintptr_t align = (uintptr_t)input->data | (uintptr_t)output->data;
+  if (es == 4 && gperm[ng - 1] == ng - 1 && inner % 2 == 0 && (align & 7) == 0) {
+    const int V = (inner % 4 == 0 && (align & 15) == 0) ? 4 : 2;
+    const int64_t rows = total / inner, iv = inner / V;
+    const int grid = grid_for(total / V, 256, 8);
+    const float* pi = (const float*)input->data;
+    float* po = (float*)output->data;
+    if (V == 4 && small)
+      permute_rows_kernel<4, uint32_t><<<grid, 256, 0, st>>>(pi, po, (uint32_t)rows, (uint32_t)iv, p);
+    else if (V == 4)
+      permute_rows_kernel<4, int64_t><<<grid, 256, 0, st>>>(pi, po, rows, iv, p);
+    else if (small)
+      permute_rows_kernel<2, uint32_t><<<grid, 256, 0, st>>>(pi, po, (uint32_t)rows, (uint32_t)iv, p);
+    else
+      permute_rows_kernel<2, int64_t><<<grid, 256, 0, st>>>(pi, po, rows, iv, p);
   } else if (es == 4) {
-    permute_kernel<float><<<grid_for(total, 256, 8), 256, 0, ctx().stream>>>(
-        (const float*)input->data, (float*)output->data, total, p);
+    const int grid = grid_for(total, 256, 8);
+    if (small)
+      permute_kernel<float, uint32_t><<<grid, 256, 0, st>>>((const float*)input->data,
+                                                           (float*)output->data, (uint32_t)total, p);
+    else
+      permute_kernel<float, int64_t><<<grid, 256, 0, st>>>((const float*)input->data,
+                                                          (float*)output->data, total, p);
   } else {
-    permute_kernel<int64_t><<<grid_for(total, 256, 8), 256, 0, ctx().stream>>>(
-        (const int64_t*)input->data, (int64_t*)output->data, total, p);
+    const int grid = grid_for(total, 256, 8);
+    if (small)
+      permute_kernel<int64_t, uint32_t><<<grid, 256, 0, st>>>(
+          (const int64_t*)input->data, (int64_t*)output->data, (uint32_t)total, p);
+    else
+      permute_kernel<int64_t, int64_t><<<grid, 256, 0, st>>>(
+          (const int64_t*)input->data, (int64_t*)output->data, total, p);
   }
   check_launch(op);
 }

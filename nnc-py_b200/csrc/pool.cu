@@ -34,18 +34,37 @@ __device__ __forceinline__ void window(const PoolGeom& g, int oh, int ow, int& h
   w1 = w1 > g.W ? g.W : w1;
 }
 
-template <bool MAX>
+// FULL2: 2x2 windows, stride 2, no padding, every window inside the input and
+// W even — the two values of a window row are one aligned 8-byte load.
+template <bool MAX, typename Idx, bool FULL2>
 __global__ void __launch_bounds__(256) pool_nchw_kernel(const float* __restrict__ in,
                                                         float* __restrict__ out, PoolGeom g) {
-  const int64_t total = (int64_t)g.N * g.C * g.OH * g.OW;
-  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
-       idx += (int64_t)gridDim.x * blockDim.x) {
-    const int ow = (int)(idx % g.OW);
-    const int oh = (int)((idx / g.OW) % g.OH);
-    const int64_t nc = idx / ((int64_t)g.OW * g.OH);
+  const Idx total = (Idx)g.N * g.C * g.OH * g.OW;
+  for (Idx idx = blockIdx.x * (Idx)blockDim.x + threadIdx.x; idx < total;
+       idx += (Idx)gridDim.x * blockDim.x) {
+    const Idx r = idx / g.OW;
+    const int ow = (int)(idx - r * g.OW);
+    const Idx nc = r / g.OH;
+    const int oh = (int)(r - nc * g.OH);
+    const float* plane = in + nc * g.H * g.W;
+    if constexpr (FULL2) {
+      const float2 t0 = __ldg(reinterpret_cast<const float2*>(plane + (2 * oh) * g.W + 2 * ow));
+      const float2 t1 =
+          __ldg(reinterpret_cast<const float2*>(plane + (2 * oh + 1) * g.W + 2 * ow));
+      if (MAX) {
+        float m = t0.x;
+        if (t0.y > m) m = t0.y;
+        if (t1.x > m) m = t1.x;
+        if (t1.y > m) m = t1.y;
+        out[idx] = m;
+      } else {
+        const float s = __fadd_rn(__fadd_rn(__fadd_rn(t0.x, t0.y), t1.x), t1.y);
+        out[idx] = __fdiv_rn(s, 4.0f);
+      }
+      continue;
+    }
     int h0, h1, w0, w1;
     window(g, oh, ow, h0, h1, w0, w1);
-    const float* plane = in + nc * g.H * g.W;
     if (MAX) {
       float m = kEmptyMax;
       bool has = false;
@@ -131,6 +150,41 @@ __global__ void __launch_bounds__(256) pool_nhwc_kernel(const float* __restrict_
 }
 
 template <bool MAX>
+void launch_pool(const float* pi, float* po, const PoolGeom& g, bool nhwc) {
+  const int64_t total = (int64_t)g.N * g.C * g.OH * g.OW;
+  // 32-bit indexing when every offset (and the grid-stride overshoot) fits.
+  const int64_t in_elems = (int64_t)g.N * g.C * g.H * g.W;
+  const bool small = in_elems < (int64_t(1) << 30) && total < (int64_t(1) << 30);
+  cudaStream_t st = ctx().stream;
+  if (!nhwc) {
+    const int grid = grid_for(total, 256, 8);
+    const bool full2 = g.kh == 2 && g.kw == 2 && g.sh == 2 && g.sw == 2 && g.ph == 0 &&
+                       g.pw == 0 && g.W % 2 == 0 && 2 * g.OH <= g.H && 2 * g.OW <= g.W &&
+                       ((uintptr_t)pi & 7) == 0;
+    if (small && full2)
+      pool_nchw_kernel<MAX, int, true><<<grid, 256, 0, st>>>(pi, po, g);
+    else if (small)
+      pool_nchw_kernel<MAX, int, false><<<grid, 256, 0, st>>>(pi, po, g);
+    else if (full2)
+      pool_nchw_kernel<MAX, int64_t, true><<<grid, 256, 0, st>>>(pi, po, g);
+    else
+      pool_nchw_kernel<MAX, int64_t, false><<<grid, 256, 0, st>>>(pi, po, g);
+  } else if (g.C % 4 == 0 && aligned16(pi) && aligned16(po)) {
+    const int grid = grid_for(total / 4, 256, 8);
+    if (small)
+      pool_nhwc_kernel<MAX, 4, int><<<grid, 256, 0, st>>>(pi, po, g);
+    else
+      pool_nhwc_kernel<MAX, 4, int64_t><<<grid, 256, 0, st>>>(pi, po, g);
+  } else {
+    const int grid = grid_for(total, 256, 8);
+    if (small)
+      pool_nhwc_kernel<MAX, 1, int><<<grid, 256, 0, st>>>(pi, po, g);
+    else
+      pool_nhwc_kernel<MAX, 1, int64_t><<<grid, 256, 0, st>>>(pi, po, g);
+  }
+}
+
+template <bool MAX>
 void pool_impl(Tensor* input, Tensor* output, int kh, int kw, int sh, int sw, int ph, int pw,
                const char* op) {
   OpScope scope(op);
@@ -161,28 +215,7 @@ void pool_impl(Tensor* input, Tensor* output, int kh, int kw, int sh, int sw, in
   }
   const int64_t total = (int64_t)g.N * g.C * g.OH * g.OW;
   if (total == 0) return;
-  const float* pi = (const float*)input->data;
-  float* po = (float*)output->data;
-  if (!is_nhwc(input)) {
-    pool_nchw_kernel<MAX><<<grid_for(total, 256, 8), 256, 0, ctx().stream>>>(pi, po, g);
-  } else {
-    // 32-bit indexing when every offset (and the grid-stride overshoot) fits.
-    const int64_t in_elems = (int64_t)g.N * g.C * g.H * g.W;
-    const bool small = in_elems < (int64_t(1) << 30) && total < (int64_t(1) << 30);
-    if (g.C % 4 == 0 && aligned16(pi) && aligned16(po)) {
-      const int grid = grid_for(total / 4, 256, 8);
-      if (small)
-        pool_nhwc_kernel<MAX, 4, int><<<grid, 256, 0, ctx().stream>>>(pi, po, g);
-      else
-        pool_nhwc_kernel<MAX, 4, int64_t><<<grid, 256, 0, ctx().stream>>>(pi, po, g);
-    } else {
-      const int grid = grid_for(total, 256, 8);
-      if (small)
-        pool_nhwc_kernel<MAX, 1, int><<<grid, 256, 0, ctx().stream>>>(pi, po, g);
-      else
-        pool_nhwc_kernel<MAX, 1, int64_t><<<grid, 256, 0, ctx().stream>>>(pi, po, g);
-    }
-  }
+  launch_pool<MAX>((const float*)input->data, (float*)output->data, g, is_nhwc(input));
   check_launch(op);
 }
 
@@ -194,27 +227,8 @@ void pool_impl(Tensor* input, Tensor* output, int kh, int kw, int sh, int sw, in
 bool launch_maxpool_f32(const float* in, float* out, int N, int C, int H, int W, int OH, int OW,
                         int kh, int kw, int sh, int sw, int ph, int pw, bool nhwc, const char* op) {
   PoolGeom g{N, C, H, W, OH, OW, kh, kw, sh, sw, ph, pw};
-  const int64_t total = (int64_t)N * C * OH * OW;
-  if (total == 0) return true;
-  if (!nhwc) {
-    pool_nchw_kernel<true><<<grid_for(total, 256, 8), 256, 0, ctx().stream>>>(in, out, g);
-  } else {
-    const int64_t in_elems = (int64_t)N * C * H * W;
-    const bool small = in_elems < (int64_t(1) << 30) && total < (int64_t(1) << 30);
-    if (C % 4 == 0 && aligned16(in) && aligned16(out)) {
-      const int grid = grid_for(total / 4, 256, 8);
-      if (small)
-        pool_nhwc_kernel<true, 4, int><<<grid, 256, 0, ctx().stream>>>(in, out, g);
-      else
-        pool_nhwc_kernel<true, 4, int64_t><<<grid, 256, 0, ctx().stream>>>(in, out, g);
-    } else {
-      const int grid = grid_for(total, 256, 8);
-      if (small)
-        pool_nhwc_kernel<true, 1, int><<<grid, 256, 0, ctx().stream>>>(in, out, g);
-      else
-        pool_nhwc_kernel<true, 1, int64_t><<<grid, 256, 0, ctx().stream>>>(in, out, g);
-    }
-  }
+  if ((int64_t)N * C * OH * OW == 0) return true;
+  launch_pool<true>(in, out, g, nhwc);
   return check_launch(op);
 }
 

@@ -38,16 +38,29 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
 // One try with a suspend-time hint: a thread whose phase has not completed
 // sleeps in hardware until it does or kSuspendNs pass, instead of spinning
 // and taking issue slots from the warps that do the work.
-constexpr uint32_t kSuspendNs = 100000;  // 0.1 ms per try
+#ifndef NNC_MBAR_SUSPEND_NS
+#define NNC_MBAR_SUSPEND_NS 100000  // 0.1 ms per try
+#endif
+constexpr uint32_t kSuspendNs = NNC_MBAR_SUSPEND_NS;
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendNs)
-      : "memory");
+  if constexpr (kSuspendNs == 0) {  // the system-dependent time limit
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendNs)
+        : "memory");
+  }
   return ok != 0;
 }
 __device__ __forceinline__ uint64_t global_ns() {
@@ -87,6 +100,36 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
       " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
       : "memory");
+}
+// TMA store of a 3-D box from shared memory (bulk-group completion). The
+// box's x coordinate times the element size must be a multiple of 16 bytes
+// and no coordinate may be negative; parts of the box outside the tensor are
+// not written.
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* src, int x,
+                                             int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// Waits until at most N committed bulk groups still read their shared source.
+template <int N>
+__device__ __forceinline__ void bulk_wait_group_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+// Waits until at most N committed bulk groups are incomplete.
+template <int N>
+__device__ __forceinline__ void bulk_wait_group() {
+  asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
+// Makes this thread's generic-proxy shared-memory writes visible to the
+// async proxy (a following TMA store reads them).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar,
                                             int x, int y, int z, int w) {
@@ -251,6 +294,26 @@ __device__ __forceinline__ uint64_t desc_kmajor_noswizzle(uint32_t smem_addr, ui
   return d;  // layout type 0 = SWIZZLE_NONE
 }
 
+// Shared-memory matrix descriptor: MN-major fp32 operand in the 128-byte,
+// 32-byte-atom swizzle (layout type 1, the only MN-major layout kind::tf32
+// accepts), as TMA writes a {32 (MN), rows (K)} box with
+// CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B: each 128-byte row holds 32
+// consecutive MN elements of one k, 4-k groups are 512 bytes apart (stride
+// byte offset) and successive 32-element MN chunks are `lbo` bytes apart
+// (leading byte offset). One MMA (K = 8) reads two 4-row groups per chunk.
+__device__ __forceinline__ uint64_t desc_mn_sw128_atom32(uint32_t smem_addr, uint32_t lbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_addr & 0x3FFFFu) >> 4);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)(512u >> 4) << 32;
+  d |= (uint64_t)1u << 46;
+  d |= (uint64_t)1u << 61;
+  return d;
+}
+
+// Instruction-descriptor bit that marks the B operand MN-major ("transpose B").
+constexpr uint32_t kIdescBMajorMN = 1u << 16;
+
 // Instruction descriptor for kind::tf32 with fp32 accumulation, both operands
 // K-major: c_format F32 (1) at [4,6), a/b_format TF32 (2) at [7,10)/[10,13),
 // N >> 3 at [17,23), M >> 4 at [24,29).
@@ -351,9 +414,15 @@ __device__ __forceinline__ void tma_load_im2col_4d_pair(void* dst, const CUtenso
 
 }  // namespace tc
 
+// swizzle_bytes value selecting CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B: 128-byte
+// rows whose four 32-byte chunks are XOR-permuted by (row & 3), the layout
+// MN-major kind::tf32 operands take (descriptor layout type 1).
+constexpr int kSwizzle128Atom32 = 32;
+
 // Host: encodes a tiled tensor map (fp32, zero OOB fill) over a row-major
-// tensor with dims[0] innermost, in the 128-byte (default) or 64-byte
-// swizzle layout (the box's inner extent must equal the span). Returns false
+// tensor with dims[0] innermost, in the 128-byte (default), 64-byte or
+// 128-byte 32-byte-atom (kSwizzle128Atom32) swizzle layout (the box's inner
+// extent must equal the span). Returns false
 // (status set) on failure. strides_bytes has rank-1 entries (dims 1..rank-1).
 bool encode_tmap_f32(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
                      const uint64_t* strides_bytes, const uint32_t* box,

@@ -64,15 +64,16 @@ bool encode_tmap_f32(CUtensorMap* map, const void* base, int rank, const uint64_
     estr[i] = elem_strides ? elem_strides[i] : 1;
   }
   for (int i = 0; i + 1 < rank; ++i) gstride[i] = strides_bytes[i];
-  if (swizzle_bytes != 128 && swizzle_bytes != 64) {
+  if (swizzle_bytes != 128 && swizzle_bytes != 64 && swizzle_bytes != kSwizzle128Atom32) {
     fail(NNC_CUDA_ERR_LAUNCH, op, "unsupported TMA swizzle span %d", swizzle_bytes);
     return false;
   }
+  const CUtensorMapSwizzle swz = swizzle_bytes == 64                  ? CU_TENSOR_MAP_SWIZZLE_64B
+                                 : swizzle_bytes == kSwizzle128Atom32 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B
+                                                                      : CU_TENSOR_MAP_SWIZZLE_128B;
   CUresult r = g_encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, (cuuint32_t)rank,
                               const_cast<void*>(base), gdim, gstride, bdim, estr,
-                              CU_TENSOR_MAP_INTERLEAVE_NONE,
-                              swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
-                                                  : CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     fail(NNC_CUDA_ERR_LAUNCH, op, "cuTensorMapEncodeTiled failed (%d)", (int)r);

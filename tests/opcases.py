@@ -328,11 +328,12 @@ def seeded_cases():
     for op in ("nnc_maxpool2d", "nnc_avgpool2d"):
         for tag, shape, k, s, p in (("k3s2p1", (2, 3, 11, 13), 3, 2, 1), ("k2s2", (2, 6, 28, 28), 2, 2, 0),
                                     ("global7", (2, 8, 7, 7), 7, 7, 0), ("empty", (1, 1, 2, 2), 1, 1, 4),
-                                    ("k3s1p1", (1, 4, 6, 5), 3, 1, 1)):
+                                    ("k3s1p1", (1, 4, 6, 5), 3, 1, 1), ("k2s2odd", (2, 3, 11, 10), 2, 2, 0),
+                                    ("k2s2oddw", (1, 2, 6, 9), 2, 2, 0)):
             name = f"{op}_{tag}"
             r = rng_for(name)
             x = r.standard_normal(shape).astype(np.float32)
-            if tag == "k3s2p1":
+            if tag in ("k3s2p1", "k2s2odd"):
                 x.flat[::17] = np.nan
             oh, ow = conv_out(shape[2], k, s, p), conv_out(shape[3], k, s, p)
             add({"name": name, "op": op, "tol": "exact",
@@ -420,7 +421,9 @@ def seeded_cases():
     # --- data movement
     for tag, shape, perm in (("2d", (5, 7), (1, 0)), ("3d", (2, 3, 4), (1, 0, 2)), ("3dlast", (4, 5, 6), (0, 2, 1)),
                              ("null", (3, 4, 5), None), ("heads", (2, 8, 4, 16), (0, 2, 1, 3)),
-                             ("4dgen", (2, 3, 5, 7), (3, 1, 0, 2))):
+                             ("4dgen", (2, 3, 5, 7), (3, 1, 0, 2)), ("keys", (2, 8, 4, 16), (0, 2, 3, 1)),
+                             ("unit", (3, 1, 4, 1, 5), (4, 1, 2, 0, 3)), ("merge5", (2, 3, 4, 5, 6), (2, 3, 0, 1, 4)),
+                             ("oddinner", (3, 5, 7), (1, 0, 2)), ("ident", (2, 3, 4), (0, 1, 2))):
         name = f"nnc_transpose_{tag}"
         r = rng_for(name)
         x = r.standard_normal(shape).astype(np.float32)

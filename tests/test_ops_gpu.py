@@ -140,6 +140,42 @@ def test_gemm_nt_sizes_vs_oracle(cuda_lib, prec, shape):
     C.assert_close(got, want, C.TC_RTOL[prec], f"gemm_nt{shape}")
 
 
+# [K, N] B operands read MN-major by the tensor-core kernel (N % 4 == 0), the
+# transposed fallback (N % 4 != 0), ragged M/N/K tile edges, the reference's
+# overlapping batch offsets, and the TMA-store epilogue with bias / C / alpha.
+MATMUL_CASES = [
+    ("mm", (300, 200), (200, 132)), ("mm", (257, 36), (36, 260)), ("mm", (128, 256), (256, 1024)),
+    ("mm", (130, 1000), (1000, 36)), ("mm", (200, 64), (64, 130)), ("mm", (96, 40), (40, 4096)),
+    ("mm", (4, 2, 128, 64), (4, 2, 64, 128)), ("mm", (4, 2, 128, 128), (4, 2, 128, 64)),
+    ("mm", (8, 128, 256), (256, 256)), ("mm", (3, 100, 48), (3, 48, 72)),
+    ("gemm00", (300, 100), (100, 200)), ("gemm10", (64, 200), (64, 132)), ("gemm01", (150, 96), (260, 96)),
+]
+
+
+@pytest.mark.parametrize("prec", [0, 1])
+@pytest.mark.parametrize("cfg", MATMUL_CASES)
+def test_matmul_layouts_vs_oracle(cuda_lib, prec, cfg):
+    kind, sa, sb = cfg
+    r = np.random.default_rng(sum(sa) * 31 + sum(sb))
+    arrays = {"a": r.standard_normal(sa).astype(np.float32), "b": r.standard_normal(sb).astype(np.float32)}
+    if kind == "mm":
+        nd = max(len(sa), len(sb))
+        lead = (sa if len(sa) == nd else sb)[:-2]
+        so = tuple(lead) + (sa[-2], sb[-1])
+        case = {"name": "m", "op": "nnc_matmul", "args": [C._t("a"), C._t("b"), C._o("out", so)]}
+    else:
+        ta, tb = int(kind[4]), int(kind[5])
+        M = sa[1] if ta else sa[0]
+        N = sb[0] if tb else sb[1]
+        arrays["c"] = r.standard_normal((M, N)).astype(np.float32)
+        case = {"name": "g", "op": "nnc_gemm", "args": [C._t("a"), C._t("b"), C._t("c"), C._o("out", (M, N)),
+                                                        C._f(0.75), C._f(-1.25), C._i(ta), C._i(tb)]}
+    cuda_lib.nnc_cuda_set_precision(prec)
+    got = C.run_cuda(cuda_lib, case, arrays)["out"]
+    want = C.run_host(_oracle(), case, arrays)["out"]
+    C.assert_close(got, want, C.TC_RTOL[prec], f"{kind}{sa}x{sb}")
+
+
 @pytest.mark.parametrize("prec", [0, 1])
 @pytest.mark.parametrize("cfg", [(4, 64, 28, 64, 3, 1, 1), (2, 128, 14, 256, 3, 2, 1), (2, 256, 7, 512, 3, 1, 1),
                                  (2, 3, 56, 64, 7, 2, 3), (2, 64, 28, 128, 1, 2, 0)])
@@ -343,6 +379,55 @@ def test_conv_relu_maxpool_vs_oracle(cuda_lib, prec, cfg):
     for layout in ((), ("out",), ("x", "out")):
         got = C.run_cuda(cuda_lib, case, arrays, nhwc=set(layout))["out"]
         C.assert_close(got, want, C.TC_RTOL[prec], f"conv_relu_maxpool{cfg}[{layout}]")
+
+
+# Few output channels over a short reduction (C_out <= 16, C KH KW <= 256)
+# run on the direct CUDA-core kernel: LeNet's two layers, stride 2 with
+# padding and a residual, sigmoid, NCHW and channels-last tensors, raw and
+# prepacked (element and chunk order) weights, both precision modes.
+DIRECT_CASES = [
+    # n, c, h, w, co, k, s, p, op
+    (4, 1, 32, 32, 6, 5, 1, 0, "nnc_conv_relu"),
+    (4, 6, 14, 14, 16, 5, 1, 0, "nnc_conv"),
+    (2, 3, 17, 19, 8, 3, 2, 1, "nnc_conv_add_relu"),
+    (2, 12, 11, 9, 13, 3, 1, 2, "nnc_conv_sigmoid"),
+]
+
+
+@pytest.mark.parametrize("prec", [0, 1])
+@pytest.mark.parametrize("cfg", DIRECT_CASES, ids=lambda c: "x".join(str(v) for v in c[:8]))
+def test_conv_direct_small_vs_oracle(cuda_lib, prec, cfg):
+    import torch
+
+    from nnc_cuda import tensor as T
+
+    n, c, h, w, co, k, st, p, op = cfg
+    r = np.random.default_rng(17 + sum(cfg[:8]))
+    oh, ow = C.conv_out(h, k, st, p), C.conv_out(w, k, st, p)
+    arrays = {"x": r.standard_normal((n, c, h, w)).astype(np.float32),
+              "w": (r.standard_normal((co, c, k, k)) * np.sqrt(2.0 / (c * k * k))).astype(np.float32),
+              "b": r.uniform(-0.01, 0.01, co).astype(np.float32),
+              "res": r.standard_normal((n, co, oh, ow)).astype(np.float32)}
+    args = [C._t("x"), C._t("w"), C._t("b")]
+    nhwc = {"x", "out"}
+    if op == "nnc_conv_add_relu":
+        args.append(C._t("res"))
+        nhwc.add("res")
+    args += [C._o("out", (n, co, oh, ow)), C._i(k), C._i(k), C._i(st), C._i(st), C._i(p), C._i(p)]
+    case = {"name": "c", "op": op, "args": args}
+    cuda_lib.nnc_cuda_set_precision(prec)
+    want = C.run_host(_oracle(), case, arrays)["out"]
+    tol = 1e-5  # fp32 FMA accumulation in either precision mode
+    C.assert_close(C.run_cuda(cuda_lib, case, arrays)["out"], want, tol, f"conv{cfg}")
+    C.assert_close(C.run_cuda(cuda_lib, case, arrays, nhwc=nhwc)["out"], want, tol, f"conv{cfg}[nhwc]")
+    # Prepacked weight (element order for K <= 64, chunk order above).
+    wt = torch.from_numpy(arrays["w"]).cuda()
+    wref = T.from_torch(wt)
+    nbytes = cuda_lib.nnc_cuda_prepacked_conv_weight_bytes(wref.ptr)
+    packed = torch.empty(nbytes // 4, dtype=torch.float32, device="cuda")
+    assert cuda_lib.nnc_cuda_prepack_conv_weight(wref.ptr, ctypes.c_void_p(packed.data_ptr()), nbytes) == 0
+    got = _run_with_weight(cuda_lib, case, arrays, "w", wref)["out"]
+    C.assert_close(got, want, tol, f"conv{cfg}[prepacked]")
 
 
 # Row-op dispatch: one warp per row up to 1024 elements, a block per row with
