@@ -46,6 +46,7 @@
 #include <math.h>
 #include <stdlib.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "common.cuh"
@@ -1808,30 +1809,55 @@ __global__ void __launch_bounds__(256) s2d_weight_kernel(const float* __restrict
 // prepacked weight). Accumulation is fp32 FMA over k = (c, kh, kw), the
 // reference's order; bias, residual and activation as in store_tile.
 constexpr int kDirectMaxK = 256;
+// Stages the C_out x K weight in shared memory as ws[k * CO + co] (zero for
+// co >= C_out) from OIHW (src_mode 0) or a prepacked [hi, lo][C_out][K_pad]
+// weight in chunk (1) or element (2) order.
 template <int CO>
-__global__ void __launch_bounds__(128) conv_direct_kernel(ConvArgs g, const float* __restrict__ w,
-                                                          int src_mode, int src_c4, int src_kpad) {
-  __shared__ __align__(16) float ws[kDirectMaxK * CO];
+__device__ __forceinline__ void stage_direct_weights(const ConvArgs& g, const float* __restrict__ w,
+                                                     int src_mode, int src_c4, int src_kpad,
+                                                     float* ws) {
   const int K = g.K;  // C KH KW
-  const int C = K / (g.KH * g.KW);
   for (int idx = threadIdx.x; idx < K * CO; idx += blockDim.x) {
     const int k = idx / CO, co = idx - k * CO;
     float v = 0.0f;
     if (co < g.Cout) {
       const int c = k / (g.KH * g.KW), t = k - c * (g.KH * g.KW);
-      if (src_mode == 0) {  // OIHW
+      if (src_mode == 0) {
         v = w[(int64_t)co * K + k];
       } else {
-        // Prepacked: [hi, lo][C_out][K_pad], chunk (tap, c) or element order.
         const int64_t off = (int64_t)co * src_kpad + (src_mode == 1 ? t * src_c4 + c : k);
         v = __fadd_rn(w[off], w[(int64_t)g.Cout * src_kpad + off]);
       }
     }
     ws[k * CO + co] = v;
   }
+}
+
+// Writes one output pixel's channels: bias, residual (conv+add+relu), activation.
+template <int CO>
+__device__ __forceinline__ void direct_store(const ConvArgs& g, const float (&acc)[CO], int64_t m,
+                                             int64_t n, int64_t p, int64_t OHW, int co0 = 0) {
+  const bool add = g.act == kActAddRelu;
+#pragma unroll
+  for (int j = 0; j < CO; ++j) {
+    const int co = co0 + j;
+    if (co >= g.Cout) break;
+    const int64_t off = g.out_nhwc ? m * g.Cout + co : (n * g.Cout + co) * OHW + p;
+    float o = acc[j];
+    if (g.bias) o = __fadd_rn(o, __ldg(g.bias + co));
+    if (add) o = __fadd_rn(o, __ldg(g.residual + off));
+    g.out[off] = activate(o, g.act);
+  }
+}
+
+template <int CO>
+__global__ void __launch_bounds__(128) conv_direct_kernel(ConvArgs g, const float* __restrict__ w,
+                                                          int src_mode, int src_c4, int src_kpad) {
+  __shared__ __align__(16) float ws[kDirectMaxK * CO];
+  const int C = g.K / (g.KH * g.KW);
+  stage_direct_weights<CO>(g, w, src_mode, src_c4, src_kpad, ws);
   __syncthreads();
   const int64_t OHW = (int64_t)g.OH * g.OW;
-  const bool add = g.act == kActAddRelu;
   for (int64_t m = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; m < g.M;
        m += (int64_t)gridDim.x * blockDim.x) {
     const int64_t n = m / OHW;
@@ -1865,15 +1891,133 @@ __global__ void __launch_bounds__(128) conv_direct_kernel(ConvArgs g, const floa
         }
       }
     }
+    direct_store<CO>(g, acc, m, n, p, OHW);
+  }
+}
+
+// Stride-1-wide variant for a compile-time window width KW: a thread computes
+// OWB horizontally adjacent output pixels of one row for CO of the CO * CG
+// staged channels (CG threads, adjacent in the grid, share a pixel block),
+// loading each input row segment (OWB - 1 + KW values) once per (channel,
+// kh) into registers and reusing it across the KW taps. CG > 1 keeps the
+// accumulators (OWB x CO) small enough for several blocks per SM. Same
+// summation order per output as conv_direct_kernel (channel, kh, kw).
+template <int CO, int CG, int KW, int OWB>
+__global__ void __launch_bounds__(128, 5) conv_direct_row_kernel(ConvArgs g,
+                                                                 const float* __restrict__ w,
+                                                                 int src_mode, int src_c4,
+                                                                 int src_kpad) {
+  constexpr int CS = CO * CG;  // staged channels
+  constexpr int kPix = 128 / CG * OWB;  // output pixels of one block pass
+  __shared__ __align__(16) float ws[kDirectMaxK * CS];
+  // Channels-last outputs leave through this buffer: the pass's pixels form
+  // one contiguous range, written with coalesced stores (a thread's own
+  // pixels are CO * OWB scattered scalars otherwise).
+  __shared__ __align__(16) float obuf[kPix * CS];
+  constexpr int XW = OWB - 1 + KW;
+  const int C = g.K / (g.KH * KW);
+  stage_direct_weights<CS>(g, w, src_mode, src_c4, src_kpad, ws);
+  __syncthreads();
+  const int64_t OHW = (int64_t)g.OH * g.OW;
+  const int nb = (g.OW + OWB - 1) / OWB;
+  const int64_t units = (int64_t)g.N * g.OH * nb * CG;
+  const int sc = (int)g.xs_c, shh = (int)g.xs_h, sww = (int)g.xs_w;
+  const bool staged = g.out_nhwc && g.Cout <= CS;
+  const bool add = g.act == kActAddRelu;
+  // Block-uniform passes (every thread takes part in the barriers).
+  for (int64_t base = blockIdx.x * (int64_t)blockDim.x; base < units;
+       base += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t u = base + threadIdx.x;
+    const bool active = u < units;
+    const int cg = (int)(u % CG);
+    const int64_t ub = u / CG;
+    const int64_t row = ub / nb;  // n * OH + oh
+    const int ob = (int)(ub - row * nb);
+    const int64_t n = row / g.OH;
+    const int oh = (int)(row - n * g.OH);
+    const int ow0 = ob * OWB;
+    float acc[OWB][CO];
 #pragma unroll
-    for (int co = 0; co < CO; ++co) {
-      if (co >= g.Cout) break;
-      const int64_t off = g.out_nhwc ? m * g.Cout + co : (n * g.Cout + co) * OHW + p;
-      float o = acc[co];
-      if (g.bias) o = __fadd_rn(o, __ldg(g.bias + co));
-      if (add) o = __fadd_rn(o, __ldg(g.residual + off));
-      g.out[off] = activate(o, g.act);
+    for (int o = 0; o < OWB; ++o)
+#pragma unroll
+      for (int co = 0; co < CO; ++co) acc[o][co] = 0.0f;
+    if (active) {
+      const int ih0 = oh * g.sh - g.ph, iw0 = ow0 - g.pw;
+      const float* xn = g.x_hi + n * g.xs_n;
+      const float4* wk = reinterpret_cast<const float4*>(ws) + cg * (CO / 4);
+      for (int c = 0; c < C; ++c) {
+        const float* xc = xn + c * sc;
+        for (int kh = 0; kh < g.KH; ++kh, wk += KW * (CS / 4)) {
+          const int ih = ih0 + kh;
+          const bool row_ok = (unsigned)ih < (unsigned)g.H;
+          const float* xr = xc + ih * shh;
+          float xv[XW];
+#pragma unroll
+          for (int j = 0; j < XW; ++j) {
+            const int iw = iw0 + j;
+            xv[j] = (row_ok && (unsigned)iw < (unsigned)g.W) ? __ldg(xr + iw * sww) : 0.0f;
+          }
+#pragma unroll
+          for (int kw = 0; kw < KW; ++kw)
+#pragma unroll
+            for (int q = 0; q < CO / 4; ++q) {
+              const float4 wv = wk[kw * (CS / 4) + q];
+#pragma unroll
+              for (int o = 0; o < OWB; ++o) {
+                const float xo = xv[o + kw];
+                acc[o][4 * q] = fmaf(xo, wv.x, acc[o][4 * q]);
+                acc[o][4 * q + 1] = fmaf(xo, wv.y, acc[o][4 * q + 1]);
+                acc[o][4 * q + 2] = fmaf(xo, wv.z, acc[o][4 * q + 2]);
+                acc[o][4 * q + 3] = fmaf(xo, wv.w, acc[o][4 * q + 3]);
+              }
+            }
+        }
+      }
     }
+    if (!staged) {
+      if (active) {
+#pragma unroll
+        for (int o = 0; o < OWB; ++o) {
+          const int ow = ow0 + o;
+          if (ow >= g.OW) break;
+          direct_store<CO>(g, acc[o], row * g.OW + ow, n, (int64_t)oh * g.OW + ow, OHW, cg * CO);
+        }
+      }
+      continue;  // block-uniform
+    }
+    // The pass's pixel range [m0, m1): from its first unit to its last.
+    const int64_t ub0 = base / CG;
+    const int64_t row0 = ub0 / nb;
+    const int64_t m0 = row0 * g.OW + (int64_t)(ub0 - row0 * nb) * OWB;
+    const int64_t u_last = (base + blockDim.x < units ? base + blockDim.x : units) - 1;
+    const int64_t ubl = u_last / CG;
+    const int64_t rowl = ubl / nb;
+    const int owl = (int)(ubl - rowl * nb) * OWB + OWB;
+    const int64_t m1 = rowl * g.OW + (owl < g.OW ? owl : g.OW);
+    if (active) {
+#pragma unroll
+      for (int o = 0; o < OWB; ++o) {
+        const int ow = ow0 + o;
+        if (ow >= g.OW) break;
+        const int pl = (int)(row * g.OW + ow - m0);
+#pragma unroll
+        for (int j = 0; j < CO; ++j) {
+          const int co = cg * CO + j;
+          if (co < g.Cout)
+            obuf[pl * g.Cout + co] = g.bias ? __fadd_rn(acc[o][j], __ldg(g.bias + co)) : acc[o][j];
+        }
+      }
+    }
+    __syncthreads();
+    const int total = (int)(m1 - m0) * g.Cout;
+    float* dst = g.out + m0 * g.Cout;
+    const float* res = add ? g.residual + m0 * g.Cout : nullptr;
+    for (int i = threadIdx.x; i < total; i += blockDim.x) {
+      float o = obuf[i];
+      if (add) o = __fadd_rn(o, __ldg(res + i));
+      dst[i] = activate(o, g.act);
+    }
+    __syncthreads();  // obuf is rewritten by the next pass
   }
 }
 
@@ -2261,7 +2405,25 @@ void conv_impl(Tensor* input, Tensor* weight, Tensor* bias, Tensor* residual, Te
     g.act = act;
     const int src_mode = packed_w ? (wl0.element ? 2 : 1) : 0;
     const int grid = (int)(cdiv(M, 128) < (int64_t)sm_count() * 8 ? cdiv(M, 128) : (int64_t)sm_count() * 8);
-    if (Cout <= 8)
+    const float* wp = (const float*)weight->data;
+    cudaStream_t st = ctx().stream;
+    // Row-blocked kernel for stride-1-wide 3- and 5-wide windows: 4 output
+    // pixels per thread, 8 channels per thread (two threads per pixel block
+    // above 8 output channels).
+    const int cgs = Cout <= 8 ? 1 : 2;
+    const int64_t units = (int64_t)N * OH * cdiv(OW, 4) * cgs;
+    const int grid4 = (int)(cdiv(units, 128) < (int64_t)sm_count() * 8 ? cdiv(units, 128)
+                                                                         : (int64_t)sm_count() * 8);
+    if (sw == 1 && (KW == 5 || KW == 3)) {
+      if (Cout <= 8 && KW == 5)
+        conv_direct_row_kernel<8, 1, 5, 4><<<grid4, 128, 0, st>>>(g, wp, src_mode, wl0.C4, wl0.Kpad);
+      else if (KW == 5)
+        conv_direct_row_kernel<8, 2, 5, 4><<<grid4, 128, 0, st>>>(g, wp, src_mode, wl0.C4, wl0.Kpad);
+      else if (Cout <= 8)
+        conv_direct_row_kernel<8, 1, 3, 4><<<grid4, 128, 0, st>>>(g, wp, src_mode, wl0.C4, wl0.Kpad);
+      else
+        conv_direct_row_kernel<8, 2, 3, 4><<<grid4, 128, 0, st>>>(g, wp, src_mode, wl0.C4, wl0.Kpad);
+    } else if (Cout <= 8)
       conv_direct_kernel<8><<<grid, 128, 0, ctx().stream>>>(g, (const float*)weight->data, src_mode,
                                                             wl0.C4, wl0.Kpad);
     else

@@ -96,7 +96,7 @@ __global__ void __launch_bounds__(256) pool_nchw_kernel(const float* __restrict_
 template <bool MAX, int V, typename Idx>
 __global__ void __launch_bounds__(256) pool_nhwc_kernel(const float* __restrict__ in,
                                                         float* __restrict__ out, PoolGeom g) {
-  // V channels per thread (4 with 16-byte alignment, else 1).
+  // V channels per thread (4 or 2 with 16- or 8-byte alignment, else 1).
   const Idx cg = g.C / V;
   const Idx total = (Idx)g.N * g.OH * g.OW * cg;
   for (Idx idx = blockIdx.x * (Idx)blockDim.x + threadIdx.x; idx < total;
@@ -122,6 +122,9 @@ __global__ void __launch_bounds__(256) pool_nhwc_kernel(const float* __restrict_
         if constexpr (V == 4) {
           const float4 t = *reinterpret_cast<const float4*>(src);
           v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+        } else if constexpr (V == 2) {
+          const float2 t = *reinterpret_cast<const float2*>(src);
+          v[0] = t.x; v[1] = t.y;
         } else {
           v[0] = src[0];
         }
@@ -143,6 +146,8 @@ __global__ void __launch_bounds__(256) pool_nhwc_kernel(const float* __restrict_
     }
     if constexpr (V == 4) {
       *reinterpret_cast<float4*>(dst) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    } else if constexpr (V == 2) {
+      *reinterpret_cast<float2*>(dst) = make_float2(acc[0], acc[1]);
     } else {
       dst[0] = acc[0];
     }
@@ -175,6 +180,12 @@ void launch_pool(const float* pi, float* po, const PoolGeom& g, bool nhwc) {
       pool_nhwc_kernel<MAX, 4, int><<<grid, 256, 0, st>>>(pi, po, g);
     else
       pool_nhwc_kernel<MAX, 4, int64_t><<<grid, 256, 0, st>>>(pi, po, g);
+  } else if (g.C % 2 == 0 && (((uintptr_t)pi | (uintptr_t)po) & 7) == 0) {
+    const int grid = grid_for(total / 2, 256, 8);
+    if (small)
+      pool_nhwc_kernel<MAX, 2, int><<<grid, 256, 0, st>>>(pi, po, g);
+    else
+      pool_nhwc_kernel<MAX, 2, int64_t><<<grid, 256, 0, st>>>(pi, po, g);
   } else {
     const int grid = grid_for(total, 256, 8);
     if (small)

@@ -33,6 +33,23 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
+// Compensated fp32 accumulation (Neumaier): s + c carries the running sum
+// to about one fp32 ulp whatever the count, at full fp32 rate; the lanes'
+// (s + c) are then combined in fp64.
+__device__ __forceinline__ void comp_add(float& s, float& c, float x) {
+  const float t = __fadd_rn(s, x);
+  const float e = fabsf(s) >= fabsf(x) ? __fadd_rn(__fsub_rn(s, t), x) : __fadd_rn(__fsub_rn(x, t), s);
+  c = __fadd_rn(c, e);
+  s = t;
+}
+
+// Element k of a lane's VPT values in a warp-per-row kernel: lane-strided
+// scalars, or (VEC) float4 runs 4 lane + 128 (k / 4) + {0..3}.
+template <bool VEC>
+__device__ __forceinline__ int row_index(int lane, int k) {
+  return VEC ? 128 * (k >> 2) + 4 * lane + (k & 3) : lane + 32 * k;
+}
+
 // Block-wide reductions for kThreads threads; `red` holds kThreads/32 slots.
 __device__ double block_sum(double v, double* red) {
   v = warp_sum(v);
@@ -111,11 +128,14 @@ __global__ void __launch_bounds__(kThreads) softmax_row_kernel(const float* __re
 }
 
 // Short rows (dim <= 32 VPT): one warp per row, VPT values per lane in
-// registers, shuffle reductions only; 8 rows per 256-thread block.
-template <int VPT>
+// registers (VEC: 16-byte loads and stores), shuffle reductions only; 8 rows
+// per 256-thread block. The sum is compensated fp32 per lane, combined in
+// fp64; outputs are e * (1 / sum) (within one ulp of e / sum).
+template <int VPT, bool VEC>
 __global__ void __launch_bounds__(kThreads) softmax_warp_kernel(const float* __restrict__ in,
                                                                 float* __restrict__ out,
                                                                 int64_t rows, int dim) {
+  static_assert(!VEC || VPT % 4 == 0, "vector rows hold whole float4 runs");
   const int lane = threadIdx.x & 31;
   const int64_t step = (int64_t)gridDim.x * (kThreads / 32);
   for (int64_t row = (int64_t)blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5); row < rows;
@@ -124,26 +144,48 @@ __global__ void __launch_bounds__(kThreads) softmax_warp_kernel(const float* __r
     float* y = out + row * dim;
     float v[VPT];
     float m = -INFINITY;
+    if constexpr (VEC) {
 #pragma unroll
-    for (int k = 0; k < VPT; ++k) {
-      const int i = lane + 32 * k;
-      v[k] = i < dim ? x[i] : -INFINITY;
-      m = (v[k] > m) ? v[k] : m;
-    }
-    m = warp_max(m);
-    double sacc = 0.0;
+      for (int k = 0; k < VPT; k += 4) {
+        const int i = row_index<true>(lane, k);
+        float4 t = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+        if (i < dim) t = __ldg(reinterpret_cast<const float4*>(x + i));
+        v[k] = t.x; v[k + 1] = t.y; v[k + 2] = t.z; v[k + 3] = t.w;
+      }
+    } else {
 #pragma unroll
-    for (int k = 0; k < VPT; ++k) {
-      if (lane + 32 * k < dim) {
-        v[k] = expf(v[k] - m);
-        sacc += (double)v[k];
+      for (int k = 0; k < VPT; ++k) {
+        const int i = row_index<false>(lane, k);
+        v[k] = i < dim ? x[i] : -INFINITY;
       }
     }
-    const float sum = (float)warp_sum(sacc);
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) m = (v[k] > m) ? v[k] : m;
+    m = warp_max(m);
+    float s = 0.0f, c = 0.0f;
 #pragma unroll
     for (int k = 0; k < VPT; ++k) {
-      const int i = lane + 32 * k;
-      if (i < dim) y[i] = __fdiv_rn(v[k], sum);
+      if (row_index<VEC>(lane, k) < dim) {
+        v[k] = expf(v[k] - m);
+        comp_add(s, c, v[k]);
+      }
+    }
+    const float inv = __frcp_rn((float)warp_sum((double)s + (double)c));
+    if constexpr (VEC) {
+#pragma unroll
+      for (int k = 0; k < VPT; k += 4) {
+        const int i = row_index<true>(lane, k);
+        if (i < dim)
+          *reinterpret_cast<float4*>(y + i) =
+              make_float4(__fmul_rn(v[k], inv), __fmul_rn(v[k + 1], inv), __fmul_rn(v[k + 2], inv),
+                          __fmul_rn(v[k + 3], inv));
+      }
+    } else {
+#pragma unroll
+      for (int k = 0; k < VPT; ++k) {
+        const int i = row_index<false>(lane, k);
+        if (i < dim) y[i] = __fmul_rn(v[k], inv);
+      }
     }
   }
 }
@@ -199,21 +241,21 @@ __global__ void __launch_bounds__(kRowThreads) softmax_smem_kernel(const float* 
       }
     }
     m = block_max128(m, red_f);
-    double sacc = 0.0;
+    float s = 0.0f, c = 0.0f;
     for (int i = threadIdx.x; i < dim; i += kRowThreads) {
       const float e = expf(rowbuf[i] - m);
       rowbuf[i] = e;
-      sacc += (double)e;
+      comp_add(s, c, e);
     }
-    const float sum = (float)block_sum128(sacc, red_d);
+    const float inv = __frcp_rn((float)block_sum128((double)s + (double)c, red_d));
     if (vec) {
       for (int i = threadIdx.x; i < dim / 4; i += kRowThreads) {
         const float4 e = reinterpret_cast<const float4*>(rowbuf)[i];
         reinterpret_cast<float4*>(y)[i] =
-            make_float4(__fdiv_rn(e.x, sum), __fdiv_rn(e.y, sum), __fdiv_rn(e.z, sum), __fdiv_rn(e.w, sum));
+            make_float4(__fmul_rn(e.x, inv), __fmul_rn(e.y, inv), __fmul_rn(e.z, inv), __fmul_rn(e.w, inv));
       }
     } else {
-      for (int i = threadIdx.x; i < dim; i += kRowThreads) y[i] = __fdiv_rn(rowbuf[i], sum);
+      for (int i = threadIdx.x; i < dim; i += kRowThreads) y[i] = __fmul_rn(rowbuf[i], inv);
     }
     __syncthreads();  // rowbuf is reused by the next row
   }
@@ -307,45 +349,90 @@ __global__ void __launch_bounds__(kThreads) layernorm_kernel(
 }
 
 // Short slabs (len <= 32 VPT): one warp per slab; `inner` == 1 indexes
-// scale/bias by the element, else by i / inner (32-bit: len fits).
-template <int VPT>
+// scale/bias by the element, else by i / inner (32-bit: len fits). VEC:
+// 16-byte loads and stores (inner == 1 only). Statistics: compensated fp32
+// per lane combined in fp64; outputs scale * ((x - mean) * (1 / sd)) + bias
+// (within one ulp of the division).
+template <int VPT, bool VEC>
 __global__ void __launch_bounds__(kThreads) layernorm_warp_kernel(
     const float* __restrict__ in, const float* __restrict__ scale, const float* __restrict__ bias,
     float* __restrict__ out, int64_t rows, int len, int inner, float eps) {
+  static_assert(!VEC || VPT % 4 == 0, "vector slabs hold whole float4 runs");
   const int lane = threadIdx.x & 31;
   const int64_t step = (int64_t)gridDim.x * (kThreads / 32);
   const float inv_n = (float)len;
+  // Scale and bias are the same for every slab: held in registers for short
+  // slabs (VPT <= 8), re-read (L1 hits) per slab otherwise.
+  constexpr bool kHold = VPT <= 8;
+  float gm[kHold ? VPT : 1], bt[kHold ? VPT : 1];
+  if constexpr (kHold) {
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      const int i = row_index<VEC>(lane, k);
+      const int a = inner == 1 ? i : i / inner;
+      gm[k] = (scale && i < len) ? __ldg(scale + a) : 1.0f;
+      bt[k] = (bias && i < len) ? __ldg(bias + a) : 0.0f;
+    }
+  }
   for (int64_t row = (int64_t)blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5); row < rows;
        row += step) {
     const float* x = in + row * len;
     float* y = out + row * len;
     float v[VPT];
-    double sacc = 0.0;
+    if constexpr (VEC) {
 #pragma unroll
-    for (int k = 0; k < VPT; ++k) {
-      const int i = lane + 32 * k;
-      v[k] = i < len ? x[i] : 0.0f;
-      sacc += (double)v[k];
-    }
-    const float mean = __fdiv_rn((float)warp_sum(sacc), inv_n);
-    double q = 0.0;
+      for (int k = 0; k < VPT; k += 4) {
+        const int i = row_index<true>(lane, k);
+        float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (i < len) t = __ldg(reinterpret_cast<const float4*>(x + i));
+        v[k] = t.x; v[k + 1] = t.y; v[k + 2] = t.z; v[k + 3] = t.w;
+      }
+    } else {
 #pragma unroll
-    for (int k = 0; k < VPT; ++k) {
-      if (lane + 32 * k < len) {
-        const float d = __fsub_rn(v[k], mean);
-        q += (double)__fmul_rn(d, d);
+      for (int k = 0; k < VPT; ++k) {
+        const int i = row_index<false>(lane, k);
+        v[k] = i < len ? x[i] : 0.0f;
       }
     }
-    const float var = __fdiv_rn((float)warp_sum(q), inv_n);
-    const float sd = __fsqrt_rn(__fadd_rn(var, eps));
+    float s = 0.0f, c = 0.0f;
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) comp_add(s, c, v[k]);  // padding adds 0
+    const float mean = __fdiv_rn((float)warp_sum((double)s + (double)c), inv_n);
+    float q = 0.0f, qc = 0.0f;
 #pragma unroll
     for (int k = 0; k < VPT; ++k) {
-      const int i = lane + 32 * k;
-      if (i < len) {
+      if (row_index<VEC>(lane, k) < len) {
+        const float d = __fsub_rn(v[k], mean);
+        comp_add(q, qc, __fmul_rn(d, d));
+      }
+    }
+    const float var = __fdiv_rn((float)warp_sum((double)q + (double)qc), inv_n);
+    const float rsd = __frcp_rn(__fsqrt_rn(__fadd_rn(var, eps)));
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      float g_k, b_k;
+      if constexpr (kHold) {
+        g_k = gm[k];
+        b_k = bt[k];
+      } else {
+        const int i = row_index<VEC>(lane, k);
         const int a = inner == 1 ? i : i / inner;
-        const float gm = scale ? __ldg(scale + a) : 1.0f;
-        const float bt = bias ? __ldg(bias + a) : 0.0f;
-        y[i] = __fadd_rn(__fmul_rn(gm, __fdiv_rn(__fsub_rn(v[k], mean), sd)), bt);
+        g_k = (scale && i < len) ? __ldg(scale + a) : 1.0f;
+        b_k = (bias && i < len) ? __ldg(bias + a) : 0.0f;
+      }
+      v[k] = __fadd_rn(__fmul_rn(g_k, __fmul_rn(__fsub_rn(v[k], mean), rsd)), b_k);
+    }
+    if constexpr (VEC) {
+#pragma unroll
+      for (int k = 0; k < VPT; k += 4) {
+        const int i = row_index<true>(lane, k);
+        if (i < len) *reinterpret_cast<float4*>(y + i) = make_float4(v[k], v[k + 1], v[k + 2], v[k + 3]);
+      }
+    } else {
+#pragma unroll
+      for (int k = 0; k < VPT; ++k) {
+        const int i = row_index<false>(lane, k);
+        if (i < len) y[i] = v[k];
       }
     }
   }
@@ -362,26 +449,26 @@ __global__ void __launch_bounds__(kRowThreads) layernorm_smem_kernel(
   for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
     const float* x = in + row * len;
     float* y = out + row * len;
-    double sacc = 0.0;
+    float s = 0.0f, c = 0.0f;
     for (int i = threadIdx.x; i < len; i += kRowThreads) {
       const float t = x[i];
       rowbuf[i] = t;
-      sacc += (double)t;
+      comp_add(s, c, t);
     }
-    const float mean = __fdiv_rn((float)block_sum128(sacc, red_d), inv_n);
-    double q = 0.0;
+    const float mean = __fdiv_rn((float)block_sum128((double)s + (double)c, red_d), inv_n);
+    float q = 0.0f, qc = 0.0f;
     for (int i = threadIdx.x; i < len; i += kRowThreads) {
       const float d = __fsub_rn(rowbuf[i], mean);
-      q += (double)__fmul_rn(d, d);
+      comp_add(q, qc, __fmul_rn(d, d));
     }
     __syncthreads();  // red_d is reused
-    const float var = __fdiv_rn((float)block_sum128(q, red_d), inv_n);
-    const float sd = __fsqrt_rn(__fadd_rn(var, eps));
+    const float var = __fdiv_rn((float)block_sum128((double)q + (double)qc, red_d), inv_n);
+    const float rsd = __frcp_rn(__fsqrt_rn(__fadd_rn(var, eps)));
     for (int i = threadIdx.x; i < len; i += kRowThreads) {
       const int a = inner == 1 ? i : i / inner;
       const float gm = scale ? __ldg(scale + a) : 1.0f;
       const float bt = bias ? __ldg(bias + a) : 0.0f;
-      y[i] = __fadd_rn(__fmul_rn(gm, __fdiv_rn(__fsub_rn(rowbuf[i], mean), sd)), bt);
+      y[i] = __fadd_rn(__fmul_rn(gm, __fmul_rn(__fsub_rn(rowbuf[i], mean), rsd)), bt);
     }
     __syncthreads();  // rowbuf and red_d are reused by the next slab
   }
@@ -509,18 +596,29 @@ void nnc_softmax(Tensor* input, Tensor* output, int axis) {
     const int64_t blocks = cdiv(outer, (int64_t)(kThreads / 32));
     const int grid = (int)(blocks < (int64_t)sm_count() * 16 ? blocks : (int64_t)sm_count() * 16);
     const int d = (int)dim;
+    cudaStream_t st = ctx().stream;
+    // 16-byte rows: dim % 4 == 0 and aligned bases (then every row is aligned).
+    const bool vec = dim % 4 == 0 && aligned16(pi) && aligned16(po);
     if (dim <= 32)
-      softmax_warp_kernel<1><<<grid, kThreads, 0, ctx().stream>>>(pi, po, outer, d);
+      softmax_warp_kernel<1, false><<<grid, kThreads, 0, st>>>(pi, po, outer, d);
     else if (dim <= 64)
-      softmax_warp_kernel<2><<<grid, kThreads, 0, ctx().stream>>>(pi, po, outer, d);
+      softmax_warp_kernel<2, false><<<grid, kThreads, 0, st>>>(pi, po, outer, d);
+    else if (dim <= 128 && vec)
+      softmax_warp_kernel<4, true><<<grid, kThreads, 0, st>>>(pi, po, outer, d);
     else if (dim <= 128)
-      softmax_warp_kernel<4><<<grid, kThreads, 0, ctx().stream>>>(pi, po, outer, d);
+      softmax_warp_kernel<4, false><<<grid, kThreads, 0, st>>>(pi, po, outer, d);
+    else if (dim <= 256 && vec)
+      softmax_warp_kernel<8, true><<<grid, kThreads, 0, st>>>(pi, po, outer, d);
     else if (dim <= 256)
-      softmax_warp_kernel<8><<<grid, kThreads, 0, ctx().stream>>>(pi, po, outer, d);
+      softmax_warp_kernel<8, false><<<grid, kThreads, 0, st>>>(pi, po, outer, d);
+    else if (dim <= 512 && vec)
+      softmax_warp_kernel<16, true><<<grid, kThreads, 0, st>>>(pi, po, outer, d);
     else if (dim <= 512)
-      softmax_warp_kernel<16><<<grid, kThreads, 0, ctx().stream>>>(pi, po, outer, d);
+      softmax_warp_kernel<16, false><<<grid, kThreads, 0, st>>>(pi, po, outer, d);
+    else if (vec)
+      softmax_warp_kernel<32, true><<<grid, kThreads, 0, st>>>(pi, po, outer, d);
     else
-      softmax_warp_kernel<32><<<grid, kThreads, 0, ctx().stream>>>(pi, po, outer, d);
+      softmax_warp_kernel<32, false><<<grid, kThreads, 0, st>>>(pi, po, outer, d);
   } else if (inner == 1 && dim <= kSmemRowMax) {
     const size_t smem = (size_t)dim * 4;
     if (smem > 48 * 1024 &&
@@ -567,16 +665,29 @@ void nnc_layernorm(Tensor* input, Tensor* scale, Tensor* bias, Tensor* output, i
     const int64_t blocks = cdiv(outer, (int64_t)(kThreads / 32));
     const int grid = (int)(blocks < (int64_t)sm_count() * 16 ? blocks : (int64_t)sm_count() * 16);
     const int l = (int)len, in1 = (int)inner;
+    cudaStream_t st = ctx().stream;
+    const bool vec = len % 4 == 0 && aligned16(pi) && aligned16(po);
+#define NNC_LN_WARP(VPT, VEC) \
+  layernorm_warp_kernel<VPT, VEC><<<grid, kThreads, 0, st>>>(pi, ps, pb, po, outer, l, in1, epsilon)
     if (len <= 64)
-      layernorm_warp_kernel<2><<<grid, kThreads, 0, ctx().stream>>>(pi, ps, pb, po, outer, l, in1, epsilon);
+      NNC_LN_WARP(2, false);
+    else if (len <= 128 && vec)
+      NNC_LN_WARP(4, true);
     else if (len <= 128)
-      layernorm_warp_kernel<4><<<grid, kThreads, 0, ctx().stream>>>(pi, ps, pb, po, outer, l, in1, epsilon);
+      NNC_LN_WARP(4, false);
+    else if (len <= 256 && vec)
+      NNC_LN_WARP(8, true);
     else if (len <= 256)
-      layernorm_warp_kernel<8><<<grid, kThreads, 0, ctx().stream>>>(pi, ps, pb, po, outer, l, in1, epsilon);
+      NNC_LN_WARP(8, false);
+    else if (len <= 512 && vec)
+      NNC_LN_WARP(16, true);
     else if (len <= 512)
-      layernorm_warp_kernel<16><<<grid, kThreads, 0, ctx().stream>>>(pi, ps, pb, po, outer, l, in1, epsilon);
+      NNC_LN_WARP(16, false);
+    else if (vec)
+      NNC_LN_WARP(32, true);
     else
-      layernorm_warp_kernel<32><<<grid, kThreads, 0, ctx().stream>>>(pi, ps, pb, po, outer, l, in1, epsilon);
+      NNC_LN_WARP(32, false);
+#undef NNC_LN_WARP
   } else if (len <= kSmemRowMax) {
     const size_t smem = (size_t)len * 4;
     if (smem > 48 * 1024 &&

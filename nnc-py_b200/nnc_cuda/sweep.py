@@ -146,6 +146,60 @@ def op_sweep(so, torch, timer: Timer, pk: dict) -> list[dict]:
     rx, ro = T.from_torch(x), T.from_torch(o)
     hbm("nnc_reducemean", (16384, 4096), lambda: so.nnc_reducemean(rx.ptr, ro.ptr, 1, 1), 4 * 16384 * 4096 + 4 * 16384)
     hbm("nnc_reducesum", (16384, 4096), lambda: so.nnc_reducesum(rx.ptr, ro.ptr, 1, 1), 4 * 16384 * 4096 + 4 * 16384)
+    del x, o
+    # The transformer's (batch 256, S 128, d 256, 4 heads) per-layer shapes,
+    # with the reference's batched-matmul offsets.
+    for name, sa, sb in (("linear", (256, 128, 256), (256, 256)), ("ffn1", (256, 128, 256), (256, 1024)),
+                         ("ffn2", (256, 128, 1024), (1024, 256)), ("scores", (256, 4, 128, 64), (256, 4, 64, 128)),
+                         ("probs@v", (256, 4, 128, 128), (256, 4, 128, 64))):
+        so_ = sa[:-1] + sb[-1:]
+        a, b, o = rnd(*sa), rnd(*sb), torch.empty(*so_, device="cuda")
+        ra, rb, ro = T.from_torch(a), T.from_torch(b), T.from_torch(o)
+        fl = 2.0 * o.numel() * sa[-1]
+        tensor(f"nnc_matmul {name}", sa + sb, lambda: so.nnc_matmul(ra.ptr, rb.ptr, ro.ptr), fl,
+               "B read MN-major; output-bound (small K)")
+        del a, b, o
+    x = rnd(256, 128, 4, 64)
+    o = torch.empty(256, 4, 64, 128, device="cuda")
+    rx, ro = T.from_torch(x), T.from_torch(o)
+    perm = (ctypes.c_int64 * 4)(0, 2, 3, 1)
+    hbm("nnc_transpose [0,2,3,1]", (256, 128, 4, 64), lambda: so.nnc_transpose(rx.ptr, ro.ptr, perm, 4),
+        8 * x.numel())
+    o2 = torch.empty(256, 4, 128, 64, device="cuda")
+    ro2 = T.from_torch(o2)
+    perm2 = (ctypes.c_int64 * 4)(0, 2, 1, 3)
+    hbm("nnc_transpose [0,2,1,3]", (256, 128, 4, 64), lambda: so.nnc_transpose(rx.ptr, ro2.ptr, perm2, 4),
+        8 * x.numel())
+    del x, o, o2
+    x, o = rnd(256, 4, 128, 128), torch.empty(256, 4, 128, 128, device="cuda")
+    rx, ro = T.from_torch(x), T.from_torch(o)
+    hbm("nnc_softmax", (256, 4, 128, 128), lambda: so.nnc_softmax(rx.ptr, ro.ptr, -1), 8 * x.numel())
+    del x, o
+    x, o = rnd(256, 128, 256), torch.empty(256, 128, 256, device="cuda")
+    gam, bet = rnd(256), rnd(256)
+    rx, ro, rg, rbt = T.from_torch(x), T.from_torch(o), T.from_torch(gam), T.from_torch(bet)
+    hbm("nnc_layernorm", (256, 128, 256), lambda: so.nnc_layernorm(rx.ptr, rg.ptr, rbt.ptr, ro.ptr, -1, 1e-5),
+        8 * x.numel())
+    del x, o
+    # LeNet-5 at batch 8192 (channels-last activations, as the model keeps them).
+    for name, C, H, Co, cl in (("conv1 1->6 5x5", 1, 32, 6, False), ("conv2 6->16 5x5", 6, 14, 16, True)):
+        n, OH = 8192, H - 4
+        x = rnd(n, H, H, C) if cl else rnd(n, C, H, H)
+        rx = T.from_torch(x, tag=L.TAG_NHWC if cl else 0, shape=(n, C, H, H))
+        o = torch.empty(n, OH, OH, Co, device="cuda")
+        ro = T.from_torch(o, tag=L.TAG_NHWC, shape=(n, Co, OH, OH))
+        w, bias = rnd(Co, C, 5, 5) * 0.1, rnd(Co)
+        rw, rbias = T.from_torch(w), T.from_torch(bias)
+        hbm(f"nnc_conv LeNet {name}", (n, C, H, H),
+            lambda: so.nnc_conv(rx.ptr, rw.ptr, rbias.ptr, ro.ptr, 5, 5, 1, 1, 0, 0), 4 * (x.numel() + o.numel()))
+        del x, o
+    x = rnd(8192, 28, 28, 6)
+    o = torch.empty(8192, 14, 14, 6, device="cuda")
+    rx = T.from_torch(x, tag=L.TAG_NHWC, shape=(8192, 6, 28, 28))
+    ro = T.from_torch(o, tag=L.TAG_NHWC, shape=(8192, 6, 14, 14))
+    hbm("nnc_maxpool2d 2x2/2 (C 6, channels-last)", (8192, 6, 28, 28),
+        lambda: so.nnc_maxpool2d(rx.ptr, ro.ptr, 2, 2, 2, 2, 0, 0), 4 * (x.numel() + o.numel()))
+    del x, o
     return rows
 
 

@@ -384,13 +384,17 @@ def test_conv_relu_maxpool_vs_oracle(cuda_lib, prec, cfg):
 # Few output channels over a short reduction (C_out <= 16, C KH KW <= 256)
 # run on the direct CUDA-core kernel: LeNet's two layers, stride 2 with
 # padding and a residual, sigmoid, NCHW and channels-last tensors, raw and
-# prepacked (element and chunk order) weights, both precision modes.
+# prepacked (element and chunk order) weights, both precision modes. Stride-1
+# 3- and 5-wide windows take the row-blocked kernel (4 pixels per thread,
+# ragged row ends included), the others the per-pixel one.
 DIRECT_CASES = [
     # n, c, h, w, co, k, s, p, op
     (4, 1, 32, 32, 6, 5, 1, 0, "nnc_conv_relu"),
     (4, 6, 14, 14, 16, 5, 1, 0, "nnc_conv"),
     (2, 3, 17, 19, 8, 3, 2, 1, "nnc_conv_add_relu"),
     (2, 12, 11, 9, 13, 3, 1, 2, "nnc_conv_sigmoid"),
+    (3, 2, 9, 13, 4, 3, 1, 1, "nnc_conv_add_relu"),
+    (2, 4, 12, 7, 10, 5, 1, 2, "nnc_conv_relu"),
 ]
 
 
@@ -438,6 +442,10 @@ ROW_CASES = [
     ("nnc_softmax", (300, 10), 1), ("nnc_softmax", (64, 1024), 1), ("nnc_softmax", (4, 4096), 1),
     ("nnc_softmax", (2, 40000), 1), ("nnc_layernorm", (8, 1024), -1), ("nnc_layernorm", (5, 2000), -1),
     ("nnc_layernorm", (2, 40000), -1), ("nnc_layernorm", (3, 4, 200), 1), ("nnc_layernorm", (2, 40, 50), 1),
+    # 16-byte rows (ragged float4 runs per lane) and scalar rows of the warp kernels
+    ("nnc_softmax", (37, 100), 1), ("nnc_softmax", (33, 128), 1), ("nnc_softmax", (16, 260), 1),
+    ("nnc_softmax", (9, 250), 1), ("nnc_layernorm", (33, 100), -1), ("nnc_layernorm", (64, 256), -1),
+    ("nnc_layernorm", (8, 6, 20), 1), ("nnc_layernorm", (7, 98), -1), ("nnc_layernorm", (5, 1000), -1),
 ]
 
 
