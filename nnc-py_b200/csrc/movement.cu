@@ -14,31 +14,34 @@ namespace {
 
 constexpr int kTile = 32;
 
-// out[b][c][r] = in[b][r][c] for a batch of R x C matrices (32x32 smem tiles,
-// both the read and the write are coalesced).
+// out[b][c][r] = in[b][r][c] for a batch of R x C matrices: one 32 x 32
+// tile per block (blockIdx.x: column tile, y: row tile, z: batch; y and z
+// strided past 65535), staged in shared memory so that both the read and
+// the write are coalesced; no index division.
 template <typename T>
 __global__ void __launch_bounds__(256) batched_transpose_kernel(const T* __restrict__ in,
                                                                 T* __restrict__ out, int64_t batch,
                                                                 int64_t R, int64_t C,
                                                                 int64_t in_bs) {
   __shared__ T tile[kTile][kTile + 1];
-  const int64_t tiles_r = cdiv(R, kTile), tiles_c = cdiv(C, kTile);
-  const int64_t per_batch = tiles_r * tiles_c;
-  for (int64_t t = blockIdx.x; t < batch * per_batch; t += gridDim.x) {
-    const int64_t b = t / per_batch;
-    const int64_t tr = (t % per_batch) / tiles_c, tc = (t % per_batch) % tiles_c;
+  const int tx = threadIdx.x % kTile, ty = threadIdx.x / kTile;
+  const int64_t c = (int64_t)blockIdx.x * kTile + tx;
+  for (int64_t rt = blockIdx.y; rt * kTile < R; rt += gridDim.y)
+  for (int64_t b = blockIdx.z; b < batch; b += gridDim.z) {
+    const int64_t r0 = rt * kTile;
+    const int64_t r2 = r0 + tx;
     const T* src = in + b * in_bs;
     T* dst = out + b * R * C;
-    const int64_t c = tc * kTile + threadIdx.x % kTile;
-    for (int j = threadIdx.x / kTile; j < kTile; j += 256 / kTile) {
-      const int64_t r = tr * kTile + j;
-      if (r < R && c < C) tile[j][threadIdx.x % kTile] = src[r * C + c];
+#pragma unroll
+    for (int j = ty; j < kTile; j += 256 / kTile) {
+      const int64_t r = r0 + j;
+      if (r < R && c < C) tile[j][tx] = src[r * C + c];
     }
     __syncthreads();
-    const int64_t r2 = tr * kTile + threadIdx.x % kTile;
-    for (int j = threadIdx.x / kTile; j < kTile; j += 256 / kTile) {
-      const int64_t c2 = tc * kTile + j;
-      if (r2 < R && c2 < C) dst[c2 * R + r2] = tile[threadIdx.x % kTile][j];
+#pragma unroll
+    for (int j = ty; j < kTile; j += 256 / kTile) {
+      const int64_t c2 = (int64_t)blockIdx.x * kTile + j;
+      if (r2 < R && c2 < C) dst[c2 * R + r2] = tile[tx][j];
     }
     __syncthreads();
   }
@@ -138,8 +141,14 @@ void flat_copy(Tensor* input, Tensor* output, const char* op) {
 bool batched_transpose_f32(const float* in, float* out, int64_t batch, int64_t R, int64_t C,
                            const char* op, int64_t in_batch_stride) {
   if (batch * R * C == 0) return true;
-  const int64_t tiles = batch * cdiv(R, kTile) * cdiv(C, kTile);
-  const int grid = (int)(tiles < (int64_t)sm_count() * 16 ? tiles : (int64_t)sm_count() * 16);
+  const int64_t tc = cdiv(C, kTile), tr = cdiv(R, kTile);
+  if (tc > 0x7fffffff) {
+    fail(NNC_CUDA_ERR_UNSUPPORTED, op, "transpose of %lld x %lld matrices", (long long)R,
+         (long long)C);
+    return false;
+  }
+  const dim3 grid((unsigned)tc, (unsigned)(tr < 65535 ? tr : 65535),
+                  (unsigned)(batch < 65535 ? batch : 65535));
   batched_transpose_kernel<float><<<grid, 256, 0, ctx().stream>>>(
       in, out, batch, R, C, in_batch_stride < 0 ? R * C : in_batch_stride);
   return check_launch(op);

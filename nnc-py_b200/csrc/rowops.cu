@@ -11,9 +11,11 @@
 //   inner  > 1 : one thread per (outer, inner) column walking `dim` with
 //                stride `inner`; consecutive threads read consecutive
 //                addresses, so every pass is coalesced.
-// Reductions accumulate in fp64 (the reference uses Kahan-compensated fp32
-// for reduce, plain fp32 for softmax/layernorm); results agree to within a
-// few fp32 ulps and the final roundings/divisions are the reference's.
+// Reduce accumulates in fp64 (the reference: Kahan-compensated fp32).
+// Softmax and layernorm (reference: sequential fp32) sum each lane's values
+// pairwise (warp kernels) or compensated (block kernels) in fp32 and combine
+// the lanes in fp64, and scale by a reciprocal instead of dividing each
+// element: results agree with the reference to within a few fp32 ulps.
 #include <math.h>
 
 #include "common.cuh"
@@ -41,6 +43,20 @@ __device__ __forceinline__ void comp_add(float& s, float& c, float x) {
   const float e = fabsf(s) >= fabsf(x) ? __fadd_rn(__fsub_rn(s, t), x) : __fadd_rn(__fsub_rn(x, t), s);
   c = __fadd_rn(c, e);
   s = t;
+}
+
+// Pairwise (tree) fp32 sum of a lane's N values: error O(log2 N) ulps of
+// the magnitudes summed, one add per value.
+template <int N>
+__device__ __forceinline__ float tree_sum(const float (&x)[N]) {
+  float t[N];
+#pragma unroll
+  for (int k = 0; k < N; ++k) t[k] = x[k];
+#pragma unroll
+  for (int w = 1; w < N; w *= 2)
+#pragma unroll
+    for (int k = 0; k + w < N; k += 2 * w) t[k] = __fadd_rn(t[k], t[k + w]);
+  return t[0];
 }
 
 // Element k of a lane's VPT values in a warp-per-row kernel: lane-strided
@@ -129,7 +145,7 @@ __global__ void __launch_bounds__(kThreads) softmax_row_kernel(const float* __re
 
 // Short rows (dim <= 32 VPT): one warp per row, VPT values per lane in
 // registers (VEC: 16-byte loads and stores), shuffle reductions only; 8 rows
-// per 256-thread block. The sum is compensated fp32 per lane, combined in
+// per 256-thread block. The sum is a pairwise fp32 sum per lane, combined in
 // fp64; outputs are e * (1 / sum) (within one ulp of e / sum).
 template <int VPT, bool VEC>
 __global__ void __launch_bounds__(kThreads) softmax_warp_kernel(const float* __restrict__ in,
@@ -162,15 +178,9 @@ __global__ void __launch_bounds__(kThreads) softmax_warp_kernel(const float* __r
 #pragma unroll
     for (int k = 0; k < VPT; ++k) m = (v[k] > m) ? v[k] : m;
     m = warp_max(m);
-    float s = 0.0f, c = 0.0f;
 #pragma unroll
-    for (int k = 0; k < VPT; ++k) {
-      if (row_index<VEC>(lane, k) < dim) {
-        v[k] = expf(v[k] - m);
-        comp_add(s, c, v[k]);
-      }
-    }
-    const float inv = __frcp_rn((float)warp_sum((double)s + (double)c));
+    for (int k = 0; k < VPT; ++k) v[k] = row_index<VEC>(lane, k) < dim ? expf(v[k] - m) : 0.0f;
+    const float inv = __frcp_rn((float)warp_sum((double)tree_sum(v)));
     if constexpr (VEC) {
 #pragma unroll
       for (int k = 0; k < VPT; k += 4) {
@@ -350,9 +360,9 @@ __global__ void __launch_bounds__(kThreads) layernorm_kernel(
 
 // Short slabs (len <= 32 VPT): one warp per slab; `inner` == 1 indexes
 // scale/bias by the element, else by i / inner (32-bit: len fits). VEC:
-// 16-byte loads and stores (inner == 1 only). Statistics: compensated fp32
-// per lane combined in fp64; outputs scale * ((x - mean) * (1 / sd)) + bias
-// (within one ulp of the division).
+// 16-byte loads and stores. Statistics: pairwise fp32 sums per lane combined
+// in fp64; outputs scale * ((x - mean) * (1 / sd)) + bias (within one ulp of
+// the division).
 template <int VPT, bool VEC>
 __global__ void __launch_bounds__(kThreads) layernorm_warp_kernel(
     const float* __restrict__ in, const float* __restrict__ scale, const float* __restrict__ bias,
@@ -394,19 +404,16 @@ __global__ void __launch_bounds__(kThreads) layernorm_warp_kernel(
         v[k] = i < len ? x[i] : 0.0f;
       }
     }
-    float s = 0.0f, c = 0.0f;
-#pragma unroll
-    for (int k = 0; k < VPT; ++k) comp_add(s, c, v[k]);  // padding adds 0
-    const float mean = __fdiv_rn((float)warp_sum((double)s + (double)c), inv_n);
-    float q = 0.0f, qc = 0.0f;
+    // Padding holds 0 and adds nothing to the sum; its squared deviations
+    // are zeroed.
+    const float mean = __fdiv_rn((float)warp_sum((double)tree_sum(v)), inv_n);
+    float dd[VPT];
 #pragma unroll
     for (int k = 0; k < VPT; ++k) {
-      if (row_index<VEC>(lane, k) < len) {
-        const float d = __fsub_rn(v[k], mean);
-        comp_add(q, qc, __fmul_rn(d, d));
-      }
+      const float d = __fsub_rn(v[k], mean);
+      dd[k] = row_index<VEC>(lane, k) < len ? __fmul_rn(d, d) : 0.0f;
     }
-    const float var = __fdiv_rn((float)warp_sum((double)q + (double)qc), inv_n);
+    const float var = __fdiv_rn((float)warp_sum((double)tree_sum(dd)), inv_n);
     const float rsd = __frcp_rn(__fsqrt_rn(__fadd_rn(var, eps)));
 #pragma unroll
     for (int k = 0; k < VPT; ++k) {
