@@ -18,6 +18,7 @@
 // ops.c:1800-1840). Shapes the TMA path cannot take (K % 4 != 0, unaligned
 // bases, very small M or N) go to a SIMT kernel with fp64 accumulation.
 #include <math.h>
+#include <stdlib.h>
 
 #include "common.cuh"
 #include "movement.cuh"
@@ -322,6 +323,255 @@ __global__ void __launch_bounds__(kTCThreads, 1)
   }
 }
 
+// ------------------------------------------------------- CTA pairs ----
+//
+// TF32 problems with N > 128 and enough 256-row tiles to occupy the SMs run on
+// CTA pairs (tcgen05 cta_group::2): a cluster of two CTAs computes a 256 x BN
+// tile. CTA r loads rows [m0 + 128 r, +128) of A and its half of the tile's
+// B (BN / 2 rows of a [N, K] B, or BN / 2 columns of a [K, N] B); the even
+// CTA issues M = 256 MMAs that read both CTAs' operands at the same shared
+// offsets, each CTA's TMEM holding its 128 rows x BN columns. Per k-block an
+// SM receives 16 + 16 KB for 512 MMA cycles (the single-CTA kernel's BN = 256
+// tiles need 16 + 32 KB, more than the ~80 B/clk TMA delivers per SM).
+// Barriers as in the conv pair kernel: the even CTA's full[s] counts both
+// CTAs' bytes, its commits arrive in both CTAs (empty, tfull, done), and all
+// eight epilogue warps arrive on the even CTA's tempty. Rows past M are zero
+// filled by TMA and clipped by the TMA stores. No load uses cluster multicast.
+template <int BN, int STAGES>
+struct GemmPairCfg {
+  static constexpr uint32_t A_BYTES = BM * BK * 4;         // 16 KB
+  static constexpr uint32_t B_BYTES = (BN / 2) * BK * 4;   // this CTA's half of B
+  static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr uint32_t TMEM_COLS = 2 * BN;
+  static constexpr uint32_t STAGING_BYTES = 4 * 2 * 4096;
+  static constexpr size_t SMEM =
+      (size_t)STAGES * STAGE_BYTES + STAGING_BYTES + 1024 /*align*/ + 256 /*bars*/;
+};
+
+template <int BN, int STAGES>
+__global__ void __launch_bounds__(kTCThreads, 1)
+    gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    const __grid_constant__ CUtensorMap tmD, const GemmArgs g) {
+  using Cfg = GemmPairCfg<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  float* staging = reinterpret_cast<float*>(smem + STAGES * Cfg::STAGE_BYTES);
+  uint64_t* full =
+      reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES + Cfg::STAGING_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* done = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = tc::cluster_ctarank();  // 0: issues the MMAs
+  const int64_t cluster = blockIdx.x >> 1, clusters = gridDim.x >> 1;
+  const int kblocks = (g.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      tc::mbar_init(&full[s], 1);
+      tc::mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      tc::mbar_init(&tfull[a], 1);
+      tc::mbar_init(&tempty[a], 8);  // even CTA: both CTAs' four epilogue warps
+    }
+    tc::mbar_init(done, 1);
+    tc::fence_barrier_init();
+    tc::prefetch_tmap(&tmA);
+    tc::prefetch_tmap(&tmB);
+  }
+  if (warp == 1) {
+    tc::tmem_alloc_pair(tmem_slot, Cfg::TMEM_COLS);
+    tc::tmem_relinquish_pair();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::cluster_sync();  // both CTAs' barriers initialised, TMEM allocated
+  tc::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int per_b = g.m_tiles * g.n_tiles;  // m_tiles counts 256-row tiles here
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- producer (one thread per CTA) ----------------
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int64_t t = cluster; t < g.tiles && ok; t += clusters) {
+        const int b = (int)(t / per_b);
+        const int mt = (int)((t % per_b) / g.n_tiles), nt = (int)((t % per_b) % g.n_tiles);
+        const int row0 = mt * (2 * BM) + (int)rank * BM;
+        const int n_half = nt * BN + (int)rank * (BN / 2);
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!tc::mbar_wait(&empty[stage], phase ^ 1, g.err)) {
+            ok = false;
+            break;
+          }
+          uint8_t* s = smem + stage * Cfg::STAGE_BYTES;
+          if (rank == 0) tc::mbar_arrive_expect_tx(&full[stage], 2 * Cfg::STAGE_BYTES);
+          const uint32_t bar = tc::mapa(tc::smem_u32(&full[stage]), 0);
+          const int kx = kb * BK;
+          tc::tma_load_3d_pair(s, &tmA, bar, kx, row0, b * g.a_batched);
+          uint8_t* sb = s + Cfg::A_BYTES;
+          if (g.b_mn) {
+#pragma unroll
+            for (int c = 0; c < BN / 64; ++c)
+              tc::tma_load_3d_pair(sb + c * 4096, &tmB, bar, n_half + 32 * c, kx, b * g.b_batched);
+          } else {
+            tc::tma_load_3d_pair(sb, &tmB, bar, kx, n_half, b * g.b_batched);
+          }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      // The even CTA lets the last issued loads of both CTAs land before it
+      // can leave (the odd CTA's loads count on these barriers too).
+      if (ok && rank == 0) {
+        for (int q = 0; q < STAGES; ++q) {
+          if (stage == 0) {
+            stage = STAGES;
+            phase ^= 1;
+          }
+          --stage;
+          tc::mbar_wait(&full[stage], phase, g.err);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (rank == 0 && lane == 0) {
+      // ---------------- MMA issuer (even CTA) ----------------
+      const uint32_t idesc = tc::idesc_tf32(2 * BM, BN) | (g.b_mn ? tc::kIdescBMajorMN : 0u);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int64_t t = cluster; t < g.tiles && ok; t += clusters, ++local) {
+        const int acc = local & 1;
+        const uint32_t aphase = (local >> 1) & 1;
+        if (!tc::mbar_wait(&tempty[acc], aphase ^ 1, g.err)) break;
+        tc::tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!tc::mbar_wait(&full[stage], phase, g.err)) {
+            ok = false;
+            break;
+          }
+          tc::tc_fence_after();
+          const uint32_t sa = tc::smem_u32(smem + stage * Cfg::STAGE_BYTES);
+          const uint32_t sb = sa + Cfg::A_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / 8; ++k) {
+            const uint64_t bd = g.b_mn ? tc::desc_mn_sw128_atom32(sb + k * 1024, 4096)
+                                       : tc::desc_kmajor_sw128(sb + k * 32);
+            tc::mma_tf32_pair(d_tmem, tc::desc_kmajor_sw128(sa + k * 32), bd, idesc,
+                              (kb | k) != 0);
+          }
+          tc::mma_commit_pair_both(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        tc::mma_commit_pair_both(&tfull[acc]);
+      }
+      tc::mma_commit_pair_both(done);
+      tc::mbar_wait(done, 0, g.err);
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5 of both CTAs) ----------------
+    const int quad = warp & 3;
+    float* box0 = staging + quad * 2 * 1024;
+    int bsel = 0;
+    const uint32_t tempty0 = tc::mapa(tc::smem_u32(&tempty[0]), 0);
+    int local = 0;
+    for (int64_t t = cluster; t < g.tiles; t += clusters, ++local) {
+      const int b = (int)(t / per_b);
+      const int mt = (int)((t % per_b) / g.n_tiles), nt = (int)((t % per_b) % g.n_tiles);
+      const int acc = local & 1;
+      const uint32_t aphase = (local >> 1) & 1;
+      if (!tc::mbar_wait(&tfull[acc], aphase, g.err)) break;
+      tc::tc_fence_after();
+      const int row0 = mt * (2 * BM) + (int)rank * BM + quad * 32;
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        const int n0 = nt * BN + c0;
+        if (n0 >= g.N) break;  // warp-uniform
+        uint32_t r[32];
+        __syncwarp();
+        const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN + c0;
+        tc::tmem_ld16(taddr, *reinterpret_cast<uint32_t(*)[16]>(&r[0]));
+        tc::tmem_ld16(taddr + 16, *reinterpret_cast<uint32_t(*)[16]>(&r[16]));
+        tc::tmem_ld_wait();
+        if (row0 >= g.M) continue;  // warp-uniform: the whole box lies below M
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = g.alpha * __uint_as_float(r[j]);
+        if (g.c_mode == 1) {
+          const float* cb = g.C + n0;
+          if (n0 + 32 <= g.N && ((uintptr_t)cb & 15) == 0) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const float4 c4 = __ldg(reinterpret_cast<const float4*>(cb) + j);
+              v[4 * j] = fmaf(g.beta, c4.x, v[4 * j]);
+              v[4 * j + 1] = fmaf(g.beta, c4.y, v[4 * j + 1]);
+              v[4 * j + 2] = fmaf(g.beta, c4.z, v[4 * j + 2]);
+              v[4 * j + 3] = fmaf(g.beta, c4.w, v[4 * j + 3]);
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (n0 + j < g.N) v[j] = fmaf(g.beta, __ldg(cb + j), v[j]);
+          }
+        } else if (g.c_mode == 2 && row0 + lane < g.M) {
+          const float* crow =
+              g.C + (int64_t)b * g.c_batch_stride + (int64_t)(row0 + lane) * g.ldc;
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (n0 + j < g.N) v[j] = fmaf(g.beta, crow[n0 + j], v[j]);
+        }
+        if (g.relu) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = v[j] > 0.0f ? v[j] : 0.0f;
+        }
+        float* box = box0 + bsel * 1024;
+        if (lane == 0) tc::bulk_wait_group_read<1>();
+        __syncwarp();
+        float4* brow = reinterpret_cast<float4*>(box + lane * 32);
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          brow[j ^ (lane & 7)] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+        tc::fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tc::tma_store_3d(&tmD, box, n0, row0, b);
+          tc::bulk_commit_group();
+        }
+        bsel ^= 1;
+      }
+      tc::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive_cluster(tempty0 + acc * (uint32_t)sizeof(uint64_t));
+    }
+    if (lane == 0) tc::bulk_wait_group<0>();
+    // The odd CTA leaves only after the even CTA's last commit has arrived
+    // here (its barriers receive the pair's commits).
+    if (rank == 1 && warp == 2) tc::mbar_wait_warp(done, 0, g.err);
+  }
+
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::cluster_sync();  // no CTA frees the pair's TMEM or leaves while the other works
+  if (warp == 1) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc_pair(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
 // hi = tf32(x), lo = x - hi (exact in fp32), for matrices of `mat` elements
 // read at x + b * in_bs and written densely.
 __global__ void __launch_bounds__(256) split_tf32_kernel(const float* __restrict__ x,
@@ -481,6 +731,94 @@ bool launch_tc(const Problem& p, const float* A0, const float* A1, const float* 
   return check_launch(op);
 }
 
+// CTA-pair launch (TF32, D written by TMA stores): see gemm_tc2_kernel.
+template <int BN, int STAGES>
+bool launch_tc2(const Problem& p, const float* A, const float* B, const char* op) {
+  using Cfg = GemmPairCfg<BN, STAGES>;
+  CUtensorMap ta, tb, td;
+  const uint64_t a_dims[3] = {(uint64_t)p.K, (uint64_t)p.M, (uint64_t)(p.a_bs ? p.batches : 1)};
+  const uint64_t a_str[2] = {(uint64_t)p.K * 4, (uint64_t)(p.a_bs ? p.a_bs : (int64_t)p.M * p.K) * 4};
+  const uint32_t a_box[3] = {BK, BM, 1};
+  if (!encode_tmap_f32(&ta, A, 3, a_dims, a_str, a_box, nullptr, op)) return false;
+  const bool mn = !p.b_kmajor;
+  const uint64_t b_dims[3] = {(uint64_t)(mn ? p.N : p.K), (uint64_t)(mn ? p.K : p.N),
+                              (uint64_t)(p.b_bs ? p.batches : 1)};
+  const uint64_t b_str[2] = {(uint64_t)(mn ? p.N : p.K) * 4,
+                             (uint64_t)(p.b_bs ? p.b_bs : (int64_t)p.N * p.K) * 4};
+  const uint32_t b_box[3] = {mn ? 32u : (uint32_t)BK, mn ? (uint32_t)BK : (uint32_t)(BN / 2), 1};
+  if (!encode_tmap_f32(&tb, B, 3, b_dims, b_str, b_box, nullptr, op, mn ? kSwizzle128Atom32 : 128))
+    return false;
+  const uint64_t d_dims[3] = {(uint64_t)p.N, (uint64_t)p.M, (uint64_t)p.batches};
+  const uint64_t d_str[2] = {(uint64_t)p.N * 4,
+                             (uint64_t)(p.batches > 1 ? p.d_bs : (int64_t)p.M * p.N) * 4};
+  const uint32_t d_box[3] = {32, 32, 1};
+  if (!encode_tmap_f32(&td, p.D, 3, d_dims, d_str, d_box, nullptr, op)) return false;
+  GemmArgs g;
+  g.M = p.M;
+  g.N = p.N;
+  g.K = p.K;
+  g.m_tiles = (int)cdiv(p.M, 2 * BM);
+  g.n_tiles = (int)cdiv(p.N, BN);
+  g.tiles = (int64_t)p.batches * g.m_tiles * g.n_tiles;
+  g.a_batched = p.a_bs ? 1 : 0;
+  g.b_batched = p.b_bs ? 1 : 0;
+  g.alpha = p.alpha;
+  g.beta = p.beta;
+  g.C = p.C;
+  g.c_mode = p.c_mode;
+  g.ldc = p.ldc;
+  g.c_batch_stride = p.c_bs;
+  g.D = p.D;
+  g.ldd = p.N;
+  g.d_batch_stride = p.d_bs;
+  g.relu = p.relu;
+  g.tma_store = 1;
+  g.b_mn = mn ? 1 : 0;
+  g.err = device_error_word();
+  auto kern = gemm_tc2_kernel<BN, STAGES>;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(kTCThreads, 1, 1);
+  cfg.dynamicSmemBytes = Cfg::SMEM;
+  cfg.stream = ctx().stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  static bool attr_set[64] = {};
+  static int max_pairs[64] = {};
+  if (!attr_set[ctx().device]) {
+    if (!check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)Cfg::SMEM),
+                    op, "cudaFuncSetAttribute"))
+      return false;
+    int n = 0;
+    cfg.gridDim = dim3(2 * (sm_count() / 2), 1, 1);
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = sm_count() / 2;
+    }
+    max_pairs[ctx().device] = n;
+    attr_set[ctx().device] = true;
+  }
+  const int64_t pairs = g.tiles < max_pairs[ctx().device] ? g.tiles : max_pairs[ctx().device];
+  cfg.gridDim = dim3((unsigned)(2 * pairs), 1, 1);
+  if (!check_cuda(cudaLaunchKernelEx(&cfg, kern, ta, tb, td, g), op, "cudaLaunchKernelEx"))
+    return false;
+  return check_launch(op);
+}
+
+// Whether NNC_CUDA_GEMM_PAIR (default on) lets large TF32 problems use CTA pairs.
+bool gemm_pair_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("NNC_CUDA_GEMM_PAIR");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
 void launch_simt(const Problem& p, const char* op) {
   SimtArgs a;
   a.M = p.M;
@@ -568,6 +906,14 @@ void run_problem(Problem p, const char* op) {
     if (p.b_bs) p.b_bs = (int64_t)p.N * p.K;
   }
   if (!split) {
+    // CTA pairs: N > 128, whole 256-row tiles' worth of M, TMA-storable D and
+    // enough pair tiles to keep most pairs busy.
+    const bool d_tma = (p.N % 4 == 0) && (p.d_bs % 4 == 0) && aligned16(p.D);
+    if (gemm_pair_enabled() && d_tma && p.N > 128 && p.M >= 2 * BM &&
+        (int64_t)cdiv(p.M, 2 * BM) * cdiv(p.N, 256) * p.batches >= sm_count() / 2 - 10) {
+      launch_tc2<256, 6>(p, A, B, op);
+      return;
+    }
     if (p.N > 128 && (int64_t)cdiv(p.M, BM) * cdiv(p.N, 256) * p.batches >= sm_count())
       launch_tc<256, 1, 4>(p, A, nullptr, B, nullptr, op);
     else if (p.N > 64)

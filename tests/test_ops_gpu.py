@@ -176,6 +176,37 @@ def test_matmul_layouts_vs_oracle(cuda_lib, prec, cfg):
     C.assert_close(got, want, C.TC_RTOL[prec], f"{kind}{sa}x{sb}")
 
 
+# TF32 problems large enough for the CTA-pair GEMM kernel (N > 128, M >= 256,
+# at least ~64 tiles of 256 x 256): [K, N] B read MN-major and [N, K] B
+# K-major, the reference's batch offsets, ragged M / N / K, C matrix with
+# alpha / beta, relu.
+PAIR_GEMM_CASES = [
+    ("mm", (2048, 128), (128, 2048)), ("mm", (64, 256, 96), (64, 96, 264)),
+    ("gemm01", (4100, 36), (1032, 36)), ("gemm00_relu", (1300, 64), (64, 3000)),
+]
+
+
+@pytest.mark.parametrize("cfg", PAIR_GEMM_CASES, ids=lambda c: c[0] + "x".join(map(str, c[1] + c[2])))
+def test_gemm_cta_pairs_vs_oracle(cuda_lib, cfg):
+    kind, sa, sb = cfg
+    r = np.random.default_rng(sum(sa) * 7 + sum(sb))
+    arrays = {"a": r.standard_normal(sa).astype(np.float32), "b": r.standard_normal(sb).astype(np.float32)}
+    if kind == "mm":
+        so = sa[:-1] + sb[-1:]
+        case = {"name": "m", "op": "nnc_matmul", "args": [C._t("a"), C._t("b"), C._o("out", so)]}
+    else:
+        tb = int(kind[5])
+        M, N = sa[0], (sb[0] if tb else sb[1])
+        arrays["c"] = r.standard_normal((M, N)).astype(np.float32)
+        op = "nnc_gemm_relu" if kind.endswith("relu") else "nnc_gemm"
+        case = {"name": "g", "op": op, "args": [C._t("a"), C._t("b"), C._t("c"), C._o("out", (M, N)),
+                                                C._f(0.75), C._f(-1.25), C._i(0), C._i(tb)]}
+    cuda_lib.nnc_cuda_set_precision(0)
+    got = C.run_cuda(cuda_lib, case, arrays)["out"]
+    want = C.run_host(_oracle(), case, arrays)["out"]
+    C.assert_close(got, want, C.TC_RTOL[0], f"{kind}{sa}x{sb}")
+
+
 @pytest.mark.parametrize("prec", [0, 1])
 @pytest.mark.parametrize("cfg", [(4, 64, 28, 64, 3, 1, 1), (2, 128, 14, 256, 3, 2, 1), (2, 256, 7, 512, 3, 1, 1),
                                  (2, 3, 56, 64, 7, 2, 3), (2, 64, 28, 128, 1, 2, 0)])
