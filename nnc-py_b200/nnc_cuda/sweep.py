@@ -207,13 +207,18 @@ def op_sweep(so, torch, timer: Timer, pk: dict) -> list[dict]:
 MODEL_FLOPS = {"lenet5": 0.833e6, "resnet18": 3.628e9, "transformer": 0.872e9}
 
 
-def model_runs(so, torch, pk: dict, reps: int) -> list[dict]:
+MODELS = (("lenet5_o1_b8192", "lenet5", 8192), ("resnet18_o1_b64", "resnet18", 64),
+          ("resnet18_o1_b256", "resnet18", 256), ("transformer_o1_b256", "transformer", 256))
+
+
+def model_runs(so, torch, pk: dict, reps: int, only_model: str | None = None) -> list[dict]:
     from .model import CudaModel
     from .workloads import BUILDERS
 
     rows = []
-    for tag, name, batch in (("lenet5_o1_b8192", "lenet5", 8192), ("resnet18_o1_b64", "resnet18", 64),
-                             ("resnet18_o1_b256", "resnet18", 256), ("transformer_o1_b256", "transformer", 256)):
+    for tag, name, batch in MODELS:
+        if only_model and tag != only_model:
+            continue
         m = CudaModel(tag)
         m.init(0)
         wl = BUILDERS[name](batch)
@@ -255,6 +260,8 @@ def main() -> int:
     ap.add_argument("--reps", type=int, default=10)
     ap.add_argument("--json", type=str, default=None)
     ap.add_argument("--only", choices=["ops", "models"], default=None)
+    ap.add_argument("--model", choices=[m[0] for m in MODELS], default=None,
+                    help="run this model only (with --only models)")
     opt = ap.parse_args()
     import torch
 
@@ -274,7 +281,7 @@ def main() -> int:
                   f"{r['frac']:.3f}", flush=True)
     if opt.only in (None, "models"):
         so.nnc_cuda_set_stream(None)
-        out["models"] = model_runs(so, torch, pk, max(opt.reps, 20))
+        out["models"] = model_runs(so, torch, pk, max(opt.reps, 20), opt.model)
         for r in out["models"]:
             print(f"{r['model']:22s} {r['ms_per_forward']:9.4f} ms {r['samples_per_s']:12.1f} /s "
                   f"{r['tflops']:7.1f} TF/s {r['frac_tf32']:.3f}", flush=True)
