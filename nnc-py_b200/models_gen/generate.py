@@ -32,6 +32,7 @@ CONFIGS = [
     ("lenet5_o1_b8192", "lenet5", 8192, 1),
     ("lenet5_o1_b16", "lenet5", 16, 1),
     # config 4: transformer
+    ("transformer_o1_b2048", "transformer", 2048, 1),
     ("transformer_o1_b256", "transformer", 256, 1),
     ("transformer_o1_b1", "transformer", 1, 1),
 ]

@@ -208,7 +208,8 @@ MODEL_FLOPS = {"lenet5": 0.833e6, "resnet18": 3.628e9, "transformer": 0.872e9}
 
 
 MODELS = (("lenet5_o1_b8192", "lenet5", 8192), ("resnet18_o1_b64", "resnet18", 64),
-          ("resnet18_o1_b256", "resnet18", 256), ("transformer_o1_b256", "transformer", 256))
+          ("resnet18_o1_b256", "resnet18", 256), ("transformer_o1_b256", "transformer", 256),
+          ("transformer_o1_b2048", "transformer", 2048))
 
 
 def model_runs(so, torch, pk: dict, reps: int, only_model: str | None = None) -> list[dict]:
