@@ -1588,24 +1588,28 @@ __global__ void __launch_bounds__(256) pack_weight_kernel(const float* __restric
 }
 
 // NCHW [N][C][HW] -> NHWC [N][HW][C4] (channels >= C zero), optional hi/lo.
+// One 32 x 32 (channel x pixel) tile per block: blockIdx.x pixel tile, y
+// channel tile, z image (strided past 65535); no index division.
 __global__ void __launch_bounds__(256) nchw_to_nhwc_pad_kernel(const float* __restrict__ x,
                                                                float* __restrict__ hi,
                                                                float* __restrict__ lo, int N, int C,
                                                                int64_t HW, int C4) {
   __shared__ float tile[32][33];
-  const int64_t tiles_p = cdiv(HW, 32), tiles_c = cdiv(C4, 32);
-  const int64_t per_img = tiles_p * tiles_c;
-  for (int64_t t = blockIdx.x; t < (int64_t)N * per_img; t += gridDim.x) {
-    const int64_t n = t / per_img;
-    const int64_t tp = (t % per_img) / tiles_c, tcb = (t % per_img) % tiles_c;
-    const int tx = threadIdx.x & 31;
-    for (int j = threadIdx.x >> 5; j < 32; j += 8) {
-      const int64_t c = tcb * 32 + j, pix = tp * 32 + tx;
-      tile[j][tx] = (c < C && pix < HW) ? x[(n * C + c) * HW + pix] : 0.0f;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const int64_t p0 = (int64_t)blockIdx.x * 32;
+  const int c0 = blockIdx.y * 32;
+  for (int64_t n = blockIdx.z; n < N; n += gridDim.z) {
+#pragma unroll
+    for (int j = ty; j < 32; j += 8) {
+      const int c = c0 + j;
+      const int64_t pix = p0 + tx;
+      tile[j][tx] = (c < C && pix < HW) ? __ldg(x + (n * C + c) * HW + pix) : 0.0f;
     }
     __syncthreads();
-    for (int j = threadIdx.x >> 5; j < 32; j += 8) {
-      const int64_t pix = tp * 32 + j, c = tcb * 32 + tx;
+#pragma unroll
+    for (int j = ty; j < 32; j += 8) {
+      const int64_t pix = p0 + j;
+      const int c = c0 + tx;
       if (pix < HW && c < C4) {
         const float v = tile[tx][j];
         const int64_t o = (n * HW + pix) * C4 + c;
@@ -2615,8 +2619,8 @@ void conv_impl(Tensor* input, Tensor* weight, Tensor* bias, Tensor* residual, Te
         nchw_to_nhwc_small_kernel<<<grid_for((int64_t)N * H * W, 256, 8), 256, 0, ctx().stream>>>(
             (const float*)input->data, hi, lo, N, C, (int64_t)H * W, C4);
       } else {
-        const int64_t tiles = (int64_t)N * cdiv((int64_t)H * W, 32) * cdiv(C4, 32);
-        const int grid = (int)(tiles < (int64_t)sm_count() * 16 ? tiles : (int64_t)sm_count() * 16);
+        const dim3 grid((unsigned)cdiv((int64_t)H * W, 32), (unsigned)cdiv(C4, 32),
+                        (unsigned)(N < 65535 ? N : 65535));
         nchw_to_nhwc_pad_kernel<<<grid, 256, 0, ctx().stream>>>((const float*)input->data, hi, lo,
                                                                 N, C, (int64_t)H * W, C4);
       }
