@@ -148,18 +148,14 @@ __global__ void __launch_bounds__(kThreads) softmax_row_kernel(const float* __re
 // per 256-thread block. The sum is a pairwise fp32 sum per lane, combined in
 // fp64; outputs are e * (1 / sum) (within one ulp of e / sum).
 template <int VPT, bool VEC>
-__global__ void __launch_bounds__(kThreads) softmax_warp_kernel(const float* __restrict__ in,
+__global__ void __launch_bounds__(kThreads, VPT <= 8 ? 4 : 2) softmax_warp_kernel(const float* __restrict__ in,
                                                                 float* __restrict__ out,
                                                                 int64_t rows, int dim) {
   static_assert(!VEC || VPT % 4 == 0, "vector rows hold whole float4 runs");
   const int lane = threadIdx.x & 31;
   const int64_t step = (int64_t)gridDim.x * (kThreads / 32);
-  for (int64_t row = (int64_t)blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5); row < rows;
-       row += step) {
+  auto load_row = [&](int64_t row, float (&v)[VPT]) {
     const float* x = in + row * dim;
-    float* y = out + row * dim;
-    float v[VPT];
-    float m = -INFINITY;
     if constexpr (VEC) {
 #pragma unroll
       for (int k = 0; k < VPT; k += 4) {
@@ -175,6 +171,23 @@ __global__ void __launch_bounds__(kThreads) softmax_warp_kernel(const float* __r
         v[k] = i < dim ? x[i] : -INFINITY;
       }
     }
+  };
+  // Short rows keep the next row's loads in flight while this row reduces.
+  constexpr bool kPrefetch = VPT <= 8;
+  int64_t row = (int64_t)blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5);
+  float vn[VPT];
+  if (kPrefetch && row < rows) load_row(row, vn);
+  for (; row < rows; row += step) {
+    float* y = out + row * dim;
+    float v[VPT];
+    if constexpr (kPrefetch) {
+#pragma unroll
+      for (int k = 0; k < VPT; ++k) v[k] = vn[k];
+      if (row + step < rows) load_row(row + step, vn);
+    } else {
+      load_row(row, v);
+    }
+    float m = -INFINITY;
 #pragma unroll
     for (int k = 0; k < VPT; ++k) m = (v[k] > m) ? v[k] : m;
     m = warp_max(m);
@@ -364,7 +377,7 @@ __global__ void __launch_bounds__(kThreads) layernorm_kernel(
 // in fp64; outputs scale * ((x - mean) * (1 / sd)) + bias (within one ulp of
 // the division).
 template <int VPT, bool VEC>
-__global__ void __launch_bounds__(kThreads) layernorm_warp_kernel(
+__global__ void __launch_bounds__(kThreads, VPT <= 8 ? 4 : 2) layernorm_warp_kernel(
     const float* __restrict__ in, const float* __restrict__ scale, const float* __restrict__ bias,
     float* __restrict__ out, int64_t rows, int len, int inner, float eps) {
   static_assert(!VEC || VPT % 4 == 0, "vector slabs hold whole float4 runs");
@@ -384,11 +397,8 @@ __global__ void __launch_bounds__(kThreads) layernorm_warp_kernel(
       bt[k] = (bias && i < len) ? __ldg(bias + a) : 0.0f;
     }
   }
-  for (int64_t row = (int64_t)blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5); row < rows;
-       row += step) {
+  auto load_row = [&](int64_t row, float (&v)[VPT]) {
     const float* x = in + row * len;
-    float* y = out + row * len;
-    float v[VPT];
     if constexpr (VEC) {
 #pragma unroll
       for (int k = 0; k < VPT; k += 4) {
@@ -403,6 +413,22 @@ __global__ void __launch_bounds__(kThreads) layernorm_warp_kernel(
         const int i = row_index<false>(lane, k);
         v[k] = i < len ? x[i] : 0.0f;
       }
+    }
+  };
+  // Short slabs keep the next slab's loads in flight while this one reduces.
+  constexpr bool kPrefetch = VPT <= 8;
+  int64_t row = (int64_t)blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5);
+  float vn[VPT];
+  if (kPrefetch && row < rows) load_row(row, vn);
+  for (; row < rows; row += step) {
+    float* y = out + row * len;
+    float v[VPT];
+    if constexpr (kPrefetch) {
+#pragma unroll
+      for (int k = 0; k < VPT; ++k) v[k] = vn[k];
+      if (row + step < rows) load_row(row + step, vn);
+    } else {
+      load_row(row, v);
     }
     // Padding holds 0 and adds nothing to the sum; its squared deviations
     // are zeroed.

@@ -6,9 +6,11 @@ ResNet-18 -O1 (N = 64, 256) and the small transformer (B = 256).
     python -m nnc_cuda.sweep [--reps 10] [--json sweep.json] [--only ops|models]
 
 Every number is a median over `reps` calls timed with CUDA events on the
-launching stream. Before each timed op call the runner reads a 512 MB buffer
-(larger than the 126 MB L2), so inputs come from HBM; a model step replays one
-captured CUDA graph. Denominators: MEASURED_PEAKS.json at the repository root
+launching stream. Each op call is captured once into a CUDA graph and replayed
+per rep (the events bracket its kernels, not the host-side setup of a direct
+call); before each rep the runner reads a 512 MB buffer (larger than the
+126 MB L2), so inputs come from HBM. A model step replays one captured CUDA
+graph of the whole forward. Denominators: MEASURED_PEAKS.json at the repository root
 (HBM copy GB/s; dense TF32 = bf16 burst / 2, each op being timed alone), else
 the pool's fallback figures (6650 GB/s, 1590 TFLOP/s bf16). Inputs are seeded
 N(0, 1), the shapes are BASELINE.json's.
@@ -44,26 +46,41 @@ class Timer:
         self.flush_buf = torch.empty(512 << 18, dtype=torch.float32, device="cuda")  # 512 MB
 
     def time_op(self, fn, warmup: int = 2) -> float:
-        """Median device time in ms of fn() (library calls on the stream)."""
-        torch = self.torch
+        """Median device time in ms of fn() (library calls on the stream).
+
+        The call is captured once into a CUDA graph (nnc_cuda_graph_*) and
+        each timed rep replays it between two events, so the interval holds
+        the op's kernels and not the host work (argument checks, tensor-map
+        encoding) that a direct call would put between the events."""
+        torch, so = self.torch, self.so
         with torch.cuda.stream(self.stream):
             for _ in range(warmup):
                 fn()
         self.stream.synchronize()
+        if so.nnc_cuda_graph_begin() != 0:
+            raise RuntimeError("nnc_cuda_graph_begin failed")
+        fn()
+        graph = so.nnc_cuda_graph_end()
+        if not graph:
+            raise RuntimeError(so.nnc_cuda_get_last_error_string().decode())
         times = []
-        for _ in range(self.reps):
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            with torch.cuda.stream(self.stream):
-                # Read (not write) the buffer: L2 then holds clean lines, so
-                # the timed call pays no write-back of the flush.
-                self.flush_sink = self.flush_buf.sum()
-                e0.record(self.stream)
-                fn()
-                e1.record(self.stream)
-            e1.synchronize()
-            times.append(e0.elapsed_time(e1))
-        if self.so.nnc_cuda_get_last_error() != 0:
-            raise RuntimeError(self.so.nnc_cuda_get_last_error_string().decode())
+        try:
+            for _ in range(self.reps):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                with torch.cuda.stream(self.stream):
+                    # Read (not write) the buffer: L2 then holds clean lines, so
+                    # the timed call pays no write-back of the flush.
+                    self.flush_sink = self.flush_buf.sum()
+                    e0.record(self.stream)
+                    if so.nnc_cuda_graph_launch(ctypes.c_void_p(graph)) != 0:
+                        raise RuntimeError(so.nnc_cuda_get_last_error_string().decode())
+                    e1.record(self.stream)
+                e1.synchronize()
+                times.append(e0.elapsed_time(e1))
+        finally:
+            so.nnc_cuda_graph_destroy(ctypes.c_void_p(graph))
+        if so.nnc_cuda_get_last_error() != 0:
+            raise RuntimeError(so.nnc_cuda_get_last_error_string().decode())
         return statistics.median(times)
 
 
