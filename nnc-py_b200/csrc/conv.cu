@@ -1924,20 +1924,21 @@ __global__ void __launch_bounds__(128, 5) conv_direct_row_kernel(ConvArgs g,
   __syncthreads();
   const int64_t OHW = (int64_t)g.OH * g.OW;
   const int nb = (g.OW + OWB - 1) / OWB;
-  const int64_t units = (int64_t)g.N * g.OH * nb * CG;
+  // Unit and row indices are 32-bit (the host checks N * OH * nb * CG < 2^31):
+  // 64-bit divisions cost ~70 instructions each here.
+  const unsigned units = (unsigned)g.N * g.OH * nb * CG;
   const int sc = (int)g.xs_c, shh = (int)g.xs_h, sww = (int)g.xs_w;
   const bool staged = g.out_nhwc && g.Cout <= CS;
   const bool add = g.act == kActAddRelu;
   // Block-uniform passes (every thread takes part in the barriers).
-  for (int64_t base = blockIdx.x * (int64_t)blockDim.x; base < units;
-       base += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t u = base + threadIdx.x;
+  for (unsigned base = blockIdx.x * blockDim.x; base < units; base += gridDim.x * blockDim.x) {
+    const unsigned u = base + threadIdx.x;
     const bool active = u < units;
     const int cg = (int)(u % CG);
-    const int64_t ub = u / CG;
-    const int64_t row = ub / nb;  // n * OH + oh
+    const unsigned ub = u / CG;
+    const unsigned row = ub / nb;  // n * OH + oh
     const int ob = (int)(ub - row * nb);
-    const int64_t n = row / g.OH;
+    const unsigned n = row / g.OH;
     const int oh = (int)(row - n * g.OH);
     const int ow0 = ob * OWB;
     float acc[OWB][CO];
@@ -1947,7 +1948,7 @@ __global__ void __launch_bounds__(128, 5) conv_direct_row_kernel(ConvArgs g,
       for (int co = 0; co < CO; ++co) acc[o][co] = 0.0f;
     if (active) {
       const int ih0 = oh * g.sh - g.ph, iw0 = ow0 - g.pw;
-      const float* xn = g.x_hi + n * g.xs_n;
+      const float* xn = g.x_hi + (int64_t)n * g.xs_n;
       const float4* wk = reinterpret_cast<const float4*>(ws) + cg * (CO / 4);
       for (int c = 0; c < C; ++c) {
         const float* xc = xn + c * sc;
@@ -1984,26 +1985,27 @@ __global__ void __launch_bounds__(128, 5) conv_direct_row_kernel(ConvArgs g,
         for (int o = 0; o < OWB; ++o) {
           const int ow = ow0 + o;
           if (ow >= g.OW) break;
-          direct_store<CO>(g, acc[o], row * g.OW + ow, n, (int64_t)oh * g.OW + ow, OHW, cg * CO);
+          direct_store<CO>(g, acc[o], (int64_t)row * g.OW + ow, n, (int64_t)oh * g.OW + ow, OHW,
+                           cg * CO);
         }
       }
       continue;  // block-uniform
     }
     // The pass's pixel range [m0, m1): from its first unit to its last.
-    const int64_t ub0 = base / CG;
-    const int64_t row0 = ub0 / nb;
-    const int64_t m0 = row0 * g.OW + (int64_t)(ub0 - row0 * nb) * OWB;
-    const int64_t u_last = (base + blockDim.x < units ? base + blockDim.x : units) - 1;
-    const int64_t ubl = u_last / CG;
-    const int64_t rowl = ubl / nb;
+    const unsigned ub0 = base / CG;
+    const unsigned row0 = ub0 / nb;
+    const int64_t m0 = (int64_t)row0 * g.OW + (int64_t)(ub0 - row0 * nb) * OWB;
+    const unsigned u_last = (base + blockDim.x < units ? base + blockDim.x : units) - 1;
+    const unsigned ubl = u_last / CG;
+    const unsigned rowl = ubl / nb;
     const int owl = (int)(ubl - rowl * nb) * OWB + OWB;
-    const int64_t m1 = rowl * g.OW + (owl < g.OW ? owl : g.OW);
+    const int64_t m1 = (int64_t)rowl * g.OW + (owl < g.OW ? owl : g.OW);
     if (active) {
 #pragma unroll
       for (int o = 0; o < OWB; ++o) {
         const int ow = ow0 + o;
         if (ow >= g.OW) break;
-        const int pl = (int)(row * g.OW + ow - m0);
+        const int pl = (int)((int64_t)row * g.OW + ow - m0);
 #pragma unroll
         for (int j = 0; j < CO; ++j) {
           const int co = cg * CO + j;
@@ -2418,7 +2420,7 @@ void conv_impl(Tensor* input, Tensor* weight, Tensor* bias, Tensor* residual, Te
     const int64_t units = (int64_t)N * OH * cdiv(OW, 4) * cgs;
     const int grid4 = (int)(cdiv(units, 128) < (int64_t)sm_count() * 8 ? cdiv(units, 128)
                                                                          : (int64_t)sm_count() * 8);
-    if (sw == 1 && (KW == 5 || KW == 3)) {
+    if (sw == 1 && (KW == 5 || KW == 3) && units + (int64_t)grid4 * 128 < (1ll << 31)) {
       if (Cout <= 8 && KW == 5)
         conv_direct_row_kernel<8, 1, 5, 4><<<grid4, 128, 0, st>>>(g, wp, src_mode, wl0.C4, wl0.Kpad);
       else if (KW == 5)
