@@ -1919,11 +1919,16 @@ __global__ void __launch_bounds__(128, 5) conv_direct_row_kernel(ConvArgs g,
   // pixels are CO * OWB scattered scalars otherwise).
   __shared__ __align__(16) float obuf[kPix * CS];
   constexpr int XW = OWB - 1 + KW;
+  constexpr int XW4 = (XW + 3) / 4;
   const int C = g.K / (g.KH * KW);
   stage_direct_weights<CS>(g, w, src_mode, src_c4, src_kpad, ws);
   __syncthreads();
   const int64_t OHW = (int64_t)g.OH * g.OW;
   const int nb = (g.OW + OWB - 1) / OWB;
+  // 16-byte row reads need an aligned base, row and plane pitches that are
+  // multiples of 4 floats, and a left pad that keeps ow0 - pw aligned.
+  const bool x_vec = ((uintptr_t)g.x_hi & 15) == 0 && g.xs_h % 4 == 0 && g.xs_c % 4 == 0 &&
+                     g.xs_n % 4 == 0 && g.pw % 4 == 0;
   // Unit and row indices are 32-bit (the host checks N * OH * nb * CG < 2^31):
   // 64-bit divisions cost ~70 instructions each here.
   const unsigned units = (unsigned)g.N * g.OH * nb * CG;
@@ -1949,6 +1954,9 @@ __global__ void __launch_bounds__(128, 5) conv_direct_row_kernel(ConvArgs g,
     if (active) {
       const int ih0 = oh * g.sh - g.ph, iw0 = ow0 - g.pw;
       const float* xn = g.x_hi + (int64_t)n * g.xs_n;
+      // Unit-stride rows whose segment starts 16-byte aligned and lies inside
+      // the image width (planar input, W and the pad multiples of 4).
+      const bool vec_rows = sww == 1 && iw0 >= 0 && iw0 + XW4 * 4 <= g.W && x_vec;
       const float4* wk = reinterpret_cast<const float4*>(ws) + cg * (CO / 4);
       for (int c = 0; c < C; ++c) {
         const float* xc = xn + c * sc;
@@ -1956,11 +1964,23 @@ __global__ void __launch_bounds__(128, 5) conv_direct_row_kernel(ConvArgs g,
           const int ih = ih0 + kh;
           const bool row_ok = (unsigned)ih < (unsigned)g.H;
           const float* xr = xc + ih * shh;
-          float xv[XW];
+          float xv[XW4 * 4];
+          if (vec_rows) {  // the whole segment inside the row: 16-byte loads
 #pragma unroll
-          for (int j = 0; j < XW; ++j) {
-            const int iw = iw0 + j;
-            xv[j] = (row_ok && (unsigned)iw < (unsigned)g.W) ? __ldg(xr + iw * sww) : 0.0f;
+            for (int j = 0; j < XW4; ++j) {
+              float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
+              if (row_ok) t = __ldg(reinterpret_cast<const float4*>(xr + iw0) + j);
+              xv[4 * j] = t.x;
+              xv[4 * j + 1] = t.y;
+              xv[4 * j + 2] = t.z;
+              xv[4 * j + 3] = t.w;
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < XW; ++j) {
+              const int iw = iw0 + j;
+              xv[j] = (row_ok && (unsigned)iw < (unsigned)g.W) ? __ldg(xr + iw * sww) : 0.0f;
+            }
           }
 #pragma unroll
           for (int kw = 0; kw < KW; ++kw)
@@ -2018,7 +2038,27 @@ __global__ void __launch_bounds__(128, 5) conv_direct_row_kernel(ConvArgs g,
     const int total = (int)(m1 - m0) * g.Cout;
     float* dst = g.out + m0 * g.Cout;
     const float* res = add ? g.residual + m0 * g.Cout : nullptr;
-    for (int i = threadIdx.x; i < total; i += blockDim.x) {
+    int i0 = 0;
+    if ((((uintptr_t)dst | (uintptr_t)res) & 15) == 0) {  // 16-byte runs, scalar tail
+      const int n4 = total >> 2;
+      for (int i = threadIdx.x; i < n4; i += blockDim.x) {
+        float4 o = reinterpret_cast<const float4*>(obuf)[i];
+        if (add) {
+          const float4 r = __ldg(reinterpret_cast<const float4*>(res) + i);
+          o.x = __fadd_rn(o.x, r.x);
+          o.y = __fadd_rn(o.y, r.y);
+          o.z = __fadd_rn(o.z, r.z);
+          o.w = __fadd_rn(o.w, r.w);
+        }
+        o.x = activate(o.x, g.act);
+        o.y = activate(o.y, g.act);
+        o.z = activate(o.z, g.act);
+        o.w = activate(o.w, g.act);
+        reinterpret_cast<float4*>(dst)[i] = o;
+      }
+      i0 = n4 << 2;
+    }
+    for (int i = i0 + threadIdx.x; i < total; i += blockDim.x) {
       float o = obuf[i];
       if (add) o = __fadd_rn(o, __ldg(res + i));
       dst[i] = activate(o, g.act);
