@@ -64,6 +64,97 @@ struct GemmCfg {
       (size_t)STAGES * STAGE_BYTES + STAGING_BYTES + 1024 /*align*/ + 256 /*bars*/;
 };
 
+// Epilogue of one accumulator tile for one warp: TMEM lanes [32 quad, +32)
+// hold rows row0 .. row0 + 31 of batch b; columns nt * BN + [0, BN) in
+// 32-column slices: alpha, beta * C, relu, then a TMA store of a 32 x 32
+// shared box (tma_store; two boxes at box0, alternated through bsel) or
+// per-thread row stores.
+template <int BN>
+__device__ __forceinline__ void store_slices(const GemmArgs& g, const CUtensorMap* tmD,
+                                             uint32_t tmem_base, int acc, int quad, int lane,
+                                             int row0, int nt, int b, float* box0, int& bsel,
+                                             bool vec_ok) {
+  const int row = row0 + lane;
+  float* drow = g.D + (int64_t)b * g.d_batch_stride + (int64_t)row * g.ldd;
+  const float* crow = nullptr;
+  if (g.c_mode == 2) crow = g.C + (int64_t)b * g.c_batch_stride + (int64_t)row * g.ldc;
+#pragma unroll 1
+  for (int c0 = 0; c0 < BN; c0 += 32) {
+    const int n0 = nt * BN + c0;
+    if (n0 >= g.N) break;  // warp-uniform
+    uint32_t r[32];
+    __syncwarp();  // tcgen05.ld is .sync.aligned: the warp must be converged
+    const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN + c0;
+    tc::tmem_ld16(taddr, *reinterpret_cast<uint32_t(*)[16]>(&r[0]));
+    tc::tmem_ld16(taddr + 16, *reinterpret_cast<uint32_t(*)[16]>(&r[16]));
+    tc::tmem_ld_wait();
+    // The modes are tested once per slice, outside the element loops: a
+    // per-element test of c_mode with its guarded loads cost ~2,900
+    // cycles per 32-column slice (measured), 30x the TMEM load.
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = g.alpha * __uint_as_float(r[j]);
+    if (g.c_mode == 1) {  // C[n], the same 32 values for every lane (broadcast loads)
+      const float* cb = g.C + n0;
+      if (n0 + 32 <= g.N && ((uintptr_t)cb & 15) == 0) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float4 c4 = __ldg(reinterpret_cast<const float4*>(cb) + j);
+          v[4 * j] = fmaf(g.beta, c4.x, v[4 * j]);
+          v[4 * j + 1] = fmaf(g.beta, c4.y, v[4 * j + 1]);
+          v[4 * j + 2] = fmaf(g.beta, c4.z, v[4 * j + 2]);
+          v[4 * j + 3] = fmaf(g.beta, c4.w, v[4 * j + 3]);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (n0 + j < g.N) v[j] = fmaf(g.beta, __ldg(cb + j), v[j]);
+      }
+    } else if (g.c_mode == 2 && row < g.M) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (n0 + j < g.N) v[j] = fmaf(g.beta, crow[n0 + j], v[j]);
+    }
+    if (g.relu) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = v[j] > 0.0f ? v[j] : 0.0f;
+    }
+    if (g.tma_store) {
+      if (row0 >= g.M) continue;  // warp-uniform: the whole box lies below M
+      float* box = box0 + bsel * 1024;
+      if (lane == 0) tc::bulk_wait_group_read<1>();  // the store 2 slices ago read `box`
+      __syncwarp();
+      float4* brow = reinterpret_cast<float4*>(box + lane * 32);
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        brow[j ^ (lane & 7)] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+      tc::fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        tc::tma_store_3d(tmD, box, n0, row0, b);
+        tc::bulk_commit_group();
+      }
+      bsel ^= 1;
+    } else if (row < g.M) {
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int nh = n0 + 16 * h;
+        if (vec_ok && nh + 16 <= g.N) {
+          float4* d4 = reinterpret_cast<float4*>(drow + nh);
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            d4[j] = make_float4(v[16 * h + 4 * j], v[16 * h + 4 * j + 1],
+                                v[16 * h + 4 * j + 2], v[16 * h + 4 * j + 3]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            if (nh + j < g.N) drow[nh + j] = v[16 * h + j];
+        }
+      }
+    }
+  }
+}
+
 template <int BN, int SPLIT, int STAGES>
 __global__ void __launch_bounds__(kTCThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmA1,
@@ -228,86 +319,8 @@ __global__ void __launch_bounds__(kTCThreads, 1)
       const uint32_t aphase = (local >> 1) & 1;
       if (!tc::mbar_wait(&tfull[acc], aphase, g.err)) break;
       tc::tc_fence_after();
-      const int row0 = mt * BM + quad * 32;
-      const int row = row0 + lane;
-      float* drow = g.D + (int64_t)b * g.d_batch_stride + (int64_t)row * g.ldd;
-      const float* crow = nullptr;
-      if (g.c_mode == 2) crow = g.C + (int64_t)b * g.c_batch_stride + (int64_t)row * g.ldc;
-#pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 32) {
-        const int n0 = nt * BN + c0;
-        if (n0 >= g.N) break;  // warp-uniform
-        uint32_t r[32];
-        __syncwarp();  // tcgen05.ld is .sync.aligned: the warp must be converged
-        const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN + c0;
-        tc::tmem_ld16(taddr, *reinterpret_cast<uint32_t(*)[16]>(&r[0]));
-        tc::tmem_ld16(taddr + 16, *reinterpret_cast<uint32_t(*)[16]>(&r[16]));
-        tc::tmem_ld_wait();
-        // The modes are tested once per slice, outside the element loops: a
-        // per-element test of c_mode with its guarded loads cost ~2,900
-        // cycles per 32-column slice (measured), 30x the TMEM load.
-        float v[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = g.alpha * __uint_as_float(r[j]);
-        if (g.c_mode == 1) {  // C[n], the same 32 values for every lane (broadcast loads)
-          const float* cb = g.C + n0;
-          if (n0 + 32 <= g.N && ((uintptr_t)cb & 15) == 0) {
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              const float4 c4 = __ldg(reinterpret_cast<const float4*>(cb) + j);
-              v[4 * j] = fmaf(g.beta, c4.x, v[4 * j]);
-              v[4 * j + 1] = fmaf(g.beta, c4.y, v[4 * j + 1]);
-              v[4 * j + 2] = fmaf(g.beta, c4.z, v[4 * j + 2]);
-              v[4 * j + 3] = fmaf(g.beta, c4.w, v[4 * j + 3]);
-            }
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (n0 + j < g.N) v[j] = fmaf(g.beta, __ldg(cb + j), v[j]);
-          }
-        } else if (g.c_mode == 2 && row < g.M) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (n0 + j < g.N) v[j] = fmaf(g.beta, crow[n0 + j], v[j]);
-        }
-        if (g.relu) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = v[j] > 0.0f ? v[j] : 0.0f;
-        }
-        if (g.tma_store) {
-          if (row0 >= g.M) continue;  // warp-uniform: the whole box lies below M
-          float* box = box0 + bsel * 1024;
-          if (lane == 0) tc::bulk_wait_group_read<1>();  // the store 2 slices ago read `box`
-          __syncwarp();
-          float4* brow = reinterpret_cast<float4*>(box + lane * 32);
-#pragma unroll
-          for (int j = 0; j < 8; ++j)
-            brow[j ^ (lane & 7)] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-          tc::fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) {
-            tc::tma_store_3d(&tmD, box, n0, row0, b);
-            tc::bulk_commit_group();
-          }
-          bsel ^= 1;
-        } else if (row < g.M) {
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const int nh = n0 + 16 * h;
-            if (vec_ok && nh + 16 <= g.N) {
-              float4* d4 = reinterpret_cast<float4*>(drow + nh);
-#pragma unroll
-              for (int j = 0; j < 4; ++j)
-                d4[j] = make_float4(v[16 * h + 4 * j], v[16 * h + 4 * j + 1],
-                                    v[16 * h + 4 * j + 2], v[16 * h + 4 * j + 3]);
-            } else {
-#pragma unroll
-              for (int j = 0; j < 16; ++j)
-                if (nh + j < g.N) drow[nh + j] = v[16 * h + j];
-            }
-          }
-        }
-      }
+      store_slices<BN>(g, &tmD, tmem_base, acc, quad, lane, mt * BM + quad * 32, nt, b, box0, bsel,
+                       vec_ok);
       tc::tc_fence_before();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&tempty[acc]);
@@ -496,63 +509,8 @@ __global__ void __launch_bounds__(kTCThreads, 1)
       const uint32_t aphase = (local >> 1) & 1;
       if (!tc::mbar_wait(&tfull[acc], aphase, g.err)) break;
       tc::tc_fence_after();
-      const int row0 = mt * (2 * BM) + (int)rank * BM + quad * 32;
-#pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 32) {
-        const int n0 = nt * BN + c0;
-        if (n0 >= g.N) break;  // warp-uniform
-        uint32_t r[32];
-        __syncwarp();
-        const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN + c0;
-        tc::tmem_ld16(taddr, *reinterpret_cast<uint32_t(*)[16]>(&r[0]));
-        tc::tmem_ld16(taddr + 16, *reinterpret_cast<uint32_t(*)[16]>(&r[16]));
-        tc::tmem_ld_wait();
-        if (row0 >= g.M) continue;  // warp-uniform: the whole box lies below M
-        float v[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = g.alpha * __uint_as_float(r[j]);
-        if (g.c_mode == 1) {
-          const float* cb = g.C + n0;
-          if (n0 + 32 <= g.N && ((uintptr_t)cb & 15) == 0) {
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              const float4 c4 = __ldg(reinterpret_cast<const float4*>(cb) + j);
-              v[4 * j] = fmaf(g.beta, c4.x, v[4 * j]);
-              v[4 * j + 1] = fmaf(g.beta, c4.y, v[4 * j + 1]);
-              v[4 * j + 2] = fmaf(g.beta, c4.z, v[4 * j + 2]);
-              v[4 * j + 3] = fmaf(g.beta, c4.w, v[4 * j + 3]);
-            }
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (n0 + j < g.N) v[j] = fmaf(g.beta, __ldg(cb + j), v[j]);
-          }
-        } else if (g.c_mode == 2 && row0 + lane < g.M) {
-          const float* crow =
-              g.C + (int64_t)b * g.c_batch_stride + (int64_t)(row0 + lane) * g.ldc;
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (n0 + j < g.N) v[j] = fmaf(g.beta, crow[n0 + j], v[j]);
-        }
-        if (g.relu) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = v[j] > 0.0f ? v[j] : 0.0f;
-        }
-        float* box = box0 + bsel * 1024;
-        if (lane == 0) tc::bulk_wait_group_read<1>();
-        __syncwarp();
-        float4* brow = reinterpret_cast<float4*>(box + lane * 32);
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-          brow[j ^ (lane & 7)] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-        tc::fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          tc::tma_store_3d(&tmD, box, n0, row0, b);
-          tc::bulk_commit_group();
-        }
-        bsel ^= 1;
-      }
+      store_slices<BN>(g, &tmD, tmem_base, acc, quad, lane, mt * (2 * BM) + (int)rank * BM + quad * 32,
+                       nt, b, box0, bsel, true);
       tc::tc_fence_before();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive_cluster(tempty0 + acc * (uint32_t)sizeof(uint64_t));

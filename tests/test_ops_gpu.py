@@ -176,13 +176,17 @@ def test_matmul_layouts_vs_oracle(cuda_lib, prec, cfg):
     C.assert_close(got, want, C.TC_RTOL[prec], f"{kind}{sa}x{sb}")
 
 
-# TF32 problems large enough for the CTA-pair GEMM kernel (N > 128, M >= 256,
-# at least ~64 tiles of 256 x 256): [K, N] B read MN-major and [N, K] B
-# K-major, the reference's batch offsets, ragged M / N / K, C matrix with
-# alpha / beta, relu.
+# Large TF32 problems: the CTA-pair GEMM kernel (N > 128, M >= 256, at least
+# ~64 tiles of 256 x 256) with [K, N] B read MN-major and [N, K] B K-major,
+# the reference's batch offsets, ragged M / N / K, C matrix with alpha /
+# beta, relu; then many-tile short-K problems.
 PAIR_GEMM_CASES = [
     ("mm", (2048, 128), (128, 2048)), ("mm", (64, 256, 96), (64, 96, 264)),
     ("gemm01", (4100, 36), (1032, 36)), ("gemm00_relu", (1300, 64), (64, 3000)),
+    # Short K against one B over many tiles (single-CTA kernel): batched A
+    # with a shared [K, N] B, and a K-major B with a ragged k-block and a row
+    # bias.
+    ("mm", (300, 128, 64), (64, 136)), ("gemmnt_bias", (19000, 100), (260, 100)),
 ]
 
 
@@ -194,6 +198,11 @@ def test_gemm_cta_pairs_vs_oracle(cuda_lib, cfg):
     if kind == "mm":
         so = sa[:-1] + sb[-1:]
         case = {"name": "m", "op": "nnc_matmul", "args": [C._t("a"), C._t("b"), C._o("out", so)]}
+    elif kind == "gemmnt_bias":
+        M, N = sa[0], sb[0]
+        arrays["c"] = r.standard_normal((N,)).astype(np.float32)
+        case = {"name": "g", "op": "nnc_gemm_nt", "args": [C._t("a"), C._t("b"), C._t("c"), C._o("out", (M, N)),
+                                                           C._f(1.0), C._f(1.0)]}
     else:
         tb = int(kind[5])
         M, N = sa[0], (sb[0] if tb else sb[1])
