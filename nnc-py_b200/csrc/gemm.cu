@@ -45,6 +45,8 @@ struct GemmArgs {
   int relu;
   int tma_store;  // 1: D written by TMA stores through tmD (dense, 16-byte rows)
   int b_mn;       // 1: B tiles are MN-major ({32 n, 32 k} boxes of a [K, N] matrix)
+  int pair_b;     // CTA pairs only: 1 = the two CTAs take consecutive batches (M <= 128)
+  int batches;
   int* err;
 };
 
@@ -414,9 +416,13 @@ __global__ void __launch_bounds__(kTCThreads, 1)
       uint32_t phase = 0;
       bool ok = true;
       for (int64_t t = cluster; t < g.tiles && ok; t += clusters) {
-        const int b = (int)(t / per_b);
-        const int mt = (int)((t % per_b) / g.n_tiles), nt = (int)((t % per_b) % g.n_tiles);
-        const int row0 = mt * (2 * BM) + (int)rank * BM;
+        // Pair tile: 256 rows of one batch, or (pair_b) rows 0..127 of
+        // batches 2 j and 2 j + 1, one per CTA (a batch past the last is
+        // read as zeros and not stored).
+        const int b = g.pair_b ? (int)(t / g.n_tiles) * 2 + (int)rank : (int)(t / per_b);
+        const int mt = g.pair_b ? 0 : (int)((t % per_b) / g.n_tiles);
+        const int nt = (int)((g.pair_b ? t : t % per_b) % g.n_tiles);
+        const int row0 = g.pair_b ? 0 : mt * (2 * BM) + (int)rank * BM;
         const int n_half = nt * BN + (int)rank * (BN / 2);
         for (int kb = 0; kb < kblocks; ++kb) {
           if (!tc::mbar_wait(&empty[stage], phase ^ 1, g.err)) {
@@ -503,14 +509,17 @@ __global__ void __launch_bounds__(kTCThreads, 1)
     const uint32_t tempty0 = tc::mapa(tc::smem_u32(&tempty[0]), 0);
     int local = 0;
     for (int64_t t = cluster; t < g.tiles; t += clusters, ++local) {
-      const int b = (int)(t / per_b);
-      const int mt = (int)((t % per_b) / g.n_tiles), nt = (int)((t % per_b) % g.n_tiles);
+      const int b = g.pair_b ? (int)(t / g.n_tiles) * 2 + (int)rank : (int)(t / per_b);
+      const int mt = g.pair_b ? 0 : (int)((t % per_b) / g.n_tiles);
+      const int nt = (int)((g.pair_b ? t : t % per_b) % g.n_tiles);
       const int acc = local & 1;
       const uint32_t aphase = (local >> 1) & 1;
       if (!tc::mbar_wait(&tfull[acc], aphase, g.err)) break;
       tc::tc_fence_after();
-      store_slices<BN>(g, &tmD, tmem_base, acc, quad, lane, mt * (2 * BM) + (int)rank * BM + quad * 32,
-                       nt, b, box0, bsel, true);
+      const int row0 = g.pair_b ? quad * 32 : mt * (2 * BM) + (int)rank * BM + quad * 32;
+      // (a missing last batch still takes part: its TMEM loads are warp-wide)
+      store_slices<BN>(g, &tmD, tmem_base, acc, quad, lane, b < g.batches ? row0 : g.M, nt, b, box0,
+                       bsel, true);
       tc::tc_fence_before();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive_cluster(tempty0 + acc * (uint32_t)sizeof(uint64_t));
@@ -670,6 +679,8 @@ bool launch_tc(const Problem& p, const float* A0, const float* A1, const float* 
   g.ldd = p.N;
   g.d_batch_stride = p.d_bs;
   g.relu = p.relu;
+  g.pair_b = 0;
+  g.batches = p.batches;
   g.tma_store = tma_store ? 1 : 0;
   g.b_mn = mn ? 1 : 0;
   g.err = device_error_word();
@@ -691,7 +702,8 @@ bool launch_tc(const Problem& p, const float* A0, const float* A1, const float* 
 
 // CTA-pair launch (TF32, D written by TMA stores): see gemm_tc2_kernel.
 template <int BN, int STAGES>
-bool launch_tc2(const Problem& p, const float* A, const float* B, const char* op) {
+bool launch_tc2(const Problem& p, const float* A, const float* B, const char* op,
+                bool pair_batches = false) {
   using Cfg = GemmPairCfg<BN, STAGES>;
   CUtensorMap ta, tb, td;
   const uint64_t a_dims[3] = {(uint64_t)p.K, (uint64_t)p.M, (uint64_t)(p.a_bs ? p.batches : 1)};
@@ -715,9 +727,11 @@ bool launch_tc2(const Problem& p, const float* A, const float* B, const char* op
   g.M = p.M;
   g.N = p.N;
   g.K = p.K;
-  g.m_tiles = (int)cdiv(p.M, 2 * BM);
+  g.pair_b = pair_batches ? 1 : 0;
+  g.batches = p.batches;
+  g.m_tiles = pair_batches ? 1 : (int)cdiv(p.M, 2 * BM);
   g.n_tiles = (int)cdiv(p.N, BN);
-  g.tiles = (int64_t)p.batches * g.m_tiles * g.n_tiles;
+  g.tiles = (pair_batches ? (int64_t)(p.batches + 1) / 2 : (int64_t)p.batches * g.m_tiles) * g.n_tiles;
   g.a_batched = p.a_bs ? 1 : 0;
   g.b_batched = p.b_bs ? 1 : 0;
   g.alpha = p.alpha;
@@ -870,6 +884,13 @@ void run_problem(Problem p, const char* op) {
     if (gemm_pair_enabled() && d_tma && p.N > 128 && p.M >= 2 * BM &&
         (int64_t)cdiv(p.M, 2 * BM) * cdiv(p.N, 256) * p.batches >= sm_count() / 2 - 10) {
       launch_tc2<256, 6>(p, A, B, op);
+      return;
+    }
+    // Batched A of at most 128 rows per batch against one B: each pair takes
+    // two consecutive batches (one per CTA) and splits B's tile between them.
+    if (gemm_pair_enabled() && d_tma && p.N > 128 && p.M <= BM && p.a_bs != 0 && p.b_bs == 0 &&
+        p.batches >= 2 && (int64_t)(p.batches + 1) / 2 * cdiv(p.N, 256) >= sm_count() / 2 - 10) {
+      launch_tc2<256, 6>(p, A, B, op, true);
       return;
     }
     if (p.N > 128 && (int64_t)cdiv(p.M, BM) * cdiv(p.N, 256) * p.batches >= sm_count())

@@ -187,6 +187,9 @@ PAIR_GEMM_CASES = [
     # with a shared [K, N] B, and a K-major B with a ragged k-block and a row
     # bias.
     ("mm", (300, 128, 64), (64, 136)), ("gemmnt_bias", (19000, 100), (260, 100)),
+    # Batches of at most 128 rows against one B on CTA pairs, one batch per
+    # CTA (the reference's overlapping batch offsets; ragged M and N).
+    ("mm", (132, 100, 64), (64, 264)), ("mm", (128, 128, 32), (32, 384)),
 ]
 
 
