@@ -154,6 +154,60 @@ __global__ void __launch_bounds__(256) pool_nhwc_kernel(const float* __restrict_
   }
 }
 
+// Channels-last with few channels (C even, at most 8; LeNet's 6): one thread
+// per output pixel takes all its channels as float2 pairs, so the index
+// arithmetic is paid once per pixel instead of once per pair. Same window
+// order and tie rules as pool_nhwc_kernel.
+template <bool MAX>
+__global__ void __launch_bounds__(256) pool_nhwc_pixel_kernel(const float* __restrict__ in,
+                                                              float* __restrict__ out, PoolGeom g) {
+  const int pairs = g.C / 2;
+  const int total = g.N * g.OH * g.OW;  // host: fits 32 bits
+  for (int p = blockIdx.x * blockDim.x + threadIdx.x; p < total; p += gridDim.x * blockDim.x) {
+    const int ow = p % g.OW;
+    const int q = p / g.OW;
+    const int oh = q % g.OH;
+    const int n = q / g.OH;
+    int h0, h1, w0, w1;
+    window(g, oh, ow, h0, h1, w0, w1);
+    const float* img = in + (int64_t)n * g.H * g.W * g.C;
+    float2 acc[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[j] = MAX ? make_float2(kEmptyMax, kEmptyMax) : make_float2(0.f, 0.f);
+    bool has = false;
+    int cnt = 0;
+    for (int h = h0; h < h1; ++h)
+      for (int w = w0; w < w1; ++w) {
+        const float2* src = reinterpret_cast<const float2*>(img + (h * g.W + w) * g.C);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          if (j >= pairs) break;
+          const float2 v = __ldg(src + j);
+          if (MAX) {
+            if (!has || v.x > acc[j].x) acc[j].x = v.x;
+            if (!has || v.y > acc[j].y) acc[j].y = v.y;
+          } else {
+            acc[j].x = __fadd_rn(acc[j].x, v.x);
+            acc[j].y = __fadd_rn(acc[j].y, v.y);
+          }
+        }
+        has = true;
+        ++cnt;
+      }
+    float2* dst = reinterpret_cast<float2*>(out + (int64_t)p * g.C);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (j >= pairs) break;
+      float2 o = acc[j];
+      if (!MAX) {
+        o.x = cnt > 0 ? __fdiv_rn(o.x, (float)cnt) : 0.0f;
+        o.y = cnt > 0 ? __fdiv_rn(o.y, (float)cnt) : 0.0f;
+      }
+      dst[j] = o;
+    }
+  }
+}
+
 template <bool MAX>
 void launch_pool(const float* pi, float* po, const PoolGeom& g, bool nhwc) {
   const int64_t total = (int64_t)g.N * g.C * g.OH * g.OW;
@@ -180,6 +234,8 @@ void launch_pool(const float* pi, float* po, const PoolGeom& g, bool nhwc) {
       pool_nhwc_kernel<MAX, 4, int><<<grid, 256, 0, st>>>(pi, po, g);
     else
       pool_nhwc_kernel<MAX, 4, int64_t><<<grid, 256, 0, st>>>(pi, po, g);
+  } else if (g.C % 2 == 0 && g.C <= 8 && small && (((uintptr_t)pi | (uintptr_t)po) & 7) == 0) {
+    pool_nhwc_pixel_kernel<MAX><<<grid_for(total / g.C, 256, 8), 256, 0, st>>>(pi, po, g);
   } else if (g.C % 2 == 0 && (((uintptr_t)pi | (uintptr_t)po) & 7) == 0) {
     const int grid = grid_for(total / 2, 256, 8);
     if (small)
