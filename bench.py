@@ -8,16 +8,30 @@
 Our arm: every rank loads nnc-py_b200/models_gen/resnet18_o3_b<1024/N>
 (libmodel.so over libnnc_cuda.so), uploads the seeded weights, and runs
 its shard of the seeded input. A step = one forward of the whole global
-batch; ranks add an NCCL gather of the logits to rank 0 when N > 1 (the
-config's output gather). Timing: W untimed warm-up steps, then K steps
+batch; when N > 1 the ranks then gather the logits to rank 0 (NCCL gather,
+the config's output gather). Timing: W untimed warm-up steps, then K steps
 bracketed by barrier + synchronize, CUDA events on the launching stream,
 max over ranks. Inputs (616 MB) exceed the 126 MB L2, so no flush is
 needed. `e2e` repeats the measurement through the model's host-buffer path:
 every step copies its input shard from pinned host memory and reads the
 logits back, the copy of step i+1 overlapping the compute of step i (two
-device staging buffers, a second stream). `roofline` covers the dominant kernel (the tcgen05 implicit-GEMM
-conv): algorithmic conv FLOPs per step / conv device time, both measured
-live in the timed region with per-call CUDA events.
+device staging buffers, a second stream).
+
+`roofline` covers the dominant kernels (the tcgen05 implicit-GEMM convs):
+algorithmic conv FLOPs per step / conv device time per step. The forward is
+captured once into a CUDA graph with tracing on, so the graph holds two
+event-record nodes around every library call; each timed replay re-binds
+them to fresh events (nnc_cuda_graph_launch), and the conv time is the sum
+over the conv calls' event pairs of all K timed replays, divided by K. The
+peak is dense TF32 = bf16 / 2 from MEASURED_PEAKS.json: the burst figure
+when the SM clock sampled during the timed region stayed at its maximum,
+the sustained one when the power cap lowered it (tf32_peak).
+
+`parity` compares, on rank 0 after the timed region, the logits of the
+last step (gathered over all ranks) at the 32 indices of
+tests/golden/bench_resnet18_o3.npz with the reference's own -O3 x86 build
+of the same graph on the same seeded images (normwise, see
+tests/opcases.assert_close).
 
 Reference arm: rank 0 runs the reference's own x86 build of the same graph
 (nnc-py X86Backend, legacy -O3 pass list, runtime/x86/ops.c, gcc -O3; see
@@ -55,6 +69,47 @@ def peaks():
                 "bf16_tflops_sustained": d.get("bf16_tflops_sustained"), "source": "measured"}
     # Fallback figures of this pool (burst 1.59 PFLOP/s; ~1.4 sustained under the power cap).
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+def tf32_peak(pk: dict, clocks: dict | None) -> tuple[float, str]:
+    """Dense TF32 peak (TFLOP/s) for a kernel timed under `clocks` (the
+    sampler's record; None for a kernel timed alone in short bursts): half the
+    burst bf16 figure when the median SM clock under load stayed within 3% of
+    its maximum, else half the sustained (power-capped) figure."""
+    burst = pk["bf16_tflops"] / 2.0
+    sustained = (pk.get("bf16_tflops_sustained") or pk["bf16_tflops"]) / 2.0
+    if clocks is None:
+        return burst, f"burst bf16/2 of {pk['source']} MEASURED_PEAKS.json (timed alone)"
+    sm, mx = clocks.get("sm_mhz"), clocks.get("sm_max_mhz")
+    if sm and mx and sm >= 0.97 * mx:
+        return burst, f"burst bf16/2 of {pk['source']} MEASURED_PEAKS.json (median SM clock {sm:.0f} of max {mx:.0f} MHz)"
+    return sustained, (f"sustained bf16/2 of {pk['source']} MEASURED_PEAKS.json "
+                       f"(median SM clock {sm} of max {mx} MHz)")
+
+
+GOLDEN = ROOT / "tests" / "golden" / "bench_resnet18_o3.npz"
+# Normwise tolerance of whole-model logits against the reference's x86 build.
+PARITY_RTOL = {"tf32": 2e-2, "3xtf32": 1e-4}
+
+
+def parity(logits, precision: str) -> dict:
+    """Logits of the whole global batch (numpy [1024, 1000]) at the golden
+    indices against the reference's -O3 x86 build."""
+    import numpy as np
+
+    if not GOLDEN.exists():
+        return {"checked": 0, "ok": None, "why": "golden fixture missing"}
+    z = np.load(GOLDEN)
+    idx, want = z["indices"], z["logits"].astype(np.float64)
+    got = logits[idx].astype(np.float64)
+    scale = float(np.max(np.abs(want)))
+    err = float(np.max(np.abs(got - want) / (np.abs(want) + scale)))
+    rtol = PARITY_RTOL[precision]
+    return {"checked": int(len(idx)), "indices": "first/last of every 128-image shard + 16 seeded",
+            "max_normwise_err": float(f"{err:.3g}"), "rtol": rtol,
+            "argmax_agree": int(np.sum(got.argmax(1) == want.argmax(1))),
+            "reference": "nnc-py X86Backend legacy -O3 build of the same graph (tests/golden/make_bench_golden.py)",
+            "ok": bool(err <= rtol)}
 
 
 class ClockSampler:
@@ -248,8 +303,9 @@ def our_arm(opt):
     assert count == B
     x_host = torch.from_numpy(wl.input_array(B, offset=first)).pin_memory()
     logits_host = torch.empty((B, 1000), dtype=torch.float32).pin_memory()
-    gathered = torch.empty((GLOBAL_BATCH, 1000), dtype=torch.float32, device="cuda") if world > 1 else None
+    gathered = torch.empty((GLOBAL_BATCH, 1000), dtype=torch.float32, device="cuda") if rank == 0 else None
     mine = torch.empty((B, 1000), dtype=torch.float32, device="cuda") if world > 1 else None
+    parts = list(gathered.split(B)) if (world > 1 and rank == 0) else None
     in_bytes, out_bytes = B * IMG_BYTES, B * LOGIT_BYTES
 
     def h2d():
@@ -260,10 +316,11 @@ def our_arm(opt):
                                  out_bytes, 2)
 
     def gather():
+        # The logits of every shard to rank 0 (shards in rank order).
         if world > 1:
             rt.nnc_cuda_memcpy_async(ctypes.c_void_p(mine.data_ptr()), ctypes.c_void_p(model.output_ptr()), out_bytes, 3)
             with torch.cuda.stream(stream):
-                dist.all_gather_into_tensor(gathered, mine)
+                dist.gather(mine, parts, dst=0)
 
     def barrier():
         torch.cuda.synchronize()
@@ -285,11 +342,16 @@ def our_arm(opt):
     # ---- device-resident timing (value) ----
     sampler = ClockSampler(local) if rank == 0 else None
     # One step's library calls (the forward pass) captured once into a CUDA
-    # graph; every timed step replays it (the same kernels, one launch).
+    # graph, with tracing on so that every call sits between two event-record
+    # nodes; every timed step replays it (the same kernels, one launch) and
+    # logs the calls' device times.
+    rt.nnc_cuda_trace_clear()
+    rt.nnc_cuda_trace_enable(1)
     model.capture()
     with torch.cuda.stream(stream):
         model.replay()  # untimed first replay (graph upload)
     barrier()
+    rt.nnc_cuda_trace_clear()
     if sampler:
         sampler.start()
     launches0 = rt.nnc_cuda_launch_count()
@@ -307,23 +369,23 @@ def our_arm(opt):
     clocks = sampler.stop() if sampler else None
     ms_max = max_over_ranks(ms)
 
-    # Per-operator device times: the same calls run uncaptured with the
-    # library's per-call CUDA events (a separate, untimed pass).
-    trace_steps = min(opt.steps, 5)
-    rt.nnc_cuda_trace_clear()
-    rt.nnc_cuda_trace_enable(1)
-    with torch.cuda.stream(stream):
-        for _ in range(trace_steps):
-            model.run()
-    rt.nnc_cuda_trace_enable(0)
+    # Per-operator device times of the timed replays (the graph's event
+    # pairs, K replays).
     n = rt.nnc_cuda_trace_count()
-    conv_us = sum(rt.nnc_cuda_trace_us(i) for i in range(n) if rt.nnc_cuda_trace_name(i).startswith(b"nnc_conv"))
+    rt.nnc_cuda_trace_enable(0)
     op_us = {}
     for i in range(n):
         nm = rt.nnc_cuda_trace_name(i).decode()
-        op_us[nm] = op_us.get(nm, 0.0) + rt.nnc_cuda_trace_us(i)
+        us = rt.nnc_cuda_trace_us(i)
+        if us < 0:
+            raise RuntimeError(f"trace entry {i} ({nm}) has no device time")
+        op_us[nm] = op_us.get(nm, 0.0) + us
     rt.nnc_cuda_trace_clear()
-    conv_ms_step = max_over_ranks(conv_us / 1e3 / trace_steps)
+    traced_steps = opt.steps
+    conv_us = sum(v for k, v in op_us.items() if k.startswith("nnc_conv"))
+    conv_ms_step = max_over_ranks(conv_us / 1e3 / traced_steps)
+    if conv_ms_step > ms_max / opt.steps * 1.001:
+        raise RuntimeError(f"conv time {conv_ms_step:.4f} ms exceeds the step ({ms_max / opt.steps:.4f} ms)")
 
     # ---- end-to-end through host buffers (e2e) ----
     # Every step copies its input shard from pinned host memory and reads its
@@ -371,15 +433,20 @@ def our_arm(opt):
     if rt.nnc_cuda_get_last_error() != 0 or rt.nnc_cuda_check_device_status() != 0:
         raise RuntimeError(rt.nnc_cuda_get_last_error_string().decode())
 
+    # Parity of the last step's logits (all shards) on rank 0.
+    par = None
+    if rank == 0:
+        if world == 1:
+            rt.nnc_cuda_memcpy_async(ctypes.c_void_p(gathered.data_ptr()), ctypes.c_void_p(model.output_ptr()),
+                                     out_bytes, 3)
+            torch.cuda.synchronize()
+        par = parity(gathered.cpu().numpy(), opt.precision)
+
     line = None
     if rank == 0:
         pk = peaks()
-        # The convs run back to back for the whole step under the 1 kW power
-        # cap: the sustained bf16 figure is the comparable one (its TF32 rate
-        # is half).
-        sustained = pk.get("bf16_tflops_sustained")
-        tf32_peak = (sustained or pk["bf16_tflops"]) / 2.0
-        peak = tf32_peak / (3.0 if prec == L.PRECISION_3XTF32 else 1.0)
+        base_peak, peak_note = tf32_peak(pk, clocks)
+        peak = base_peak / (3.0 if prec == L.PRECISION_3XTF32 else 1.0)
         cflops = conv_flops(wl)  # per rank per step
         achieved = cflops / (conv_ms_step * 1e-3) / 1e12 if conv_ms_step > 0 else None
         value = opt.steps * GLOBAL_BATCH / (ms_max * 1e-3)
@@ -392,7 +459,7 @@ def our_arm(opt):
             "config": {"workload": "resnet18 fp32 224x224, nnc -O3 cuda target (conv+relu, conv+add+relu fused), "
                                    f"global batch {GLOBAL_BATCH} split over {world} GPU(s)",
                        "model": "resnet18", "global_batch": GLOBAL_BATCH, "per_gpu_batch": B, "seq_len": None,
-                       "parallelism": f"dp{world} (batch shards, logits gathered to rank 0)" if world > 1 else "single GPU",
+                       "parallelism": f"dp{world} (batch shards, logits gathered to rank 0 by NCCL gather)" if world > 1 else "single GPU",
                        "precision": opt.precision, "l2": "inputs (616 MB/step) larger than L2; no flush",
                        "launch": "one CUDA graph replay per step (the captured forward pass)"},
             "roofline": {"bound": "tensor", "kernel": "conv kernels (conv_halo_kernel, conv_tc2_kernel CTA pairs, conv_tc_kernel; tcgen05 implicit GEMM)",
@@ -401,18 +468,20 @@ def our_arm(opt):
                          "traffic": roofline_traffic(B),
                          "traffic_scope": "DRAM bytes per step over all conv launches (ncu, scaled per image)",
                          "algorithmic_bytes": round(conv_bytes(wl)),
-                         "peak_note": f"dense TF32 = {'sustained' if sustained else 'burst'} bf16/2 of "
-                                      f"{pk['source']} MEASURED_PEAKS.json"
+                         "peak_note": "dense TF32 = " + peak_note
                                       + (", /3 for the 3 MMAs of 3xTF32" if prec == L.PRECISION_3XTF32 else ""),
                          "conv_ms_per_step": round(conv_ms_step, 4),
+                         "conv_time_source": f"event-record nodes around each conv call inside the replayed graph, "
+                                             f"{traced_steps} timed replays",
                          "conv_gflop_per_step_per_gpu": round(cflops / 1e9, 1)},
             "e2e": {"value": round(opt.steps * GLOBAL_BATCH / (e2e_ms * 1e-3), 2), "unit": "images/s",
                     "h2d_bytes_per_step": GLOBAL_BATCH * IMG_BYTES, "d2h_bytes_per_step": GLOBAL_BATCH * LOGIT_BYTES,
                     "pipeline": "step i+1's host-to-device input copy overlaps step i's compute (two staging buffers)"},
             "gpu_launches": int(launches),
             "clocks": clocks,
-            "op_ms_per_step": {k: round(v / 1e3 / trace_steps, 4)
+            "op_ms_per_step": {k: round(v / 1e3 / traced_steps, 4)
                                for k, v in sorted(op_us.items(), key=lambda kv: -kv[1])},
+            "parity": par,
         }
     if world == 1 and rank == 0 and not opt.no_cpu_baseline:
         work = pathlib.Path(tempfile.mkdtemp(prefix="nnc_cpu_"))

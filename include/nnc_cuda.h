@@ -127,7 +127,11 @@ long long nnc_cuda_launch_count(void);
  * was invalidated). Run the same calls once uncaptured first: the workspace
  * cannot grow during a capture. nnc_cuda_graph_launch replays the graph on
  * the current stream (its tensors' addresses are fixed at capture) and adds
- * its kernels to nnc_cuda_launch_count. */
+ * its kernels to nnc_cuda_launch_count. A graph captured while tracing is on
+ * holds two event-record nodes around each captured call; every replay made
+ * while tracing is on logs those calls' device times in the trace below (one
+ * record per call per replay), so operator times come from the replayed
+ * graph itself. */
 int nnc_cuda_graph_begin(void);
 void* nnc_cuda_graph_end(void);
 int nnc_cuda_graph_launch(void* graph);

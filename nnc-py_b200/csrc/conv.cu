@@ -2324,9 +2324,15 @@ struct StaticScratch {
 // (the first nnc_conv_static_scratch call on that device, with it current).
 // Returns false with the thread's status set when it cannot be resolved.
 bool static_scratch_on_device(StaticScratch* out, const char* op) {
+  constexpr int kDevices = 64;
   static std::mutex mu;
-  static float* ptrs[64] = {};
+  static float* ptrs[kDevices] = {};
   const int dev = ctx().device;
+  if (dev < 0 || dev >= kDevices) {
+    fail(NNC_CUDA_ERR_INVALID, op, "device %d is outside the %d devices this library tracks", dev,
+         kDevices);
+    return false;
+  }
   std::lock_guard<std::mutex> lock(mu);
   if (!ptrs[dev]) {
     float* ptr = nullptr;

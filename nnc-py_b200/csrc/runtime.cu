@@ -37,9 +37,21 @@ struct TraceRec {
 thread_local std::vector<TraceRec> t_trace;
 int g_trace_on = -1;  // -1: read NNC_CUDA_TRACE on first use
 // Between nnc_cuda_graph_begin and nnc_cuda_graph_end: the calls of this
-// thread are being captured (no tracing, no workspace growth).
+// thread are being captured (no workspace growth). With tracing on, each
+// captured call is bracketed by two event-record nodes of the graph; the
+// events are taken from a pool made before the capture started.
 thread_local bool t_capturing = false;
 thread_local long long t_capture_launches0 = 0;
+thread_local std::vector<TraceRec> t_capture_ops;
+thread_local std::vector<cudaEvent_t> t_capture_pool;
+constexpr int kCaptureTraceEvents = 1024;
+
+cudaEvent_t capture_event() {
+  if (t_capture_pool.empty()) return nullptr;
+  cudaEvent_t e = t_capture_pool.back();
+  t_capture_pool.pop_back();
+  return e;
+}
 
 bool trace_on() {
   if (g_trace_on < 0) {
@@ -171,7 +183,17 @@ void* workspace(size_t bytes, const char* op) {
 OpScope::OpScope(const char* name) : name_(name), slot_(-1) {
   int dev = 0;
   if (cudaGetDevice(&dev) == cudaSuccess && dev >= 0 && dev < kMaxDevices) ctx().device = dev;
-  if (!trace_on() || t_capturing) return;
+  if (!trace_on()) return;
+  if (t_capturing) {
+    // Captured call: event-record nodes in the graph (re-bound to fresh
+    // events at every traced replay by nnc_cuda_graph_launch).
+    if (t_capture_pool.size() < 2) return;
+    TraceRec r{name, capture_event(), capture_event()};
+    cudaEventRecordWithFlags(r.start, ctx().stream, cudaEventRecordExternal);
+    t_capture_ops.push_back(r);
+    slot_ = (int)t_capture_ops.size() - 1;
+    return;
+  }
   TraceRec r{name, nullptr, nullptr};
   cudaEventCreate(&r.start);
   cudaEventCreate(&r.stop);
@@ -181,7 +203,13 @@ OpScope::OpScope(const char* name) : name_(name), slot_(-1) {
 }
 
 OpScope::~OpScope() {
-  if (slot_ >= 0 && slot_ < (int)t_trace.size()) cudaEventRecord(t_trace[slot_].stop, ctx().stream);
+  if (slot_ < 0) return;
+  if (t_capturing) {
+    if (slot_ < (int)t_capture_ops.size())
+      cudaEventRecordWithFlags(t_capture_ops[slot_].stop, ctx().stream, cudaEventRecordExternal);
+    return;
+  }
+  if (slot_ < (int)t_trace.size()) cudaEventRecord(t_trace[slot_].stop, ctx().stream);
 }
 
 }  // namespace nnc
@@ -274,10 +302,74 @@ int nnc_cuda_memcpy_async(void* dst, const void* src, size_t bytes, int kind) {
 long long nnc_cuda_launch_count(void) { return ctx().launches; }
 
 // ---- CUDA graphs ---------------------------------------------------------
+// A traced call inside a captured graph: its two event-record nodes and the
+// events the graph owns for them (bound whenever a replay is not traced).
+struct GraphOp {
+  const char* name;
+  cudaGraphNode_t start_node, stop_node;
+  cudaEvent_t own_start, own_stop;
+};
+
 struct NncGraph {
+  cudaGraph_t graph;  // kept while the exec graph lives when it holds trace nodes
   cudaGraphExec_t exec;
   long long kernels;  // library kernels in one replay
+  std::vector<GraphOp> ops;
+  bool own_bound;  // the exec graph's trace nodes record into the own events
 };
+
+namespace {
+void release_capture_trace() {
+  for (auto& r : t_capture_ops) {
+    cudaEventDestroy(r.start);
+    cudaEventDestroy(r.stop);
+  }
+  t_capture_ops.clear();
+  for (cudaEvent_t e : t_capture_pool) cudaEventDestroy(e);
+  t_capture_pool.clear();
+}
+
+// Binds a traced graph's event-record nodes to fresh events and logs them as
+// one trace record per captured call (this replay's device times).
+bool bind_trace_events(NncGraph* g, const char* op) {
+  for (const GraphOp& o : g->ops) {
+    TraceRec r{o.name, nullptr, nullptr};
+    if (!check_cuda(cudaEventCreate(&r.start), op, "cudaEventCreate") ||
+        !check_cuda(cudaEventCreate(&r.stop), op, "cudaEventCreate"))
+      return false;
+    if (!check_cuda(cudaGraphExecEventRecordNodeSetEvent(g->exec, o.start_node, r.start), op,
+                    "cudaGraphExecEventRecordNodeSetEvent") ||
+        !check_cuda(cudaGraphExecEventRecordNodeSetEvent(g->exec, o.stop_node, r.stop), op,
+                    "cudaGraphExecEventRecordNodeSetEvent"))
+      return false;
+    t_trace.push_back(r);
+  }
+  g->own_bound = false;
+  return true;
+}
+
+bool bind_own_events(NncGraph* g, const char* op) {
+  for (const GraphOp& o : g->ops) {
+    if (!check_cuda(cudaGraphExecEventRecordNodeSetEvent(g->exec, o.start_node, o.own_start), op,
+                    "cudaGraphExecEventRecordNodeSetEvent") ||
+        !check_cuda(cudaGraphExecEventRecordNodeSetEvent(g->exec, o.stop_node, o.own_stop), op,
+                    "cudaGraphExecEventRecordNodeSetEvent"))
+      return false;
+  }
+  g->own_bound = true;
+  return true;
+}
+
+void destroy_graph(NncGraph* g) {
+  if (g->exec) cudaGraphExecDestroy(g->exec);
+  if (g->graph) cudaGraphDestroy(g->graph);
+  for (auto& o : g->ops) {
+    cudaEventDestroy(o.own_start);
+    cudaEventDestroy(o.own_stop);
+  }
+  delete g;
+}
+}  // namespace
 
 int nnc_cuda_graph_begin(void) {
   const char* op = "nnc_cuda_graph_begin";
@@ -290,9 +382,23 @@ int nnc_cuda_graph_begin(void) {
                                    "legacy default stream");
     return NNC_CUDA_ERR_INVALID;
   }
+  release_capture_trace();
+  if (trace_on()) {
+    // Events for the captured calls' trace nodes, made before the capture.
+    for (int i = 0; i < kCaptureTraceEvents; ++i) {
+      cudaEvent_t e = nullptr;
+      if (!check_cuda(cudaEventCreate(&e), op, "cudaEventCreate")) {
+        release_capture_trace();
+        return ctx().status;
+      }
+      t_capture_pool.push_back(e);
+    }
+  }
   if (!check_cuda(cudaStreamBeginCapture(ctx().stream, cudaStreamCaptureModeThreadLocal), op,
-                  "cudaStreamBeginCapture"))
+                  "cudaStreamBeginCapture")) {
+    release_capture_trace();
     return ctx().status;
+  }
   t_capturing = true;
   t_capture_launches0 = ctx().launches;
   return NNC_CUDA_OK;
@@ -306,19 +412,60 @@ void* nnc_cuda_graph_end(void) {
   }
   t_capturing = false;
   cudaGraph_t graph = nullptr;
-  if (!check_cuda(cudaStreamEndCapture(ctx().stream, &graph), op, "cudaStreamEndCapture"))
+  if (!check_cuda(cudaStreamEndCapture(ctx().stream, &graph), op, "cudaStreamEndCapture")) {
+    release_capture_trace();
     return nullptr;
+  }
   const long long kernels = ctx().launches - t_capture_launches0;
   ctx().launches = t_capture_launches0;  // captured, not launched
   if (ctx().status != NNC_CUDA_OK) {  // a call inside the capture failed
     cudaGraphDestroy(graph);
+    release_capture_trace();
     return nullptr;
   }
-  cudaGraphExec_t exec = nullptr;
-  const bool ok = check_cuda(cudaGraphInstantiate(&exec, graph, 0), op, "cudaGraphInstantiate");
-  cudaGraphDestroy(graph);
-  if (!ok) return nullptr;
-  return new NncGraph{exec, kernels};
+  NncGraph* g = new NncGraph{nullptr, nullptr, kernels, {}, true};
+  if (!t_capture_ops.empty()) {
+    // Find each traced call's two event-record nodes by their events.
+    size_t n = 0;
+    cudaGraphGetNodes(graph, nullptr, &n);
+    std::vector<cudaGraphNode_t> nodes(n);
+    if (n) cudaGraphGetNodes(graph, nodes.data(), &n);
+    for (const TraceRec& r : t_capture_ops)
+      g->ops.push_back(GraphOp{r.name, nullptr, nullptr, r.start, r.stop});
+    for (cudaGraphNode_t node : nodes) {
+      cudaGraphNodeType type;
+      if (cudaGraphNodeGetType(node, &type) != cudaSuccess || type != cudaGraphNodeTypeEventRecord)
+        continue;
+      cudaEvent_t e = nullptr;
+      if (cudaGraphEventRecordNodeGetEvent(node, &e) != cudaSuccess) continue;
+      for (GraphOp& o : g->ops) {
+        if (o.own_start == e) o.start_node = node;
+        if (o.own_stop == e) o.stop_node = node;
+      }
+    }
+    t_capture_ops.clear();  // the events now belong to the graph
+    bool found = true;
+    for (const GraphOp& o : g->ops) found = found && o.start_node && o.stop_node;
+    if (!found) {
+      fail(NNC_CUDA_ERR_LAUNCH, op, "trace nodes of the captured calls not found in the graph");
+      cudaGraphDestroy(graph);
+      destroy_graph(g);
+      release_capture_trace();
+      return nullptr;
+    }
+  }
+  release_capture_trace();
+  const bool ok = check_cuda(cudaGraphInstantiate(&g->exec, graph, 0), op, "cudaGraphInstantiate");
+  if (g->ops.empty()) {
+    cudaGraphDestroy(graph);
+  } else {
+    g->graph = graph;  // node handles stay valid while the graph exists
+  }
+  if (!ok) {
+    destroy_graph(g);
+    return nullptr;
+  }
+  return g;
 }
 
 int nnc_cuda_graph_launch(void* graph) {
@@ -328,6 +475,16 @@ int nnc_cuda_graph_launch(void* graph) {
     return NNC_CUDA_ERR_INVALID;
   }
   NncGraph* g = static_cast<NncGraph*>(graph);
+  if (!g->ops.empty()) {
+    // A graph captured with tracing: a traced replay logs its calls' device
+    // times; an untraced one records into the graph's own events. Rebinding
+    // affects this and later replays only, never one already queued.
+    if (trace_on()) {
+      if (!bind_trace_events(g, op)) return ctx().status;
+    } else if (!g->own_bound) {
+      if (!bind_own_events(g, op)) return ctx().status;
+    }
+  }
   if (!check_cuda(cudaGraphLaunch(g->exec, ctx().stream), op, "cudaGraphLaunch")) return ctx().status;
   ctx().launches += g->kernels;
   return NNC_CUDA_OK;
@@ -339,9 +496,7 @@ long long nnc_cuda_graph_kernels(const void* graph) {
 
 void nnc_cuda_graph_destroy(void* graph) {
   if (!graph) return;
-  NncGraph* g = static_cast<NncGraph*>(graph);
-  cudaGraphExecDestroy(g->exec);
-  delete g;
+  destroy_graph(static_cast<NncGraph*>(graph));
 }
 
 int nnc_cuda_trace_count(void) {

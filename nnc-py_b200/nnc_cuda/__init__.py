@@ -2,7 +2,6 @@
 
 * :mod:`nnc_cuda.lib`      ctypes binding of libnnc_cuda.so (strict loading)
 * :mod:`nnc_cuda.tensor`   ``Tensor`` descriptors over torch / numpy buffers
-* :mod:`nnc_cuda.oracle`   ctypes binding of the CPU oracle (tests/bench only)
 * :mod:`nnc_cuda.workloads` BASELINE configs as layer lists + seeded weights
 * :mod:`nnc_cuda.model`    runs a compiled ``-t cuda`` model library
 * :mod:`nnc_cuda.codegen`  the ``cuda`` target for nnc-py's compiler

@@ -27,6 +27,7 @@ the same artifact set as the x86 backend (codegen/x86_backend.py:89-147):
 from __future__ import annotations
 
 import json
+import os
 import pathlib
 import re
 import sys
@@ -36,15 +37,15 @@ import numpy as np
 
 from .workloads import Model
 
-REFERENCE_SRC = pathlib.Path("/root/reference/src")
-
-
 def _import_nnc_py():
+    """Imports nnc-py: from the environment, else from the checkout that the
+    NNC_REFERENCE variable names (its ``src`` directory)."""
     try:
         import nnc_py  # noqa: F401
     except ImportError:
-        if (REFERENCE_SRC / "nnc_py").exists():
-            sys.path.insert(0, str(REFERENCE_SRC))
+        ref = os.environ.get("NNC_REFERENCE")
+        if ref and (pathlib.Path(ref) / "src" / "nnc_py").exists():
+            sys.path.insert(0, str(pathlib.Path(ref) / "src"))
         import nnc_py  # noqa: F401
 
 
@@ -129,7 +130,7 @@ class ConvAddReluFusionPass(PassBase):
 
 class ConvReluMaxPoolFusionPass(PassBase):
     """Collapses Conv+ReLU -> MaxPool into one call, nnc_conv_relu_maxpool
-    (the ResNet stem; SURVEY's "wider O3 fused groups"), so the conv result
+    (the ResNet stem), so the conv result
     (1024 x 64 x 112 x 112 floats for the bench batch) is never written.
 
     Runs after PatternFusion (the Conv+ReLU is then a FUSED_CONV_RELU node)

@@ -64,6 +64,14 @@ class CudaModel:
             raise RuntimeError(f"nnc_model_init({device}) failed: {self.rt.nnc_cuda_get_last_error_string()}")
         self.device = device
 
+    def free(self) -> None:
+        """Releases this device's arena and constant slab (init() again to
+        reuse the model on it)."""
+        if self.device is not None:
+            self.release_graph()
+            self.lib.nnc_model_free(self.device)
+            self.device = None
+
     def select(self) -> None:
         if self.lib.nnc_model_select(self.device) != 0:
             raise RuntimeError("nnc_model_select failed")

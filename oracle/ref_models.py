@@ -12,12 +12,13 @@ Needs the reference checkout (nnc-py importable); run by
 __graft_entry__.build() where it exists. Outputs stay in oracle/_ref/
 (git-ignored; they travel to the GPU box with the rest of the tree).
 
-    python oracle/ref_models.py [--ref /root/reference]
+    python oracle/ref_models.py [--ref <nnc-py checkout>]
 """
 
 from __future__ import annotations
 
 import argparse
+import os
 import json
 import pathlib
 import shutil
@@ -82,7 +83,8 @@ def build_one(ref: pathlib.Path, tag: str, model_name: str, batch: int, opt: int
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("NNC_REFERENCE"), required="NNC_REFERENCE" not in os.environ,
+                    help="nnc-py checkout (default: $NNC_REFERENCE)")
     ap.add_argument("--only", default=None)
     opt = ap.parse_args()
     ref = pathlib.Path(opt.ref)

@@ -3,7 +3,7 @@ the single-op sweep against the measured peaks (tensor pipe for conv/GEMM,
 HBM for every other op) and the model throughput of LeNet-5 (N = 8192),
 ResNet-18 -O1 (N = 64, 256) and the small transformer (B = 256).
 
-    python -m nnc_cuda.sweep [--reps 10] [--json sweep.json] [--only ops|models]
+    python sweep.py [--reps 10] [--json sweep.json] [--only ops|models]
 
 Every number is a median over `reps` calls timed with CUDA events on the
 launching stream. Each op call is captured once into a CUDA graph and replayed
@@ -11,8 +11,10 @@ per rep (the events bracket its kernels, not the host-side setup of a direct
 call); before each rep the runner reads a 512 MB buffer (larger than the
 126 MB L2), so inputs come from HBM. A model step replays one captured CUDA
 graph of the whole forward. Denominators: MEASURED_PEAKS.json at the repository root
-(HBM copy GB/s; dense TF32 = bf16 burst / 2, each op being timed alone), else
-the pool's fallback figures (6650 GB/s, 1590 TFLOP/s bf16). Inputs are seeded
+(HBM copy GB/s; dense TF32 = bf16 / 2), else the pool's fallback figures
+(6650 GB/s, 1590 TFLOP/s bf16), read by bench.peaks(); each op is timed
+alone in short bursts, so the burst figure applies (bench.tf32_peak's rule
+with the clocks at their maximum). Inputs are seeded
 N(0, 1), the shapes are BASELINE.json's.
 """
 
@@ -23,21 +25,22 @@ import ctypes
 import json
 import pathlib
 import statistics
+import sys
 
 import numpy as np
 
-from . import lib as L
-from . import tensor as T
+ROOT = pathlib.Path(__file__).resolve().parent
+sys.path[:0] = [str(ROOT), str(ROOT / "nnc-py_b200")]
 
-ROOT = pathlib.Path(__file__).resolve().parents[2]
+import bench  # noqa: E402
+from nnc_cuda import lib as L  # noqa: E402
+from nnc_cuda import tensor as T  # noqa: E402
 
 
 def peaks() -> dict:
-    p = ROOT / "MEASURED_PEAKS.json"
-    if p.exists():
-        d = json.loads(p.read_text())
-        return {"hbm_gbs": d["hbm_gbs"], "tf32_tflops": d["bf16_tflops"] / 2.0, "source": "measured"}
-    return {"hbm_gbs": 6650.0, "tf32_tflops": 1590.0 / 2.0, "source": "fallback"}
+    pk = bench.peaks()
+    tf32, note = bench.tf32_peak(pk, None)
+    return {"hbm_gbs": pk["hbm_gbs"], "tf32_tflops": tf32, "tf32_note": note, "source": pk["source"]}
 
 
 class Timer:
@@ -230,8 +233,8 @@ MODELS = (("lenet5_o1_b8192", "lenet5", 8192), ("resnet18_o1_b64", "resnet18", 6
 
 
 def model_runs(so, torch, pk: dict, reps: int, only_model: str | None = None) -> list[dict]:
-    from .model import CudaModel
-    from .workloads import BUILDERS
+    from nnc_cuda.model import CudaModel
+    from nnc_cuda.workloads import BUILDERS
 
     rows = []
     for tag, name, batch in MODELS:

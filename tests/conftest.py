@@ -1,3 +1,4 @@
+import os
 import pathlib
 import sys
 
@@ -7,6 +8,12 @@ ROOT = pathlib.Path(__file__).resolve().parent.parent
 for p in (ROOT, ROOT / "nnc-py_b200", ROOT / "tests"):
     if str(p) not in sys.path:
         sys.path.insert(0, str(p))
+
+# Where the reference checkout lives (codegen and pin tests that need it skip
+# when it is absent): the build entry's default unless NNC_REFERENCE is set.
+import __graft_entry__  # noqa: E402
+
+os.environ.setdefault("NNC_REFERENCE", str(__graft_entry__.REFERENCE))
 
 
 def pytest_configure(config):

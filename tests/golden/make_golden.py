@@ -3,7 +3,7 @@
 Run where the reference checkout and its compiled operator library exist
 (``make -C oracle ref``):
 
-    python tests/golden/make_golden.py [--ref /root/reference]
+    python tests/golden/make_golden.py [--ref <nnc-py checkout>]
 
 Three groups of fixtures:
 
@@ -23,6 +23,7 @@ load; nothing at test time reads the reference checkout.
 from __future__ import annotations
 
 import argparse
+import os
 import ast
 import json
 import pathlib
@@ -155,7 +156,8 @@ def kat_case(test, line, env):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("NNC_REFERENCE"), required="NNC_REFERENCE" not in os.environ,
+                    help="nnc-py checkout (default: $NNC_REFERENCE)")
     opt = ap.parse_args()
     ref = O.load_reference()
     orc = O.load_oracle()

@@ -1,6 +1,7 @@
 """The cuda codegen target (CPU-only; needs nnc-py importable, i.e. where the
 reference checkout exists — skipped elsewhere)."""
 
+import os
 import pathlib
 import re
 import sys
@@ -9,7 +10,7 @@ import numpy as np
 import pytest
 
 ROOT = pathlib.Path(__file__).resolve().parent.parent
-REF_SRC = pathlib.Path("/root/reference/src")
+REF_SRC = pathlib.Path(os.environ.get("NNC_REFERENCE", "-")) / "src"
 if REF_SRC.exists() and str(REF_SRC) not in sys.path:
     sys.path.insert(0, str(REF_SRC))
 nnc_py = pytest.importorskip("nnc_py")

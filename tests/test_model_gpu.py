@@ -57,6 +57,40 @@ def test_resnet18_batch_shards_agree(cuda_lib, golden, prec):
     C.assert_close(got[:2], golden["resnet18_b2/output"], MODEL_RTOL[prec], f"b128[:2] prec{prec}")
 
 
+BENCH_GOLDEN = pathlib.Path(__file__).resolve().parent / "golden" / "bench_resnet18_o3.npz"
+GLOBAL_BATCH = 1024
+
+
+@pytest.fixture(scope="module")
+def bench_input():
+    """The benchmark's seeded batch-1024 input (616 MB) and the reference
+    logits of 32 of its images (the -O3 x86 build)."""
+    z = np.load(BENCH_GOLDEN)
+    return W.resnet18(1).input_array(GLOBAL_BATCH), z["indices"], z["logits"]
+
+
+@pytest.mark.parametrize("prec", [L.PRECISION_TF32, L.PRECISION_3XTF32])
+@pytest.mark.parametrize("per_gpu", [1024, 512, 256, 128])
+def test_bench_config_matches_reference_x86_build(cuda_lib, bench_input, per_gpu, prec):
+    """The benchmarked configuration itself: ResNet-18 -O3 over the global
+    batch of 1024, compiled for the per-GPU batch of 1, 2, 4 and 8 GPUs and
+    run shard by shard (as the ranks of `bench.py --gpus N` do), the shards'
+    logits put together in rank order and compared at the fixture's indices
+    (the first and last image of every 128-image shard and 16 others) with
+    the reference's -O3 x86 build on the same images."""
+    x, idx, want = bench_input
+    m = _model(f"resnet18_o3_b{per_gpu}")
+    try:
+        m.load_constants(W.resnet18(per_gpu))
+        cuda_lib.nnc_cuda_set_precision(prec)
+        shards = [m.run_host(x[s:s + per_gpu]) for s in range(0, GLOBAL_BATCH, per_gpu)]
+    finally:
+        m.free()
+    got = np.concatenate(shards)
+    assert got.shape == (GLOBAL_BATCH, 1000)
+    C.assert_close(got[idx], want, MODEL_RTOL[prec], f"resnet18_o3_b{per_gpu} prec{prec}")
+
+
 def test_lenet5_matches_reference_x86_build(cuda_lib, golden):
     m = _model("lenet5_o1_b16")
     m.load_constants(W.lenet5(16))

@@ -190,6 +190,10 @@ PAIR_GEMM_CASES = [
     # Batches of at most 128 rows against one B on CTA pairs, one batch per
     # CTA (the reference's overlapping batch offsets; ragged M and N).
     ("mm", (132, 100, 64), (64, 264)), ("mm", (128, 128, 32), (32, 384)),
+    # An odd batch count on that route: the last pair's second CTA has no
+    # batch (its A tile reads as zeros through the tensor map's bounds and
+    # its store is skipped); also with a row bias and relu in the epilogue.
+    ("mm", (131, 100, 64), (64, 264)), ("mmrelu_bias", (129, 128, 32), (32, 384)),
 ]
 
 
@@ -201,6 +205,10 @@ def test_gemm_cta_pairs_vs_oracle(cuda_lib, cfg):
     if kind == "mm":
         so = sa[:-1] + sb[-1:]
         case = {"name": "m", "op": "nnc_matmul", "args": [C._t("a"), C._t("b"), C._o("out", so)]}
+    elif kind == "mmrelu_bias":
+        so = sa[:-1] + sb[-1:]
+        arrays["bias"] = r.standard_normal((sb[-1],)).astype(np.float32)
+        case = {"name": "m", "op": "nnc_matmul_relu", "args": [C._t("a"), C._t("b"), C._t("bias"), C._o("out", so)]}
     elif kind == "gemmnt_bias":
         M, N = sa[0], sb[0]
         arrays["c"] = r.standard_normal((N,)).astype(np.float32)

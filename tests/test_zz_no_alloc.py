@@ -23,12 +23,15 @@ from nnc_cuda import tensor as T
 pytestmark = pytest.mark.gpu
 
 # (N, C_in, H, W, C_out, KH, KW, sh, sw, ph, pw): one per kernel feeding mode,
-# each with an NCHW input so the scratch holds its NHWC copy and packed weights.
+# each with an NCHW input so the scratch holds its NHWC copy (or, in element
+# mode, its 3xTF32 hi/lo planes) and the packed weights. C_out > 16 keeps
+# every case on the tensor-core kernels (smaller ones take a CUDA-core kernel
+# that reads the weights in place and needs no scratch).
 CASES = {
     "im2col128": (2, 64, 28, 28, 128, 3, 3, 1, 1, 1, 1),
     "im2col16_stem": (2, 3, 30, 30, 16, 7, 7, 2, 2, 3, 3),
     "chunk_gather": (1, 5, 17, 13, 24, 3, 5, 2, 1, 1, 2),
-    "element": (4, 1, 12, 12, 6, 5, 5, 1, 1, 0, 0),
+    "element": (4, 1, 12, 12, 24, 5, 5, 1, 1, 0, 0),
 }
 SCRATCH_LIMIT = 16 << 20
 
@@ -79,6 +82,25 @@ def test_matches_nnc_conv_on_consecutive_calls(cuda_lib, precision):
     # The calls ran on the GPU and never touched the growable workspace.
     assert so.nnc_cuda_launch_count() > launches_before
     assert so.nnc_cuda_get_workspace_capacity() == ws_before
+
+
+@pytest.mark.parametrize("precision", [L.PRECISION_TF32, L.PRECISION_3XTF32])
+def test_matches_cpu_oracle(cuda_lib, precision):
+    """Beside the comparison with nnc_conv: every case against the CPU
+    restatement of the reference's nnc_conv (double accumulation, one
+    rounding), after the other cases have used the shared scratch."""
+    from oracle import oracle as O
+
+    so = cuda_lib
+    so.nnc_cuda_set_precision(precision)
+    orc = O.load_oracle()
+    for name in reversed(list(CASES)):
+        x, wt, b, oshape, geo = _inputs(name)
+        case = {"name": name, "op": "nnc_conv",
+                "args": [C._t("x"), C._t("w"), C._t("b"), C._o("out", oshape)] + [C._i(v) for v in geo]}
+        want = C.run_host(orc, case, {"x": x, "w": wt, "b": b})["out"]
+        got = _run(so, "nnc_conv_static_scratch", name)
+        C.assert_close(got, want, C.TC_RTOL[precision], f"{name} vs oracle precision={precision}")
 
 
 def test_rejects_scratch_beyond_limit(cuda_lib):
