@@ -319,6 +319,10 @@ struct NncGraph {
 };
 
 namespace {
+// This thread's live graphs that hold trace nodes: nnc_cuda_trace_clear
+// re-binds them to their own events before it destroys the logged ones.
+thread_local std::vector<NncGraph*> t_traced_graphs;
+
 void release_capture_trace() {
   for (auto& r : t_capture_ops) {
     cudaEventDestroy(r.start);
@@ -361,6 +365,12 @@ bool bind_own_events(NncGraph* g, const char* op) {
 }
 
 void destroy_graph(NncGraph* g) {
+  for (size_t i = 0; i < t_traced_graphs.size(); ++i) {
+    if (t_traced_graphs[i] == g) {
+      t_traced_graphs.erase(t_traced_graphs.begin() + i);
+      break;
+    }
+  }
   if (g->exec) cudaGraphExecDestroy(g->exec);
   if (g->graph) cudaGraphDestroy(g->graph);
   for (auto& o : g->ops) {
@@ -465,6 +475,7 @@ void* nnc_cuda_graph_end(void) {
     destroy_graph(g);
     return nullptr;
   }
+  if (!g->ops.empty()) t_traced_graphs.push_back(g);
   return g;
 }
 
@@ -516,6 +527,12 @@ float nnc_cuda_trace_us(int i) {
 }
 
 void nnc_cuda_trace_clear(void) {
+  // The logged events may still be bound to a traced graph's nodes (its last
+  // traced replay): bind the graph's own events first, then wait for the
+  // replays that record into the logged ones.
+  for (NncGraph* g : t_traced_graphs)
+    if (!g->own_bound) bind_own_events(g, "nnc_cuda_trace_clear");
+  cudaStreamSynchronize(ctx().stream);
   for (auto& r : t_trace) {
     cudaEventDestroy(r.start);
     cudaEventDestroy(r.stop);
@@ -536,10 +553,8 @@ int nnc_cuda_trace_dump(void) {
     cudaEventElapsedTime(&e, t0, t_trace[i].stop);
     fprintf(stderr, "[nnc_cuda_trace] #%d op=%s start_us=%.1f end_us=%.1f dur_us=%.1f\n", i,
             t_trace[i].name, s * 1e3, e * 1e3, (e - s) * 1e3);
-    cudaEventDestroy(t_trace[i].start);
-    cudaEventDestroy(t_trace[i].stop);
   }
-  t_trace.clear();
+  nnc_cuda_trace_clear();
   return n;
 }
 
