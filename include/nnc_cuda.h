@@ -107,6 +107,19 @@ void nnc_conv_static_scratch(Tensor* input, Tensor* weight, Tensor* bias, Tensor
                              int kernel_h, int kernel_w, int stride_h, int stride_w,
                              int pad_h, int pad_w);
 
+/* ---- failure injection (tests of the error paths; no reference counterpart) --
+ * nnc_cuda_inject_alloc_failures(n): the library's next n device allocations
+ * (workspace growth; process-wide) fail as if the device were out of
+ * memory: the op reports NNC_CUDA_ERR_NOMEM and queues nothing. 0 clears it.
+ * nnc_cuda_selftest_bounded_wait(limit_us): queues one kernel whose thread
+ * waits on an mbarrier that nothing completes, through the bounded wait the
+ * tensor-core pipelines use, given up after limit_us microseconds (1 ..
+ * 2000000): the kernel then records NNC_CUDA_ERR_DEVICE_TIMEOUT in the
+ * device error word and returns, so nnc_cuda_check_device_status reports it
+ * and the context stays usable. Neither faults nor hangs the GPU. */
+void nnc_cuda_inject_alloc_failures(int count);
+int nnc_cuda_selftest_bounded_wait(int limit_us);
+
 /* ---- layout conversion at model boundaries (logical shapes are NCHW) ---- */
 void nnc_cuda_nchw_to_nhwc(Tensor* input, Tensor* output);
 void nnc_cuda_nhwc_to_nchw(Tensor* input, Tensor* output);

@@ -8,6 +8,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "tc.cuh"
 
 namespace nnc {
 
@@ -29,6 +30,30 @@ struct Workspace {
   size_t user_cap[kMaxDevices] = {};
 };
 thread_local Workspace t_ws;
+// Failure injection: the next this-many device allocations of the library
+// (workspace growth) fail as if the device were out of memory.
+int g_fail_allocs = 0;
+std::mutex g_fail_mu;
+
+bool injected_alloc_failure() {
+  std::lock_guard<std::mutex> lock(g_fail_mu);
+  if (g_fail_allocs <= 0) return false;
+  --g_fail_allocs;
+  return true;
+}
+
+// One thread waits on a barrier that nothing completes, through the same
+// bounded wait as the tensor-core pipelines, with a caller-chosen bound; the
+// expired wait records the timeout in the device error word and the kernel
+// returns.
+__global__ void bounded_wait_selftest_kernel(int* err, uint64_t limit_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    tc::mbar_init(&bar, 1);
+    tc::fence_barrier_init();
+    tc::mbar_wait_for(&bar, 0, err, limit_ns);
+  }
+}
 
 struct TraceRec {
   const char* name;
@@ -174,6 +199,10 @@ void* workspace(size_t bytes, const char* op) {
     t_ws.cap[d] = 0;
   }
   void* p = nullptr;
+  if (injected_alloc_failure()) {
+    fail(NNC_CUDA_ERR_NOMEM, op, "workspace allocation of %zu bytes failed (injected)", want);
+    return nullptr;
+  }
   if (!check_cuda(cudaMallocAsync(&p, want, c.stream), op, "workspace allocation")) return nullptr;
   t_ws.ptr[d] = p;
   t_ws.cap[d] = want;
@@ -300,6 +329,28 @@ int nnc_cuda_memcpy_async(void* dst, const void* src, size_t bytes, int kind) {
 }
 
 long long nnc_cuda_launch_count(void) { return ctx().launches; }
+
+void nnc_cuda_inject_alloc_failures(int count) {
+  std::lock_guard<std::mutex> lock(g_fail_mu);
+  g_fail_allocs = count > 0 ? count : 0;
+}
+
+int nnc_cuda_selftest_bounded_wait(int limit_us) {
+  const char* op = "nnc_cuda_selftest_bounded_wait";
+  OpScope scope(op);
+  if (limit_us < 1 || limit_us > 2000000) {
+    fail(NNC_CUDA_ERR_INVALID, op, "limit %d us outside [1, 2000000]", limit_us);
+    return NNC_CUDA_ERR_INVALID;
+  }
+  int* err = device_error_word();
+  if (!err) {
+    fail(NNC_CUDA_ERR_NOMEM, op, "no device error word");
+    return NNC_CUDA_ERR_NOMEM;
+  }
+  bounded_wait_selftest_kernel<<<1, 32, 0, ctx().stream>>>(err, (uint64_t)limit_us * 1000ull);
+  if (!check_launch(op)) return ctx().status;
+  return NNC_CUDA_OK;
+}
 
 // ---- CUDA graphs ---------------------------------------------------------
 // A traced call inside a captured graph: its two event-record nodes and the

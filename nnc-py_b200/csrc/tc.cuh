@@ -73,15 +73,19 @@ __device__ __forceinline__ uint64_t global_ns() {
 // tries until it does, giving up after kWaitNs nanoseconds (or kWaitLimit
 // tries) and recording the timeout.
 constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, int* err,
+                                              uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_ns();
   for (uint32_t i = 0; i < kWaitLimit; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (global_ns() - t0 > kWaitNs) break;
+    if (global_ns() - t0 > limit_ns) break;
   }
   if (err) atomicExch(err, 5 /* NNC_CUDA_ERR_DEVICE_TIMEOUT */);
   return false;
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
+  return mbar_wait_for(bar, parity, err, kWaitNs);
 }
 
 // ---------------------------------------------------------------- TMA ----
