@@ -151,7 +151,9 @@ struct ConvCfg {
   static constexpr uint32_t A_BYTES = BM * BK * 4;
   static constexpr uint32_t B_BYTES = BN * BK * 4;
   static constexpr uint32_t STAGE_BYTES = SPLIT * (A_BYTES + B_BYTES);
-  static constexpr uint32_t TMEM_COLS = 2 * BN;
+  // Two accumulators; in 3xTF32 mode two chunk buffers plus the running sum
+  // (tc::promote_chunk32), rounded up to a power of two.
+  static constexpr uint32_t TMEM_COLS = SPLIT == 1 ? 2 * BN : (3 * BN <= 256 ? 256 : 512);
   static constexpr uint32_t EPI_OFF = STAGES * STAGE_BYTES;
   static constexpr uint32_t KTAB_OFF = EPI_OFF + kEpiBytes;
   static constexpr uint32_t BAR_OFF = KTAB_OFF + 2 * kMaxElementK * 4;
@@ -703,15 +705,24 @@ __global__ void __launch_bounds__(kConvThreads, 1)
       constexpr uint32_t idesc = tc::idesc_tf32(BM, BN);
       int stage = 0;
       uint32_t phase = 0;
-      int local = 0;
+      int local = 0;  // accumulator fills so far (tiles, or 3xTF32 chunks)
       bool ok = true;
-      for (int64_t t = blockIdx.x; t < g.tiles && ok; t += gridDim.x, ++local) {
+      // 3xTF32: each chunk of kChunkKBlocks k-blocks starts a fresh
+      // accumulator in the next buffer (see tc::promote_chunk32).
+      const int chunk_kb = SPLIT == 2 ? tc::kChunkKBlocks : g.kblocks;
+      const int chunks = SPLIT == 2 ? (g.kblocks + chunk_kb - 1) / chunk_kb : 1;
+      for (int64_t t = blockIdx.x; t < g.tiles && ok; t += gridDim.x) {
+       for (int ci = 0, kc = 0; ci < chunks && ok; ++ci, kc += chunk_kb, ++local) {
         const int acc = local & 1;
         const uint32_t aphase = (local >> 1) & 1;
-        if (!tc::mbar_wait(&tempty[acc], aphase ^ 1, g.err)) break;
+        if (!tc::mbar_wait(&tempty[acc], aphase ^ 1, g.err)) {
+          ok = false;
+          break;
+        }
         tc::tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
-        for (int kb = 0; kb < g.kblocks; ++kb) {
+        const int kend = kc + chunk_kb < g.kblocks ? kc + chunk_kb : g.kblocks;
+        for (int kb = kc; kb < kend; ++kb) {
           if (!tc::mbar_wait(&full[stage], phase, g.err)) {
             ok = false;
             break;
@@ -731,7 +742,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
             const uint64_t a0 = a_cols ? tc::desc_kmajor_noswizzle(sa + k * 4096, 2048, 128)
                                        : tc::desc_kmajor_sw128(sa + k * 32);
             const uint64_t b0 = tc::desc_kmajor_sw128(sb + k * 32);
-            const uint32_t accum = (kb | k) != 0;
+            const uint32_t accum = ((kb - kc) | k) != 0;
             if (SPLIT == 1) {
               tc::mma_tf32(d_tmem, a0, b0, idesc, accum);
             } else {
@@ -751,6 +762,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
           }
         }
         tc::mma_commit(&tfull[acc]);
+       }
       }
       tc::mma_commit(done);
       tc::mbar_wait(done, 0, g.err);
@@ -766,20 +778,57 @@ __global__ void __launch_bounds__(kConvThreads, 1)
                         (!g.residual || ((((uintptr_t)g.residual) & 15) == 0));
     const bool bias_vec = g.bias && ((((uintptr_t)g.bias) & 15) == 0);
     const bool direct = vec_ok && perm_rows(g.Cout) && g.direct_epi;
+    if constexpr (SPLIT == 1) {
+      int local = 0;
+      for (int64_t t = blockIdx.x; t < g.tiles; t += gridDim.x, ++local) {
+        const int mt = (int)(t / g.n_tiles), nt = (int)(t % g.n_tiles);
+        const int acc = local & 1;
+        const uint32_t aphase = (local >> 1) & 1;
+        if (!tc::mbar_wait(&tfull[acc], aphase, g.err)) break;
+        tc::tc_fence_after();
+        store_tile<BN, false>(g, tmem_base, acc * BN, nt, quad, half * kStageCols, 2 * kStageCols,
+                              lane, stage_tile, vec_ok, bias_vec, LinearRows{(int64_t)mt * BM, g.M},
+                              direct);
+        tc::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&tempty[acc]);
+      }
+    } else {
+    const int chunk_kb = tc::kChunkKBlocks;
     int local = 0;
-    for (int64_t t = blockIdx.x; t < g.tiles; t += gridDim.x, ++local) {
+    bool ok = true;
+    for (int64_t t = blockIdx.x; t < g.tiles && ok; t += gridDim.x) {
       const int mt = (int)(t / g.n_tiles), nt = (int)(t % g.n_tiles);
-      const int acc = local & 1;
-      const uint32_t aphase = (local >> 1) & 1;
-      if (!tc::mbar_wait(&tfull[acc], aphase, g.err)) break;
-      tc::tc_fence_after();
-      store_tile<BN, false>(g, tmem_base, acc * BN, nt, quad, half * kStageCols, 2 * kStageCols,
-                            lane,
-                     stage_tile, vec_ok, bias_vec, LinearRows{(int64_t)mt * BM, g.M}, direct);
-      tc::tc_fence_before();
-      __syncwarp();
-      if (lane == 0) tc::mbar_arrive(&tempty[acc]);
+      for (int kc = 0; kc < g.kblocks; kc += chunk_kb, ++local) {
+        const int acc = local & 1;
+        const uint32_t aphase = (local >> 1) & 1;
+        if (!tc::mbar_wait(&tfull[acc], aphase, g.err)) {
+          ok = false;
+          break;
+        }
+        tc::tc_fence_after();
+        const bool last = kc + chunk_kb >= g.kblocks;
+        if (!(kc == 0 && last)) {
+          // 3xTF32 chunk: fold the partial sums of this warp's column slices
+          // into the running sum (columns 2 BN + c).
+          const uint32_t lane_addr = tmem_base + ((uint32_t)(quad * 32) << 16);
+#pragma unroll 1
+          for (int c0 = half * kStageCols; c0 < BN; c0 += 2 * kStageCols) {
+            if (nt * BN + c0 >= g.Cout) continue;  // warp-uniform
+            tc::promote_chunk32(lane_addr, acc * BN + c0, 2 * BN + c0, kc == 0, last);
+          }
+          tc::tmem_st_wait();
+        }
+        if (last)
+          store_tile<BN, false>(g, tmem_base, acc * BN, nt, quad, half * kStageCols,
+                                2 * kStageCols, lane, stage_tile, vec_ok, bias_vec,
+                                LinearRows{(int64_t)mt * BM, g.M}, direct);
+        tc::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&tempty[acc]);
+      }
     }
+    }  // SPLIT == 2
   }
 
   tc::tc_fence_before();
@@ -2767,9 +2816,9 @@ void conv_impl(Tensor* input, Tensor* weight, Tensor* bias, Tensor* residual, Te
     else
       launch_conv<64, 1, 8>(g, w0, nullptr, op);
   } else {
-    if (Cout > 128)
-      launch_conv<256, 2, 2>(g, w0, w1, op);
-    else if (Cout > 64)
+    // 3xTF32: at most 128 channels per tile (two chunk buffers and the
+    // running sum fit TMEM's 512 columns).
+    if (Cout > 64)
       launch_conv<128, 2, 3>(g, w0, w1, op);
     else
       launch_conv<64, 2, 4>(g, w0, w1, op);

@@ -46,6 +46,7 @@ struct GemmArgs {
   int tma_store;  // 1: D written by TMA stores through tmD (dense, 16-byte rows)
   int b_mn;       // 1: B tiles are MN-major ({32 n, 32 k} boxes of a [K, N] matrix)
   int pair_b;     // CTA pairs only: 1 = the two CTAs take consecutive batches (M <= 128)
+  int softmax;    // 1: each output row is replaced by the softmax of alpha * row (N <= BN)
   int batches;
   int* err;
 };
@@ -59,7 +60,10 @@ struct GemmCfg {
   static constexpr uint32_t A_BYTES = BM * BK * 4;
   static constexpr uint32_t B_BYTES = BN * BK * 4;
   static constexpr uint32_t STAGE_BYTES = SPLIT * (A_BYTES + B_BYTES);
-  static constexpr uint32_t TMEM_COLS = 2 * BN;  // power of two for BN in {64,128,256}
+  // Two accumulators (a power of two for BN in {64, 128, 256}); in 3xTF32
+  // mode two chunk buffers plus the running sum (tc::promote_chunk32),
+  // rounded up to a power of two.
+  static constexpr uint32_t TMEM_COLS = SPLIT == 1 ? 2 * BN : (3 * BN <= 256 ? 256 : 512);
   // Epilogue staging: per epilogue warp two 32 x 32 fp32 boxes (4 KB each).
   static constexpr uint32_t STAGING_BYTES = 4 * 2 * 4096;
   static constexpr size_t SMEM =
@@ -75,7 +79,7 @@ template <int BN>
 __device__ __forceinline__ void store_slices(const GemmArgs& g, const CUtensorMap* tmD,
                                              uint32_t tmem_base, int acc, int quad, int lane,
                                              int row0, int nt, int b, float* box0, int& bsel,
-                                             bool vec_ok) {
+                                             bool vec_ok, float alpha) {
   const int row = row0 + lane;
   float* drow = g.D + (int64_t)b * g.d_batch_stride + (int64_t)row * g.ldd;
   const float* crow = nullptr;
@@ -95,7 +99,7 @@ __device__ __forceinline__ void store_slices(const GemmArgs& g, const CUtensorMa
     // cycles per 32-column slice (measured), 30x the TMEM load.
     float v[32];
 #pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = g.alpha * __uint_as_float(r[j]);
+    for (int j = 0; j < 32; ++j) v[j] = alpha * __uint_as_float(r[j]);
     if (g.c_mode == 1) {  // C[n], the same 32 values for every lane (broadcast loads)
       const float* cb = g.C + n0;
       if (n0 + 32 <= g.N && ((uintptr_t)cb & 15) == 0) {
@@ -155,6 +159,55 @@ __device__ __forceinline__ void store_slices(const GemmArgs& g, const CUtensorMa
       }
     }
   }
+}
+
+// Row softmax in the epilogue (nnc_matmul_scale_softmax): this warp's 32
+// TMEM lanes hold 32 output rows whose N <= BN columns are all in this tile.
+// Each thread takes its row through three passes over the accumulator, in
+// column order as the reference's nnc_softmax does (ops.c:283-307): the max
+// of v = alpha * acc; e = expf(v - max) with a sequential fp32 sum, e
+// written back over the accumulator; then e / sum written back, which the
+// ordinary epilogue stores with alpha 1.
+template <int BN>
+__device__ __forceinline__ void softmax_rows_tmem(uint32_t lane_addr, uint32_t col0, int N,
+                                                  float alpha) {
+  float mx = -INFINITY;
+#pragma unroll 1
+  for (int c0 = 0; c0 < BN && c0 < N; c0 += 16) {
+    uint32_t r[16];
+    tc::tmem_ld16(lane_addr + col0 + c0, r);
+    tc::tmem_ld_wait();
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const float v = alpha * __uint_as_float(r[j]);
+      if (c0 + j < N && v > mx) mx = v;
+    }
+  }
+  float sum = 0.0f;
+#pragma unroll 1
+  for (int c0 = 0; c0 < BN && c0 < N; c0 += 16) {
+    uint32_t r[16];
+    tc::tmem_ld16(lane_addr + col0 + c0, r);
+    tc::tmem_ld_wait();
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const float e = expf(alpha * __uint_as_float(r[j]) - mx);
+      if (c0 + j < N) sum = __fadd_rn(sum, e);
+      r[j] = __float_as_uint(e);
+    }
+    tc::tmem_st16(lane_addr + col0 + c0, r);
+  }
+  tc::tmem_st_wait();
+#pragma unroll 1
+  for (int c0 = 0; c0 < BN && c0 < N; c0 += 16) {
+    uint32_t r[16];
+    tc::tmem_ld16(lane_addr + col0 + c0, r);
+    tc::tmem_ld_wait();
+#pragma unroll
+    for (int j = 0; j < 16; ++j) r[j] = __float_as_uint(__fdiv_rn(__uint_as_float(r[j]), sum));
+    tc::tmem_st16(lane_addr + col0 + c0, r);
+  }
+  tc::tmem_st_wait();
 }
 
 template <int BN, int SPLIT, int STAGES>
@@ -256,15 +309,24 @@ __global__ void __launch_bounds__(kTCThreads, 1)
       const uint32_t idesc = tc::idesc_tf32(BM, BN) | (g.b_mn ? tc::kIdescBMajorMN : 0u);
       int stage = 0;
       uint32_t phase = 0;
-      int local = 0;
+      int local = 0;  // accumulator fills so far (tiles, or 3xTF32 chunks)
       bool ok = true;
-      for (int64_t t = blockIdx.x; t < g.tiles && ok; t += gridDim.x, ++local) {
+      // 3xTF32: each chunk of kChunkKBlocks k-blocks starts a fresh
+      // accumulator in the next buffer (see tc::promote_chunk32).
+      const int chunk_kb = SPLIT == 2 ? tc::kChunkKBlocks : kblocks;
+      const int chunks = SPLIT == 2 ? (kblocks + chunk_kb - 1) / chunk_kb : 1;
+      for (int64_t t = blockIdx.x; t < g.tiles && ok; t += gridDim.x) {
+       for (int ci = 0, kc = 0; ci < chunks && ok; ++ci, kc += chunk_kb, ++local) {
         const int acc = local & 1;
         const uint32_t aphase = (local >> 1) & 1;
-        if (!tc::mbar_wait(&tempty[acc], aphase ^ 1, g.err)) break;
+        if (!tc::mbar_wait(&tempty[acc], aphase ^ 1, g.err)) {
+          ok = false;
+          break;
+        }
         tc::tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
-        for (int kb = 0; kb < kblocks; ++kb) {
+        const int kend = kc + chunk_kb < kblocks ? kc + chunk_kb : kblocks;
+        for (int kb = kc; kb < kend; ++kb) {
           if (!tc::mbar_wait(&full[stage], phase, g.err)) {
             ok = false;
             break;
@@ -277,7 +339,7 @@ __global__ void __launch_bounds__(kTCThreads, 1)
             const uint64_t a0 = tc::desc_kmajor_sw128(sa + k * 32);
             const uint64_t b0 = g.b_mn ? tc::desc_mn_sw128_atom32(sb + k * 1024, 4096)
                                        : tc::desc_kmajor_sw128(sb + k * 32);
-            const uint32_t first = (kb | k) != 0;
+            const uint32_t first = ((kb - kc) | k) != 0;
             if (SPLIT == 1) {
               tc::mma_tf32(d_tmem, a0, b0, idesc, first);
             } else {
@@ -296,6 +358,7 @@ __global__ void __launch_bounds__(kTCThreads, 1)
           }
         }
         tc::mma_commit(&tfull[acc]);
+       }
       }
       // Drain: every MMA issued above has completed once `done` fires.
       tc::mma_commit(done);
@@ -313,19 +376,67 @@ __global__ void __launch_bounds__(kTCThreads, 1)
     const bool vec_ok = ((g.ldd & 3) == 0) && ((((uintptr_t)g.D) & 15) == 0);
     float* box0 = staging + quad * 2 * 1024;
     int bsel = 0;
-    for (int64_t t = blockIdx.x; t < g.tiles; t += gridDim.x, ++local) {
-      const int per_b = g.m_tiles * g.n_tiles;
-      const int b = (int)(t / per_b);
-      const int mt = (int)((t % per_b) / g.n_tiles), nt = (int)((t % per_b) % g.n_tiles);
-      const int acc = local & 1;
-      const uint32_t aphase = (local >> 1) & 1;
-      if (!tc::mbar_wait(&tfull[acc], aphase, g.err)) break;
-      tc::tc_fence_after();
-      store_slices<BN>(g, &tmD, tmem_base, acc, quad, lane, mt * BM + quad * 32, nt, b, box0, bsel,
-                       vec_ok);
-      tc::tc_fence_before();
-      __syncwarp();
-      if (lane == 0) tc::mbar_arrive(&tempty[acc]);
+    if constexpr (SPLIT == 1) {
+      for (int64_t t = blockIdx.x; t < g.tiles; t += gridDim.x, ++local) {
+        const int per_b = g.m_tiles * g.n_tiles;
+        const int b = (int)(t / per_b);
+        const int mt = (int)((t % per_b) / g.n_tiles), nt = (int)((t % per_b) % g.n_tiles);
+        const int acc = local & 1;
+        const uint32_t aphase = (local >> 1) & 1;
+        if (!tc::mbar_wait(&tfull[acc], aphase, g.err)) break;
+        tc::tc_fence_after();
+        float alpha = g.alpha;
+        if (g.softmax) {
+          softmax_rows_tmem<BN>(tmem_base + ((uint32_t)(quad * 32) << 16), acc * BN, g.N, g.alpha);
+          alpha = 1.0f;
+        }
+        store_slices<BN>(g, &tmD, tmem_base, acc, quad, lane, mt * BM + quad * 32, nt, b, box0,
+                         bsel, vec_ok, alpha);
+        tc::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&tempty[acc]);
+      }
+    } else {
+      // 3xTF32: every chunk's partial sums are folded into the running sum
+      // (columns 2 BN + c); the last chunk's buffer receives the total and
+      // is stored as usual.
+      const uint32_t lane_addr = tmem_base + ((uint32_t)(quad * 32) << 16);
+      bool ok = true;
+      for (int64_t t = blockIdx.x; t < g.tiles && ok; t += gridDim.x) {
+        const int per_b = g.m_tiles * g.n_tiles;
+        const int b = (int)(t / per_b);
+        const int mt = (int)((t % per_b) / g.n_tiles), nt = (int)((t % per_b) % g.n_tiles);
+        for (int kc = 0; kc < kblocks; kc += tc::kChunkKBlocks, ++local) {
+          const int acc = local & 1;
+          const uint32_t aphase = (local >> 1) & 1;
+          if (!tc::mbar_wait(&tfull[acc], aphase, g.err)) {
+            ok = false;
+            break;
+          }
+          tc::tc_fence_after();
+          const bool last = kc + tc::kChunkKBlocks >= kblocks;
+          if (!(kc == 0 && last)) {
+#pragma unroll 1
+            for (int c0 = 0; c0 < BN; c0 += 32) {
+              if (nt * BN + c0 >= g.N) break;  // warp-uniform
+              tc::promote_chunk32(lane_addr, acc * BN + c0, 2 * BN + c0, kc == 0, last);
+            }
+            tc::tmem_st_wait();
+          }
+          if (last) {
+            float alpha = g.alpha;
+            if (g.softmax) {
+              softmax_rows_tmem<BN>(lane_addr, acc * BN, g.N, g.alpha);
+              alpha = 1.0f;
+            }
+            store_slices<BN>(g, &tmD, tmem_base, acc, quad, lane, mt * BM + quad * 32, nt, b, box0,
+                             bsel, vec_ok, alpha);
+          }
+          tc::tc_fence_before();
+          __syncwarp();
+          if (lane == 0) tc::mbar_arrive(&tempty[acc]);
+        }
+      }
     }
     if (g.tma_store && lane == 0) tc::bulk_wait_group<0>();
   }
@@ -519,7 +630,7 @@ __global__ void __launch_bounds__(kTCThreads, 1)
       const int row0 = g.pair_b ? quad * 32 : mt * (2 * BM) + (int)rank * BM + quad * 32;
       // (a missing last batch still takes part: its TMEM loads are warp-wide)
       store_slices<BN>(g, &tmD, tmem_base, acc, quad, lane, b < g.batches ? row0 : g.M, nt, b, box0,
-                       bsel, true);
+                       bsel, true, g.alpha);
       tc::tc_fence_before();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive_cluster(tempty0 + acc * (uint32_t)sizeof(uint64_t));
@@ -623,6 +734,7 @@ struct Problem {
   float* D;
   int64_t d_bs;
   int relu;
+  int softmax;  // row softmax of alpha * A B in the epilogue (N <= 128, see run_problem)
 };
 
 template <int BN, int SPLIT, int STAGES>
@@ -680,6 +792,7 @@ bool launch_tc(const Problem& p, const float* A0, const float* A1, const float* 
   g.d_batch_stride = p.d_bs;
   g.relu = p.relu;
   g.pair_b = 0;
+  g.softmax = p.softmax;
   g.batches = p.batches;
   g.tma_store = tma_store ? 1 : 0;
   g.b_mn = mn ? 1 : 0;
@@ -728,6 +841,7 @@ bool launch_tc2(const Problem& p, const float* A, const float* B, const char* op
   g.N = p.N;
   g.K = p.K;
   g.pair_b = pair_batches ? 1 : 0;
+  g.softmax = 0;
   g.batches = p.batches;
   g.m_tiles = pair_batches ? 1 : (int)cdiv(p.M, 2 * BM);
   g.n_tiles = (int)cdiv(p.N, BN);
@@ -830,15 +944,20 @@ bool split_batches(const float* src, int64_t in_bs, float* hi, float* lo, int64_
   return check_launch(op);
 }
 
-void run_problem(Problem p, const char* op) {
-  if ((int64_t)p.M * p.N * p.batches == 0) return;
+// Whether a problem runs on the tensor-core kernels (else the SIMT kernel).
+// TMA needs 16-byte aligned bases, row pitches and batch strides. The
+// reference's batch offsets (see matmul_impl) may overlap; the tensor maps
+// take the batch strides as given (overlapping reads are fine).
+bool tensor_core_eligible(const Problem& p) {
   const bool tiny = p.M < 64 || p.N < 16 || (int64_t)p.M * p.N * p.K < (1 << 18);
-  // TMA needs 16-byte aligned bases, row pitches and batch strides. The
-  // reference's batch offsets (see matmul_impl) may overlap; the tensor maps
-  // take the batch strides as given (overlapping reads are fine).
   const bool tma_ok = (p.K % 4 == 0) && aligned16(p.A) && aligned16(p.B) && (p.a_bs % 4 == 0) &&
                       p.K > 0;
-  if (tiny || !tma_ok) {
+  return !tiny && tma_ok;
+}
+
+void run_problem(Problem p, const char* op) {
+  if ((int64_t)p.M * p.N * p.batches == 0) return;
+  if (!tensor_core_eligible(p)) {
     launch_simt(p, op);
     return;
   }
@@ -876,6 +995,27 @@ void run_problem(Problem p, const char* op) {
   if (split) {  // the hi/lo planes are dense copies
     if (p.a_bs) p.a_bs = (int64_t)p.M * p.K;
     if (p.b_bs) p.b_bs = (int64_t)p.N * p.K;
+  }
+  if (p.softmax) {
+    // Row softmax in the epilogue: every row's N <= 128 columns in one tile.
+    if (split) {
+      float* a_hi = cur;
+      float* a_lo = a_hi + a_elems;
+      float* b_hi = a_lo + a_elems;
+      float* b_lo = b_hi + b_elems;
+      if (!split_batches(A, a_in_bs, a_hi, a_lo, (int64_t)p.M * p.K, a_elems, op) ||
+          !split_batches(B, b_in_bs, b_hi, b_lo, (int64_t)p.N * p.K, b_elems, op))
+        return;
+      if (p.N > 64)
+        launch_tc<128, 2, 3>(p, a_hi, a_lo, b_hi, b_lo, op);
+      else
+        launch_tc<64, 2, 4>(p, a_hi, a_lo, b_hi, b_lo, op);
+    } else if (p.N > 64) {
+      launch_tc<128, 1, 6>(p, A, nullptr, B, nullptr, op);
+    } else {
+      launch_tc<64, 1, 8>(p, A, nullptr, B, nullptr, op);
+    }
+    return;
   }
   if (!split) {
     // CTA pairs: N > 128, whole 256-row tiles' worth of M, TMA-storable D and
@@ -1041,11 +1181,14 @@ void gemm_nt_impl(Tensor* a, Tensor* b, Tensor* c, Tensor* out, float alpha, flo
 }
 
 // nnc_matmul semantics (ops.c:1607-1730), optional bias (row broadcast) + relu.
-void matmul_impl(Tensor* a, Tensor* b, Tensor* bias, Tensor* out, int relu, const char* op) {
+// nnc_matmul and its fused forms: D = alpha * A B (+ bias[n]) (relu), or the
+// softmax of alpha * A B over the last axis.
+void matmul_impl(Tensor* a, Tensor* b, Tensor* bias, Tensor* out, int relu, const char* op,
+                 float alpha = 1.0f, bool softmax = false) {
   OpScope scope(op);
   if (!f32(a, op, "a") || !f32(b, op, "b") || !f32(out, op, "output")) return;
   Problem p{};
-  p.alpha = 1.0f;
+  p.alpha = alpha;
   p.beta = 1.0f;
   p.A = (const float*)a->data;
   p.B = (const float*)b->data;
@@ -1104,6 +1247,17 @@ void matmul_impl(Tensor* a, Tensor* b, Tensor* bias, Tensor* out, int relu, cons
     p.C = (const float*)bias->data;
     p.c_mode = 1;
   }
+  if (softmax) {
+    // Fused into the epilogue when every row fits one tensor-core tile;
+    // otherwise the contraction, then the row softmax in place.
+    if (tensor_core_eligible(p) && p.N <= 128) {
+      p.softmax = 1;
+    } else {
+      run_problem(p, op);
+      if (ctx().status == NNC_CUDA_OK) nnc_softmax(out, out, -1);
+      return;
+    }
+  }
   run_problem(p, op);
 }
 
@@ -1130,6 +1284,12 @@ void nnc_gemm_nt_relu(Tensor* a, Tensor* b, Tensor* c, Tensor* output, float alp
 }
 void nnc_matmul(Tensor* a, Tensor* b, Tensor* output) {
   matmul_impl(a, b, nullptr, output, 0, "nnc_matmul");
+}
+void nnc_matmul_bias(Tensor* a, Tensor* b, Tensor* bias, Tensor* output) {
+  matmul_impl(a, b, bias, output, 0, "nnc_matmul_bias");
+}
+void nnc_matmul_scale_softmax(Tensor* a, Tensor* b, Tensor* output, float alpha) {
+  matmul_impl(a, b, nullptr, output, 0, "nnc_matmul_scale_softmax", alpha, true);
 }
 void nnc_matmul_relu(Tensor* a, Tensor* b, Tensor* bias, Tensor* output) {
   matmul_impl(a, b, bias, output, 1, "nnc_matmul_relu");

@@ -251,6 +251,62 @@ __device__ __forceinline__ void tmem_ld_16x256b_x2(uint32_t taddr, uint32_t (&r)
 __device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
+// Stores 16 consecutive 32-bit columns of this warp's 32 TMEM lanes (lane i
+// of the warp writes lane base + i).
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32"
+      " [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// Chunked accumulation of the 3xTF32 contractions. Measured on B200, the
+// error of a K-long 3xTF32 dot product accumulated in one TMEM accumulator
+// grows ~K^1.5 (normwise 8e-6 at K = 2048, 3.4e-5 at 8192): the accumulator
+// does not round to nearest, and its error follows the running sum. So the
+// MMA issuer restarts the accumulator every kChunkKBlocks k-blocks in
+// alternating TMEM buffers, and the epilogue warps fold each chunk's partial
+// sums into a running sum held in TMEM with round-to-nearest fp32 adds.
+// promote_chunk32 does that for one warp's 32 lanes x 32 columns: `part` is
+// the chunk's buffer column, `sum` the running sum's; the first chunk copies,
+// later ones add; the last chunk writes the total back over its own buffer,
+// where the tile's ordinary epilogue reads it. The caller waits for the
+// stores (tmem_st_wait) before releasing the buffer. A single-chunk
+// reduction needs no call.
+constexpr int kChunkKBlocks = 4;  // k-blocks of 32 (K = 128) per chunk
+__device__ __forceinline__ void promote_chunk32(uint32_t lane_addr, uint32_t part, uint32_t sum,
+                                                bool first, bool last) {
+  const uint32_t dst = lane_addr + (last ? part : sum);
+#pragma unroll 1
+  for (uint32_t h = 0; h < 32; h += 8) {  // 8 columns at a time (register budget)
+    uint32_t p[8], q[8];
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                 : "=r"(p[0]), "=r"(p[1]), "=r"(p[2]), "=r"(p[3]), "=r"(p[4]), "=r"(p[5]),
+                   "=r"(p[6]), "=r"(p[7])
+                 : "r"(lane_addr + part + h));
+    if (!first)
+      asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                   : "=r"(q[0]), "=r"(q[1]), "=r"(q[2]), "=r"(q[3]), "=r"(q[4]), "=r"(q[5]),
+                     "=r"(q[6]), "=r"(q[7])
+                   : "r"(lane_addr + sum + h));
+    tmem_ld_wait();
+    if (!first) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        p[j] = __float_as_uint(__fadd_rn(__uint_as_float(q[j]), __uint_as_float(p[j])));
+    }
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(
+                     dst + h),
+                 "r"(p[0]), "r"(p[1]), "r"(p[2]), "r"(p[3]), "r"(p[4]), "r"(p[5]), "r"(p[6]),
+                 "r"(p[7])
+                 : "memory");
+  }
+}
 
 // Shared-memory matrix descriptor: K-major operand in the 128-byte swizzle
 // layout written by TMA with CU_TENSOR_MAP_SWIZZLE_128B (rows of 128 bytes,

@@ -35,6 +35,12 @@ CONFIGS = [
     ("transformer_o1_b2048", "transformer", 2048, 1),
     ("transformer_o1_b256", "transformer", 256, 1),
     ("transformer_o1_b1", "transformer", 1, 1),
+    # configs 1 and 4 at -O3 (Gemm+Relu, MatMul+bias(+Relu), MatMul+scale+Softmax groups)
+    ("lenet5_o3_b8192", "lenet5", 8192, 3),
+    ("lenet5_o3_b16", "lenet5", 16, 3),
+    ("transformer_o3_b2048", "transformer", 2048, 3),
+    ("transformer_o3_b256", "transformer", 256, 3),
+    ("transformer_o3_b1", "transformer", 1, 3),
 ]
 
 

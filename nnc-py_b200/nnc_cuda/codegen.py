@@ -161,6 +161,18 @@ class ConvReluMaxPoolFusionPass(PassBase):
             dims = [int(d) for d in g.tensors[src].shape.dims]
             if len(dims) != 4:
                 continue
+            # Only where the pooled epilogue runs (the space-to-depth route:
+            # a stride-2 conv over at most 8 channels into at most 64, pooled
+            # by a stride-2 window of at most 3 with pad <= 1); elsewhere the
+            # entry point would only compose the two kernels through a
+            # temporary allocation.
+            cin = int(g.tensors[conv.inputs[0]].shape.dims[1])
+            pk = list(node.attrs.get("kernel_shape", [2, 2]))
+            ps = list(node.attrs.get("strides", [2, 2]))
+            pp = list(node.attrs.get("pads", [0, 0, 0, 0]))
+            if (list(conv.attrs.get("strides", [1, 1])) != [2, 2] or cin > 8 or dims[1] > 64 or ps != [2, 2]
+                    or max(pk) > 3 or max(pp) > 1):
+                continue
             meta = {"cuda_fused": "conv_relu_maxpool", "conv_out_hw": dims[2:4],
                     "pool_kernel": list(node.attrs.get("kernel_shape", [2, 2])),
                     "pool_strides": list(node.attrs.get("strides", [2, 2])),
@@ -172,6 +184,126 @@ class ConvReluMaxPoolFusionPass(PassBase):
             g.nodes.pop(node.name)
             g.tensors.pop(src, None)
             g.add_node(fused)
+
+
+def _single_consumer(g, tensor):
+    """The only consumer of `tensor`, or None (several, none, or a graph output)."""
+    cons = g.get_consumers(tensor)
+    if len(cons) != 1 or tensor in g.outputs:
+        return None
+    return cons[0]
+
+
+def _replace(g, old_nodes, new_node, dropped_tensors):
+    for n in old_nodes:
+        g.nodes.pop(n.name)
+    for t in dropped_tensors:
+        g.tensors.pop(t, None)
+    g.add_node(new_node)  # also drops nnc-py's cached dependency graph
+
+
+class GemmReluFusionPass(PassBase):
+    """Collapses Gemm -> ReLU into one GEMM node whose call is
+    nnc_gemm_relu / nnc_gemm_nt_relu (ReLU in the GEMM epilogue): the
+    Gemm+Relu group of the cuda target's O3 list (LeNet's fully connected
+    layers). nnc-py's own registry fuses MatMul+Relu
+    (pattern/fusion_patterns.py:147-155) but not Gemm+Relu. The node keeps op
+    type GEMM (PrepackLowering still picks the gemm_nt form) with metadata
+    ``cuda_fused = "gemm_relu"``."""
+
+    @property
+    def name(self) -> str:
+        return "CudaGemmReluFusion"
+
+    def _execute(self, ctx: CompileContext) -> None:
+        g = ctx.graph
+        for node in list(g.topological_sort()):
+            if node.op_type != OpType.GEMM or node.metadata.get("cuda_fused"):
+                continue
+            relu = _single_consumer(g, node.outputs[0])
+            if relu is None or relu.op_type != OpType.RELU:
+                continue
+            fused = Node(OpType.GEMM, f"{node.name}_relu", list(node.inputs), list(relu.outputs),
+                         dict(node.attrs), metadata={"cuda_fused": "gemm_relu", "fused_from": [node.name, relu.name]})
+            _replace(g, [node, relu], fused, [node.outputs[0]])
+
+
+class MatMulEpilogueFusionPass(PassBase):
+    """Collapses the transformer's MatMul epilogues into the MatMul call:
+
+    * MatMul -> Add(bias) with a constant bias of the MatMul's last extent
+      (N values, broadcast per row as the reference's modular add does) ->
+      ``nnc_matmul_bias``; after PatternFusion's add_relu, MatMul ->
+      FusedAddRelu(bias) -> FUSED_MATMUL_RELU [a, b, bias], which nnc-py's
+      CEmitter emits as ``nnc_matmul_relu(a, b, bias, out)``
+      (codegen/c_emitter.py:1143-1171);
+    * MatMul -> Div(s) (or Mul(1 / s)) by a constant power-of-two scalar ->
+      Softmax over the last axis -> ``nnc_matmul_scale_softmax(a, b, out,
+      1 / s)`` (scaled attention scores; x / s == x * (1 / s) exactly for a
+      power of two, so the fused scale is the reference's division).
+
+    Each intermediate must feed only the next node of its group.
+    """
+
+    @property
+    def name(self) -> str:
+        return "CudaMatMulEpilogueFusion"
+
+    @staticmethod
+    def _const_scalar(g, t):
+        if t in g.constants:
+            arr = np.asarray(g.constants[t])
+            if arr.size == 1:
+                return float(arr.reshape(-1)[0])
+        return None
+
+    def _execute(self, ctx: CompileContext) -> None:
+        g = ctx.graph
+        for node in list(g.topological_sort()):
+            if node.name not in g.nodes or node.op_type != OpType.MATMUL or node.metadata.get("cuda_fused"):
+                continue
+            if len(node.inputs) != 2:
+                continue
+            mm = node.outputs[0]
+            nxt = _single_consumer(g, mm)
+            if nxt is None:
+                continue
+            dims = [int(d) for d in g.tensors[mm].shape.dims]
+            if nxt.op_type in (OpType.ADD, OpType.FUSED_ADD_RELU) and len(nxt.inputs) == 2:
+                bias = nxt.inputs[1] if nxt.inputs[0] == mm else nxt.inputs[0]
+                if bias == mm or bias not in g.constants:
+                    continue
+                if list(np.asarray(g.constants[bias]).shape) != dims[-1:]:
+                    continue
+                if list(g.tensors[nxt.outputs[0]].shape.dims) != dims:
+                    continue
+                relu = nxt.op_type == OpType.FUSED_ADD_RELU
+                fused = Node(OpType.FUSED_MATMUL_RELU if relu else OpType.MATMUL,
+                             f"{node.name}_bias{'_relu' if relu else ''}", list(node.inputs) + [bias],
+                             list(nxt.outputs), dict(node.attrs),
+                             metadata={"fused_from": [node.name, nxt.name]} if relu else
+                             {"cuda_fused": "matmul_bias", "fused_from": [node.name, nxt.name]})
+                _replace(g, [node, nxt], fused, [mm])
+                continue
+            if nxt.op_type in (OpType.DIV, OpType.MUL) and len(nxt.inputs) == 2 and nxt.inputs[0] == mm:
+                s = self._const_scalar(g, nxt.inputs[1])
+                if s is None or s == 0.0 or not np.isfinite(s):
+                    continue
+                alpha = 1.0 / s if nxt.op_type == OpType.DIV else s
+                mant, _ = np.frexp(abs(alpha))
+                if alpha <= 0.0 or mant != 0.5:  # a positive power of two
+                    continue
+                scaled = nxt.outputs[0]
+                sm = _single_consumer(g, scaled)
+                if sm is None or sm.op_type != OpType.SOFTMAX:
+                    continue
+                axis = int(sm.attrs.get("axis", -1))
+                if axis not in (-1, len(dims) - 1):
+                    continue
+                fused = Node(OpType.MATMUL, f"{node.name}_scale_softmax", list(node.inputs), list(sm.outputs),
+                             dict(node.attrs), metadata={"cuda_fused": "matmul_scale_softmax", "alpha": alpha,
+                                                         "fused_from": [node.name, nxt.name, sm.name]})
+                _replace(g, [node, nxt, sm], fused, [mm, scaled])
 
 
 # Whether O3 fuses Conv+ReLU -> MaxPool into nnc_conv_relu_maxpool. On: on
@@ -186,8 +318,10 @@ def cuda_passes(opt_level: int, fuse_conv_relu_maxpool: bool | None = None) -> l
 
     O0-O2: nnc-py's own lists (passes/base.py:88-106). O3: cleanup, nnc-py's
     PatternFusion (conv_relu, add_relu, ...), the Conv+Add+Relu group (and
-    the Conv+Relu+MaxPool group when enabled), PrepackLowering (entry-point selection, Gemm weight prepack), liveness
-    and the cost_aware arena plan. nnc-py's NPU tiling passes are not used:
+    the Conv+Relu+MaxPool group when enabled), the Gemm+Relu group, the
+    MatMul epilogue groups (bias, bias+relu, scale+softmax), PrepackLowering
+    (entry-point selection, Gemm weight prepack), liveness and the
+    cost_aware arena plan. nnc-py's NPU tiling passes are not used:
     the GPU kernels tile internally.
     """
     from nnc_py.passes.dead_code_elimination import DeadCodeEliminationPass
@@ -202,6 +336,7 @@ def cuda_passes(opt_level: int, fuse_conv_relu_maxpool: bool | None = None) -> l
     fuse_pool = FUSE_CONV_RELU_MAXPOOL if fuse_conv_relu_maxpool is None else fuse_conv_relu_maxpool
     return [IdentityEliminationPass(), DeadCodeEliminationPass(), PatternFusionPass(), ConvAddReluFusionPass()] + (
         [ConvReluMaxPoolFusionPass()] if fuse_pool else []) + [
+        GemmReluFusionPass(), MatMulEpilogueFusionPass(),
         PrepackLoweringPass(), LivenessAnalysisPass(), MemoryPlanningPassV2()]
 
 
@@ -261,8 +396,8 @@ def channels_last_tensors(ctx: CompileContext) -> set[str]:
 
 # ------------------------------------------------------------- emitter ----
 class CudaEmitter(CEmitter):
-    """nnc-py's CEmitter with the cuda target's fused conv+add+relu and
-    conv+relu+maxpool calls."""
+    """nnc-py's CEmitter with the cuda target's fused calls: conv+add+relu,
+    conv+relu+maxpool, gemm+relu, matmul+bias and matmul+scale+softmax."""
 
     def _emit_includes(self, ctx: CompileContext) -> None:
         super()._emit_includes(ctx)
@@ -283,6 +418,27 @@ class CudaEmitter(CEmitter):
                     *m["pool_strides"][:2], m["pool_pads"][0], m["pool_pads"][1]]
             args = [f"&{sym[x]}", f"&{sym[w]}", bias, f"&{sym[node.outputs[0]]}"] + [str(int(v)) for v in vals]
             self.write_line(f"nnc_conv_relu_maxpool({', '.join(args)});")
+            return
+        fused = node.metadata.get("cuda_fused")
+        if fused == "gemm_relu":
+            # nnc-py's own Gemm call line (gemm or gemm_nt form), ReLU variant.
+            lines = []
+            write = self.write_line
+            self.write_line = lambda text="": lines.append(text)
+            try:
+                self._emit_gemm_call(ctx, node)
+            finally:
+                self.write_line = write
+            for text in lines:
+                text = text.replace("nnc_gemm_nt(", "nnc_gemm_nt_relu(").replace("nnc_gemm(", "nnc_gemm_relu(")
+                self.write_line(text)
+            return
+        if fused in ("matmul_bias", "matmul_scale_softmax"):
+            sym = ctx.tensor_symbols
+            args = [f"&{sym[t]}" for t in node.inputs] + [f"&{sym[node.outputs[0]]}"]
+            if fused == "matmul_scale_softmax":
+                args.append(f"{float(node.metadata['alpha'])!r}f")
+            self.write_line(f"nnc_{fused}({', '.join(args)});")
             return
         if node.metadata.get("cuda_fused") == "conv_add_relu":
             sym = ctx.tensor_symbols

@@ -474,6 +474,20 @@ void nnc_matmul(Tensor* a, Tensor* b, Tensor* out) { matmul_any(a, b, NULL, out,
  * (codegen/c_emitter.py:1143-1171), absent from the reference's ops.c:
  * restated as relu(matmul(a, b) + bias). */
 void nnc_matmul_relu(Tensor* a, Tensor* b, Tensor* bias, Tensor* out) { matmul_any(a, b, bias, out, 1); }
+/* MatMul -> Add(bias[N]) of the reference (ops.c:1607-1730, then the
+ * modular broadcast add of ops.c:90-118 with the bias as the short operand). */
+void nnc_matmul_bias(Tensor* a, Tensor* b, Tensor* bias, Tensor* out) { matmul_any(a, b, bias, out, 0); }
+/* MatMul -> scale -> Softmax over the last axis (ops.c:1607-1730, ops.c:260-310):
+ * the product rounded to fp32, times alpha (one rounding; exact for the
+ * power-of-two alpha the codegen fuses, equal to the reference's division by
+ * 1 / alpha), then the reference's softmax. */
+void nnc_matmul_scale_softmax(Tensor* a, Tensor* b, Tensor* out, float alpha) {
+    matmul_any(a, b, NULL, out, 0);
+    float* D = (float*)out->data;
+    const int64_t n = count_of(out);
+    for (int64_t i = 0; i < n; ++i) D[i] = D[i] * alpha;
+    nnc_softmax(out, out, -1);
+}
 
 /* ---------------------------------------------------------------------------
  * Data movement (ops.c:1510-1601, :1995-2086, :2173-2251).

@@ -38,6 +38,10 @@ BUILDS = [
     ("lenet5_o0_b1", "lenet5", 1, 0),
     ("lenet5_o1_b16", "lenet5", 16, 1),
     ("transformer_o1_b1", "transformer", 1, 1),
+    # The reference's batched MatMul offsets batches by the batch count
+    # (ops.c:1680-1700), not by the matrix size, so a sample's result depends
+    # on the batch it runs in: batch 256 needs its own build.
+    ("transformer_o1_b256", "transformer", 256, 1),
 ]
 
 

@@ -491,6 +491,29 @@ def fused_cases():
         tail = [_f(1.0), _f(1.0)] + ([_i(0), _i(1)] if op == "nnc_gemm_relu" else [])
         out.append(({"name": name, "op": op, "tol": "tc",
                      "args": [_t("a"), _t("b"), _t("c"), _o("out", (150, 90))] + tail}, {"a": a, "b": b, "c": c}))
+    for tag, sa, sb in (("2d", (300, 96), (96, 264)), ("batched", (3, 128, 256), (256, 72)),
+                        ("small", (5, 12), (12, 7))):
+        name = f"nnc_matmul_bias_{tag}"
+        r = rng_for(name)
+        a = r.standard_normal(sa).astype(np.float32)
+        b = r.standard_normal(sb).astype(np.float32)
+        bias = r.standard_normal((sb[-1],)).astype(np.float32)
+        out.append(({"name": name, "op": "nnc_matmul_bias", "tol": "tc",
+                     "args": [_t("a"), _t("b"), _t("bias"), _o("out", sa[:-1] + sb[-1:])]},
+                    {"a": a, "b": b, "bias": bias}))
+    # Scaled attention scores with a row softmax: rows of 128 (fused into the
+    # GEMM epilogue), of 72 (a partial tile), of 200 (longer than a tile: the
+    # contraction, then the softmax kernel) and a tiny case (SIMT contraction).
+    for tag, sa, sb, alpha in (("heads", (2, 4, 128, 64), (2, 4, 64, 128), 0.125),
+                               ("ragged", (3, 100, 40), (3, 40, 72), 0.5),
+                               ("long", (2, 130, 64), (2, 64, 200), 0.25),
+                               ("small", (6, 8), (8, 5), 2.0)):
+        name = f"nnc_matmul_scale_softmax_{tag}"
+        r = rng_for(name)
+        a = r.standard_normal(sa).astype(np.float32)
+        b = r.standard_normal(sb).astype(np.float32)
+        out.append(({"name": name, "op": "nnc_matmul_scale_softmax", "tol": "tc",
+                     "args": [_t("a"), _t("b"), _o("out", sa[:-1] + sb[-1:]), _f(alpha)]}, {"a": a, "b": b}))
     name = "nnc_matmul_relu_seeded"
     r = rng_for(name)
     a = r.standard_normal((128, 48)).astype(np.float32)

@@ -79,6 +79,36 @@ def test_o3_conv_relu_maxpool_group(tmp_path):
     assert off["calls"][:2] == ["nnc_conv_relu7x7_s2", "nnc_maxpool2d"]
 
 
+def test_o3_gemm_relu_group(tmp_path):
+    """LeNet's Gemm -> Relu pairs become nnc_gemm_nt_relu calls (ReLU in the
+    GEMM epilogue, PrepackLowering's gemm_nt form kept); the last Gemm feeds
+    the softmax and stays a plain gemm_nt."""
+    man = CG.compile_model(W.lenet5(4), tmp_path, opt_level=3)
+    calls = man["calls"]
+    assert calls.count("nnc_gemm_nt_relu") == 2 and calls.count("nnc_gemm_nt") == 1
+    assert "nnc_relu" not in calls[calls.index("nnc_flatten"):]
+    # LeNet's stride-1 convs keep their pool separate (no pooled epilogue).
+    assert calls.count("nnc_maxpool2d") == 2 and "nnc_conv_relu_maxpool" not in calls
+
+
+def test_o3_matmul_epilogue_groups(tmp_path):
+    """The transformer's MatMul -> Add(bias) [-> Relu] and MatMul -> Div(8) ->
+    Softmax chains each become one call; the residual Adds, LayerNorms and
+    the probs . V MatMul stay."""
+    man = CG.compile_model(W.transformer(1), tmp_path, opt_level=3)
+    calls = man["calls"]
+    layers = 4
+    assert calls.count("nnc_matmul_bias") == 5 * layers  # q, k, v, output projection, FFN2
+    assert calls.count("nnc_matmul_relu") == layers       # FFN1
+    assert calls.count("nnc_matmul_scale_softmax") == layers
+    assert calls.count("nnc_matmul") == layers            # probs . V
+    assert "nnc_softmax" not in calls and "nnc_div" not in calls and "nnc_add_relu" not in calls
+    assert calls.count("nnc_add") == 2 * layers           # residuals
+    src = (tmp_path / "model.c").read_text()
+    line = next(l for l in src.splitlines() if "nnc_matmul_scale_softmax(" in l)
+    assert line.strip().endswith("0.125f);")  # 1 / sqrt(64)
+
+
 def test_channels_last_assignment(tmp_path):
     man = CG.compile_model(W.resnet18(2), tmp_path, opt_level=3)
     cl = set(man["channels_last"])

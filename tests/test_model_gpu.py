@@ -91,8 +91,10 @@ def test_bench_config_matches_reference_x86_build(cuda_lib, bench_input, per_gpu
     C.assert_close(got[idx], want, MODEL_RTOL[prec], f"resnet18_o3_b{per_gpu} prec{prec}")
 
 
-def test_lenet5_matches_reference_x86_build(cuda_lib, golden):
-    m = _model("lenet5_o1_b16")
+@pytest.mark.parametrize("tag", ["lenet5_o1_b16", "lenet5_o3_b16"])
+def test_lenet5_matches_reference_x86_build(cuda_lib, golden, tag):
+    """-O1, and -O3 with the Gemm+Relu group (nnc_gemm_nt_relu)."""
+    m = _model(tag)
     m.load_constants(W.lenet5(16))
     for prec in (L.PRECISION_TF32, L.PRECISION_3XTF32):
         cuda_lib.nnc_cuda_set_precision(prec)
@@ -100,8 +102,11 @@ def test_lenet5_matches_reference_x86_build(cuda_lib, golden):
         C.assert_close(got, golden["lenet5_b16/output"], MODEL_RTOL[prec], f"lenet5 prec{prec}")
 
 
-def test_transformer_matches_reference_x86_build(cuda_lib, golden):
-    m = _model("transformer_o1_b1")
+@pytest.mark.parametrize("tag", ["transformer_o1_b1", "transformer_o3_b1"])
+def test_transformer_matches_reference_x86_build(cuda_lib, golden, tag):
+    """-O1, and -O3 with the MatMul epilogue groups (bias, bias+relu,
+    scale+softmax); the reference's x86 build runs the unfused ops."""
+    m = _model(tag)
     m.load_constants(W.transformer(1))
     for prec in (L.PRECISION_TF32, L.PRECISION_3XTF32):
         cuda_lib.nnc_cuda_set_precision(prec)

@@ -4,9 +4,11 @@ configurations that bench.py does not run), against the CPU oracle.
 Where the oracle would take minutes on the whole problem, it checks a
 subset whose values do not depend on the rest: rows of a GEMM (every output
 row is its own dot products), images of a convolution, slices of an
-element-wise op, the first samples of a model batch (samples are
-independent in every operator of these models). Row reductions, softmax and
-LayerNorm are checked whole.
+element-wise op, the first samples of a CNN batch (their samples are
+independent in every operator). The transformer's are not (the reference's
+batched MatMul offsets), so its batch-256 build is checked against the
+reference's own batch-256 build. Row reductions, softmax and LayerNorm are
+checked whole.
 """
 
 from __future__ import annotations
@@ -143,9 +145,9 @@ def golden():
 @pytest.mark.parametrize("prec", [L.PRECISION_TF32, L.PRECISION_3XTF32])
 @pytest.mark.parametrize("tag,model,batch,key,k", [
     ("lenet5_o1_b8192", "lenet5", 8192, "lenet5_b16", 16),
+    ("lenet5_o3_b8192", "lenet5", 8192, "lenet5_b16", 16),
     ("resnet18_o1_b64", "resnet18", 64, "resnet18_b2", 2),
     ("resnet18_o1_b256", "resnet18", 256, "resnet18_b2", 2),
-    ("transformer_o1_b256", "transformer", 256, "transformer_b1", 1),
 ])
 def test_sweep_models_first_samples_vs_reference(cuda_lib, golden, tag, model, batch, key, k, prec):
     """The sweep's model builds at their measured batch: the first k samples
@@ -163,3 +165,27 @@ def test_sweep_models_first_samples_vs_reference(cuda_lib, golden, tag, model, b
         m.free()
     assert np.array_equal(golden[f"{key}/input"], W.BUILDERS[model](k).input_array(k))
     C.assert_close(got[:k], golden[f"{key}/output"], MODEL_RTOL[prec], f"{tag}[:{k}] prec{prec}")
+
+
+@pytest.mark.parametrize("prec", [L.PRECISION_TF32, L.PRECISION_3XTF32])
+@pytest.mark.parametrize("tag", ["transformer_o1_b256", "transformer_o3_b256"])
+def test_transformer_b256_vs_reference(cuda_lib, golden, tag, prec):
+    """The transformer at batch 256. Its samples are not independent in the
+    reference: batched MatMul offsets batch b by b times the batch count
+    (ops.c:1680-1700), so the attention products of one sample read other
+    samples' rows and the batch-256 result differs from a batch-1 run. The
+    golden is the reference's own batch-256 x86 build (samples 0, 101, 255
+    kept), which the cuda build must reproduce quirk and all."""
+    from nnc_cuda.model import CudaModel
+
+    m = CudaModel(tag)
+    m.init(0)
+    try:
+        model = W.transformer(256)
+        m.load_constants(model)
+        cuda_lib.nnc_cuda_set_precision(prec)
+        got = m.run_host(model.input_array(256))
+    finally:
+        m.free()
+    keep = golden["transformer_b256/samples"]
+    C.assert_close(got[keep], golden["transformer_b256/output"], MODEL_RTOL[prec], f"{tag} prec{prec}")
