@@ -153,9 +153,19 @@ void nnc_cuda_graph_destroy(void* graph);
 
 /* ---- observability ------------------------------------------------------------
  * When enabled (or NNC_CUDA_TRACE=1 in the environment), every operator call
- * records CUDA events around its launches; nnc_cuda_trace_dump prints one line
- * per call (name, stream-ordered start/end in microseconds) to stderr and
- * clears the log. Synchronises the current stream. */
+ * records CUDA events around its launches and the bytes of the tensors it
+ * reads and writes. nnc_cuda_trace_dump prints the log to stdout in the line
+ * format of nnc-py's costmodel runtime (runtime/x86/costmodel.c:253-357),
+ *   [costmodel] #k op=<name> cu=<device> start=<t0> end=<t1> read=0
+ *               compute=<t1 - t0> write=0 in=<bytes>B out=<bytes>B
+ * one per call in issue order (k from 1), then
+ *   [costmodel] summary ops=<n> total_cycles=<last end> shared_ready=<same>
+ *   [costmodel] summary cu=<device> ready=<last end on that device>
+ * with times in nanoseconds of device time since the first call's start
+ * (where the costmodel prints simulated cycles; a kernel overlaps its reads
+ * and writes with its arithmetic, so the whole duration is compute). It
+ * returns the number of calls and clears the log. Synchronises the current
+ * stream. */
 void nnc_cuda_trace_enable(int on);
 int nnc_cuda_trace_dump(void);
 /* Programmatic access to the same log: nnc_cuda_trace_count synchronises

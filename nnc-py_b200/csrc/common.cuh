@@ -64,7 +64,15 @@ struct OpScope {
   ~OpScope();
   const char* name_;
   int slot_;
+  int prev_slot_;
+  bool prev_captured_;
 };
+// Bytes of a tensor's storage (nbytes, else numel x element size; 0 for NULL).
+uint64_t tensor_bytes(const Tensor* t);
+// Records on the innermost open OpScope of this thread (when it is traced)
+// the bytes of the tensors the call reads and writes (the trace's in= / out=);
+// a call's first annotation stands.
+void trace_io(uint64_t in_bytes, uint64_t out_bytes);
 
 // ---------------------------------------------------------------------------
 // Tensor metadata helpers (host).

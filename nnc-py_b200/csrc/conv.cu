@@ -2436,6 +2436,8 @@ void conv_impl(Tensor* input, Tensor* weight, Tensor* bias, Tensor* residual, Te
     fail(NNC_CUDA_ERR_INVALID, op, "expected 4-D tensors");
     return;
   }
+  trace_io(tensor_bytes(input) + tensor_bytes(weight) + tensor_bytes(bias) + tensor_bytes(residual),
+           tensor_bytes(output));
   const int N = (int)input->shape[0], C = (int)input->shape[1], H = (int)input->shape[2],
             W = (int)input->shape[3];
   const int Cout = (int)weight->shape[0];

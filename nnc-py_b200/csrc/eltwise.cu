@@ -177,6 +177,7 @@ template <int OP>
 void binary_dispatch(Tensor* a, Tensor* b, Tensor* out, const char* name) {
   OpScope scope(name);
   if (!check_f32(a, name, "a") || !check_f32(b, name, "b") || !check_f32(out, name, "out")) return;
+  trace_io(tensor_bytes(a) + tensor_bytes(b), tensor_bytes(out));
   const int64_t n = numel(out), an = numel(a), bn = numel(b);
   if (n == 0) return;
   // Which elements the reference writes, and how each operand is indexed
@@ -228,6 +229,7 @@ template <int OP>
 void unary_dispatch(Tensor* in, Tensor* out, const char* name, UnaryArgs p = {0.f, 0.f}) {
   OpScope scope(name);
   if (!check_f32(in, name, "input") || !check_f32(out, name, "output")) return;
+  trace_io(tensor_bytes(in), tensor_bytes(out));
   // The reference iterates over numel(output) (ops.c:231).
   const int64_t n = numel(out);
   if (n == 0) return;

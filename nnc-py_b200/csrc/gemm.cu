@@ -1093,6 +1093,7 @@ void gemm_impl(Tensor* a, Tensor* b, Tensor* c, Tensor* out, float alpha, float 
                int trans_a, int trans_b, int relu, const char* op) {
   OpScope scope(op);
   if (!f32(a, op, "a") || !f32(b, op, "b") || !f32(out, op, "output")) return;
+  trace_io(tensor_bytes(a) + tensor_bytes(b) + tensor_bytes(c), tensor_bytes(out));
   int M, N, K;
   if (a->ndim == 2 && b->ndim == 2) {
     M = (int)(trans_a ? a->shape[1] : a->shape[0]);
@@ -1146,6 +1147,7 @@ void gemm_nt_impl(Tensor* a, Tensor* b, Tensor* c, Tensor* out, float alpha, flo
                   const char* op) {
   OpScope scope(op);
   if (!f32(a, op, "a") || !f32(b, op, "b") || !f32(out, op, "output")) return;
+  trace_io(tensor_bytes(a) + tensor_bytes(b) + tensor_bytes(c), tensor_bytes(out));
   int M, N, K;
   if (a->ndim == 2 && b->ndim == 2) {
     M = (int)a->shape[0];
@@ -1187,6 +1189,7 @@ void matmul_impl(Tensor* a, Tensor* b, Tensor* bias, Tensor* out, int relu, cons
                  float alpha = 1.0f, bool softmax = false) {
   OpScope scope(op);
   if (!f32(a, op, "a") || !f32(b, op, "b") || !f32(out, op, "output")) return;
+  trace_io(tensor_bytes(a) + tensor_bytes(b) + tensor_bytes(bias), tensor_bytes(out));
   Problem p{};
   p.alpha = alpha;
   p.beta = 1.0f;

@@ -176,6 +176,7 @@ bool copy_bytes(void* dst, const void* src, size_t bytes, const char* op) {
 void flat_copy(Tensor* input, Tensor* output, const char* op) {
   OpScope scope(op);
   if (!valid_tensor(input, op, "input") || !valid_tensor(output, op, "output")) return;
+  trace_io(tensor_bytes(output), tensor_bytes(output));
   const int64_t n = numel(output);
   if (numel(input) < n) {
     fail(NNC_CUDA_ERR_INVALID, op, "input has fewer elements (%lld) than output (%lld)",
@@ -236,6 +237,7 @@ void nnc_identity(Tensor* input, Tensor* output) {
   const char* op = "nnc_identity";
   OpScope scope(op);
   if (!valid_tensor(input, op, "input") || !valid_tensor(output, op, "output")) return;
+  trace_io(tensor_bytes(input), tensor_bytes(output));
   // min(numel(out), numel(in)) floats, as in ops.c:2173-2181.
   const int64_t n = numel(output) < numel(input) ? numel(output) : numel(input);
   copy_bytes(output->data, input->data, (size_t)n * sizeof(float), op);
@@ -245,6 +247,7 @@ void nnc_transpose(Tensor* input, Tensor* output, int64_t* perm, int ndim) {
   const char* op = "nnc_transpose";
   OpScope scope(op);
   if (!valid_tensor(input, op, "input") || !valid_tensor(output, op, "output")) return;
+  trace_io(tensor_bytes(input), tensor_bytes(output));
   if (ndim < 1 || ndim > 8 || ndim != input->ndim || ndim != output->ndim) {
     fail(NNC_CUDA_ERR_INVALID, op, "ndim %d does not match the tensors (%d, %d)", ndim,
          input->ndim, output->ndim);
@@ -405,6 +408,7 @@ void nnc_concat(Tensor** inputs, Tensor* output, int num_inputs, int axis) {
     fail(NNC_CUDA_ERR_INVALID, op, "invalid arguments");
     return;
   }
+  trace_io(tensor_bytes(output), tensor_bytes(output));
   const int ax = axis < 0 ? axis + output->ndim : axis;
   if (ax < 0 || ax >= output->ndim) {
     fail(NNC_CUDA_ERR_INVALID, op, "axis %d out of range", axis);
@@ -447,6 +451,7 @@ void nnc_split(Tensor* input, Tensor** outputs, int num_outputs, int axis) {
     fail(NNC_CUDA_ERR_INVALID, op, "invalid arguments");
     return;
   }
+  trace_io(tensor_bytes(input), tensor_bytes(input));
   const int ax = axis < 0 ? axis + input->ndim : axis;
   if (ax < 0 || ax >= input->ndim) {
     fail(NNC_CUDA_ERR_INVALID, op, "axis %d out of range", axis);
@@ -476,6 +481,7 @@ void nnc_cuda_nchw_to_nhwc(Tensor* input, Tensor* output) {
   const char* op = "nnc_cuda_nchw_to_nhwc";
   OpScope scope(op);
   if (!valid_tensor(input, op, "input") || !valid_tensor(output, op, "output")) return;
+  trace_io(tensor_bytes(input), tensor_bytes(output));
   if (input->ndim != 4 || numel(output) != numel(input)) {
     fail(NNC_CUDA_ERR_INVALID, op, "expected two 4-D tensors of equal size");
     return;

@@ -256,6 +256,7 @@ void pool_impl(Tensor* input, Tensor* output, int kh, int kw, int sh, int sw, in
                const char* op) {
   OpScope scope(op);
   if (!valid_tensor(input, op, "input") || !valid_tensor(output, op, "output")) return;
+  trace_io(tensor_bytes(input), tensor_bytes(output));
   if (input->ndim != 4 || output->ndim != 4) {
     // The reference returns silently for non-4-D tensors (ops.c:332-334).
     fail(NNC_CUDA_ERR_INVALID, op, "expected 4-D tensors");

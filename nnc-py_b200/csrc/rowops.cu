@@ -585,6 +585,7 @@ bool f32_plain(const Tensor* t, const char* op, const char* name) {
 void reduce_impl(Tensor* in, Tensor* out, int axis, int mean, const char* op) {
   OpScope scope(op);
   if (!f32_plain(in, op, "input") || !f32_plain(out, op, "output")) return;
+  trace_io(tensor_bytes(in), tensor_bytes(out));
   int64_t outer, dim, inner;
   if (!decompose(in, axis, &outer, &dim, &inner, op)) return;
   if (numel(out) != outer * inner) {
@@ -616,6 +617,7 @@ void nnc_softmax(Tensor* input, Tensor* output, int axis) {
   const char* op = "nnc_softmax";
   OpScope scope(op);
   if (!f32_plain(input, op, "input") || !f32_plain(output, op, "output")) return;
+  trace_io(tensor_bytes(input), tensor_bytes(output));
   int64_t outer, dim, inner;
   if (!decompose(input, axis, &outer, &dim, &inner, op)) return;
   if (numel(output) < outer * dim * inner) {
@@ -677,6 +679,7 @@ void nnc_layernorm(Tensor* input, Tensor* scale, Tensor* bias, Tensor* output, i
   OpScope scope(op);
   if (!f32_plain(input, op, "input") || !f32_plain(output, op, "output")) return;
   if ((scale && !f32_plain(scale, op, "scale")) || (bias && !f32_plain(bias, op, "bias"))) return;
+  trace_io(tensor_bytes(input) + tensor_bytes(scale) + tensor_bytes(bias), tensor_bytes(output));
   int64_t outer, norm, inner;
   if (!decompose(input, axis, &outer, &norm, &inner, op)) return;
   if (numel(output) < outer * norm * inner) {

@@ -58,6 +58,8 @@ __global__ void bounded_wait_selftest_kernel(int* err, uint64_t limit_ns) {
 struct TraceRec {
   const char* name;
   cudaEvent_t start, stop;
+  uint64_t in_bytes = 0, out_bytes = 0;  // tensor bytes the call reads / writes
+  int device = 0;
 };
 thread_local std::vector<TraceRec> t_trace;
 int g_trace_on = -1;  // -1: read NNC_CUDA_TRACE on first use
@@ -209,29 +211,43 @@ void* workspace(size_t bytes, const char* op) {
   return p;
 }
 
-OpScope::OpScope(const char* name) : name_(name), slot_(-1) {
+// The innermost traced call of this thread (trace_io annotates it).
+thread_local int t_scope_slot = -1;
+thread_local bool t_scope_captured = false;
+
+OpScope::OpScope(const char* name)
+    : name_(name), slot_(-1), prev_slot_(t_scope_slot), prev_captured_(t_scope_captured) {
   int dev = 0;
   if (cudaGetDevice(&dev) == cudaSuccess && dev >= 0 && dev < kMaxDevices) ctx().device = dev;
+  t_scope_slot = -1;
   if (!trace_on()) return;
   if (t_capturing) {
     // Captured call: event-record nodes in the graph (re-bound to fresh
     // events at every traced replay by nnc_cuda_graph_launch).
     if (t_capture_pool.size() < 2) return;
     TraceRec r{name, capture_event(), capture_event()};
+    r.device = ctx().device;
     cudaEventRecordWithFlags(r.start, ctx().stream, cudaEventRecordExternal);
     t_capture_ops.push_back(r);
     slot_ = (int)t_capture_ops.size() - 1;
+    t_scope_slot = slot_;
+    t_scope_captured = true;
     return;
   }
   TraceRec r{name, nullptr, nullptr};
+  r.device = ctx().device;
   cudaEventCreate(&r.start);
   cudaEventCreate(&r.stop);
   cudaEventRecord(r.start, ctx().stream);
   t_trace.push_back(r);
   slot_ = (int)t_trace.size() - 1;
+  t_scope_slot = slot_;
+  t_scope_captured = false;
 }
 
 OpScope::~OpScope() {
+  t_scope_slot = prev_slot_;
+  t_scope_captured = prev_captured_;
   if (slot_ < 0) return;
   if (t_capturing) {
     if (slot_ < (int)t_capture_ops.size())
@@ -239,6 +255,24 @@ OpScope::~OpScope() {
     return;
   }
   if (slot_ < (int)t_trace.size()) cudaEventRecord(t_trace[slot_].stop, ctx().stream);
+}
+
+uint64_t tensor_bytes(const Tensor* t) {
+  if (!t) return 0;
+  if (t->nbytes > 0) return (uint64_t)t->nbytes;
+  if (t->ndim > 0 && !t->shape) return 0;
+  return (uint64_t)numel(t) * elem_size(elem_type(t));
+}
+
+void trace_io(uint64_t in_bytes, uint64_t out_bytes) {
+  if (t_scope_slot < 0) return;
+  std::vector<TraceRec>& v = t_scope_captured ? t_capture_ops : t_trace;
+  // The first annotation of a call wins: helpers it runs (a conv into a
+  // temporary, a softmax after a contraction) do not overwrite it.
+  if (t_scope_slot < (int)v.size() && v[t_scope_slot].in_bytes == 0 && v[t_scope_slot].out_bytes == 0) {
+    v[t_scope_slot].in_bytes = in_bytes;
+    v[t_scope_slot].out_bytes = out_bytes;
+  }
 }
 
 }  // namespace nnc
@@ -359,6 +393,8 @@ struct GraphOp {
   const char* name;
   cudaGraphNode_t start_node, stop_node;
   cudaEvent_t own_start, own_stop;
+  uint64_t in_bytes, out_bytes;
+  int device;
 };
 
 struct NncGraph {
@@ -388,7 +424,7 @@ void release_capture_trace() {
 // one trace record per captured call (this replay's device times).
 bool bind_trace_events(NncGraph* g, const char* op) {
   for (const GraphOp& o : g->ops) {
-    TraceRec r{o.name, nullptr, nullptr};
+    TraceRec r{o.name, nullptr, nullptr, o.in_bytes, o.out_bytes, o.device};
     if (!check_cuda(cudaEventCreate(&r.start), op, "cudaEventCreate") ||
         !check_cuda(cudaEventCreate(&r.stop), op, "cudaEventCreate"))
       return false;
@@ -492,7 +528,7 @@ void* nnc_cuda_graph_end(void) {
     std::vector<cudaGraphNode_t> nodes(n);
     if (n) cudaGraphGetNodes(graph, nodes.data(), &n);
     for (const TraceRec& r : t_capture_ops)
-      g->ops.push_back(GraphOp{r.name, nullptr, nullptr, r.start, r.stop});
+      g->ops.push_back(GraphOp{r.name, nullptr, nullptr, r.start, r.stop, r.in_bytes, r.out_bytes, r.device});
     for (cudaGraphNode_t node : nodes) {
       cudaGraphNodeType type;
       if (cudaGraphNodeGetType(node, &type) != cudaSuccess || type != cudaGraphNodeTypeEventRecord)
@@ -597,14 +633,39 @@ int nnc_cuda_trace_dump(void) {
   cudaStreamSynchronize(ctx().stream);
   if (t_trace.empty()) return 0;
   const int n = (int)t_trace.size();
+  // The costmodel runtime's line format (one line per call, then a summary;
+  // nnc-py runtime/x86/costmodel.c): times are device nanoseconds since the
+  // first traced call's start instead of simulated cycles, `cu` is the
+  // device, and the whole duration counts as compute (a kernel overlaps its
+  // reads and writes with its arithmetic).
   cudaEvent_t t0 = t_trace[0].start;
+  uint64_t total = 0;
+  std::vector<std::pair<int, uint64_t>> ready;  // (device, last end)
   for (int i = 0; i < n; ++i) {
     float s = 0.f, e = 0.f;
     cudaEventElapsedTime(&s, t0, t_trace[i].start);
     cudaEventElapsedTime(&e, t0, t_trace[i].stop);
-    fprintf(stderr, "[nnc_cuda_trace] #%d op=%s start_us=%.1f end_us=%.1f dur_us=%.1f\n", i,
-            t_trace[i].name, s * 1e3, e * 1e3, (e - s) * 1e3);
+    const uint64_t start = (uint64_t)(s * 1e6 + 0.5), end = (uint64_t)(e * 1e6 + 0.5);
+    const TraceRec& r = t_trace[i];
+    printf("[costmodel] #%d op=%s cu=%d start=%llu end=%llu read=0 compute=%llu write=0 in=%lluB "
+           "out=%lluB\n",
+           i + 1, r.name, r.device, (unsigned long long)start, (unsigned long long)end,
+           (unsigned long long)(end > start ? end - start : 0), (unsigned long long)r.in_bytes,
+           (unsigned long long)r.out_bytes);
+    if (end > total) total = end;
+    bool found = false;
+    for (auto& d : ready)
+      if (d.first == r.device) {
+        if (end > d.second) d.second = end;
+        found = true;
+      }
+    if (!found) ready.push_back({r.device, end});
   }
+  printf("[costmodel] summary ops=%d total_cycles=%llu shared_ready=%llu\n", n,
+         (unsigned long long)total, (unsigned long long)total);
+  for (auto& d : ready)
+    printf("[costmodel] summary cu=%d ready=%llu\n", d.first, (unsigned long long)d.second);
+  fflush(stdout);
   nnc_cuda_trace_clear();
   return n;
 }
