@@ -89,8 +89,9 @@ def tf32_peak(pk: dict, clocks: dict | None) -> tuple[float, str]:
 
 
 GOLDEN = ROOT / "tests" / "golden" / "bench_resnet18_o3.npz"
-# Normwise tolerance of whole-model logits against the reference's x86 build.
-PARITY_RTOL = {"tf32": 2e-2, "3xtf32": 1e-4}
+# Normwise tolerance of whole-model logits against the reference's x86 build
+# (the model-level tolerances of the tests, tests/opcases.MODEL_RTOL).
+PARITY_RTOL = {"tf32": 5e-3, "3xtf32": 1e-5}
 
 
 def parity(logits, precision: str) -> dict:

@@ -227,9 +227,10 @@ def op_sweep(so, torch, timer: Timer, pk: dict) -> list[dict]:
 MODEL_FLOPS = {"lenet5": 0.833e6, "resnet18": 3.628e9, "transformer": 0.872e9}
 
 
-MODELS = (("lenet5_o1_b8192", "lenet5", 8192), ("resnet18_o1_b64", "resnet18", 64),
-          ("resnet18_o1_b256", "resnet18", 256), ("transformer_o1_b256", "transformer", 256),
-          ("transformer_o1_b2048", "transformer", 2048))
+MODELS = (("lenet5_o1_b8192", "lenet5", 8192), ("lenet5_o3_b8192", "lenet5", 8192),
+          ("resnet18_o1_b64", "resnet18", 64), ("resnet18_o1_b256", "resnet18", 256),
+          ("transformer_o1_b256", "transformer", 256), ("transformer_o3_b256", "transformer", 256),
+          ("transformer_o1_b2048", "transformer", 2048), ("transformer_o3_b2048", "transformer", 2048))
 
 
 def model_runs(so, torch, pk: dict, reps: int, only_model: str | None = None) -> list[dict]:

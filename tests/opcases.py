@@ -198,6 +198,26 @@ def assert_close(got, want, tol, what=""):
 
 # Tolerances of the tensor-core contractions (normwise rtol, see assert_close).
 TC_RTOL = {0: 2e-3, 1: 1e-5}  # NNC_CUDA_PRECISION_TF32, _3XTF32
+# Whole models against the reference's x86 build (normwise). Measured on
+# B200: TF32 1.7e-3 (ResNet-18) to 2.6e-3 (transformer); 3xTF32 (chunked
+# accumulation) 3.5e-6 (ResNet-18), 3.9e-6 (the batch-1024 bench images),
+# 2.8e-6 (transformer), 3.7e-7 (LeNet-5).
+MODEL_RTOL = {0: 5e-3, 1: 1e-5}
+# Per-element bound of a contraction's error relative to the sum of the
+# magnitudes of its products, |d_ij| <= rtol * sum_k |a_ik| |b_kj| (the
+# standard dot-product error bound; holds even where the result cancels).
+DOT_RTOL = {0: 1e-3, 1: 1e-6}
+
+
+def assert_dot_close(got, want, absdot, tol, what=""):
+    """Per-element check of a contraction: |got - want| <= tol * absdot, with
+    absdot the same contraction of |a| and |b| (computed by the oracle)."""
+    assert got.shape == want.shape == absdot.shape, what
+    err = np.abs(got.astype(np.float64) - want.astype(np.float64))
+    lim = tol * absdot.astype(np.float64) + 1e-30
+    bad = np.flatnonzero(err > lim)
+    assert bad.size == 0, (f"{what}: {bad.size} of {err.size} exceed {tol} x sum|a||b|; worst "
+                           f"{float(np.max(err / lim)) * tol:.3g}")
 
 
 # --------------------------------------------------------- seeded cases --

@@ -53,6 +53,8 @@ def test_gemm_sweep_sizes_rows_vs_oracle(cuda_lib, n, op, prec):
     sub = {"name": op, "op": op, "args": [C._t("a"), C._t("b"), C.NULL, C._o("out", (len(rows), n))] + tail}
     want = C.run_host(_oracle(), sub, {"a": np.ascontiguousarray(a[rows]), "b": b})["out"]
     C.assert_close(got[rows], want, C.TC_RTOL[prec], f"{op} {n}^3 prec{prec}")
+    absdot = C.run_host(_oracle(), sub, {"a": np.abs(a[rows]), "b": np.abs(b)})["out"]
+    C.assert_dot_close(got[rows], want, absdot, C.DOT_RTOL[prec], f"{op} {n}^3 prec{prec} per element")
 
 
 # ------------------------------------------------------------------ conv --
@@ -78,6 +80,13 @@ def test_conv_sweep_sizes_images_vs_oracle(cuda_lib, ch, prec):
     want = C.run_host(_oracle(), case(len(imgs)), {"x": np.ascontiguousarray(x[imgs]), "w": w, "b": b})["out"]
     C.assert_close(got[imgs], want, C.TC_RTOL[prec], f"conv {ch} NCHW prec{prec}")
     C.assert_close(got_cl[imgs], want, C.TC_RTOL[prec], f"conv {ch} channels-last prec{prec}")
+    # Per element against sum |x| |w| (the bias, below 0.03, is left out of
+    # the bound's sum but is exact in both).
+    absdot = C.run_host(_oracle(), case(len(imgs)), {"x": np.abs(x[imgs]), "w": np.abs(w),
+                                                       "b": np.zeros_like(b)})["out"]
+    absdot = absdot + np.abs(b)[None, :, None, None]
+    C.assert_dot_close(got[imgs], want, absdot, C.DOT_RTOL[prec], f"conv {ch} NCHW prec{prec} per element")
+    C.assert_dot_close(got_cl[imgs], want, absdot, C.DOT_RTOL[prec], f"conv {ch} channels-last prec{prec} per element")
 
 
 # ------------------------------------------------------------- row ops --
@@ -133,7 +142,7 @@ def test_eltwise_2pow28_slices_vs_oracle(cuda_lib, op, tol):
 
 # ---------------------------------------------------------------- models --
 GOLDEN = pathlib.Path(__file__).resolve().parent / "golden" / "models.npz"
-MODEL_RTOL = {L.PRECISION_TF32: 2e-2, L.PRECISION_3XTF32: 1e-4}
+MODEL_RTOL = C.MODEL_RTOL
 
 
 @pytest.fixture(scope="module")
