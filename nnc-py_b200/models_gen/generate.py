@@ -41,7 +41,14 @@ CONFIGS = [
     ("transformer_o3_b2048", "transformer", 2048, 3),
     ("transformer_o3_b256", "transformer", 256, 3),
     ("transformer_o3_b1", "transformer", 1, 3),
+    # debug builds (every intermediate tensor dumped; layer-by-layer parity)
+    ("resnet18_o1_b1_debug", "resnet18", 1, 1),
+    ("lenet5_o1_b1_debug", "lenet5", 1, 1),
 ]
+
+
+def is_debug(d: str) -> bool:
+    return d.endswith("_debug")
 
 
 def generate(only: str | None = None) -> list[str]:
@@ -51,7 +58,7 @@ def generate(only: str | None = None) -> list[str]:
     for d, model, batch, opt in CONFIGS:
         if only and d != only:
             continue
-        codegen.compile_model(workloads.BUILDERS[model](batch), HERE / d, opt_level=opt)
+        codegen.compile_model(workloads.BUILDERS[model](batch), HERE / d, opt_level=opt, debug=is_debug(d))
         done.append(d)
     return done
 

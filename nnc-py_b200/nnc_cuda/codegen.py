@@ -499,12 +499,19 @@ class CudaBackend(BackendBase):
         arena, arena_bytes = self._arena_offsets(ctx, plan)
         consts, const_bytes = self._const_layout(ctx)
         entry = ctx.metadata.get("entry_point", "nnc_run")
-        res.add_file("model.c", CudaEmitter().emit(ctx), "source")
+        model_c = CudaEmitter().emit(ctx)
+        if self.debug_mode:
+            model_c = inject_debug_dumps(model_c, ctx)
+        res.add_file("model.c", model_c, "source")
         res.add_file("model.h", self._model_h(ctx, entry), "header")
         res.add_file("tensors.c", self._tensors_c(ctx, arena, arena_bytes, consts, const_bytes, layout), "source")
         res.add_file("constants_loader.c", _CONSTANTS_LOADER, "source")
-        res.add_file("model_runtime.c", _MODEL_RUNTIME, "source")
-        res.add_file("test_runner.c", self._runner_c(ctx), "source")
+        res.add_file("model_runtime.c", _MODEL_RUNTIME + (_DEBUG_RUNTIME if self.debug_mode else ""), "source")
+        runner = self._runner_c(ctx)
+        if self.debug_mode:
+            runner = runner.replace("    int avail = 0;\n", "    int avail = 0;\n"
+                                    "    if (nnc_model_set_debug_file(\"nnc_debug_output.txt\") != 0) return 1;\n", 1)
+        res.add_file("test_runner.c", runner, "source")
         res.add_file("Makefile", _MAKEFILE, "build")
         manifest = {
             "graph": ctx.graph.name,
@@ -572,6 +579,11 @@ class CudaBackend(BackendBase):
     def _model_h(self, ctx, entry):
         ins = ", ".join(ctx.tensor_symbols[n] for n in ctx.graph.inputs)
         outs = ", ".join(ctx.tensor_symbols[n] for n in ctx.graph.outputs)
+        debug_decls = ("/* Debug build: every intermediate tensor is dumped after its node, in\n"
+                       " * nnc-py's x86 debug-dump text format, to this file (NULL: stdout). */\n"
+                       "int nnc_model_set_debug_file(const char* path);\n"
+                       "void nnc_model_debug_dump(const char* name, int node_idx, const Tensor* t);\n"
+                       ) if self.debug_mode else ""
         return f"""/* Auto-generated by nnc_cuda (cuda target) - DO NOT EDIT */
 #ifndef NNC_MODEL_H
 #define NNC_MODEL_H
@@ -608,7 +620,7 @@ Tensor* nnc_model_output(int i);
 /* Synchronous host-buffer forward on the selected device: input host ->
  * device, forward, output device -> host (pinned buffers recommended). */
 int nnc_model_run_host(const void* input, void* output);
-
+{debug_decls}
 #ifdef __cplusplus
 }}
 #endif
@@ -761,6 +773,95 @@ int nnc_model_run_host(const void* input, void* output) {
     return nnc_cuda_get_last_error();
 }
 """
+
+# Debug builds (CudaBackend(debug_mode=True)): every intermediate tensor is
+# written after its node in the text format of nnc-py's x86 debug builds
+# (codegen/x86_emitters/model_source.py, debug dumps), which nnc-py's
+# DebugOutputParser (tools/debug_compare.py) reads: DEBUG_TENSOR_START
+# <name> <node index>, SHAPE <ndim>, DIM <i> <extent> lines, DATA_START, one
+# "%f" line per element in logical (NCHW, row-major) order, DATA_END,
+# DEBUG_TENSOR_END <name>. Channels-last tensors are reordered to NCHW.
+_DEBUG_RUNTIME = r"""
+/* ---- debug dumps (debug builds only) ---- */
+#include <stdlib.h>
+static FILE* g_debug_file = NULL;
+
+/* Where the dumps go (NULL: stdout, as in nnc-py's x86 debug builds). */
+int nnc_model_set_debug_file(const char* path) {
+    if (g_debug_file) fclose(g_debug_file);
+    g_debug_file = NULL;
+    if (!path) return 0;
+    g_debug_file = fopen(path, "w");
+    return g_debug_file ? 0 : 1;
+}
+
+/* Waits for the current stream, copies the tensor to the host and writes it. */
+void nnc_model_debug_dump(const char* name, int node_idx, const Tensor* t) {
+    FILE* f = g_debug_file ? g_debug_file : stdout;
+    if (report(cudaStreamSynchronize((cudaStream_t)nnc_cuda_get_stream()), "debug dump sync")) return;
+    size_t n = 1;
+    for (int i = 0; i < t->ndim; ++i) n *= (size_t)t->shape[i];
+    float* h = (float*)malloc(n * sizeof(float) + 1);
+    float* o = (float*)malloc(n * sizeof(float) + 1);
+    if (!h || !o) { free(h); free(o); return; }
+    if (n && report(cudaMemcpy(h, t->data, n * sizeof(float), cudaMemcpyDeviceToHost), "debug dump copy")) {
+        free(h); free(o); return;
+    }
+    const float* v = h;
+    if ((t->dtype & NNC_CUDA_TAG_NHWC) && t->ndim == 4) {
+        const size_t N = (size_t)t->shape[0], C = (size_t)t->shape[1], H = (size_t)t->shape[2], W = (size_t)t->shape[3];
+        for (size_t b = 0; b < N; ++b)
+            for (size_t y = 0; y < H; ++y)
+                for (size_t x = 0; x < W; ++x)
+                    for (size_t c = 0; c < C; ++c)
+                        o[((b * C + c) * H + y) * W + x] = h[((b * H + y) * W + x) * C + c];
+        v = o;
+    }
+    fprintf(f, "DEBUG_TENSOR_START %s %d\n", name, node_idx);
+    fprintf(f, "SHAPE %d\n", t->ndim);
+    for (int i = 0; i < t->ndim; ++i) fprintf(f, "DIM %d %d\n", i, (int)t->shape[i]);
+    fprintf(f, "DATA_START\n");
+    for (size_t i = 0; i < n; ++i) fprintf(f, "%f\n", v[i]);
+    fprintf(f, "DATA_END\n");
+    fprintf(f, "DEBUG_TENSOR_END %s\n\n", name);
+    fflush(f);
+    free(h);
+    free(o);
+}
+"""
+
+
+def inject_debug_dumps(model_c: str, ctx: CompileContext) -> str:
+    """Adds, after each node call in nnc_run, a dump of the node's
+    non-constant outputs (node index = position among the non-constant nodes
+    in topological order, as nnc-py's x86 debug builds number them)."""
+    g = ctx.graph
+    after: dict[str, list[str]] = {}
+    idx = 0
+    for node in g.topological_sort():
+        if node.op_type == OpType.CONSTANT:
+            continue
+        sym = ctx.node_symbols.get(node.name, node.name)
+        after[f"{sym}();"] = [
+            f'    nnc_model_debug_dump("{t}", {idx}, &{ctx.tensor_symbols[t]});'
+            for t in node.outputs if t in g.tensors and t not in g.constants]
+        idx += 1
+    out, in_run = [], False
+    for line in model_c.split("\n"):
+        out.append(line)
+        if line.startswith("void nnc_run(void)"):
+            in_run = True
+            continue
+        if in_run:
+            if line.startswith("}"):
+                in_run = False
+            else:
+                out.extend(after.get(line.strip(), []))
+    src = "\n".join(out)
+    decl = "void nnc_model_debug_dump(const char* name, int node_idx, const Tensor* t);\n"
+    first_fn = src.index("void node_") if "void node_" in src else src.index("void nnc_run")
+    return src[:first_fn] + decl + "\n" + src[first_fn:]
+
 
 _CONSTANTS_LOADER = r"""/* Auto-generated by nnc_cuda (cuda target) - DO NOT EDIT
  * Loads nnc-py's NNCB v1 constants container: 'NNCB', u32 version (1),
@@ -966,7 +1067,8 @@ clean:
 
 
 def compile_model(model: Model, out_dir: str | pathlib.Path, opt_level: int = 3,
-                  channels_last: bool = True, fuse_conv_relu_maxpool: bool | None = None) -> dict[str, Any]:
+                  channels_last: bool = True, fuse_conv_relu_maxpool: bool | None = None,
+                  debug: bool = False) -> dict[str, Any]:
     """Runs the cuda target on a workload Model and writes the artifacts."""
     ctx = CompileContext(to_nnc_graph(model), "cuda", opt_level)
     ctx.metadata["entry_point"] = "nnc_run"
@@ -974,7 +1076,7 @@ def compile_model(model: Model, out_dir: str | pathlib.Path, opt_level: int = 3,
     for p in cuda_passes(opt_level, fuse_conv_relu_maxpool):
         pm.register(p)
     pm.run(ctx)
-    res = CudaBackend(channels_last=channels_last).generate(ctx)
+    res = CudaBackend(debug_mode=debug, channels_last=channels_last).generate(ctx)
     out = pathlib.Path(out_dir)
     out.mkdir(parents=True, exist_ok=True)
     for a in res.files:

@@ -26,6 +26,11 @@
 
 extern Tensor MODEL_INPUT;
 extern Tensor MODEL_OUTPUT;
+#ifdef NNC_DEBUG_DUMP
+/* nnc-py's x86 debug builds print every intermediate tensor through this
+ * stream (declared extern in their model.c); NULL selects stdout. */
+FILE* debug_file = NULL;
+#endif
 int nnc_load_constants(const char* path);
 
 static double now(void) {

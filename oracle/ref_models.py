@@ -42,6 +42,9 @@ BUILDS = [
     # (ops.c:1680-1700), not by the matrix size, so a sample's result depends
     # on the batch it runs in: batch 256 needs its own build.
     ("transformer_o1_b256", "transformer", 256, 1),
+    # Debug builds: every intermediate tensor printed (nnc-py's debug dump).
+    ("resnet18_o1_b1_debug", "resnet18", 1, 1),
+    ("lenet5_o1_b1_debug", "lenet5", 1, 1),
 ]
 
 
@@ -61,7 +64,8 @@ def build_one(ref: pathlib.Path, tag: str, model_name: str, batch: int, opt: int
     for p in PassManager.get_default_passes(opt):
         pm.register(p)
     pm.run(ctx)
-    res = X86Backend().generate(ctx)
+    debug = tag.endswith("_debug")
+    res = X86Backend(debug_mode=debug).generate(ctx)
     out = HERE / "_ref" / tag
     shutil.rmtree(out, ignore_errors=True)
     out.mkdir(parents=True)
@@ -74,6 +78,8 @@ def build_one(ref: pathlib.Path, tag: str, model_name: str, batch: int, opt: int
     cmd = ["gcc", "-O3", "-std=c11", "-D_GNU_SOURCE", f"-I{ref / 'runtime' / 'include'}", f"-I{out}",
            f"-DMODEL_INPUT={sym_in}", f"-DMODEL_OUTPUT={sym_out}", *srcs, str(ref / "runtime" / "x86" / "ops.c"),
            str(HERE / "ref_model_main.c"), "-lm", "-lpthread", "-o", str(out / "model_x86")]
+    if debug:
+        cmd.insert(1, "-DNNC_DEBUG_DUMP")
     subprocess.run(cmd, check=True, capture_output=True, text=True)
     consts = [[n, ctx.tensor_symbols[n]] for n in ctx.graph.constants]
     (out / "build.json").write_text(json.dumps({"model": model_name, "batch": batch, "opt_level": opt,

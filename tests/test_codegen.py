@@ -27,7 +27,7 @@ def test_committed_sources_are_up_to_date(tmp_path):
 
     for d, model, batch, opt in generate.CONFIGS:
         out = tmp_path / d
-        CG.compile_model(W.BUILDERS[model](batch), out, opt_level=opt)
+        CG.compile_model(W.BUILDERS[model](batch), out, opt_level=opt, debug=generate.is_debug(d))
         for f in sorted(p.name for p in out.iterdir()):
             assert (GEN / d / f).read_text() == (out / f).read_text(), f"{d}/{f} is stale: rerun generate.py"
 
