@@ -22,6 +22,8 @@ LIB_PATH = PKG_DIR / "libnnc_cuda.so"
 
 # Element types (runtime/include/nnc_types.h:16-24 of the reference).
 DTYPE_FLOAT32 = 0
+DTYPE_INT32 = 2
+DTYPE_BOOL = 5  # one byte per element (numpy / torch uint8)
 DTYPE_INT64 = 6
 # Storage tags (include/nnc_cuda.h).
 TAG_NHWC = 0x100

@@ -13,7 +13,8 @@ import numpy as np
 
 from . import lib as _lib
 
-_NP_DTYPE = {np.dtype(np.float32): _lib.DTYPE_FLOAT32, np.dtype(np.int64): _lib.DTYPE_INT64}
+_NP_DTYPE = {np.dtype(np.float32): _lib.DTYPE_FLOAT32, np.dtype(np.int64): _lib.DTYPE_INT64,
+             np.dtype(np.int32): _lib.DTYPE_INT32, np.dtype(np.uint8): _lib.DTYPE_BOOL}
 
 
 class TensorRef:
@@ -46,7 +47,8 @@ def from_torch(t, tag: int = 0, shape: tuple[int, ...] | None = None) -> TensorR
 
     if not t.is_contiguous():
         raise ValueError("tensor must be contiguous")
-    dt = {torch.float32: _lib.DTYPE_FLOAT32, torch.int64: _lib.DTYPE_INT64}[t.dtype]
+    dt = {torch.float32: _lib.DTYPE_FLOAT32, torch.int64: _lib.DTYPE_INT64, torch.int32: _lib.DTYPE_INT32,
+          torch.uint8: _lib.DTYPE_BOOL}[t.dtype]
     shp = tuple(int(s) for s in (shape if shape is not None else t.shape))
     return TensorRef(t.data_ptr(), dt | tag, shp, t.numel() * t.element_size(), t)
 

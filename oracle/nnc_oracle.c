@@ -548,3 +548,235 @@ void nnc_split(Tensor* in, Tensor** outputs, int num, int axis) {
             memcpy((char*)outputs[k]->data + (size_t)(o * part * inner) * es,
                    (const char*)in->data + (size_t)((o * dim + k * part) * inner) * es, (size_t)(part * inner) * es);
 }
+
+/* ---------------------------------------------------------------------------
+ * The rest of the operator library (ops.c:2088-3116).
+ * ------------------------------------------------------------------------- */
+
+/* ops.c:2517-2599: numel(input) elements; integer targets truncate (C casts,
+ * the x86 conversion); float16 and unknown targets copy 4-byte elements. */
+void nnc_cast(Tensor* in, Tensor* out, int to) {
+    const int64_t n = count_of(in);
+    const int from_bool = in->dtype == NNC_DTYPE_BOOL;
+    const float* f = (const float*)in->data;
+    const uint8_t* u = (const uint8_t*)in->data;
+    if (to == NNC_DTYPE_FLOAT32) {
+        if (!from_bool) { memcpy(out->data, in->data, (size_t)n * 4); return; }
+        for (int64_t i = 0; i < n; ++i) ((float*)out->data)[i] = (float)u[i];
+    } else if (to == NNC_DTYPE_INT32) {
+        for (int64_t i = 0; i < n; ++i) ((int32_t*)out->data)[i] = from_bool ? (int32_t)u[i] : (int32_t)f[i];
+    } else if (to == NNC_DTYPE_INT64) {
+        for (int64_t i = 0; i < n; ++i) ((int64_t*)out->data)[i] = from_bool ? (int64_t)u[i] : (int64_t)f[i];
+    } else if (to == NNC_DTYPE_BOOL) {
+        if (from_bool) { memcpy(out->data, in->data, (size_t)n); return; }
+        for (int64_t i = 0; i < n; ++i) ((uint8_t*)out->data)[i] = f[i] != 0.0f;
+    } else {
+        memcpy(out->data, in->data, (size_t)n * 4);
+    }
+}
+
+/* ops.c:2342-2432: index by index over min(n, a_n, b_n), then the modular
+ * broadcast of the shorter operand when the other spans the output. */
+static void compare_apply(Tensor* a, Tensor* b, Tensor* out, int is_and) {
+    const int64_t n = count_of(out), an = count_of(a), bn = count_of(b);
+    const float* x = (const float*)a->data;
+    const float* y = (const float*)b->data;
+    float* z = (float*)out->data;
+    int64_t m = n < an ? n : an;
+    if (bn < m) m = bn;
+    const int64_t end = (an == n || bn == n) ? n : m;
+    for (int64_t i = 0; i < end; ++i) {
+        const float p = x[i < an ? i : i % an], q = y[i < bn ? i : i % bn];
+        const int r = is_and ? (p != 0.0f && q != 0.0f) : (p == q);
+        z[i] = r ? 1.0f : 0.0f;
+    }
+}
+void nnc_equal(Tensor* a, Tensor* b, Tensor* out) { compare_apply(a, b, out, 0); }
+void nnc_and(Tensor* a, Tensor* b, Tensor* out) { compare_apply(a, b, out, 1); }
+
+/* ops.c:2655-2703. */
+void nnc_greater(Tensor* a, Tensor* b, Tensor* out) {
+    const int64_t n = count_of(out), an = count_of(a), bn = count_of(b);
+    for (int64_t i = 0; i < n; ++i)
+        ((uint8_t*)out->data)[i] = ((const float*)a->data)[i % an] > ((const float*)b->data)[i % bn];
+}
+void nnc_or(Tensor* a, Tensor* b, Tensor* out) {
+    const int64_t n = count_of(out);
+    for (int64_t i = 0; i < n; ++i)
+        ((uint8_t*)out->data)[i] = ((const uint8_t*)a->data)[i] || ((const uint8_t*)b->data)[i];
+}
+void nnc_not(Tensor* in, Tensor* out) {
+    const int64_t n = count_of(out);
+    for (int64_t i = 0; i < n; ++i) ((uint8_t*)out->data)[i] = !((const uint8_t*)in->data)[i];
+}
+
+/* ops.c:2601-2653. */
+void nnc_shape(Tensor* in, Tensor* out, int64_t* shape_data, int ndim) {
+    for (int d = 0; d < ndim; ++d) ((int64_t*)out->data)[d] = shape_data ? shape_data[d] : in->shape[d];
+}
+void nnc_constantofshape(Tensor* out, float value, int ndim) {
+    (void)ndim;
+    const int64_t n = count_of(out);
+    for (int64_t i = 0; i < n; ++i) ((float*)out->data)[i] = value;
+}
+void nnc_expand(Tensor* in, Tensor* out, int64_t* shape, int ndim) {
+    (void)shape; (void)ndim;
+    const int64_t n = count_of(out), m = count_of(in);
+    for (int64_t i = 0; i < n; ++i) ((float*)out->data)[i] = ((const float*)in->data)[i % m];
+}
+
+/* ops.c:2264-2336: the output coordinates (over the output's extents), the
+ * first input-rank of them taken modulo the input's extents. */
+void nnc_tile(Tensor* in, Tensor* out, int64_t* repeats, int ndim) {
+    (void)ndim;
+    const int64_t n = count_of(out);
+    const float* x = (const float*)in->data;
+    float* z = (float*)out->data;
+    if (!repeats) { memcpy(z, x, (size_t)n * 4); return; }
+    int64_t stride[8];
+    stride[in->ndim - 1] = 1;
+    for (int d = in->ndim - 2; d >= 0; --d) stride[d] = stride[d + 1] * in->shape[d + 1];
+    for (int64_t o = 0; o < n; ++o) {
+        int64_t c[8], rem = o, src = 0;
+        for (int d = out->ndim - 1; d >= 0; --d) { c[d] = rem % out->shape[d]; rem /= out->shape[d]; }
+        for (int d = 0; d < in->ndim; ++d) src += (c[d] % in->shape[d]) * stride[d];
+        z[o] = x[src];
+    }
+}
+
+/* ops.c:2705-2910: the reference's cascade of gather cases. */
+static int64_t wrap_clamp(int64_t g, int64_t extent) {
+    if (g < 0) g += extent;
+    if (g < 0) g = 0;
+    if (g >= extent) g = extent - 1;
+    return g;
+}
+void nnc_gather(Tensor* data, Tensor* indices, Tensor* out, int axis, int data_dtype) {
+    const int rank = data->ndim, irank = indices->ndim, orank = out->ndim;
+    const int64_t* idx = (const int64_t*)indices->data;
+    const float* df = (const float*)data->data;
+    const int64_t* dl = (const int64_t*)data->data;
+    float* of = (float*)out->data;
+    int64_t* ol = (int64_t*)out->data;
+    const int64_t on = count_of(out);
+    if (axis < 0) axis += rank;
+    if (axis < 0) axis = 0;
+    if (axis >= rank) axis = rank - 1;
+    if (irank == 0 || (irank == 1 && indices->shape[0] == 1)) {
+        const int64_t g = wrap_clamp(idx[0], data->shape[axis]);
+        if (data_dtype == 1) {
+            if (rank == 1) { ol[0] = dl[g]; return; }
+            int64_t copy = 1;
+            for (int d = axis + 1; d < rank; ++d) copy *= data->shape[d];
+            for (int64_t i = 0; i < copy; ++i) ol[i] = dl[g * copy + i];
+            return;
+        }
+        if (rank == 1) { for (int64_t i = 0; i < on; ++i) of[i] = df[g]; return; }
+        if (rank == 2 && orank == 2) {
+            const int64_t d1 = data->shape[1];
+            for (int64_t i = 0; i < out->shape[0]; ++i)
+                for (int64_t j = 0; j < out->shape[1]; ++j)
+                    of[i * out->shape[1] + j] = axis == 0 ? df[g * d1 + j] : df[i * d1 + g];
+            return;
+        }
+        if (rank == 3) {
+            const int64_t d0 = data->shape[0], d1 = data->shape[1], d2 = data->shape[2];
+            if (axis == 0 && (orank == 2 || orank == 3)) {
+                const int64_t n0 = orank == 2 ? 1 : out->shape[0];
+                const int64_t n1 = orank == 2 ? d1 : out->shape[1], n2 = orank == 2 ? d2 : out->shape[2];
+                for (int64_t i = 0; i < n0; ++i)
+                    for (int64_t j = 0; j < n1; ++j)
+                        for (int64_t k = 0; k < n2; ++k) of[(i * n1 + j) * n2 + k] = df[(g * d1 + j) * d2 + k];
+                return;
+            }
+            if (axis == 1) {
+                for (int64_t i = 0; i < d0; ++i)
+                    for (int64_t k = 0; k < d2; ++k) of[i * d2 + k] = df[(i * d1 + g) * d2 + k];
+                return;
+            }
+            if (axis == 2) {
+                for (int64_t i = 0; i < d0; ++i)
+                    for (int64_t j = 0; j < d1; ++j) of[i * d1 + j] = df[(i * d1 + j) * d2 + g];
+                return;
+            }
+        }
+    }
+    if (irank == 1) {
+        const int64_t num = indices->shape[0];
+        if (data_dtype == 1 && rank == 1) {
+            for (int64_t k = 0; k < num; ++k) ol[k] = dl[wrap_clamp(idx[k], data->shape[0])];
+            return;
+        }
+        if (rank == 2) {
+            const int64_t d1 = data->shape[1];
+            for (int64_t k = 0; k < num; ++k) {
+                const int64_t g = wrap_clamp(idx[k], data->shape[axis]);
+                if (axis == 0) {
+                    for (int64_t j = 0; j < d1; ++j) of[k * d1 + j] = df[g * d1 + j];
+                } else {
+                    for (int64_t i = 0; i < data->shape[0]; ++i) of[i * num + k] = df[i * d1 + g];
+                }
+            }
+            return;
+        }
+    }
+    const int64_t dn = count_of(data);
+    for (int64_t i = 0; i < on; ++i) {
+        if (data_dtype == 1) ol[i] = dl[i % dn];
+        else of[i] = df[i % dn];
+    }
+}
+
+/* ops.c:2088-2093: an empty TODO in the reference. */
+void nnc_batchnorm(Tensor* input, Tensor* scale, Tensor* bias, Tensor* mean, Tensor* var,
+                   Tensor* output, float epsilon, int momentum) {
+    (void)input; (void)scale; (void)bias; (void)mean; (void)var; (void)output; (void)epsilon; (void)momentum;
+}
+
+/* ops.c:2928-3116: gate order I, O, F, C; each gate a sequential fp32 sum of
+ * W x, then R h, then the sum of its two biases; one state carried through
+ * every (step, batch item); Y indexed by the forward step. */
+void nnc_lstm(Tensor* X, Tensor* W, Tensor* R, Tensor* B, Tensor* Y, Tensor* Y_h, Tensor* Y_c,
+              int direction, int hidden) {
+    const int64_t T = X->shape[0], Bn = X->shape[1], I = X->shape[2], H = hidden;
+    const int dirs = direction == 2 ? 2 : 1;
+    float* h = calloc((size_t)H, sizeof(float));
+    float* c = calloc((size_t)H, sizeof(float));
+    float* hn = calloc((size_t)H, sizeof(float));
+    float* cn = calloc((size_t)H, sizeof(float));
+    for (int dir = 0; dir < dirs; ++dir) {
+        memset(h, 0, (size_t)H * sizeof(float));
+        memset(c, 0, (size_t)H * sizeof(float));
+        const float* w = (const float*)W->data + (int64_t)dir * 4 * H * I;
+        const float* r = (const float*)R->data + (int64_t)dir * 4 * H * H;
+        const float* bb = B ? (const float*)B->data + (int64_t)dir * 8 * H : NULL;
+        for (int64_t t = 0; t < T; ++t) {
+            const int64_t tt = dir == 1 ? T - 1 - t : t;
+            for (int64_t b = 0; b < Bn; ++b) {
+                const float* x = (const float*)X->data + (tt * Bn + b) * I;
+                for (int64_t row = 0; row < H; ++row) {
+                    float g[4];
+                    for (int q = 0; q < 4; ++q) {
+                        float s = 0.0f;
+                        for (int64_t j = 0; j < I; ++j) s += w[(q * H + row) * I + j] * x[j];
+                        for (int64_t j = 0; j < H; ++j) s += r[(q * H + row) * H + j] * h[j];
+                        if (bb) s += bb[q * H + row] + bb[(4 + q) * H + row];
+                        g[q] = s;
+                    }
+                    const float ig = 1.0f / (1.0f + expf(-g[0])), og = 1.0f / (1.0f + expf(-g[1]));
+                    const float fg = 1.0f / (1.0f + expf(-g[2])), gg = tanhf(g[3]);
+                    cn[row] = fg * c[row] + ig * gg;
+                    hn[row] = og * tanhf(cn[row]);
+                }
+                memcpy(h, hn, (size_t)H * sizeof(float));
+                memcpy(c, cn, (size_t)H * sizeof(float));
+                memcpy((float*)Y->data + ((t * dirs + dir) * Bn + b) * H, h, (size_t)H * sizeof(float));
+            }
+        }
+        for (int64_t b = 0; b < Bn; ++b) {
+            memcpy((float*)Y_h->data + (dir * Bn + b) * H, h, (size_t)H * sizeof(float));
+            memcpy((float*)Y_c->data + (dir * Bn + b) * H, c, (size_t)H * sizeof(float));
+        }
+    }
+    free(h); free(c); free(hn); free(cn);
+}

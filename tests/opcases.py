@@ -168,6 +168,12 @@ def assert_close(got, want, tol, what=""):
     — or a float rtol applied normwise: |got - want| <= rtol * (|want| +
     max|want|), NaNs in the same places."""
     assert got.shape == want.shape, f"{what}: shape {got.shape} vs {want.shape}"
+    if tol == "exact" and got.dtype.kind != "f":
+        assert got.dtype == want.dtype, f"{what}: dtype {got.dtype} vs {want.dtype}"
+        bad = np.flatnonzero(got.reshape(-1) != want.reshape(-1))
+        assert bad.size == 0, (f"{what}: {bad.size} of {got.size} differ; first at {bad[0]}: "
+                               f"got {got.flat[bad[0]]!r} want {want.flat[bad[0]]!r}")
+        return
     if tol == "exact":
         g = got.view(np.uint32 if got.dtype == np.float32 else np.uint64)
         w = want.view(np.uint32 if want.dtype == np.float32 else np.uint64)
@@ -481,6 +487,109 @@ def seeded_cases():
         names = [f"out{j}" for j in range(parts)]
         add({"name": name, "op": "nnc_split", "tol": "exact",
              "args": [_t("x"), {"k": "ol", "n": names, "shape": [os_] * parts}, _i(parts), _i(axis)]}, {"x": x})
+    out.extend(library_cases())
+    return out
+
+
+def library_cases():
+    """The operators off the BASELINE models' path (cast, comparisons and
+    logic, shape / expand / tile, gather, batchnorm, LSTM), including the
+    reference's broadcast, clamping and fallback branches."""
+    out = []
+
+    def add(case, arrays):
+        out.append((case, arrays))
+
+    cast_in = np.concatenate([EDGE, np.array([3e9, -3e9, 2.1e9, -2.1e9, 0.7, -0.7, 1e19, -1e19, 9.9e18],
+                                             dtype=np.float32), rng_for("cast").standard_normal(40).astype(np.float32) * 50])
+    bools = (rng_for("bools").random(37) > 0.5).astype(np.uint8)
+    for to, odt, tag in ((0, "float32", "f32"), (2, "int32", "i32"), (6, "int64", "i64"), (5, "uint8", "bool"),
+                         (1, "float32", "f16copy"), (9, "float32", "unknown")):
+        add({"name": f"nnc_cast_float_to_{tag}", "op": "nnc_cast", "tol": "exact",
+             "args": [_t("x"), _o("out", cast_in.shape, odt), _i(to)]}, {"x": cast_in.copy()})
+    for to, odt, tag in ((0, "float32", "f32"), (2, "int32", "i32"), (6, "int64", "i64"), (5, "uint8", "bool")):
+        add({"name": f"nnc_cast_bool_to_{tag}", "op": "nnc_cast", "tol": "exact",
+             "args": [_t("x"), _o("out", bools.shape, odt), _i(to)]}, {"x": bools.copy()})
+    for op in ("nnc_equal", "nnc_and", "nnc_greater"):
+        odt = "uint8" if op == "nnc_greater" else "float32"
+        for tag, sa, sb, so in (("same", (5, 7), (5, 7), (5, 7)), ("bscalar", (4, 9), (1,), (4, 9)),
+                                ("ascalar", (1,), (4, 9), (4, 9)), ("bsuffix", (3, 8), (8,), (3, 8)),
+                                ("asuffix", (6,), (5, 6), (5, 6)), ("partial", (6,), (4,), (10,))):
+            if op == "nnc_greater" and tag == "partial":
+                continue  # the reference reads both operands modulo their sizes over the whole output
+            name = f"{op}_{tag}"
+            r = rng_for(name)
+            a = r.integers(-2, 3, sa).astype(np.float32)
+            b = r.integers(-2, 3, sb).astype(np.float32)
+            add({"name": name, "op": op, "tol": "exact", "args": [_t("a"), _t("b"), _o("out", so, odt)]},
+                {"a": a, "b": b})
+    r = rng_for("logic")
+    a = (r.random(50) > 0.5).astype(np.uint8)
+    b = (r.random(50) > 0.5).astype(np.uint8)
+    add({"name": "nnc_or_seeded", "op": "nnc_or", "tol": "exact",
+         "args": [_t("a"), _t("b"), _o("out", (50,), "uint8")]}, {"a": a, "b": b})
+    add({"name": "nnc_not_seeded", "op": "nnc_not", "tol": "exact",
+         "args": [_t("a"), _o("out", (50,), "uint8")]}, {"a": a})
+    x = rng_for("shape").standard_normal((2, 3, 5)).astype(np.float32)
+    add({"name": "nnc_shape_runtime", "op": "nnc_shape", "tol": "exact",
+         "args": [_t("x"), _o("out", (3,), "int64"), {"k": "perm", "v": None}, _i(3)]}, {"x": x})
+    add({"name": "nnc_shape_given", "op": "nnc_shape", "tol": "exact",
+         "args": [_t("x"), _o("out", (4,), "int64"), {"k": "perm", "v": [7, 1, 9, 4]}, _i(4)]}, {"x": x})
+    add({"name": "nnc_constantofshape_seeded", "op": "nnc_constantofshape", "tol": "exact",
+         "args": [_o("out", (3, 4, 5)), _f(-2.5), _i(3)]}, {})
+    for tag, si, so in (("rows", (7,), (4, 7)), ("same", (3, 4), (3, 4)), ("odd", (5,), (2, 6))):
+        name = f"nnc_expand_{tag}"
+        add({"name": name, "op": "nnc_expand", "tol": "exact",
+             "args": [_t("x"), _o("out", so), {"k": "perm", "v": list(so)}, _i(len(so))]},
+            {"x": rng_for(name).standard_normal(si).astype(np.float32)})
+    for tag, si, rep, so in (("2d", (2, 3), [2, 3], (4, 9)), ("3d", (2, 1, 3), [1, 4, 2], (2, 4, 6)),
+                             ("null", (3, 4), None, (3, 4)), ("longrep", (3, 2), [2, 2, 1], (6, 2))):
+        name = f"nnc_tile_{tag}"
+        add({"name": name, "op": "nnc_tile", "tol": "exact",
+             "args": [_t("x"), _o("out", so), {"k": "perm", "v": rep}, _i(len(rep) if rep else len(si))]},
+            {"x": rng_for(name).standard_normal(si).astype(np.float32)})
+    # gather: (tag, data shape, data dtype, indices, axis, output shape)
+    for tag, ds, ddt, idx, axis, os_ in (
+            ("f1_scalar", (9,), 0, np.array(4), 0, (3,)),
+            ("f1_neg", (9,), 0, np.array([-2]), 0, (1,)),
+            ("f2_scalar_ax0", (5, 6), 0, np.array([3]), 0, (1, 6)),
+            ("f2_scalar_ax1", (5, 6), 0, np.array(7), 1, (5, 1)),
+            ("f3_ax0_out2", (3, 4, 5), 0, np.array(1), 0, (4, 5)),
+            ("f3_ax0_out3", (3, 4, 5), 0, np.array([2]), 0, (1, 4, 5)),
+            ("f3_ax1", (3, 4, 5), 0, np.array(-1), 1, (3, 5)),
+            ("f3_ax2", (3, 4, 5), 0, np.array(9), -1, (3, 4)),
+            ("i1_scalar", (6,), 1, np.array(2), 0, (1,)),
+            ("i2_rows", (4, 3), 1, np.array([1]), 0, (3,)),
+            ("i1_list", (6,), 1, np.array([5, 0, -1, 9, -9]), 0, (5,)),
+            ("f2_list_ax0", (5, 4), 0, np.array([4, 0, -1, 2]), 0, (4, 4)),
+            ("f2_list_ax1", (5, 4), 0, np.array([3, -4, 8]), 1, (5, 3)),
+            ("f3_list_fallback", (2, 3, 4), 0, np.array([1, 0]), 1, (2, 2, 4)),
+            ("i3_list_fallback", (2, 3, 4), 1, np.array([1, 0]), 0, (2, 3, 4))):
+        name = f"nnc_gather_{tag}"
+        r = rng_for(name)
+        data = (r.integers(-50, 50, ds).astype(np.int64) if ddt else r.standard_normal(ds).astype(np.float32))
+        add({"name": name, "op": "nnc_gather", "tol": "exact",
+             "args": [_t("data"), _t("idx"), _o("out", os_, "int64" if ddt else "float32"), _i(axis), _i(ddt)]},
+            {"data": data, "idx": np.asarray(idx, dtype=np.int64)})
+    x = rng_for("bn").standard_normal((2, 3, 4, 4)).astype(np.float32)
+    prm = {k: rng_for("bn" + k).standard_normal(3).astype(np.float32) for k in ("s", "b", "m")}
+    prm["v"] = np.abs(prm["m"]) + 0.5
+    add({"name": "nnc_batchnorm_untouched", "op": "nnc_batchnorm", "tol": "exact",
+         "args": [_t("x"), _t("s"), _t("b"), _t("m"), _t("v"), _o("out", x.shape), _f(1e-5), _i(0)]},
+        dict(x=x, **prm))
+    for tag, T, B, I, H, direction, bias in (("fwd", 3, 2, 5, 4, 0, True), ("bidir", 4, 2, 3, 6, 2, True),
+                                             ("nobias", 2, 3, 4, 5, 0, False), ("wide", 3, 1, 16, 40, 0, True)):
+        name = f"nnc_lstm_{tag}"
+        r = rng_for(name)
+        D = 2 if direction == 2 else 1
+        arrays = {"X": r.standard_normal((T, B, I)).astype(np.float32),
+                  "W": (r.standard_normal((D, 4 * H, I)) * 0.4).astype(np.float32),
+                  "R": (r.standard_normal((D, 4 * H, H)) * 0.4).astype(np.float32)}
+        if bias:
+            arrays["Bv"] = (r.standard_normal((D, 8 * H)) * 0.1).astype(np.float32)
+        add({"name": name, "op": "nnc_lstm", "tol": 2e-6,
+             "args": [_t("X"), _t("W"), _t("R"), _t("Bv") if bias else NULL, _o("Y", (T, D, B, H)),
+                      _o("Yh", (D, B, H)), _o("Yc", (D, B, H)), _i(direction), _i(H)]}, arrays)
     return out
 
 
