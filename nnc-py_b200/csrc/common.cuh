@@ -100,6 +100,42 @@ inline int64_t numel(const Tensor* t) {
 bool valid_tensor(const Tensor* t, const char* op, const char* name);
 inline bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
 
+// ---------------------------------------------------------------------------
+// Programmatic dependent launch. Kernels on the forward path are launched
+// with the programmatic-stream-serialisation attribute (captured into CUDA
+// graphs as programmatic edges): each kernel lets the next one be scheduled
+// as soon as all of its own CTAs have started (pdl_trigger, first thing), and
+// the next one's CTAs run their prologue (barrier set-up, TMEM allocation,
+// tensor-map prefetch) on SMs freed by the tail of this one, then wait
+// (pdl_wait) until this grid has completed and its writes are visible before
+// touching any activation memory (reads, and writes to arena slots the
+// previous kernel may still read). Launched without the attribute, both are
+// no-ops. NNC_CUDA_PDL=0 turns the attribute off.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+bool pdl_enabled();
+
+// Launches `kern` on the current stream with the PDL attribute (when
+// enabled), like `kern<<<grid, block, smem, stream>>>(args...)`: follow it
+// with check_launch(op), which counts it and checks the launch.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = ctx().stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
 // Ceil-div and grid sizing in multiples of the SM count.
 __host__ __device__ inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
 int grid_for(int64_t work_items, int threads, int max_ctas_per_sm = 8);

@@ -434,6 +434,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
                    const ConvArgs g) {
   using Cfg = ConvCfg<BN, SPLIT, STAGES>;
   extern __shared__ uint8_t smem_raw[];
+  pdl_trigger();
   uint8_t* smem = align1024(smem_raw);
   float* epi = reinterpret_cast<float*>(smem + Cfg::EPI_OFF);
   int* ktab_off = reinterpret_cast<int*>(smem + Cfg::KTAB_OFF);
@@ -490,6 +491,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_wait();  // the previous kernel's outputs are complete from here on
 
   if (tma_a && warp < kProducerWarps) {
     // ---------------- producer (one thread): TMA im2col of A, TMA of W ----------------
@@ -882,6 +884,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   using Cfg = ConvPairCfg<BN_, STAGES>;
   constexpr int BN = Cfg::BN;
   extern __shared__ uint8_t smem_raw[];
+  pdl_trigger();
   uint8_t* smem = align1024(smem_raw);
   float* epi = reinterpret_cast<float*>(smem + Cfg::EPI_OFF);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::BAR_OFF);
@@ -918,6 +921,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   tc::cluster_sync();  // both CTAs' barriers initialised, TMEM allocated
   tc::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_wait();  // the previous kernel's outputs are complete from here on
 
   if (warp < kPairMmaWarp) {
     // ---------------- producer (one thread per CTA): A half, B half ----------------
@@ -1352,6 +1356,7 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
                      const ConvArgs g) {
   using Cfg = HaloCfg<BN, G, STAGES, CB, POOL, STAGED>;
   extern __shared__ uint8_t smem_raw[];
+  pdl_trigger();
   uint8_t* smem = align1024(smem_raw);
   uint8_t* halo = smem + Cfg::HALO_OFF;
   float* epi = reinterpret_cast<float*>(smem + Cfg::EPI_OFF);
@@ -1397,6 +1402,7 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_wait();  // the previous kernel's outputs are complete from here on
 
   if (warp == 0) {
     if (lane == 0) {
@@ -1775,6 +1781,8 @@ __global__ void __launch_bounds__(128) s2d_rows_kernel(const float* __restrict__
                                                        int H2, int W2, int64_t xs_n, int64_t xs_c,
                                                        int64_t xs_h) {
   extern __shared__ float rows[];  // [2 C][W]: row 2 c + dy = channel c, input row 2 i + dy
+  pdl_trigger();
+  pdl_wait();
   const int64_t row = blockIdx.x;  // n H2 + i
   const int n = (int)(row / H2), i = (int)(row - (int64_t)n * H2);
   const float* src = x + n * xs_n;
@@ -1827,6 +1835,8 @@ __global__ void __launch_bounds__(256) s2d_weight_kernel(const float* __restrict
                                                          int KH, int KW, int ph, int pw, int KH2,
                                                          int KW2, int pad_h, int pad_w, int src_mode,
                                                          int src_c4, int src_kpad, int C2) {
+  pdl_trigger();
+  pdl_wait();
   const int64_t total = (int64_t)Cout * KH2 * KW2 * C2;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
@@ -2200,7 +2210,7 @@ bool launch_conv(ConvArgs g, const float* w0, const float* w1, const char* op) {
   }
   const int grid = (int)(g.tiles < sm_count() ? g.tiles : sm_count());
   g.direct_epi = direct_epilogue() ? 1 : 0;
-  kern<<<grid, kConvThreads, Cfg::SMEM, ctx().stream>>>(tw0, tw1, tx0, tx1, g);
+  launch_pdl(kern, grid, kConvThreads, Cfg::SMEM, tw0, tw1, tx0, tx1, g);
   return check_launch(op);
 }
 
@@ -2237,7 +2247,7 @@ bool launch_conv_pair(ConvArgs g, const float* w0, const char* op) {
   g.direct_epi = direct_epilogue() ? 1 : 0;
   auto kern = conv_tc2_kernel<BN_, STAGES>;
   cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
@@ -2266,6 +2276,9 @@ bool launch_conv_pair(ConvArgs g, const float* w0, const char* op) {
   }
   const int64_t pairs = g.tiles < max_pairs[ctx().device] ? g.tiles : max_pairs[ctx().device];
   cfg.gridDim = dim3((unsigned)(2 * pairs), 1, 1);
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // see pdl_trigger
+  attr[1].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.numAttrs = 2;
   if (!check_cuda(cudaLaunchKernelEx(&cfg, kern, tw, tx, g), op, "cudaLaunchKernelEx")) return false;
   return check_launch(op);
 }
@@ -2321,7 +2334,7 @@ bool launch_halo(ConvArgs g, const float* w0, const char* op) {
     fail(NNC_CUDA_ERR_INVALID, op, "internal: unstaged halo instance for a staged epilogue");
     return false;
   }
-  kern<<<grid, kHaloThreads, Cfg::SMEM, ctx().stream>>>(tw, tx, g);
+  launch_pdl(kern, grid, kHaloThreads, Cfg::SMEM, tw, tx, g);
   return check_launch(op);
 }
 
@@ -2575,16 +2588,16 @@ void conv_impl(Tensor* input, Tensor* weight, Tensor* bias, Tensor* residual, Te
         const int64_t xs_n = (int64_t)H * W * C;
         const unsigned blocks = (unsigned)((int64_t)N * H2);
         if (C2 == 16 && vec)
-          s2d_rows_kernel<16, true><<<blocks, 128, rows_smem, ctx().stream>>>(
+          launch_pdl(s2d_rows_kernel<16, true>, blocks, 128, rows_smem,
               xin, xs2, C, H, W, H2, W2, xs_n, sx_c, sx_h);
         else if (C2 == 16)
-          s2d_rows_kernel<16, false><<<blocks, 128, rows_smem, ctx().stream>>>(
+          launch_pdl(s2d_rows_kernel<16, false>, blocks, 128, rows_smem,
               xin, xs2, C, H, W, H2, W2, xs_n, sx_c, sx_h);
         else if (vec)
-          s2d_rows_kernel<BK, true><<<blocks, 128, rows_smem, ctx().stream>>>(
+          launch_pdl(s2d_rows_kernel<BK, true>, blocks, 128, rows_smem,
               xin, xs2, C, H, W, H2, W2, xs_n, sx_c, sx_h);
         else
-          s2d_rows_kernel<BK, false><<<blocks, 128, rows_smem, ctx().stream>>>(
+          launch_pdl(s2d_rows_kernel<BK, false>, blocks, 128, rows_smem,
               xin, xs2, C, H, W, H2, W2, xs_n, sx_c, sx_h);
       } else if (C2 == 16) {
         s2d_input_kernel<16><<<grid_for(x2 / C2, 256, 8), 256, 0, ctx().stream>>>(
@@ -2597,9 +2610,9 @@ void conv_impl(Tensor* input, Tensor* weight, Tensor* bias, Tensor* residual, Te
       }
       if (!check_launch(op)) return;
       const int src_mode = packed ? (wl.element ? 2 : 1) : 0;
-      s2d_weight_kernel<<<grid_for(w2, 256, 8), 256, 0, ctx().stream>>>(
-          (const float*)weight->data, wts2, Cout, C, KH, KW, ph, pw, s2d.KH2, s2d.KW2, s2d.pad_h,
-          s2d.pad_w, src_mode, wl.C4, wl.Kpad, C2);
+      launch_pdl(s2d_weight_kernel, grid_for(w2, 256, 8), 256, 0, (const float*)weight->data, wts2,
+                 Cout, C, KH, KW, ph, pw, s2d.KH2, s2d.KW2, s2d.pad_h, s2d.pad_w, src_mode, wl.C4,
+                 wl.Kpad, C2);
       if (!check_launch(op)) return;
       ConvArgs g{};
       g.mode = kHalo;

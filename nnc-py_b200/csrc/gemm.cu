@@ -217,6 +217,7 @@ __global__ void __launch_bounds__(kTCThreads, 1)
                    const __grid_constant__ CUtensorMap tmD, const GemmArgs g) {
   using Cfg = GemmCfg<BN, SPLIT, STAGES>;
   extern __shared__ uint8_t smem_raw[];
+  pdl_trigger();
   uint8_t* smem = align1024(smem_raw);
   float* staging = reinterpret_cast<float*>(smem + STAGES * Cfg::STAGE_BYTES);
   uint64_t* full =
@@ -258,6 +259,7 @@ __global__ void __launch_bounds__(kTCThreads, 1)
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_wait();  // the previous kernel's outputs are complete from here on
 
   if (warp == 0) {
     if (lane == 0) {
@@ -480,6 +482,7 @@ __global__ void __launch_bounds__(kTCThreads, 1)
                     const __grid_constant__ CUtensorMap tmD, const GemmArgs g) {
   using Cfg = GemmPairCfg<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
+  pdl_trigger();
   uint8_t* smem = align1024(smem_raw);
   float* staging = reinterpret_cast<float*>(smem + STAGES * Cfg::STAGE_BYTES);
   uint64_t* full =
@@ -518,6 +521,7 @@ __global__ void __launch_bounds__(kTCThreads, 1)
   tc::cluster_sync();  // both CTAs' barriers initialised, TMEM allocated
   tc::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_wait();  // the previous kernel's outputs are complete from here on
   const int per_b = g.m_tiles * g.n_tiles;  // m_tiles counts 256-row tiles here
 
   if (warp == 0) {
@@ -809,7 +813,7 @@ bool launch_tc(const Problem& p, const float* A0, const float* A1, const float* 
     attr_set[ctx().device] = true;
   }
   const int grid = (int)(g.tiles < sm_count() ? g.tiles : sm_count());
-  kern<<<grid, kTCThreads, Cfg::SMEM, ctx().stream>>>(ta0, ta1, tb0, tb1, td, g);
+  launch_pdl(kern, grid, kTCThreads, Cfg::SMEM, ta0, ta1, tb0, tb1, td, g);
   return check_launch(op);
 }
 
@@ -863,7 +867,7 @@ bool launch_tc2(const Problem& p, const float* A, const float* B, const char* op
   g.err = device_error_word();
   auto kern = gemm_tc2_kernel<BN, STAGES>;
   cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
@@ -891,6 +895,9 @@ bool launch_tc2(const Problem& p, const float* A, const float* B, const char* op
   }
   const int64_t pairs = g.tiles < max_pairs[ctx().device] ? g.tiles : max_pairs[ctx().device];
   cfg.gridDim = dim3((unsigned)(2 * pairs), 1, 1);
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // see pdl_trigger
+  attr[1].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.numAttrs = 2;
   if (!check_cuda(cudaLaunchKernelEx(&cfg, kern, ta, tb, td, g), op, "cudaLaunchKernelEx"))
     return false;
   return check_launch(op);

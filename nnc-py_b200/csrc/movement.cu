@@ -147,6 +147,8 @@ __global__ void __launch_bounds__(256) permute_rows_kernel(const float* __restri
 // Device-to-device copy of n 16-byte vectors, four in flight per thread.
 __global__ void __launch_bounds__(256) copy_vec4_kernel(const float4* __restrict__ in,
                                                         float4* __restrict__ out, int64_t n) {
+  pdl_trigger();
+  pdl_wait();
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   for (; i + 3 * stride < n; i += 4 * stride) {
@@ -163,8 +165,7 @@ bool copy_bytes(void* dst, const void* src, size_t bytes, const char* op) {
   if (bytes == 0 || dst == src) return true;
   if ((((uintptr_t)dst | (uintptr_t)src | bytes) & 15) == 0) {
     const int64_t n = (int64_t)(bytes / 16);
-    copy_vec4_kernel<<<grid_for(n, 256, 8), 256, 0, ctx().stream>>>((const float4*)src,
-                                                                    (float4*)dst, n);
+    launch_pdl(copy_vec4_kernel, grid_for(n, 256, 8), 256, 0, (const float4*)src, (float4*)dst, n);
     return check_launch(op);
   }
   return check_cuda(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, ctx().stream), op,

@@ -96,6 +96,8 @@ __global__ void __launch_bounds__(256) pool_nchw_kernel(const float* __restrict_
 template <bool MAX, int V, typename Idx>
 __global__ void __launch_bounds__(256) pool_nhwc_kernel(const float* __restrict__ in,
                                                         float* __restrict__ out, PoolGeom g) {
+  pdl_trigger();
+  pdl_wait();
   // V channels per thread (4 or 2 with 16- or 8-byte alignment, else 1).
   const Idx cg = g.C / V;
   const Idx total = (Idx)g.N * g.OH * g.OW * cg;
@@ -228,26 +230,29 @@ void launch_pool(const float* pi, float* po, const PoolGeom& g, bool nhwc) {
       pool_nchw_kernel<MAX, int64_t, true><<<grid, 256, 0, st>>>(pi, po, g);
     else
       pool_nchw_kernel<MAX, int64_t, false><<<grid, 256, 0, st>>>(pi, po, g);
-  } else if (g.C % 4 == 0 && aligned16(pi) && aligned16(po)) {
+  } else if (g.C % 4 == 0 && aligned16(pi) && aligned16(po) &&
+             total / 4 >= (int64_t)2 * sm_count() * 256) {
+    // Four channels per thread; with fewer outputs (a global pool over a
+    // small batch) one channel per thread instead, four times the threads.
     const int grid = grid_for(total / 4, 256, 8);
     if (small)
-      pool_nhwc_kernel<MAX, 4, int><<<grid, 256, 0, st>>>(pi, po, g);
+      launch_pdl(pool_nhwc_kernel<MAX, 4, int>, grid, 256, 0, pi, po, g);
     else
-      pool_nhwc_kernel<MAX, 4, int64_t><<<grid, 256, 0, st>>>(pi, po, g);
+      launch_pdl(pool_nhwc_kernel<MAX, 4, int64_t>, grid, 256, 0, pi, po, g);
   } else if (g.C % 2 == 0 && g.C <= 8 && small && (((uintptr_t)pi | (uintptr_t)po) & 7) == 0) {
     pool_nhwc_pixel_kernel<MAX><<<grid_for(total / g.C, 256, 8), 256, 0, st>>>(pi, po, g);
   } else if (g.C % 2 == 0 && (((uintptr_t)pi | (uintptr_t)po) & 7) == 0) {
     const int grid = grid_for(total / 2, 256, 8);
     if (small)
-      pool_nhwc_kernel<MAX, 2, int><<<grid, 256, 0, st>>>(pi, po, g);
+      launch_pdl(pool_nhwc_kernel<MAX, 2, int>, grid, 256, 0, pi, po, g);
     else
-      pool_nhwc_kernel<MAX, 2, int64_t><<<grid, 256, 0, st>>>(pi, po, g);
+      launch_pdl(pool_nhwc_kernel<MAX, 2, int64_t>, grid, 256, 0, pi, po, g);
   } else {
     const int grid = grid_for(total, 256, 8);
     if (small)
-      pool_nhwc_kernel<MAX, 1, int><<<grid, 256, 0, st>>>(pi, po, g);
+      launch_pdl(pool_nhwc_kernel<MAX, 1, int>, grid, 256, 0, pi, po, g);
     else
-      pool_nhwc_kernel<MAX, 1, int64_t><<<grid, 256, 0, st>>>(pi, po, g);
+      launch_pdl(pool_nhwc_kernel<MAX, 1, int64_t>, grid, 256, 0, pi, po, g);
   }
 }
 

@@ -144,6 +144,14 @@ bool device_ready() {
 }
 int sm_count() { return dev_state(ctx().device).sms; }
 
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("NNC_CUDA_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
 int grid_for(int64_t work_items, int threads, int max_ctas_per_sm) {
   int64_t want = cdiv(work_items, threads);
   int64_t cap = (int64_t)sm_count() * max_ctas_per_sm;
