@@ -2214,19 +2214,6 @@ bool launch_conv(ConvArgs g, const float* w0, const float* w1, const char* op) {
   return check_launch(op);
 }
 
-// Wave quantisation of few-tile problems (small per-GPU batches): with
-// pairs of 74 on this part, 98 tiles of 256 x 256 take two rounds of full
-// tiles, while 196 tiles of 256 x 128 take three rounds of tiles that cost
-// ~0.55 of one (same MMA rate, half the work, a little more feed per FLOP).
-// Half-width tiles are chosen when their rounds cost less in that model.
-static bool pair_half_tiles_win(int64_t M, int Cout) {
-  const int64_t slots = sm_count() / 2;
-  const int64_t m_tiles = cdiv(M, 2 * 128);
-  const int64_t full = m_tiles * cdiv(Cout, 256), half = m_tiles * cdiv(Cout, 128);
-  const double rounds_full = (double)cdiv(full, slots), rounds_half = (double)cdiv(half, slots);
-  return rounds_half * 0.55 < rounds_full;
-}
-
 // Whether the im2col route runs C_out > 64 on CTA pairs (the default);
 // NNC_CUDA_CONV_PAIR=0 selects the single-CTA kernel (for comparison).
 static bool conv_pair_enabled() {
@@ -2833,9 +2820,7 @@ void conv_impl(Tensor* input, Tensor* weight, Tensor* bias, Tensor* residual, Te
     }
   } else if (!split) {
     const bool pair = g.mode == kIm2col128 && conv_pair_enabled();
-    if (Cout > 128 && pair && pair_half_tiles_win(g.M, Cout))
-      launch_conv_pair<128, 8>(g, w0, op);
-    else if (Cout > 128 && pair)
+    if (Cout > 128 && pair)
       launch_conv_pair<256, 6>(g, w0, op);
     else if (Cout > 128)
       launch_conv<256, 1, 4>(g, w0, nullptr, op);
