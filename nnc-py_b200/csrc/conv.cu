@@ -1373,6 +1373,14 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
   const int hw = kHaloTW + g.KW - 1, hh = 2 * kHaloTH + g.KH - 1;  // window extent in pixels
   const int taps = g.KH * g.KW, cblocks = g.C4 / CB;
   const int per_img = g.tiles_x * g.tiles_y;
+  // Resident weights: when one channel tile and one channel block cover the
+  // call and all the tap groups fit the ring (the space-to-depth stem's 16
+  // taps x 64 channels: 64 KB), the weights are loaded once per CTA and the
+  // MMAs of every tile read them in place — no per-tile weight stream
+  // competing with the operand reads for the shared-memory port, no
+  // per-stage barrier round trips.
+  const int groups = (taps + G - 1) / G;
+  const bool resident = g.n_tiles == 1 && cblocks == 1 && groups <= STAGES;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -1411,6 +1419,15 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
       int stage = 0, hs = 0;
       uint32_t phase = 0, hphase = 0;
       bool ok = true;
+      if (resident) {
+        for (int grp = 0; grp < groups; ++grp) {
+          const int t0 = grp * G, gt = taps - t0 < G ? taps - t0 : G;
+          tc::mbar_arrive_expect_tx(&full[grp], (uint32_t)gt * Cfg::B_BYTES);
+          for (int j = 0; j < gt; ++j)
+            tc::tma_load_2d(smem + grp * Cfg::STAGE_BYTES + j * Cfg::B_BYTES, &tmW, &full[grp],
+                            (t0 + j) * g.C4, 0);
+        }
+      }
       for (int64_t k = 0; ok; ++k) {
         const int64_t tile = halo_tile<POOL>(g, k);
         if (tile < 0) break;
@@ -1430,7 +1447,7 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
             hs = 0;
             hphase ^= 1;
           }
-          for (int t0 = 0; t0 < taps; t0 += G) {
+          for (int t0 = 0; t0 < taps && !resident; t0 += G) {
             const int gt = taps - t0 < G ? taps - t0 : G;
             if (!tc::mbar_wait(&empty[stage], phase ^ 1, g.err)) {
               ok = false;
@@ -1448,8 +1465,11 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
         }
       }
       // Let the last issued loads land before the CTA can exit.
+      if (ok && resident) {
+        for (int grp = 0; grp < groups; ++grp) tc::mbar_wait(&full[grp], 0, g.err);
+      }
       if (ok) {
-        for (int q = 0; q < STAGES; ++q) {
+        for (int q = 0; q < STAGES && !resident; ++q) {
           if (stage == 0) {
             stage = STAGES;
             phase ^= 1;
@@ -1480,6 +1500,10 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
     int stage = 0, hs = 0;
     uint32_t phase = 0, hphase = 0;
     bool ok = true;
+    if (resident) {
+      for (int grp = 0; grp < groups && ok; ++grp) ok = tc::mbar_wait_warp(&full[grp], 0, g.err);
+      tc::tc_fence_after();
+    }
     for (int64_t local = 0; ok && halo_tile<POOL>(g, local) >= 0; ++local) {
       const int acc = local & 1;
       const uint32_t aphase = (local >> 1) & 1;
@@ -1497,11 +1521,15 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
         int kh = 0, kw = 0;
         for (int t0 = 0; t0 < taps; t0 += G) {
           const int gt = taps - t0 < G ? taps - t0 : G;
-          if (!tc::mbar_wait_warp(&full[stage], phase, g.err)) {
-            ok = false;
-            break;
+          if (resident) {
+            stage = t0 / G;
+          } else {
+            if (!tc::mbar_wait_warp(&full[stage], phase, g.err)) {
+              ok = false;
+              break;
+            }
+            tc::tc_fence_after();
           }
-          tc::tc_fence_after();
           const uint64_t b_stage = b_desc0 + (uint32_t)stage * (Cfg::STAGE_BYTES >> 4);
           if (tc::elect_one()) {
             int th = kh, tw = kw;
@@ -1522,7 +1550,7 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
                 }
               }
             }
-            tc::mma_commit(&empty[stage]);
+            if (!resident) tc::mma_commit(&empty[stage]);
           }
           __syncwarp();
           accumulate = 1;
@@ -1532,7 +1560,7 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
               ++kh;
             }
           }
-          if (++stage == STAGES) {
+          if (!resident && ++stage == STAGES) {
             stage = 0;
             phase ^= 1;
           }
