@@ -471,6 +471,92 @@ __global__ void __launch_bounds__(kThreads, VPT <= 8 ? 4 : 2) layernorm_warp_ker
   }
 }
 
+// Slabs of 513..1024 values with 16-byte rows: WPR = 4 warps per slab, 8
+// values (two float4 runs) per lane, two slabs per 256-thread block in
+// flight at once and the next slab's loads issued before this one reduces.
+// A warp-per-slab kernel needs 32 values per lane there (128 registers, 16
+// warps per SM, nothing in flight while a warp reduces: 0.60 of HBM on
+// [32768, 1024]). The group's partial sums meet in shared memory in a fixed
+// order (fp64), each group synchronising on its own named barrier.
+template <int WPR>
+__global__ void __launch_bounds__(kThreads) layernorm_group_kernel(
+    const float* __restrict__ in, const float* __restrict__ scale, const float* __restrict__ bias,
+    float* __restrict__ out, int64_t rows, int len, int inner, float eps) {
+  constexpr int kGroups = kThreads / 32 / WPR;
+  constexpr int kRuns = 1024 / (WPR * 32 * 4);  // float4 runs per lane
+  constexpr int VPT = 4 * kRuns;
+  __shared__ double red[2][kGroups][WPR];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int grp = warp / WPR, wg = warp % WPR;
+  const int tg = wg * 32 + lane;  // thread within the group
+  const int bar = 1 + grp;        // named barrier of the group
+  const float inv_n = (float)len;
+  auto idx = [&](int k) { return 4 * (tg + (k >> 2) * WPR * 32) + (k & 3); };
+  auto group_sync = [&]() { asm volatile("bar.sync %0, %1;" ::"r"(bar), "r"(WPR * 32) : "memory"); };
+  auto load = [&](int64_t row, float (&v)[VPT]) {
+    const float* x = in + row * len;
+#pragma unroll
+    for (int r = 0; r < kRuns; ++r) {
+      const int i = 4 * (tg + r * WPR * 32);
+      float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (i < len) t = __ldg(reinterpret_cast<const float4*>(x + i));
+      v[4 * r] = t.x; v[4 * r + 1] = t.y; v[4 * r + 2] = t.z; v[4 * r + 3] = t.w;
+    }
+  };
+  float gm[VPT], bt[VPT];
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) {
+    const int i = idx(k);
+    const int a = inner == 1 ? i : i / inner;
+    gm[k] = (scale && i < len) ? __ldg(scale + a) : 1.0f;
+    bt[k] = (bias && i < len) ? __ldg(bias + a) : 0.0f;
+  }
+  const int64_t step = (int64_t)gridDim.x * kGroups;
+  int64_t row = (int64_t)blockIdx.x * kGroups + grp;
+  float vn[VPT];
+  if (row < rows) load(row, vn);
+  for (; row < rows; row += step) {
+    float v[VPT];
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) v[k] = vn[k];
+    if (row + step < rows) load(row + step, vn);
+    double part = warp_sum((double)tree_sum(v));
+    if (lane == 0) red[0][grp][wg] = part;
+    group_sync();
+    double tot = 0.0;
+#pragma unroll
+    for (int w = 0; w < WPR; ++w) tot += red[0][grp][w];
+    const float mean = __fdiv_rn((float)tot, inv_n);
+    float dd[VPT];
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      const float d = __fsub_rn(v[k], mean);
+      dd[k] = idx(k) < len ? __fmul_rn(d, d) : 0.0f;
+    }
+    part = warp_sum((double)tree_sum(dd));
+    if (lane == 0) red[1][grp][wg] = part;
+    group_sync();
+    double q = 0.0;
+#pragma unroll
+    for (int w = 0; w < WPR; ++w) q += red[1][grp][w];
+    const float var = __fdiv_rn((float)q, inv_n);
+    const float rsd = __frcp_rn(__fsqrt_rn(__fadd_rn(var, eps)));
+    float* y = out + row * len;
+#pragma unroll
+    for (int r = 0; r < kRuns; ++r) {
+      const int i = 4 * (tg + r * WPR * 32);
+      float o[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int k = 4 * r + c;
+        o[c] = __fadd_rn(__fmul_rn(gm[k], __fmul_rn(__fsub_rn(v[k], mean), rsd)), bt[k]);
+      }
+      if (i < len) *reinterpret_cast<float4*>(y + i) = make_float4(o[0], o[1], o[2], o[3]);
+    }
+    group_sync();  // the partial sums' slots are rewritten by the next slab
+  }
+}
+
 // Long slabs (len <= kSmemRowMax): one 128-thread block per slab, the slab
 // cached in shared memory.
 __global__ void __launch_bounds__(kRowThreads) layernorm_smem_kernel(
@@ -703,6 +789,13 @@ void nnc_layernorm(Tensor* input, Tensor* scale, Tensor* bias, Tensor* output, i
     const int l = (int)len, in1 = (int)inner;
     cudaStream_t st = ctx().stream;
     const bool vec = len % 4 == 0 && aligned16(pi) && aligned16(po);
+    if (len > 512 && vec) {
+      const int64_t gblocks = cdiv(outer, (int64_t)(kThreads / 32 / 4));
+      const int ggrid = (int)(gblocks < (int64_t)sm_count() * 8 ? gblocks : (int64_t)sm_count() * 8);
+      layernorm_group_kernel<4><<<ggrid, kThreads, 0, st>>>(pi, ps, pb, po, outer, l, in1, epsilon);
+      check_launch(op);
+      return;
+    }
 #define NNC_LN_WARP(VPT, VEC) \
   layernorm_warp_kernel<VPT, VEC><<<grid, kThreads, 0, st>>>(pi, ps, pb, po, outer, l, in1, epsilon)
     if (len <= 64)

@@ -321,7 +321,9 @@ def seeded_cases():
         add({"name": name, "op": "nnc_softmax", "tol": 2e-6,
              "args": [_t("x"), _o("out", shape), _i(axis)]}, {"x": x})
     for tag, shape, axis, with_params in (("last", (33, 300), -1, True), ("slab", (4, 6, 5), 1, True),
-                                          ("noparams", (8, 64), -1, False), ("wide", (3, 10000), -1, True)):
+                                          ("noparams", (8, 64), -1, False), ("wide", (3, 10000), -1, True),
+                                          ("grp768", (37, 768), -1, True), ("grp1024", (11, 1024), -1, False),
+                                          ("grp_inner", (5, 3, 256), 1, True)):
         name = f"nnc_layernorm_{tag}"
         r = rng_for(name)
         x = r.standard_normal(shape).astype(np.float32)
