@@ -314,7 +314,9 @@ def seeded_cases():
 
     # --- softmax / layernorm / reduce
     for tag, shape, axis in (("last", (37, 129), -1), ("axis0", (5, 6, 7), 0),
-                             ("mid", (4, 9, 6), 1), ("wide", (3, 9000), 1), ("ten", (2, 10), 1)):
+                             ("mid", (4, 9, 6), 1), ("wide", (3, 9000), 1), ("ten", (2, 10), 1),
+                             ("block4096", (9, 4096), -1), ("block2052", (5, 2052), -1),
+                             ("block8192", (3, 8192), -1)):
         name = f"nnc_softmax_{tag}"
         r = rng_for(name)
         x = (r.standard_normal(shape) * 2).astype(np.float32)
