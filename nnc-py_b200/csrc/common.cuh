@@ -136,6 +136,28 @@ cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t sme
   return cudaLaunchKernelEx(&cfg, kern, args...);
 }
 
+// Grid for a kernel whose blocks loop over `work` units: every block
+// resident at once (the occupancy of `kern` at this block size, per device,
+// cached), or `work` blocks when there are fewer. A grid between the two
+// leaves its last blocks waiting until whole loops of others end.
+template <typename K>
+int resident_grid(K kern, int threads, size_t smem, int64_t work) {
+  static int per_sm[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int& r = per_sm[dev & 63];
+  if (r == 0) {
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&r, kern, threads, smem) != cudaSuccess || r <= 0) {
+      cudaGetLastError();
+      r = 1;
+    }
+  }
+  int sms = 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = 148;
+  const int64_t cap = (int64_t)sms * r;
+  return (int)(work < cap ? (work < 1 ? 1 : work) : cap);
+}
+
 // Ceil-div and grid sizing in multiples of the SM count.
 __host__ __device__ inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
 int grid_for(int64_t work_items, int threads, int max_ctas_per_sm = 8);

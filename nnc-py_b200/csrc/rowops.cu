@@ -773,37 +773,41 @@ void nnc_softmax(Tensor* input, Tensor* output, int axis) {
   float* po = (float*)output->data;
   if (inner == 1 && dim <= 1024) {
     const int64_t blocks = cdiv(outer, (int64_t)(kThreads / 32));
-    const int grid = (int)(blocks < (int64_t)sm_count() * 16 ? blocks : (int64_t)sm_count() * 16);
     const int d = (int)dim;
     cudaStream_t st = ctx().stream;
     // 16-byte rows: dim % 4 == 0 and aligned bases (then every row is aligned).
     const bool vec = dim % 4 == 0 && aligned16(pi) && aligned16(po);
     if (dim <= 32)
-      softmax_warp_kernel<1, false><<<grid, kThreads, 0, st>>>(pi, po, outer, d);
+      softmax_warp_kernel<1, false><<<resident_grid(softmax_warp_kernel<1, false>, kThreads, 0, blocks), kThreads, 0, st>>>(pi, po, outer, d);
     else if (dim <= 64)
-      softmax_warp_kernel<2, false><<<grid, kThreads, 0, st>>>(pi, po, outer, d);
+      softmax_warp_kernel<2, false><<<resident_grid(softmax_warp_kernel<2, false>, kThreads, 0, blocks), kThreads, 0, st>>>(pi, po, outer, d);
     else if (dim <= 128 && vec)
-      softmax_warp_kernel<4, true><<<grid, kThreads, 0, st>>>(pi, po, outer, d);
+      softmax_warp_kernel<4, true><<<resident_grid(softmax_warp_kernel<4, true>, kThreads, 0, blocks), kThreads, 0, st>>>(pi, po, outer, d);
     else if (dim <= 128)
-      softmax_warp_kernel<4, false><<<grid, kThreads, 0, st>>>(pi, po, outer, d);
+      softmax_warp_kernel<4, false><<<resident_grid(softmax_warp_kernel<4, false>, kThreads, 0, blocks), kThreads, 0, st>>>(pi, po, outer, d);
     else if (dim <= 256 && vec)
-      softmax_warp_kernel<8, true><<<grid, kThreads, 0, st>>>(pi, po, outer, d);
+      softmax_warp_kernel<8, true><<<resident_grid(softmax_warp_kernel<8, true>, kThreads, 0, blocks), kThreads, 0, st>>>(pi, po, outer, d);
     else if (dim <= 256)
-      softmax_warp_kernel<8, false><<<grid, kThreads, 0, st>>>(pi, po, outer, d);
+      softmax_warp_kernel<8, false><<<resident_grid(softmax_warp_kernel<8, false>, kThreads, 0, blocks), kThreads, 0, st>>>(pi, po, outer, d);
     else if (dim <= 512 && vec)
-      softmax_warp_kernel<16, true><<<grid, kThreads, 0, st>>>(pi, po, outer, d);
+      softmax_warp_kernel<16, true><<<resident_grid(softmax_warp_kernel<16, true>, kThreads, 0, blocks), kThreads, 0, st>>>(pi, po, outer, d);
     else if (dim <= 512)
-      softmax_warp_kernel<16, false><<<grid, kThreads, 0, st>>>(pi, po, outer, d);
+      softmax_warp_kernel<16, false><<<resident_grid(softmax_warp_kernel<16, false>, kThreads, 0, blocks), kThreads, 0, st>>>(pi, po, outer, d);
     else if (vec)
-      softmax_warp_kernel<32, true><<<grid, kThreads, 0, st>>>(pi, po, outer, d);
+      softmax_warp_kernel<32, true><<<resident_grid(softmax_warp_kernel<32, true>, kThreads, 0, blocks), kThreads, 0, st>>>(pi, po, outer, d);
     else
-      softmax_warp_kernel<32, false><<<grid, kThreads, 0, st>>>(pi, po, outer, d);
+      softmax_warp_kernel<32, false><<<resident_grid(softmax_warp_kernel<32, false>, kThreads, 0, blocks), kThreads, 0, st>>>(pi, po, outer, d);
   } else if (inner == 1 && dim <= 16 * kGroupThreads && dim % 4 == 0 && aligned16(pi) && aligned16(po)) {
-    const int grid = (int)(outer < (int64_t)sm_count() * 4 ? outer : (int64_t)sm_count() * 4);
+    // Exactly the resident blocks (the kernel loops over rows): a grid
+    // beyond them would leave its last blocks waiting for whole row loops.
+    auto run = [&](auto kern) {
+      kern<<<resident_grid(kern, kGroupThreads, 0, outer), kGroupThreads, 0, ctx().stream>>>(pi, po, outer,
+                                                                                              (int)dim);
+    };
     if (dim <= 8 * kGroupThreads)
-      softmax_block_kernel<8><<<grid, kGroupThreads, 0, ctx().stream>>>(pi, po, outer, (int)dim);
+      run(softmax_block_kernel<8>);
     else
-      softmax_block_kernel<16><<<grid, kGroupThreads, 0, ctx().stream>>>(pi, po, outer, (int)dim);
+      run(softmax_block_kernel<16>);
   } else if (inner == 1 && dim <= kSmemRowMax) {
     const size_t smem = (size_t)dim * 4;
     if (smem > 48 * 1024 &&
@@ -849,19 +853,19 @@ void nnc_layernorm(Tensor* input, Tensor* scale, Tensor* bias, Tensor* output, i
   const int64_t len = norm * inner;
   if (len <= 1024) {
     const int64_t blocks = cdiv(outer, (int64_t)(kThreads / 32));
-    const int grid = (int)(blocks < (int64_t)sm_count() * 16 ? blocks : (int64_t)sm_count() * 16);
     const int l = (int)len, in1 = (int)inner;
     cudaStream_t st = ctx().stream;
     const bool vec = len % 4 == 0 && aligned16(pi) && aligned16(po);
     if (len > 512 && vec) {
       const int64_t gblocks = cdiv(outer, (int64_t)(kThreads / 32 / 4));
-      const int ggrid = (int)(gblocks < (int64_t)sm_count() * 8 ? gblocks : (int64_t)sm_count() * 8);
+      const int ggrid = resident_grid(layernorm_group_kernel<4>, kThreads, 0, gblocks);
       layernorm_group_kernel<4><<<ggrid, kThreads, 0, st>>>(pi, ps, pb, po, outer, l, in1, epsilon);
       check_launch(op);
       return;
     }
-#define NNC_LN_WARP(VPT, VEC) \
-  layernorm_warp_kernel<VPT, VEC><<<grid, kThreads, 0, st>>>(pi, ps, pb, po, outer, l, in1, epsilon)
+#define NNC_LN_WARP(VPT, VEC)                                                                  \
+  layernorm_warp_kernel<VPT, VEC><<<resident_grid(layernorm_warp_kernel<VPT, VEC>, kThreads, 0, blocks), \
+                                    kThreads, 0, st>>>(pi, ps, pb, po, outer, l, in1, epsilon)
     if (len <= 64)
       NNC_LN_WARP(2, false);
     else if (len <= 128 && vec)
