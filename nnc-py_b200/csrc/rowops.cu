@@ -236,64 +236,6 @@ __device__ float block_max128(float v, float* red) {
   const float b = red[2] > red[3] ? red[2] : red[3];
   return a > b ? a : b;
 }
-// Rows of 1025..512 VPT values with 16-byte rows: one 512-thread block per
-// row, VPT values per thread in registers (float4 runs), so a row is read
-// once and many rows are in flight (4 blocks per SM) with a fine tail: the
-// shared-memory kernel below runs ~13 rows per SM at a time, and 4096 rows
-// then take three rounds, the last 13% full (0.68 of HBM on [4096, 4096]).
-constexpr int kGroupThreads = 512;
-template <int VPT>
-__global__ void __launch_bounds__(kGroupThreads) softmax_block_kernel(const float* __restrict__ in,
-                                                                      float* __restrict__ out,
-                                                                      int64_t rows, int dim) {
-  constexpr int kWarps = kGroupThreads / 32;
-  __shared__ float red_f[kWarps];
-  __shared__ double red_d[kWarps];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
-    const float* x = in + row * dim;
-    float* y = out + row * dim;
-    float v[VPT];
-    float m = -INFINITY;
-#pragma unroll
-    for (int r = 0; r < VPT / 4; ++r) {
-      const int i = 4 * (threadIdx.x + r * kGroupThreads);
-      float4 t = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
-      if (i < dim) t = __ldg(reinterpret_cast<const float4*>(x + i));
-      v[4 * r] = t.x; v[4 * r + 1] = t.y; v[4 * r + 2] = t.z; v[4 * r + 3] = t.w;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) m = (v[4 * r + c] > m) ? v[4 * r + c] : m;
-    }
-    m = warp_max(m);
-    if (lane == 0) red_f[warp] = m;
-    __syncthreads();
-    m = red_f[0];
-#pragma unroll
-    for (int w = 1; w < kWarps; ++w) m = red_f[w] > m ? red_f[w] : m;
-#pragma unroll
-    for (int k = 0; k < VPT; ++k) {
-      const int i = 4 * (threadIdx.x + (k >> 2) * kGroupThreads) + (k & 3);
-      v[k] = i < dim ? expf(v[k] - m) : 0.0f;
-    }
-    double sd = warp_sum((double)tree_sum(v));
-    if (lane == 0) red_d[warp] = sd;
-    __syncthreads();
-    double tot = 0.0;
-#pragma unroll
-    for (int w = 0; w < kWarps; ++w) tot += red_d[w];
-    const float sum = (float)tot;
-#pragma unroll
-    for (int r = 0; r < VPT / 4; ++r) {
-      const int i = 4 * (threadIdx.x + r * kGroupThreads);
-      if (i < dim)
-        *reinterpret_cast<float4*>(y + i) =
-            make_float4(__fdiv_rn(v[4 * r], sum), __fdiv_rn(v[4 * r + 1], sum),
-                        __fdiv_rn(v[4 * r + 2], sum), __fdiv_rn(v[4 * r + 3], sum));
-    }
-    __syncthreads();  // red_f / red_d are reused by the next row
-  }
-}
-
 __global__ void __launch_bounds__(kRowThreads) softmax_smem_kernel(const float* __restrict__ in,
                                                                    float* __restrict__ out,
                                                                    int64_t rows, int dim) {
@@ -773,41 +715,31 @@ void nnc_softmax(Tensor* input, Tensor* output, int axis) {
   float* po = (float*)output->data;
   if (inner == 1 && dim <= 1024) {
     const int64_t blocks = cdiv(outer, (int64_t)(kThreads / 32));
+    const int grid = (int)(blocks < (int64_t)sm_count() * 16 ? blocks : (int64_t)sm_count() * 16);
     const int d = (int)dim;
     cudaStream_t st = ctx().stream;
     // 16-byte rows: dim % 4 == 0 and aligned bases (then every row is aligned).
     const bool vec = dim % 4 == 0 && aligned16(pi) && aligned16(po);
     if (dim <= 32)
-      softmax_warp_kernel<1, false><<<resident_grid(softmax_warp_kernel<1, false>, kThreads, 0, blocks), kThreads, 0, st>>>(pi, po, outer, d);
+      softmax_warp_kernel<1, false><<<grid, kThreads, 0, st>>>(pi, po, outer, d);
     else if (dim <= 64)
-      softmax_warp_kernel<2, false><<<resident_grid(softmax_warp_kernel<2, false>, kThreads, 0, blocks), kThreads, 0, st>>>(pi, po, outer, d);
+      softmax_warp_kernel<2, false><<<grid, kThreads, 0, st>>>(pi, po, outer, d);
     else if (dim <= 128 && vec)
-      softmax_warp_kernel<4, true><<<resident_grid(softmax_warp_kernel<4, true>, kThreads, 0, blocks), kThreads, 0, st>>>(pi, po, outer, d);
+      softmax_warp_kernel<4, true><<<grid, kThreads, 0, st>>>(pi, po, outer, d);
     else if (dim <= 128)
-      softmax_warp_kernel<4, false><<<resident_grid(softmax_warp_kernel<4, false>, kThreads, 0, blocks), kThreads, 0, st>>>(pi, po, outer, d);
+      softmax_warp_kernel<4, false><<<grid, kThreads, 0, st>>>(pi, po, outer, d);
     else if (dim <= 256 && vec)
-      softmax_warp_kernel<8, true><<<resident_grid(softmax_warp_kernel<8, true>, kThreads, 0, blocks), kThreads, 0, st>>>(pi, po, outer, d);
+      softmax_warp_kernel<8, true><<<grid, kThreads, 0, st>>>(pi, po, outer, d);
     else if (dim <= 256)
-      softmax_warp_kernel<8, false><<<resident_grid(softmax_warp_kernel<8, false>, kThreads, 0, blocks), kThreads, 0, st>>>(pi, po, outer, d);
+      softmax_warp_kernel<8, false><<<grid, kThreads, 0, st>>>(pi, po, outer, d);
     else if (dim <= 512 && vec)
-      softmax_warp_kernel<16, true><<<resident_grid(softmax_warp_kernel<16, true>, kThreads, 0, blocks), kThreads, 0, st>>>(pi, po, outer, d);
+      softmax_warp_kernel<16, true><<<grid, kThreads, 0, st>>>(pi, po, outer, d);
     else if (dim <= 512)
-      softmax_warp_kernel<16, false><<<resident_grid(softmax_warp_kernel<16, false>, kThreads, 0, blocks), kThreads, 0, st>>>(pi, po, outer, d);
+      softmax_warp_kernel<16, false><<<grid, kThreads, 0, st>>>(pi, po, outer, d);
     else if (vec)
-      softmax_warp_kernel<32, true><<<resident_grid(softmax_warp_kernel<32, true>, kThreads, 0, blocks), kThreads, 0, st>>>(pi, po, outer, d);
+      softmax_warp_kernel<32, true><<<grid, kThreads, 0, st>>>(pi, po, outer, d);
     else
-      softmax_warp_kernel<32, false><<<resident_grid(softmax_warp_kernel<32, false>, kThreads, 0, blocks), kThreads, 0, st>>>(pi, po, outer, d);
-  } else if (inner == 1 && dim <= 16 * kGroupThreads && dim % 4 == 0 && aligned16(pi) && aligned16(po)) {
-    // Exactly the resident blocks (the kernel loops over rows): a grid
-    // beyond them would leave its last blocks waiting for whole row loops.
-    auto run = [&](auto kern) {
-      kern<<<resident_grid(kern, kGroupThreads, 0, outer), kGroupThreads, 0, ctx().stream>>>(pi, po, outer,
-                                                                                              (int)dim);
-    };
-    if (dim <= 8 * kGroupThreads)
-      run(softmax_block_kernel<8>);
-    else
-      run(softmax_block_kernel<16>);
+      softmax_warp_kernel<32, false><<<grid, kThreads, 0, st>>>(pi, po, outer, d);
   } else if (inner == 1 && dim <= kSmemRowMax) {
     const size_t smem = (size_t)dim * 4;
     if (smem > 48 * 1024 &&
