@@ -4,6 +4,7 @@ HBM for every other op) and the model throughput of LeNet-5 (N = 8192),
 ResNet-18 -O1 (N = 64, 256) and the small transformer (B = 256).
 
     python sweep.py [--reps 10] [--json sweep.json] [--only ops|models]
+    python sweep.py --case <name>        (one op three times, for ncu captures)
 
 Every number is a median over `reps` calls timed with CUDA events on the
 launching stream. Each op call is captured once into a CUDA graph and replayed
@@ -277,8 +278,76 @@ def model_runs(so, torch, pk: dict, reps: int, only_model: str | None = None) ->
     return rows
 
 
+# Single-op cases for kernel captures (ncu): each is run three times (the
+# first launch warms up, a capture takes the second with -s 1 -c 1). Inputs
+# are larger than L2 so that DRAM counters mean something, but a few hundred
+# MB at most.
+PROFILE_CASES = ("layernorm", "layernorm256", "softmax", "softmax128", "transpose", "transpose_k", "add",
+                 "stem", "stage1")
+
+
+def profile_case(so, torch, case: str) -> None:
+    g = torch.Generator(device="cuda").manual_seed(0)
+    keep = []
+
+    def rnd(*shape):
+        return torch.randn(*shape, generator=g, device="cuda")
+
+    def R(t, tag=0, shape=None):
+        r = T.from_torch(t, tag=tag, shape=shape)
+        keep.append(r)
+        return r.ptr
+
+    if case in ("layernorm", "layernorm256"):
+        rows, d = (32768, 1024) if case == "layernorm" else (131072, 256)
+        x, gam, bet = rnd(rows, d), rnd(d) * 0.1 + 1, rnd(d) * 0.1
+        o = torch.empty_like(x)
+        fn = lambda: so.nnc_layernorm(R(x), R(gam), R(bet), R(o), -1, ctypes.c_float(1e-5))
+    elif case in ("softmax", "softmax128"):
+        x = rnd(8192, 4096) if case == "softmax" else rnd(1024, 4, 128, 128)
+        o = torch.empty_like(x)
+        fn = lambda: so.nnc_softmax(R(x), R(o), -1)
+    elif case in ("transpose", "transpose_k"):
+        x = rnd(1024, 128, 4, 64)
+        perm = (ctypes.c_int64 * 4)(*((0, 2, 1, 3) if case == "transpose" else (0, 2, 3, 1)))
+        o = torch.empty(1024, 4, 128, 64, device="cuda") if case == "transpose" else \
+            torch.empty(1024, 4, 64, 128, device="cuda")
+        fn = lambda: so.nnc_transpose(R(x), R(o), perm, 4)
+    elif case == "add":
+        a, b = rnd(1 << 26), rnd(1 << 26)
+        o = torch.empty_like(a)
+        fn = lambda: so.nnc_add(R(a), R(b), R(o))
+    elif case == "stem":  # the ResNet stem at batch 192: space-to-depth + conv 7x7/2 + relu + max pool
+        n = 192
+        x, w, bias = rnd(n, 3, 224, 224), rnd(64, 3, 7, 7) * 0.1, rnd(64) * 0.01
+        o = torch.empty(n, 56, 56, 64, device="cuda")
+        fn = lambda: so.nnc_conv_relu_maxpool(R(x), R(w), R(bias), R(o, L.TAG_NHWC, (n, 64, 56, 56)),
+                                              7, 7, 2, 2, 3, 3, 112, 112, 3, 3, 2, 2, 1, 1)
+    elif case == "stage1":  # a stage-1 conv+add+relu at batch 128, channels-last, prepacked weights
+        n = 128
+        x, w, bias, res = rnd(n, 56, 56, 64), rnd(64, 64, 3, 3) * 0.05, rnd(64) * 0.01, rnd(n, 56, 56, 64)
+        wp = torch.empty(so.nnc_cuda_prepacked_conv_weight_bytes(R(w)) // 4, device="cuda")
+        rw = T.from_torch(w.clone())
+        keep.append(rw)
+        assert so.nnc_cuda_prepack_conv_weight(rw.ptr, ctypes.c_void_p(wp.data_ptr()), wp.numel() * 4) == 0
+        o = torch.empty(n, 56, 56, 64, device="cuda")
+        shp = (n, 64, 56, 56)
+        fn = lambda: so.nnc_conv_add_relu3x3_s1(R(x, L.TAG_NHWC, shp), rw.ptr, R(bias), R(res, L.TAG_NHWC, shp),
+                                                R(o, L.TAG_NHWC, shp))
+    else:
+        raise SystemExit(f"unknown case {case}")
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    if so.nnc_cuda_get_last_error() != 0:
+        raise RuntimeError(so.nnc_cuda_get_last_error_string().decode())
+    print("ok", case)
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
+    ap.add_argument("--case", choices=PROFILE_CASES, default=None,
+                    help="run one op case three times and exit (for kernel captures)")
     ap.add_argument("--reps", type=int, default=10)
     ap.add_argument("--json", type=str, default=None)
     ap.add_argument("--only", choices=["ops", "models"], default=None)
@@ -292,6 +361,10 @@ def main() -> int:
     if so.nnc_cuda_init(0) != 0:
         raise RuntimeError("nnc_cuda_init failed")
     so.nnc_cuda_set_precision(L.PRECISION_TF32)
+    if opt.case:
+        so.nnc_cuda_set_stream(ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+        profile_case(so, torch, opt.case)
+        return 0
     pk = peaks()
     stream = torch.cuda.Stream()
     so.nnc_cuda_set_stream(ctypes.c_void_p(stream.cuda_stream))
