@@ -50,6 +50,15 @@ bool device_ready();
 // Scratch memory on the current device for the current stream.
 void* workspace(size_t bytes, const char* op);
 
+// Stream-K scratch on the current device for this thread: `slots` partial
+// slots of slot_bytes each and one zeroed arrival counter per slot. Returns
+// false, recording no error, when it cannot be had without allocating inside
+// a graph capture or beside a caller-supplied workspace (or the allocation
+// fails): the caller then runs without stream-K. Like the workspace, it is
+// shared by the thread's calls, which must therefore run in stream order.
+constexpr size_t kStreamKCounterBytes = 4096;
+bool streamk_scratch(int slots, size_t slot_bytes, unsigned** counters, float** parts);
+
 // Max pooling between two device buffers (pool.cu), nnc_maxpool2d semantics.
 bool launch_maxpool_f32(const float* in, float* out, int N, int C, int H, int W, int OH, int OW,
                         int kh, int kw, int sh, int sw, int ph, int pw, bool nhwc, const char* op);

@@ -107,6 +107,12 @@ struct ConvArgs {
   int act;
   int direct_epi;  // channels-last epilogues store from TMEM fragments (store_tile's `direct`)
   int* err;
+  // Paired kernel, stream-K (sk_q > 0): tiles [0, sk_dp_tiles) run whole,
+  // cluster by cluster; the k-block iterations of the other tiles are split
+  // evenly over the clusters (sk_q each, one more for the first sk_r).
+  int64_t sk_dp_tiles, sk_q, sk_r;
+  float* sk_part;      // one slot of 2 x BM x BN partial sums per cluster
+  unsigned* sk_count;  // one arrival counter per slot (zero between launches)
 };
 
 // Output-channel order of packed conv weights. When C_out is a multiple of
@@ -861,6 +867,146 @@ __global__ void __launch_bounds__(kConvThreads, 1)
 // barriers after set-up and before the pair's TMEM is freed; the odd CTA
 // waits for the final commit before it leaves. No TMA load uses cluster
 // multicast.
+//
+// Stream-K (g.sk_q > 0, chosen by the host when whole tiles would leave the
+// last wave of pairs less than 90% full): after its whole tiles each cluster
+// takes an equal share of the remaining tiles' k-block iterations, walking
+// its share from its last tile to its first. A share that begins a tile
+// (or sits inside one) stops before the tile's last k-block: the cluster
+// writes those partial sums to its slot first thing and counts its 16
+// epilogue warps in on the slot's counter. The share that ends a tile does
+// that tile's epilogue last thing: it waits for the slots of the clusters
+// before it, adds them to its accumulator in cluster order (so the result is
+// the same on every run) and counts itself in; the last of the 32 arrivals
+// puts the counter back to zero for the next launch. A cluster only ever
+// waits for lower-numbered clusters, whose partial units come first.
+struct PairUnit {
+  int64_t tile;
+  int kb0, kb1;  // k-blocks [kb0, kb1) of the tile
+};
+// SK = false: whole tiles only, every clusters-th tile from the cluster's own.
+template <bool SK>
+struct PairSchedule {
+  int64_t lo, hi;  // this cluster's stream-K share [lo, hi) (iteration = tile * KB + kb)
+  __device__ PairSchedule(const ConvArgs& g) : lo(0), hi(0) {
+    if (SK) {
+      const int64_t c = cluster();
+      lo = g.sk_dp_tiles * g.kblocks + c * g.sk_q + (c < g.sk_r ? c : g.sk_r);
+      hi = lo + g.sk_q + (c < g.sk_r ? 1 : 0);
+    }
+  }
+  // The cluster (CTA pair) and the number of clusters of this launch.
+  static __device__ int cluster() { return (int)(blockIdx.x >> 1); }
+  static __device__ int clusters() { return (int)(gridDim.x >> 1); }
+  static __device__ int64_t n_dp(const ConvArgs& g) {
+    const int64_t dp_end = SK ? g.sk_dp_tiles : g.tiles;
+    return cluster() < dp_end ? (dp_end - 1 - cluster()) / clusters() + 1 : 0;
+  }
+  __device__ int64_t count(const ConvArgs& g) const {
+    return n_dp(g) + (SK && hi > lo ? (hi - 1) / g.kblocks - lo / g.kblocks + 1 : 0);
+  }
+  __device__ PairUnit unit(const ConvArgs& g, int64_t u) const {
+    const int KB = g.kblocks;
+    if (!SK) return {cluster() + u * clusters(), 0, KB};
+    const int64_t nd = n_dp(g);
+    if (u < nd) return {cluster() + u * clusters(), 0, KB};
+    const int64_t t_hi = (hi - 1) / KB, t = t_hi - (u - nd);
+    return {t, t == lo / KB ? (int)(lo - t * KB) : 0, t == t_hi ? (int)(hi - t * KB) : KB};
+  }
+  // The cluster whose share holds iteration `it` (stream-K tiles only).
+  static __device__ int64_t owner(const ConvArgs& g, int64_t it) {
+    const int64_t rel = it - g.sk_dp_tiles * g.kblocks, split = g.sk_r * (g.sk_q + 1);
+    return rel < split ? rel / (g.sk_q + 1) : g.sk_r + (rel - split) / g.sk_q;
+  }
+};
+
+constexpr unsigned kSkWarps = 2 * kEpilogueWarps;  // arrivals per side of a slot
+
+// A slot holds, per CTA of the pair, 128 rows x BN columns in 16-column
+// chunks of one warp (32 rows x 16 columns, 2 KB): chunk (quad, cc) at
+// float offset (quad * BN / 16 + cc) * 512, and inside it lane l's four
+// float4 at (j * 32 + l) * 4, so each warp-wide access covers 512
+// contiguous bytes. The warps of half h take the 32-column groups h, h + 2,
+// ... (chunks 4 i + 2 h and 4 i + 2 h + 1): the columns store_tile has the
+// same warp write out, so a warp's fixed-up sums are its own to read.
+template <int BN>
+__device__ __forceinline__ float4* sk_chunk(float* slot, int quad, int cc) {
+  return reinterpret_cast<float4*>(slot + (size_t)(quad * (BN / 16) + cc) * 512);
+}
+
+// Partial sums of this warp's rows and chunks -> the slot (TMEM address
+// `acc` = this warp's lane quadrant at the accumulator's first column).
+template <int BN>
+__device__ __forceinline__ void sk_save(float* slot, uint32_t acc, int quad, int half, int lane) {
+#pragma unroll 1
+  for (int cc = 2 * half; cc < BN / 16; cc += 1 + 2 * (cc & 1)) {
+    uint32_t r[16];
+    tc::tmem_ld16(acc + cc * 16, r);
+    tc::tmem_ld_wait();
+    float4* dst = sk_chunk<BN>(slot, quad, cc);
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      __stcg(dst + j * 32 + lane, make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                              __uint_as_float(r[4 * j + 2]),
+                                              __uint_as_float(r[4 * j + 3])));
+  }
+}
+
+// Bounded wait (every lane) until *count reaches `want`; acquire ordering.
+__device__ __forceinline__ bool sk_wait(const unsigned* count, unsigned want, int* err) {
+  const uint64_t t0 = tc::global_ns();
+  for (uint32_t i = 0; i < tc::kWaitLimit; ++i) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(count) : "memory");
+    if (v >= want) return true;
+    if (tc::global_ns() - t0 > tc::kWaitNs) break;
+    __nanosleep(200);
+  }
+  if (err) atomicExch(err, 5 /* NNC_CUDA_ERR_DEVICE_TIMEOUT */);
+  return false;
+}
+
+// Adds the slots of clusters [first, last) to this warp's accumulator
+// chunks, in cluster order, once each slot's writers are all in; then
+// counts this warp in on each slot (the last arrival zeroes the counter).
+// A chunk's TMEM load and its first partial-sum loads are in flight
+// together.
+template <int BN>
+__device__ __forceinline__ void sk_fixup(const ConvArgs& g, int64_t first, int64_t last,
+                                         uint32_t rank, uint32_t acc, int quad, int half,
+                                         int lane) {
+  const size_t slot_floats = (size_t)2 * BM * BN;
+  bool ok = true;
+  for (int64_t s = first; s < last; ++s) ok = sk_wait(&g.sk_count[s], kSkWarps, g.err) && ok;
+  ok = __all_sync(0xffffffffu, ok) && first < last;
+#pragma unroll 1
+  for (int cc = 2 * half; cc < BN / 16; cc += 1 + 2 * (cc & 1)) {
+    uint32_t r[16];
+    tc::tmem_ld16(acc + cc * 16, r);
+    for (int64_t s = first; s < last && ok; ++s) {
+      const float4* src = sk_chunk<BN>(g.sk_part + s * slot_floats + rank * (BM * BN), quad, cc);
+      float4 p[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) p[j] = __ldcg(src + j * 32 + lane);
+      if (s == first) tc::tmem_ld_wait();
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        r[4 * j] = __float_as_uint(__fadd_rn(__uint_as_float(r[4 * j]), p[j].x));
+        r[4 * j + 1] = __float_as_uint(__fadd_rn(__uint_as_float(r[4 * j + 1]), p[j].y));
+        r[4 * j + 2] = __float_as_uint(__fadd_rn(__uint_as_float(r[4 * j + 2]), p[j].z));
+        r[4 * j + 3] = __float_as_uint(__fadd_rn(__uint_as_float(r[4 * j + 3]), p[j].w));
+      }
+    }
+    if (!ok) tc::tmem_ld_wait();
+    tc::tmem_st16(acc + cc * 16, r);
+  }
+  tc::tmem_st_wait();
+  __syncwarp();
+  if (lane == 0 && ok)
+    for (int64_t s = first; s < last; ++s)
+      if (atomicAdd(&g.sk_count[s], 1u) == 2 * kSkWarps - 1) atomicExch(&g.sk_count[s], 0u);
+}
+
 template <int BN_, int STAGES>
 struct ConvPairCfg {
   static constexpr int BN = BN_;        // MMA N (128 or 256); each CTA holds BN / 2 weight rows
@@ -877,7 +1023,7 @@ struct ConvPairCfg {
 // 2..9 drain TMEM; 3 warps per SM sub-partition at most leave 168 registers
 // per thread, room for the direct epilogue.
 constexpr int kPairMmaWarp = 1, kPairThreads = 32 * (2 + kEpilogueWarps);
-template <int BN_, int STAGES>
+template <int BN_, int STAGES, bool SK>
 __global__ void __launch_bounds__(kPairThreads, 1)
     conv_tc2_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
                     const ConvArgs g) {
@@ -896,7 +1042,6 @@ __global__ void __launch_bounds__(kPairThreads, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = tc::cluster_ctarank();  // 0: issues the MMAs
-  const int64_t cluster = blockIdx.x >> 1, clusters = gridDim.x >> 1;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -930,9 +1075,11 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int64_t tile = cluster; tile < g.tiles && ok; tile += clusters) {
-        const int64_t mt = tile / g.n_tiles;
-        const int nt = (int)(tile % g.n_tiles);
+      const PairSchedule<SK> sch(g);
+      for (int64_t u = 0; u < sch.count(g) && ok; ++u) {
+        const PairUnit pu = sch.unit(g, u);
+        const int64_t mt = pu.tile / g.n_tiles;
+        const int nt = (int)(pu.tile % g.n_tiles);
         // This CTA's first pixel; a half past the last pixel loads the
         // pair's first half again (valid coordinates; its rows are masked).
         int64_t m0 = mt * (2 * BM) + (int64_t)rank * BM;
@@ -940,7 +1087,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         const int n0 = (int)(m0 / OHW);
         const int rem = (int)(m0 - (int64_t)n0 * OHW);
         const int w0 = (rem % g.OW) * g.sw - g.pw, h0 = (rem / g.OW) * g.sh - g.ph;
-        for (int kb = 0; kb < g.kblocks; ++kb) {
+        for (int kb = pu.kb0; kb < pu.kb1; ++kb) {
           if (!tc::mbar_wait(&empty[stage], phase ^ 1, g.err)) {
             ok = false;
             break;
@@ -979,13 +1126,15 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       uint32_t phase = 0;
       int local = 0;
       bool ok = true;
-      for (int64_t t = cluster; t < g.tiles && ok; t += clusters, ++local) {
+      const PairSchedule<SK> sch(g);
+      for (int64_t u = 0; u < sch.count(g) && ok; ++u, ++local) {
+        const PairUnit pu = sch.unit(g, u);
         const int acc = local & 1;
         const uint32_t aphase = (local >> 1) & 1;
         if (!tc::mbar_wait(&tempty[acc], aphase ^ 1, g.err)) break;
         tc::tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
-        for (int kb = 0; kb < g.kblocks; ++kb) {
+        for (int kb = pu.kb0; kb < pu.kb1; ++kb) {
           if (!tc::mbar_wait(&full[stage], phase, g.err)) {
             ok = false;
             break;
@@ -996,7 +1145,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
 #pragma unroll
           for (int k = 0; k < BK / 8; ++k)
             tc::mma_tf32_pair(d_tmem, tc::desc_kmajor_sw128(sa + k * 32),
-                              tc::desc_kmajor_sw128(sb + k * 32), idesc, (kb | k) != 0);
+                              tc::desc_kmajor_sw128(sb + k * 32), idesc,
+                              ((kb - pu.kb0) | k) != 0);
           tc::mma_commit_pair_both(&empty[stage]);
           if (++stage == STAGES) {
             stage = 0;
@@ -1018,13 +1168,33 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     const bool direct = vec_ok && perm_rows(g.Cout) && g.direct_epi;
     const uint32_t tempty0 = tc::mapa(tc::smem_u32(&tempty[0]), 0);
     int local = 0;
-    for (int64_t t = cluster; t < g.tiles; t += clusters, ++local) {
-      const int64_t mt = t / g.n_tiles;
-      const int nt = (int)(t % g.n_tiles);
+    const PairSchedule<SK> sch(g);
+    for (int64_t u = 0; u < sch.count(g); ++u, ++local) {
+      const PairUnit pu = sch.unit(g, u);
+      const int64_t mt = pu.tile / g.n_tiles;
+      const int nt = (int)(pu.tile % g.n_tiles);
       const int acc = local & 1;
       const uint32_t aphase = (local >> 1) & 1;
       if (!tc::mbar_wait(&tfull[acc], aphase, g.err)) break;
       tc::tc_fence_after();
+      const uint32_t acc_addr = tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN;
+      if (SK && pu.kb1 < g.kblocks) {
+        // Partial unit: sums to this cluster's slot, buffer back to the
+        // issuer, then the slot's writers count in (stores visible first).
+        const int me = PairSchedule<SK>::cluster();
+        sk_save<BN>(g.sk_part + (size_t)me * (2 * BM * BN) + rank * (BM * BN), acc_addr, quad, half,
+                    lane);
+        tc::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive_cluster(tempty0 + acc * (uint32_t)sizeof(uint64_t));
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) atomicAdd(&g.sk_count[me], 1u);
+        continue;
+      }
+      if (SK && pu.kb0 > 0)
+        sk_fixup<BN>(g, PairSchedule<SK>::owner(g, pu.tile * g.kblocks), PairSchedule<SK>::cluster(),
+                     rank, acc_addr, quad, half, lane);
       store_tile<BN, true>(g, tmem_base, acc * BN, nt, quad, half * kStageCols, 2 * kStageCols,
                            lane, stage_tile, vec_ok, bias_vec,
                            LinearRows{mt * (2 * BM) + (int64_t)rank * BM, g.M}, direct);
@@ -1101,12 +1271,14 @@ constexpr uint32_t kPoolXchgFloats = 2 * 2 * 8 * 32 * 4;
 // (64-byte rows, 64-byte swizzle: the space-to-depth stem's 12 channels).
 // STAGED = false: the instance serves only calls whose epilogue takes the
 // direct path (no shared staging tile; the space goes to the weight ring).
-template <int BN, int G, int STAGES, int CB, bool POOL = false, bool STAGED = true>
+template <int BN, int G, int STAGES, int CB, bool POOL = false, bool STAGED = true,
+          bool PAIR = false>
 struct HaloCfg {
   static constexpr int ROW = CB * 4;                    // bytes per window row
   static constexpr uint32_t SLOT_BYTES = (2 * kHaloTH + kHaloMaxK - 1) *
                                              (kHaloTW + kHaloMaxK - 1) * ROW / 1024 * 1024 + 1024;
-  static constexpr uint32_t B_BYTES = BN * CB * 4;      // one tap's weight tile
+  // One tap's weight tile (PAIR: this CTA's half of the BN rows).
+  static constexpr uint32_t B_BYTES = (PAIR ? BN / 2 : BN) * CB * 4;
   static constexpr uint32_t STAGE_BYTES = G * B_BYTES;  // G taps per ring stage
   static constexpr uint32_t HALO_OFF = STAGES * STAGE_BYTES;
   static constexpr uint32_t EPI_OFF = HALO_OFF + kHaloSlots * SLOT_BYTES;
@@ -1338,23 +1510,40 @@ __device__ __forceinline__ void pool_tile(const ConvArgs& g, uint32_t tmem_base,
 
 // The k-th tile a CTA processes, or -1 past its last: every gridDim-th tile,
 // or (POOL, one channel tile) every gridDim-th image with its tiles in
-// raster order.
-template <bool POOL>
-__device__ __forceinline__ int64_t halo_tile(const ConvArgs& g, int64_t k) {
-  if (!POOL) {
-    const int64_t t = blockIdx.x + k * gridDim.x;
-    return t < g.tiles ? t : -1;
-  }
+// raster order. PAIR (not with POOL): the two CTAs of a cluster take
+// neighbouring tiles of one channel tile in lockstep, CTA r the r-th; a CTA
+// whose neighbour is past the end gets the pair's first tile again with
+// `valid` false (its MMA rows are computed and not stored), so both run out
+// at the same k.
+struct HaloUnit {
+  int64_t tile;
+  bool valid;
+};
+template <bool POOL, bool PAIR>
+__device__ __forceinline__ HaloUnit halo_unit(const ConvArgs& g, int64_t k, uint32_t rank) {
   const int64_t per = (int64_t)g.tiles_x * g.tiles_y;
-  const int64_t img = blockIdx.x + (k / per) * gridDim.x;
-  return img < g.N ? img * per + k % per : -1;
+  if (!PAIR) {
+    if (!POOL) {
+      const int64_t t = blockIdx.x + k * gridDim.x;
+      return {t < g.tiles ? t : -1, true};
+    }
+    const int64_t img = blockIdx.x + (k / per) * gridDim.x;
+    return {img < g.N ? img * per + k % per : -1, true};
+  }
+  static_assert(!(POOL && PAIR), "the pooled epilogue runs on single CTAs");
+  const int64_t cluster = blockIdx.x >> 1, clusters = gridDim.x >> 1;
+  const int64_t pt = cluster + k * clusters;
+  if (pt >= (int64_t)((g.m_tiles + 1) >> 1) * g.n_tiles) return {-1, false};
+  const int64_t mt0 = 2 * (pt / g.n_tiles), mt = mt0 + rank;
+  const bool valid = mt < g.m_tiles;
+  return {(valid ? mt : mt0) * g.n_tiles + pt % g.n_tiles, valid};
 }
 
-template <int BN, int G, int STAGES, int CB, bool POOL, bool STAGED>
+template <int BN, int G, int STAGES, int CB, bool POOL, bool STAGED, bool PAIR>
 __global__ void __launch_bounds__(kHaloThreads, 1)
     conv_halo_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
                      const ConvArgs g) {
-  using Cfg = HaloCfg<BN, G, STAGES, CB, POOL, STAGED>;
+  using Cfg = HaloCfg<BN, G, STAGES, CB, POOL, STAGED, PAIR>;
   extern __shared__ uint8_t smem_raw[];
   pdl_trigger();
   uint8_t* smem = align1024(smem_raw);
@@ -1370,6 +1559,8 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // PAIR: this CTA's rank in the cluster; rank 0 issues the MMAs of both.
+  const uint32_t rank = PAIR ? tc::cluster_ctarank() : 0;
   const int hw = kHaloTW + g.KW - 1, hh = 2 * kHaloTH + g.KH - 1;  // window extent in pixels
   const int taps = g.KH * g.KW, cblocks = g.C4 / CB;
   const int per_img = g.tiles_x * g.tiles_y;
@@ -1393,7 +1584,8 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
     }
     for (int a = 0; a < 4; ++a) {
       tc::mbar_init(&tfull[a], 1);
-      tc::mbar_init(&tempty[a], kEpilogueWarps / 2);
+      // The block's epilogue warps (PAIR: of both CTAs, on rank 0's barrier).
+      tc::mbar_init(&tempty[a], PAIR ? kEpilogueWarps : kEpilogueWarps / 2);
     }
     tc::mbar_init(&done[0], 1);
     tc::mbar_init(&done[1], 1);
@@ -1403,11 +1595,17 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
     tc::prefetch_tmap(&tmX);
   }
   if (warp == 1) {
-    tc::tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
-    tc::tmem_relinquish();
+    if (PAIR) {
+      tc::tmem_alloc_pair(tmem_slot, Cfg::TMEM_COLS);
+      tc::tmem_relinquish_pair();
+    } else {
+      tc::tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+      tc::tmem_relinquish();
+    }
   }
   tc::tc_fence_before();
   __syncthreads();
+  if (PAIR) tc::cluster_sync();  // both CTAs' barriers initialised, TMEM allocated
   tc::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   pdl_wait();  // the previous kernel's outputs are complete from here on
@@ -1415,21 +1613,32 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
   if (warp == 0) {
     if (lane == 0) {
       // ---------------- producer: input windows and weight tiles ----------------
+      // PAIR: both CTAs load into their own shared memory at the same
+      // offsets and count the bytes on rank 0's barriers, which rank 0
+      // arms for both; weight rows [rank BN / 2, + BN / 2) of the tile.
       const uint32_t halo_bytes = (uint32_t)(hw * hh) * Cfg::ROW;
+      constexpr uint32_t kCtas = PAIR ? 2 : 1;
+      const bool arm = !PAIR || rank == 0;
+      const int wrow = PAIR ? (int)rank * (BN / 2) : 0;
+      auto load_w = [&](void* dst, uint64_t* bar, int x, int y) {
+        if (PAIR)
+          tc::tma_load_2d_pair(dst, &tmW, tc::mapa(tc::smem_u32(bar), 0), x, y + wrow);
+        else
+          tc::tma_load_2d(dst, &tmW, bar, x, y);
+      };
       int stage = 0, hs = 0;
       uint32_t phase = 0, hphase = 0;
       bool ok = true;
       if (resident) {
         for (int grp = 0; grp < groups; ++grp) {
           const int t0 = grp * G, gt = taps - t0 < G ? taps - t0 : G;
-          tc::mbar_arrive_expect_tx(&full[grp], (uint32_t)gt * Cfg::B_BYTES);
+          if (arm) tc::mbar_arrive_expect_tx(&full[grp], kCtas * gt * Cfg::B_BYTES);
           for (int j = 0; j < gt; ++j)
-            tc::tma_load_2d(smem + grp * Cfg::STAGE_BYTES + j * Cfg::B_BYTES, &tmW, &full[grp],
-                            (t0 + j) * g.C4, 0);
+            load_w(smem + grp * Cfg::STAGE_BYTES + j * Cfg::B_BYTES, &full[grp], (t0 + j) * g.C4, 0);
         }
       }
       for (int64_t k = 0; ok; ++k) {
-        const int64_t tile = halo_tile<POOL>(g, k);
+        const int64_t tile = halo_unit<POOL, PAIR>(g, k, rank).tile;
         if (tile < 0) break;
         const int64_t mt = tile / g.n_tiles;
         const int nt = (int)(tile % g.n_tiles);
@@ -1440,9 +1649,14 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
             ok = false;
             break;
           }
-          tc::mbar_arrive_expect_tx(&hfull[hs], halo_bytes);
-          tc::tma_load_4d(halo + hs * Cfg::SLOT_BYTES, &tmX, &hfull[hs], cb * CB, x0 * g.sw - g.pw,
-                          y0 * g.sh - g.ph, n);
+          if (arm) tc::mbar_arrive_expect_tx(&hfull[hs], kCtas * halo_bytes);
+          if (PAIR)
+            tc::tma_load_4d_pair(halo + hs * Cfg::SLOT_BYTES, &tmX,
+                                 tc::mapa(tc::smem_u32(&hfull[hs]), 0), cb * CB, x0 * g.sw - g.pw,
+                                 y0 * g.sh - g.ph, n);
+          else
+            tc::tma_load_4d(halo + hs * Cfg::SLOT_BYTES, &tmX, &hfull[hs], cb * CB,
+                            x0 * g.sw - g.pw, y0 * g.sh - g.ph, n);
           if (++hs == kHaloSlots) {
             hs = 0;
             hphase ^= 1;
@@ -1453,10 +1667,10 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
               ok = false;
               break;
             }
-            tc::mbar_arrive_expect_tx(&full[stage], (uint32_t)gt * Cfg::B_BYTES);
+            if (arm) tc::mbar_arrive_expect_tx(&full[stage], kCtas * gt * Cfg::B_BYTES);
             for (int j = 0; j < gt; ++j)
-              tc::tma_load_2d(smem + stage * Cfg::STAGE_BYTES + j * Cfg::B_BYTES, &tmW, &full[stage],
-                              (t0 + j) * g.C4 + cb * CB, nt * BN);
+              load_w(smem + stage * Cfg::STAGE_BYTES + j * Cfg::B_BYTES, &full[stage],
+                     (t0 + j) * g.C4 + cb * CB, nt * BN);
             if (++stage == STAGES) {
               stage = 0;
               phase ^= 1;
@@ -1464,11 +1678,13 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
           }
         }
       }
-      // Let the last issued loads land before the CTA can exit.
-      if (ok && resident) {
+      // Let the last issued loads land before the CTA can exit (PAIR: rank
+      // 0's barriers count both CTAs' loads; rank 1 leaves only after the
+      // final commit, which follows every MMA that read them).
+      if (ok && resident && arm) {
         for (int grp = 0; grp < groups; ++grp) tc::mbar_wait(&full[grp], 0, g.err);
       }
-      if (ok) {
+      if (ok && arm) {
         for (int q = 0; q < STAGES && !resident; ++q) {
           if (stage == 0) {
             stage = STAGES;
@@ -1487,10 +1703,21 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
         }
       }
     }
+  } else if (warp <= 2 && PAIR && rank != 0) {
+    // PAIR, rank 1: rank 0 issues; wait for its final commits before leaving.
+    tc::mbar_wait_warp(&done[warp - 1], 0, g.err);
   } else if (warp <= 2) {
     // ---------------- MMA issuers: warp 1 upper block, warp 2 lower block ----------------
+    // PAIR: M = 256 MMAs over both CTAs' windows and weight halves, into
+    // both CTAs' accumulators; commits reach both CTAs' barriers.
     const int blk = warp - 1;
-    constexpr uint32_t idesc = tc::idesc_tf32(BM, BN);
+    constexpr uint32_t idesc = tc::idesc_tf32(PAIR ? 2 * BM : BM, BN);
+    auto commit = [](uint64_t* bar) {
+      if (PAIR)
+        tc::mma_commit_pair_both(bar);
+      else
+        tc::mma_commit(bar);
+    };
     // Descriptor start addresses are in 16-byte units: adding (bytes >> 4)
     // moves a descriptor (all shared addresses here are below 256 KB).
     const uint64_t a_desc0 =
@@ -1504,7 +1731,7 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
       for (int grp = 0; grp < groups && ok; ++grp) ok = tc::mbar_wait_warp(&full[grp], 0, g.err);
       tc::tc_fence_after();
     }
-    for (int64_t local = 0; ok && halo_tile<POOL>(g, local) >= 0; ++local) {
+    for (int64_t local = 0; ok && halo_unit<POOL, PAIR>(g, local, rank).tile >= 0; ++local) {
       const int acc = local & 1;
       const uint32_t aphase = (local >> 1) & 1;
       if (!tc::mbar_wait_warp(&tempty[acc * 2 + blk], aphase ^ 1, g.err)) break;
@@ -1541,7 +1768,10 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
                 const uint64_t b = b_stage + (uint32_t)j * (Cfg::B_BYTES >> 4);
 #pragma unroll
                 for (int k = 0; k < CB / 8; ++k) {
-                  tc::mma_tf32(d_tmem, a + 2 * k, b + 2 * k, idesc, accum);
+                  if (PAIR)
+                    tc::mma_tf32_pair(d_tmem, a + 2 * k, b + 2 * k, idesc, accum);
+                  else
+                    tc::mma_tf32(d_tmem, a + 2 * k, b + 2 * k, idesc, accum);
                   accum = 1;
                 }
                 if (++tw == g.KW) {
@@ -1550,7 +1780,7 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
                 }
               }
             }
-            if (!resident) tc::mma_commit(&empty[stage]);
+            if (!resident) commit(&empty[stage]);
           }
           __syncwarp();
           accumulate = 1;
@@ -1566,17 +1796,17 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
           }
         }
         // The window is free once both blocks' taps that read it completed.
-        if (tc::elect_one()) tc::mma_commit(&hempty[hs]);
+        if (tc::elect_one()) commit(&hempty[hs]);
         __syncwarp();
         if (++hs == kHaloSlots) {
           hs = 0;
           hphase ^= 1;
         }
       }
-      if (tc::elect_one()) tc::mma_commit(&tfull[acc * 2 + blk]);
+      if (tc::elect_one()) commit(&tfull[acc * 2 + blk]);
       __syncwarp();
     }
-    if (tc::elect_one()) tc::mma_commit(&done[blk]);
+    if (tc::elect_one()) commit(&done[blk]);
     __syncwarp();
     tc::mbar_wait_warp(&done[blk], 0, g.err);
   } else {
@@ -1592,8 +1822,11 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
     float* col_carry = row_carry + kPoolMaxOW * Cfg::ROW_CARRY_STRIDE;
     uint32_t parity = 0;  // POOL: exchange-buffer alternation
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    // PAIR: both CTAs' epilogue warps release an accumulator on rank 0.
+    const uint32_t tempty_bar = PAIR ? tc::mapa(tc::smem_u32(&tempty[0]), 0) : 0;
     for (int64_t local = 0;; ++local) {
-      const int64_t t = halo_tile<POOL>(g, local);
+      const HaloUnit hu = halo_unit<POOL, PAIR>(g, local, rank);
+      const int64_t t = hu.tile;
       if (t < 0) break;
       const int64_t mt = t / g.n_tiles;
       const int nt = (int)(t % g.n_tiles);
@@ -1611,7 +1844,9 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
         break;
       }
       tc::tc_fence_after();
-      if (POOL) {
+      if (!hu.valid) {
+        // PAIR: the neighbour's stand-in tile (never stored).
+      } else if (POOL) {
         pool_tile<BN>(g, tmem_base, acc, blk, quad, lane, epi, row_carry, col_carry, parity, n,
                       (rem / g.tiles_x) * 2 * kHaloTH, (rem % g.tiles_x) * kHaloTW);
       } else {
@@ -1624,15 +1859,24 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
       }
       tc::tc_fence_before();
       __syncwarp();
-      if (lane == 0) tc::mbar_arrive(&tempty[acc * 2 + blk]);
+      if (lane == 0) {
+        if (PAIR)
+          tc::mbar_arrive_cluster(tempty_bar + (acc * 2 + blk) * (uint32_t)sizeof(uint64_t));
+        else
+          tc::mbar_arrive(&tempty[acc * 2 + blk]);
+      }
     }
   }
 
   tc::tc_fence_before();
   __syncthreads();
+  if (PAIR) tc::cluster_sync();  // neither CTA frees the pair's TMEM while the other works
   if (warp == 1) {
     tc::tc_fence_after();
-    tc::tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+    if (PAIR)
+      tc::tmem_dealloc_pair(tmem_base, Cfg::TMEM_COLS);
+    else
+      tc::tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
   }
 }
 
@@ -2252,8 +2496,23 @@ static bool conv_pair_enabled() {
   return on;
 }
 
+// Whether the paired kernel may split tiles along K (stream-K) when whole
+// tiles fill the last wave of pairs badly; NNC_CUDA_CONV_STREAMK=0 turns it
+// off (for comparison).
+static bool conv_streamk_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("NNC_CUDA_CONV_STREAMK");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+// Stream-K needs at least this many k-blocks per tile (shorter reductions
+// are HBM-bound, and their partial sums would cost as much as they save) and
+// this many iterations per cluster.
+constexpr int kStreamKMinKBlocks = 16, kStreamKMinShare = 8;
+
 template <int BN_, int STAGES>
-bool launch_conv_pair(ConvArgs g, const float* w0, const char* op) {
+bool launch_conv_pair(ConvArgs g, const float* w0, const char* op, bool streamk_ok) {
   using Cfg = ConvPairCfg<BN_, STAGES>;
   constexpr int BN = Cfg::BN;
   const int Kpad = g.kblocks * BK;
@@ -2273,7 +2532,8 @@ bool launch_conv_pair(ConvArgs g, const float* w0, const char* op) {
   g.m_tiles = (int)cdiv(g.M, 2 * BM);
   g.tiles = (int64_t)g.m_tiles * g.n_tiles;
   g.direct_epi = direct_epilogue() ? 1 : 0;
-  auto kern = conv_tc2_kernel<BN_, STAGES>;
+  auto kern = conv_tc2_kernel<BN_, STAGES, false>;
+  auto kern_sk = conv_tc2_kernel<BN_, STAGES, true>;
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -2291,23 +2551,55 @@ bool launch_conv_pair(ConvArgs g, const float* w0, const char* op) {
   if (!attr_set[ctx().device]) {
     if (!check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)Cfg::SMEM),
+                    op, "cudaFuncSetAttribute") ||
+        !check_cuda(cudaFuncSetAttribute(kern_sk, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)Cfg::SMEM),
                     op, "cudaFuncSetAttribute"))
       return false;
-    int n = 0;
+    // Both instances: the stream-K one must fit as many pairs as it is given.
+    int n = 0, n_sk = 0;
     cfg.gridDim = dim3(2 * (sm_count() / 2), 1, 1);
-    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0 ||
+        cudaOccupancyMaxActiveClusters(&n_sk, kern_sk, &cfg) != cudaSuccess || n_sk <= 0) {
       cudaGetLastError();
-      n = sm_count() / 2;
+      n = n_sk = sm_count() / 2;
     }
-    max_pairs[ctx().device] = n;
+    max_pairs[ctx().device] = n < n_sk ? n : n_sk;
     attr_set[ctx().device] = true;
   }
-  const int64_t pairs = g.tiles < max_pairs[ctx().device] ? g.tiles : max_pairs[ctx().device];
+  const int64_t P = max_pairs[ctx().device];
+  int64_t pairs = g.tiles < P ? g.tiles : P;
+  // Stream-K when whole tiles would fill the last wave under 90%: the last
+  // full wave and the remainder are split into equal shares of k-blocks
+  // over all P pairs (every pair is resident at once: P is the occupancy
+  // query's count).
+  const int64_t waves = cdiv(g.tiles, P);
+  // Stride-1 windows only: measured on the ResNet shapes at 128 images,
+  // stream-K took stage-3/4 3 x 3 stride-1 convs from 67.6 / 63.5 us to
+  // 61.4 / 59.4 but the stride-2 ones from 57.3 / 38.9 us to 61.4 / 43.0.
+  if (streamk_ok && conv_streamk_enabled() && g.kblocks >= kStreamKMinKBlocks && g.sh == 1 &&
+      g.sw == 1 && g.tiles < waves * P && 10 * g.tiles < 9 * waves * P) {
+    const int64_t dp_end = waves >= 2 ? (waves - 2) * P : 0;
+    const int64_t iters = (g.tiles - dp_end) * g.kblocks;
+    unsigned* count = nullptr;
+    float* part = nullptr;
+    if (iters >= kStreamKMinShare * P &&
+        streamk_scratch((int)P, (size_t)2 * BM * 256 * sizeof(float), &count, &part)) {
+      g.sk_dp_tiles = dp_end;
+      g.sk_q = iters / P;
+      g.sk_r = iters % P;
+      g.sk_part = part;
+      g.sk_count = count;
+      pairs = P;
+    }
+  }
   cfg.gridDim = dim3((unsigned)(2 * pairs), 1, 1);
   attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // see pdl_trigger
   attr[1].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
   cfg.numAttrs = 2;
-  if (!check_cuda(cudaLaunchKernelEx(&cfg, kern, tw, tx, g), op, "cudaLaunchKernelEx")) return false;
+  if (!check_cuda(cudaLaunchKernelEx(&cfg, g.sk_q ? kern_sk : kern, tw, tx, g), op,
+                  "cudaLaunchKernelEx"))
+    return false;
   return check_launch(op);
 }
 
@@ -2322,14 +2614,24 @@ static bool halo_direct(const ConvArgs& g) {
          (((uintptr_t)g.out) & 15) == 0 && (!g.residual || (((uintptr_t)g.residual) & 15) == 0);
 }
 
-template <int BN, int G, int STAGES, int CB, bool POOL = false, bool STAGED = true>
-bool launch_halo(ConvArgs g, const float* w0, const char* op) {
-  using Cfg = HaloCfg<BN, G, STAGES, CB, POOL, STAGED>;
+// Whether halo calls run on CTA pairs (the default); NNC_CUDA_CONV_HALO_PAIR=0
+// selects the single-CTA kernel (for comparison).
+static bool halo_pair_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("NNC_CUDA_CONV_HALO_PAIR");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
+template <int BN, int G, int STAGES, int CB, bool POOL, bool STAGED, bool PAIR>
+bool launch_halo_kernel(ConvArgs g, const float* w0, const char* op) {
+  using Cfg = HaloCfg<BN, G, STAGES, CB, POOL, STAGED, PAIR>;
   const int Kpad = g.K;  // taps x C4, a multiple of CB
   CUtensorMap tw, tx;
   const uint64_t dims[2] = {(uint64_t)Kpad, (uint64_t)g.Cout};
   const uint64_t strides[1] = {(uint64_t)Kpad * 4};
-  const uint32_t box[2] = {CB, BN};
+  const uint32_t box[2] = {CB, PAIR ? BN / 2 : BN};
   if (!encode_tmap_f32(&tw, w0, 2, dims, strides, box, nullptr, op, Cfg::ROW)) return false;
   // Input windows: CB channels x (8 + KW - 1) x (32 + KH - 1) pixels of one image.
   const uint64_t xd[4] = {(uint64_t)g.C4, (uint64_t)g.W, (uint64_t)g.H, (uint64_t)g.N};
@@ -2346,24 +2648,79 @@ bool launch_halo(ConvArgs g, const float* w0, const char* op) {
   g.m_tiles = g.N * g.tiles_x * g.tiles_y;
   g.n_tiles = (int)cdiv(g.Cout, BN);
   g.tiles = (int64_t)g.m_tiles * g.n_tiles;
-  auto kern = conv_halo_kernel<BN, G, STAGES, CB, POOL, STAGED>;
-  static bool attr_set[64] = {};
-  if (!attr_set[ctx().device]) {
-    if (!check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)Cfg::SMEM),
-                    op, "cudaFuncSetAttribute"))
-      return false;
-    attr_set[ctx().device] = true;
-  }
-  const int64_t units = POOL ? (int64_t)g.N : g.tiles;  // POOL: whole images per CTA
-  const int grid = (int)(units < sm_count() ? units : sm_count());
+  auto kern = conv_halo_kernel<BN, G, STAGES, CB, POOL, STAGED, PAIR>;
   g.direct_epi = halo_direct(g) ? 1 : 0;
   if (!STAGED && !POOL && !g.direct_epi) {
     fail(NNC_CUDA_ERR_INVALID, op, "internal: unstaged halo instance for a staged epilogue");
     return false;
   }
-  launch_pdl(kern, grid, kHaloThreads, Cfg::SMEM, tw, tx, g);
+  // POOL: whole images per CTA.
+  const int64_t units = POOL ? (int64_t)g.N : (PAIR ? cdiv(g.m_tiles, 2) * g.n_tiles : g.tiles);
+  static bool attr_set[64] = {};
+  static int max_units[64] = {};
+  if (!PAIR) {
+    if (!attr_set[ctx().device]) {
+      if (!check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)Cfg::SMEM),
+                      op, "cudaFuncSetAttribute"))
+        return false;
+      attr_set[ctx().device] = true;
+    }
+    const int grid = (int)(units < sm_count() ? units : sm_count());
+    launch_pdl(kern, grid, kHaloThreads, Cfg::SMEM, tw, tx, g);
+    return check_launch(op);
+  }
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(kHaloThreads, 1, 1);
+  cfg.dynamicSmemBytes = Cfg::SMEM;
+  cfg.stream = ctx().stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  // Per device: the shared-memory opt-in, then how many pairs fit at once.
+  if (!attr_set[ctx().device]) {
+    if (!check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)Cfg::SMEM),
+                    op, "cudaFuncSetAttribute"))
+      return false;
+    int n = 0;
+    cfg.gridDim = dim3(2 * (sm_count() / 2), 1, 1);
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = sm_count() / 2;
+    }
+    max_units[ctx().device] = n;
+    attr_set[ctx().device] = true;
+  }
+  const int64_t pairs = units < max_units[ctx().device] ? units : max_units[ctx().device];
+  cfg.gridDim = dim3((unsigned)(2 * pairs), 1, 1);
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // see pdl_trigger
+  attr[1].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.numAttrs = 2;
+  if (!check_cuda(cudaLaunchKernelEx(&cfg, kern, tw, tx, g), op, "cudaLaunchKernelEx")) return false;
   return check_launch(op);
+}
+
+// The halo kernel for a call: on CTA pairs unless turned off, a lone tile
+// would leave the pair's second CTA only a stand-in, or the epilogue pools.
+// Measured at batch 1024 (graph replay): ResNet stage-1 3 x 3 convs 474 ->
+// 419 us and stage-2 3 x 3 convs 360 -> 338 us on pairs (M = 256 MMAs: each
+// SM reads its 128 rows of the window and half of the weight tile, 5 KB per
+// N = 64 MMA instead of 6, against the shared-memory port that bounds N <=
+// 128); the pooled stem went 1.57 -> 1.76 ms in lockstep pairs, whose MMAs
+// wait for both CTAs' heavier epilogues.
+template <int BN, int G, int STAGES, int CB, bool POOL = false, bool STAGED = true>
+bool launch_halo(ConvArgs g, const float* w0, const char* op) {
+  const int64_t m_tiles = (int64_t)g.N * cdiv(g.OW, kHaloTW) * cdiv(g.OH, 2 * kHaloTH);
+  if constexpr (!POOL) {
+    if (halo_pair_enabled() && m_tiles >= 2)
+      return launch_halo_kernel<BN, G, STAGES, CB, POOL, STAGED, true>(g, w0, op);
+  }
+  return launch_halo_kernel<BN, G, STAGES, CB, POOL, STAGED, false>(g, w0, op);
 }
 
 // Whether the halo kernel serves a call: stride 1 with windows of at most
@@ -2851,12 +3208,13 @@ void conv_impl(Tensor* input, Tensor* weight, Tensor* bias, Tensor* residual, Te
     }
   } else if (!split) {
     const bool pair = g.mode == kIm2col128 && conv_pair_enabled();
+    // Stream-K's scratch is its own allocation: not with a fixed scratch.
     if (Cout > 128 && pair)
-      launch_conv_pair<256, 6>(g, w0, op);
+      launch_conv_pair<256, 6>(g, w0, op, fixed == nullptr);
     else if (Cout > 128)
       launch_conv<256, 1, 4>(g, w0, nullptr, op);
     else if (Cout > 64 && pair)
-      launch_conv_pair<128, 8>(g, w0, op);
+      launch_conv_pair<128, 8>(g, w0, op, fixed == nullptr);
     else if (Cout > 64)
       launch_conv<128, 1, 6>(g, w0, nullptr, op);
     else

@@ -219,6 +219,48 @@ void* workspace(size_t bytes, const char* op) {
   return p;
 }
 
+// Stream-K scratch of the paired conv kernel, per device for this thread:
+// kStreamKCounterBytes of arrival counters (zeroed when allocated; every
+// launch leaves them at zero) followed by the partial-accumulator slots.
+struct StreamKScratch {
+  void* ptr[kMaxDevices] = {};
+  size_t cap[kMaxDevices] = {};
+};
+thread_local StreamKScratch t_sk;
+
+bool streamk_scratch(int slots, size_t slot_bytes, unsigned** counters, float** parts) {
+  ThreadCtx& c = ctx();
+  const int d = c.device;
+  if (slots <= 0 || (size_t)slots * sizeof(unsigned) > kStreamKCounterBytes) return false;
+  const size_t bytes = kStreamKCounterBytes + (size_t)slots * slot_bytes;
+  if (bytes > t_sk.cap[d]) {
+    // Stream-K only saves time: it allocates nothing inside a capture or
+    // beside a caller-supplied workspace, and a failed allocation just runs
+    // the call without it.
+    if (t_capturing || t_ws.user_ptr[d]) return false;
+    if (t_sk.ptr[d]) {
+      cudaFreeAsync(t_sk.ptr[d], c.stream);
+      t_sk.ptr[d] = nullptr;
+      t_sk.cap[d] = 0;
+    }
+    void* p = nullptr;
+    if (cudaMallocAsync(&p, bytes, c.stream) != cudaSuccess) {
+      cudaGetLastError();
+      return false;
+    }
+    if (cudaMemsetAsync(p, 0, kStreamKCounterBytes, c.stream) != cudaSuccess) {
+      cudaGetLastError();
+      cudaFreeAsync(p, c.stream);
+      return false;
+    }
+    t_sk.ptr[d] = p;
+    t_sk.cap[d] = bytes;
+  }
+  *counters = (unsigned*)t_sk.ptr[d];
+  *parts = (float*)((char*)t_sk.ptr[d] + kStreamKCounterBytes);
+  return true;
+}
+
 // The innermost traced call of this thread (trace_io annotates it).
 thread_local int t_scope_slot = -1;
 thread_local bool t_scope_captured = false;
@@ -334,6 +376,8 @@ int nnc_cuda_check_device_status(void) {
     return ctx().status;
   if (h != 0) {
     cudaMemset(w, 0, sizeof(int));
+    // An expired wait may have left stream-K arrival counters non-zero.
+    if (t_sk.ptr[ctx().device]) cudaMemset(t_sk.ptr[ctx().device], 0, kStreamKCounterBytes);
     fail(NNC_CUDA_ERR_DEVICE_TIMEOUT, "nnc_cuda_check_device_status",
          "a kernel's bounded wait expired (code %d)", h);
     return NNC_CUDA_ERR_DEVICE_TIMEOUT;

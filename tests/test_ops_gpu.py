@@ -252,6 +252,9 @@ def test_conv_resnet_layers_vs_oracle(cuda_lib, prec, cfg):
 # take the halo-tile kernel in TF32 mode (the im2col kernel in 3xTF32 mode):
 # ragged output blocks, partial C_out tiles (48, 200), C_out not a multiple of
 # 4 (scalar epilogue), three channel blocks, a 4 x 4 window, 1 x 1 windows.
+# Tiles run on CTA pairs, neighbouring tiles side by side; an odd tile count
+# (5 tiles of 24 x 40, 49 x 3 of the stride-2 case) leaves the last pair's
+# second CTA a stand-in tile that is computed and not stored.
 HALO_CASES = [
     # n, c, h, w, co, k, p, op
     (2, 32, 30, 30, 48, 3, 1, "nnc_conv_add_relu"),
@@ -263,6 +266,7 @@ HALO_CASES = [
     (2, 64, 56, 56, 128, 1, 0, "nnc_conv"),  # the ResNet stage-2 projection, stride 2
     (1, 128, 56, 56, 256, 1, 0, "nnc_conv_add_relu"),  # stride 2, two 128-channel tiles
     (2, 32, 20, 20, 64, 1, 0, "nnc_conv_relu"),  # 1 x 1 over 32 channels (chunk order)
+    (3, 64, 56, 56, 64, 1, 0, "nnc_conv_add_relu"),  # stride 2, 64 channels: strided windows
 ]
 
 
@@ -314,9 +318,32 @@ PAIR_CASES = [
 ]
 
 
+
+# Stream-K on CTA pairs (TF32, stride 1): whole tiles would fill the last
+# wave of the 74 resident pairs under 90%, so tiles are split along K between
+# pairs and the pair that ends a tile adds the others' partial sums. For 74
+# pairs: 8 tiles of 144 k-blocks (15-16 per pair, each tile over ~10 pairs;
+# the last tile's upper half past the last pixel; residual and relu); 49
+# tiles of 36 (128-channel tiles); 8 tiles with C_out 200 (the staged
+# epilogue); 150 tiles of 16, the first 74 whole and the other 76 split.
+STREAMK_CASES = [
+    # n, c, h, w, co, k, s, p, op
+    (16, 512, 7, 7, 512, 3, 1, 1, "nnc_conv_add_relu"),
+    (64, 128, 14, 14, 128, 3, 1, 1, "nnc_conv_relu"),
+    (16, 512, 10, 12, 200, 3, 1, 1, "nnc_conv"),
+    (1200, 512, 4, 4, 512, 1, 1, 0, "nnc_conv_add_relu"),
+]
+
+
+@pytest.mark.parametrize("cfg", STREAMK_CASES, ids=lambda c: "x".join(str(v) for v in c[:8]))
+def test_conv_stream_k_vs_oracle(cuda_lib, cfg):
+    test_conv_cta_pairs_vs_oracle(cuda_lib, 0, cfg, repeat=3)
+    assert cuda_lib.nnc_cuda_check_device_status() == 0  # no bounded wait expired
+
+
 @pytest.mark.parametrize("prec", [0, 1])
 @pytest.mark.parametrize("cfg", PAIR_CASES, ids=lambda c: "x".join(str(v) for v in c[:8]))
-def test_conv_cta_pairs_vs_oracle(cuda_lib, prec, cfg):
+def test_conv_cta_pairs_vs_oracle(cuda_lib, prec, cfg, repeat=1):
     n, c, h, w, co, k, st, p, op = cfg
     r = np.random.default_rng(13 + sum(cfg[:8]))
     oh, ow = C.conv_out(h, k, st, p), C.conv_out(w, k, st, p)
@@ -335,6 +362,11 @@ def test_conv_cta_pairs_vs_oracle(cuda_lib, prec, cfg):
     want = C.run_host(_oracle(), case, arrays)["out"]
     got_nhwc = C.run_cuda(cuda_lib, case, arrays, nhwc=nhwc)["out"]
     C.assert_close(got_nhwc, want, C.TC_RTOL[prec], f"conv{cfg}[nhwc]")
+    # Later calls reuse whatever earlier calls left behind (stream-K's
+    # counters return to zero after every launch): same result each time.
+    for _ in range(repeat - 1):
+        again = C.run_cuda(cuda_lib, case, arrays, nhwc=nhwc)["out"]
+        np.testing.assert_array_equal(again, got_nhwc)
     got = C.run_cuda(cuda_lib, case, arrays)["out"]
     C.assert_close(got, want, C.TC_RTOL[prec], f"conv{cfg}")
 
@@ -409,6 +441,8 @@ POOL_CASES = [
     (1, 3, 64, 64, 64, 7, 2, 3, (2, 2, 1)),
     # More images than SMs: CTAs walk several images (carries reset at each).
     (150, 3, 56, 56, 64, 7, 2, 3, (3, 2, 1)),
+    # An odd image count (the pooled epilogue runs on single CTAs).
+    (3, 3, 64, 64, 64, 7, 2, 3, (3, 2, 1)),
 ]
 
 
