@@ -45,6 +45,7 @@
 // (relu: v > 0 ? v : 0; sigmoid: 1 / (1 + expf(-v))).
 #include <math.h>
 #include <stdlib.h>
+#include <string.h>
 
 #include <algorithm>
 #include <mutex>
@@ -113,6 +114,11 @@ struct ConvArgs {
   int64_t sk_dp_tiles, sk_q, sk_r;
   float* sk_part;      // one slot of 2 x BM x BN partial sums per cluster
   unsigned* sk_count;  // one arrival counter per slot (zero between launches)
+  // Halo kernel, GATHER: the original 3-channel input of a space-to-depth
+  // conv (element strides), whose windows the kernel builds itself.
+  const float* src;
+  int src_H, src_W;
+  int64_t src_sn, src_sc, src_sh, src_sw;
 };
 
 // Output-channel order of packed conv weights. When C_out is a multiple of
@@ -1256,6 +1262,7 @@ constexpr int kHaloTW = 8, kHaloTH = 16;  // one accumulator block
 constexpr int kHaloMaxK = 4;               // largest KH and KW
 constexpr int kHaloSlots = 2;
 constexpr int kHaloThreads = 32 * (3 + kEpilogueWarps);
+constexpr int kGatherThreads = 128;  // GATHER: four window-building warps after the epilogue
 constexpr int kPoolMaxOW = 128;  // widest conv output the pooled epilogue carries a row of
 // POOL shared buffers. A thread's 8 values of a 32-channel chunk travel as
 // two float4 runs u = 0, 1 (values 4 u .. 4 u + 3), every run at a
@@ -1272,8 +1279,9 @@ constexpr uint32_t kPoolXchgFloats = 2 * 2 * 8 * 32 * 4;
 // STAGED = false: the instance serves only calls whose epilogue takes the
 // direct path (no shared staging tile; the space goes to the weight ring).
 template <int BN, int G, int STAGES, int CB, bool POOL = false, bool STAGED = true,
-          bool PAIR = false>
+          bool PAIR = false, bool GATHER = false>
 struct HaloCfg {
+  static constexpr int SLOTS = kHaloSlots;  // window slots
   static constexpr int ROW = CB * 4;                    // bytes per window row
   static constexpr uint32_t SLOT_BYTES = (2 * kHaloTH + kHaloMaxK - 1) *
                                              (kHaloTW + kHaloMaxK - 1) * ROW / 1024 * 1024 + 1024;
@@ -1281,7 +1289,7 @@ struct HaloCfg {
   static constexpr uint32_t B_BYTES = (PAIR ? BN / 2 : BN) * CB * 4;
   static constexpr uint32_t STAGE_BYTES = G * B_BYTES;  // G taps per ring stage
   static constexpr uint32_t HALO_OFF = STAGES * STAGE_BYTES;
-  static constexpr uint32_t EPI_OFF = HALO_OFF + kHaloSlots * SLOT_BYTES;
+  static constexpr uint32_t EPI_OFF = HALO_OFF + SLOTS * SLOT_BYTES;
   static constexpr uint32_t EPI_BYTES = POOL ? kPoolXchgFloats * 4 : (STAGED ? kEpiBytes : 0);
   static constexpr uint32_t CARRY_OFF = EPI_OFF + EPI_BYTES;
   static constexpr int ROW_CARRY_STRIDE = BN + 16;
@@ -1539,11 +1547,24 @@ __device__ __forceinline__ HaloUnit halo_unit(const ConvArgs& g, int64_t k, uint
   return {(valid ? mt : mt0) * g.n_tiles + pt % g.n_tiles, valid};
 }
 
-template <int BN, int G, int STAGES, int CB, bool POOL, bool STAGED, bool PAIR>
-__global__ void __launch_bounds__(kHaloThreads, 1)
+// GATHER (single CTAs, CB = 16, a 3-channel source): instead of TMA window
+// loads, four more warps build each tile's space-to-depth window from the
+// original input: window row r = (wy, wx) is s2d pixel (y0 - ph + wy,
+// x0 - pw + wx), whose channel 3 q + c (q = 2 dy + dx) is source channel c
+// at (2 i + dy, 2 j + dx), zero outside the image, channels 12..15 zero. A
+// row's four 16-byte chunks go where the 64-byte swizzle puts them (chunk j
+// of row r at j ^ ((r >> 1) & 3): the slot is 1024-byte aligned and rows
+// are 64 bytes), then a proxy fence makes the generic stores visible to
+// the tensor core's reads before the warp arrives on the window barrier.
+// This replaces a separate space-to-depth pass and its round trip through
+// HBM.
+template <int BN, int G, int STAGES, int CB, bool POOL, bool STAGED, bool PAIR, bool GATHER>
+__global__ void __launch_bounds__(kHaloThreads + (GATHER ? kGatherThreads : 0), 1)
     conv_halo_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
                      const ConvArgs g) {
-  using Cfg = HaloCfg<BN, G, STAGES, CB, POOL, STAGED, PAIR>;
+  static_assert(!GATHER || (CB == 16 && !PAIR), "window gathering: 16-channel blocks, single CTAs");
+  using Cfg = HaloCfg<BN, G, STAGES, CB, POOL, STAGED, PAIR, GATHER>;
+  constexpr int kSlots = Cfg::SLOTS;
   extern __shared__ uint8_t smem_raw[];
   pdl_trigger();
   uint8_t* smem = align1024(smem_raw);
@@ -1552,8 +1573,8 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::BAR_OFF);
   uint64_t* empty = full + STAGES;
   uint64_t* hfull = empty + STAGES;
-  uint64_t* hempty = hfull + kHaloSlots;
-  uint64_t* tfull = hempty + kHaloSlots;  // [acc][block]
+  uint64_t* hempty = hfull + kSlots;
+  uint64_t* tfull = hempty + kSlots;  // [acc][block]
   uint64_t* tempty = tfull + 4;           // [acc][block]
   uint64_t* done = tempty + 4;            // [block]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 2);
@@ -1578,8 +1599,9 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
       tc::mbar_init(&full[s], 1);
       tc::mbar_init(&empty[s], 2);  // both MMA warps release a stage
     }
-    for (int h = 0; h < kHaloSlots; ++h) {
-      tc::mbar_init(&hfull[h], 1);
+    for (int h = 0; h < kSlots; ++h) {
+      // TMA: the producer's expect_tx arrival; GATHER: each gathering warp.
+      tc::mbar_init(&hfull[h], GATHER ? kGatherThreads / 32 : 1);
       tc::mbar_init(&hempty[h], 2);
     }
     for (int a = 0; a < 4; ++a) {
@@ -1592,7 +1614,7 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
     tmem_slot[1] = 0;  // epilogue abort flag (POOL)
     tc::fence_barrier_init();
     tc::prefetch_tmap(&tmW);
-    tc::prefetch_tmap(&tmX);
+    if (!GATHER) tc::prefetch_tmap(&tmX);
   }
   if (warp == 1) {
     if (PAIR) {
@@ -1645,21 +1667,23 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
         const int n = (int)(mt / per_img), rem = (int)(mt % per_img);
         const int y0 = (rem / g.tiles_x) * 2 * kHaloTH, x0 = (rem % g.tiles_x) * kHaloTW;
         for (int cb = 0; cb < cblocks && ok; ++cb) {
-          if (!tc::mbar_wait(&hempty[hs], hphase ^ 1, g.err)) {
-            ok = false;
-            break;
-          }
-          if (arm) tc::mbar_arrive_expect_tx(&hfull[hs], kCtas * halo_bytes);
-          if (PAIR)
-            tc::tma_load_4d_pair(halo + hs * Cfg::SLOT_BYTES, &tmX,
-                                 tc::mapa(tc::smem_u32(&hfull[hs]), 0), cb * CB, x0 * g.sw - g.pw,
-                                 y0 * g.sh - g.ph, n);
-          else
-            tc::tma_load_4d(halo + hs * Cfg::SLOT_BYTES, &tmX, &hfull[hs], cb * CB,
-                            x0 * g.sw - g.pw, y0 * g.sh - g.ph, n);
-          if (++hs == kHaloSlots) {
-            hs = 0;
-            hphase ^= 1;
+          if (!GATHER) {  // else the gathering warps fill the windows
+            if (!tc::mbar_wait(&hempty[hs], hphase ^ 1, g.err)) {
+              ok = false;
+              break;
+            }
+            if (arm) tc::mbar_arrive_expect_tx(&hfull[hs], kCtas * halo_bytes);
+            if (PAIR)
+              tc::tma_load_4d_pair(halo + hs * Cfg::SLOT_BYTES, &tmX,
+                                   tc::mapa(tc::smem_u32(&hfull[hs]), 0), cb * CB, x0 * g.sw - g.pw,
+                                   y0 * g.sh - g.ph, n);
+            else
+              tc::tma_load_4d(halo + hs * Cfg::SLOT_BYTES, &tmX, &hfull[hs], cb * CB,
+                              x0 * g.sw - g.pw, y0 * g.sh - g.ph, n);
+            if (++hs == kSlots) {
+              hs = 0;
+              hphase ^= 1;
+            }
           }
           for (int t0 = 0; t0 < taps && !resident; t0 += G) {
             const int gt = taps - t0 < G ? taps - t0 : G;
@@ -1693,9 +1717,9 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
           --stage;
           tc::mbar_wait(&full[stage], phase, g.err);
         }
-        for (int q = 0; q < kHaloSlots; ++q) {
+        for (int q = 0; q < kSlots && !GATHER; ++q) {
           if (hs == 0) {
-            hs = kHaloSlots;
+            hs = kSlots;
             hphase ^= 1;
           }
           --hs;
@@ -1798,7 +1822,7 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
         // The window is free once both blocks' taps that read it completed.
         if (tc::elect_one()) commit(&hempty[hs]);
         __syncwarp();
-        if (++hs == kHaloSlots) {
+        if (++hs == kSlots) {
           hs = 0;
           hphase ^= 1;
         }
@@ -1809,6 +1833,129 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
     if (tc::elect_one()) commit(&done[blk]);
     __syncwarp();
     tc::mbar_wait_warp(&done[blk], 0, g.err);
+  } else if (GATHER && warp >= 3 + kEpilogueWarps) {
+    // ---------------- GATHER: space-to-depth windows from the source ----------------
+    const int p = threadIdx.x - 32 * (3 + kEpilogueWarps);
+    const int rows = hw * hh;
+    // 16-byte loads: unit column stride, rows, planes and images in 4-float
+    // multiples from a 16-byte aligned base, window origins on even s2d
+    // columns (tile columns are 8 apart: an even pad).
+    const bool vec = g.src_sw == 1 && g.src_sh % 4 == 0 && g.src_sc % 4 == 0 &&
+                     g.src_sn % 4 == 0 && (((uintptr_t)g.src) & 15) == 0 && g.pw % 2 == 0;
+    int hs = 0;
+    uint32_t hphase = 0;
+    for (int64_t k = 0;; ++k) {
+      const int64_t tile = halo_unit<POOL, false>(g, k, 0).tile;
+      if (tile < 0) break;
+      const int64_t mt = tile / g.n_tiles;
+      const int n = (int)(mt / per_img), rem = (int)(mt % per_img);
+      const int i0 = (rem / g.tiles_x) * 2 * kHaloTH - g.ph, j0 = (rem % g.tiles_x) * kHaloTW - g.pw;
+      if (!tc::mbar_wait_warp(&hempty[hs], hphase ^ 1, g.err)) break;
+      uint8_t* slot = halo + hs * Cfg::SLOT_BYTES;
+      const float* src = g.src + (int64_t)n * g.src_sn;
+      if (vec) {
+        // NCHW rows of 4-float multiples: a work item is two neighbouring
+        // window pixels (wx even), whose 2 x 2 source blocks of one channel
+        // row are one 16-byte load: 6 loads per item, two items in flight.
+        const int pw2 = (hw + 1) >> 1, items = hh * pw2;
+#pragma unroll 1
+        for (int it0 = p; it0 < items; it0 += 2 * kGatherThreads) {
+          float4 d[2][3][2];  // [item][c][dy]: (dx 0, 1) of pixel wx, then of wx + 1
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int it = it0 + u * kGatherThreads;
+            const int wy = it / pw2, wx = 2 * (it - (it / pw2) * pw2);
+            const int Y0 = 2 * (i0 + wy), X0 = 2 * (j0 + wx);
+            const bool whole = X0 >= 0 && X0 + 3 < g.src_W;
+#pragma unroll
+            for (int dy = 0; dy < 2; ++dy) {
+              const int Y = Y0 + dy;
+              const bool row_in = it < items && (unsigned)Y < (unsigned)g.src_H;
+#pragma unroll
+              for (int c = 0; c < 3; ++c) {
+                const float* px = src + c * g.src_sc + Y * g.src_sh + X0;
+                if (row_in && whole) {
+                  d[u][c][dy] = __ldg(reinterpret_cast<const float4*>(px));
+                } else {
+                  float e[4];
+#pragma unroll
+                  for (int k = 0; k < 4; ++k)
+                    e[k] = row_in && (unsigned)(X0 + k) < (unsigned)g.src_W ? __ldg(px + k) : 0.0f;
+                  d[u][c][dy] = make_float4(e[0], e[1], e[2], e[3]);
+                }
+              }
+            }
+          }
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int it = it0 + u * kGatherThreads;
+            if (it >= items) continue;
+            const int wy = it / pw2, wx = 2 * (it - (it / pw2) * pw2);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              if (wx + h >= hw) continue;
+              const int r = wy * hw + wx + h;
+              // channel 3 q + c, q = 2 dy + dx: component 2 h + dx of d[c][dy]
+              float v[12];
+#pragma unroll
+              for (int c = 0; c < 3; ++c)
+#pragma unroll
+                for (int dy = 0; dy < 2; ++dy) {
+                  const float4 t = d[u][c][dy];
+                  v[3 * (2 * dy) + c] = h ? t.z : t.x;
+                  v[3 * (2 * dy + 1) + c] = h ? t.w : t.y;
+                }
+              float4* row = reinterpret_cast<float4*>(slot + r * 64);
+              const int sw = (r >> 1) & 3;
+              row[0 ^ sw] = make_float4(v[0], v[1], v[2], v[3]);
+              row[1 ^ sw] = make_float4(v[4], v[5], v[6], v[7]);
+              row[2 ^ sw] = make_float4(v[8], v[9], v[10], v[11]);
+              row[3 ^ sw] = make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+          }
+        }
+      } else {
+      // Up to four rows per thread in flight (the 4 x 4 stem window is
+      // 35 x 11 = 385 rows for 128 threads: one pass).
+#pragma unroll 1
+      for (int r0 = p; r0 < rows; r0 += 4 * kGatherThreads) {
+        float v[4][12];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int r = r0 + u * kGatherThreads;
+          const int wy = r / hw, wx = r - (r / hw) * hw;
+          const int Y0 = 2 * (i0 + wy), X0 = 2 * (j0 + wx);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int Y = Y0 + (q >> 1), X = X0 + (q & 1);
+            const bool in = r < rows && (unsigned)Y < (unsigned)g.src_H && (unsigned)X < (unsigned)g.src_W;
+            const float* px = src + Y * g.src_sh + X * g.src_sw;
+#pragma unroll
+            for (int c = 0; c < 3; ++c) v[u][3 * q + c] = in ? __ldg(px + c * g.src_sc) : 0.0f;
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int r = r0 + u * kGatherThreads;
+          if (r < rows) {
+            float4* row = reinterpret_cast<float4*>(slot + r * 64);
+            const int sw = (r >> 1) & 3;
+            row[0 ^ sw] = make_float4(v[u][0], v[u][1], v[u][2], v[u][3]);
+            row[1 ^ sw] = make_float4(v[u][4], v[u][5], v[u][6], v[u][7]);
+            row[2 ^ sw] = make_float4(v[u][8], v[u][9], v[u][10], v[u][11]);
+            row[3 ^ sw] = make_float4(0.f, 0.f, 0.f, 0.f);
+          }
+        }
+      }
+      }
+      tc::fence_proxy_async_smem();  // generic stores -> the MMAs' async-proxy reads
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&hfull[hs]);
+      if (++hs == kSlots) {
+        hs = 0;
+        hphase ^= 1;
+      }
+    }
   } else {
     // ---------------- epilogue: warps 3..6 upper, 7..10 lower block ----------------
     const int e = warp - 3, blk = e >> 2, quad = warp & 3;
@@ -2624,9 +2771,10 @@ static bool halo_pair_enabled() {
   return on;
 }
 
-template <int BN, int G, int STAGES, int CB, bool POOL, bool STAGED, bool PAIR>
+template <int BN, int G, int STAGES, int CB, bool POOL, bool STAGED, bool PAIR, bool GATHER>
 bool launch_halo_kernel(ConvArgs g, const float* w0, const char* op) {
-  using Cfg = HaloCfg<BN, G, STAGES, CB, POOL, STAGED, PAIR>;
+  using Cfg = HaloCfg<BN, G, STAGES, CB, POOL, STAGED, PAIR, GATHER>;
+  constexpr int kThreads = kHaloThreads + (GATHER ? kGatherThreads : 0);
   const int Kpad = g.K;  // taps x C4, a multiple of CB
   CUtensorMap tw, tx;
   const uint64_t dims[2] = {(uint64_t)Kpad, (uint64_t)g.Cout};
@@ -2642,13 +2790,16 @@ bool launch_halo_kernel(ConvArgs g, const float* w0, const char* op) {
   const uint32_t xbox[4] = {CB, (uint32_t)((kHaloTW + g.KW - 1) * g.sw),
                             (uint32_t)((2 * kHaloTH + g.KH - 1) * g.sh), 1};
   const uint32_t xes[4] = {1, (uint32_t)g.sw, (uint32_t)g.sh, 1};
-  if (!encode_tmap_f32(&tx, g.x_hi, 4, xd, xs, xbox, xes, op, Cfg::ROW)) return false;
+  if (GATHER)
+    memset(&tx, 0, sizeof(tx));  // windows come from the gathering warps
+  else if (!encode_tmap_f32(&tx, g.x_hi, 4, xd, xs, xbox, xes, op, Cfg::ROW))
+    return false;
   g.tiles_x = (int)cdiv(g.OW, kHaloTW);
   g.tiles_y = (int)cdiv(g.OH, 2 * kHaloTH);
   g.m_tiles = g.N * g.tiles_x * g.tiles_y;
   g.n_tiles = (int)cdiv(g.Cout, BN);
   g.tiles = (int64_t)g.m_tiles * g.n_tiles;
-  auto kern = conv_halo_kernel<BN, G, STAGES, CB, POOL, STAGED, PAIR>;
+  auto kern = conv_halo_kernel<BN, G, STAGES, CB, POOL, STAGED, PAIR, GATHER>;
   g.direct_epi = halo_direct(g) ? 1 : 0;
   if (!STAGED && !POOL && !g.direct_epi) {
     fail(NNC_CUDA_ERR_INVALID, op, "internal: unstaged halo instance for a staged epilogue");
@@ -2667,7 +2818,7 @@ bool launch_halo_kernel(ConvArgs g, const float* w0, const char* op) {
       attr_set[ctx().device] = true;
     }
     const int grid = (int)(units < sm_count() ? units : sm_count());
-    launch_pdl(kern, grid, kHaloThreads, Cfg::SMEM, tw, tx, g);
+    launch_pdl(kern, grid, kThreads, Cfg::SMEM, tw, tx, g);
     return check_launch(op);
   }
   cudaLaunchConfig_t cfg = {};
@@ -2676,7 +2827,7 @@ bool launch_halo_kernel(ConvArgs g, const float* w0, const char* op) {
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
-  cfg.blockDim = dim3(kHaloThreads, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = Cfg::SMEM;
   cfg.stream = ctx().stream;
   cfg.attrs = attr;
@@ -2713,14 +2864,26 @@ bool launch_halo_kernel(ConvArgs g, const float* w0, const char* op) {
 // N = 64 MMA instead of 6, against the shared-memory port that bounds N <=
 // 128); the pooled stem went 1.57 -> 1.76 ms in lockstep pairs, whose MMAs
 // wait for both CTAs' heavier epilogues.
-template <int BN, int G, int STAGES, int CB, bool POOL = false, bool STAGED = true>
+template <int BN, int G, int STAGES, int CB, bool POOL = false, bool STAGED = true,
+          bool GATHER = false>
 bool launch_halo(ConvArgs g, const float* w0, const char* op) {
   const int64_t m_tiles = (int64_t)g.N * cdiv(g.OW, kHaloTW) * cdiv(g.OH, 2 * kHaloTH);
-  if constexpr (!POOL) {
+  if constexpr (!POOL && !GATHER) {
     if (halo_pair_enabled() && m_tiles >= 2)
-      return launch_halo_kernel<BN, G, STAGES, CB, POOL, STAGED, true>(g, w0, op);
+      return launch_halo_kernel<BN, G, STAGES, CB, POOL, STAGED, true, false>(g, w0, op);
   }
-  return launch_halo_kernel<BN, G, STAGES, CB, POOL, STAGED, false>(g, w0, op);
+  return launch_halo_kernel<BN, G, STAGES, CB, POOL, STAGED, false, GATHER>(g, w0, op);
+}
+
+// Whether the pooled stem builds its space-to-depth windows in the conv
+// kernel (the default); NNC_CUDA_STEM_GATHER=0 runs the separate
+// space-to-depth pass instead (for comparison).
+static bool stem_gather_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("NNC_CUDA_STEM_GATHER");
+    return !(e && e[0] == '0');
+  }();
+  return on;
 }
 
 // Whether the halo kernel serves a call: stride 1 with windows of at most
@@ -2959,7 +3122,11 @@ void conv_impl(Tensor* input, Tensor* weight, Tensor* bias, Tensor* residual, Te
   if (!split && (!pool || pool_fused) && s2d_plan(C, KH, KW, sh, sw, ph, pw, &s2d) &&
       halo_eligible(C2, Cout, s2d.KH2, s2d.KW2, 1, 1, s2d.pad_h, s2d.pad_w, OH, OW, split, C2)) {
     const int H2 = (H + 1) / 2, W2 = (W + 1) / 2;
-    const int64_t x2 = (int64_t)N * H2 * W2 * C2, w2 = (int64_t)Cout * s2d.KH2 * s2d.KW2 * C2;
+    // The pooled 3-channel stem gathers its windows in the conv kernel: no
+    // space-to-depth copy of the input.
+    const bool gather = pool_fused && C == 3 && stem_gather_enabled();
+    const int64_t x2 = gather ? 0 : (int64_t)N * H2 * W2 * C2,
+                  w2 = (int64_t)Cout * s2d.KH2 * s2d.KW2 * C2;
     const size_t need2 = (size_t)((x2 + 63) / 64 * 64 + w2) * 4 + 256;
     if (!fixed || need2 <= fixed->bytes) {
       float* ws2 = fixed ? fixed->ptr : (float*)workspace(need2, op);
@@ -2970,7 +3137,9 @@ void conv_impl(Tensor* input, Tensor* weight, Tensor* bias, Tensor* residual, Te
       const int64_t sx_c = in_nhwc ? 1 : (int64_t)H * W, sx_h = in_nhwc ? (int64_t)W * C : W,
                     sx_w = in_nhwc ? C : 1;
       const size_t rows_smem = (size_t)2 * C * W * 4;
-      if (!in_nhwc && rows_smem <= 48 * 1024) {
+      if (gather) {
+        // nothing to convert
+      } else if (!in_nhwc && rows_smem <= 48 * 1024) {
         const bool vec = W % 4 == 0 && (((uintptr_t)input->data) & 15) == 0;
         const float* xin = (const float*)input->data;
         const int64_t xs_n = (int64_t)H * W * C;
@@ -2996,7 +3165,7 @@ void conv_impl(Tensor* input, Tensor* weight, Tensor* bias, Tensor* residual, Te
             (const float*)input->data, xs2, N, C, H, W, H2, W2, (int64_t)H * W * C, sx_c, sx_h,
             sx_w);
       }
-      if (!check_launch(op)) return;
+      if (!gather && !check_launch(op)) return;
       const int src_mode = packed ? (wl.element ? 2 : 1) : 0;
       launch_pdl(s2d_weight_kernel, grid_for(w2, 256, 8), 256, 0, (const float*)weight->data, wts2,
                  Cout, C, KH, KW, ph, pw, s2d.KH2, s2d.KW2, s2d.pad_h, s2d.pad_w, src_mode, wl.C4,
@@ -3036,7 +3205,23 @@ void conv_impl(Tensor* input, Tensor* weight, Tensor* bias, Tensor* residual, Te
         g.psw = pool->sw;
         g.pph = pool->ph;
         g.ppw = pool->pw;
-        launch_halo<64, 8, 3, 16, true>(g, wts2, op);
+        if (gather) {
+          g.x_hi = nullptr;
+          g.src = (const float*)input->data;
+          g.src_H = H;
+          g.src_W = W;
+          g.src_sn = (int64_t)H * W * C;
+          g.src_sc = sx_c;
+          g.src_sh = sx_h;
+          g.src_sw = sx_w;
+          // Two weight stages (the 16 resident taps): measured at batch
+          // 1024, 1279 us against 1383 with three; the smaller shared
+          // allocation leaves L1 room for the gathered rows (a third window
+          // slot: 1350; an L2 bulk prefetch of the next tile's rows: 2057).
+          launch_halo<64, 8, 2, 16, true, true, true>(g, wts2, op);
+        } else {
+          launch_halo<64, 8, 3, 16, true>(g, wts2, op);
+        }
         return;
       } else if (C2 == 16) {
         if (Cout > 64)
