@@ -446,10 +446,14 @@ __device__ __forceinline__ void mma_commit_pair_both(uint64_t* bar) {
       "h"((uint16_t)3)
       : "memory");
 }
-// Arrive on an mbarrier of another cluster CTA (a mapa address).
+// Arrive on an mbarrier of another cluster CTA (a mapa address), with the
+// default release at CTA scope. Its users hand a TMEM accumulator back to the
+// pair's MMA issuer: the arriving warps' TMEM reads are ordered by tcgen05
+// fences around the arrive and the wait, and the waiter reads nothing that
+// this CTA stored to global memory, which a cluster-scope release would
+// first wait for (ncu showed epilogue warps stalled on that memory barrier).
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
-               : "memory");
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 // TMA loads into this CTA's shared memory whose completion is counted on an
 // mbarrier of either CTA of the pair (`bar` a shared::cluster address).

@@ -283,7 +283,7 @@ def model_runs(so, torch, pk: dict, reps: int, only_model: str | None = None) ->
 # are larger than L2 so that DRAM counters mean something, but a few hundred
 # MB at most.
 PROFILE_CASES = ("layernorm", "layernorm256", "softmax", "softmax128", "transpose", "transpose_k", "add",
-                 "stem", "stage1")
+                 "stem", "stage1", "stage2s2")
 
 
 def profile_case(so, torch, case: str) -> None:
@@ -334,6 +334,16 @@ def profile_case(so, torch, case: str) -> None:
         shp = (n, 64, 56, 56)
         fn = lambda: so.nnc_conv_add_relu3x3_s1(R(x, L.TAG_NHWC, shp), rw.ptr, R(bias), R(res, L.TAG_NHWC, shp),
                                                 R(o, L.TAG_NHWC, shp))
+    elif case == "stage2s2":  # the stage-2 3x3/2 conv+relu at batch 256, channels-last, prepacked
+        n = 256
+        x, w, bias = rnd(n, 56, 56, 64), rnd(128, 64, 3, 3) * 0.05, rnd(128) * 0.01
+        wp = torch.empty(so.nnc_cuda_prepacked_conv_weight_bytes(R(w)) // 4, device="cuda")
+        rw = T.from_torch(w.clone())
+        keep.append(rw)
+        assert so.nnc_cuda_prepack_conv_weight(rw.ptr, ctypes.c_void_p(wp.data_ptr()), wp.numel() * 4) == 0
+        o = torch.empty(n, 28, 28, 128, device="cuda")
+        fn = lambda: so.nnc_conv_relu(R(x, L.TAG_NHWC, (n, 64, 56, 56)), rw.ptr, R(bias),
+                                      R(o, L.TAG_NHWC, (n, 128, 28, 28)), 3, 3, 2, 2, 1, 1)
     else:
         raise SystemExit(f"unknown case {case}")
     for _ in range(3):
