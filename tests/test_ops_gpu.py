@@ -335,6 +335,25 @@ STREAMK_CASES = [
 ]
 
 
+# Stride-2 3 x 3 windows over 32-channel blocks (the CTA-pair im2col route in
+# TF32 mode): the ResNet stage-2 shape, pad 1 and pad 0, a ragged 25 x 31
+# output with three channel blocks and C_out 100 (staged epilogue), two
+# 128-channel tiles.
+S2_CASES_3X3 = [
+    # n, c, h, w, co, k, s, p, op
+    (2, 64, 56, 56, 128, 3, 2, 1, "nnc_conv_relu"),
+    (2, 64, 57, 57, 64, 3, 2, 0, "nnc_conv"),
+    (1, 96, 50, 62, 100, 3, 2, 1, "nnc_conv_add_relu"),
+    (1, 64, 64, 64, 256, 3, 2, 1, "nnc_conv_add_relu"),
+]
+
+
+@pytest.mark.parametrize("prec", [0, 1])
+@pytest.mark.parametrize("cfg", S2_CASES_3X3, ids=lambda c: "x".join(str(v) for v in c[:8]))
+def test_conv_stride2_3x3_vs_oracle(cuda_lib, prec, cfg):
+    test_conv_cta_pairs_vs_oracle(cuda_lib, prec, cfg)
+
+
 @pytest.mark.parametrize("cfg", STREAMK_CASES, ids=lambda c: "x".join(str(v) for v in c[:8]))
 def test_conv_stream_k_vs_oracle(cuda_lib, cfg):
     test_conv_cta_pairs_vs_oracle(cuda_lib, 0, cfg, repeat=3)
