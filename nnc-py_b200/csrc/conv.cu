@@ -2774,6 +2774,7 @@ static bool halo_pair_enabled() {
 template <int BN, int G, int STAGES, int CB, bool POOL, bool STAGED, bool PAIR, bool GATHER>
 bool launch_halo_kernel(ConvArgs g, const float* w0, const char* op) {
   using Cfg = HaloCfg<BN, G, STAGES, CB, POOL, STAGED, PAIR, GATHER>;
+  static_assert(Cfg::SMEM <= 227 * 1024, "halo instance exceeds the shared memory of a CTA");
   constexpr int kThreads = kHaloThreads + (GATHER ? kGatherThreads : 0);
   const int Kpad = g.K;  // taps x C4, a multiple of CB
   CUtensorMap tw, tx;
@@ -2864,13 +2865,15 @@ bool launch_halo_kernel(ConvArgs g, const float* w0, const char* op) {
 // N = 64 MMA instead of 6, against the shared-memory port that bounds N <=
 // 128); the pooled stem went 1.57 -> 1.76 ms in lockstep pairs, whose MMAs
 // wait for both CTAs' heavier epilogues.
+// PG, PSTAGES: the weight ring of the CTA-pair instance (taps per stage,
+// stages), whose per-tap weight tiles are half as large.
 template <int BN, int G, int STAGES, int CB, bool POOL = false, bool STAGED = true,
-          bool GATHER = false>
+          bool GATHER = false, int PG = G, int PSTAGES = STAGES>
 bool launch_halo(ConvArgs g, const float* w0, const char* op) {
   const int64_t m_tiles = (int64_t)g.N * cdiv(g.OW, kHaloTW) * cdiv(g.OH, 2 * kHaloTH);
   if constexpr (!POOL && !GATHER) {
     if (halo_pair_enabled() && m_tiles >= 2)
-      return launch_halo_kernel<BN, G, STAGES, CB, POOL, STAGED, true, false>(g, w0, op);
+      return launch_halo_kernel<BN, PG, PSTAGES, CB, POOL, STAGED, true, false>(g, w0, op);
   }
   return launch_halo_kernel<BN, G, STAGES, CB, POOL, STAGED, false, GATHER>(g, w0, op);
 }
@@ -3380,14 +3383,18 @@ void conv_impl(Tensor* input, Tensor* weight, Tensor* bias, Tensor* residual, Te
     // Direct-epilogue calls take the unstaged instances, whose deeper weight
     // rings cover the weight stream's L2 latency.
     const bool direct = halo_direct(g);
+    // Pair rings measured at batch 1024 (graph replay): stage-2 3 x 3 337.9
+    // -> 329.7 us with 3 taps x 4 stages (against 1 x 7), stage-1 418.8 ->
+    // 402.5 us with all 9 taps x 2 stages (against 3 x 5; 9 x 3 took 437.2:
+    // a larger shared allocation leaves less L1).
     if (Cout > 64) {
       if (direct)
-        launch_halo<128, 1, 7, 32, false, false>(g, w0, op);
+        launch_halo<128, 1, 7, 32, false, false, false, 3, 4>(g, w0, op);
       else
         launch_halo<128, 1, 4, 32>(g, w0, op);
     } else {
       if (direct)
-        launch_halo<64, 3, 5, 32, false, false>(g, w0, op);
+        launch_halo<64, 3, 5, 32, false, false, false, 9, 2>(g, w0, op);
       else
         launch_halo<64, 3, 3, 32>(g, w0, op);
     }
