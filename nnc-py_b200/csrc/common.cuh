@@ -59,8 +59,11 @@ void* workspace(size_t bytes, const char* op);
 constexpr size_t kStreamKCounterBytes = 4096;
 bool streamk_scratch(int slots, size_t slot_bytes, unsigned** counters, float** parts);
 
-// Max pooling between two device buffers (pool.cu), nnc_maxpool2d semantics.
+// Max / average pooling between two device buffers (pool.cu), nnc_maxpool2d /
+// nnc_avgpool2d semantics.
 bool launch_maxpool_f32(const float* in, float* out, int N, int C, int H, int W, int OH, int OW,
+                        int kh, int kw, int sh, int sw, int ph, int pw, bool nhwc, const char* op);
+bool launch_avgpool_f32(const float* in, float* out, int N, int C, int H, int W, int OH, int OW,
                         int kh, int kw, int sh, int sw, int ph, int pw, bool nhwc, const char* op);
 
 // Opened at the top of every entry point: refreshes the thread's device from

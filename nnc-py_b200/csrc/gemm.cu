@@ -1149,12 +1149,19 @@ void gemm_impl(Tensor* a, Tensor* b, Tensor* c, Tensor* out, float alpha, float 
   run_problem(p, op);
 }
 
-// nnc_gemm_nt semantics (ops.c:1843-1886): B stored [N, K].
+// nnc_gemm_nt semantics (ops.c:1843-1886): B stored [N, K]. The body, for
+// callers that have opened the call's scope themselves.
+void gemm_nt_body(Tensor* a, Tensor* b, Tensor* c, Tensor* out, float alpha, float beta, int relu,
+                  const char* op);
 void gemm_nt_impl(Tensor* a, Tensor* b, Tensor* c, Tensor* out, float alpha, float beta, int relu,
                   const char* op) {
   OpScope scope(op);
   if (!f32(a, op, "a") || !f32(b, op, "b") || !f32(out, op, "output")) return;
   trace_io(tensor_bytes(a) + tensor_bytes(b) + tensor_bytes(c), tensor_bytes(out));
+  gemm_nt_body(a, b, c, out, alpha, beta, relu, op);
+}
+void gemm_nt_body(Tensor* a, Tensor* b, Tensor* c, Tensor* out, float alpha, float beta, int relu,
+                  const char* op) {
   int M, N, K;
   if (a->ndim == 2 && b->ndim == 2) {
     M = (int)a->shape[0];
@@ -1291,6 +1298,36 @@ void nnc_gemm_nt(Tensor* a, Tensor* b, Tensor* c, Tensor* output, float alpha, f
 }
 void nnc_gemm_nt_relu(Tensor* a, Tensor* b, Tensor* c, Tensor* output, float alpha, float beta) {
   gemm_nt_impl(a, b, c, output, alpha, beta, 1, "nnc_gemm_nt_relu");
+}
+
+// GlobalAveragePool -> Flatten -> Gemm(transB = 1) as one call: the pooled
+// [N, C] features go to the end of the workspace (whose front holds what the
+// GEMM itself may need: the 3xTF32 hi/lo planes of both operands), never to
+// an arena tensor, and no flatten copy runs. Same arithmetic as
+// nnc_avgpool2d(kernel = stride = H x W) then nnc_gemm_nt.
+void nnc_gap_gemm_nt(Tensor* input, Tensor* b, Tensor* c, Tensor* output, float alpha,
+                     float beta) {
+  const char* op = "nnc_gap_gemm_nt";
+  OpScope scope(op);
+  if (!f32(input, op, "input") || !f32(b, op, "b") || !f32(output, op, "output")) return;
+  if (input->ndim != 4 || b->ndim != 2 || input->shape[1] != b->shape[1]) {
+    fail(NNC_CUDA_ERR_INVALID, op, "expected a 4-D input [N, C, H, W] and b [O, C]");
+    return;
+  }
+  trace_io(tensor_bytes(input) + tensor_bytes(b) + tensor_bytes(c), tensor_bytes(output));
+  const int64_t N = input->shape[0], C = input->shape[1], O = b->shape[0];
+  const int H = (int)input->shape[2], W = (int)input->shape[3];
+  const bool split = ctx().precision == NNC_CUDA_PRECISION_3XTF32;
+  const size_t front = ((split ? 2 * (size_t)(N * C + O * C) * 4 : 0) + 64 + 255) & ~(size_t)255;
+  char* ws = (char*)workspace(front + (size_t)N * C * 4, op);
+  if (!ws) return;
+  float* pooled = (float*)(ws + front);
+  if (!launch_avgpool_f32((const float*)input->data, pooled, (int)N, (int)C, H, W, 1, 1, H, W, H, W,
+                          0, 0, is_nhwc(input), op))
+    return;
+  int64_t shape[2] = {N, C};
+  Tensor flat{pooled, NNC_DTYPE_FLOAT32, shape, 2, N * C * 4};
+  gemm_nt_body(&flat, b, c, output, alpha, beta, 0, op);
 }
 void nnc_matmul(Tensor* a, Tensor* b, Tensor* output) {
   matmul_impl(a, b, nullptr, output, 0, "nnc_matmul");

@@ -305,6 +305,16 @@ bool launch_maxpool_f32(const float* in, float* out, int N, int C, int H, int W,
   return check_launch(op);
 }
 
+// Average pooling between two device buffers (nnc_avgpool2d semantics), for
+// fused callers whose pooled output is an intermediate.
+bool launch_avgpool_f32(const float* in, float* out, int N, int C, int H, int W, int OH, int OW,
+                        int kh, int kw, int sh, int sw, int ph, int pw, bool nhwc, const char* op) {
+  PoolGeom g{N, C, H, W, OH, OW, kh, kw, sh, sw, ph, pw};
+  if ((int64_t)N * C * OH * OW == 0) return true;
+  launch_pool<false>(in, out, g, nhwc);
+  return check_launch(op);
+}
+
 }  // namespace nnc
 
 extern "C" {

@@ -306,6 +306,40 @@ class MatMulEpilogueFusionPass(PassBase):
                 _replace(g, [node, nxt, sm], fused, [mm, scaled])
 
 
+class GapGemmFusionPass(PassBase):
+    """Collapses the classifier head GlobalAveragePool -> Flatten(axis 1) ->
+    Gemm into one GEMM node called as nnc_gap_gemm_nt (the pooled features
+    stay in the library's scratch; no flatten copy). The Gemm must not
+    transpose A and its B must be a constant or already transposed, so that
+    PrepackLowering leaves it in the gemm_nt form (passes/prepack_lowering.py:
+    80-117). The node keeps op type GEMM with metadata ``cuda_fused =
+    "gap_gemm"`` and inputs [pool input, B, C]."""
+
+    @property
+    def name(self) -> str:
+        return "CudaGapGemmFusion"
+
+    def _execute(self, ctx: CompileContext) -> None:
+        g = ctx.graph
+        for node in list(g.topological_sort()):
+            if node.name not in g.nodes or node.op_type != OpType.GLOBAL_AVGPOOL or len(node.inputs) != 1:
+                continue
+            flat = _single_consumer(g, node.outputs[0])
+            if flat is None or flat.op_type != OpType.FLATTEN or int(flat.attrs.get("axis", 1)) != 1:
+                continue
+            gemm = _single_consumer(g, flat.outputs[0])
+            if gemm is None or gemm.op_type != OpType.GEMM or gemm.metadata.get("cuda_fused"):
+                continue
+            if gemm.inputs[0] != flat.outputs[0] or int(gemm.attrs.get("transA", 0)) != 0:
+                continue
+            if len(gemm.inputs) < 2 or not (int(gemm.attrs.get("transB", 0)) == 1 or gemm.inputs[1] in g.constants):
+                continue
+            fused = Node(OpType.GEMM, f"{gemm.name}_gap", [node.inputs[0]] + list(gemm.inputs[1:]),
+                         list(gemm.outputs), dict(gemm.attrs),
+                         metadata={"cuda_fused": "gap_gemm", "fused_from": [node.name, flat.name, gemm.name]})
+            _replace(g, [node, flat, gemm], fused, [node.outputs[0], flat.outputs[0]])
+
+
 # Whether O3 fuses Conv+ReLU -> MaxPool into nnc_conv_relu_maxpool. On: on
 # the ResNet stem at batch 1024 the fused call (pooled epilogue in the conv
 # kernel, 1.83 ms) beats the conv and pool kernels it replaces (2.42 ms) and
@@ -319,7 +353,8 @@ def cuda_passes(opt_level: int, fuse_conv_relu_maxpool: bool | None = None) -> l
     O0-O2: nnc-py's own lists (passes/base.py:88-106). O3: cleanup, nnc-py's
     PatternFusion (conv_relu, add_relu, ...), the Conv+Add+Relu group (and
     the Conv+Relu+MaxPool group when enabled), the Gemm+Relu group, the
-    MatMul epilogue groups (bias, bias+relu, scale+softmax), PrepackLowering
+    GlobalAveragePool+Flatten+Gemm head, the MatMul epilogue groups (bias,
+    bias+relu, scale+softmax), PrepackLowering
     (entry-point selection, Gemm weight prepack), liveness and the
     cost_aware arena plan. nnc-py's NPU tiling passes are not used:
     the GPU kernels tile internally.
@@ -336,7 +371,7 @@ def cuda_passes(opt_level: int, fuse_conv_relu_maxpool: bool | None = None) -> l
     fuse_pool = FUSE_CONV_RELU_MAXPOOL if fuse_conv_relu_maxpool is None else fuse_conv_relu_maxpool
     return [IdentityEliminationPass(), DeadCodeEliminationPass(), PatternFusionPass(), ConvAddReluFusionPass()] + (
         [ConvReluMaxPoolFusionPass()] if fuse_pool else []) + [
-        GemmReluFusionPass(), MatMulEpilogueFusionPass(),
+        GemmReluFusionPass(), GapGemmFusionPass(), MatMulEpilogueFusionPass(),
         PrepackLoweringPass(), LivenessAnalysisPass(), MemoryPlanningPassV2()]
 
 
@@ -372,6 +407,8 @@ def channels_last_tensors(ctx: CompileContext) -> set[str]:
             for t in acts:
                 if t not in full:
                     bad.add(t)  # broadcast operand: keep logical order
+        elif node.metadata.get("cuda_fused") == "gap_gemm":
+            continue  # its 4-D input may be channels-last (the pooling reads either)
         elif node.op_type in _NHWC_OPS:
             if node.op_type in (OpType.MAXPOOL, OpType.AVGPOOL, OpType.GLOBAL_AVGPOOL):
                 if node.inputs[0] in four_d and node.outputs[0] in four_d:
@@ -397,7 +434,8 @@ def channels_last_tensors(ctx: CompileContext) -> set[str]:
 # ------------------------------------------------------------- emitter ----
 class CudaEmitter(CEmitter):
     """nnc-py's CEmitter with the cuda target's fused calls: conv+add+relu,
-    conv+relu+maxpool, gemm+relu, matmul+bias and matmul+scale+softmax."""
+    conv+relu+maxpool, gemm+relu, the pooled classifier head (gap+gemm),
+    matmul+bias and matmul+scale+softmax."""
 
     def _emit_includes(self, ctx: CompileContext) -> None:
         super()._emit_includes(ctx)
@@ -432,6 +470,16 @@ class CudaEmitter(CEmitter):
             for text in lines:
                 text = text.replace("nnc_gemm_nt(", "nnc_gemm_nt_relu(").replace("nnc_gemm(", "nnc_gemm_relu(")
                 self.write_line(text)
+            return
+        if fused == "gap_gemm":
+            sym = ctx.tensor_symbols
+            x, w = node.inputs[:2]
+            c = node.inputs[2] if len(node.inputs) > 2 and node.inputs[2] else ""
+            alpha = float(node.attrs.get("alpha", 1.0))
+            beta = float(node.attrs.get("beta", 1.0))
+            args = [f"&{sym[x]}", f"&{sym[w]}", f"&{sym[c]}" if c else "NULL", f"&{sym[node.outputs[0]]}",
+                    f"{alpha!r}f", f"{beta!r}f"]
+            self.write_line(f"nnc_gap_gemm_nt({', '.join(args)});")
             return
         if fused in ("matmul_bias", "matmul_scale_softmax"):
             sym = ctx.tensor_symbols

@@ -489,6 +489,22 @@ void nnc_matmul_scale_softmax(Tensor* a, Tensor* b, Tensor* out, float alpha) {
     nnc_softmax(out, out, -1);
 }
 
+/* GlobalAveragePool -> Flatten -> Gemm(transB = 1), the cuda target's O3
+ * head group: the reference's avgpool with kernel = stride = H x W
+ * (ops.c:393-461), its flatten (a copy, ops.c:1521) and gemm_nt
+ * (ops.c:1843-1886), composed. */
+void nnc_gap_gemm_nt(Tensor* in, Tensor* b, Tensor* c, Tensor* out, float alpha, float beta) {
+    const int64_t N = in->shape[0], C = in->shape[1];
+    const int H = (int)in->shape[2], W = (int)in->shape[3];
+    float* pooled = (float*)malloc((size_t)(N * C > 0 ? N * C : 1) * sizeof(float));
+    int64_t s4[4] = {N, C, 1, 1}, s2[2] = {N, C};
+    Tensor p4 = {pooled, NNC_DTYPE_FLOAT32, s4, 4, N * C * 4};
+    Tensor p2 = {pooled, NNC_DTYPE_FLOAT32, s2, 2, N * C * 4};
+    nnc_avgpool2d(in, &p4, H, W, H, W, 0, 0);
+    nnc_gemm_nt(&p2, b, c, out, alpha, beta);
+    free(pooled);
+}
+
 /* ---------------------------------------------------------------------------
  * Data movement (ops.c:1510-1601, :1995-2086, :2173-2251).
  * ------------------------------------------------------------------------- */

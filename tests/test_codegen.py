@@ -63,7 +63,7 @@ def test_o3_fuses_every_residual_join(tmp_path):
     assert calls.count("nnc_conv_add_relu3x3_s1") == 8
     assert "nnc_add" not in calls and "nnc_relu" not in calls and "nnc_add_relu" not in calls
     assert calls.count("nnc_conv_relu3x3_s1") + calls.count("nnc_conv_relu") == 8
-    assert calls[0] == "nnc_conv_relu_maxpool" and calls[-1] == "nnc_gemm_nt"
+    assert calls[0] == "nnc_conv_relu_maxpool" and calls[-1] == "nnc_gap_gemm_nt"
 
 
 def test_o3_conv_relu_maxpool_group(tmp_path):
@@ -91,6 +91,21 @@ def test_o3_gemm_relu_group(tmp_path):
     assert calls.count("nnc_maxpool2d") == 2 and "nnc_conv_relu_maxpool" not in calls
 
 
+def test_o3_gap_gemm_head(tmp_path):
+    """ResNet's GlobalAveragePool -> Flatten -> Gemm head becomes one
+    nnc_gap_gemm_nt call reading the channels-last stage-4 output; the pooled
+    and flattened tensors leave the graph (no arena slots)."""
+    man = CG.compile_model(W.resnet18(2), tmp_path, opt_level=3)
+    calls = man["calls"]
+    assert calls[-1] == "nnc_gap_gemm_nt" and calls.count("nnc_gap_gemm_nt") == 1
+    assert "nnc_avgpool2d" not in calls and "nnc_flatten" not in calls and "nnc_gemm_nt" not in calls
+    src = (tmp_path / "model.c").read_text()
+    assert "nnc_gap_gemm_nt(&tensor_layer4_1_out_relu, &tensor_fc_w, &tensor_fc_b, &tensor_logits, 1.0f, 1.0f);" in src
+    tensors = (tmp_path / "tensors.c").read_text()
+    assert "Tensor tensor_gap " not in tensors and "Tensor tensor_flat " not in tensors
+    assert "tensor_layer4_1_out_relu = {.data = NULL, .dtype = (nnc_dtype_t)(NNC_DTYPE_FLOAT32 | NNC_CUDA_TAG_NHWC)" in tensors
+
+
 def test_o3_matmul_epilogue_groups(tmp_path):
     """The transformer's MatMul -> Add(bias) [-> Relu] and MatMul -> Div(8) ->
     Softmax chains each become one call; the residual Adds, LayerNorms and
@@ -113,7 +128,9 @@ def test_channels_last_assignment(tmp_path):
     man = CG.compile_model(W.resnet18(2), tmp_path, opt_level=3)
     cl = set(man["channels_last"])
     assert "tensor_input" not in cl          # user-facing NCHW input
-    assert "tensor_pool1" in cl and "tensor_gap" in cl
+    # The pooled classifier head (one call) reads the stage-4 output
+    # channels-last; its pooled and flattened tensors are gone.
+    assert "tensor_pool1" in cl and "tensor_layer4_1_out_relu" in cl and "tensor_gap" not in cl
     assert "tensor_logits" not in cl and "tensor_flat" not in cl  # 2-D
     man_t = CG.compile_model(W.transformer(1), tmp_path / "t", opt_level=1)
     assert man_t["channels_last"] == []  # 4-D tensors meet transpose/softmax

@@ -335,6 +335,44 @@ STREAMK_CASES = [
 ]
 
 
+# The GlobalAveragePool -> Flatten -> Gemm head as one call (the ResNet
+# classifier; odd extents, no bias, a [N, O] bias with alpha/beta), both
+# precisions, NCHW and channels-last inputs, against the oracle's composition
+# of the reference's avgpool, flatten and gemm_nt.
+GAP_GEMM_CASES = [
+    # n, c, h, w, o, bias
+    (8, 512, 7, 7, 1000, "row"),
+    (3, 96, 5, 3, 33, None),
+    (130, 64, 2, 2, 257, "full"),
+]
+
+
+@pytest.mark.parametrize("prec", [0, 1])
+@pytest.mark.parametrize("cfg", GAP_GEMM_CASES, ids=lambda c: "x".join(str(v) for v in c))
+def test_gap_gemm_nt_vs_oracle(cuda_lib, prec, cfg):
+    n, c, h, w, o, bias = cfg
+    r = np.random.default_rng(29 + n + c + o)
+    arrays = {"x": r.standard_normal((n, c, h, w)).astype(np.float32),
+              "b": (r.standard_normal((o, c)) * 0.05).astype(np.float32)}
+    args = [C._t("x"), C._t("b")]
+    if bias == "row":
+        arrays["c"] = r.uniform(-0.01, 0.01, o).astype(np.float32)
+        args.append(C._t("c"))
+    elif bias == "full":
+        arrays["c"] = r.standard_normal((n, o)).astype(np.float32)
+        args.append(C._t("c"))
+    else:
+        args.append({"k": "null"})
+    alpha, beta = (1.0, 1.0) if bias != "full" else (0.5, -2.0)
+    args += [C._o("out", (n, o)), C._f(alpha), C._f(beta)]
+    case = {"name": "g", "op": "nnc_gap_gemm_nt", "args": args}
+    cuda_lib.nnc_cuda_set_precision(prec)
+    want = C.run_host(_oracle(), case, arrays)["out"]
+    for nhwc in (set(), {"x"}):
+        got = C.run_cuda(cuda_lib, case, arrays, nhwc=nhwc)["out"]
+        C.assert_close(got, want, C.TC_RTOL[prec], f"gap_gemm_nt{cfg}{sorted(nhwc)}")
+
+
 # Stride-2 3 x 3 windows over 32-channel blocks (the CTA-pair im2col route in
 # TF32 mode): the ResNet stage-2 shape, pad 1 and pad 0, a ragged 25 x 31
 # output with three channel blocks and C_out 100 (staged epilogue), two
