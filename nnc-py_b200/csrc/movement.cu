@@ -255,11 +255,13 @@ void nnc_identity(Tensor* input, Tensor* output) {
   copy_bytes(output->data, input->data, (size_t)n * sizeof(float), op);
 }
 
-void nnc_transpose(Tensor* input, Tensor* output, int64_t* perm, int ndim) {
-  const char* op = "nnc_transpose";
-  OpScope scope(op);
-  if (!valid_tensor(input, op, "input") || !valid_tensor(output, op, "output")) return;
-  trace_io(tensor_bytes(input), tensor_bytes(output));
+}  // extern "C"
+
+namespace nnc {
+namespace {
+// nnc_transpose after the scope and the NULL checks (transpose_shaped passes
+// views of its tensors).
+void transpose_tensors(Tensor* input, Tensor* output, int64_t* perm, int ndim, const char* op) {
   if (ndim < 1 || ndim > 8 || ndim != input->ndim || ndim != output->ndim) {
     fail(NNC_CUDA_ERR_INVALID, op, "ndim %d does not match the tensors (%d, %d)", ndim,
          input->ndim, output->ndim);
@@ -411,6 +413,61 @@ void nnc_transpose(Tensor* input, Tensor* output, int64_t* perm, int ndim) {
           (const int64_t*)input->data, (int64_t*)output->data, total, p);
   }
   check_launch(op);
+}
+
+}  // namespace
+}  // namespace nnc
+
+extern "C" {
+
+void nnc_transpose(Tensor* input, Tensor* output, int64_t* perm, int ndim) {
+  const char* op = "nnc_transpose";
+  OpScope scope(op);
+  if (!valid_tensor(input, op, "input") || !valid_tensor(output, op, "output")) return;
+  trace_io(tensor_bytes(input), tensor_bytes(output));
+  transpose_tensors(input, output, perm, ndim, op);
+}
+
+// Reshape -> Transpose and Transpose -> Reshape as one call: the input read
+// with extents in_shape (NULL: its own), permuted by perm, the output written
+// as the permuted extents in row-major order whatever its own shape says
+// (element counts must agree). Equals nnc_reshape / nnc_transpose /
+// nnc_reshape composed: the reshapes are views, so no copy runs for them.
+void nnc_transpose_shaped(Tensor* input, Tensor* output, int64_t* in_shape, int64_t* perm,
+                          int ndim) {
+  const char* op = "nnc_transpose_shaped";
+  OpScope scope(op);
+  if (!valid_tensor(input, op, "input") || !valid_tensor(output, op, "output")) return;
+  trace_io(tensor_bytes(input), tensor_bytes(output));
+  if (ndim < 1 || ndim > 8 || (!in_shape && ndim != input->ndim)) {
+    fail(NNC_CUDA_ERR_INVALID, op, "ndim %d does not fit the input (%d)", ndim, input->ndim);
+    return;
+  }
+  int64_t ish[8], osh[8], pm[8];
+  bool seen[8] = {};
+  int64_t n = 1;
+  for (int i = 0; i < ndim; ++i) {
+    ish[i] = in_shape ? in_shape[i] : input->shape[i];
+    pm[i] = perm ? perm[i] : (ndim - 1 - i);
+    if (pm[i] < 0 || pm[i] >= ndim || seen[pm[i]] || ish[i] < 0) {
+      fail(NNC_CUDA_ERR_INVALID, op, "perm or shape entry %d invalid", i);
+      return;
+    }
+    seen[pm[i]] = true;
+    n *= ish[i];
+  }
+  if (n != numel(input) || n != numel(output)) {
+    fail(NNC_CUDA_ERR_INVALID, op, "element counts differ (%lld, %lld, %lld)", (long long)n,
+         (long long)numel(input), (long long)numel(output));
+    return;
+  }
+  for (int i = 0; i < ndim; ++i) osh[i] = ish[pm[i]];
+  Tensor vin = *input, vout = *output;
+  vin.shape = ish;
+  vin.ndim = ndim;
+  vout.shape = osh;
+  vout.ndim = ndim;
+  transpose_tensors(&vin, &vout, pm, ndim, op);
 }
 
 void nnc_concat(Tensor** inputs, Tensor* output, int num_inputs, int axis) {

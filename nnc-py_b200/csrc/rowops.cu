@@ -376,10 +376,14 @@ __global__ void __launch_bounds__(kThreads) layernorm_kernel(
 // 16-byte loads and stores. Statistics: pairwise fp32 sums per lane combined
 // in fp64; outputs scale * ((x - mean) * (1 / sd)) + bias (within one ulp of
 // the division).
+// `res` (nullable): a second addend of the same shape, added to the input as
+// it is loaded (one fp32 rounding, the reference's nnc_add) before the
+// statistics: layernorm(in + res) in one pass (nnc_add_layernorm).
 template <int VPT, bool VEC>
 __global__ void __launch_bounds__(kThreads, VPT <= 8 ? 4 : 2) layernorm_warp_kernel(
-    const float* __restrict__ in, const float* __restrict__ scale, const float* __restrict__ bias,
-    float* __restrict__ out, int64_t rows, int len, int inner, float eps) {
+    const float* __restrict__ in, const float* __restrict__ res, const float* __restrict__ scale,
+    const float* __restrict__ bias, float* __restrict__ out, int64_t rows, int len, int inner,
+    float eps) {
   static_assert(!VEC || VPT % 4 == 0, "vector slabs hold whole float4 runs");
   const int lane = threadIdx.x & 31;
   const int64_t step = (int64_t)gridDim.x * (kThreads / 32);
@@ -399,19 +403,25 @@ __global__ void __launch_bounds__(kThreads, VPT <= 8 ? 4 : 2) layernorm_warp_ker
   }
   auto load_row = [&](int64_t row, float (&v)[VPT]) {
     const float* x = in + row * len;
+    const float* r = res ? res + row * len : nullptr;
     if constexpr (VEC) {
 #pragma unroll
       for (int k = 0; k < VPT; k += 4) {
         const int i = row_index<true>(lane, k);
         float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
         if (i < len) t = __ldg(reinterpret_cast<const float4*>(x + i));
+        if (r && i < len) {
+          const float4 u = __ldg(reinterpret_cast<const float4*>(r + i));
+          t = make_float4(__fadd_rn(t.x, u.x), __fadd_rn(t.y, u.y), __fadd_rn(t.z, u.z),
+                          __fadd_rn(t.w, u.w));
+        }
         v[k] = t.x; v[k + 1] = t.y; v[k + 2] = t.z; v[k + 3] = t.w;
       }
     } else {
 #pragma unroll
       for (int k = 0; k < VPT; ++k) {
         const int i = row_index<false>(lane, k);
-        v[k] = i < len ? x[i] : 0.0f;
+        v[k] = i < len ? (r ? __fadd_rn(x[i], r[i]) : x[i]) : 0.0f;
       }
     }
   };
@@ -480,8 +490,9 @@ __global__ void __launch_bounds__(kThreads, VPT <= 8 ? 4 : 2) layernorm_warp_ker
 // order (fp64), each group synchronising on its own named barrier.
 template <int WPR>
 __global__ void __launch_bounds__(kThreads) layernorm_group_kernel(
-    const float* __restrict__ in, const float* __restrict__ scale, const float* __restrict__ bias,
-    float* __restrict__ out, int64_t rows, int len, int inner, float eps) {
+    const float* __restrict__ in, const float* __restrict__ res, const float* __restrict__ scale,
+    const float* __restrict__ bias, float* __restrict__ out, int64_t rows, int len, int inner,
+    float eps) {
   constexpr int kGroups = kThreads / 32 / WPR;
   constexpr int kRuns = 1024 / (WPR * 32 * 4);  // float4 runs per lane
   constexpr int VPT = 4 * kRuns;
@@ -495,11 +506,17 @@ __global__ void __launch_bounds__(kThreads) layernorm_group_kernel(
   auto group_sync = [&]() { asm volatile("bar.sync %0, %1;" ::"r"(bar), "r"(WPR * 32) : "memory"); };
   auto load = [&](int64_t row, float (&v)[VPT]) {
     const float* x = in + row * len;
+    const float* rr = res ? res + row * len : nullptr;
 #pragma unroll
     for (int r = 0; r < kRuns; ++r) {
       const int i = 4 * (tg + r * WPR * 32);
       float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
       if (i < len) t = __ldg(reinterpret_cast<const float4*>(x + i));
+      if (rr && i < len) {
+        const float4 u = __ldg(reinterpret_cast<const float4*>(rr + i));
+        t = make_float4(__fadd_rn(t.x, u.x), __fadd_rn(t.y, u.y), __fadd_rn(t.z, u.z),
+                        __fadd_rn(t.w, u.w));
+      }
       v[4 * r] = t.x; v[4 * r + 1] = t.y; v[4 * r + 2] = t.z; v[4 * r + 3] = t.w;
     }
   };
@@ -759,13 +776,25 @@ void nnc_softmax(Tensor* input, Tensor* output, int axis) {
   check_launch(op);
 }
 
-void nnc_layernorm(Tensor* input, Tensor* scale, Tensor* bias, Tensor* output, int axis,
-                   float epsilon) {
-  const char* op = "nnc_layernorm";
-  OpScope scope(op);
+}  // extern "C"
+
+namespace nnc {
+namespace {
+// nnc_layernorm of (input + res) when res is given (same extents as the
+// input): the warp and group kernels add on load; the longer-slab kernels
+// run nnc_add into the output first and normalise it in place.
+void layernorm_impl(Tensor* input, Tensor* res, Tensor* scale, Tensor* bias, Tensor* output,
+                    int axis, float epsilon, const char* op) {
   if (!f32_plain(input, op, "input") || !f32_plain(output, op, "output")) return;
+  if (res && !f32_plain(res, op, "addend")) return;
   if ((scale && !f32_plain(scale, op, "scale")) || (bias && !f32_plain(bias, op, "bias"))) return;
-  trace_io(tensor_bytes(input) + tensor_bytes(scale) + tensor_bytes(bias), tensor_bytes(output));
+  trace_io(tensor_bytes(input) + tensor_bytes(res) + tensor_bytes(scale) + tensor_bytes(bias),
+           tensor_bytes(output));
+  if (res && numel(res) != numel(input)) {
+    fail(NNC_CUDA_ERR_INVALID, op, "the addends differ in size (%lld, %lld)",
+         (long long)numel(input), (long long)numel(res));
+    return;
+  }
   int64_t outer, norm, inner;
   if (!decompose(input, axis, &outer, &norm, &inner, op)) return;
   if (numel(output) < outer * norm * inner) {
@@ -779,6 +808,7 @@ void nnc_layernorm(Tensor* input, Tensor* scale, Tensor* bias, Tensor* output, i
   }
   if (outer * norm * inner == 0) return;
   const float* pi = (const float*)input->data;
+  const float* pr = res ? (const float*)res->data : nullptr;
   const float* ps = scale ? (const float*)scale->data : nullptr;
   const float* pb = bias ? (const float*)bias->data : nullptr;
   float* po = (float*)output->data;
@@ -787,17 +817,18 @@ void nnc_layernorm(Tensor* input, Tensor* scale, Tensor* bias, Tensor* output, i
     const int64_t blocks = cdiv(outer, (int64_t)(kThreads / 32));
     const int l = (int)len, in1 = (int)inner;
     cudaStream_t st = ctx().stream;
-    const bool vec = len % 4 == 0 && aligned16(pi) && aligned16(po);
+    const bool vec = len % 4 == 0 && aligned16(pi) && aligned16(po) && (!pr || aligned16(pr));
     if (len > 512 && vec) {
       const int64_t gblocks = cdiv(outer, (int64_t)(kThreads / 32 / 4));
       const int ggrid = resident_grid(layernorm_group_kernel<4>, kThreads, 0, gblocks);
-      layernorm_group_kernel<4><<<ggrid, kThreads, 0, st>>>(pi, ps, pb, po, outer, l, in1, epsilon);
+      layernorm_group_kernel<4><<<ggrid, kThreads, 0, st>>>(pi, pr, ps, pb, po, outer, l, in1,
+                                                          epsilon);
       check_launch(op);
       return;
     }
 #define NNC_LN_WARP(VPT, VEC)                                                                  \
   layernorm_warp_kernel<VPT, VEC><<<resident_grid(layernorm_warp_kernel<VPT, VEC>, kThreads, 0, blocks), \
-                                    kThreads, 0, st>>>(pi, ps, pb, po, outer, l, in1, epsilon)
+                                    kThreads, 0, st>>>(pi, pr, ps, pb, po, outer, l, in1, epsilon)
     if (len <= 64)
       NNC_LN_WARP(2, false);
     else if (len <= 128 && vec)
@@ -817,6 +848,15 @@ void nnc_layernorm(Tensor* input, Tensor* scale, Tensor* bias, Tensor* output, i
     else
       NNC_LN_WARP(32, false);
 #undef NNC_LN_WARP
+  } else if (pr) {
+    // Longer slabs: the sum into the output, then the output normalised in
+    // place (each kernel reads a slab before writing it).
+    nnc_add(input, res, output);
+    Tensor sum = *output;
+    sum.ndim = input->ndim;
+    sum.shape = input->shape;
+    layernorm_impl(&sum, nullptr, scale, bias, output, axis, epsilon, op);
+    return;
   } else if (len <= kSmemRowMax) {
     const size_t smem = (size_t)len * 4;
     if (smem > 48 * 1024 &&
@@ -832,6 +872,27 @@ void nnc_layernorm(Tensor* input, Tensor* scale, Tensor* bias, Tensor* output, i
     layernorm_kernel<<<grid, kThreads, 0, ctx().stream>>>(pi, ps, pb, po, outer, norm, inner, epsilon);
   }
   check_launch(op);
+}
+}  // namespace
+}  // namespace nnc
+
+extern "C" {
+
+void nnc_layernorm(Tensor* input, Tensor* scale, Tensor* bias, Tensor* output, int axis,
+                   float epsilon) {
+  const char* op = "nnc_layernorm";
+  OpScope scope(op);
+  layernorm_impl(input, nullptr, scale, bias, output, axis, epsilon, op);
+}
+
+// Add -> LayerNormalization (the post-LN residual joins of a transformer at
+// -O3): layernorm(a + b) with the sum never stored.
+void nnc_add_layernorm(Tensor* a, Tensor* b, Tensor* scale, Tensor* bias, Tensor* output, int axis,
+                       float epsilon) {
+  const char* op = "nnc_add_layernorm";
+  OpScope scope(op);
+  if (!valid_tensor(b, op, "b")) return;
+  layernorm_impl(a, b, scale, bias, output, axis, epsilon, op);
 }
 
 void nnc_reducemean(Tensor* input, Tensor* output, int axis, int keepdims) {

@@ -340,6 +340,81 @@ class GapGemmFusionPass(PassBase):
             _replace(g, [node, flat, gemm], fused, [node.outputs[0], flat.outputs[0]])
 
 
+class AddLayerNormFusionPass(PassBase):
+    """Collapses Add -> LayerNormalization (a post-LN transformer's residual
+    joins) into one LAYER_NORM node called as nnc_add_layernorm: the sum is
+    formed as the rows are loaded and never stored. Both addends must be
+    activations of the LayerNorm input's extents (no broadcast) and the sum
+    must feed only the LayerNorm. Metadata ``cuda_fused = "add_layernorm"``;
+    inputs [a, b, scale, bias]."""
+
+    @property
+    def name(self) -> str:
+        return "CudaAddLayerNormFusion"
+
+    def _execute(self, ctx: CompileContext) -> None:
+        g = ctx.graph
+        for node in list(g.topological_sort()):
+            if node.name not in g.nodes or node.op_type != OpType.LAYER_NORM or not node.inputs:
+                continue
+            x = node.inputs[0]
+            add = next((n for n in g.nodes.values() if x in n.outputs), None)
+            if add is None or add.op_type != OpType.ADD or len(add.inputs) != 2:
+                continue
+            if _single_consumer(g, x) is not node:
+                continue
+            dims = list(g.tensors[x].shape.dims)
+            if any(t in g.constants or list(g.tensors[t].shape.dims) != dims for t in add.inputs):
+                continue
+            fused = Node(OpType.LAYER_NORM, f"{node.name}_add", list(add.inputs) + list(node.inputs[1:]),
+                         list(node.outputs), dict(node.attrs),
+                         metadata={"cuda_fused": "add_layernorm", "fused_from": [add.name, node.name]})
+            _replace(g, [add, node], fused, [x])
+
+
+class ReshapeTransposeFusionPass(PassBase):
+    """Folds the reshapes around transposes into the transpose call
+    (nnc_transpose_shaped): Reshape -> Transpose reads the reshape's input
+    with the reshaped extents, Transpose -> Reshape writes the reshape's
+    output as the permuted extents, so neither reshape copies (the
+    transformer's head split and merge). The node keeps op type TRANSPOSE
+    with metadata ``cuda_fused = "transpose_shaped"`` and ``in_shape`` (the
+    extents its input is read with)."""
+
+    @property
+    def name(self) -> str:
+        return "CudaReshapeTransposeFusion"
+
+    def _execute(self, ctx: CompileContext) -> None:
+        g = ctx.graph
+        for node in list(g.topological_sort()):
+            if node.name not in g.nodes or node.op_type != OpType.TRANSPOSE or not node.inputs:
+                continue
+            perm = node.attrs.get("perm")
+            if perm is None:
+                continue
+            cur = node
+            in_shape = list(node.metadata.get("in_shape") or [int(d) for d in g.tensors[node.inputs[0]].shape.dims])
+            inputs, outputs, dropped, old = list(node.inputs), list(node.outputs), [], [node]
+            src = next((n for n in g.nodes.values() if inputs[0] in n.outputs), None)
+            if (src is not None and src.op_type == OpType.RESHAPE and src.inputs and
+                    _single_consumer(g, inputs[0]) is node and src.inputs[0] not in g.constants):
+                dropped.append(inputs[0])
+                old.append(src)
+                inputs = [src.inputs[0]]
+            dst = _single_consumer(g, outputs[0])
+            if dst is not None and dst.op_type == OpType.RESHAPE and dst.inputs and dst.inputs[0] == outputs[0]:
+                dropped.append(outputs[0])
+                old.append(dst)
+                outputs = list(dst.outputs)
+            if len(old) == 1:
+                continue
+            fused = Node(OpType.TRANSPOSE, f"{cur.name}_shaped", inputs, outputs, dict(node.attrs),
+                         metadata={"cuda_fused": "transpose_shaped", "in_shape": in_shape,
+                                   "fused_from": [n.name for n in old]})
+            _replace(g, old, fused, dropped)
+
+
 # Whether O3 fuses Conv+ReLU -> MaxPool into nnc_conv_relu_maxpool. On: on
 # the ResNet stem at batch 1024 the fused call (pooled epilogue in the conv
 # kernel, 1.83 ms) beats the conv and pool kernels it replaces (2.42 ms) and
@@ -354,7 +429,8 @@ def cuda_passes(opt_level: int, fuse_conv_relu_maxpool: bool | None = None) -> l
     PatternFusion (conv_relu, add_relu, ...), the Conv+Add+Relu group (and
     the Conv+Relu+MaxPool group when enabled), the Gemm+Relu group, the
     GlobalAveragePool+Flatten+Gemm head, the MatMul epilogue groups (bias,
-    bias+relu, scale+softmax), PrepackLowering
+    bias+relu, scale+softmax), the reshapes folded into their transposes,
+    Add+LayerNorm, PrepackLowering
     (entry-point selection, Gemm weight prepack), liveness and the
     cost_aware arena plan. nnc-py's NPU tiling passes are not used:
     the GPU kernels tile internally.
@@ -371,7 +447,8 @@ def cuda_passes(opt_level: int, fuse_conv_relu_maxpool: bool | None = None) -> l
     fuse_pool = FUSE_CONV_RELU_MAXPOOL if fuse_conv_relu_maxpool is None else fuse_conv_relu_maxpool
     return [IdentityEliminationPass(), DeadCodeEliminationPass(), PatternFusionPass(), ConvAddReluFusionPass()] + (
         [ConvReluMaxPoolFusionPass()] if fuse_pool else []) + [
-        GemmReluFusionPass(), GapGemmFusionPass(), MatMulEpilogueFusionPass(),
+        GemmReluFusionPass(), GapGemmFusionPass(), MatMulEpilogueFusionPass(), ReshapeTransposeFusionPass(),
+        AddLayerNormFusionPass(),
         PrepackLoweringPass(), LivenessAnalysisPass(), MemoryPlanningPassV2()]
 
 
@@ -470,6 +547,27 @@ class CudaEmitter(CEmitter):
             for text in lines:
                 text = text.replace("nnc_gemm_nt(", "nnc_gemm_nt_relu(").replace("nnc_gemm(", "nnc_gemm_relu(")
                 self.write_line(text)
+            return
+        if fused == "add_layernorm":
+            sym = ctx.tensor_symbols
+            a, b = node.inputs[:2]
+            scale = f"&{sym[node.inputs[2]]}" if len(node.inputs) > 2 and node.inputs[2] else "NULL"
+            bias = f"&{sym[node.inputs[3]]}" if len(node.inputs) > 3 and node.inputs[3] else "NULL"
+            axis = node.attrs.get("axis", -1)
+            eps = node.attrs.get("epsilon", 1e-5)
+            self.write_line(f"nnc_add_layernorm(&{sym[a]}, &{sym[b]}, {scale}, {bias}, &{sym[node.outputs[0]]}, "
+                            f"{axis}, {eps}f);")
+            return
+        if fused == "transpose_shaped":
+            sym = ctx.tensor_symbols
+            perm = [int(v) for v in node.attrs["perm"]]
+            shape = [int(v) for v in node.metadata["in_shape"]]
+            self.write_line("{")
+            self.write_line(f"    static int64_t in_shape[{len(shape)}] = {{{', '.join(map(str, shape))}}};")
+            self.write_line(f"    static int64_t perm[{len(perm)}] = {{{', '.join(map(str, perm))}}};")
+            self.write_line(f"    nnc_transpose_shaped(&{sym[node.inputs[0]]}, &{sym[node.outputs[0]]}, in_shape, perm, "
+                            f"{len(perm)});")
+            self.write_line("}")
             return
         if fused == "gap_gemm":
             sym = ctx.tensor_symbols

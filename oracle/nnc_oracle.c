@@ -489,6 +489,20 @@ void nnc_matmul_scale_softmax(Tensor* a, Tensor* b, Tensor* out, float alpha) {
     nnc_softmax(out, out, -1);
 }
 
+/* Add -> LayerNormalization, the cuda target's O3 residual join: the
+ * reference's add (ops.c:82-118) into a temporary, then its layernorm
+ * (ops.c:2095-2171). */
+void nnc_add_layernorm(Tensor* a, Tensor* b, Tensor* scale, Tensor* bias, Tensor* out, int axis,
+                       float eps) {
+    const int64_t n = count_of(a);
+    float* sum = (float*)malloc((size_t)(n > 0 ? n : 1) * sizeof(float));
+    Tensor t = *a;
+    t.data = sum;
+    nnc_add(a, b, &t);
+    nnc_layernorm(&t, scale, bias, out, axis, eps);
+    free(sum);
+}
+
 /* GlobalAveragePool -> Flatten -> Gemm(transB = 1), the cuda target's O3
  * head group: the reference's avgpool with kernel = stride = H x W
  * (ops.c:393-461), its flatten (a copy, ops.c:1521) and gemm_nt
@@ -538,6 +552,21 @@ void nnc_transpose(Tensor* in, Tensor* out, int64_t* perm, int ndim) {
         }
         z[o] = x[src];
     }
+}
+
+/* Reshape -> Transpose / Transpose -> Reshape of the cuda target's O3
+ * groups: the reference's reshape (a copy, ops.c:1510), transpose
+ * (ops.c:1531-1581) and reshape composed, through views of the same bytes. */
+void nnc_transpose_shaped(Tensor* in, Tensor* out, int64_t* in_shape, int64_t* perm, int ndim) {
+    int64_t ish[8], osh[8];
+    for (int d = 0; d < ndim; ++d) ish[d] = in_shape ? in_shape[d] : in->shape[d];
+    for (int d = 0; d < ndim; ++d) osh[d] = ish[perm ? perm[d] : ndim - 1 - d];
+    Tensor vin = *in, vout = *out;
+    vin.shape = ish;
+    vin.ndim = ndim;
+    vout.shape = osh;
+    vout.ndim = ndim;
+    nnc_transpose(&vin, &vout, perm, ndim);
 }
 
 void nnc_concat(Tensor** inputs, Tensor* out, int num, int axis) {

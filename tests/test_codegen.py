@@ -108,8 +108,9 @@ def test_o3_gap_gemm_head(tmp_path):
 
 def test_o3_matmul_epilogue_groups(tmp_path):
     """The transformer's MatMul -> Add(bias) [-> Relu] and MatMul -> Div(8) ->
-    Softmax chains each become one call; the residual Adds, LayerNorms and
-    the probs . V MatMul stay."""
+    Softmax chains each become one call, as do the residual Add ->
+    LayerNorm joins and the reshapes around the head transposes; the
+    probs . V MatMul stays."""
     man = CG.compile_model(W.transformer(1), tmp_path, opt_level=3)
     calls = man["calls"]
     layers = 4
@@ -118,10 +119,19 @@ def test_o3_matmul_epilogue_groups(tmp_path):
     assert calls.count("nnc_matmul_scale_softmax") == layers
     assert calls.count("nnc_matmul") == layers            # probs . V
     assert "nnc_softmax" not in calls and "nnc_div" not in calls and "nnc_add_relu" not in calls
-    assert calls.count("nnc_add") == 2 * layers           # residuals
+    # Residual joins: Add -> LayerNorm as one call each.
+    assert calls.count("nnc_add_layernorm") == 2 * layers
+    assert "nnc_add" not in calls and "nnc_layernorm" not in calls
     src = (tmp_path / "model.c").read_text()
     line = next(l for l in src.splitlines() if "nnc_matmul_scale_softmax(" in l)
     assert line.strip().endswith("0.125f);")  # 1 / sqrt(64)
+    # Head split (Reshape -> Transpose of q, k, v) and merge (Transpose ->
+    # Reshape of the context): the reshapes fold into the transpose calls.
+    assert "nnc_reshape" not in calls and "nnc_transpose" not in calls
+    assert calls.count("nnc_transpose_shaped") == 4 * layers
+    assert "nnc_transpose_shaped(&tensor_l0_q_out, &tensor_l0_q_heads, in_shape, perm, 4);" in src
+    assert "static int64_t in_shape[4] = {1, 128, 4, 64};" in src
+    assert "nnc_transpose_shaped(&tensor_l0_ctx_heads, &tensor_l0_ctx, in_shape, perm, 4);" in src
 
 
 def test_channels_last_assignment(tmp_path):

@@ -335,6 +335,74 @@ STREAMK_CASES = [
 ]
 
 
+# Reshape -> Transpose and Transpose -> Reshape as one call (the
+# transformer's head split and merge at -O3): bit-exact against the oracle's
+# composition of the reference's reshape and transpose; NULL in_shape, a
+# reversed (NULL) perm, float4 and scalar paths.
+SHAPED_TRANSPOSE_CASES = [
+    # input shape, in_shape (None: own), perm (None: reverse)
+    ((2, 128, 256), (2, 128, 4, 64), (0, 2, 1, 3)),
+    ((2, 128, 256), (2, 128, 4, 64), (0, 2, 3, 1)),
+    ((2, 4, 128, 64), None, (0, 2, 1, 3)),
+    ((3, 5, 7), (5, 3, 7), None),
+    ((6, 10), (2, 3, 10), (2, 0, 1)),
+]
+
+
+@pytest.mark.parametrize("cfg", SHAPED_TRANSPOSE_CASES, ids=lambda c: str(c).replace(" ", ""))
+def test_transpose_shaped_vs_oracle(cuda_lib, cfg):
+    shape, in_shape, perm = cfg
+    r = np.random.default_rng(41 + sum(shape))
+    arrays = {"x": r.standard_normal(shape).astype(np.float32)}
+    ish = in_shape or shape
+    nd = len(ish)
+    pm = perm or tuple(reversed(range(nd)))
+    n = int(np.prod(shape))
+    args = [C._t("x"), C._o("out", (n,)), {"k": "perm", "v": list(ish) if in_shape else None},
+            {"k": "perm", "v": list(pm) if perm else None}, C._i(nd)]
+    case = {"name": "t", "op": "nnc_transpose_shaped", "args": args, "tol": "exact"}
+    want = C.run_host(_oracle(), case, arrays)["out"]
+    got = C.run_cuda(cuda_lib, case, arrays)["out"]
+    C.assert_close(got, want, "exact", f"transpose_shaped{cfg}")
+    np.testing.assert_array_equal(got.reshape(-1), np.transpose(arrays["x"].reshape(ish), pm).reshape(-1))
+
+
+# Add -> LayerNorm as one call (the transformer's post-LN residual joins):
+# the warp kernel (256 and 100 values per slab), the four-warps-per-slab
+# kernel (768), and a long slab (4096: the sum into the output, then the
+# normalisation in place), against the oracle's composition of the
+# reference's add and layernorm.
+ADD_LN_CASES = [
+    # shape, axis
+    ((64, 128, 256), -1),
+    ((37, 100), -1),
+    ((50, 768), -1),
+    ((9, 4096), -1),
+    ((4, 6, 8, 8), 1),
+]
+
+
+@pytest.mark.parametrize("cfg", ADD_LN_CASES, ids=lambda c: "x".join(map(str, c[0])) + f"a{c[1]}")
+def test_add_layernorm_vs_oracle(cuda_lib, cfg):
+    shape, axis = cfg
+    r = np.random.default_rng(53 + sum(shape))
+    ax = axis % len(shape)
+    norm = int(np.prod(shape[ax:]))
+    arrays = {"a": r.standard_normal(shape).astype(np.float32), "b": r.standard_normal(shape).astype(np.float32),
+              "g": r.uniform(0.5, 1.5, norm).astype(np.float32), "bt": r.uniform(-0.1, 0.1, norm).astype(np.float32)}
+    args = [C._t("a"), C._t("b"), C._t("g"), C._t("bt"), C._o("out", shape), C._i(axis), C._f(1e-5)]
+    case = {"name": "aln", "op": "nnc_add_layernorm", "args": args}
+    want = C.run_host(_oracle(), case, arrays)["out"]
+    got = C.run_cuda(cuda_lib, case, arrays)["out"]
+    C.assert_close(got, want, 1e-5, f"add_layernorm{cfg}")
+    # The same as the library's own add then layernorm.
+    s = {"name": "s", "op": "nnc_add", "args": [C._t("a"), C._t("b"), C._o("out", shape)]}
+    arrays["s"] = C.run_cuda(cuda_lib, s, arrays)["out"]
+    ln = {"name": "ln", "op": "nnc_layernorm",
+          "args": [C._t("s"), C._t("g"), C._t("bt"), C._o("out", shape), C._i(axis), C._f(1e-5)]}
+    np.testing.assert_array_equal(got, C.run_cuda(cuda_lib, ln, arrays)["out"])
+
+
 # The GlobalAveragePool -> Flatten -> Gemm head as one call (the ResNet
 # classifier; odd extents, no bias, a [N, O] bias with alpha/beta), both
 # precisions, NCHW and channels-last inputs, against the oracle's composition
