@@ -1309,7 +1309,12 @@ void nnc_gap_gemm_nt(Tensor* input, Tensor* b, Tensor* c, Tensor* output, float 
                      float beta) {
   const char* op = "nnc_gap_gemm_nt";
   OpScope scope(op);
-  if (!f32(input, op, "input") || !f32(b, op, "b") || !f32(output, op, "output")) return;
+  // The pooled input may be channels-last (tagged); the GEMM operands not.
+  if (!valid_tensor(input, op, "input") || !f32(b, op, "b") || !f32(output, op, "output")) return;
+  if (elem_type(input) != NNC_DTYPE_FLOAT32 || (tag_of(input) & ~NNC_CUDA_TAG_NHWC) != 0) {
+    fail(NNC_CUDA_ERR_UNSUPPORTED, op, "input: needs a float32 tensor (NCHW or channels-last)");
+    return;
+  }
   if (input->ndim != 4 || b->ndim != 2 || input->shape[1] != b->shape[1]) {
     fail(NNC_CUDA_ERR_INVALID, op, "expected a 4-D input [N, C, H, W] and b [O, C]");
     return;
