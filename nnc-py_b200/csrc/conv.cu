@@ -2377,6 +2377,209 @@ __global__ void __launch_bounds__(128) conv_direct_kernel(ConvArgs g, const floa
   }
 }
 
+// ------------------------------------------- small conv on tensor cores ----
+// The same calls (C_out <= 16) in TF32 mode with many output pixels and a
+// reduction of at most 160 over at most 32 window taps (LeNet's layers at
+// batch 8192): one M = 128 pixels x N = 16 channels tcgen05 tile per step.
+// The CTA's threads build the tile's im2col rows in shared memory themselves
+// (a few channels per pixel are too narrow for TMA im2col): row r is output
+// pixel m0 + r, K-major in 32-float k-blocks under the 128-byte swizzle
+// (16-byte chunk j of row r at j ^ (r & 7)); TPR threads share a row, one
+// k-block each in turn. The k order is the reference's (c, kh, kw), or (kh,
+// kw, c) for channels-last inputs with an even channel count, whose channel
+// pairs then load as float2; the weight (zero rows up to 16 channels, zero k
+// up to the k-blocks) is staged once per CTA in the same order. Each element
+// reads its input offset and window-tap bit from per-k tables passed by value
+// (constant-bank operands of the unrolled loads); a pixel's bit mask of
+// in-bounds taps turns padding and k past K into zeros. Two row buffers and
+// two 16-column TMEM accumulators pipeline the tiles: the MMAs of tile i run
+// while the threads drain tile i - 1 (bias, residual, activation) and build
+// tile i + 1.
+constexpr int64_t kSmallTcMinM = 148 * 128 * 2;  // at least two tiles per SM
+constexpr int kSmallTcMaxK = 160;                // five k-blocks
+
+struct SmallTcTable {
+  int off[kSmallTcMaxK];       // input element offset of k from the window origin
+  unsigned bit[kSmallTcMaxK];  // 1 << (kh KW + kw) of k; 0 past K
+};
+
+template <int KB>
+struct SmallTcCfg {
+  static constexpr int TPR = KB;                        // threads per row: one k-block each
+  static constexpr int THREADS = 128 * TPR;
+  static constexpr int EPI = TPR < 4 ? TPR : 4;         // warp groups sharing the epilogue
+  static constexpr uint32_t A_BYTES = KB * 128 * 128;  // one tile: KB k-blocks of 128 rows x 128 B
+  static constexpr uint32_t B_BYTES = KB * 16 * 128;   // KB k-blocks of 16 rows x 128 B
+  static constexpr uint32_t BAR_OFF = 2 * A_BYTES + B_BYTES;
+  static constexpr size_t SMEM = (size_t)BAR_OFF + 64 + 1024;
+};
+
+template <int KB, bool VEC2>
+__global__ void __launch_bounds__(SmallTcCfg<KB>::THREADS) conv_small_tc_kernel(
+    const __grid_constant__ ConvArgs g, const __grid_constant__ SmallTcTable tab,
+    const float* __restrict__ w, int src_mode, int src_c4, int src_kpad) {
+  using Cfg = SmallTcCfg<KB>;
+  constexpr int KP = KB * 32;
+  constexpr int TPR = Cfg::TPR, EPI = Cfg::EPI, EPC = 16 / EPI;  // epilogue channels per group
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint8_t* sb = smem + 2 * Cfg::A_BYTES;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + Cfg::BAR_OFF);  // [2]: MMAs of a buffer done
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 2);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = threadIdx.x & 127, part = threadIdx.x >> 7;
+  const int K = g.K, KHW = g.KH * g.KW, C = K / KHW;
+
+  for (int idx = threadIdx.x; idx < 16 * KP; idx += Cfg::THREADS) {
+    const int co = idx / KP, k = idx - co * KP;
+    float v = 0.0f;
+    if (co < g.Cout && k < K) {
+      const int c = VEC2 ? k % C : k / KHW, t = VEC2 ? k / C : k % KHW;
+      if (src_mode == 0) {
+        v = w[(int64_t)co * K + c * KHW + t];
+      } else {
+        const int64_t off = (int64_t)co * src_kpad + (src_mode == 1 ? t * src_c4 + c : c * KHW + t);
+        v = __fadd_rn(w[off], w[(int64_t)g.Cout * src_kpad + off]);
+      }
+    }
+    const int kb = k >> 5, j = (k >> 2) & 7;
+    *reinterpret_cast<float*>(sb + kb * 2048 + co * 128 + ((j ^ (co & 7)) << 4) + (k & 3) * 4) = v;
+  }
+  if (threadIdx.x == 0) {
+    tc::mbar_init(&bar[0], 1);
+    tc::mbar_init(&bar[1], 1);
+    tc::fence_barrier_init();
+  }
+  if (warp == 0) {
+    tc::tmem_alloc(tmem_slot, 32);
+    tc::tmem_relinquish();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  constexpr uint32_t idesc = tc::idesc_tf32(BM, 16);
+  const int OHW = g.OH * g.OW, M = (int)g.M, Cout = g.Cout;
+  const int tiles = (M + BM - 1) / BM;
+  unsigned rep = 0;  // bit kh KW for every kh: one bit per window row
+  for (int kh = 0; kh < g.KH; ++kh) rep |= 1u << (kh * g.KW);
+  float bias[EPC];  // this thread's epilogue channels
+#pragma unroll
+  for (int j = 0; j < EPC; ++j) {
+    const int co = (part < EPI ? part : 0) * EPC + j;
+    bias[j] = g.bias && co < Cout ? __ldg(g.bias + co) : 0.0f;
+  }
+  const bool add = g.act == kActAddRelu;
+  bool ok = true;
+  int prev = -1, i = 0;  // tile whose MMAs are in flight; this CTA's step
+  for (int tile = blockIdx.x;; tile += gridDim.x, ++i) {
+    const bool have = tile < tiles;
+    const int buf = (int)(i & 1);
+    if (have) {
+      // This thread's k-blocks of row r (zeros past the last pixel).
+      const int m = (int)tile * BM + r;  // pixel indices stay 32-bit (host-checked)
+      unsigned taps = 0;
+      const float* xn = g.x_hi;
+      if (m < M) {
+        const int n = m / OHW, p = m - n * OHW;
+        const int oh = p / g.OW, ow = p - oh * g.OW;
+        const int ih0 = oh * g.sh - g.ph, iw0 = ow * g.sw - g.pw;
+        // In-bounds taps: kw in [c_lo, c_hi) of every kh in [r_lo, r_hi); the
+        // product places the column mask at each such row's bit offset.
+        const int c_lo = max(0, -iw0), c_hi = min(g.KW, g.W - iw0);
+        const int r_lo = max(0, -ih0), r_hi = min(g.KH, g.H - ih0);
+        if (c_hi > c_lo && r_hi > r_lo) {
+          const unsigned cols = (unsigned)((1ull << c_hi) - (1ull << c_lo));
+          const unsigned rows = rep & (unsigned)((1ull << (r_hi * g.KW)) - (1ull << (r_lo * g.KW)));
+          taps = cols * rows;
+        }
+        xn = g.x_hi + (int64_t)n * g.xs_n + (int64_t)ih0 * g.xs_h + (int64_t)iw0 * g.xs_w;
+      }
+      uint8_t* row = smem + buf * Cfg::A_BYTES + r * 128;
+#pragma unroll
+      for (int kb = 0; kb < KB; ++kb) {
+        if (kb % TPR != part) continue;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int k = kb * 32 + j * 4;
+          float4 v;
+          if constexpr (VEC2) {
+            float2 lo = make_float2(0.0f, 0.0f), hi = make_float2(0.0f, 0.0f);
+            if (taps & tab.bit[k]) lo = __ldg(reinterpret_cast<const float2*>(xn + tab.off[k]));
+            if (taps & tab.bit[k + 2]) hi = __ldg(reinterpret_cast<const float2*>(xn + tab.off[k + 2]));
+            v = make_float4(lo.x, lo.y, hi.x, hi.y);
+          } else {
+            v.x = (taps & tab.bit[k]) ? __ldg(xn + tab.off[k]) : 0.0f;
+            v.y = (taps & tab.bit[k + 1]) ? __ldg(xn + tab.off[k + 1]) : 0.0f;
+            v.z = (taps & tab.bit[k + 2]) ? __ldg(xn + tab.off[k + 2]) : 0.0f;
+            v.w = (taps & tab.bit[k + 3]) ? __ldg(xn + tab.off[k + 3]) : 0.0f;
+          }
+          *reinterpret_cast<float4*>(row + kb * 16384 + ((j ^ (r & 7)) << 4)) = v;
+        }
+      }
+      tc::fence_proxy_async_smem();  // the rows -> the MMAs' async-proxy reads
+    }
+    tc::tc_fence_before();
+    // Every thread leaves the loop together if a wait gave up.
+    ok = __syncthreads_and(ok ? 1 : 0) != 0;
+    if (!ok) break;
+    if (have && warp == 0) {
+      tc::tc_fence_after();
+      if (tc::elect_one()) {
+        const uint32_t a0 = tc::smem_u32(smem + buf * Cfg::A_BYTES), b0 = tc::smem_u32(sb);
+#pragma unroll
+        for (int kb = 0; kb < KB; ++kb)
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            tc::mma_tf32(tmem_base + buf * 16, tc::desc_kmajor_sw128(a0 + kb * 16384 + k * 32),
+                         tc::desc_kmajor_sw128(b0 + kb * 2048 + k * 32), idesc, (kb | k) != 0);
+        tc::mma_commit(&bar[buf]);
+      }
+      __syncwarp();
+    }
+    if (prev >= 0) {
+      // Drain the previous tile (buffer buf ^ 1, its (i - 1) / 2-th use).
+      ok = tc::mbar_wait_warp(&bar[buf ^ 1], (uint32_t)(((i - 1) >> 1) & 1), g.err);
+      tc::tc_fence_after();
+      if (ok && part < EPI) {
+        uint32_t acc_bits[16];
+        tc::tmem_ld16(tmem_base + (uint32_t)((buf ^ 1) * 16) + ((uint32_t)((warp & 3) * 32) << 16),
+                      acc_bits);
+        tc::tmem_ld_wait();
+        const int m = prev * BM + (warp & 3) * 32 + lane;
+        if (m < M) {
+          // Channels [part EPC, part EPC + EPC): bias, residual, activation.
+          const int n = m / OHW, p = m - n * OHW;
+#pragma unroll
+          for (int j = 0; j < EPC; ++j) {
+            const int co = part * EPC + j;
+            if (co >= Cout) break;
+            uint32_t v = acc_bits[j];
+#pragma unroll
+            for (int q = 1; q < EPI; ++q) v = part == q ? acc_bits[q * EPC + j] : v;
+            const int64_t off = g.out_nhwc ? (int64_t)m * Cout + co : ((int64_t)n * Cout + co) * OHW + p;
+            float o = __uint_as_float(v);
+            if (g.bias) o = __fadd_rn(o, bias[j]);
+            if (add) o = __fadd_rn(o, __ldg(g.residual + off));
+            g.out[off] = activate(o, g.act);
+          }
+        }
+      }
+    }
+    prev = have ? tile : -1;
+    if (!have) break;
+  }
+  // After a wait gave up, the last issued MMAs (step i - 1) may still be in
+  // flight: wait for them (bounded) before the accumulators are freed.
+  if (!ok && prev >= 0) tc::mbar_wait(&bar[(i - 1) & 1], (uint32_t)(((i - 1) >> 1) & 1), nullptr);
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem_base, 32);
+  }
+}
+
 // Stride-1-wide variant for a compile-time window width KW: a thread computes
 // OWB horizontally adjacent output pixels of one row for CO of the CO * CG
 // staged channels (CG threads, adjacent in the grid, share a pixel block),
@@ -2771,6 +2974,78 @@ static bool halo_pair_enabled() {
   return on;
 }
 
+// NNC_CUDA_CONV_SMALL_TC=0 keeps few-channel convs on the CUDA-core kernels.
+static bool small_tc_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("NNC_CUDA_CONV_SMALL_TC");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
+template <int KB, bool VEC2>
+bool launch_small_tc(const ConvArgs& g, const SmallTcTable& tab, const float* w, int src_mode,
+                     int src_c4, int src_kpad, const char* op) {
+  using Cfg = SmallTcCfg<KB>;
+  auto kern = conv_small_tc_kernel<KB, VEC2>;
+  static bool attr_set[64] = {};
+  static int per_sm[64] = {};
+  if (!attr_set[ctx().device]) {
+    if (!check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)Cfg::SMEM),
+                    op, "cudaFuncSetAttribute"))
+      return false;
+    // CTAs an SM holds by shared memory, registers and TMEM (32 of its 512
+    // columns each). The grid is sized from these rather than from the
+    // occupancy query, which gave one CTA per SM for this kernel; a CTA that
+    // does not fit yet only starts when another ends, since CTAs never wait
+    // on one another.
+    cudaFuncAttributes fa{};
+    if (!check_cuda(cudaFuncGetAttributes(&fa, kern), op, "cudaFuncGetAttributes")) return false;
+    const int by_smem = (int)((228u * 1024u) / (Cfg::SMEM + 1024u));
+    const int by_regs = 65536 / (Cfg::THREADS * (fa.numRegs > 0 ? fa.numRegs : 255));
+    int r = by_smem < by_regs ? by_smem : by_regs;
+    r = r < 16 ? r : 16;
+    per_sm[ctx().device] = r > 0 ? r : 1;
+    attr_set[ctx().device] = true;
+  }
+  const int64_t tiles = cdiv(g.M, BM), cap = (int64_t)sm_count() * per_sm[ctx().device];
+  const int grid = (int)(tiles < cap ? tiles : cap);
+  ConvArgs a = g;
+  a.err = device_error_word();
+  kern<<<grid, Cfg::THREADS, Cfg::SMEM, ctx().stream>>>(a, tab, w, src_mode, src_c4, src_kpad);
+  return check_launch(op);
+}
+
+// Few-channel conv on the tensor-core tile kernel: builds the per-k tables
+// (channel pairs adjacent for a channels-last input with an even channel
+// count) and picks the instance by k-blocks.
+void launch_small_tc_conv(const ConvArgs& g, int C, bool in_nhwc, const float* w, int src_mode,
+                          int src_c4, int src_kpad, const char* op) {
+  SmallTcTable tab;
+  const int KHW = g.KH * g.KW;
+  const bool vec2 = in_nhwc && C % 2 == 0 && ((uintptr_t)g.x_hi & 7u) == 0;
+  for (int k = 0; k < kSmallTcMaxK; ++k) {
+    tab.off[k] = 0;
+    tab.bit[k] = 0;
+    if (k >= g.K) continue;
+    const int c = vec2 ? k % C : k / KHW, t = vec2 ? k / C : k % KHW;
+    const int kh = t / g.KW, kw = t - kh * g.KW;
+    tab.off[k] = (int)(c * g.xs_c + kh * g.xs_h + kw * g.xs_w);
+    tab.bit[k] = 1u << t;
+  }
+  const int kb = (int)cdiv(g.K, 32);
+  if (kb <= 1)
+    vec2 ? launch_small_tc<1, true>(g, tab, w, src_mode, src_c4, src_kpad, op)
+         : launch_small_tc<1, false>(g, tab, w, src_mode, src_c4, src_kpad, op);
+  else if (kb <= 2)
+    vec2 ? launch_small_tc<2, true>(g, tab, w, src_mode, src_c4, src_kpad, op)
+         : launch_small_tc<2, false>(g, tab, w, src_mode, src_c4, src_kpad, op);
+  else
+    vec2 ? launch_small_tc<5, true>(g, tab, w, src_mode, src_c4, src_kpad, op)
+         : launch_small_tc<5, false>(g, tab, w, src_mode, src_c4, src_kpad, op);
+}
+
 template <int BN, int G, int STAGES, int CB, bool POOL, bool STAGED, bool PAIR, bool GATHER>
 bool launch_halo_kernel(ConvArgs g, const float* w0, const char* op) {
   using Cfg = HaloCfg<BN, G, STAGES, CB, POOL, STAGED, PAIR, GATHER>;
@@ -3077,6 +3352,12 @@ void conv_impl(Tensor* input, Tensor* weight, Tensor* bias, Tensor* residual, Te
     const int grid = (int)(cdiv(M, 128) < (int64_t)sm_count() * 8 ? cdiv(M, 128) : (int64_t)sm_count() * 8);
     const float* wp = (const float*)weight->data;
     cudaStream_t st = ctx().stream;
+    // TF32 mode with many pixels: the tensor-core tile kernel.
+    if (!split && M >= kSmallTcMinM && M + BM < (1ll << 31) && g.K <= kSmallTcMaxK && KH * KW <= 32 &&
+        small_tc_enabled()) {
+      launch_small_tc_conv(g, (int)C, in_nhwc, wp, src_mode, wl0.C4, wl0.Kpad, op);
+      return;
+    }
     // Row-blocked kernel for stride-1-wide 3- and 5-wide windows: 4 output
     // pixels per thread, 8 channels per thread (two threads per pixel block
     // above 8 output channels).

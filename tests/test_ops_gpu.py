@@ -592,7 +592,8 @@ def test_conv_relu_maxpool_vs_oracle(cuda_lib, prec, cfg):
 
 
 # Few output channels over a short reduction (C_out <= 16, C KH KW <= 256)
-# run on the direct CUDA-core kernel: LeNet's two layers, stride 2 with
+# run on the direct CUDA-core kernel up to 37,887 output pixels (and at any
+# size in 3xTF32 mode): LeNet's two layers, stride 2 with
 # padding and a residual, sigmoid, NCHW and channels-last tensors, raw and
 # prepacked (element and chunk order) weights, both precision modes. Stride-1
 # 3- and 5-wide windows take the row-blocked kernel (4 pixels per thread,
@@ -608,9 +609,9 @@ DIRECT_CASES = [
 ]
 
 
-@pytest.mark.parametrize("prec", [0, 1])
-@pytest.mark.parametrize("cfg", DIRECT_CASES, ids=lambda c: "x".join(str(v) for v in c[:8]))
-def test_conv_direct_small_vs_oracle(cuda_lib, prec, cfg):
+def _check_direct_conv(cuda_lib, prec, cfg, tol):
+    """Runs one few-channel conv case NCHW, channels-last and with prepacked
+    weights against the oracle; returns the NCHW result and the oracle's."""
     import torch
 
     from nnc_cuda import tensor as T
@@ -631,8 +632,8 @@ def test_conv_direct_small_vs_oracle(cuda_lib, prec, cfg):
     case = {"name": "c", "op": op, "args": args}
     cuda_lib.nnc_cuda_set_precision(prec)
     want = C.run_host(_oracle(), case, arrays)["out"]
-    tol = 1e-5  # fp32 FMA accumulation in either precision mode
-    C.assert_close(C.run_cuda(cuda_lib, case, arrays)["out"], want, tol, f"conv{cfg}")
+    got = C.run_cuda(cuda_lib, case, arrays)["out"]
+    C.assert_close(got, want, tol, f"conv{cfg}")
     C.assert_close(C.run_cuda(cuda_lib, case, arrays, nhwc=nhwc)["out"], want, tol, f"conv{cfg}[nhwc]")
     # Prepacked weight (element order for K <= 64, chunk order above).
     wt = torch.from_numpy(arrays["w"]).cuda()
@@ -640,8 +641,44 @@ def test_conv_direct_small_vs_oracle(cuda_lib, prec, cfg):
     nbytes = cuda_lib.nnc_cuda_prepacked_conv_weight_bytes(wref.ptr)
     packed = torch.empty(nbytes // 4, dtype=torch.float32, device="cuda")
     assert cuda_lib.nnc_cuda_prepack_conv_weight(wref.ptr, ctypes.c_void_p(packed.data_ptr()), nbytes) == 0
-    got = _run_with_weight(cuda_lib, case, arrays, "w", wref)["out"]
-    C.assert_close(got, want, tol, f"conv{cfg}[prepacked]")
+    C.assert_close(_run_with_weight(cuda_lib, case, arrays, "w", wref)["out"], want, tol,
+                   f"conv{cfg}[prepacked]")
+    return got, want
+
+
+@pytest.mark.parametrize("prec", [0, 1])
+@pytest.mark.parametrize("cfg", DIRECT_CASES, ids=lambda c: "x".join(str(v) for v in c[:8]))
+def test_conv_direct_small_vs_oracle(cuda_lib, prec, cfg):
+    _check_direct_conv(cuda_lib, prec, cfg, 1e-5)  # fp32 FMA accumulation in either precision mode
+
+
+# The same few-channel convs with at least 37,888 output pixels (two 128-pixel
+# tiles per SM), a reduction of at most 160 and at most 32 window taps run in
+# TF32 mode on the tensor-core tile kernel, whose CTAs build the im2col rows
+# in shared memory: one, two and five 32-float k-blocks (K = 18 to 150),
+# channel pairs loaded as float2 (channels-last inputs with an even channel
+# count), ragged last tiles, padding, stride 2, a residual, sigmoid. 3xTF32
+# keeps them on the fp32 CUDA-core kernels.
+SMALL_TC_CASES = [
+    # n, c, h, w, co, k, s, p, op
+    (64, 1, 32, 32, 6, 5, 1, 0, "nnc_conv_relu"),      # LeNet conv1, M = 50,176, K = 25
+    (512, 6, 14, 14, 16, 5, 1, 0, "nnc_conv"),         # LeNet conv2, M = 51,200, K = 150
+    (160, 3, 33, 31, 8, 3, 2, 1, "nnc_conv_add_relu"),  # M = 43,520, K = 27
+    (48, 5, 30, 30, 13, 5, 1, 2, "nnc_conv_sigmoid"),  # M = 43,200, K = 125
+    (64, 2, 30, 30, 10, 5, 1, 2, "nnc_conv_relu"),     # M = 57,600, K = 50
+    (80, 2, 28, 28, 12, 3, 1, 1, "nnc_conv"),          # M = 62,720, K = 18
+    (80, 7, 24, 24, 9, 3, 1, 0, "nnc_conv_add_relu"),  # M = 38,720, K = 63
+]
+
+
+@pytest.mark.parametrize("prec", [0, 1])
+@pytest.mark.parametrize("cfg", SMALL_TC_CASES, ids=lambda c: "x".join(str(v) for v in c[:8]))
+def test_conv_small_tensor_core_vs_oracle(cuda_lib, prec, cfg):
+    got, want = _check_direct_conv(cuda_lib, prec, cfg, C.TC_RTOL[prec])
+    if prec == 0:
+        # TF32 operands: the result is not the fp32 one, so the tensor-core
+        # kernel (not a CUDA-core one) produced it.
+        assert not np.allclose(got, want, rtol=0, atol=1e-7)
 
 
 # Row-op dispatch: one warp per row up to 1024 elements, a block per row with
