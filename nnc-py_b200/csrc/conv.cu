@@ -2398,9 +2398,28 @@ __global__ void __launch_bounds__(128) conv_direct_kernel(ConvArgs g, const floa
 constexpr int64_t kSmallTcMinM = 148 * 128 * 2;  // at least two tiles per SM
 constexpr int kSmallTcMaxK = 160;                // five k-blocks
 
+// Unsigned division by a launch constant d as a multiply and shift
+// (Granlund and Montgomery, "Division by invariant integers using
+// multiplication", PLDI 1994, round-up method with N = 32): l = ceil(log2 d),
+// mul = floor(2^32 (2^l - d) / d) + 1, n / d = (umulhi(n, mul) + n) >> l for
+// every 32-bit n.
+struct FastDiv {
+  unsigned mul, shift;
+};
+inline FastDiv fast_div(unsigned d) {
+  unsigned l = 0;
+  while ((1ull << l) < d) ++l;
+  return {(unsigned)((((1ull << 32) * ((1ull << l) - d)) / d) + 1), l};
+}
+__device__ __forceinline__ unsigned fast_div(unsigned n, FastDiv f) {
+  return (unsigned)(((uint64_t)__umulhi(n, f.mul) + n) >> f.shift);
+}
+
 struct SmallTcTable {
   int off[kSmallTcMaxK];       // input element offset of k from the window origin
   unsigned bit[kSmallTcMaxK];  // 1 << (kh KW + kw) of k; 0 past K
+  FastDiv ohw, ow;             // pixel -> (image, row, column)
+  int stage;                   // channels-last output through shared memory (16-byte aligned)
 };
 
 template <int KB>
@@ -2408,6 +2427,7 @@ struct SmallTcCfg {
   static constexpr int TPR = KB;                        // threads per row: one k-block each
   static constexpr int THREADS = 128 * TPR;
   static constexpr int EPI = TPR < 4 ? TPR : 4;         // warp groups sharing the epilogue
+  static constexpr int MIN_CTAS = KB == 1 ? 6 : KB == 2 ? 3 : 1;  // resident by shared memory
   static constexpr uint32_t A_BYTES = KB * 128 * 128;  // one tile: KB k-blocks of 128 rows x 128 B
   static constexpr uint32_t B_BYTES = KB * 16 * 128;   // KB k-blocks of 16 rows x 128 B
   static constexpr uint32_t BAR_OFF = 2 * A_BYTES + B_BYTES;
@@ -2415,7 +2435,7 @@ struct SmallTcCfg {
 };
 
 template <int KB, bool VEC2>
-__global__ void __launch_bounds__(SmallTcCfg<KB>::THREADS) conv_small_tc_kernel(
+__global__ void __launch_bounds__(SmallTcCfg<KB>::THREADS, SmallTcCfg<KB>::MIN_CTAS) conv_small_tc_kernel(
     const __grid_constant__ ConvArgs g, const __grid_constant__ SmallTcTable tab,
     const float* __restrict__ w, int src_mode, int src_c4, int src_kpad) {
   using Cfg = SmallTcCfg<KB>;
@@ -2481,8 +2501,8 @@ __global__ void __launch_bounds__(SmallTcCfg<KB>::THREADS) conv_small_tc_kernel(
       unsigned taps = 0;
       const float* xn = g.x_hi;
       if (m < M) {
-        const int n = m / OHW, p = m - n * OHW;
-        const int oh = p / g.OW, ow = p - oh * g.OW;
+        const int n = (int)fast_div((unsigned)m, tab.ohw), p = m - n * OHW;
+        const int oh = (int)fast_div((unsigned)p, tab.ow), ow = p - oh * g.OW;
         const int ih0 = oh * g.sh - g.ph, iw0 = ow * g.sw - g.pw;
         // In-bounds taps: kw in [c_lo, c_hi) of every kh in [r_lo, r_hi); the
         // product places the column mask at each such row's bit offset.
@@ -2539,17 +2559,23 @@ __global__ void __launch_bounds__(SmallTcCfg<KB>::THREADS) conv_small_tc_kernel(
     }
     if (prev >= 0) {
       // Drain the previous tile (buffer buf ^ 1, its (i - 1) / 2-th use).
+      // Its row buffer, read by those MMAs, stages a channels-last output:
+      // the tile's pixels are one contiguous range there, written back with
+      // coalesced float4 stores (residual and activation on the way).
       ok = tc::mbar_wait_warp(&bar[buf ^ 1], (uint32_t)(((i - 1) >> 1) & 1), g.err);
       tc::tc_fence_after();
+      const int m0 = prev * BM;
+      float* obuf = reinterpret_cast<float*>(smem + (buf ^ 1) * Cfg::A_BYTES);
       if (ok && part < EPI) {
         uint32_t acc_bits[16];
         tc::tmem_ld16(tmem_base + (uint32_t)((buf ^ 1) * 16) + ((uint32_t)((warp & 3) * 32) << 16),
                       acc_bits);
         tc::tmem_ld_wait();
-        const int m = prev * BM + (warp & 3) * 32 + lane;
+        const int rr = (warp & 3) * 32 + lane, m = m0 + rr;
         if (m < M) {
-          // Channels [part EPC, part EPC + EPC): bias, residual, activation.
-          const int n = m / OHW, p = m - n * OHW;
+          // Channels [part EPC, part EPC + EPC): bias, then (unstaged)
+          // residual and activation.
+          const int n = (int)fast_div((unsigned)m, tab.ohw), p = m - n * OHW;
 #pragma unroll
           for (int j = 0; j < EPC; ++j) {
             const int co = part * EPC + j;
@@ -2557,13 +2583,47 @@ __global__ void __launch_bounds__(SmallTcCfg<KB>::THREADS) conv_small_tc_kernel(
             uint32_t v = acc_bits[j];
 #pragma unroll
             for (int q = 1; q < EPI; ++q) v = part == q ? acc_bits[q * EPC + j] : v;
-            const int64_t off = g.out_nhwc ? (int64_t)m * Cout + co : ((int64_t)n * Cout + co) * OHW + p;
             float o = __uint_as_float(v);
             if (g.bias) o = __fadd_rn(o, bias[j]);
-            if (add) o = __fadd_rn(o, __ldg(g.residual + off));
-            g.out[off] = activate(o, g.act);
+            if (tab.stage) {
+              obuf[rr * Cout + co] = o;
+            } else {
+              const int64_t off = g.out_nhwc ? (int64_t)m * Cout + co : ((int64_t)n * Cout + co) * OHW + p;
+              if (add) o = __fadd_rn(o, __ldg(g.residual + off));
+              g.out[off] = activate(o, g.act);
+            }
           }
         }
+      }
+      if (tab.stage) {
+        __syncthreads();
+        const int nf = min(BM, M - m0) * Cout;
+        float* out = g.out + (int64_t)m0 * Cout;
+        const float* res = add ? g.residual + (int64_t)m0 * Cout : nullptr;
+        for (int q = threadIdx.x * 4; q < nf; q += Cfg::THREADS * 4) {
+          if (q + 4 <= nf) {
+            float4 v = *reinterpret_cast<const float4*>(obuf + q);
+            if (add) {
+              const float4 rv = __ldg(reinterpret_cast<const float4*>(res + q));
+              v.x = __fadd_rn(v.x, rv.x);
+              v.y = __fadd_rn(v.y, rv.y);
+              v.z = __fadd_rn(v.z, rv.z);
+              v.w = __fadd_rn(v.w, rv.w);
+            }
+            v.x = activate(v.x, g.act);
+            v.y = activate(v.y, g.act);
+            v.z = activate(v.z, g.act);
+            v.w = activate(v.w, g.act);
+            *reinterpret_cast<float4*>(out + q) = v;
+          } else {
+            for (int e = q; e < nf; ++e) {
+              float o = obuf[e];
+              if (add) o = __fadd_rn(o, __ldg(res + e));
+              out[e] = activate(o, g.act);
+            }
+          }
+        }
+        __syncthreads();  // the next step rebuilds this buffer's rows
       }
     }
     prev = have ? tile : -1;
@@ -3034,6 +3094,9 @@ void launch_small_tc_conv(const ConvArgs& g, int C, bool in_nhwc, const float* w
     tab.off[k] = (int)(c * g.xs_c + kh * g.xs_h + kw * g.xs_w);
     tab.bit[k] = 1u << t;
   }
+  tab.ohw = fast_div((unsigned)(g.OH * g.OW));
+  tab.ow = fast_div((unsigned)g.OW);
+  tab.stage = g.out_nhwc && aligned16(g.out) && (!g.residual || aligned16(g.residual));
   const int kb = (int)cdiv(g.K, 32);
   if (kb <= 1)
     vec2 ? launch_small_tc<1, true>(g, tab, w, src_mode, src_c4, src_kpad, op)
@@ -3044,6 +3107,270 @@ void launch_small_tc_conv(const ConvArgs& g, int C, bool in_nhwc, const float* w
   else
     vec2 ? launch_small_tc<5, true>(g, tab, w, src_mode, src_c4, src_kpad, op)
          : launch_small_tc<5, false>(g, tab, w, src_mode, src_c4, src_kpad, op);
+}
+
+// ----------------------------------------- row-banded conv on tensor cores ----
+// Few-channel convs whose output row fits one MMA (OW C_out <= 256) and whose
+// input row (x = iw C + c over W C floats: channels-last, or one channel) is
+// contiguous. For window row kh, output row (n, oh) takes input row (n, oh -
+// ph + kh) times the banded weight T_kh[x][col], col the output column in the
+// output's own order ((ow, co) channels-last, (co, ow) otherwise):
+// T_kh[x][col] = w[co][c][kh][iw - ow sw + pw] inside the window, 0 elsewhere.
+// A tile is IMGS whole images (IMGS OH <= 128 rows). A = one TMA box of input
+// rows (a 32-float k-block of each row, OH rows from kh - ph, IMGS images;
+// rows and images outside the tensor read as zeros, which is the vertical
+// padding); B = that k-block of T_kh, bulk-copied from the banded weight that
+// a small kernel builds per call (rows pre-swizzled). The D rows are the
+// tile's output rows with all their columns; they are staged in shared memory
+// in the output's layout and leave as one bulk copy, since a tile's images are
+// one contiguous range of the output in either layout. Warp 0 loads, warp 1
+// issues the MMAs into two TMEM accumulators, warps 2-9 drain them (bias,
+// residual, activation). The tensor cores do ~W C / (C KW) times the useful
+// work, which is cheap next to building im2col rows for a few channels.
+constexpr int kRowBandThreads = 64 + 32 * kEpilogueWarps;
+
+struct RowBandArgs {
+  const float* band;   // [KH][kb][n_pad][32] pre-swizzled banded weight
+  int imgs, nimg;      // images per tile, images in all
+  int kb;              // 32-float k-blocks of an input row
+  int n_cols, n_pad;   // output columns (OW C_out), rounded up to 16
+  int stages;          // load ring depth
+  int nchw;            // output column order (co, ow) instead of (ow, co)
+  int vec4;            // channels-last with OW C_out a multiple of 4 (float4 staging)
+  int row_stride;      // elements between output rows oh, oh + 1 of an image
+  int acc_stride;      // TMEM columns between the two accumulators (n_pad rounded up to 32)
+  int tmem_cols;       // power of two >= 2 acc_stride
+  uint32_t a_bytes, b_bytes, stage_bytes;  // box bytes, n_pad x 128, 16 KB + b_bytes
+  uint32_t img_elems;  // C_out OH OW
+  uint32_t out_off, col_off, bar_off;      // shared-memory layout
+};
+
+__global__ void __launch_bounds__(kRowBandThreads, 1)
+    conv_rowband_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ ConvArgs g,
+                        const __grid_constant__ RowBandArgs rb) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  float* obuf = reinterpret_cast<float*>(smem + rb.out_off);
+  int* colpart = reinterpret_cast<int*>(smem + rb.col_off);  // column -> offset in an image
+  float* biasc = reinterpret_cast<float*>(colpart + rb.n_pad);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + rb.bar_off);
+  uint64_t* empty = full + rb.stages;
+  uint64_t* tfull = empty + rb.stages;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int OH = g.OH, OW = g.OW, Cout = g.Cout;
+
+  for (int n = threadIdx.x; n < rb.n_pad; n += kRowBandThreads) {
+    int cp = 0;
+    float bv = 0.0f;
+    if (n < rb.n_cols) {
+      const int co = rb.nchw ? n / OW : n % Cout, ow = rb.nchw ? n % OW : n / Cout;
+      cp = rb.nchw ? co * OH * OW + ow : n;
+      if (g.bias) bv = __ldg(g.bias + co);
+    }
+    colpart[n] = cp;
+    biasc[n] = bv;
+  }
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < rb.stages; ++s) {
+      tc::mbar_init(&full[s], 1);
+      tc::mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      tc::mbar_init(&tfull[a], 1);
+      tc::mbar_init(&tempty[a], kEpilogueWarps);
+    }
+    tc::fence_barrier_init();
+  }
+  if (warp == 1) {
+    tc::tmem_alloc(tmem_slot, (uint32_t)rb.tmem_cols);
+    tc::tmem_relinquish();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int tiles = (rb.nimg + rb.imgs - 1) / rb.imgs;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tc::prefetch_tmap(&tmX);
+      int s = 0;
+      uint32_t ph = 0, armed = 0, armed_ph = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x)
+        for (int kh = 0; kh < g.KH && ok; ++kh)
+          for (int kb = 0; kb < rb.kb; ++kb) {
+            if (!tc::mbar_wait(&empty[s], ph ^ 1, g.err)) {
+              ok = false;
+              break;
+            }
+            uint8_t* st = smem + s * rb.stage_bytes;
+            tc::mbar_arrive_expect_tx(&full[s], rb.a_bytes + rb.b_bytes);
+            tc::tma_load_3d(st, &tmX, &full[s], kb * 32, kh - g.ph, tile * rb.imgs);
+            tc::bulk_load(st + 16384, rb.band + (size_t)(kh * rb.kb + kb) * rb.n_pad * 32, rb.b_bytes,
+                          &full[s]);
+            armed |= 1u << s;
+            armed_ph = (armed_ph & ~(1u << s)) | (ph << s);
+            if (++s == rb.stages) {
+              s = 0;
+              ph ^= 1;
+            }
+          }
+      // Copies still in flight (only after a wait gave up) land before exit.
+      for (int q = 0; q < rb.stages; ++q)
+        if ((armed >> q) & 1) tc::mbar_wait(&full[q], (armed_ph >> q) & 1, g.err);
+    }
+  } else if (warp == 1) {
+    const uint32_t idesc = tc::idesc_tf32(BM, rb.n_pad);
+    int s = 0, acc = 0;
+    uint32_t ph = 0, aph = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+      ok = tc::mbar_wait_warp(&tempty[acc], aph ^ 1, g.err);
+      tc::tc_fence_after();
+      const int steps = g.KH * rb.kb;
+      for (int step = 0; step < steps && ok; ++step) {
+        ok = tc::mbar_wait_warp(&full[s], ph, g.err);
+        tc::tc_fence_after();
+        if (ok && tc::elect_one()) {
+          const uint32_t a0 = tc::smem_u32(smem + s * rb.stage_bytes), b0 = a0 + 16384;
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            tc::mma_tf32(tmem_base + acc * rb.acc_stride, tc::desc_kmajor_sw128(a0 + k * 32),
+                         tc::desc_kmajor_sw128(b0 + k * 32), idesc, (step | k) != 0);
+          tc::mma_commit(&empty[s]);
+        }
+        __syncwarp();
+        if (++s == rb.stages) {
+          s = 0;
+          ph ^= 1;
+        }
+      }
+      if (ok && tc::elect_one()) tc::mma_commit(&tfull[acc]);
+      __syncwarp();
+      acc ^= 1;
+      if (acc == 0) aph ^= 1;
+    }
+  } else {
+    const int quarter = warp & 3, half = (warp - 2) >> 2;
+    const bool leader = threadIdx.x == 64;  // issues the bulk stores
+    const bool add = g.act == kActAddRelu;
+    int acc = 0;
+    uint32_t aph = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+      ok = ok && tc::mbar_wait_warp(&tfull[acc], aph, g.err);
+      tc::tc_fence_after();
+      if (leader) tc::bulk_wait_group_read<0>();  // the last tile's copy has read obuf
+      epi_bar_sync();
+      const int img0 = tile * rb.imgs;
+      const int nim = min(rb.imgs, rb.nimg - img0);
+      const int r = quarter * 32 + lane;
+      const bool live = ok && r < nim * OH;
+      const int img = r / OH, oh = r - img * OH;
+      const int rowpart = img * (int)rb.img_elems + oh * rb.row_stride;
+      const float* res = add ? g.residual + (size_t)img0 * rb.img_elems + rowpart : nullptr;
+      for (int c = half; c < rb.n_pad / 16; c += 2) {
+        uint32_t v[16];
+        tc::tmem_ld16(tmem_base + (uint32_t)(acc * rb.acc_stride + c * 16) + ((uint32_t)(quarter * 32) << 16),
+                      v);
+        tc::tmem_ld_wait();
+        if (live && rb.vec4) {
+          // Channels-last, OW C_out a multiple of 4: four columns per store.
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int n = c * 16 + q * 4;
+            if (n < rb.n_cols) {
+              float o[4] = {__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]),
+                            __uint_as_float(v[4 * q + 2]), __uint_as_float(v[4 * q + 3])};
+              if (g.bias) {
+                const float4 b = *reinterpret_cast<const float4*>(biasc + n);
+                o[0] = __fadd_rn(o[0], b.x);
+                o[1] = __fadd_rn(o[1], b.y);
+                o[2] = __fadd_rn(o[2], b.z);
+                o[3] = __fadd_rn(o[3], b.w);
+              }
+              if (add) {
+                const float4 rv = __ldg(reinterpret_cast<const float4*>(res + n));
+                o[0] = __fadd_rn(o[0], rv.x);
+                o[1] = __fadd_rn(o[1], rv.y);
+                o[2] = __fadd_rn(o[2], rv.z);
+                o[3] = __fadd_rn(o[3], rv.w);
+              }
+              *reinterpret_cast<float4*>(obuf + rowpart + n) =
+                  make_float4(activate(o[0], g.act), activate(o[1], g.act), activate(o[2], g.act),
+                              activate(o[3], g.act));
+            }
+          }
+        } else if (live) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int n = c * 16 + j;
+            if (n < rb.n_cols) {
+              float o = __uint_as_float(v[j]);
+              if (g.bias) o = __fadd_rn(o, biasc[n]);
+              if (add) o = __fadd_rn(o, __ldg(res + colpart[n]));
+              obuf[rowpart + colpart[n]] = activate(o, g.act);
+            }
+          }
+        }
+      }
+      tc::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&tempty[acc]);
+      tc::fence_proxy_async_smem();  // obuf -> the bulk copy's reads
+      epi_bar_sync();
+      if (leader && ok) {
+        tc::bulk_store(g.out + (size_t)img0 * rb.img_elems, obuf, (uint32_t)nim * rb.img_elems * 4u);
+        tc::bulk_commit_group();
+      }
+      acc ^= 1;
+      if (acc == 0) aph ^= 1;
+    }
+    if (leader) tc::bulk_wait_group<0>();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem_base, (uint32_t)rb.tmem_cols);
+  }
+}
+
+// Builds the banded weight of conv_rowband_kernel from an OIHW or prepacked
+// weight: element (kh, kb, col, k) at [kh][kb][col][k] with the row's 16-byte
+// chunks in the 128-byte swizzle order (chunk j of row col at j ^ (col & 7)).
+__global__ void rowband_weight_kernel(ConvArgs g, RowBandArgs rb, float* band, const float* __restrict__ w,
+                                      int src_mode, int src_c4, int src_kpad, int C) {
+  const int64_t total = (int64_t)g.KH * rb.kb * rb.n_pad * 32;
+  const int KHW = g.KH * g.KW;
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int kk = (int)(idx & 31);
+    int64_t rest = idx >> 5;
+    const int n = (int)(rest % rb.n_pad);
+    rest /= rb.n_pad;
+    const int kb = (int)(rest % rb.kb), kh = (int)(rest / rb.kb);
+    const int x = kb * 32 + kk;
+    float v = 0.0f;
+    if (n < rb.n_cols && x < g.W * C) {
+      const int iw = x / C, c = x - iw * C;
+      const int co = rb.nchw ? n / g.OW : n % g.Cout, ow = rb.nchw ? n % g.OW : n / g.Cout;
+      const int kw = iw - ow * g.sw + g.pw;
+      if (kw >= 0 && kw < g.KW) {
+        const int t = kh * g.KW + kw;
+        if (src_mode == 0) {
+          v = w[(int64_t)co * g.K + c * KHW + t];
+        } else {
+          const int64_t off = (int64_t)co * src_kpad + (src_mode == 1 ? t * src_c4 + c : c * KHW + t);
+          v = __fadd_rn(w[off], w[(int64_t)g.Cout * src_kpad + off]);
+        }
+      }
+    }
+    band[(idx >> 5) * 32 + (((kk >> 2) ^ (n & 7)) << 2) + (kk & 3)] = v;
+  }
 }
 
 template <int BN, int G, int STAGES, int CB, bool POOL, bool STAGED, bool PAIR, bool GATHER>
@@ -3257,6 +3584,102 @@ bool s2d_plan(int C, int KH, int KW, int sh, int sw, int ph, int pw, S2dPlan* p)
   return p->KH2 >= 1 && p->KW2 >= 1 && p->KH2 <= kHaloMaxK && p->KW2 <= kHaloMaxK;
 }
 
+// NNC_CUDA_CONV_ROWBAND=0 keeps these convs off the row-banded kernel.
+static bool rowband_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("NNC_CUDA_CONV_ROWBAND");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
+// Shape of the row-banded kernel for a call (input rows contiguous: one
+// channel or channels-last); false when the call does not fit it: stride 1
+// down the rows, input rows of 32 to 256 floats (a multiple of 4), at most 128
+// output rows per image, at most 256 output columns (OW C_out), images of a
+// multiple of 4 output elements, and a load ring of at least two stages beside
+// a tile's staged output in shared memory.
+static bool rowband_plan(const ConvArgs& g, int C, RowBandArgs* rb, size_t* smem, size_t* band_bytes) {
+  const int64_t L = (int64_t)g.W * C;
+  const int64_t n_cols = (int64_t)g.OW * g.Cout;
+  if (g.sh != 1 || L < 32 || L > 256 || L % 4 != 0 || g.OH > 128 || g.OH > g.H || n_cols > 256 ||
+      (n_cols * g.OH) % 4 != 0)
+    return false;
+  RowBandArgs r{};
+  r.imgs = (int)(128 / g.OH < g.N ? 128 / g.OH : g.N);
+  r.nimg = g.N;
+  r.kb = (int)cdiv(L, 32);
+  r.n_cols = (int)n_cols;
+  r.n_pad = (int)cdiv(n_cols, 16) * 16;
+  r.nchw = g.out_nhwc ? 0 : 1;
+  r.vec4 = g.out_nhwc && n_cols % 4 == 0;
+  r.row_stride = g.out_nhwc ? (int)n_cols : g.OW;
+  r.acc_stride = (int)cdiv(r.n_pad, 32) * 32;
+  r.tmem_cols = 32;
+  while (r.tmem_cols < 2 * r.acc_stride) r.tmem_cols *= 2;
+  r.a_bytes = (uint32_t)(128 * g.OH * r.imgs);
+  r.b_bytes = (uint32_t)r.n_pad * 128;
+  r.stage_bytes = 16384 + r.b_bytes;
+  r.img_elems = (uint32_t)(n_cols * g.OH);
+  const uint32_t out_bytes = (uint32_t)cdiv((int64_t)r.imgs * r.img_elems * 4, 1024) * 1024;
+  const uint32_t col_bytes = (uint32_t)r.n_pad * 8;  // column offsets and biases
+  const uint32_t fixed_bytes = out_bytes + col_bytes + 8 * (2 * 8 + 4) + 16 + 1024;
+  const int64_t stages = ((int64_t)227 * 1024 - fixed_bytes) / r.stage_bytes;
+  if (stages < 2) return false;
+  r.stages = (int)(stages < 8 ? stages : 8);
+  r.out_off = (uint32_t)r.stages * r.stage_bytes;
+  r.col_off = r.out_off + out_bytes;
+  r.bar_off = r.col_off + col_bytes;
+  *smem = (size_t)r.bar_off + 8 * (2 * r.stages + 4) + 16 + 1024;
+  *band_bytes = (size_t)g.KH * r.kb * r.n_pad * 128;
+  *rb = r;
+  return true;
+}
+
+// Builds the banded weight (in the workspace, or the fixed scratch) and runs
+// the row-banded kernel on a persistent grid.
+static void launch_rowband(ConvArgs g, int C, const RowBandArgs& plan, size_t smem, size_t band_bytes,
+                           const float* w, int src_mode, int src_c4, int src_kpad,
+                           const StaticScratch* fixed, const char* op) {
+  float* band = nullptr;
+  if (fixed) {
+    if (band_bytes > fixed->bytes) {
+      fail(NNC_CUDA_ERR_INVALID, op, "needs %zu bytes of scratch; the static scratch holds %zu",
+           band_bytes, fixed->bytes);
+      return;
+    }
+    band = fixed->ptr;
+  } else {
+    band = (float*)workspace(band_bytes, op);
+    if (!band) return;
+  }
+  RowBandArgs rb = plan;
+  rb.band = band;
+  cudaStream_t st = ctx().stream;
+  const int64_t total = (int64_t)band_bytes / 4;
+  rowband_weight_kernel<<<grid_for(total, 256), 256, 0, st>>>(g, rb, band, w, src_mode, src_c4, src_kpad, C);
+  if (!check_launch(op)) return;
+  CUtensorMap tm;
+  const uint64_t L = (uint64_t)g.W * C;
+  const uint64_t dims[3] = {L, (uint64_t)g.H, (uint64_t)g.N};
+  const uint64_t strides[2] = {L * 4, L * g.H * 4};
+  const uint32_t box[3] = {32, (uint32_t)g.OH, (uint32_t)rb.imgs};
+  if (!encode_tmap_f32(&tm, g.x_hi, 3, dims, strides, box, nullptr, op)) return;
+  static bool attr_set[64] = {};
+  if (!attr_set[ctx().device]) {
+    if (!check_cuda(cudaFuncSetAttribute(conv_rowband_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         227 * 1024),
+                    op, "cudaFuncSetAttribute"))
+      return;
+    attr_set[ctx().device] = true;
+  }
+  const int tiles = (int)cdiv(g.N, rb.imgs);
+  const int grid = tiles < sm_count() ? tiles : sm_count();
+  g.err = device_error_word();
+  conv_rowband_kernel<<<grid, kRowBandThreads, smem, st>>>(tm, g, rb);
+  check_launch(op);
+}
+
 // fixed == nullptr: scratch comes from the runtime workspace (which may grow
 // with cudaMallocAsync); otherwise from *fixed, and a call that needs more
 // than it holds is rejected before any work is queued.
@@ -3352,7 +3775,18 @@ void conv_impl(Tensor* input, Tensor* weight, Tensor* bias, Tensor* residual, Te
     const int grid = (int)(cdiv(M, 128) < (int64_t)sm_count() * 8 ? cdiv(M, 128) : (int64_t)sm_count() * 8);
     const float* wp = (const float*)weight->data;
     cudaStream_t st = ctx().stream;
-    // TF32 mode with many pixels: the tensor-core tile kernel.
+    // TF32 mode with many pixels: the row-banded tensor-core kernel where
+    // input rows are contiguous and an output row fits one MMA, else the
+    // im2col tile kernel.
+    if (!split && M >= kSmallTcMinM && rowband_enabled() && (C == 1 || in_nhwc) &&
+        aligned16(g.x_hi) && aligned16(g.out)) {
+      RowBandArgs rb{};
+      size_t smem = 0, band_bytes = 0;
+      if (rowband_plan(g, (int)C, &rb, &smem, &band_bytes)) {
+        launch_rowband(g, (int)C, rb, smem, band_bytes, wp, src_mode, wl0.C4, wl0.Kpad, fixed, op);
+        return;
+      }
+    }
     if (!split && M >= kSmallTcMinM && M + BM < (1ll << 31) && g.K <= kSmallTcMaxK && KH * KW <= 32 &&
         small_tc_enabled()) {
       launch_small_tc_conv(g, (int)C, in_nhwc, wp, src_mode, wl0.C4, wl0.Kpad, op);

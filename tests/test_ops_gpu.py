@@ -635,6 +635,7 @@ def _check_direct_conv(cuda_lib, prec, cfg, tol):
     got = C.run_cuda(cuda_lib, case, arrays)["out"]
     C.assert_close(got, want, tol, f"conv{cfg}")
     C.assert_close(C.run_cuda(cuda_lib, case, arrays, nhwc=nhwc)["out"], want, tol, f"conv{cfg}[nhwc]")
+    C.assert_close(C.run_cuda(cuda_lib, case, arrays, nhwc={"x"})["out"], want, tol, f"conv{cfg}[nhwc in]")
     # Prepacked weight (element order for K <= 64, chunk order above).
     wt = torch.from_numpy(arrays["w"]).cuda()
     wref = T.from_torch(wt)
@@ -653,21 +654,28 @@ def test_conv_direct_small_vs_oracle(cuda_lib, prec, cfg):
 
 
 # The same few-channel convs with at least 37,888 output pixels (two 128-pixel
-# tiles per SM), a reduction of at most 160 and at most 32 window taps run in
-# TF32 mode on the tensor-core tile kernel, whose CTAs build the im2col rows
-# in shared memory: one, two and five 32-float k-blocks (K = 18 to 150),
-# channel pairs loaded as float2 (channels-last inputs with an even channel
-# count), ragged last tiles, padding, stride 2, a residual, sigmoid. 3xTF32
-# keeps them on the fp32 CUDA-core kernels.
+# tiles per SM) run in TF32 mode on tensor cores (3xTF32 keeps them on the fp32
+# CUDA-core kernels), each case NCHW, channels-last, channels-last in with
+# NCHW out, and with prepacked weights:
+# * the row-banded kernel where the input rows are contiguous (one channel or
+#   channels-last) and an output row fits one MMA (OW C_out <= 256): whole
+#   images per tile with a partial last tile, vertical padding read as zeros
+#   by the tensor map, horizontal padding in the banded weight, input rows of
+#   one to six k-blocks, float4 and scalar staging of channels-last outputs,
+#   NCHW outputs, a residual;
+# * the im2col tile kernel otherwise (reduction <= 160 over <= 32 taps): one,
+#   two and five 32-float k-blocks, channel pairs loaded as float2, stride 2,
+#   sigmoid.
 SMALL_TC_CASES = [
     # n, c, h, w, co, k, s, p, op
-    (64, 1, 32, 32, 6, 5, 1, 0, "nnc_conv_relu"),      # LeNet conv1, M = 50,176, K = 25
-    (512, 6, 14, 14, 16, 5, 1, 0, "nnc_conv"),         # LeNet conv2, M = 51,200, K = 150
-    (160, 3, 33, 31, 8, 3, 2, 1, "nnc_conv_add_relu"),  # M = 43,520, K = 27
-    (48, 5, 30, 30, 13, 5, 1, 2, "nnc_conv_sigmoid"),  # M = 43,200, K = 125
-    (64, 2, 30, 30, 10, 5, 1, 2, "nnc_conv_relu"),     # M = 57,600, K = 50
-    (80, 2, 28, 28, 12, 3, 1, 1, "nnc_conv"),          # M = 62,720, K = 18
-    (80, 7, 24, 24, 9, 3, 1, 0, "nnc_conv_add_relu"),  # M = 38,720, K = 63
+    (66, 1, 32, 32, 6, 5, 1, 0, "nnc_conv_relu"),      # LeNet conv1: banded (C = 1), 16.5 tiles of 4 images
+    (512, 6, 14, 14, 16, 5, 1, 0, "nnc_conv"),         # LeNet conv2: banded channels-last, im2col NCHW
+    (100, 2, 20, 20, 8, 5, 1, 2, "nnc_conv_relu"),     # banded with padding, M = 40,000
+    (80, 7, 24, 24, 9, 3, 1, 0, "nnc_conv_add_relu"),  # banded, 6 k-blocks, OW C_out = 198 (scalar staging)
+    (160, 3, 33, 31, 8, 3, 2, 1, "nnc_conv_add_relu"),  # im2col, M = 43,520, K = 27
+    (48, 5, 30, 30, 13, 5, 1, 2, "nnc_conv_sigmoid"),  # im2col, M = 43,200, K = 125
+    (64, 2, 30, 30, 10, 5, 1, 2, "nnc_conv_relu"),     # im2col, M = 57,600, K = 50
+    (80, 2, 28, 28, 12, 3, 1, 1, "nnc_conv"),          # im2col, M = 62,720, K = 18
 ]
 
 
