@@ -3257,6 +3257,7 @@ __global__ void __launch_bounds__(kRowBandThreads, 1)
     const int quarter = warp & 3, half = (warp - 2) >> 2;
     const bool leader = threadIdx.x == 64;  // issues the bulk stores
     const bool add = g.act == kActAddRelu;
+    const bool relu = add || g.act == kActRelu, sig = g.act == kActSigmoid;
     int acc = 0;
     uint32_t aph = 0;
     bool ok = true;
@@ -3272,11 +3273,9 @@ __global__ void __launch_bounds__(kRowBandThreads, 1)
       const int img = r / OH, oh = r - img * OH;
       const int rowpart = img * (int)rb.img_elems + oh * rb.row_stride;
       const float* res = add ? g.residual + (size_t)img0 * rb.img_elems + rowpart : nullptr;
-      for (int c = half; c < rb.n_pad / 16; c += 2) {
-        uint32_t v[16];
-        tc::tmem_ld16(tmem_base + (uint32_t)(acc * rb.acc_stride + c * 16) + ((uint32_t)(quarter * 32) << 16),
-                      v);
-        tc::tmem_ld_wait();
+      // Columns of chunk c (16 from TMEM): bias, residual, activation, into
+      // the staging buffer.
+      auto drain = [&](int c, const uint32_t(&v)[16]) {
         if (live && rb.vec4) {
           // Channels-last, OW C_out a multiple of 4: four columns per store.
 #pragma unroll
@@ -3299,9 +3298,14 @@ __global__ void __launch_bounds__(kRowBandThreads, 1)
                 o[2] = __fadd_rn(o[2], rv.z);
                 o[3] = __fadd_rn(o[3], rv.w);
               }
-              *reinterpret_cast<float4*>(obuf + rowpart + n) =
-                  make_float4(activate(o[0], g.act), activate(o[1], g.act), activate(o[2], g.act),
-                              activate(o[3], g.act));
+              if (sig) {
+#pragma unroll
+                for (int e = 0; e < 4; ++e) o[e] = activate(o[e], kActSigmoid);
+              } else if (relu) {
+#pragma unroll
+                for (int e = 0; e < 4; ++e) o[e] = o[e] > 0.0f ? o[e] : 0.0f;
+              }
+              *reinterpret_cast<float4*>(obuf + rowpart + n) = make_float4(o[0], o[1], o[2], o[3]);
             }
           }
         } else if (live) {
@@ -3316,6 +3320,20 @@ __global__ void __launch_bounds__(kRowBandThreads, 1)
             }
           }
         }
+      };
+      // This warp's chunks (every other one) four at a time: the TMEM loads
+      // are issued together and waited for once.
+      const int nch = rb.n_pad / 16;
+      const uint32_t tbase = tmem_base + (uint32_t)(acc * rb.acc_stride) + ((uint32_t)(quarter * 32) << 16);
+      for (int c0 = half; c0 < nch; c0 += 8) {
+        uint32_t v[4][16];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (c0 + 2 * u < nch) tc::tmem_ld16(tbase + (uint32_t)((c0 + 2 * u) * 16), v[u]);
+        tc::tmem_ld_wait();
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (c0 + 2 * u < nch) drain(c0 + 2 * u, v[u]);
       }
       tc::tc_fence_before();
       __syncwarp();
