@@ -3142,6 +3142,7 @@ struct RowBandArgs {
   int tmem_cols;       // power of two >= 2 acc_stride
   uint32_t a_bytes, b_bytes, stage_bytes;  // box bytes, n_pad x 128, 16 KB + b_bytes
   uint32_t img_elems;  // C_out OH OW
+  uint32_t img_stride; // staged elements per image: img_elems, padded against bank conflicts
   uint32_t out_off, col_off, bar_off;      // shared-memory layout
 };
 
@@ -3271,8 +3272,9 @@ __global__ void __launch_bounds__(kRowBandThreads, 1)
       const int r = quarter * 32 + lane;
       const bool live = ok && r < nim * OH;
       const int img = r / OH, oh = r - img * OH;
-      const int rowpart = img * (int)rb.img_elems + oh * rb.row_stride;
-      const float* res = add ? g.residual + (size_t)img0 * rb.img_elems + rowpart : nullptr;
+      const int rowpart = img * (int)rb.img_stride + oh * rb.row_stride;  // in the staging buffer
+      const float* res =
+          add ? g.residual + (size_t)(img0 + img) * rb.img_elems + oh * rb.row_stride : nullptr;
       // Columns of chunk c (16 from TMEM): bias, residual, activation, into
       // the staging buffer.
       auto drain = [&](int c, const uint32_t(&v)[16]) {
@@ -3316,7 +3318,11 @@ __global__ void __launch_bounds__(kRowBandThreads, 1)
               float o = __uint_as_float(v[j]);
               if (g.bias) o = __fadd_rn(o, biasc[n]);
               if (add) o = __fadd_rn(o, __ldg(res + colpart[n]));
-              obuf[rowpart + colpart[n]] = activate(o, g.act);
+              if (sig)
+                o = activate(o, kActSigmoid);
+              else if (relu)
+                o = o > 0.0f ? o : 0.0f;
+              obuf[rowpart + colpart[n]] = o;
             }
           }
         }
@@ -3341,7 +3347,13 @@ __global__ void __launch_bounds__(kRowBandThreads, 1)
       tc::fence_proxy_async_smem();  // obuf -> the bulk copy's reads
       epi_bar_sync();
       if (leader && ok) {
-        tc::bulk_store(g.out + (size_t)img0 * rb.img_elems, obuf, (uint32_t)nim * rb.img_elems * 4u);
+        if (rb.img_stride == rb.img_elems) {
+          tc::bulk_store(g.out + (size_t)img0 * rb.img_elems, obuf, (uint32_t)nim * rb.img_elems * 4u);
+        } else {
+          for (int i = 0; i < nim; ++i)
+            tc::bulk_store(g.out + (size_t)(img0 + i) * rb.img_elems, obuf + (size_t)i * rb.img_stride,
+                           rb.img_elems * 4u);
+        }
         tc::bulk_commit_group();
       }
       acc ^= 1;
@@ -3639,7 +3651,32 @@ static bool rowband_plan(const ConvArgs& g, int C, RowBandArgs* rb, size_t* smem
   r.b_bytes = (uint32_t)r.n_pad * 128;
   r.stage_bytes = 16384 + r.b_bytes;
   r.img_elems = (uint32_t)(n_cols * g.OH);
-  const uint32_t out_bytes = (uint32_t)cdiv((int64_t)r.imgs * r.img_elems * 4, 1024) * 1024;
+  // NCHW staging writes: the lanes of a warp hold consecutive output rows,
+  // OW apart within an image and img_stride apart across images. Pad the
+  // image stride (by a multiple of 4 floats, keeping each image's copy
+  // 16-byte aligned) to the value that spreads those rows over the most
+  // shared-memory banks.
+  r.img_stride = r.img_elems;
+  if (r.nchw) {
+    int best = 1 << 30;
+    for (uint32_t pad = 0; pad < 32; pad += 4) {
+      int cost = 0;
+      for (int q = 0; q < 4; ++q) {
+        int hits[32] = {}, worst = 0;
+        for (int row = 32 * q; row < 32 * q + 32 && row < r.imgs * g.OH; ++row) {
+          const int img = row / g.OH, oh = row - img * g.OH;
+          const int b = (int)(((int64_t)img * (r.img_elems + pad) + (int64_t)oh * g.OW) & 31);
+          worst = ++hits[b] > worst ? hits[b] : worst;
+        }
+        cost += worst;
+      }
+      if (cost < best) {
+        best = cost;
+        r.img_stride = r.img_elems + pad;
+      }
+    }
+  }
+  const uint32_t out_bytes = (uint32_t)cdiv((int64_t)r.imgs * r.img_stride * 4, 1024) * 1024;
   const uint32_t col_bytes = (uint32_t)r.n_pad * 8;  // column offsets and biases
   const uint32_t fixed_bytes = out_bytes + col_bytes + 8 * (2 * 8 + 4) + 16 + 1024;
   const int64_t stages = ((int64_t)227 * 1024 - fixed_bytes) / r.stage_bytes;
