@@ -3122,12 +3122,16 @@ void launch_small_tc_conv(const ConvArgs& g, int C, bool in_nhwc, const float* w
 // padding); B = that k-block of T_kh, bulk-copied from the banded weight that
 // a small kernel builds per call (rows pre-swizzled). The D rows are the
 // tile's output rows with all their columns; they are staged in shared memory
-// in the output's layout and leave as one bulk copy, since a tile's images are
+// in the output's layout and leave by bulk copy, since a tile's images are
 // one contiguous range of the output in either layout. Warp 0 loads, warp 1
-// issues the MMAs into two TMEM accumulators, warps 2-9 drain them (bias,
+// issues the MMAs into two TMEM accumulators, warps 2-17 drain them (bias,
 // residual, activation). The tensor cores do ~W C / (C KW) times the useful
 // work, which is cheap next to building im2col rows for a few channels.
-constexpr int kRowBandThreads = 64 + 32 * kEpilogueWarps;
+constexpr int kRowBandEpiWarps = 16;  // four per TMEM lane quadrant, splitting the columns
+constexpr int kRowBandThreads = 64 + 32 * kRowBandEpiWarps;
+__device__ __forceinline__ void rowband_epi_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(32 * kRowBandEpiWarps) : "memory");
+}
 
 struct RowBandArgs {
   const float* band;   // [KH][kb][n_pad][32] pre-swizzled banded weight
@@ -3180,7 +3184,7 @@ __global__ void __launch_bounds__(kRowBandThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       tc::mbar_init(&tfull[a], 1);
-      tc::mbar_init(&tempty[a], kEpilogueWarps);
+      tc::mbar_init(&tempty[a], kRowBandEpiWarps);
     }
     tc::fence_barrier_init();
   }
@@ -3255,7 +3259,7 @@ __global__ void __launch_bounds__(kRowBandThreads, 1)
       if (acc == 0) aph ^= 1;
     }
   } else {
-    const int quarter = warp & 3, half = (warp - 2) >> 2;
+    const int quarter = warp & 3, part = (warp - 2) >> 2;  // chunks part, part + 4, ...
     const bool leader = threadIdx.x == 64;  // issues the bulk stores
     const bool add = g.act == kActAddRelu;
     const bool relu = add || g.act == kActRelu, sig = g.act == kActSigmoid;
@@ -3266,7 +3270,7 @@ __global__ void __launch_bounds__(kRowBandThreads, 1)
       ok = ok && tc::mbar_wait_warp(&tfull[acc], aph, g.err);
       tc::tc_fence_after();
       if (leader) tc::bulk_wait_group_read<0>();  // the last tile's copy has read obuf
-      epi_bar_sync();
+      rowband_epi_sync();
       const int img0 = tile * rb.imgs;
       const int nim = min(rb.imgs, rb.nimg - img0);
       const int r = quarter * 32 + lane;
@@ -3327,25 +3331,25 @@ __global__ void __launch_bounds__(kRowBandThreads, 1)
           }
         }
       };
-      // This warp's chunks (every other one) four at a time: the TMEM loads
+      // This warp's chunks (every fourth one) three at a time: the TMEM loads
       // are issued together and waited for once.
       const int nch = rb.n_pad / 16;
       const uint32_t tbase = tmem_base + (uint32_t)(acc * rb.acc_stride) + ((uint32_t)(quarter * 32) << 16);
-      for (int c0 = half; c0 < nch; c0 += 8) {
-        uint32_t v[4][16];
+      for (int c0 = part; c0 < nch; c0 += 12) {
+        uint32_t v[3][16];
 #pragma unroll
-        for (int u = 0; u < 4; ++u)
-          if (c0 + 2 * u < nch) tc::tmem_ld16(tbase + (uint32_t)((c0 + 2 * u) * 16), v[u]);
+        for (int u = 0; u < 3; ++u)
+          if (c0 + 4 * u < nch) tc::tmem_ld16(tbase + (uint32_t)((c0 + 4 * u) * 16), v[u]);
         tc::tmem_ld_wait();
 #pragma unroll
-        for (int u = 0; u < 4; ++u)
-          if (c0 + 2 * u < nch) drain(c0 + 2 * u, v[u]);
+        for (int u = 0; u < 3; ++u)
+          if (c0 + 4 * u < nch) drain(c0 + 4 * u, v[u]);
       }
       tc::tc_fence_before();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&tempty[acc]);
       tc::fence_proxy_async_smem();  // obuf -> the bulk copy's reads
-      epi_bar_sync();
+      rowband_epi_sync();
       if (leader && ok) {
         if (rb.img_stride == rb.img_elems) {
           tc::bulk_store(g.out + (size_t)img0 * rb.img_elems, obuf, (uint32_t)nim * rb.img_elems * 4u);
