@@ -3260,7 +3260,20 @@ __global__ void __launch_bounds__(kRowBandThreads, 1)
     }
   } else {
     const int quarter = warp & 3, part = (warp - 2) >> 2;  // chunks part, part + 4, ...
-    const bool leader = threadIdx.x == 64;  // issues the bulk stores
+    // Channels-last outputs: each TMEM lane quadrant's 32 rows are one
+    // contiguous range of the output, stored by the quadrant's own leader
+    // once its four warps are done (no tile-wide barrier). NCHW outputs: one
+    // leader stores whole images after all sixteen warps.
+    const bool by_quadrant = !rb.nchw;
+    const bool leader = by_quadrant ? (lane == 0 && part == 0) : threadIdx.x == 64;
+    auto quadrant_sync = [&]() {  // named barriers 2-5: the four warps of a quadrant
+      switch (quarter) {
+        case 0: asm volatile("bar.sync 2, 128;" ::: "memory"); break;
+        case 1: asm volatile("bar.sync 3, 128;" ::: "memory"); break;
+        case 2: asm volatile("bar.sync 4, 128;" ::: "memory"); break;
+        default: asm volatile("bar.sync 5, 128;" ::: "memory"); break;
+      }
+    };
     const bool add = g.act == kActAddRelu;
     const bool relu = add || g.act == kActRelu, sig = g.act == kActSigmoid;
     int acc = 0;
@@ -3270,7 +3283,10 @@ __global__ void __launch_bounds__(kRowBandThreads, 1)
       ok = ok && tc::mbar_wait_warp(&tfull[acc], aph, g.err);
       tc::tc_fence_after();
       if (leader) tc::bulk_wait_group_read<0>();  // the last tile's copy has read obuf
-      rowband_epi_sync();
+      if (by_quadrant)
+        quadrant_sync();
+      else
+        rowband_epi_sync();
       const int img0 = tile * rb.imgs;
       const int nim = min(rb.imgs, rb.nimg - img0);
       const int r = quarter * 32 + lane;
@@ -3349,8 +3365,18 @@ __global__ void __launch_bounds__(kRowBandThreads, 1)
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&tempty[acc]);
       tc::fence_proxy_async_smem();  // obuf -> the bulk copy's reads
-      rowband_epi_sync();
-      if (leader && ok) {
+      if (by_quadrant) {
+        quadrant_sync();
+        const int r0 = quarter * 32, r1 = min(r0 + 32, nim * OH);
+        if (leader && ok && r1 > r0) {
+          tc::bulk_store(g.out + ((size_t)img0 * OH + r0) * rb.n_cols, obuf + (size_t)r0 * rb.n_cols,
+                         (uint32_t)(r1 - r0) * (uint32_t)rb.n_cols * 4u);
+          tc::bulk_commit_group();
+        }
+      } else {
+        rowband_epi_sync();
+      }
+      if (!by_quadrant && leader && ok) {
         if (rb.img_stride == rb.img_elems) {
           tc::bulk_store(g.out + (size_t)img0 * rb.img_elems, obuf, (uint32_t)nim * rb.img_elems * 4u);
         } else {
