@@ -283,7 +283,7 @@ def model_runs(so, torch, pk: dict, reps: int, only_model: str | None = None) ->
 # are larger than L2 so that DRAM counters mean something, but a few hundred
 # MB at most.
 PROFILE_CASES = ("layernorm", "layernorm256", "softmax", "softmax128", "transpose", "transpose_k", "add",
-                 "stem", "stage1", "stage2s2")
+                 "stem", "stage1", "stage2s2", "lenet_conv1", "lenet_conv2")
 
 
 def profile_case(so, torch, case: str) -> None:
@@ -344,6 +344,18 @@ def profile_case(so, torch, case: str) -> None:
         o = torch.empty(n, 28, 28, 128, device="cuda")
         fn = lambda: so.nnc_conv_relu(R(x, L.TAG_NHWC, (n, 64, 56, 56)), rw.ptr, R(bias),
                                       R(o, L.TAG_NHWC, (n, 128, 28, 28)), 3, 3, 2, 2, 1, 1)
+    elif case in ("lenet_conv1", "lenet_conv2"):  # LeNet-5's convs at batch 8192 in the model's layouts
+        n = 8192
+        if case == "lenet_conv1":  # [n, 1, 32, 32] -> channels-last [n, 6, 28, 28]
+            x, w, bias = rnd(n, 1, 32, 32), rnd(6, 1, 5, 5) * 0.2, rnd(6) * 0.01
+            o = torch.empty(n, 28, 28, 6, device="cuda")
+            xi, oi = R(x), R(o, L.TAG_NHWC, (n, 6, 28, 28))
+        else:  # channels-last [n, 6, 14, 14] -> NCHW [n, 16, 10, 10]
+            x, w, bias = rnd(n, 14, 14, 6), rnd(16, 6, 5, 5) * 0.1, rnd(16) * 0.01
+            o = torch.empty(n, 16, 10, 10, device="cuda")
+            xi, oi = R(x, L.TAG_NHWC, (n, 6, 14, 14)), R(o)
+        wi, bi = R(w), R(bias)
+        fn = lambda: so.nnc_conv_relu(xi, wi, bi, oi, 5, 5, 1, 1, 0, 0)
     else:
         raise SystemExit(f"unknown case {case}")
     for _ in range(3):
