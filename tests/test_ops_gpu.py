@@ -286,7 +286,7 @@ def test_conv_stride1_blocks_vs_oracle(cuda_lib, prec, cfg):
     if op == "nnc_conv_add_relu":
         args.append(C._t("res"))
         nhwc.add("res")
-    args += [C._o("out", (n, co, oh, ow)), C._i(k), C._i(k), C._i(st), C._i(st), C._i(p), C._i(p)]
+    args += [C._o("out", (n, co, oh, ow)), C._i(k), C._i(k), C._i(sh), C._i(sw), C._i(p), C._i(p)]
     case = {"name": "c", "op": op, "args": args}
     cuda_lib.nnc_cuda_set_precision(prec)
     want = C.run_host(_oracle(), case, arrays)["out"]
@@ -606,6 +606,7 @@ DIRECT_CASES = [
     (2, 12, 11, 9, 13, 3, 1, 2, "nnc_conv_sigmoid"),
     (3, 2, 9, 13, 4, 3, 1, 1, "nnc_conv_add_relu"),
     (2, 4, 12, 7, 10, 5, 1, 2, "nnc_conv_relu"),
+    (2, 3, 17, 19, 8, 3, (2, 1), 1, "nnc_conv_relu"),  # row stride 2, column stride 1
 ]
 
 
@@ -617,8 +618,9 @@ def _check_direct_conv(cuda_lib, prec, cfg, tol):
     from nnc_cuda import tensor as T
 
     n, c, h, w, co, k, st, p, op = cfg
-    r = np.random.default_rng(17 + sum(cfg[:8]))
-    oh, ow = C.conv_out(h, k, st, p), C.conv_out(w, k, st, p)
+    sh, sw = st if isinstance(st, tuple) else (st, st)  # one stride, or (rows, columns)
+    r = np.random.default_rng(17 + sum(sum(v) if isinstance(v, tuple) else v for v in cfg[:8]))
+    oh, ow = C.conv_out(h, k, sh, p), C.conv_out(w, k, sw, p)
     arrays = {"x": r.standard_normal((n, c, h, w)).astype(np.float32),
               "w": (r.standard_normal((co, c, k, k)) * np.sqrt(2.0 / (c * k * k))).astype(np.float32),
               "b": r.uniform(-0.01, 0.01, co).astype(np.float32),
@@ -628,7 +630,7 @@ def _check_direct_conv(cuda_lib, prec, cfg, tol):
     if op == "nnc_conv_add_relu":
         args.append(C._t("res"))
         nhwc.add("res")
-    args += [C._o("out", (n, co, oh, ow)), C._i(k), C._i(k), C._i(st), C._i(st), C._i(p), C._i(p)]
+    args += [C._o("out", (n, co, oh, ow)), C._i(k), C._i(k), C._i(sh), C._i(sw), C._i(p), C._i(p)]
     case = {"name": "c", "op": op, "args": args}
     cuda_lib.nnc_cuda_set_precision(prec)
     want = C.run_host(_oracle(), case, arrays)["out"]
@@ -676,6 +678,8 @@ SMALL_TC_CASES = [
     (48, 5, 30, 30, 13, 5, 1, 2, "nnc_conv_sigmoid"),  # im2col, M = 43,200, K = 125
     (64, 2, 30, 30, 10, 5, 1, 2, "nnc_conv_relu"),     # im2col, M = 57,600, K = 50
     (80, 2, 28, 28, 12, 3, 1, 1, "nnc_conv"),          # im2col, M = 62,720, K = 18
+    (66, 1, 32, 64, 6, 5, (1, 2), 0, "nnc_conv_relu"),  # banded, column stride 2, OW C_out = 180
+    (160, 3, 31, 33, 8, 3, (2, 1), 1, "nnc_conv_add_relu"),  # im2col, row stride 2, M = 84,480
 ]
 
 
