@@ -3825,8 +3825,9 @@ void conv_impl(Tensor* input, Tensor* weight, Tensor* bias, Tensor* residual, Te
   const int64_t M = (int64_t)N * OH * OW;
   if (M == 0 || Cout == 0) return;
   const bool split = ctx().precision == NNC_CUDA_PRECISION_3XTF32;
-  // Few output channels and a short reduction: the direct CUDA-core kernel
-  // (full fp32, so either precision mode).
+  // Few output channels and a short reduction: in TF32 mode with many pixels
+  // the tensor-core kernels below (row-banded, else im2col tiles); otherwise
+  // the direct CUDA-core kernels (full fp32, so either precision mode).
   if (!pool && Cout <= 16 && (int64_t)C * KH * KW <= kDirectMaxK && (int64_t)C * H * W < (1ll << 31)) {
     const bool packed_w = (tag_of(weight) & NNC_CUDA_TAG_PACKED_CONV) != 0;
     const WeightLayout wl0 = weight_layout(C, KH, KW);
